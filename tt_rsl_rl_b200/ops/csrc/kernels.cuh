@@ -1,0 +1,5 @@
+// Registration hook for the RL kernels' Python bindings (implemented in bindings_rl.cpp).
+#pragma once
+#include <torch/extension.h>
+
+void rlb_register_kernels(pybind11::module& m);
