@@ -1,0 +1,156 @@
+"""Seeded synthetic linear-Gaussian environment used by the benchmark configurations.
+
+Dynamics ``s' = A s + B a + noise_std * eps`` with ``eps ~ N(0, I)``; ``A`` (S x S) and ``B`` (S x A) are drawn from a
+seed, ``A`` scaled to spectral radius ``rho`` and ``B`` to spectral norm ``rho``. Reward ``-|s'|^2 - 0.01 |a|^2``.
+Episodes terminate at random with probability ``reset_prob`` per step (a termination) and are truncated at
+``episode_length`` steps (a time-out, reported in ``extras["time_outs"]``); a reset draws ``s ~ N(0, I)``.
+
+Observations: group ``"policy"`` is the state ``s`` (S values); group ``"critic"`` appends ``privileged_dim``
+privileged features (|s|^2 / S, |a_prev|^2 / A, episode progress, then zeros) when ``privileged_dim > 0``.
+
+``step`` performs only asynchronous device work (no host synchronisation), so it can be captured in a CUDA graph. With ``host_noise=True`` the process noise is read from a pinned host pool and copied
+to the device every step (the input of an end-to-end measurement). The same class serves the CPU path, the CUDA path
+and the unmodified-reference benchmark arm; it depends only on torch and a TensorDict class.
+"""
+
+from __future__ import annotations
+
+import torch
+
+try:  # the TensorDict class the caller's framework uses (real package or a stand-in on sys.path)
+    from tensordict import TensorDict  # type: ignore
+except ImportError:  # pragma: no cover - depends on the environment
+    from ..utils.tensordict import TensorDict
+
+from .vec_env import VecEnv
+
+
+def make_system_matrices(state_dim: int, action_dim: int, seed: int, rho: float = 0.95):
+    """Seeded ``(A, B)`` on the CPU: A with spectral radius ``rho``, B with largest singular value ``rho``."""
+    g = torch.Generator().manual_seed(seed)
+    A = torch.randn(state_dim, state_dim, generator=g, dtype=torch.float64)
+    radius = torch.linalg.eigvals(A).abs().max().item()
+    A = A * (rho / radius)
+    B = torch.randn(state_dim, action_dim, generator=g, dtype=torch.float64)
+    B = B * (rho / torch.linalg.matrix_norm(B, ord=2).item())
+    return A.float(), B.float()
+
+
+class LinearGaussianVecEnv(VecEnv):
+    graph_capturable = True
+
+    def __init__(self, num_envs: int, obs_dim: int = 48, num_actions: int = 12, privileged_dim: int = 0,
+                 episode_length: int = 1000, reset_prob: float = 0.005, noise_std: float = 0.05, seed: int = 0,
+                 device: str | torch.device = "cpu", host_noise: bool = False, host_noise_pool_steps: int = 8,
+                 step_dt: float = 0.02) -> None:
+        self.num_envs = num_envs
+        self.num_obs = obs_dim
+        self.num_actions = num_actions
+        self.privileged_dim = privileged_dim
+        self.max_episode_length = episode_length
+        self.reset_prob = reset_prob
+        self.noise_std = noise_std
+        self.device = torch.device(device)
+        self.step_dt = step_dt
+        self.cfg = {
+            "num_envs": num_envs, "obs_dim": obs_dim, "num_actions": num_actions, "privileged_dim": privileged_dim,
+            "episode_length": episode_length, "reset_prob": reset_prob, "noise_std": noise_std, "seed": seed,
+        }
+        A, B = make_system_matrices(obs_dim, num_actions, seed)
+        # row-vector form: s'[n] = s[n] @ A^T + a[n] @ B^T
+        self.At = A.t().contiguous().to(self.device)
+        self.Bt = B.t().contiguous().to(self.device)
+        gen = torch.Generator(device="cpu").manual_seed(seed + 1)
+        self.state = torch.randn(num_envs, obs_dim, generator=gen).to(self.device)
+        self.episode_length_buf = torch.zeros(num_envs, dtype=torch.long, device=self.device)
+        self.rewards = torch.zeros(num_envs, device=self.device)
+        self.dones = torch.zeros(num_envs, device=self.device)
+        self.time_outs = torch.zeros(num_envs, device=self.device)
+        self._noise = torch.zeros(num_envs, obs_dim, device=self.device)
+        self._reset_noise = torch.zeros(num_envs, obs_dim, device=self.device)
+        self._uniform = torch.zeros(num_envs, device=self.device)
+        self._next = torch.zeros(num_envs, obs_dim, device=self.device)
+        self._policy_obs = torch.zeros(num_envs, obs_dim, device=self.device)
+        crit_dim = obs_dim + privileged_dim
+        self._critic_obs = torch.zeros(num_envs, crit_dim, device=self.device) if privileged_dim > 0 else None
+        self.host_noise = host_noise
+        if host_noise:
+            pin = self.device.type == "cuda"
+            pool = torch.randn(host_noise_pool_steps, num_envs, obs_dim, generator=gen)
+            self._host_pool = pool.pin_memory() if pin else pool
+            self._host_step = 0
+        self._write_obs(torch.zeros(num_envs, num_actions, device=self.device))
+        self._obs = self._make_obs_dict()
+
+    # ---- VecEnv -----------------------------------------------------------------------------------------------------
+    @property
+    def unwrapped(self) -> LinearGaussianVecEnv:
+        return self
+
+    def get_observations(self):
+        return self._obs
+
+    def _make_obs_dict(self):
+        groups = {"policy": self._policy_obs}
+        if self._critic_obs is not None:
+            groups["critic"] = self._critic_obs
+        return TensorDict(groups, batch_size=[self.num_envs], device=self.device)
+
+    def _draw_noise(self) -> None:
+        if self.host_noise:
+            src = self._host_pool[self._host_step % self._host_pool.shape[0]]
+            self._host_step += 1
+            self._noise.copy_(src, non_blocking=True)
+        else:
+            self._noise.normal_()
+
+    def _write_obs(self, actions: torch.Tensor) -> None:
+        self._policy_obs.copy_(self.state)
+        if self._critic_obs is not None:
+            S, A = self.num_obs, self.num_actions
+            self._critic_obs[:, :S].copy_(self.state)
+            extra = self._critic_obs[:, S:]
+            extra.zero_()
+            extra[:, 0].copy_(self.state.square().sum(dim=1) / S)
+            if self.privileged_dim > 1:
+                extra[:, 1].copy_(actions.square().sum(dim=1) / A)
+            if self.privileged_dim > 2:
+                extra[:, 2].copy_(self.episode_length_buf.float() / float(self.max_episode_length))
+
+    def step(self, actions: torch.Tensor):
+        a = actions.to(self.device)
+        self._draw_noise()
+        # s' = A s + B a + sigma * eps
+        torch.addmm(torch.mm(self.state, self.At), a, self.Bt, out=self._next)
+        self._next.add_(self._noise, alpha=self.noise_std)
+        # reward on the new state and the applied action
+        torch.sum(self._next.square(), dim=1, out=self.rewards)
+        self.rewards.add_(a.square().sum(dim=1), alpha=0.01).neg_()
+        # episode bookkeeping: random terminations and time-outs
+        self.episode_length_buf.add_(1)
+        self._uniform.uniform_()
+        terminated = self._uniform < self.reset_prob
+        timed_out = self.episode_length_buf >= self.max_episode_length
+        done = terminated | timed_out
+        self.time_outs.copy_(timed_out & ~terminated)
+        self.dones.copy_(done)
+        # reset finished environments to s ~ N(0, I)
+        self._reset_noise.normal_()
+        self.state.copy_(torch.where(done.unsqueeze(1), self._reset_noise, self._next))
+        self.episode_length_buf.masked_fill_(done, 0)
+        self._write_obs(a)
+        extras = {"time_outs": self.time_outs, "log": {"/state_norm": self.rewards}}
+        return self._obs, self.rewards, self.dones, extras
+
+
+def humanoid_like(num_envs: int, device: str | torch.device = "cpu", seed: int = 0, **kw) -> LinearGaussianVecEnv:
+    """The benchmark shape: actor obs 96, critic obs 99 (3 privileged features), 29 actions."""
+    return LinearGaussianVecEnv(num_envs, obs_dim=96, num_actions=29, privileged_dim=3, seed=seed, device=device, **kw)
+
+
+def spectral_radius(matrix: torch.Tensor) -> float:
+    """Largest eigenvalue modulus (used by tests)."""
+    return float(torch.linalg.eigvals(matrix.double()).abs().max())
+
+
+__all__ = ["LinearGaussianVecEnv", "humanoid_like", "make_system_matrices", "spectral_radius"]
