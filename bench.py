@@ -1,0 +1,261 @@
+#!/usr/bin/env python
+"""Benchmark: PPO training throughput (samples/s) of one learn() iteration on the BASELINE configuration.
+
+Configuration: 65536 environments in total split evenly across ranks, synthetic
+linear-Gaussian environment (actor obs 96, critic obs 99, 29 actions), actor and critic MLPs [512, 256, 128] ELU with
+empirical observation normalisation, 24 steps per environment, 5 epochs x 4 minibatches, bf16 GEMM operands with fp32
+master weights and Adam. Data: synthetic, seeded; weights: random init.
+
+A step is one ``OnPolicyRunner.learn`` iteration (rollout of 24 env steps, returns, update, normaliser update), driven
+through the public API. Timing: W untimed warm-up iterations, then K iterations bracketed by a barrier and
+``torch.cuda.synchronize()`` and timed with CUDA events on the launching stream; the max over ranks is reported.
+Every iteration streams ~T*N*S*4 bytes of rollout data (the rollout arena alone is far larger than the 126 MB L2),
+so consecutive iterations do not run from a warm L2.
+
+``value`` is measured with the environment's process noise generated on the device. ``e2e`` repeats the measurement
+with the noise of every environment step copied from pinned host memory (``host_noise=True``) plus the device-to-host
+read of each iteration's loss statistics and learning rate.
+
+Usage: ``python bench.py --gpus N --steps K --warmup W [--impl ours|reference]`` (N > 1 under torchrun).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+TOTAL_ENVS = 65536
+T_STEPS = 24
+BASELINE_VALUE = None  # BASELINE.md publishes no NVIDIA number for this configuration
+
+
+def train_cfg(impl: str) -> dict:
+    alg = {
+        "class_name": "PPO", "num_learning_epochs": 5, "num_mini_batches": 4, "clip_param": 0.2, "gamma": 0.99,
+        "lam": 0.95, "value_loss_coef": 1.0, "entropy_coef": 0.01, "learning_rate": 1e-3, "max_grad_norm": 1.0,
+        "schedule": "adaptive", "desired_kl": 0.01, "use_clipped_value_loss": True,
+    }
+    if impl == "reference":
+        alg["use_mixed_precision"] = True  # bf16 autocast GEMMs on the reference arm
+    return {
+        "num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
+        "obs_groups": {"actor": ["policy"], "critic": ["critic"]},
+        "algorithm": alg,
+        "actor": {"class_name": "MLPModel", "hidden_dims": [512, 256, 128], "activation": "elu",
+                  "obs_normalization": True,
+                  "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+        "critic": {"class_name": "MLPModel", "hidden_dims": [512, 256, 128], "activation": "elu",
+                   "obs_normalization": True},
+    }
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons every 200 ms while active."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]) -> None:
+        self.gpus = gpus
+        self.rows: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                      "-i", ",".join(map(str, self.gpus))], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.rows.append([x.strip() for x in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_info() -> tuple[int, int, int]:
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK",
+                                                                                                      "0"))
+
+
+def make_env(num_envs: int, device: str, host_noise: bool, seed: int):
+    from tt_rsl_rl_b200.env import humanoid_like
+
+    return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise)
+
+
+def timed_learn(runner, steps: int, warmup: int, world: int) -> float:
+    """Seconds per iteration (device time), max over ranks."""
+    import torch
+
+    runner.learn(warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    runner.learn(steps)
+    stop.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(stop) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / 1000.0
+
+
+def build_runner(impl: str, env, device: str):
+    import copy
+
+    cfg = copy.deepcopy(train_cfg(impl))
+    if impl == "reference":
+        from rsl_rl.runners import OnPolicyRunner as RefRunner  # noqa: the unmodified reference
+
+        return RefRunner(env, cfg, log_dir=None, device=device)
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    return OnPolicyRunner(env, cfg, log_dir=None, device=device)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    world, rank, local_rank = dist_info()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+
+    if args.impl == "reference":
+        import baseline
+
+        if not baseline.reference_available():
+            print(json.dumps({"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}))
+            return
+        baseline.add_reference_to_path()
+
+    import torch
+
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    torch.cuda.set_device(local_rank)
+    device = f"cuda:{local_rank}"
+    if world > 1 and not torch.distributed.is_initialized():
+        import datetime
+
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device(device),
+                                             timeout=datetime.timedelta(seconds=120))
+    torch.manual_seed(1 + rank)
+    n_local = TOTAL_ENVS // world
+
+    env = make_env(n_local, device, host_noise=False, seed=rank)
+    runner = build_runner(args.impl, env, device)
+    sampler = ClockSampler([local_rank]) if local_rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    s_per_iter = timed_learn(runner, args.steps, args.warmup, world)
+    if sampler:
+        sampler.__exit__()
+    samples = TOTAL_ENVS * T_STEPS
+    value = samples / s_per_iter
+
+    e2e = None
+    if not args.no_e2e:
+        env2 = make_env(n_local, device, host_noise=True, seed=rank)
+        runner2 = build_runner(args.impl, env2, device)
+        e2e_s = timed_learn(runner2, args.steps, args.warmup, world)
+        h2d = T_STEPS * n_local * 96 * 4
+        e2e = {"value": samples / e2e_s, "unit": "samples/s", "ms_per_step": e2e_s * 1e3,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 20 if args.impl == "ours" else 16,
+               "input": "environment process noise copied from pinned host memory every env step"}
+
+    launches = None
+    if args.impl == "ours":
+        eng = getattr(runner.alg, "engine", None)
+        launches = kernel_launches_per_iteration(eng) if eng is not None else 0
+
+    if rank == 0:
+        line = {
+            "metric": "PPO train samples/s (box, max over ranks)",
+            "value": value,
+            "unit": "samples/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": s_per_iter * 1e3,
+            "s_per_iter": s_per_iter,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+            "dtype": "bf16",
+            "data": "synthetic (seeded linear-Gaussian env), random-init weights",
+            "config": {"model": "PPO MLP actor-critic [512,256,128] ELU, obs 96/99, 29 actions",
+                       "global_batch": samples, "seq_len": T_STEPS, "num_envs_total": TOTAL_ENVS,
+                       "epochs": 5, "minibatches": 4, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (rollout arena >> 126 MB)"},
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": sampler.summary() if sampler else None,
+        }
+        if args.impl == "reference":
+            line["impl"] = "reference"
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def kernel_launches_per_iteration(engine) -> int:
+    """Launches of this framework's kernels per timed iteration (counted from the engine's structure)."""
+    if engine is None:
+        return 0
+    L_a, L_c = engine.plan_a.L, engine.plan_c.L
+    per_act = 2 + L_a + 1 + L_c  # prep x2, actor GEMMs, sample, critic GEMMs
+    per_step = per_act + 1  # + process_step
+    returns = 1 + L_c + 2  # prep, critic GEMMs, gae, normalise
+    per_mb = 1 + L_a + L_c + 1 + (2 * L_a - 1) + (2 * L_c - 1) + 1 + 1  # gather, fwd, loss, bwd, reduce, adam
+    update = 1 + engine.E * engine.M * per_mb + 2 * 2  # perm key, minibatches, normaliser (2 kernels x 2 models)
+    return engine.T * per_step + returns + update
+
+
+if __name__ == "__main__":
+    main()

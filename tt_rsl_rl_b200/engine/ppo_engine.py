@@ -1,11 +1,537 @@
-"""Placeholder replaced below."""
+"""Fused CUDA engine of :class:`tt_rsl_rl_b200.algorithms.PPO`.
+
+State lives on the device for the whole run: a flat fp32 parameter arena (the ``nn.Parameter``s of actor and critic
+are views into it, so ``state_dict`` and checkpoints are unchanged), flat Adam moments (views installed into the
+``torch.optim.Adam`` object on ``save``), bf16 weight shadows, the rollout arena ``[T * N, ...]`` and the minibatch
+buffers. Per iteration:
+
+* ``act`` / ``process_env_step``: observation concat + normalisation, actor and critic forward (tcgen05 GEMMs), the
+  Gaussian head with Philox sampling, time-out bootstrap and storage writes;
+* ``compute_returns``: critic forward on the last observation, GAE reverse scan, advantage normalisation;
+* ``update``: for each of ``E x M`` minibatches: Feistel-permuted gather, forward of both models, fused PPO loss and
+  output gradients, backward GEMMs, gradient reduction, and the fused (exchange +) clip + adaptive-LR + Adam kernel;
+  then the observation normaliser update. From the second call on the whole update is one CUDA graph replay and the
+  only host synchronisation is the read of the loss statistics at the end.
+
+Semantics follow ``rsl_rl/algorithms/ppo.py`` (see the kernels' comments for the exact rules). The random number
+streams differ from PyTorch's (Philox in-kernel sampling, Feistel permutation instead of ``torch.randperm``).
+"""
+
+from __future__ import annotations
+
+from itertools import chain
+
+import torch
+import torch.nn as nn
+
+from ..modules import EmpiricalNormalization, GaussianDistribution, HeteroscedasticGaussianDistribution
+from ..ops import ext
+from .mlp_plan import MLPPlan, pad8
+
+_GROUP_ACTOR = 0
+_GROUP_CRITIC = 1
+_TAIL = 4  # exchanged statistics after the parameters: surrogate, value, entropy, kl (each a minibatch mean)
+
+
+def _elu_mlp(model) -> str | None:
+    mlp = getattr(model, "mlp", None)
+    if mlp is None:
+        return "model has no MLP head"
+    for m in mlp:
+        if isinstance(m, nn.Linear) or isinstance(m, nn.Unflatten):
+            continue
+        if not isinstance(m, nn.ELU) or m.alpha != 1.0:
+            return f"activation {type(m).__name__} is not fused (ELU only)"
+    return None
 
 
 class PPOEngine:
+    # ---- capability checks ------------------------------------------------------------------------------------------
     @staticmethod
-    def unsupported_reason(alg):
-        return "engine not built"
+    def supports_models(actor, critic, alg_cfg: dict) -> str | None:
+        from ..models import CNNModel, MLPModel
+
+        for name, m in (("actor", actor), ("critic", critic)):
+            if type(m) is not MLPModel:
+                if isinstance(m, CNNModel):
+                    return f"{name} is a CNNModel"
+                return f"{name} type {type(m).__name__} is not fused"
+            reason = _elu_mlp(m)
+            if reason:
+                return f"{name}: {reason}"
+            if m.obs_dim > 1024:
+                return f"{name} observation width {m.obs_dim} too large"
+        dist = actor.distribution
+        if not isinstance(dist, (GaussianDistribution, HeteroscedasticGaussianDistribution)):
+            return "actor distribution is not Gaussian"
+        if dist.output_dim > 64:
+            return "more than 64 actions"
+        if critic.distribution is not None:
+            return "critic has a distribution"
+        if critic.mlp.linears[-1].out_features != 1:
+            return "critic output is not scalar"
+        if alg_cfg.get("rnd_cfg"):
+            return "RND extension runs on the PyTorch path"
+        if alg_cfg.get("symmetry_cfg"):
+            return "symmetry extension runs on the PyTorch path"
+        if alg_cfg.get("normalize_advantage_per_mini_batch"):
+            return "per-minibatch advantage normalisation runs on the PyTorch path"
+        if str(alg_cfg.get("optimizer", "adam")).lower() != "adam":
+            return "only Adam is fused"
+        return None
 
     @staticmethod
-    def supports_models(actor, critic, alg_cfg):
-        return "engine not built"
+    def unsupported_reason(alg) -> str | None:
+        cfg = {
+            "rnd_cfg": alg.rnd is not None,
+            "symmetry_cfg": alg.symmetry is not None,
+            "normalize_advantage_per_mini_batch": alg.normalize_advantage_per_mini_batch,
+            "optimizer": getattr(alg, "optimizer_name", "adam"),
+        }
+        return PPOEngine.supports_models(alg.actor, alg.critic, cfg)
+
+    # ---- construction -------------------------------------------------------------------------------------------------
+    def __init__(self, alg, num_steps_per_env: int, num_envs: int, obs_template) -> None:
+        self.alg = alg
+        self.device = torch.device(alg.device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.T = num_steps_per_env
+        self.N = num_envs
+        self.total = self.T * self.N
+        self.M = alg.num_mini_batches
+        self.E = alg.num_learning_epochs
+        if not 1 <= self.M <= self.total:
+            raise ValueError("num_mini_batches must be between 1 and the rollout batch size.")
+        self.B_max = max((i + 1) * self.total // self.M - i * self.total // self.M for i in range(self.M))
+        props = torch.cuda.get_device_properties(self.device)
+        self.sm_count = props.multi_processor_count
+        self.actor = alg.actor
+        self.critic = alg.critic
+        dist = self.actor.distribution
+        self.hetero = isinstance(dist, HeteroscedasticGaussianDistribution)
+        self.log_std = dist.std_type == "log"
+        self.A = dist.output_dim
+        self.std_range = dist.std_range
+        self.log_std_range = dist.log_std_range
+        dev = self.device
+        f32 = dict(dtype=torch.float32, device=dev)
+
+        # observation layout
+        self.groups_a = list(self.actor.obs_groups)
+        self.groups_c = list(self.critic.obs_groups)
+        self.Da = self.actor.obs_dim
+        self.Dc = self.critic.obs_dim
+        self.shared_obs = self.groups_a == self.groups_c
+
+        # ---- flat parameter arena (views installed into the nn.Parameters) ----
+        self.params = list(dict.fromkeys(chain(self.actor.parameters(), self.critic.parameters())))
+        actor_ids = {id(p) for p in self.actor.parameters()}
+        self.param_group = [_GROUP_ACTOR if id(p) in actor_ids else _GROUP_CRITIC for p in self.params]
+        self.offsets = []
+        off = 0
+        for p in self.params:
+            self.offsets.append(off)
+            off += p.numel()
+        self.n_params = off
+        self.flat = torch.zeros(self.n_params, **f32)
+        for p, o in zip(self.params, self.offsets):
+            self.flat[o : o + p.numel()].copy_(p.data.reshape(-1))
+            p.data = self.flat[o : o + p.numel()].view_as(p)
+        n_ex = self.n_params + _TAIL
+        self.exp_avg = torch.zeros(self.n_params, **f32)
+        self.exp_avg_sq = torch.zeros(self.n_params, **f32)
+        self.send = [torch.zeros(n_ex, **f32), torch.zeros(n_ex, **f32)]
+        self.grads = torch.zeros(n_ex, **f32)
+        self.lr = torch.tensor([alg._learning_rate, alg._learning_rate], **f32)
+        self.step = torch.zeros(2, dtype=torch.int64, device=dev)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.barrier = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.nonfinite = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.rng_counter = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.rng_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.perm_key = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.seed = int(torch.initial_seed() % (2**62))
+        self.half_bits = ext().feistel_half_bits(self.total)
+        if self.total >= 2**31:
+            raise ValueError("rollout batch too large for the fused engine")
+
+        # ---- MLP plans ----
+        self.plan_a = MLPPlan(self.actor.mlp, self.Da, self.N, self.B_max, dev, self.sm_count)
+        self.plan_c = MLPPlan(self.critic.mlp, self.Dc, self.N, self.B_max, dev, self.sm_count)
+        self.head_cols = self.plan_a.head_cols
+        self.plan_a.refresh_shadows()
+        self.plan_c.refresh_shadows()
+
+        # ---- rollout arena ----
+        T, N, A = self.T, self.N, self.A
+        self.obs_a = torch.zeros(T * N, self.Da, **f32)
+        self.obs_c = self.obs_a if self.shared_obs else torch.zeros(T * N, self.Dc, **f32)
+        self.st_actions = torch.zeros(T * N, A, **f32)
+        self.st_mean = torch.zeros(T * N, A, **f32)
+        self.st_std = torch.zeros(T * N, A, **f32)
+        self.st_logp = torch.zeros(T * N, **f32)
+        self.st_values = torch.zeros(T * N, **f32)
+        self.st_rewards = torch.zeros(T * N, **f32)
+        self.st_dones = torch.zeros(T * N, **f32)
+        self.st_returns = torch.zeros(T * N, **f32)
+        self.st_adv = torch.zeros(T * N, **f32)
+        self.actions_out = torch.zeros(N, A, **f32)
+        self.last_values = torch.zeros(N, **f32)
+        self.gae_partial = torch.zeros(2 * ext().gae_blocks(N), dtype=torch.float64, device=dev)
+        self.t = 0
+
+        # ---- minibatch buffers ----
+        B = self.B_max
+        self.idx = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.value_train = torch.zeros(B, 1, **f32)
+        self.d_value = self.plan_c.d_head  # gradient of the scalar value head, [B, 8] bf16 (7 zero padding columns)
+        self.loss_blocks = ext().ppo_loss_blocks(B)
+        self.stats_partial = torch.zeros(self.loss_blocks, _TAIL, **f32)
+        self.dhead_colsum = torch.zeros(self.loss_blocks, self.head_cols, **f32)
+        self.dvalue_colsum = torch.zeros(self.loss_blocks, 1, **f32)
+        self.dstd_partial = torch.zeros(self.loss_blocks, A, **f32)
+        self.loss_acc = torch.zeros(_TAIL, **f32)
+
+        # ---- gradient reduction plan (flat order = optimizer order) ----
+        seg = {}
+        seg.update(self.plan_a.reduce_segments(self.dhead_colsum, self.loss_blocks))
+        seg.update(self.plan_c.reduce_segments(self.dvalue_colsum, self.loss_blocks))
+        if not self.hetero:
+            std_p = dist.std_param if dist.std_type == "scalar" else dist.log_std_param
+            seg[id(std_p)] = (self.dstd_partial, self.loss_blocks, A)
+        srcs, parts, ns, offs = [], [], [], []
+        for p, o in zip(self.params, self.offsets):
+            if id(p) not in seg:
+                raise RuntimeError("fused engine: parameter without a gradient source")
+            buf, nparts, n = seg[id(p)]
+            srcs.append(buf)
+            parts.append(nparts)
+            ns.append(n)
+            offs.append(o)
+        srcs.append(self.stats_partial)
+        parts.append(self.loss_blocks)
+        ns.append(_TAIL)
+        offs.append(self.n_params)
+        self.reduce_plan, self.reduce_nseg, self.reduce_chunks = ext().make_reduce_plan(srcs, parts, ns, offs)
+
+        # ---- Adam plan ----
+        shadows = {}
+        for plan in (self.plan_a, self.plan_c):
+            for lin, wb in zip(plan.linears, plan.w_bf16):
+                shadows[id(lin.weight)] = wb
+        t_off, t_num, t_grp, t_rows, t_cols, t_sh, t_ld = [], [], [], [], [], [], []
+        for p, o, g in zip(self.params, self.offsets, self.param_group):
+            t_off.append(o)
+            t_num.append(p.numel())
+            t_grp.append(g)
+            sh = shadows.get(id(p))
+            t_rows.append(p.shape[0] if sh is not None else 1)
+            t_cols.append(p.shape[1] if sh is not None else p.numel())
+            t_sh.append(sh)
+            t_ld.append(sh.shape[1] if sh is not None else 0)
+        t_off.append(self.n_params)
+        t_num.append(_TAIL)
+        t_grp.append(-1)
+        t_rows.append(1)
+        t_cols.append(_TAIL)
+        t_sh.append(None)
+        t_ld.append(0)
+        self.adam_tensors, self.adam_chunks, self.adam_nchunks = ext().make_adam_plan(
+            t_off, t_num, t_grp, t_rows, t_cols, t_sh, t_ld, self.flat
+        )
+        self.adam_grid = ext().adam_grid(self.device.index)
+        self.norm_partial = torch.zeros(self.adam_grid * 4, **f32)
+        self.out_norms = torch.zeros(4, **f32)
+        opt = alg.optimizer
+        group0 = opt.param_groups[0]
+        b1, b2 = group0.get("betas", (0.9, 0.999))
+        self.betas = (float(b1), float(b2))
+        self.adam_eps = float(group0.get("eps", 1e-8))
+        if float(group0.get("weight_decay", 0.0)) != 0.0 or group0.get("amsgrad", False):
+            raise ValueError("fused Adam supports weight_decay=0 and amsgrad=False")
+
+        # ---- normaliser statistics scratch ----
+        self.stats_chunks = ext().colstats_chunks(self.total)
+        self.colstats_partial = {
+            "actor": torch.zeros(2 * self.stats_chunks * self.Da, dtype=torch.float64, device=dev),
+            "critic": torch.zeros(2 * self.stats_chunks * self.Dc, dtype=torch.float64, device=dev),
+        }
+
+        # ---- data parallel ----
+        self.world = alg.gpu_world_size
+        self.rank = alg.gpu_global_rank
+        self.comm = None
+        if self.world > 1:
+            from ..parallel import PeerExchange
+
+            self.comm = PeerExchange.create(self.send, rank=self.rank, world=self.world, device=self.device)
+        self.timeout_ns = int(alg.b200_cfg["comm_timeout_ms"] * 1e6)
+        self.use_graphs = bool(alg.b200_cfg["graphs"])
+        self._update_graph = None
+        self._updates_done = 0
+        self.perm_override: torch.Tensor | None = None  # int32 [T*N]: explicit sample order (tests, reproducibility)
+
+    # ---- learning rate -----------------------------------------------------------------------------------------------
+    def learning_rate(self) -> float:
+        return float(self.lr[0].item())
+
+    def set_learning_rate(self, value: float) -> None:
+        self.lr[0].fill_(value)
+
+    def action_std(self) -> torch.Tensor:
+        """Current policy std (for logging): the clamped parameter, or the mean per-row std of the last rollout."""
+        dist = self.actor.distribution
+        if self.hetero:
+            return self.st_std.mean(dim=0)
+        return dist.current_std().detach()
+
+    # ---- normaliser views --------------------------------------------------------------------------------------------
+    @staticmethod
+    def _norm_tensors(model):
+        norm = model.obs_normalizer
+        if isinstance(norm, EmpiricalNormalization):
+            return norm._mean.view(-1), norm._std.view(-1), norm.eps
+        return None, None, 0.0
+
+    def _group_tensors(self, obs, groups):
+        return [obs[g] if obs[g].is_contiguous() else obs[g].contiguous() for g in groups]
+
+    # ---- rollout ------------------------------------------------------------------------------------------------------
+    def act(self, obs) -> torch.Tensor:
+        if self.t >= self.T:
+            raise OverflowError("Rollout buffer overflow! You should call clear() before adding new transitions.")
+        N, t = self.N, self.t
+        rows = slice(t * N, (t + 1) * N)
+        C = ext()
+        mean_a, std_a, eps_a = self._norm_tensors(self.actor)
+        C.prep_obs(self._group_tensors(obs, self.groups_a), self.obs_a[rows], self.Da, self.plan_a.x_roll,
+                   self.plan_a.x_roll.shape[1], mean_a, std_a, eps_a)
+        mean_c, std_c, eps_c = self._norm_tensors(self.critic)
+        store_c = None if self.shared_obs else self.obs_c[rows]
+        C.prep_obs(self._group_tensors(obs, self.groups_c), store_c, self.Dc, self.plan_c.x_roll,
+                   self.plan_c.x_roll.shape[1], mean_c, std_c, eps_c)
+        pa = self.plan_a
+        pa.forward(pa.x_roll, pa.h_roll, N, pa.out_roll, pa.out_roll.shape[1], self.status)
+        dist = self.actor.distribution
+        std_param = None if self.hetero else (dist.std_param if dist.std_type == "scalar" else dist.log_std_param)
+        C.gaussian_sample(pa.out_roll, pa.out_roll.shape[1], N, self.A, self.hetero, self.log_std,
+                          None if std_param is None else std_param.data, self.std_range[0], self.std_range[1],
+                          self.log_std_range[0], self.log_std_range[1], self.seed, self.rng_counter, self.rng_ticket,
+                          self.st_actions[rows], self.st_mean[rows], self.st_std[rows], self.st_logp[rows],
+                          self.actions_out)
+        pc = self.plan_c
+        pc.forward(pc.x_roll, pc.h_roll, N, self.st_values[rows].view(N, 1), 1, self.status)
+        return self.actions_out
+
+    def process_env_step(self, obs, rewards, dones, extras) -> None:
+        N, t = self.N, self.t
+        rows = slice(t * N, (t + 1) * N)
+        timeouts = extras.get("time_outs") if isinstance(extras, dict) else None
+        if timeouts is not None:
+            timeouts = timeouts.to(self.device).reshape(-1)
+        ext().process_step(rewards.reshape(-1).float(), None, dones.reshape(-1), timeouts, self.st_values[rows],
+                           self.alg.gamma, self.st_rewards[rows], self.st_dones[rows], self.nonfinite)
+        self.t += 1
+
+    def check_finite(self, obs, rewards) -> None:
+        """Non-finite rewards are flagged on the device by ``process_step``; nothing to do per step."""
+
+    def raise_if_nonfinite(self) -> None:
+        if int(self.nonfinite.item()) != 0:
+            self.nonfinite.zero_()
+            raise ValueError("The rewards returned by the environment contain NaN or Inf values.")
+
+    def compute_returns(self, obs) -> None:
+        C = ext()
+        mean_c, std_c, eps_c = self._norm_tensors(self.critic)
+        pc = self.plan_c
+        C.prep_obs(self._group_tensors(obs, self.groups_c), None, self.Dc, pc.x_roll, pc.x_roll.shape[1], mean_c,
+                   std_c, eps_c)
+        pc.forward(pc.x_roll, pc.h_roll, self.N, self.last_values.view(self.N, 1), 1, self.status)
+        C.gae(self.st_rewards, self.st_dones, self.st_values, self.last_values, self.st_returns, self.st_adv, self.T,
+              self.N, self.alg.gamma, self.alg.lam, self.gae_partial)
+        if self.total > 1:
+            C.adv_normalize(self.st_adv, self.gae_partial, ext().gae_blocks(self.N))
+        self.t = 0
+
+    # ---- update -------------------------------------------------------------------------------------------------------
+    def _minibatch(self, i: int) -> None:
+        C = ext()
+        start = i * self.total // self.M
+        B = (i + 1) * self.total // self.M - start
+        pa, pc = self.plan_a, self.plan_c
+        mean_a, std_a, eps_a = self._norm_tensors(self.actor)
+        mean_c, std_c, eps_c = self._norm_tensors(self.critic)
+        if eps_a != eps_c and mean_a is not None and mean_c is not None:
+            raise ValueError("actor and critic normalisers must share eps")
+        eps = eps_a if mean_a is not None else eps_c
+        idx_in = None if self.perm_override is None else self.perm_override[start : start + B]
+        C.gather_minibatch(B, start, self.total, self.perm_key, self.half_bits, idx_in, self.idx,
+                           [self.obs_a, self.obs_c], [mean_a, mean_c], [std_a, std_c], eps,
+                           [pa.x_train, pc.x_train], [pa.x_train.shape[1], pc.x_train.shape[1]], self.status)
+        pa.forward(pa.x_train, pa.h_train, B, pa.out_train, pa.out_train.shape[1], self.status)
+        pc.forward(pc.x_train, pc.h_train, B, self.value_train, 1, self.status)
+        dist = self.actor.distribution
+        std_param = None if self.hetero else (dist.std_param if dist.std_type == "scalar" else dist.log_std_param)
+        alg = self.alg
+        C.ppo_loss(B, self.A, self.hetero, self.log_std, pa.out_train, pa.out_train.shape[1], self.value_train, 1,
+                   None if std_param is None else std_param.data, self.std_range[0], self.std_range[1],
+                   self.log_std_range[0], self.log_std_range[1], self.idx, self.st_actions, self.st_mean, self.st_std,
+                   self.st_logp, self.st_adv, self.st_returns, self.st_values, None, alg.clip_param,
+                   alg.value_loss_coef, alg.entropy_coef, alg.use_clipped_value_loss, pa.d_head, pa.d_head.shape[1],
+                   self.d_value, self.d_value.shape[1], self.stats_partial, self.dhead_colsum, self.dvalue_colsum,
+                   None if self.hetero else self.dstd_partial)
+        pa.backward(B, self.status)
+        pc.backward(B, self.status)
+        C.reduce_segments(self.reduce_plan, self.reduce_nseg, self.reduce_chunks, self.send[0], self.send[1],
+                          self.epoch)
+        adaptive = alg.desired_kl is not None and alg.schedule == "adaptive"
+        kl = self.grads[self.n_params + 3 : self.n_params + 4]
+        peers = self.comm.peer_send if self.comm is not None else None
+        flags = self.comm.peer_flags if self.comm is not None else None
+        C.adam_step(self.flat, self.send[0], self.send[1], self.grads, self.exp_avg, self.exp_avg_sq,
+                    self.adam_tensors, self.adam_chunks, self.adam_nchunks,
+                    [alg.max_grad_norm, alg.max_grad_norm], [self.betas[0]] * 2, [self.betas[1]] * 2,
+                    [self.adam_eps] * 2, [0, 0], self.lr, None, self.step, adaptive, kl,
+                    float(alg.desired_kl or 0.0), 1e-5, 1e-2, self.world, self.rank, peers, flags, self.epoch,
+                    self.timeout_ns, self.norm_partial, self.barrier, self.status, self.out_norms, self.adam_grid)
+        self.loss_acc.add_(self.grads[self.n_params : self.n_params + _TAIL])
+
+    def _normalizer_updates(self) -> None:
+        C = ext()
+        for name, model, obs, D in (("actor", self.actor, self.obs_a, self.Da), ("critic", self.critic, self.obs_c,
+                                                                                  self.Dc)):
+            norm = model.obs_normalizer
+            if not isinstance(norm, EmpiricalNormalization) or not model.obs_normalization or not norm.training:
+                continue
+            partial = self.colstats_partial[name]
+            C.colstats(obs, self.total, obs.shape[1], D, partial)
+            if self.comm is not None:
+                partial = self.comm.allreduce_moments(partial)
+                rows = self.total * self.world
+            else:
+                rows = self.total
+            until = -1 if norm.until is None else int(norm.until)
+            C.norm_update(partial, self.stats_chunks, rows, D, norm._mean.view(-1), norm._var.view(-1),
+                          norm._std.view(-1), norm.count, until, None)
+
+    def _update_body(self) -> None:
+        ext().counter_add(self.perm_key, 1)
+        self.loss_acc.zero_()
+        for _ in range(self.E):
+            for i in range(self.M):
+                self._minibatch(i)
+        self._normalizer_updates()
+
+    def update(self) -> dict[str, float]:
+        if self.use_graphs and self._updates_done >= 1 and self.comm is None:
+            if self._update_graph is None:
+                self._update_graph = self._capture(self._update_body)
+            self._update_graph.replay()
+        else:
+            self._update_body()
+        self._updates_done += 1
+        stats = (self.loss_acc / float(self.E * self.M)).tolist()
+        self._check_status()
+        return {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
+
+    def _capture(self, fn):
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                fn()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        return g
+
+    def _check_status(self) -> None:
+        st = self.status.tolist()
+        if st[0] != 0:
+            self.status.zero_()
+            from ..parallel import CommTimeoutError
+
+            raise CommTimeoutError(f"device status error code={st[0]} site={st[1]} block={st[2]} count={st[3]}")
+
+    # ---- rollout import (tests / external collectors) -------------------------------------------------------------------
+    def load_rollout(self, storage) -> None:
+        """Copy a filled :class:`RolloutStorage` (``[T, N, ...]`` tensors, returns/advantages computed) into the arena."""
+        T, N = self.T, self.N
+        obs = storage.observations.flatten(0, 1)
+        self.obs_a.copy_(torch.cat([obs[g] for g in self.groups_a], dim=-1))
+        if not self.shared_obs:
+            self.obs_c.copy_(torch.cat([obs[g] for g in self.groups_c], dim=-1))
+        mean, std = storage.distribution_params[0], storage.distribution_params[1]
+        self.st_actions.copy_(storage.actions.reshape(T * N, -1))
+        self.st_mean.copy_(mean.reshape(T * N, -1))
+        self.st_std.copy_(std.reshape(T * N, -1).expand(T * N, self.A))
+        self.st_logp.copy_(storage.actions_log_prob.reshape(-1))
+        self.st_values.copy_(storage.values.reshape(-1))
+        self.st_rewards.copy_(storage.rewards.reshape(-1))
+        self.st_dones.copy_(storage.dones.reshape(-1).float())
+        self.st_returns.copy_(storage.returns.reshape(-1))
+        self.st_adv.copy_(storage.advantages.reshape(-1))
+
+    # ---- checkpoints --------------------------------------------------------------------------------------------------
+    def sync_to_torch(self) -> None:
+        """Expose the device optimizer state through the ``torch.optim.Adam`` object (parameters are already views)."""
+        opt = self.alg.optimizer
+        steps = self.step.tolist()
+        for p, o, g in zip(self.params, self.offsets, self.param_group):
+            n = p.numel()
+            opt.state[p] = {
+                "step": torch.tensor(float(steps[g])),
+                "exp_avg": self.exp_avg[o : o + n].view_as(p),
+                "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p),
+            }
+        lr = self.learning_rate()
+        for group in opt.param_groups:
+            group["lr"] = lr
+        self.alg._learning_rate = lr
+
+    def sync_from_torch(self) -> None:
+        """Pull loaded weights / optimizer state into the device arena and refresh the bf16 shadows."""
+        opt = self.alg.optimizer
+        for p, o in zip(self.params, self.offsets):
+            n = p.numel()
+            if p.data.data_ptr() != self.flat[o : o + n].data_ptr():
+                self.flat[o : o + n].copy_(p.data.reshape(-1))
+                p.data = self.flat[o : o + n].view_as(p)
+            st = opt.state.get(p)
+            if st:
+                self.exp_avg[o : o + n].copy_(st["exp_avg"].reshape(-1))
+                self.exp_avg_sq[o : o + n].copy_(st["exp_avg_sq"].reshape(-1))
+                self.step.fill_(int(float(st["step"])))
+                opt.state[p] = {"step": st["step"], "exp_avg": self.exp_avg[o : o + n].view_as(p),
+                                "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p)}
+        self.lr.fill_(float(opt.param_groups[0]["lr"]))
+        self.plan_a.refresh_shadows()
+        self.plan_c.refresh_shadows()
+
+    # ---- data parallel ------------------------------------------------------------------------------------------------
+    def broadcast_parameters(self) -> None:
+        """Make every rank start from rank 0's parameters and normaliser buffers."""
+        if self.comm is not None:
+            self.comm.broadcast_(self.flat)
+            for model in (self.actor, self.critic):
+                for b in model.buffers():
+                    self.comm.broadcast_(b)
+        else:
+            for model in (self.actor, self.critic):
+                for t in model.state_dict().values():
+                    torch.distributed.broadcast(t, src=0)
+        self.plan_a.refresh_shadows()
+        self.plan_c.refresh_shadows()
+
+    # ---- captured rollout (graph-capturable environments) -------------------------------------------------------------
+    def can_capture_rollout(self, env, cfg) -> bool:
+        return False
+
+    def run_captured_rollout(self, env, logger, cfg):  # pragma: no cover - enabled with can_capture_rollout
+        raise NotImplementedError
+
+
+__all__ = ["PPOEngine"]

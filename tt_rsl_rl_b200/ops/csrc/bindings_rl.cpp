@@ -1,4 +1,453 @@
-// Python bindings of the RL kernels (rollout, GAE, gather, loss, optimizer, normalizer).
-#include "kernels.cuh"
+// Python bindings of the RL kernels. Tensors are validated for device and dtype; descriptor tables ("plans") are
+// built once on the host and copied to persistent device tensors so launches stay capturable in CUDA graphs.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
 
-void rlb_register_kernels(pybind11::module& m) { (void)m; }
+#include <vector>
+
+#include "kernels.cuh"
+#include "rl_kernels.cuh"
+
+namespace {
+
+using torch::Tensor;
+using OptT = c10::optional<Tensor>;
+
+cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
+
+void ok(cudaError_t e, const char* what) { TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e)); }
+
+template <typename T>
+T* P(const OptT& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+template <typename T>
+T* P(const Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+
+void check_f32(const Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32, n, " must be a CUDA float32 tensor");
+}
+void check_bf16(const Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16, n, " must be a CUDA bfloat16 tensor");
+}
+
+int flag_dtype(const Tensor& t) {
+  if (t.scalar_type() == torch::kFloat32) return 0;
+  if (t.scalar_type() == torch::kBool || t.scalar_type() == torch::kUInt8) return 1;
+  if (t.scalar_type() == torch::kInt64) return 2;
+  TORCH_CHECK(false, "flag tensors must be float32, bool, uint8 or int64");
+  return 0;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+void prep_obs(const std::vector<Tensor>& srcs, const OptT& store, int64_t ld_store, const Tensor& x, int64_t ld_x,
+              const OptT& mean, const OptT& std, double eps) {
+  TORCH_CHECK(!srcs.empty() && srcs.size() <= rlb::kMaxObsGroups, "prep_obs: 1..4 observation groups");
+  check_bf16(x, "x");
+  rlb::PrepObsArgs a{};
+  a.groups = static_cast<int>(srcs.size());
+  a.rows = static_cast<int>(srcs[0].size(0));
+  int D = 0;
+  for (size_t g = 0; g < srcs.size(); ++g) {
+    check_f32(srcs[g], "observation group");
+    TORCH_CHECK(srcs[g].dim() == 2 && srcs[g].size(0) == a.rows && srcs[g].stride(1) == 1, "bad observation group");
+    a.src[g] = P<const float>(srcs[g]);
+    a.src_ld[g] = static_cast<int>(srcs[g].stride(0));
+    a.width[g] = static_cast<int>(srcs[g].size(1));
+    D += a.width[g];
+  }
+  TORCH_CHECK(ld_x >= D && x.numel() >= (a.rows - 1) * ld_x + D, "prep_obs: x too small");
+  a.store = P<float>(store);
+  if (a.store) TORCH_CHECK(ld_store >= D && store->numel() >= (a.rows - 1) * ld_store + D, "prep_obs: store too small");
+  a.ld_store = static_cast<int>(ld_store);
+  a.x = x.data_ptr();
+  a.ld_x = static_cast<int>(ld_x);
+  a.mean = P<const float>(mean);
+  a.std = P<const float>(std);
+  a.eps = static_cast<float>(eps);
+  ok(rlb::prep_obs(a, cur()), "prep_obs");
+}
+
+void gaussian_sample(const Tensor& head, int64_t ld_head, int64_t rows, int64_t A, bool hetero, bool log_std,
+                     const OptT& std_param, double std_lo, double std_hi, double log_lo, double log_hi, int64_t seed,
+                     const Tensor& counter, const Tensor& ticket, const Tensor& actions, const Tensor& out_mean,
+                     const Tensor& out_std, const Tensor& out_logp, const OptT& actions_copy) {
+  check_f32(head, "head");
+  TORCH_CHECK(counter.scalar_type() == torch::kInt64 && ticket.scalar_type() == torch::kInt32, "counter/ticket dtype");
+  TORCH_CHECK(actions.numel() >= rows * A && out_mean.numel() >= rows * A && out_std.numel() >= rows * A &&
+                  out_logp.numel() >= rows,
+              "gaussian_sample: outputs too small");
+  TORCH_CHECK(hetero || (std_param.has_value() && std_param->numel() >= A), "gaussian_sample: std_param required");
+  rlb::SampleArgs a{};
+  a.head = P<const float>(head);
+  a.ld_head = static_cast<int>(ld_head);
+  a.rows = static_cast<int>(rows);
+  a.A = static_cast<int>(A);
+  a.hetero = hetero;
+  a.log_std = log_std;
+  a.std_param = P<const float>(std_param);
+  a.std_lo = static_cast<float>(std_lo);
+  a.std_hi = static_cast<float>(std_hi);
+  a.log_std_lo = static_cast<float>(log_lo);
+  a.log_std_hi = static_cast<float>(log_hi);
+  a.seed = static_cast<uint64_t>(seed);
+  a.counter = reinterpret_cast<uint64_t*>(counter.data_ptr());
+  a.ticket = reinterpret_cast<unsigned int*>(ticket.data_ptr());
+  a.actions = P<float>(actions);
+  a.out_mean = P<float>(out_mean);
+  a.out_std = P<float>(out_std);
+  a.out_logp = P<float>(out_logp);
+  a.actions_copy = P<float>(actions_copy);
+  ok(rlb::gaussian_sample(a, cur()), "gaussian_sample");
+}
+
+void process_step(const Tensor& rewards, const OptT& intrinsic, const Tensor& dones, const OptT& timeouts,
+                  const Tensor& values_slot, double gamma, const Tensor& rewards_slot, const Tensor& dones_slot,
+                  const OptT& nonfinite) {
+  check_f32(rewards, "rewards");
+  const int64_t n = rewards.numel();
+  TORCH_CHECK(dones.numel() == n && rewards_slot.numel() >= n && dones_slot.numel() >= n, "process_step: sizes");
+  rlb::ProcessArgs a{};
+  a.rewards = P<const float>(rewards);
+  a.intrinsic = P<const float>(intrinsic);
+  a.dones = dones.data_ptr();
+  a.dones_dtype = flag_dtype(dones);
+  if (timeouts.has_value() && timeouts->defined()) {
+    TORCH_CHECK(timeouts->numel() == n, "process_step: time_outs size");
+    a.timeouts = timeouts->data_ptr();
+    a.timeouts_dtype = flag_dtype(*timeouts);
+  }
+  a.values_slot = P<const float>(values_slot);
+  a.gamma = static_cast<float>(gamma);
+  a.rows = static_cast<int>(n);
+  a.rewards_slot = P<float>(rewards_slot);
+  a.dones_slot = P<float>(dones_slot);
+  a.nonfinite_flag = P<unsigned int>(nonfinite);
+  ok(rlb::process_step(a, cur()), "process_step");
+}
+
+int64_t gae_blocks(int64_t N) { return rlb::gae_blocks(static_cast<int>(N)); }
+
+void gae(const Tensor& rewards, const Tensor& dones, const Tensor& values, const Tensor& last_values,
+         const Tensor& returns, const Tensor& advantages, int64_t T, int64_t N, double gamma, double lam,
+         const Tensor& partial) {
+  for (const Tensor* t : {&rewards, &dones, &values, &returns, &advantages}) {
+    check_f32(*t, "gae buffer");
+    TORCH_CHECK(t->numel() >= T * N, "gae: buffer too small");
+  }
+  TORCH_CHECK(partial.scalar_type() == torch::kFloat64 && partial.numel() >= 2 * rlb::gae_blocks(N), "gae: partial");
+  rlb::GaeArgs a{P<const float>(rewards), P<const float>(dones), P<const float>(values), P<const float>(last_values),
+                 P<float>(returns),       P<float>(advantages),    static_cast<int>(T),   static_cast<int>(N),
+                 static_cast<float>(gamma), static_cast<float>(lam), P<double>(partial)};
+  ok(rlb::gae(a, cur()), "gae");
+}
+
+void adv_normalize(const Tensor& adv, const Tensor& partial, int64_t parts) {
+  check_f32(adv, "adv");
+  ok(rlb::adv_normalize(P<float>(adv), adv.numel(), P<const double>(partial), static_cast<int>(parts), cur()),
+     "adv_normalize");
+}
+
+int64_t feistel_half_bits(int64_t total) { return rlb::feistel_half_bits(total); }
+int64_t feistel_permute(int64_t i, int64_t n, int64_t half_bits, int64_t key) {
+  return rlb::feistel_permute_host(static_cast<uint32_t>(i), static_cast<uint32_t>(n), static_cast<uint32_t>(half_bits),
+                                   static_cast<uint32_t>(key));
+}
+
+void gather_minibatch(int64_t B, int64_t offset, int64_t total, const OptT& key, int64_t half_bits, const OptT& idx_in,
+                      const Tensor& idx_out, const std::vector<Tensor>& obs, const std::vector<OptT>& means,
+                      const std::vector<OptT>& stds, double eps, const std::vector<Tensor>& xs,
+                      const std::vector<int64_t>& ld_xs, const OptT& status) {
+  TORCH_CHECK(obs.size() >= 1 && obs.size() <= 2 && xs.size() == obs.size() && ld_xs.size() == obs.size() &&
+                  means.size() == obs.size() && stds.size() == obs.size(),
+              "gather_minibatch: 1 or 2 models");
+  TORCH_CHECK(idx_out.scalar_type() == torch::kInt32 && idx_out.numel() >= B, "gather_minibatch: idx_out");
+  TORCH_CHECK(total < (1ll << 31), "gather_minibatch: rollout too large");
+  rlb::GatherArgs a{};
+  a.B = static_cast<int>(B);
+  a.offset = offset;
+  a.total = total;
+  a.key_ptr = P<const uint32_t>(key);
+  a.half_bits = static_cast<int>(half_bits);
+  a.idx_in = P<const int>(idx_in);
+  a.idx_out = P<int>(idx_out);
+  a.models = static_cast<int>(obs.size());
+  for (size_t m = 0; m < obs.size(); ++m) {
+    check_f32(obs[m], "obs");
+    check_bf16(xs[m], "x");
+    TORCH_CHECK(obs[m].dim() == 2 && obs[m].size(0) >= total, "gather_minibatch: obs must be [rows, dim]");
+    a.obs[m] = P<const float>(obs[m]);
+    a.obs_ld[m] = static_cast<int>(obs[m].stride(0));
+    a.dim[m] = static_cast<int>(obs[m].size(1));
+    a.mean[m] = P<const float>(means[m]);
+    a.std[m] = P<const float>(stds[m]);
+    a.x[m] = xs[m].data_ptr();
+    a.ld_x[m] = static_cast<int>(ld_xs[m]);
+    TORCH_CHECK(xs[m].numel() >= (B - 1) * ld_xs[m] + a.dim[m], "gather_minibatch: x too small");
+  }
+  a.eps = static_cast<float>(eps);
+  a.status = P<unsigned int>(status);
+  ok(rlb::gather_minibatch(a, cur()), "gather_minibatch");
+}
+
+int64_t ppo_loss_blocks(int64_t B) { return rlb::ppo_loss_blocks(static_cast<int>(B)); }
+
+void ppo_loss(int64_t B, int64_t A, bool hetero, bool log_std, const Tensor& head, int64_t ld_head, const Tensor& value,
+              int64_t ld_value, const OptT& std_param, double std_lo, double std_hi, double log_lo, double log_hi,
+              const Tensor& idx, const Tensor& st_actions, const Tensor& st_mean, const Tensor& st_std,
+              const Tensor& st_logp, const Tensor& st_adv, const Tensor& st_ret, const Tensor& st_val,
+              const OptT& adv_override, double clip, double value_coef, double entropy_coef, bool clipped_value,
+              const Tensor& d_head, int64_t ld_dhead, const Tensor& d_value, int64_t ld_dvalue,
+              const Tensor& stats_partial, const Tensor& dhead_colsum, const Tensor& dvalue_colsum,
+              const OptT& dstd_partial) {
+  check_f32(head, "head");
+  check_f32(value, "value");
+  check_bf16(d_head, "d_head");
+  check_bf16(d_value, "d_value");
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.numel() >= B, "ppo_loss: idx");
+  const int64_t blocks = rlb::ppo_loss_blocks(static_cast<int>(B));
+  const int64_t head_cols = hetero ? 2 * A : A;
+  TORCH_CHECK(ld_dhead >= head_cols && d_head.numel() >= B * ld_dhead, "ppo_loss: d_head too small");
+  TORCH_CHECK(d_value.numel() >= B * ld_dvalue, "ppo_loss: d_value too small");
+  TORCH_CHECK(stats_partial.numel() >= blocks * 4 && dhead_colsum.numel() >= blocks * head_cols &&
+                  dvalue_colsum.numel() >= blocks,
+              "ppo_loss: partial buffers too small");
+  TORCH_CHECK(hetero || (std_param.has_value() && dstd_partial.has_value()), "ppo_loss: std_param/dstd_partial");
+  rlb::PpoLossArgs a{};
+  a.B = static_cast<int>(B);
+  a.A = static_cast<int>(A);
+  a.hetero = hetero;
+  a.log_std = log_std;
+  a.head = P<const float>(head);
+  a.ld_head = static_cast<int>(ld_head);
+  a.value = P<const float>(value);
+  a.ld_value = static_cast<int>(ld_value);
+  a.std_param = P<const float>(std_param);
+  a.std_lo = static_cast<float>(std_lo);
+  a.std_hi = static_cast<float>(std_hi);
+  a.log_std_lo = static_cast<float>(log_lo);
+  a.log_std_hi = static_cast<float>(log_hi);
+  a.idx = P<const int>(idx);
+  a.st_actions = P<const float>(st_actions);
+  a.st_mean = P<const float>(st_mean);
+  a.st_std = P<const float>(st_std);
+  a.st_logp = P<const float>(st_logp);
+  a.st_adv = P<const float>(st_adv);
+  a.st_ret = P<const float>(st_ret);
+  a.st_val = P<const float>(st_val);
+  a.adv_override = P<const float>(adv_override);
+  a.clip = static_cast<float>(clip);
+  a.value_coef = static_cast<float>(value_coef);
+  a.entropy_coef = static_cast<float>(entropy_coef);
+  a.clipped_value = clipped_value;
+  a.d_head = d_head.data_ptr();
+  a.ld_dhead = static_cast<int>(ld_dhead);
+  a.d_value = d_value.data_ptr();
+  a.ld_dvalue = static_cast<int>(ld_dvalue);
+  a.stats_partial = P<float>(stats_partial);
+  a.dhead_colsum = P<float>(dhead_colsum);
+  a.dvalue_colsum = P<float>(dvalue_colsum);
+  a.dstd_partial = P<float>(dstd_partial);
+  ok(rlb::ppo_loss(a, cur()), "ppo_loss");
+}
+
+// ---- reduction plan --------------------------------------------------------------------------------------------
+// srcs[i]: partial buffer [parts_i, n_i]; dst_offsets[i]: offset into the flat gradient vector.
+std::tuple<Tensor, int64_t, int64_t> make_reduce_plan(const std::vector<Tensor>& srcs, const std::vector<int64_t>& parts,
+                                                      const std::vector<int64_t>& ns,
+                                                      const std::vector<int64_t>& dst_offsets) {
+  TORCH_CHECK(srcs.size() == parts.size() && parts.size() == ns.size() && ns.size() == dst_offsets.size() &&
+                  !srcs.empty(),
+              "make_reduce_plan: list sizes");
+  std::vector<rlb::ReduceSegment> segs(srcs.size());
+  int chunks = 0;
+  for (size_t i = 0; i < srcs.size(); ++i) {
+    check_f32(srcs[i], "partial");
+    TORCH_CHECK(srcs[i].numel() >= parts[i] * ns[i], "make_reduce_plan: partial buffer too small");
+    segs[i].src = P<const float>(srcs[i]);
+    segs[i].dst_offset = dst_offsets[i];
+    segs[i].n = ns[i];
+    segs[i].parts = static_cast<int>(parts[i]);
+    segs[i].first_chunk = chunks;
+    chunks += static_cast<int>((ns[i] + rlb::kReduceChunk - 1) / rlb::kReduceChunk);
+  }
+  auto dev = torch::empty({static_cast<int64_t>(segs.size() * sizeof(rlb::ReduceSegment))},
+                          torch::dtype(torch::kUInt8).device(srcs[0].device()));
+  ok(cudaMemcpy(dev.data_ptr(), segs.data(), segs.size() * sizeof(rlb::ReduceSegment), cudaMemcpyHostToDevice),
+     "make_reduce_plan copy");
+  return {dev, static_cast<int64_t>(segs.size()), static_cast<int64_t>(chunks)};
+}
+
+void reduce_segments(const Tensor& plan, int64_t nseg, int64_t chunks, const Tensor& send0, const Tensor& send1,
+                     const OptT& epoch) {
+  check_f32(send0, "send0");
+  check_f32(send1, "send1");
+  ok(rlb::reduce_segments(reinterpret_cast<const rlb::ReduceSegment*>(plan.data_ptr()), static_cast<int>(nseg),
+                          static_cast<int>(chunks), P<float>(send0), P<float>(send1), P<const unsigned int>(epoch),
+                          cur()),
+     "reduce_segments");
+}
+
+// ---- Adam plan -------------------------------------------------------------------------------------------------
+// Per tensor: offset, numel, group, rows, cols, shadow (bf16 tensor or None), shadow_ld.
+std::tuple<Tensor, Tensor, int64_t> make_adam_plan(const std::vector<int64_t>& offsets, const std::vector<int64_t>& numels,
+                                                   const std::vector<int64_t>& groups, const std::vector<int64_t>& rows,
+                                                   const std::vector<int64_t>& cols, const std::vector<OptT>& shadows,
+                                                   const std::vector<int64_t>& shadow_lds, const Tensor& like) {
+  const size_t n = offsets.size();
+  TORCH_CHECK(numels.size() == n && groups.size() == n && rows.size() == n && cols.size() == n && shadows.size() == n &&
+                  shadow_lds.size() == n,
+              "make_adam_plan: list sizes");
+  std::vector<rlb::AdamTensor> ts(n);
+  std::vector<rlb::AdamChunk> chunks;
+  for (size_t i = 0; i < n; ++i) {
+    ts[i].offset = offsets[i];
+    ts[i].numel = numels[i];
+    ts[i].group = static_cast<int>(groups[i]);
+    ts[i].rows = static_cast<int>(rows[i]);
+    ts[i].cols = static_cast<int>(cols[i]);
+    ts[i].shadow = P<void>(shadows[i]);
+    ts[i].shadow_ld = static_cast<int>(shadow_lds[i]);
+    if (ts[i].shadow) {
+      TORCH_CHECK(shadows[i]->scalar_type() == torch::kBFloat16 && shadows[i]->numel() >= rows[i] * shadow_lds[i] &&
+                      rows[i] * cols[i] == numels[i],
+                  "make_adam_plan: bad shadow");
+    }
+    for (int64_t s = 0; s < numels[i]; s += rlb::kAdamChunk)
+      chunks.push_back({static_cast<int>(i), static_cast<int>(s),
+                        static_cast<int>(std::min<int64_t>(rlb::kAdamChunk, numels[i] - s))});
+  }
+  auto opts = torch::dtype(torch::kUInt8).device(like.device());
+  auto dt = torch::empty({static_cast<int64_t>(n * sizeof(rlb::AdamTensor))}, opts);
+  auto dc = torch::empty({static_cast<int64_t>(chunks.size() * sizeof(rlb::AdamChunk))}, opts);
+  ok(cudaMemcpy(dt.data_ptr(), ts.data(), n * sizeof(rlb::AdamTensor), cudaMemcpyHostToDevice), "adam plan copy");
+  ok(cudaMemcpy(dc.data_ptr(), chunks.data(), chunks.size() * sizeof(rlb::AdamChunk), cudaMemcpyHostToDevice),
+     "adam plan copy");
+  return {dt, dc, static_cast<int64_t>(chunks.size())};
+}
+
+int64_t adam_grid(int64_t device) { return rlb::adam_grid(static_cast<int>(device)); }
+
+void adam_step(const Tensor& params, const Tensor& send0, const Tensor& send1, const Tensor& grads, const Tensor& exp_avg,
+               const Tensor& exp_avg_sq, const Tensor& tensors, const Tensor& chunks, int64_t nchunks,
+               const std::vector<double>& max_norm, const std::vector<double>& beta1, const std::vector<double>& beta2,
+               const std::vector<double>& eps, const std::vector<int64_t>& lr_index, const Tensor& lr,
+               const OptT& lr_out_slot, const Tensor& step,
+               bool adaptive, const OptT& kl_mean, double desired_kl, double lr_min, double lr_max, int64_t world,
+               int64_t rank, const OptT& peer_send, const OptT& peer_flags, const Tensor& epoch, int64_t timeout_ns,
+               const Tensor& norm_partial, const Tensor& barrier, const OptT& status, const OptT& out_norms,
+               int64_t grid) {
+  for (const Tensor* t : {&params, &send0, &send1, &grads, &exp_avg, &exp_avg_sq}) check_f32(*t, "adam buffer");
+  const size_t ng = max_norm.size();
+  TORCH_CHECK(ng >= 1 && ng <= rlb::kAdamMaxGroups && beta1.size() == ng && beta2.size() == ng && eps.size() == ng,
+              "adam_step: groups");
+  TORCH_CHECK(lr.numel() >= static_cast<int64_t>(ng) && step.scalar_type() == torch::kInt64, "adam_step: lr/step");
+  TORCH_CHECK(norm_partial.numel() >= grid * rlb::kAdamMaxGroups, "adam_step: norm_partial too small");
+  TORCH_CHECK(world == 1 || (peer_send.has_value() && peer_flags.has_value()), "adam_step: peers required");
+  rlb::AdamArgs a{};
+  a.params = P<float>(params);
+  a.send[0] = P<float>(send0);
+  a.send[1] = P<float>(send1);
+  a.grads = P<float>(grads);
+  a.exp_avg = P<float>(exp_avg);
+  a.exp_avg_sq = P<float>(exp_avg_sq);
+  a.tensors = reinterpret_cast<const rlb::AdamTensor*>(tensors.data_ptr());
+  a.chunks = reinterpret_cast<const rlb::AdamChunk*>(chunks.data_ptr());
+  a.nchunks = static_cast<int>(nchunks);
+  a.ngroups = static_cast<int>(ng);
+  for (size_t g = 0; g < ng; ++g) {
+    a.max_norm[g] = static_cast<float>(max_norm[g]);
+    a.beta1[g] = static_cast<float>(beta1[g]);
+    a.beta2[g] = static_cast<float>(beta2[g]);
+    a.eps[g] = static_cast<float>(eps[g]);
+    TORCH_CHECK(g < lr_index.size() && lr_index[g] >= 0 && lr_index[g] < static_cast<int64_t>(ng), "adam_step: lr_index");
+    a.lr_index[g] = static_cast<int>(lr_index[g]);
+  }
+  a.lr = P<float>(lr);
+  a.lr_out_slot = P<float>(lr_out_slot);
+  a.step = reinterpret_cast<long long*>(step.data_ptr());
+  a.adaptive = adaptive;
+  a.kl_mean = P<const float>(kl_mean);
+  TORCH_CHECK(!adaptive || a.kl_mean, "adam_step: adaptive schedule needs kl_mean");
+  a.desired_kl = static_cast<float>(desired_kl);
+  a.lr_min = static_cast<float>(lr_min);
+  a.lr_max = static_cast<float>(lr_max);
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.peer_send = P<float* const>(peer_send);
+  a.peer_flags = P<unsigned int* const>(peer_flags);
+  a.epoch = reinterpret_cast<unsigned int*>(epoch.data_ptr());
+  a.timeout_ns = static_cast<uint64_t>(timeout_ns);
+  a.norm_partial = P<float>(norm_partial);
+  a.barrier = reinterpret_cast<unsigned int*>(barrier.data_ptr());
+  a.status = P<unsigned int>(status);
+  a.out_norms = P<float>(out_norms);
+  ok(rlb::adam_step(a, static_cast<int>(grid), cur()), "adam_step");
+}
+
+int64_t colstats_chunks(int64_t rows) { return rlb::colstats_chunks(rows); }
+
+void colstats(const Tensor& x, int64_t rows, int64_t ld, int64_t dim, const Tensor& partial) {
+  check_f32(x, "x");
+  const int chunks = rlb::colstats_chunks(rows);
+  TORCH_CHECK(partial.scalar_type() == torch::kFloat64 && partial.numel() >= 2LL * chunks * dim, "colstats: partial");
+  TORCH_CHECK(x.numel() >= (rows - 1) * ld + dim, "colstats: x too small");
+  rlb::ColStatsArgs a{P<const float>(x), rows, static_cast<int>(ld), static_cast<int>(dim), P<double>(partial), chunks};
+  ok(rlb::colstats(a, cur()), "colstats");
+}
+
+void norm_update(const Tensor& partial, int64_t chunks, int64_t rows, int64_t dim, const Tensor& mean, const Tensor& var,
+                 const Tensor& std, const Tensor& count, int64_t until, const OptT& moments_out) {
+  TORCH_CHECK(count.scalar_type() == torch::kInt64, "norm_update: count must be int64");
+  check_f32(mean, "mean");
+  check_f32(var, "var");
+  check_f32(std, "std");
+  rlb::NormUpdateArgs a{P<const double>(partial), static_cast<int>(chunks), rows, static_cast<int>(dim),
+                        P<float>(mean),           P<float>(var),            P<float>(std),
+                        reinterpret_cast<long long*>(count.data_ptr()), until, P<double>(moments_out)};
+  ok(rlb::norm_update(a, cur()), "norm_update");
+}
+
+void counter_add(const Tensor& p, int64_t delta) {
+  TORCH_CHECK(p.is_cuda() && p.element_size() == 4, "counter_add: 32-bit counter");
+  ok(rlb::counter_add(reinterpret_cast<unsigned int*>(p.data_ptr()), static_cast<unsigned int>(delta), cur()),
+     "counter_add");
+}
+
+void to_bf16_padded(const Tensor& src, const Tensor& dst, int64_t ld) {
+  check_f32(src, "src");
+  check_bf16(dst, "dst");
+  const int64_t rows = src.size(0), cols = src.numel() / src.size(0);
+  TORCH_CHECK(ld >= cols && dst.numel() >= rows * ld, "to_bf16_padded: dst too small");
+  ok(rlb::to_bf16_padded(P<const float>(src), static_cast<int>(rows), static_cast<int>(cols), dst.data_ptr(),
+                         static_cast<int>(ld), cur()),
+     "to_bf16_padded");
+}
+
+}  // namespace
+
+void rlb_register_kernels(pybind11::module& m) {
+  m.def("prep_obs", &prep_obs);
+  m.def("gaussian_sample", &gaussian_sample);
+  m.def("process_step", &process_step);
+  m.def("gae_blocks", &gae_blocks);
+  m.def("gae", &gae);
+  m.def("adv_normalize", &adv_normalize);
+  m.def("feistel_half_bits", &feistel_half_bits);
+  m.def("feistel_permute", &feistel_permute);
+  m.def("gather_minibatch", &gather_minibatch);
+  m.def("ppo_loss_blocks", &ppo_loss_blocks);
+  m.def("ppo_loss", &ppo_loss);
+  m.def("make_reduce_plan", &make_reduce_plan);
+  m.def("reduce_segments", &reduce_segments);
+  m.def("make_adam_plan", &make_adam_plan);
+  m.def("adam_grid", &adam_grid);
+  m.def("adam_step", &adam_step);
+  m.def("colstats_chunks", &colstats_chunks);
+  m.def("colstats", &colstats);
+  m.def("norm_update", &norm_update);
+  m.def("counter_add", &counter_add);
+  m.def("to_bf16_padded", &to_bf16_padded);
+}

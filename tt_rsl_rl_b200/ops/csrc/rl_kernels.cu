@@ -1,0 +1,880 @@
+// RL kernels for sm_100a: rollout head, environment-step bookkeeping, GAE, minibatch gather, PPO loss, gradient
+// reduction, fused clip + Adam (with the peer-to-peer data-parallel exchange) and the observation normaliser.
+//
+// Determinism: every cross-thread reduction runs in a fixed order (per-block partials, then a fixed-order sum), so a
+// replay of the same inputs is bit-identical and every data-parallel rank computes identical parameters.
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <cstdio>
+
+#include "rl_kernels.cuh"
+#include "sm100_primitives.cuh"
+
+namespace rlb {
+namespace {
+
+constexpr float kLogSqrt2Pi = 0.91893853320467274178f;  // 0.5 * ln(2 * pi)
+
+// ---------------------------------------------------------------------------------------------------------------
+// Philox4x32-10 counter-based generator (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as easy as 1, 2, 3",
+// SC 2011). Multipliers and Weyl key increments are the published Philox4x32 constants.
+// ---------------------------------------------------------------------------------------------------------------
+struct Philox {
+  uint32_t c[4];
+};
+__device__ __forceinline__ Philox philox10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
+                                           uint32_t k1) {
+  Philox r{{c0, c1, c2, c3}};
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const uint32_t hi0 = __umulhi(0xD2511F53u, r.c[0]);
+    const uint32_t lo0 = 0xD2511F53u * r.c[0];
+    const uint32_t hi1 = __umulhi(0xCD9E8D57u, r.c[2]);
+    const uint32_t lo1 = 0xCD9E8D57u * r.c[2];
+    r = Philox{{hi1 ^ r.c[1] ^ k0, lo1, hi0 ^ r.c[3] ^ k1, lo0}};
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return r;
+}
+// uint32 -> uniform in (0, 1)
+__device__ __forceinline__ float u01(uint32_t x) { return (static_cast<float>(x) + 0.5f) * 2.3283064365386963e-10f; }
+// Box-Muller transform of two uniforms into two standard normals.
+__device__ __forceinline__ void box_muller(uint32_t a, uint32_t b, float& n0, float& n1) {
+  const float r = sqrtf(-2.0f * logf(u01(a)));
+  float s, c;
+  sincospif(2.0f * u01(b), &s, &c);
+  n0 = r * c;
+  n1 = r * s;
+}
+
+__device__ __forceinline__ float load_flag(const void* p, int dtype, int i) {
+  if (dtype == 0) return static_cast<const float*>(p)[i] != 0.f ? 1.f : 0.f;
+  if (dtype == 1) return static_cast<const uint8_t*>(p)[i] != 0 ? 1.f : 0.f;
+  return static_cast<const long long*>(p)[i] != 0 ? 1.f : 0.f;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// prep_obs
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void prep_obs_kernel(const PrepObsArgs a, int D) {
+  const long long total = static_cast<long long>(a.rows) * D;
+  for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(e / D);
+    int c = static_cast<int>(e - static_cast<long long>(r) * D);
+    int g = 0;
+    int base = 0;
+#pragma unroll
+    for (int k = 0; k < kMaxObsGroups - 1; ++k) {
+      if (g < a.groups - 1 && c - base >= a.width[g]) {
+        base += a.width[g];
+        ++g;
+      }
+    }
+    const float v = a.src[g][static_cast<size_t>(r) * a.src_ld[g] + (c - base)];
+    if (a.store) a.store[static_cast<size_t>(r) * a.ld_store + c] = v;
+    float y = v;
+    if (a.mean) y = (v - a.mean[c]) / (a.std[c] + a.eps);
+    static_cast<__nv_bfloat16*>(a.x)[static_cast<size_t>(r) * a.ld_x + c] = __float2bfloat16_rn(y);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Gaussian head (rollout): one warp per row, lane j handles actions j, j + 32, ...
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float head_std(float raw, int log_std, float lo, float hi, float llo, float lhi) {
+  return log_std ? expf(fminf(fmaxf(raw, llo), lhi)) : fminf(fmaxf(raw, lo), hi);
+}
+
+// After every block has read the counter, the last block to finish advances it (ticket pattern).
+__device__ __forceinline__ void last_block_advance(uint64_t* counter, unsigned int* ticket) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int done = atomicAdd(ticket, 1u) + 1u;
+    if (done == gridDim.x) {
+      *counter += 1;
+      *ticket = 0u;
+      __threadfence();
+    }
+  }
+}
+
+__global__ void gaussian_sample_kernel(const SampleArgs a) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint64_t offset = *a.counter;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < a.rows; row += gridDim.x * warps) {
+    float logp = 0.f;
+    for (int j0 = 0; j0 < a.A; j0 += 32) {
+      const int j = j0 + lane;
+      // 4 normals per Philox call: counter = (row, action-group of 4, offset lo, offset hi)
+      const int grp = j >> 2;
+      const Philox rnd = philox10(static_cast<uint32_t>(row), static_cast<uint32_t>(grp),
+                                  static_cast<uint32_t>(offset), static_cast<uint32_t>(offset >> 32),
+                                  static_cast<uint32_t>(a.seed), static_cast<uint32_t>(a.seed >> 32));
+      float n0, n1, n2, n3;
+      box_muller(rnd.c[0], rnd.c[1], n0, n1);
+      box_muller(rnd.c[2], rnd.c[3], n2, n3);
+      const int k = j & 3;
+      const float eps = k == 0 ? n0 : k == 1 ? n1 : k == 2 ? n2 : n3;
+      if (j < a.A) {
+        const float* h = a.head + static_cast<size_t>(row) * a.ld_head;
+        const float mu = h[j];
+        const float raw = a.hetero ? h[a.A + j] : a.std_param[j];
+        const float sd = head_std(raw, a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
+        const float act = mu + sd * eps;
+        const size_t o = static_cast<size_t>(row) * a.A + j;
+        a.actions[o] = act;
+        if (a.actions_copy) a.actions_copy[o] = act;
+        a.out_mean[o] = mu;
+        a.out_std[o] = sd;
+        const float z = (act - mu) / sd;
+        logp += -0.5f * z * z - logf(sd) - kLogSqrt2Pi;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) logp += __shfl_xor_sync(0xffffffffu, logp, off);
+    if (lane == 0) a.out_logp[row] = logp;
+  }
+  last_block_advance(a.counter, a.ticket);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// process_step
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void process_step_kernel(const ProcessArgs a) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.rows; i += gridDim.x * blockDim.x) {
+    float r = a.rewards[i];
+    if (a.intrinsic) r += a.intrinsic[i];
+    if (a.timeouts) r += a.gamma * a.values_slot[i] * load_flag(a.timeouts, a.timeouts_dtype, i);
+    if (a.nonfinite_flag && !isfinite(r)) atomicExch(a.nonfinite_flag, 1u);
+    a.rewards_slot[i] = r;
+    a.dones_slot[i] = load_flag(a.dones, a.dones_dtype, i);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// GAE: one thread per environment, reverse scan over T
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kGaeThreads = 256;
+__global__ void gae_kernel(const GaeArgs a) {
+  const int n = blockIdx.x * kGaeThreads + threadIdx.x;
+  double s = 0.0, ss = 0.0;
+  if (n < a.N) {
+    float adv = 0.f;
+    float next_v = a.last_values[n];
+    for (int t = a.T - 1; t >= 0; --t) {
+      const size_t o = static_cast<size_t>(t) * a.N + n;
+      const float v = a.values[o];
+      const float not_done = 1.0f - a.dones[o];
+      const float delta = a.rewards[o] + not_done * a.gamma * next_v - v;
+      adv = delta + not_done * a.gamma * a.lam * adv;
+      const float ret = adv + v;
+      a.returns[o] = ret;
+      const float ad = ret - v;  // advantages = returns - values (as stored upstream)
+      a.advantages[o] = ad;
+      s += ad;
+      ss += static_cast<double>(ad) * ad;
+      next_v = v;
+    }
+  }
+  __shared__ double sh[2][kGaeThreads / 32];
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, off);
+    ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sh[0][threadIdx.x >> 5] = s;
+    sh[1][threadIdx.x >> 5] = ss;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ts = 0, tss = 0;
+    for (int w = 0; w < kGaeThreads / 32; ++w) {
+      ts += sh[0][w];
+      tss += sh[1][w];
+    }
+    a.partial[2 * blockIdx.x] = ts;
+    a.partial[2 * blockIdx.x + 1] = tss;
+  }
+}
+
+__global__ void adv_normalize_kernel(float* adv, long long n, const double* partial, int parts) {
+  __shared__ float stats[2];
+  if (threadIdx.x == 0) {
+    double s = 0, ss = 0;
+    for (int i = 0; i < parts; ++i) {
+      s += partial[2 * i];
+      ss += partial[2 * i + 1];
+    }
+    const double mean = s / static_cast<double>(n);
+    const double var = n > 1 ? fmax((ss - s * mean) / static_cast<double>(n - 1), 0.0) : 0.0;
+    stats[0] = static_cast<float>(mean);
+    stats[1] = static_cast<float>(1.0 / (sqrt(var) + 1e-8));
+  }
+  __syncthreads();
+  const float mean = stats[0], inv = stats[1];
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    adv[i] = (adv[i] - mean) * inv;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Feistel permutation of [0, n): 4-round balanced Feistel network on 2*half_bits bits with cycle walking. A bijection
+// of the padded domain restricted by cycle walking is a bijection of [0, n).
+// ---------------------------------------------------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint32_t mix32(uint32_t x, uint32_t key, uint32_t round) {
+  uint32_t h = x * 0x9E3779B1u ^ (key + round * 0x85EBCA77u);
+  h ^= h >> 15;
+  h *= 0x2C1B3C6Du;
+  h ^= h >> 12;
+  h *= 0x297A2D39u;
+  h ^= h >> 15;
+  return h;
+}
+__host__ __device__ __forceinline__ uint32_t feistel_once(uint32_t x, uint32_t half_bits, uint32_t key) {
+  const uint32_t mask = (1u << half_bits) - 1u;
+  uint32_t L = x >> half_bits, R = x & mask;
+  for (uint32_t r = 0; r < 4; ++r) {
+    const uint32_t nl = R;
+    R = L ^ (mix32(R, key, r) & mask);
+    L = nl;
+  }
+  return (L << half_bits) | R;
+}
+__host__ __device__ __forceinline__ uint32_t feistel_permute(uint32_t i, uint32_t n, uint32_t half_bits, uint32_t key,
+                                                             bool* overflow) {
+  uint32_t x = feistel_once(i, half_bits, key);
+  // Cycle walking terminates (the cycle through i < n returns to [0, n)); the cap only guards against misuse.
+  for (int it = 0; x >= n; ++it) {
+    if (it > (1 << 22)) {
+      *overflow = true;
+      return i;
+    }
+    x = feistel_once(x, half_bits, key);
+  }
+  return x;
+}
+
+__global__ void gather_minibatch_kernel(const GatherArgs a) {
+  // one warp per minibatch row
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t key = a.key_ptr ? *a.key_ptr : 0u;
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < a.B; i += gridDim.x * warps) {
+    int src;
+    if (a.idx_in) {
+      src = a.idx_in[i];
+    } else {
+      bool overflow = false;
+      src = static_cast<int>(feistel_permute(static_cast<uint32_t>(a.offset + i), static_cast<uint32_t>(a.total),
+                                             a.half_bits, key, &overflow));
+      if (overflow && lane == 0) report_error(a.status, kBadShape, 40);
+    }
+    if (lane == 0 && a.idx_out) a.idx_out[i] = src;
+    for (int m = 0; m < a.models; ++m) {
+      const float* o = a.obs[m] + static_cast<size_t>(src) * a.obs_ld[m];
+      __nv_bfloat16* x = static_cast<__nv_bfloat16*>(a.x[m]) + static_cast<size_t>(i) * a.ld_x[m];
+      for (int c = lane; c < a.dim[m]; c += 32) {
+        float v = o[c];
+        if (a.mean[m]) v = (v - a.mean[m][c]) / (a.std[m][c] + a.eps);
+        x[c] = __float2bfloat16_rn(v);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// PPO loss: one warp per row; 8 warps x 8 rows per block
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kLossWarps = 8;
+constexpr int kLossRowsPerWarp = 8;
+constexpr int kLossRowsPerBlock = kLossWarps * kLossRowsPerWarp;
+constexpr int kLossMaxA = 64;
+
+// torch.max(a, b) backward: the larger input gets the gradient, ties split it in halves.
+__device__ __forceinline__ void max_grad_split(float a, float b, float& ga, float& gb) {
+  ga = a > b ? 1.f : (a == b ? 0.5f : 0.f);
+  gb = b > a ? 1.f : (a == b ? 0.5f : 0.f);
+}
+
+__global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLossArgs a) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const float invB = 1.0f / static_cast<float>(a.B);
+  const int head_cols = a.hetero ? 2 * a.A : a.A;
+  // per-lane accumulators: columns lane and lane + 32 of the head gradient, std gradient
+  float acc_dh[4] = {0.f, 0.f, 0.f, 0.f};  // head cols lane, lane+32, lane+64, lane+96
+  float acc_dstd[2] = {0.f, 0.f};
+  float acc_surr = 0.f, acc_val = 0.f, acc_ent = 0.f, acc_kl = 0.f, acc_dv = 0.f;
+
+  const int row0 = blockIdx.x * kLossRowsPerBlock + warp * kLossRowsPerWarp;
+  for (int rr = 0; rr < kLossRowsPerWarp; ++rr) {
+    const int i = row0 + rr;
+    if (i >= a.B) break;
+    const int src = a.idx[i];
+    const float* h = a.head + static_cast<size_t>(i) * a.ld_head;
+    float mu[2], sd[2], raw[2], act[2], omu[2], osd[2];
+    float lp = 0.f, ent = 0.f, kl = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int j = lane + 32 * k;
+      mu[k] = sd[k] = raw[k] = act[k] = omu[k] = osd[k] = 0.f;
+      if (j < a.A) {
+        mu[k] = h[j];
+        raw[k] = a.hetero ? h[a.A + j] : a.std_param[j];
+        sd[k] = head_std(raw[k], a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
+        const size_t o = static_cast<size_t>(src) * a.A + j;
+        act[k] = a.st_actions[o];
+        omu[k] = a.st_mean[o];
+        osd[k] = a.st_std[o];
+        const float z = (act[k] - mu[k]) / sd[k];
+        const float lsd = logf(sd[k]);
+        lp += -0.5f * z * z - lsd - kLogSqrt2Pi;
+        ent += 0.5f + kLogSqrt2Pi + lsd;
+        // KL(old || new) for diagonal Gaussians
+        const float vr = (osd[k] / sd[k]) * (osd[k] / sd[k]);
+        const float t1 = ((omu[k] - mu[k]) / sd[k]) * ((omu[k] - mu[k]) / sd[k]);
+        kl += 0.5f * (vr + t1 - 1.0f - logf(vr));
+      }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      lp += __shfl_xor_sync(0xffffffffu, lp, off);
+      ent += __shfl_xor_sync(0xffffffffu, ent, off);
+      kl += __shfl_xor_sync(0xffffffffu, kl, off);
+    }
+    // surrogate (identical on every lane)
+    const float adv = a.adv_override ? a.adv_override[i] : a.st_adv[src];
+    const float ratio = expf(lp - a.st_logp[src]);
+    const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
+    const float rc = fminf(fmaxf(ratio, lo), hi);
+    const float s1 = -adv * ratio, s2 = -adv * rc;
+    float g1, g2;
+    max_grad_split(s1, s2, g1, g2);
+    const float in_rng = (ratio >= lo && ratio <= hi) ? 1.f : 0.f;
+    const float d_ratio = (g1 * -adv + g2 * -adv * in_rng) * invB;
+    const float d_lp = d_ratio * ratio;
+    // value loss
+    const float v = a.value[static_cast<size_t>(i) * a.ld_value];
+    const float ret = a.st_ret[src];
+    const float vold = a.st_val[src];
+    float vloss, dv;
+    if (a.clipped_value) {
+      const float dvv = v - vold;
+      const float vc = vold + fminf(fmaxf(dvv, -a.clip), a.clip);
+      const float l1 = (v - ret) * (v - ret), l2 = (vc - ret) * (vc - ret);
+      float q1, q2;
+      max_grad_split(l1, l2, q1, q2);
+      const float vin = (dvv >= -a.clip && dvv <= a.clip) ? 1.f : 0.f;
+      vloss = fmaxf(l1, l2);
+      dv = q1 * 2.f * (v - ret) + q2 * 2.f * (vc - ret) * vin;
+    } else {
+      vloss = (ret - v) * (ret - v);
+      dv = 2.f * (v - ret);
+    }
+    dv *= a.value_coef * invB;
+    // gradients w.r.t. mean and std of each action
+    __nv_bfloat16* dh = static_cast<__nv_bfloat16*>(a.d_head) + static_cast<size_t>(i) * a.ld_dhead;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int j = lane + 32 * k;
+      if (j < a.A) {
+        const float inv_var = 1.0f / (sd[k] * sd[k]);
+        const float diff = act[k] - mu[k];
+        const float dmu = d_lp * diff * inv_var;
+        const float dsd = d_lp * (diff * diff * inv_var / sd[k] - 1.0f / sd[k]) - a.entropy_coef * invB / sd[k];
+        // chain through the std parameterisation (clamp passes the gradient on [lo, hi] inclusive)
+        float dsd_raw;
+        if (a.log_std) {
+          const float in = (raw[k] >= a.log_std_lo && raw[k] <= a.log_std_hi) ? 1.f : 0.f;
+          dsd_raw = dsd * sd[k] * in;
+        } else {
+          const float in = (raw[k] >= a.std_lo && raw[k] <= a.std_hi) ? 1.f : 0.f;
+          dsd_raw = dsd * in;
+        }
+        dh[j] = __float2bfloat16_rn(dmu);
+        acc_dh[k] += dmu;
+        if (a.hetero) {
+          dh[a.A + j] = __float2bfloat16_rn(dsd_raw);
+          acc_dh[2 + k] += dsd_raw;
+        } else {
+          acc_dstd[k] += dsd_raw;
+        }
+      }
+    }
+    // zero the padding columns of the head gradient
+    for (int c = head_cols + lane; c < a.ld_dhead; c += 32) dh[c] = __float2bfloat16_rn(0.f);
+    if (lane == 0) {
+      __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.d_value) + static_cast<size_t>(i) * a.ld_dvalue;
+      dvp[0] = __float2bfloat16_rn(dv);
+      for (int c = 1; c < a.ld_dvalue; ++c) dvp[c] = __float2bfloat16_rn(0.f);
+      acc_surr += fmaxf(s1, s2) * invB;
+      acc_val += vloss * invB;
+      acc_ent += ent * invB;
+      acc_kl += kl * invB;
+      acc_dv += dv;
+    }
+  }
+  // ---- block reduction in fixed warp order ----
+  __shared__ float sh_dh[kLossWarps][4][32];
+  __shared__ float sh_dstd[kLossWarps][2][32];
+  __shared__ float sh_sc[kLossWarps][5];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) sh_dh[warp][k][lane] = acc_dh[k];
+  sh_dstd[warp][0][lane] = acc_dstd[0];
+  sh_dstd[warp][1][lane] = acc_dstd[1];
+  if (lane == 0) {
+    sh_sc[warp][0] = acc_surr;
+    sh_sc[warp][1] = acc_val;
+    sh_sc[warp][2] = acc_ent;
+    sh_sc[warp][3] = acc_kl;
+    sh_sc[warp][4] = acc_dv;
+  }
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < 64) {
+    // mean-gradient column sums (cols 0..A-1) and hetero std columns (A..2A-1)
+    const int k = t >> 5, l = t & 31;
+    const int j = 32 * k + l;
+    float s = 0.f, sstd = 0.f, sraw = 0.f;
+    for (int w = 0; w < kLossWarps; ++w) {
+      s += sh_dh[w][k][l];
+      sstd += sh_dstd[w][k][l];
+      sraw += sh_dh[w][2 + k][l];
+    }
+    if (j < a.A) {
+      a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + j] = s;
+      if (a.hetero)
+        a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + a.A + j] = sraw;
+      else if (a.dstd_partial)
+        a.dstd_partial[static_cast<size_t>(blockIdx.x) * a.A + j] = sstd;
+    }
+  } else if (t < 69) {
+    const int q = t - 64;
+    float s = 0.f;
+    for (int w = 0; w < kLossWarps; ++w) s += sh_sc[w][q];
+    if (q < 4)
+      a.stats_partial[static_cast<size_t>(blockIdx.x) * 4 + q] = s;
+    else
+      a.dvalue_colsum[blockIdx.x] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// segment reduction (sum of partial slabs in fixed order, fp64 accumulation)
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void reduce_segments_kernel(const ReduceSegment* segs, int nseg, float* send0, float* send1,
+                                       const unsigned int* epoch) {
+  const int chunk = blockIdx.x;
+  int s = 0;
+  while (s + 1 < nseg && segs[s + 1].first_chunk <= chunk) ++s;
+  const ReduceSegment g = segs[s];
+  float* dst = (((epoch ? *epoch : 0u) + 1u) & 1u) ? send1 : send0;
+  dst += g.dst_offset;
+  const long long base = static_cast<long long>(chunk - g.first_chunk) * kReduceChunk;
+  for (int k = threadIdx.x; k < kReduceChunk; k += blockDim.x) {
+    const long long e = base + k;
+    if (e >= g.n) break;
+    double acc = 0.0;
+    for (int p = 0; p < g.parts; ++p) acc += g.src[static_cast<size_t>(p) * g.n + e];
+    dst[e] = static_cast<float>(acc);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Grid barrier for co-resident (cooperatively launched) grids; bounded wait.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ bool grid_sync(unsigned int* bar, unsigned int* status, uint64_t timeout_ns) {
+  __syncthreads();
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    volatile unsigned int* gen = bar + 1;
+    const unsigned int g = *gen;
+    __threadfence();
+    const unsigned int arrived = atomicAdd(bar, 1u) + 1u;
+    if (arrived == gridDim.x) {
+      atomicExch(bar, 0u);
+      __threadfence();
+      atomicAdd(bar + 1, 1u);
+    } else {
+      const uint64_t t0 = globaltimer_ns();
+      while (*gen == g) {
+        __nanosleep(64);
+        if (globaltimer_ns() - t0 > timeout_ns) {
+          report_error(status, kTimeoutGridBarrier, 50);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Fused exchange + clip + adaptive LR + Adam
+// Phase 0 (world > 1): block 0 publishes this rank's epoch flag to every peer, then waits for every peer's flag.
+// Phase 1: each block sums its chunks' gradients over ranks in rank order (bit-identical on every rank), divides by
+//          the world size, writes the averaged gradient locally and accumulates per-group squared norms.
+// Phase 2 (after a grid barrier): every block reduces the norm partials in the same order, derives the clip
+//          coefficients and the adapted learning rate, and applies Adam to its chunks.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kAdamThreads = 256;
+
+__global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs a) {
+  __shared__ float red[kAdamThreads / 32][kAdamMaxGroups];
+  __shared__ float coef[kAdamMaxGroups];
+  __shared__ float lr_s[kAdamMaxGroups];
+  __shared__ long long step_s[kAdamMaxGroups];
+  __shared__ int peers_ok;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  __shared__ unsigned int epoch_s;
+  if (threadIdx.x == 0) {
+    peers_ok = 1;
+    for (int g = 0; g < a.ngroups; ++g) step_s[g] = a.step[g];
+    epoch_s = *a.epoch + 1u;
+  }
+  __syncthreads();
+  const unsigned int epoch = epoch_s;
+  // ---- phase 0: flags ----
+  if (a.world > 1) {
+    if (blockIdx.x == 0 && threadIdx.x < a.world) {
+      // publish: this rank's slot in every peer's flag array (release orders our gradient writes before the flag)
+      __threadfence_system();
+      st_release_sys(a.peer_flags[threadIdx.x] + a.rank, epoch);
+    }
+    if (threadIdx.x == 0) {
+      const uint64_t t0 = globaltimer_ns();
+      const unsigned int* my_flags = a.peer_flags[a.rank];
+      for (int r = 0; r < a.world; ++r) {
+        while (static_cast<int>(ld_acquire_sys(my_flags + r) - epoch) < 0) {
+          if (globaltimer_ns() - t0 > a.timeout_ns) {
+            report_error(a.status, kTimeoutPeerFlag, 60 + r);
+            peers_ok = 0;
+            break;
+          }
+          __nanosleep(32);
+        }
+        if (!peers_ok) break;
+      }
+    }
+  }
+  __syncthreads();
+  const bool exchange_ok = peers_ok != 0;
+
+  // ---- phase 1: rank-ordered sum, squared norms ----
+  float sq[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
+  const float inv_world = 1.0f / static_cast<float>(a.world);
+  const unsigned int parity = epoch & 1u;
+  const float* mine = a.send[parity];
+  for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
+    const AdamChunk ch = a.chunks[c];
+    const AdamTensor T = a.tensors[ch.tensor];
+    for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
+      const long long e = T.offset + ch.start + k;
+      float g;
+      if (a.world > 1 && exchange_ok) {
+        g = 0.f;
+        for (int r = 0; r < a.world; ++r) g += a.peer_send[parity * a.world + r][e];
+        g *= inv_world;
+      } else {
+        g = mine[e];
+      }
+      a.grads[e] = g;
+      if (T.group >= 0) sq[T.group] += g * g;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < kAdamMaxGroups; ++g) {
+#pragma unroll
+    for (int off = 16; off; off >>= 1) sq[g] += __shfl_xor_sync(0xffffffffu, sq[g], off);
+  }
+  if (lane == 0)
+    for (int g = 0; g < kAdamMaxGroups; ++g) red[warp][g] = sq[g];
+  __syncthreads();
+  if (threadIdx.x < kAdamMaxGroups) {
+    float s = 0.f;
+    for (int w = 0; w < kAdamThreads / 32; ++w) s += red[w][threadIdx.x];
+    a.norm_partial[static_cast<size_t>(blockIdx.x) * kAdamMaxGroups + threadIdx.x] = s;
+  }
+  if (!grid_sync(a.barrier, a.status, a.timeout_ns)) return;
+
+  // ---- phase 2: norms, clip coefficients, learning rate ----
+  if (threadIdx.x < a.ngroups) {
+    const int g = threadIdx.x;
+    float s = 0.f;
+    for (int b = 0; b < static_cast<int>(gridDim.x); ++b) s += a.norm_partial[static_cast<size_t>(b) * kAdamMaxGroups + g];
+    const float norm = sqrtf(s);
+    float cf = 1.0f;
+    if (a.max_norm[g] > 0.f) cf = fminf(a.max_norm[g] / (norm + 1e-6f), 1.0f);
+    coef[g] = cf;
+    float lr = a.lr[g];  // slot g
+    if (g == 0 && a.adaptive) {
+      const float kl = *a.kl_mean;
+      if (kl > a.desired_kl * 2.0f)
+        lr = fmaxf(a.lr_min, lr / 1.5f);
+      else if (kl < a.desired_kl / 2.0f && kl > 0.0f)
+        lr = fminf(a.lr_max, lr * 1.5f);
+    }
+    lr_s[g] = lr;
+    if (blockIdx.x == 0 && a.out_norms) a.out_norms[g] = norm;
+  }
+  __syncthreads();
+  if (!exchange_ok) {  // leave parameters untouched when the exchange failed; the status word reports it
+    if (blockIdx.x == 0 && threadIdx.x == 0) *a.epoch = epoch;
+    return;
+  }
+  for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
+    const AdamChunk ch = a.chunks[c];
+    const AdamTensor T = a.tensors[ch.tensor];
+    const int g = T.group;
+    if (g < 0) continue;  // exchanged statistics (e.g. the KL mean), not parameters
+    const double step = static_cast<double>(step_s[g] + 1);
+    const double bc1 = 1.0 - pow(static_cast<double>(a.beta1[g]), step);
+    const double bc2 = 1.0 - pow(static_cast<double>(a.beta2[g]), step);
+    const float step_size = static_cast<float>(static_cast<double>(lr_s[a.lr_index[g]]) / bc1);
+    const float bc2_sqrt = static_cast<float>(sqrt(bc2));
+    const float b1 = a.beta1[g], b2 = a.beta2[g], eps = a.eps[g], cf = coef[g];
+    for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
+      const long long e = T.offset + ch.start + k;
+      const float grad = a.grads[e] * cf;
+      float m = a.exp_avg[e];
+      m = m + (1.0f - b1) * (grad - m);
+      const float v = b2 * a.exp_avg_sq[e] + (1.0f - b2) * grad * grad;
+      const float denom = sqrtf(v) / bc2_sqrt + eps;
+      const float p = a.params[e] - step_size * (m / denom);
+      a.exp_avg[e] = m;
+      a.exp_avg_sq[e] = v;
+      a.params[e] = p;
+      if (T.shadow) {
+        const int idx = ch.start + k;
+        const int r = idx / T.cols, col = idx - r * T.cols;
+        static_cast<__nv_bfloat16*>(T.shadow)[static_cast<size_t>(r) * T.shadow_ld + col] = __float2bfloat16_rn(p);
+      }
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < a.ngroups) {
+    a.lr[threadIdx.x] = lr_s[threadIdx.x];
+    a.step[threadIdx.x] = step_s[threadIdx.x] + 1;
+    if (threadIdx.x == 0) {
+      *a.epoch = epoch;
+      if (a.lr_out_slot) *a.lr_out_slot = lr_s[0];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Column statistics + EmpiricalNormalization update
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kStatsRowsPerChunk = 4096;
+__global__ void colstats_kernel(const ColStatsArgs a) {
+  // block (32 columns x 8 row lanes) per (column stripe, row chunk)
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  const long long r0 = static_cast<long long>(blockIdx.y) * kStatsRowsPerChunk;
+  const long long r1 = min(a.rows, r0 + kStatsRowsPerChunk);
+  double s = 0.0, ss = 0.0;
+  if (col < a.dim) {
+    for (long long r = r0 + threadIdx.y; r < r1; r += blockDim.y) {
+      const double v = a.x[static_cast<size_t>(r) * a.ld + col];
+      s += v;
+      ss += v * v;
+    }
+  }
+  __shared__ double sh[2][8][33];
+  sh[0][threadIdx.y][threadIdx.x] = s;
+  sh[1][threadIdx.y][threadIdx.x] = ss;
+  __syncthreads();
+  if (threadIdx.y == 0 && col < a.dim) {
+    double ts = 0, tss = 0;
+    for (int y = 0; y < static_cast<int>(blockDim.y); ++y) {
+      ts += sh[0][y][threadIdx.x];
+      tss += sh[1][y][threadIdx.x];
+    }
+    a.partial[(static_cast<size_t>(blockIdx.y) * 2) * a.dim + col] = ts;
+    a.partial[(static_cast<size_t>(blockIdx.y) * 2 + 1) * a.dim + col] = tss;
+  }
+}
+
+__global__ void norm_update_kernel(const NormUpdateArgs a) {
+  __shared__ long long count0;
+  __shared__ int skip;
+  if (threadIdx.x == 0) {
+    count0 = *a.count;
+    skip = (a.until >= 0 && count0 >= a.until) ? 1 : 0;
+  }
+  __syncthreads();
+  if (skip) return;
+  const double n = static_cast<double>(a.rows);
+  const double new_count = static_cast<double>(count0) + n;
+  const float rate = static_cast<float>(n / new_count);
+  for (int c = threadIdx.x; c < a.dim; c += blockDim.x) {
+    double s = 0, ss = 0;
+    for (int k = 0; k < a.chunks; ++k) {
+      s += a.partial[(static_cast<size_t>(k) * 2) * a.dim + c];
+      ss += a.partial[(static_cast<size_t>(k) * 2 + 1) * a.dim + c];
+    }
+    if (a.moments_out) {
+      a.moments_out[2 + c] = s;
+      a.moments_out[2 + a.dim + c] = ss;
+    }
+    const double bm = s / n;
+    const double bv = fmax(ss / n - bm * bm, 0.0);
+    const float batch_mean = static_cast<float>(bm), batch_var = static_cast<float>(bv);
+    const float old_mean = a.mean[c];
+    const float delta = batch_mean - old_mean;
+    const float new_mean = old_mean + rate * delta;
+    const float new_var = a.var[c] + rate * (batch_var - a.var[c] + delta * (batch_mean - new_mean));
+    a.mean[c] = new_mean;
+    a.var[c] = new_var;
+    a.std[c] = sqrtf(new_var);
+  }
+  if (threadIdx.x == 0) {
+    *a.count = count0 + a.rows;
+    if (a.moments_out) a.moments_out[0] = n;
+  }
+}
+
+__global__ void to_bf16_padded_kernel(const float* src, int rows, int cols, __nv_bfloat16* dst, int ld) {
+  const long long total = static_cast<long long>(rows) * ld;
+  for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(e / ld), c = static_cast<int>(e - static_cast<long long>(r) * ld);
+    dst[e] = __float2bfloat16_rn(c < cols ? src[static_cast<size_t>(r) * cols + c] : 0.f);
+  }
+}
+
+int grid_for(long long work, int threads, int cap = 148 * 16) {
+  long long g = (work + threads - 1) / threads;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------------------------------------------
+cudaError_t prep_obs(const PrepObsArgs& a, cudaStream_t s) {
+  int D = 0;
+  for (int g = 0; g < a.groups; ++g) D += a.width[g];
+  if (a.groups < 1 || a.groups > kMaxObsGroups || a.rows <= 0) return cudaErrorInvalidValue;
+  prep_obs_kernel<<<grid_for(static_cast<long long>(a.rows) * D, 256), 256, 0, s>>>(a, D);
+  return cudaGetLastError();
+}
+
+cudaError_t gaussian_sample(const SampleArgs& a, cudaStream_t s) {
+  if (a.A > 64 || a.rows <= 0) return cudaErrorInvalidValue;
+  gaussian_sample_kernel<<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t process_step(const ProcessArgs& a, cudaStream_t s) {
+  process_step_kernel<<<grid_for(a.rows, 256), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+int gae_blocks(int N) { return (N + kGaeThreads - 1) / kGaeThreads; }
+
+cudaError_t gae(const GaeArgs& a, cudaStream_t s) {
+  gae_kernel<<<gae_blocks(a.N), kGaeThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t adv_normalize(float* adv, long long n, const double* partial, int parts, cudaStream_t s) {
+  adv_normalize_kernel<<<grid_for(n, 256, 148 * 4), 256, 0, s>>>(adv, n, partial, parts);
+  return cudaGetLastError();
+}
+
+uint32_t feistel_half_bits(long long total) {
+  uint32_t bits = 2;
+  while ((1ll << bits) < total) ++bits;
+  return (bits + 1) / 2;
+}
+
+uint32_t feistel_permute_host(uint32_t i, uint32_t n, uint32_t half_bits, uint32_t key) {
+  bool overflow = false;
+  return feistel_permute(i, n, half_bits, key, &overflow);
+}
+
+cudaError_t gather_minibatch(const GatherArgs& a, cudaStream_t s) {
+  if (a.B <= 0) return cudaErrorInvalidValue;
+  gather_minibatch_kernel<<<grid_for(a.B, 8, 148 * 64), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+int ppo_loss_blocks(int B) { return (B + kLossRowsPerBlock - 1) / kLossRowsPerBlock; }
+
+cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
+  if (a.A > kLossMaxA || a.B <= 0) return cudaErrorInvalidValue;
+  ppo_loss_kernel<<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_chunks, float* send0, float* send1,
+                            const unsigned int* epoch, cudaStream_t s) {
+  if (nseg <= 0 || total_chunks <= 0) return cudaErrorInvalidValue;
+  reduce_segments_kernel<<<total_chunks, 256, 0, s>>>(segs_dev, nseg, send0, send1, epoch);
+  return cudaGetLastError();
+}
+
+int adam_grid(int device) {
+  int sms = 148, per_sm = 1;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adam_step_kernel, kAdamThreads, 0);
+  if (per_sm < 1) per_sm = 1;
+  return sms * (per_sm > 2 ? 2 : per_sm);
+}
+
+cudaError_t adam_step(const AdamArgs& a, int grid, cudaStream_t s) {
+  if (a.ngroups < 1 || a.ngroups > kAdamMaxGroups) return cudaErrorInvalidValue;
+  void* args[] = {const_cast<AdamArgs*>(&a)};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(adam_step_kernel), dim3(grid), dim3(kAdamThreads), args,
+                                     0, s);
+}
+
+int colstats_chunks(long long rows) { return static_cast<int>((rows + kStatsRowsPerChunk - 1) / kStatsRowsPerChunk); }
+
+cudaError_t colstats(const ColStatsArgs& a, cudaStream_t s) {
+  dim3 grid((a.dim + 31) / 32, a.chunks);
+  colstats_kernel<<<grid, dim3(32, 8), 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t norm_update(const NormUpdateArgs& a, cudaStream_t s) {
+  norm_update_kernel<<<1, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+__global__ void counter_add_kernel(unsigned int* p, unsigned int delta) { *p += delta; }
+
+cudaError_t counter_add(unsigned int* p, unsigned int delta, cudaStream_t s) {
+  counter_add_kernel<<<1, 1, 0, s>>>(p, delta);
+  return cudaGetLastError();
+}
+
+cudaError_t to_bf16_padded(const float* src, int rows, int cols, void* dst, int ld, cudaStream_t s) {
+  to_bf16_padded_kernel<<<grid_for(static_cast<long long>(rows) * ld, 256), 256, 0, s>>>(
+      src, rows, cols, static_cast<__nv_bfloat16*>(dst), ld);
+  return cudaGetLastError();
+}
+
+}  // namespace rlb

@@ -1,0 +1,9 @@
+"""Errors raised by the communicator and the device status word."""
+
+
+class CommTimeoutError(RuntimeError):
+    """A device-side wait ran out (peer flag, grid barrier or pipeline stage) or a rank failed to join in time.
+
+    The kernels record the first failing site in a status word and return instead of hanging; the host reads the word
+    after each update and raises this error.
+    """
