@@ -4,7 +4,10 @@
 // One CTA computes one 128 x BN output tile (split-K partials along blockIdx.z). Warp roles:
 //   warp 0      : TMA producer (one elected lane), multi-stage ring of shared-memory stages
 //   warp 1      : TMEM allocator + MMA issuer (one elected lane)
-//   warps 2..5  : epilogue; warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32) = output rows of its quadrant
+//   warps 2..9  : epilogue; warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32) = output rows of its quadrant, the two
+//                 warps of a quadrant splitting the column chunks
+// Short-K layers run two CTAs per SM (TMEM 2 x BN <= 512 columns) so that one CTA's epilogue overlaps the other's
+// main loop.
 // No load uses cluster multicast: every CTA fetches its own tiles from this GPU's memory.
 //
 // The MLP layers of rsl_rl (rsl_rl/modules/mlp.py:91-95, Linear+ELU stacks) map onto three uses:
@@ -24,25 +27,33 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle atom row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, splitting the column chunks
+constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMNBoxBytes = 64 * kBK * 2;  // one {64 MN x 64 K} box
+constexpr int kStageWords = 32 * 33;       // per-warp 32 x 32-word staging tile (+1 word padding per row)
 
-template <int BN>
+template <int BN, int EPI>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 3 : 4;
+  // Short-K layers (forward, data gradient) keep two CTAs per SM so one CTA's epilogue overlaps the other's
+  // main loop; the long-K weight-gradient GEMM uses a deeper pipeline with one CTA per SM.
+  static constexpr bool kLongK = EPI == kEpiPartialF32;
+  static constexpr int kStages = kLongK ? (BN == 256 ? 4 : 6) : (BN == 256 ? 2 : BN == 128 ? 3 : 4);
+  static constexpr int kMinBlocks = kLongK ? 1 : 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kColsumBytes = 4 * BN * 4;
-  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kStages * (kABytes + kBBytes) + kBarrierBytes + kColsumBytes;
+  static constexpr int kPipeBytes = kStages * (kABytes + kBBytes);
+  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kPipeBytes + kBarrierBytes + kColsumBytes;
+  static_assert(kPipeBytes >= kEpiWarps * 2 * kStageWords * 4, "epilogue staging must fit in the pipeline buffers");
 };
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmParams p, int num_kb) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, EPI>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -155,105 +166,159 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(accum);
     }
   } else {
-    // ---------------- epilogue ----------------
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Warp w may only read TMEM lanes [32 * (w % 4), +32): its quadrant q owns output rows m0 + 32q .. +31, one row
+    // per lane. The two warps of a quadrant take alternate column chunks. The pipeline buffers are idle once the
+    // accumulator is complete, so each warp stages its chunks there to make global loads/stores row-contiguous.
+    const int ew = warp - 2;
     const int q = warp & 3;
-    const int row = m0 + q * 32 + lane;
+    const int half = ew >> 2;
+    const int row_base = m0 + q * 32;
+    const int row = row_base + lane;
     const bool row_ok = row < p.M;
+    uint32_t* stage_aux = reinterpret_cast<uint32_t*>(smem) + ew * 2 * kStageWords;
+    uint32_t* stage_out = stage_aux + kStageWords;
     uint32_t ok = 1;
     if (lane == 0) ok = mbar_wait(accum, 0) ? 1u : 0u;
     ok = __shfl_sync(0xffffffffu, ok, 0);
     if (!ok && lane == 0) report_error(p.status, kTimeoutAccum, 3);
     tc_fence_after();
+    constexpr int CW = BN >= 64 ? 64 : 32;  // columns per chunk (64 bf16 = one 128-byte line per row)
+    constexpr int WPR = CW / 2;             // 32-bit words per row of a bf16 chunk
+    constexpr int LPR = WPR / 4;            // lanes per row for 16-byte accesses
+    constexpr int RPP = 32 / LPR;           // rows per pass
     if (ok && nkb > 0) {
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        if (n0 + c >= p.N) break;
-        float v[32];
-        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), v);
-        tmem_wait_ld();
+      for (int c = half * CW; c < BN; c += 2 * CW) {
         const int nb = n0 + c;
-        const bool full_chunk = nb + 32 <= p.N;
-        if constexpr (EPI == kEpiF32 || EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16) {
-          if (p.bias != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += (nb + j < p.N) ? __ldg(p.bias + nb + j) : 0.f;
-          }
-        }
-        if constexpr (EPI == kEpiBiasEluBf16) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = elu_f(v[j]);
-        }
+        if (nb >= p.N) break;
+        const int valid = min(CW, p.N - nb);
+        const bool full_cols = valid == CW;
         if constexpr (EPI == kEpiDgradElu) {
-          const __nv_bfloat16* h = static_cast<const __nv_bfloat16*>(p.aux) + static_cast<size_t>(row) * p.ld_aux + nb;
-          if (row_ok && full_chunk && (p.ld_aux % 8) == 0) {
+          // coalesced load of the aux (ELU output) chunk, RPP rows per pass
+          const __nv_bfloat16* aux = static_cast<const __nv_bfloat16*>(p.aux);
+          const int lr = lane / LPR, lw = (lane % LPR) * 4;
+          const bool vec = full_cols && (p.ld_aux % 8) == 0;
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              const uint4 raw = __ldg(reinterpret_cast<const uint4*>(h + j));
-              const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&raw);
+          for (int r0 = 0; r0 < 32; r0 += RPP) {
+            const int r = r0 + lr;
+            const int gr = row_base + r;
+            uint32_t w4[4] = {0u, 0u, 0u, 0u};
+            if (gr < p.M) {
+              const __nv_bfloat16* src = aux + static_cast<size_t>(gr) * p.ld_aux + nb + 2 * lw;
+              if (vec) {
+                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src));
+                w4[0] = raw.x;
+                w4[1] = raw.y;
+                w4[2] = raw.z;
+                w4[3] = raw.w;
+              } else {
 #pragma unroll
-              for (int t = 0; t < 8; ++t) v[j + t] *= elu_grad_from_out(__bfloat162float(hv[t]));
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              v[j] = (row_ok && nb + j < p.N) ? v[j] * elu_grad_from_out(__bfloat162float(h[j])) : 0.f;
-          }
-        }
-        // ---- stores ----
-        if constexpr (EPI == kEpiF32 || EPI == kEpiPartialF32) {
-          float* o = static_cast<float*>(p.out) + (EPI == kEpiPartialF32 ? blockIdx.z * p.split_stride : 0ll) +
-                     static_cast<size_t>(row) * p.ldo + nb;
-          if (row_ok) {
-            if (full_chunk && (p.ldo % 4) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < p.N) o[j] = v[j];
-            }
-          }
-        } else {
-          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ldo + nb;
-          if (row_ok) {
-            if (full_chunk && (p.ldo % 8) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk;
-                pk.x = pack_bf16x2(v[j], v[j + 1]);
-                pk.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                pk.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                pk.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4*>(o + j) = pk;
+                for (int i = 0; i < 4; ++i) {
+                  const int col = 2 * (lw + i);
+                  const float lo = col < valid ? __bfloat162float(src[2 * i]) : 0.f;
+                  const float hi = col + 1 < valid ? __bfloat162float(src[2 * i + 1]) : 0.f;
+                  w4[i] = pack_bf16x2(lo, hi);
+                }
               }
-            } else {
+            }
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < p.N) o[j] = __float2bfloat16_rn(v[j]);
+            for (int i = 0; i < 4; ++i) stage_aux[r * 33 + lw + i] = w4[i];
+          }
+          __syncwarp();
+        }
+#pragma unroll
+        for (int sub = 0; sub < CW; sub += 32) {
+          float v[32];
+          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c + sub), v);
+          tmem_wait_ld();
+          const int sb = nb + sub;
+          if constexpr (EPI == kEpiF32 || EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16) {
+            if (p.bias != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += (sb + j < p.N) ? __ldg(p.bias + sb + j) : 0.f;
             }
           }
-        }
-        if constexpr (EPI == kEpiDgradElu) {
-          if (p.colsum != nullptr) {
+          if constexpr (EPI == kEpiBiasEluBf16) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.f ? v[j] : __expf(v[j]) - 1.0f;
+          }
+          if constexpr (EPI == kEpiDgradElu) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              const uint32_t w = stage_aux[lane * 33 + (sub + j) / 2];
+              __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w);
+              v[j] *= elu_grad_from_out(__low2float(h2));
+              v[j + 1] *= elu_grad_from_out(__high2float(h2));
+            }
             if (!row_ok) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
-            const float s = warp_transpose_reduce32(v);
-            colsum_s[q * BN + c + lane] = s;
+          }
+          if constexpr (EPI == kEpiF32 || EPI == kEpiPartialF32) {
+            float* o = static_cast<float*>(p.out) + (EPI == kEpiPartialF32 ? blockIdx.z * p.split_stride : 0ll) +
+                       static_cast<size_t>(row) * p.ldo + sb;
+            if (row_ok) {
+              if (sb + 32 <= p.N && (p.ldo % 4) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                  *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (sb + j < p.N) o[j] = v[j];
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) stage_out[lane * 33 + (sub + j) / 2] = pack_bf16x2(v[j], v[j + 1]);
+          }
+          if constexpr (EPI == kEpiDgradElu) {
+            if (p.colsum != nullptr) {
+              // per-column sums; columns at or past N are never written out
+              const float s = warp_transpose_reduce32(v);
+              colsum_s[q * BN + c + sub + lane] = s;
+            }
           }
         }
-      }
-      if constexpr (EPI == kEpiDgradElu) {
-        if (p.colsum != nullptr) {
-          named_barrier_sync(1, 128);
-          const int t = threadIdx.x - 64;
-          for (int n = t; n < BN; n += 128) {
-            if (n0 + n < p.N) {
-              const float s = colsum_s[n] + colsum_s[BN + n] + colsum_s[2 * BN + n] + colsum_s[3 * BN + n];
-              p.colsum[static_cast<size_t>(blockIdx.x) * p.N + n0 + n] = s;
+        if constexpr (EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16 || EPI == kEpiDgradElu) {
+          __syncwarp();
+          __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(p.out);
+          const int lr = lane / LPR, lw = (lane % LPR) * 4;
+          const bool vec = full_cols && (p.ldo % 8) == 0;
+#pragma unroll
+          for (int r0 = 0; r0 < 32; r0 += RPP) {
+            const int r = r0 + lr;
+            const int gr = row_base + r;
+            if (gr < p.M) {
+              __nv_bfloat16* dst = outp + static_cast<size_t>(gr) * p.ldo + nb + 2 * lw;
+              const uint32_t* src = stage_out + r * 33 + lw;
+              if (vec) {
+                *reinterpret_cast<uint4*>(dst) = make_uint4(src[0], src[1], src[2], src[3]);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int col = 2 * (lw + i);
+                  __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&src[i]);
+                  if (col < valid) dst[2 * i] = __low2bfloat16(h2);
+                  if (col + 1 < valid) dst[2 * i + 1] = __high2bfloat16(h2);
+                }
+              }
             }
+          }
+          __syncwarp();
+        }
+      }
+    }
+    if constexpr (EPI == kEpiDgradElu) {
+      if (p.colsum != nullptr) {
+        named_barrier_sync(1, kEpiWarps * 32);
+        const int t = threadIdx.x - 64;
+        for (int n = t; n < BN; n += kEpiWarps * 32) {
+          if (n0 + n < p.N) {
+            const float s = colsum_s[n] + colsum_s[BN + n] + colsum_s[2 * BN + n] + colsum_s[3 * BN + n];
+            p.colsum[static_cast<size_t>(blockIdx.x) * p.N + n0 + n] = s;
           }
         }
       }
@@ -301,7 +366,7 @@ bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, EPI>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;

@@ -468,21 +468,31 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
 // ---------------------------------------------------------------------------------------------------------------
 // segment reduction (sum of partial slabs in fixed order, fp64 accumulation)
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void reduce_segments_kernel(const ReduceSegment* segs, int nseg, float* send0, float* send1,
-                                       const unsigned int* epoch) {
+// Block = 32 columns x 8 part-lanes: lane y sums parts y, y + 8, ... of its column (coalesced 128-byte rows), then the
+// 8 lane sums are combined in a fixed order. Deterministic for a given launch configuration.
+constexpr int kReduceCols = 32;
+constexpr int kReduceLanes = 8;
+__global__ void __launch_bounds__(kReduceCols* kReduceLanes)
+    reduce_segments_kernel(const ReduceSegment* segs, int nseg, float* send0, float* send1, const unsigned int* epoch) {
   const int chunk = blockIdx.x;
   int s = 0;
   while (s + 1 < nseg && segs[s + 1].first_chunk <= chunk) ++s;
   const ReduceSegment g = segs[s];
   float* dst = (((epoch ? *epoch : 0u) + 1u) & 1u) ? send1 : send0;
   dst += g.dst_offset;
-  const long long base = static_cast<long long>(chunk - g.first_chunk) * kReduceChunk;
-  for (int k = threadIdx.x; k < kReduceChunk; k += blockDim.x) {
-    const long long e = base + k;
-    if (e >= g.n) break;
-    double acc = 0.0;
-    for (int p = 0; p < g.parts; ++p) acc += g.src[static_cast<size_t>(p) * g.n + e];
-    dst[e] = static_cast<float>(acc);
+  const long long e = static_cast<long long>(chunk - g.first_chunk) * kReduceCols + threadIdx.x;
+  double acc = 0.0;
+  if (e < g.n) {
+    for (int p = threadIdx.y; p < g.parts; p += kReduceLanes) acc += g.src[static_cast<size_t>(p) * g.n + e];
+  }
+  __shared__ double sh[kReduceLanes][kReduceCols];
+  sh[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && e < g.n) {
+    double t = 0.0;
+#pragma unroll
+    for (int y = 0; y < kReduceLanes; ++y) t += sh[y][threadIdx.x];
+    dst[e] = static_cast<float>(t);
   }
 }
 
@@ -547,9 +557,14 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   __shared__ unsigned int epoch_s;
+  __shared__ float lr_old[kAdamMaxGroups];
+  // Everything block 0 rewrites at the end (step, learning rates, epoch) is read here, before the grid barrier.
   if (threadIdx.x == 0) {
     peers_ok = 1;
-    for (int g = 0; g < a.ngroups; ++g) step_s[g] = a.step[g];
+    for (int g = 0; g < a.ngroups; ++g) {
+      step_s[g] = a.step[g];
+      lr_old[g] = a.lr[g];
+    }
     epoch_s = *a.epoch + 1u;
   }
   __syncthreads();
@@ -626,7 +641,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     float cf = 1.0f;
     if (a.max_norm[g] > 0.f) cf = fminf(a.max_norm[g] / (norm + 1e-6f), 1.0f);
     coef[g] = cf;
-    float lr = a.lr[g];  // slot g
+    float lr = lr_old[g];  // slot g
     if (g == 0 && a.adaptive) {
       const float kl = *a.kl_mean;
       if (kl > a.desired_kl * 2.0f)
@@ -832,7 +847,7 @@ cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
 cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_chunks, float* send0, float* send1,
                             const unsigned int* epoch, cudaStream_t s) {
   if (nseg <= 0 || total_chunks <= 0) return cudaErrorInvalidValue;
-  reduce_segments_kernel<<<total_chunks, 256, 0, s>>>(segs_dev, nseg, send0, send1, epoch);
+  reduce_segments_kernel<<<total_chunks, dim3(kReduceCols, kReduceLanes), 0, s>>>(segs_dev, nseg, send0, send1, epoch);
   return cudaGetLastError();
 }
 

@@ -157,7 +157,7 @@ struct ReduceSegment {
 };
 cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_chunks, float* send0, float* send1,
                             const unsigned int* epoch, cudaStream_t s);
-constexpr int kReduceChunk = 1024;
+constexpr int kReduceChunk = 32;  // columns per block of the reduction kernel
 
 // Fused (all-reduce over peers) + per-group global-norm clip + adaptive learning rate + Adam + bf16 weight shadows.
 struct AdamTensor {
