@@ -24,3 +24,16 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def ref():
+    """The unmodified reference (upstream rsl_rl) installed in baseline/_ref, used as the CPU oracle."""
+    import baseline
+
+    if not baseline.reference_available():
+        pytest.skip("reference not installed in baseline/_ref")
+    baseline.add_reference_to_path()
+    import rsl_rl
+
+    return rsl_rl

@@ -1,0 +1,270 @@
+"""Host-only tests of the framework layer: utilities, TensorDict, runner features, data parallelism over gloo and
+host-side failure detection. No GPU is used."""
+
+import copy
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+
+from helpers import ppo_cfg, small_env
+
+
+# ---- utilities ---------------------------------------------------------------------------------------------------------
+def test_resolve_callable_forms():
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.utils import resolve_callable
+
+    assert resolve_callable("PPO") is PPO
+    assert resolve_callable("tt_rsl_rl_b200.algorithms:PPO") is PPO
+    assert resolve_callable("tt_rsl_rl_b200.algorithms.PPO") is PPO
+    assert resolve_callable(PPO) is PPO
+    assert resolve_callable("GaussianDistribution").__name__ == "GaussianDistribution"
+    with pytest.raises(ValueError):
+        resolve_callable("NoSuchThing")
+    with pytest.raises(TypeError):
+        resolve_callable(3)
+
+
+def test_resolve_obs_groups_rules():
+    from tt_rsl_rl_b200.utils import TensorDict, resolve_obs_groups
+
+    obs = TensorDict({"policy": torch.zeros(2, 3), "critic": torch.zeros(2, 4)}, batch_size=[2])
+    g = resolve_obs_groups(obs, {"actor": ["policy"]}, ["actor", "critic"])
+    assert g["critic"] == ["critic"]
+    g = resolve_obs_groups(obs, {}, ["actor", "rnd_state"])
+    assert g == {"actor": ["policy"], "rnd_state": ["policy"]}
+    with pytest.raises(ValueError):
+        resolve_obs_groups(obs, {"actor": []}, ["actor"])
+    with pytest.raises(ValueError):
+        resolve_obs_groups(obs, {"actor": ["nope"]}, ["actor"])
+
+
+def test_activation_and_optimizer_resolution():
+    from tt_rsl_rl_b200.utils import resolve_nn_activation, resolve_optimizer
+
+    assert isinstance(resolve_nn_activation("ELU"), torch.nn.ELU)
+    assert resolve_optimizer("AdamW") is torch.optim.AdamW
+    with pytest.raises(ValueError):
+        resolve_nn_activation("bogus")
+    with pytest.raises(ValueError):
+        resolve_optimizer("bogus")
+
+
+def test_tensordict_operations():
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    td = TensorDict({"a": torch.arange(24.0).view(4, 3, 2), "b": torch.ones(4, 3, 1)}, batch_size=[4, 3])
+    assert td.batch_size == torch.Size([4, 3])
+    f = td.flatten(0, 1)
+    assert f.batch_size == torch.Size([12]) and f["a"].shape == (12, 2)
+    sub = f[torch.tensor([0, 5, 7])]
+    assert sub.batch_size == torch.Size([3])
+    torch.testing.assert_close(sub["a"][1], torch.tensor([10.0, 11.0]))
+    td[1].copy_({"a": torch.zeros(3, 2), "b": torch.zeros(3, 1)})
+    assert float(td["a"][1].sum()) == 0.0
+    cat = torch.cat([f, f])
+    assert cat.batch_size == torch.Size([24])
+    tr = td.transpose(1, 0)
+    assert tr.batch_size == torch.Size([3, 4]) and tr["a"].shape == (3, 4, 2)
+    v = tr.reshape(-1, 2)
+    assert v.batch_size == torch.Size([6, 2])
+    assert td[:, 1:].batch_size == torch.Size([4, 2])
+    assert set(td.keys()) == {"a", "b"} and "a" in td
+    with pytest.raises(ValueError):
+        td["c"] = torch.zeros(5)
+
+
+def test_feistel_permutation_is_a_bijection():
+    from tt_rsl_rl_b200.ops import ext
+
+    C = ext()
+    for n in (1, 2, 7, 100, 1000, 4097, 24 * 1001):
+        hb = C.feistel_half_bits(n)
+        vals = sorted(C.feistel_permute(i, n, hb, 12345) for i in range(n))
+        assert vals == list(range(n))
+    n = 5000
+    hb = C.feistel_half_bits(n)
+    a = [C.feistel_permute(i, n, hb, 1) for i in range(50)]
+    b = [C.feistel_permute(i, n, hb, 2) for i in range(50)]
+    assert a != b  # the key changes the order
+
+
+# ---- runner features ---------------------------------------------------------------------------------------------------
+def test_runner_learn_logs_saves_and_exports(tmp_path):
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    cfg = ppo_cfg()
+    cfg["logger"] = {"class_name": "CsvLogWriter"}
+    cfg["save_interval"] = 1
+    runner = OnPolicyRunner(small_env(), cfg, log_dir=str(tmp_path), device="cpu")
+    runner.learn(3)
+    assert (tmp_path / "metrics.csv").exists()
+    text = (tmp_path / "metrics.csv").read_text().splitlines()
+    assert "Loss/surrogate" in text[0] and len(text) >= 3
+    assert (tmp_path / "model_2.pt").exists()
+    runner.export_policy_to_jit(str(tmp_path), "policy.pt")
+    jit = torch.jit.load(str(tmp_path / "policy.pt"))
+    x = small_env().get_observations()["policy"]
+    with torch.no_grad():
+        torch.testing.assert_close(jit(x), runner.get_inference_policy()({"policy": x}))
+
+
+def test_runner_tensorboard_default(tmp_path):
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    runner = OnPolicyRunner(small_env(), ppo_cfg(), log_dir=str(tmp_path), device="cpu")
+    runner.learn(1)
+    assert any(p.name.startswith("events.out.tfevents") for p in tmp_path.iterdir())
+    assert (tmp_path / "git").is_dir()
+
+
+def test_runner_resume_continues_iteration_count(tmp_path):
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    cfg = ppo_cfg()
+    r1 = OnPolicyRunner(small_env(), copy.deepcopy(cfg), log_dir=None, device="cpu")
+    r1.learn(2)
+    r1.save(str(tmp_path / "m.pt"))
+    r2 = OnPolicyRunner(small_env(), copy.deepcopy(cfg), log_dir=None, device="cpu")
+    r2.load(str(tmp_path / "m.pt"))
+    assert r2.current_learning_iteration == 1
+    assert r2.alg.learning_rate == pytest.approx(r1.alg.learning_rate)
+
+
+def test_distillation_runner_requires_teacher(tmp_path):
+    from tt_rsl_rl_b200.runners import DistillationRunner, OnPolicyRunner
+
+    cfg = {
+        "num_steps_per_env": 8, "save_interval": 100, "obs_groups": {"student": ["policy"], "teacher": ["policy"]},
+        "algorithm": {"class_name": "Distillation", "num_learning_epochs": 1, "gradient_length": 4},
+        "student": {"class_name": "MLPModel", "hidden_dims": [32, 32],
+                    "distribution_cfg": {"class_name": "GaussianDistribution"}},
+        "teacher": {"class_name": "MLPModel", "hidden_dims": [32, 32], "obs_normalization": True,
+                    "distribution_cfg": {"class_name": "GaussianDistribution"}},
+    }
+    runner = DistillationRunner(small_env(), copy.deepcopy(cfg), log_dir=None, device="cpu")
+    with pytest.raises(ValueError):
+        runner.learn(1)
+    # an RL checkpoint provides the teacher
+    rl_cfg = ppo_cfg(hidden=(32, 32), critic_group="policy")
+    rl = OnPolicyRunner(small_env(), rl_cfg, log_dir=None, device="cpu")
+    rl.save(str(tmp_path / "rl.pt"))
+    runner.load(str(tmp_path / "rl.pt"))
+    assert runner.alg.teacher_loaded
+    runner.learn(2)
+
+
+def test_ppo_cpu_with_rnd_symmetry_and_recurrent():
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    def mirror(env, obs=None, actions=None):
+        o = a = None
+        if obs is not None:
+            o = TensorDict({k: torch.cat([v, -v]) for k, v in obs.items()}, batch_size=[2 * obs.batch_size[0]])
+        if actions is not None:
+            a = torch.cat([actions, -actions])
+        return o, a
+
+    cfg = ppo_cfg()
+    cfg["algorithm"]["rnd_cfg"] = {"num_outputs": 4, "predictor_hidden_dims": [16], "target_hidden_dims": [16],
+                                   "weight": 0.5, "state_normalization": True}
+    cfg["algorithm"]["symmetry_cfg"] = {"data_augmentation_func": mirror, "use_data_augmentation": True,
+                                        "use_mirror_loss": True, "mirror_loss_coeff": 1.0}
+    cfg["obs_groups"]["rnd_state"] = ["critic"]
+    runner = OnPolicyRunner(small_env(), cfg, log_dir=None, device="cpu")
+    runner.learn(2)
+    rcfg = ppo_cfg()
+    for m in ("actor", "critic"):
+        rcfg[m]["class_name"] = "RNNModel"
+        rcfg[m]["rnn_type"] = "gru"
+        rcfg[m]["rnn_hidden_dim"] = 16
+    runner = OnPolicyRunner(small_env(), rcfg, log_dir=None, device="cpu")
+    runner.learn(2)
+
+
+def test_b200_cfg_rejects_unknown_keys():
+    from tt_rsl_rl_b200.algorithms.ppo import resolve_b200_cfg
+
+    assert resolve_b200_cfg({"graphs": False})["graphs"] is False
+    with pytest.raises(ValueError):
+        resolve_b200_cfg({"nope": 1})
+
+
+# ---- data parallel over gloo (two CPU ranks) ------------------------------------------------------------------------------
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _dp_worker(rank, world, port, out_dir, reduce):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "WORLD_SIZE": str(world),
+                       "RANK": str(rank), "LOCAL_RANK": str(rank)})
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from helpers import ppo_cfg as cfg_fn
+    from helpers import small_env as env_fn
+
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    torch.manual_seed(rank)
+    runner = OnPolicyRunner(env_fn(seed=rank), cfg_fn(), log_dir=None, device="cpu")
+    if not reduce:
+        runner.alg.reduce_parameters = lambda: None
+    runner.learn(2)
+    torch.save({k: v for k, v in runner.alg.actor.state_dict().items()}, os.path.join(out_dir, f"r{rank}.pt"))
+    torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize("reduce", [True, False])
+def test_gloo_replicas_stay_identical_only_with_reduction(reduce):
+    out = tempfile.mkdtemp()
+    torch.multiprocessing.spawn(_dp_worker, args=(2, _free_port(), out, reduce), nprocs=2, join=True)
+    a = torch.load(os.path.join(out, "r0.pt"))
+    b = torch.load(os.path.join(out, "r1.pt"))
+    same = all(torch.equal(a[k], b[k]) for k in a)
+    assert same == reduce
+
+
+# ---- host-side failure detection ---------------------------------------------------------------------------------------
+def _wd_worker(rank, port, out_dir):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from tt_rsl_rl_b200.parallel import CommTimeoutError
+    from tt_rsl_rl_b200.parallel.watchdog import RankWatchdog
+
+    store = dist.TCPStore("127.0.0.1", port, 2, rank == 0, timeout=timedelta(seconds=30))
+    wd = RankWatchdog(store, rank, 2, timeout_s=1.5)
+    wd.beat(0)
+    wd.check(0)
+    if rank == 1:
+        # rank 1 fails between iterations: it never publishes iteration 1
+        open(os.path.join(out_dir, "r1_exit"), "w").close()
+        return
+    wd.beat(1)
+    import time
+
+    t0 = time.monotonic()
+    try:
+        wd.check(1)
+        result = "no-error"
+    except CommTimeoutError as e:
+        result = f"timeout {time.monotonic() - t0:.2f} {e}"
+    with open(os.path.join(out_dir, "r0"), "w") as f:
+        f.write(result)
+
+
+def test_watchdog_reports_a_rank_that_left():
+    out = tempfile.mkdtemp()
+    torch.multiprocessing.spawn(_wd_worker, args=(_free_port(), out), nprocs=2, join=True)
+    res = open(os.path.join(out, "r0")).read()
+    assert res.startswith("timeout"), res
+    assert "[1]" in res
+    assert float(res.split()[1]) < 5.0

@@ -1,0 +1,387 @@
+"""PyTorch path vs the unmodified reference (upstream rsl_rl v5.5.2) on CPU: same math, same checkpoints.
+
+These tests import the reference from ``baseline/_ref`` (see ``baseline/__init__.py``) and compare module outputs,
+whole PPO / distillation updates on identical data and sample order, and checkpoint interchange in both directions.
+"""
+
+import copy
+
+import pytest
+import torch
+
+from helpers import ppo_cfg, small_env
+
+TOL = dict(atol=1e-5, rtol=1e-5)
+
+
+def _obs(env):
+    return env.get_observations()
+
+
+def _ref_models(ref, obs, groups, A, hidden, hetero=False):
+    from rsl_rl.models import MLPModel as RefMLP
+
+    dist = {"class_name": "HeteroscedasticGaussianDistribution" if hetero else "GaussianDistribution", "init_std": 1.0}
+    a = RefMLP(obs, groups, "actor", A, hidden_dims=hidden, obs_normalization=True, distribution_cfg=dist)
+    c = RefMLP(obs, groups, "critic", 1, hidden_dims=hidden, obs_normalization=True)
+    return a, c
+
+
+def _our_models(obs, groups, A, hidden, hetero=False):
+    from tt_rsl_rl_b200.models import MLPModel
+
+    dist = {"class_name": "HeteroscedasticGaussianDistribution" if hetero else "GaussianDistribution", "init_std": 1.0}
+    a = MLPModel(obs, groups, "actor", A, hidden_dims=hidden, obs_normalization=True, distribution_cfg=dist)
+    c = MLPModel(obs, groups, "critic", 1, hidden_dims=hidden, obs_normalization=True)
+    return a, c
+
+
+@pytest.mark.parametrize("hetero", [False, True])
+def test_mlp_model_state_dict_and_outputs(ref, hetero):
+    env = small_env()
+    obs = _obs(env)
+    groups = {"actor": ["policy"], "critic": ["critic"]}
+    torch.manual_seed(0)
+    ra, rc = _ref_models(ref, obs, groups, 3, [16, 8], hetero)
+    oa, oc = _our_models(obs, groups, 3, [16, 8], hetero)
+    assert list(ra.state_dict()) == list(oa.state_dict())
+    assert list(rc.state_dict()) == list(oc.state_dict())
+    oa.load_state_dict(ra.state_dict())
+    oc.load_state_dict(rc.state_dict())
+    x = torch.randn(50, 10) * 2
+    ra.obs_normalizer.update(x)
+    oa.obs_normalizer.update(x)
+    td = {"policy": x, "critic": torch.randn(50, 12)}
+    torch.testing.assert_close(oa(td), ra(td), **TOL)
+    ra(td, stochastic_output=True)
+    oa(td, stochastic_output=True)
+    acts = torch.randn(50, 3)
+    torch.testing.assert_close(oa.get_output_log_prob(acts), ra.get_output_log_prob(acts), **TOL)
+    torch.testing.assert_close(oa.output_entropy, ra.output_entropy, **TOL)
+    p_old = tuple(p.clone() for p in ra.output_distribution_params)
+    torch.testing.assert_close(oa.get_kl_divergence(p_old, oa.output_distribution_params),
+                               ra.get_kl_divergence(p_old, ra.output_distribution_params), **TOL)
+    torch.testing.assert_close(oc(td), rc(td), **TOL)
+
+
+def test_normalizer_and_discounted_normalizer(ref):
+    from rsl_rl.modules import EmpiricalDiscountedVariationNormalization as RefDisc
+    from rsl_rl.modules import EmpiricalNormalization as RefNorm
+
+    from tt_rsl_rl_b200.modules import EmpiricalDiscountedVariationNormalization, EmpiricalNormalization
+
+    torch.manual_seed(1)
+    a, b = RefNorm(7, until=300), EmpiricalNormalization(7, until=300)
+    for i in range(5):
+        x = torch.randn(100, 7) * (i + 1) + i
+        a.update(x)
+        b.update(x)
+        torch.testing.assert_close(b(x), a(x), **TOL)
+    assert int(a.count) == int(b.count) == 300
+    c, d = RefDisc([]), EmpiricalDiscountedVariationNormalization([])
+    for _ in range(5):
+        r = torch.rand(64)
+        torch.testing.assert_close(d(r), c(r), **TOL)
+
+
+def test_trajectory_split_and_unpad(ref):
+    from rsl_rl.utils import split_and_pad_trajectories as ref_split
+    from rsl_rl.utils import unpad_trajectories as ref_unpad
+
+    from tt_rsl_rl_b200.utils import split_and_pad_trajectories, unpad_trajectories
+
+    torch.manual_seed(2)
+    x = torch.randn(8, 5, 3)
+    dones = (torch.rand(8, 5, 1) < 0.3).float()
+    p1, m1 = ref_split(x, dones)
+    p2, m2 = split_and_pad_trajectories(x, dones)
+    torch.testing.assert_close(p2, p1)
+    assert torch.equal(m1, m2)
+    torch.testing.assert_close(unpad_trajectories(p2, m2), ref_unpad(p1, m1))
+    torch.testing.assert_close(unpad_trajectories(p2, m2), x)
+
+
+def _rollout_into(alg, env, T):
+    obs = env.get_observations()
+    with torch.inference_mode():
+        for _ in range(T):
+            a = alg.act(obs)
+            obs, r, d, e = env.step(a)
+            alg.process_env_step(obs, r, d, e)
+        alg.compute_returns(obs)
+
+
+def _make_ppo_pair(ref, T=8, **kw):
+    from rsl_rl.algorithms import PPO as RefPPO
+    from rsl_rl.storage import RolloutStorage as RefStorage
+    from rsl_rl.utils import resolve_obs_groups  # noqa: F401
+
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    env = small_env(num_envs=32)
+    obs = _obs(env)
+    groups = {"actor": ["policy"], "critic": ["critic"]}
+    torch.manual_seed(3)
+    ra, rc = _ref_models(ref, obs, groups, 3, [32, 16])
+    oa, oc = _our_models(obs, groups, 3, [32, 16])
+    oa.load_state_dict(ra.state_dict())
+    oc.load_state_dict(rc.state_dict())
+    rs = RefStorage("rl", 32, T, obs, [3], "cpu")
+    os_ = RolloutStorage("rl", 32, T, obs, [3], "cpu")
+    rp = RefPPO(ra, rc, rs, device="cpu", **kw)
+    op = PPO(oa, oc, os_, device="cpu", **kw)
+    return env, rp, op
+
+
+def test_gae_returns_match_reference(ref):
+    env, rp, op = _make_ppo_pair(ref)
+    # identical transitions into both storages
+    torch.manual_seed(4)
+    _rollout_into(rp, env, 8)
+    st_r, st_o = rp.storage, op.storage
+    for name in ("actions", "rewards", "dones", "values", "actions_log_prob"):
+        getattr(st_o, name).copy_(getattr(st_r, name))
+    st_o.distribution_params = tuple(p.clone() for p in st_r.distribution_params)
+    st_o.step = st_r.step
+    st_o.observations.copy_(st_r.observations)
+    last = env.get_observations()
+    op.compute_returns(last)
+    torch.testing.assert_close(st_o.returns, st_r.returns, **TOL)
+    torch.testing.assert_close(st_o.advantages, st_r.advantages, **TOL)
+
+
+@pytest.mark.parametrize("clipped", [True, False])
+def test_full_ppo_update_matches_reference(ref, clipped):
+    env, rp, op = _make_ppo_pair(ref, num_learning_epochs=3, num_mini_batches=4, use_clipped_value_loss=clipped)
+    torch.manual_seed(5)
+    _rollout_into(rp, env, 8)
+    st_r, st_o = rp.storage, op.storage
+    for name in ("actions", "rewards", "dones", "values", "actions_log_prob", "returns", "advantages"):
+        getattr(st_o, name).copy_(getattr(st_r, name))
+    st_o.distribution_params = tuple(p.clone() for p in st_r.distribution_params)
+    st_o.observations.copy_(st_r.observations)
+    st_o.step = st_r.step
+    torch.manual_seed(6)
+    loss_r = rp.update()
+    torch.manual_seed(6)  # same randperm in both generators
+    loss_o = op.update()
+    for k in loss_r:
+        assert loss_o[k] == pytest.approx(loss_r[k], rel=1e-5, abs=1e-7)
+    for (n1, p1), (n2, p2) in zip(rp.actor.state_dict().items(), op.actor.state_dict().items()):
+        assert n1 == n2
+        torch.testing.assert_close(p2, p1, atol=1e-5, rtol=1e-4)
+    for (n1, p1), (n2, p2) in zip(rp.critic.state_dict().items(), op.critic.state_dict().items()):
+        torch.testing.assert_close(p2, p1, atol=1e-5, rtol=1e-4)
+    assert op.learning_rate == pytest.approx(rp.learning_rate)
+
+
+def test_checkpoint_roundtrip_both_directions(ref, tmp_path):
+    from rsl_rl.runners import OnPolicyRunner as RefRunner
+
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    cfg = ppo_cfg()
+    env = small_env()
+    ours = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir=None, device="cpu")
+    ours.learn(2)
+    p1 = tmp_path / "ours.pt"
+    ours.save(str(p1))
+    theirs = RefRunner(small_env(), copy.deepcopy(cfg), log_dir=None, device="cpu")
+    theirs.load(str(p1))  # strict load of every state dict, optimizer included
+    probe = env.get_observations()
+    with torch.no_grad():
+        torch.testing.assert_close(theirs.get_inference_policy()(probe), ours.get_inference_policy()(probe))
+    assert theirs.current_learning_iteration == ours.current_learning_iteration
+    theirs.learn(1)
+    p2 = tmp_path / "theirs.pt"
+    theirs.save(str(p2))
+    ours2 = OnPolicyRunner(small_env(), copy.deepcopy(cfg), log_dir=None, device="cpu")
+    ours2.load(str(p2))
+    with torch.no_grad():
+        torch.testing.assert_close(ours2.get_inference_policy()(probe), theirs.get_inference_policy()(probe))
+    ours2.learn(1)
+
+
+def test_storage_generators_match_reference(ref):
+    from rsl_rl.storage import RolloutStorage as RefStorage
+
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    env = small_env(num_envs=16)
+    obs = _obs(env)
+    T = 6
+    rs = RefStorage("rl", 16, T, obs, [3], "cpu")
+    os_ = RolloutStorage("rl", 16, T, obs, [3], "cpu")
+    torch.manual_seed(7)
+    for t in range(T):
+        tr = type(rs).Transition()
+        tr.observations = {k: torch.randn_like(v) for k, v in obs.items()}
+        tr.actions = torch.randn(16, 3)
+        tr.rewards = torch.randn(16)
+        tr.dones = (torch.rand(16) < 0.3).float()
+        tr.values = torch.randn(16, 1)
+        tr.actions_log_prob = torch.randn(16)
+        tr.distribution_params = (torch.randn(16, 3), torch.rand(16, 3))
+        h = torch.randn(1, 16, 5)
+        tr.hidden_states = (h, (h.clone(), h.clone() * 2))
+        from tt_rsl_rl_b200.utils import TensorDict
+
+        tr.observations = TensorDict(tr.observations, batch_size=[16])
+        rs.add_transition(tr)
+        os_.add_transition(tr)
+    rs.returns.normal_()
+    os_.returns.copy_(rs.returns)
+    rs.advantages.normal_()
+    os_.advantages.copy_(rs.advantages)
+    torch.manual_seed(8)
+    b_ref = list(rs.mini_batch_generator(4, 2))
+    torch.manual_seed(8)
+    b_our = list(os_.mini_batch_generator(4, 2))
+    for x, y in zip(b_ref, b_our):
+        torch.testing.assert_close(y.actions, x.actions)
+        torch.testing.assert_close(y.advantages, x.advantages)
+        torch.testing.assert_close(y.observations["policy"], x.observations["policy"])
+    r_ref = list(rs.recurrent_mini_batch_generator(2, 1))
+    r_our = list(os_.recurrent_mini_batch_generator(2, 1))
+    for x, y in zip(r_ref, r_our):
+        torch.testing.assert_close(y.observations["policy"], x.observations["policy"])
+        assert torch.equal(y.masks, x.masks)
+        torch.testing.assert_close(y.hidden_states[0], x.hidden_states[0])
+        torch.testing.assert_close(y.hidden_states[1][1], x.hidden_states[1][1])
+
+
+def test_rnn_model_matches_reference(ref):
+    from rsl_rl.models import RNNModel as RefRNN
+
+    from tt_rsl_rl_b200.models import RNNModel
+
+    env = small_env(num_envs=8)
+    obs = _obs(env)
+    groups = {"actor": ["policy"], "critic": ["critic"]}
+    for rnn_type in ("gru", "lstm"):
+        torch.manual_seed(9)
+        r = RefRNN(obs, groups, "actor", 3, hidden_dims=[16], rnn_type=rnn_type, rnn_hidden_dim=12,
+                   distribution_cfg={"class_name": "GaussianDistribution"})
+        o = RNNModel(obs, groups, "actor", 3, hidden_dims=[16], rnn_type=rnn_type, rnn_hidden_dim=12,
+                     distribution_cfg={"class_name": "GaussianDistribution"})
+        assert list(r.state_dict()) == list(o.state_dict())
+        o.load_state_dict(r.state_dict())
+        for _ in range(3):
+            x = {"policy": torch.randn(8, 10), "critic": torch.randn(8, 12)}
+            torch.testing.assert_close(o(x), r(x), **TOL)
+            dones = (torch.rand(8) < 0.5).float()
+            r.reset(dones)
+            o.reset(dones)
+
+
+def test_distillation_update_matches_reference(ref):
+    from rsl_rl.algorithms import Distillation as RefDist
+    from rsl_rl.storage import RolloutStorage as RefStorage
+
+    from tt_rsl_rl_b200.algorithms import Distillation
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    from rsl_rl.models import MLPModel as RefMLP
+
+    env = small_env(num_envs=16)
+    obs = _obs(env)
+    groups = {"student": ["policy"], "teacher": ["critic"]}
+    torch.manual_seed(10)
+    rs_ = RefMLP(obs, groups, "student", 3, hidden_dims=[16, 16], distribution_cfg={"class_name":
+                                                                                        "GaussianDistribution"})
+    rt = RefMLP(obs, groups, "teacher", 3, hidden_dims=[16, 16])
+    os_ = MLPModel(obs, groups, "student", 3, hidden_dims=[16, 16], distribution_cfg={"class_name":
+                                                                                         "GaussianDistribution"})
+    ot = MLPModel(obs, groups, "teacher", 3, hidden_dims=[16, 16])
+    os_.load_state_dict(rs_.state_dict())
+    ot.load_state_dict(rt.state_dict())
+    T = 8
+    rd = RefDist(rs_, rt, RefStorage("distillation", 16, T, obs, [3], "cpu"), gradient_length=3, max_grad_norm=1.0)
+    od = Distillation(os_, ot, RolloutStorage("distillation", 16, T, obs, [3], "cpu"), gradient_length=3,
+                      max_grad_norm=1.0)
+    for alg in (rd, od):
+        e = small_env(num_envs=16, seed=4)
+        torch.manual_seed(11)
+        o = e.get_observations()
+        with torch.inference_mode():
+            for _ in range(T):
+                a = alg.act(o)
+                o, r, d, x = e.step(a)
+                alg.process_env_step(o, r, d, x)
+    lr_ = rd.update()
+    lo = od.update()
+    assert lo["behavior"] == pytest.approx(lr_["behavior"], rel=1e-5)
+    for p1, p2 in zip(rd.student.parameters(), od.student.parameters()):
+        torch.testing.assert_close(p2, p1, atol=1e-6, rtol=1e-5)
+
+
+def test_rnd_reward_and_loss_match_reference(ref):
+    from rsl_rl.extensions import RandomNetworkDistillation as RefRND
+
+    from tt_rsl_rl_b200.extensions import RandomNetworkDistillation
+
+    groups = {"rnd_state": ["critic"]}
+    kw = dict(num_states=12, obs_groups=groups, num_outputs=4, predictor_hidden_dims=[16], target_hidden_dims=[16],
+              state_normalization=True, reward_normalization=True, weight=0.5,
+              weight_schedule={"mode": "linear", "initial_step": 1, "final_step": 5, "final_value": 0.1})
+    torch.manual_seed(12)
+    r = RefRND(**kw)
+    o = RandomNetworkDistillation(**kw)
+    o.load_state_dict(r.state_dict())
+    for _ in range(4):
+        x = {"critic": torch.randn(20, 12)}
+        torch.testing.assert_close(o.get_intrinsic_reward(x), r.get_intrinsic_reward(x), **TOL)
+        torch.testing.assert_close(o.compute_loss(x), r.compute_loss(x), **TOL)
+        assert o.weight == pytest.approx(r.weight)
+        o.update_normalization(x)
+        r.update_normalization(x)
+
+
+def test_symmetry_matches_reference_and_probe(ref):
+    from rsl_rl.extensions import Symmetry as RefSym
+
+    from tt_rsl_rl_b200.extensions import Symmetry
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    perm = torch.tensor([1, 0, 2, 4, 3, 5, 6, 7, 9, 8])
+    sign = torch.tensor([1, 1, -1, 1, 1, -1, 1, 1, -1, 1.0])
+
+    def mirror(env, obs=None, actions=None):
+        o = a = None
+        if obs is not None:
+            o = TensorDict({"policy": torch.cat([obs["policy"], obs["policy"][:, perm] * sign])},
+                           batch_size=[2 * obs.batch_size[0]])
+        if actions is not None:
+            a = torch.cat([actions, -actions.flip(-1)])
+        return o, a
+
+    kw = dict(env=None, data_augmentation_func=mirror, use_data_augmentation=True, use_mirror_loss=True,
+              mirror_loss_coeff=1.0)
+    sym_o, sym_r = Symmetry(**kw), RefSym(**kw)
+    obs = TensorDict({"policy": torch.randn(5, 10)}, batch_size=[5])
+    actor = MLPModel(obs, {"actor": ["policy"]}, "actor", 3, hidden_dims=[8],
+                     distribution_cfg={"class_name": "GaussianDistribution"})
+
+    class B:
+        pass
+
+    b1, b2 = B(), B()
+    for b in (b1, b2):
+        b.observations = obs
+        b.actions = torch.randn(5, 3)
+        b.old_actions_log_prob = torch.randn(5, 1)
+        b.values = torch.randn(5, 1)
+        b.advantages = torch.randn(5, 1)
+        b.returns = torch.randn(5, 1)
+    sym_o.augment_batch(b1, 5)
+    sym_r.augment_batch(b2, 5)
+    assert b1.observations.batch_size[0] == 10 and b1.values.shape[0] == 10
+    torch.testing.assert_close(sym_o.compute_loss(actor, b1, 5), sym_r.compute_loss(actor, b2, 5))
+    maps = sym_o.probe_signed_permutations(obs, 3)
+    assert maps is not None
+    (p, s), (ap, as_) = maps[0]["policy"], maps[1]
+    assert torch.equal(p[1], perm) and torch.equal(s[1], sign)
+    assert torch.equal(ap[1], torch.tensor([2, 1, 0])) and torch.equal(as_[1], -torch.ones(3))

@@ -202,7 +202,7 @@ def test_adam_with_two_clip_groups_matches_torch():
     step = torch.zeros(2, dtype=torch.int64, device=dev)
     epoch = torch.zeros(1, dtype=torch.int32, device=dev)
     norm_partial = torch.zeros(grid * 4, device=dev)
-    barrier = torch.zeros(2, dtype=torch.int32, device=dev)
+    barrier = torch.zeros(4, dtype=torch.int32, device=dev)
     status = torch.zeros(4, dtype=torch.int32, device=dev)
     for it in range(3):
         gs = [torch.randn(*s, device=dev) * (3.0 if it == 0 else 0.01) for s in shapes]
@@ -236,7 +236,7 @@ def test_adaptive_learning_rate_rule():
     grid = C().adam_grid(torch.cuda.current_device())
     lr = torch.tensor([1e-3, 1e-3], device=dev)
     args = dict(step=torch.zeros(2, dtype=torch.int64, device=dev), epoch=torch.zeros(1, dtype=torch.int32, device=dev),
-                norm_partial=torch.zeros(grid * 4, device=dev), barrier=torch.zeros(2, dtype=torch.int32, device=dev))
+                norm_partial=torch.zeros(grid * 4, device=dev), barrier=torch.zeros(4, dtype=torch.int32, device=dev))
     send = torch.zeros(n + 4, device=dev)
     grads = torch.zeros(n + 4, device=dev)
     m = torch.zeros(n, device=dev)

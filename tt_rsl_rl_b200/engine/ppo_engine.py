@@ -141,13 +141,27 @@ class PPOEngine:
         n_ex = self.n_params + _TAIL
         self.exp_avg = torch.zeros(self.n_params, **f32)
         self.exp_avg_sq = torch.zeros(self.n_params, **f32)
-        self.send = [torch.zeros(n_ex, **f32), torch.zeros(n_ex, **f32)]
+        # ---- data parallel: symmetric send buffers shared with the peers (CUDA IPC) ----
+        self.world = alg.gpu_world_size
+        self.rank = alg.gpu_global_rank
+        self.timeout_ns = int(alg.b200_cfg["comm_timeout_ms"] * 1e6)
+        self.comm = None
+        if self.world > 1:
+            from ..parallel import PeerExchange
+
+            small = max(4 * self.n_params, 8 * (2 + 2 * max(self.Da, self.Dc)), 4096)
+            self.comm = PeerExchange.create(n_ex, small, rank=self.rank, world=self.world, device=dev,
+                                            timeout_ms=alg.b200_cfg["comm_timeout_ms"])
+            self.send = self.comm.send
+        else:
+            buf = torch.zeros(n_ex, **f32)
+            self.send = [buf, buf]
         self.grads = torch.zeros(n_ex, **f32)
         self.lr = torch.tensor([alg._learning_rate, alg._learning_rate], **f32)
         self.step = torch.zeros(2, dtype=torch.int64, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = torch.zeros(4, dtype=torch.int32, device=dev)
-        self.barrier = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.barrier = torch.zeros(4, dtype=torch.int32, device=dev)
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=dev)
         self.rng_counter = torch.zeros(1, dtype=torch.int64, device=dev)
         self.rng_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -259,19 +273,17 @@ class PPOEngine:
             "critic": torch.zeros(2 * self.stats_chunks * self.Dc, dtype=torch.float64, device=dev),
         }
 
-        # ---- data parallel ----
-        self.world = alg.gpu_world_size
-        self.rank = alg.gpu_global_rank
-        self.comm = None
-        if self.world > 1:
-            from ..parallel import PeerExchange
-
-            self.comm = PeerExchange.create(self.send, rank=self.rank, world=self.world, device=self.device)
-        self.timeout_ns = int(alg.b200_cfg["comm_timeout_ms"] * 1e6)
+        self.moments_local = {k: torch.zeros(2 + 2 * D, dtype=torch.float64, device=dev)
+                              for k, D in (("actor", self.Da), ("critic", self.Dc))}
+        self.moments_global = {k: torch.zeros_like(v) for k, v in self.moments_local.items()}
         self.use_graphs = bool(alg.b200_cfg["graphs"])
         self._update_graph = None
         self._updates_done = 0
         self.perm_override: torch.Tensor | None = None  # int32 [T*N]: explicit sample order (tests, reproducibility)
+        self._rollout_graph = None
+        self._rollout_calls = 0
+        self._rollout_obs = None
+        self._rollout_delta = None
 
     # ---- learning rate -----------------------------------------------------------------------------------------------
     def learning_rate(self) -> float:
@@ -408,14 +420,17 @@ class PPOEngine:
                 continue
             partial = self.colstats_partial[name]
             C.colstats(obs, self.total, obs.shape[1], D, partial)
-            if self.comm is not None:
-                partial = self.comm.allreduce_moments(partial)
-                rows = self.total * self.world
-            else:
-                rows = self.total
             until = -1 if norm.until is None else int(norm.until)
-            C.norm_update(partial, self.stats_chunks, rows, D, norm._mean.view(-1), norm._var.view(-1),
-                          norm._std.view(-1), norm.count, until, None)
+            mean, var, std = norm._mean.view(-1), norm._var.view(-1), norm._std.view(-1)
+            if self.comm is None:
+                C.norm_update(partial, self.stats_chunks, self.total, D, mean, var, std, norm.count, until, None,
+                              False)
+                continue
+            # global statistics: per-rank column sums, rank-ordered peer all-reduce, then the running update
+            local, glob = self.moments_local[name], self.moments_global[name]
+            C.norm_update(partial, self.stats_chunks, self.total, D, mean, var, std, norm.count, until, local, True)
+            self.comm.allreduce_f64(local, glob, self.status)
+            C.norm_update(glob[2:], 1, self.total * self.world, D, mean, var, std, norm.count, until, None, False)
 
     def _update_body(self) -> None:
         ext().counter_add(self.perm_key, 1)
@@ -426,7 +441,7 @@ class PPOEngine:
         self._normalizer_updates()
 
     def update(self) -> dict[str, float]:
-        if self.use_graphs and self._updates_done >= 1 and self.comm is None:
+        if self.use_graphs and self._updates_done >= 1:
             if self._update_graph is None:
                 self._update_graph = self._capture(self._update_body)
             self._update_graph.replay()
@@ -515,10 +530,11 @@ class PPOEngine:
     def broadcast_parameters(self) -> None:
         """Make every rank start from rank 0's parameters and normaliser buffers."""
         if self.comm is not None:
-            self.comm.broadcast_(self.flat)
+            self.comm.broadcast_(self.flat, status=self.status)
             for model in (self.actor, self.critic):
                 for b in model.buffers():
-                    self.comm.broadcast_(b)
+                    self.comm.broadcast_(b, status=self.status)
+            self._check_status()
         else:
             for model in (self.actor, self.critic):
                 for t in model.state_dict().values():
@@ -528,10 +544,46 @@ class PPOEngine:
 
     # ---- captured rollout (graph-capturable environments) -------------------------------------------------------------
     def can_capture_rollout(self, env, cfg) -> bool:
-        return False
+        """A rollout can be one CUDA graph when the environment only enqueues device work (``graph_capturable``)."""
+        return self.use_graphs and bool(getattr(env, "graph_capturable", False))
 
-    def run_captured_rollout(self, env, logger, cfg):  # pragma: no cover - enabled with can_capture_rollout
-        raise NotImplementedError
+    def _rollout_steps(self, env, logger, cfg):
+        obs = env.get_observations()
+        for _ in range(self.T):
+            actions = self.act(obs)
+            obs, rewards, dones, extras = env.step(actions)
+            self.process_env_step(obs, rewards, dones, extras)
+            logger.process_env_step(rewards, dones, extras, None)
+        return obs
+
+    def run_captured_rollout(self, env, logger, cfg):
+        """Run ``T`` x (act, env step, store, episode bookkeeping); from the second call on as one graph replay.
+
+        The graph replays exactly the captured work: the environment must keep returning the same observation,
+        reward and done tensors (updated in place), as ``graph_capturable`` environments do. Host-side counters of
+        the logger are advanced by the captured amount after each replay.
+        """
+        if self._rollout_calls == 0:
+            obs = self._rollout_steps(env, logger, cfg)
+        else:
+            if self._rollout_graph is None:
+                before = logger.host_state()
+                t0 = self.t
+                holder = {}
+                self._rollout_graph = self._capture(lambda: holder.setdefault("obs", self._rollout_steps(env, logger,
+                                                                                                         cfg)))
+                self._rollout_obs = holder["obs"]
+                self._rollout_delta = (before, logger.host_state())
+                logger.set_host_state(before)
+                self.t = t0
+            self._rollout_graph.replay()
+            logger.advance_host_state(*self._rollout_delta)
+            self.t += self.T
+            obs = self._rollout_obs
+        self._rollout_calls += 1
+        if cfg.get("check_for_nan", True):
+            self.raise_if_nonfinite()
+        return obs
 
 
 __all__ = ["PPOEngine"]

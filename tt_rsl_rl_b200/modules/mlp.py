@@ -18,6 +18,8 @@ class MLP(nn.Sequential):
     output has that trailing shape (used by two-headed distributions).
     """
 
+    __jit_unused_properties__ = ["linears", "activation_name"]
+
     def __init__(
         self,
         input_dim: int,

@@ -79,4 +79,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of tt_rsl_rl_b200";
   m.def("gemm", &gemm, "tcgen05 GEMM with fused MLP epilogues");
   rlb_register_kernels(m);
+  rlb_register_p2p(m);
 }

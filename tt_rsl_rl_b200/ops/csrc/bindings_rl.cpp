@@ -346,6 +346,10 @@ void adam_step(const Tensor& params, const Tensor& send0, const Tensor& send1, c
   TORCH_CHECK(lr.numel() >= static_cast<int64_t>(ng) && step.scalar_type() == torch::kInt64, "adam_step: lr/step");
   TORCH_CHECK(norm_partial.numel() >= grid * rlb::kAdamMaxGroups, "adam_step: norm_partial too small");
   TORCH_CHECK(world == 1 || (peer_send.has_value() && peer_flags.has_value()), "adam_step: peers required");
+  TORCH_CHECK(barrier.numel() >= 4 && barrier.element_size() == 4, "adam_step: barrier must hold 4 uint32");
+  if (world > 1) {
+    TORCH_CHECK(peer_send->numel() >= 2 * world && peer_flags->numel() >= world, "adam_step: peer tables too small");
+  }
   rlb::AdamArgs a{};
   a.params = P<float>(params);
   a.send[0] = P<float>(send0);
@@ -399,14 +403,16 @@ void colstats(const Tensor& x, int64_t rows, int64_t ld, int64_t dim, const Tens
 }
 
 void norm_update(const Tensor& partial, int64_t chunks, int64_t rows, int64_t dim, const Tensor& mean, const Tensor& var,
-                 const Tensor& std, const Tensor& count, int64_t until, const OptT& moments_out) {
+                 const Tensor& std, const Tensor& count, int64_t until, const OptT& moments_out, bool reduce_only) {
   TORCH_CHECK(count.scalar_type() == torch::kInt64, "norm_update: count must be int64");
   check_f32(mean, "mean");
   check_f32(var, "var");
   check_f32(std, "std");
   rlb::NormUpdateArgs a{P<const double>(partial), static_cast<int>(chunks), rows, static_cast<int>(dim),
                         P<float>(mean),           P<float>(var),            P<float>(std),
-                        reinterpret_cast<long long*>(count.data_ptr()), until, P<double>(moments_out)};
+                        reinterpret_cast<long long*>(count.data_ptr()), until, P<double>(moments_out),
+                        reduce_only ? 1 : 0};
+  TORCH_CHECK(!reduce_only || a.moments_out, "norm_update: reduce_only needs moments_out");
   ok(rlb::norm_update(a, cur()), "norm_update");
 }
 

@@ -3,3 +3,4 @@
 #include <torch/extension.h>
 
 void rlb_register_kernels(pybind11::module& m);
+void rlb_register_p2p(pybind11::module& m);

@@ -584,6 +584,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
           if (globaltimer_ns() - t0 > a.timeout_ns) {
             report_error(a.status, kTimeoutPeerFlag, 60 + r);
             peers_ok = 0;
+            atomicExch(a.barrier + 2, epoch);  // grid-wide abort of this exchange (tagged with the epoch)
             break;
           }
           __nanosleep(32);
@@ -631,6 +632,8 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     a.norm_partial[static_cast<size_t>(blockIdx.x) * kAdamMaxGroups + threadIdx.x] = s;
   }
   if (!grid_sync(a.barrier, a.status, a.timeout_ns)) return;
+  // every block takes the same decision: the exchange failed if any block's wait gave up
+  const bool all_ok = *reinterpret_cast<volatile unsigned int*>(a.barrier + 2) != epoch;
 
   // ---- phase 2: norms, clip coefficients, learning rate ----
   if (threadIdx.x < a.ngroups) {
@@ -653,7 +656,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     if (blockIdx.x == 0 && a.out_norms) a.out_norms[g] = norm;
   }
   __syncthreads();
-  if (!exchange_ok) {  // leave parameters untouched when the exchange failed; the status word reports it
+  if (!all_ok) {  // leave parameters untouched when the exchange failed; the status word reports it
     if (blockIdx.x == 0 && threadIdx.x == 0) *a.epoch = epoch;
     return;
   }
@@ -733,7 +736,7 @@ __global__ void norm_update_kernel(const NormUpdateArgs a) {
   __shared__ int skip;
   if (threadIdx.x == 0) {
     count0 = *a.count;
-    skip = (a.until >= 0 && count0 >= a.until) ? 1 : 0;
+    skip = (a.until >= 0 && count0 >= a.until && !a.reduce_only) ? 1 : 0;
   }
   __syncthreads();
   if (skip) return;
@@ -750,6 +753,7 @@ __global__ void norm_update_kernel(const NormUpdateArgs a) {
       a.moments_out[2 + c] = s;
       a.moments_out[2 + a.dim + c] = ss;
     }
+    if (a.reduce_only) continue;
     const double bm = s / n;
     const double bv = fmax(ss / n - bm * bm, 0.0);
     const float batch_mean = static_cast<float>(bm), batch_var = static_cast<float>(bv);
@@ -762,8 +766,8 @@ __global__ void norm_update_kernel(const NormUpdateArgs a) {
     a.std[c] = sqrtf(new_var);
   }
   if (threadIdx.x == 0) {
-    *a.count = count0 + a.rows;
     if (a.moments_out) a.moments_out[0] = n;
+    if (!a.reduce_only) *a.count = count0 + a.rows;
   }
 }
 

@@ -204,7 +204,7 @@ struct AdamArgs {
   uint64_t timeout_ns;
   // scratch
   float* norm_partial;              // [gridDim, ngroups]
-  unsigned int* barrier;            // [2] zero-initialised
+  unsigned int* barrier;            // [4] zero-initialised: grid-barrier count, generation, abort epoch
   unsigned int* status;
   float* out_norms;                 // [ngroups] (optional)
 };
@@ -234,6 +234,7 @@ struct NormUpdateArgs {
   long long* count;
   long long until;        // <0: no limit
   double* moments_out;    // optional [2 + 2*dim] copy of (n, unused, sum[dim], sumsq[dim]) for cross-rank combine
+  int reduce_only;        // 1: only write moments_out (the running statistics are left untouched)
 };
 cudaError_t norm_update(const NormUpdateArgs& a, cudaStream_t s);
 

@@ -98,7 +98,8 @@ class Logger:
             for key, value in info.items():
                 if key not in self._extras_sum:
                     self._extras_order.append(key)
-                    self._extras_sum[key] = torch.zeros((), device=self.device)
+                    with torch.inference_mode(False):  # a normal tensor: it is also reset outside inference mode
+                        self._extras_sum[key] = torch.zeros((), device=self.device)
                     self._extras_cnt[key] = 0
                 v = value if isinstance(value, torch.Tensor) else torch.tensor(float(value))
                 v = v.to(self.device, torch.float32).reshape(-1)
@@ -150,6 +151,25 @@ class Logger:
         self._fin_done[:n] = False
         self._step = 0
 
+    # ---- host-side state (for CUDA-graph capture of the rollout) ----------------------------------------------------
+    def host_state(self) -> tuple:
+        """Snapshot of the host-side counters that :meth:`process_env_step` advances."""
+        return self._step, dict(self._extras_cnt), list(self._extras_order)
+
+    def set_host_state(self, state: tuple) -> None:
+        self._step, cnt, order = state
+        self._extras_cnt = dict(cnt)
+        self._extras_order = list(order)
+
+    def advance_host_state(self, before: tuple, after: tuple) -> None:
+        """Apply the counter changes of one captured rollout (``before`` -> ``after``) after a graph replay."""
+        self._step += after[0] - before[0]
+        for key, n in after[1].items():
+            self._extras_cnt[key] = self._extras_cnt.get(key, 0) + n - before[1].get(key, 0)
+        for key in after[2]:
+            if key not in self._extras_order:
+                self._extras_order.append(key)
+
     # ---- per iteration -------------------------------------------------------------------------------------------------
     def log(self, it: int, start_it: int, total_it: int, collect_time: float, learn_time: float, loss_dict: dict,
             learning_rate: float, action_std: torch.Tensor, rnd_weight: float | None, print_minimal: bool = False,
@@ -170,8 +190,9 @@ class Logger:
             else:
                 self.writer.add_scalar("Episode/" + key, value, it)
                 extras_string += f"""{f"Mean episode {key}:":>{pad}} {value:.4f}\n"""
-        self._extras_sum.clear()
-        self._extras_cnt.clear()
+        for v in self._extras_sum.values():
+            v.zero_()  # persistent accumulators (captured rollouts add into them)
+        self._extras_cnt = {k: 0 for k in self._extras_cnt}
         self._extras_order.clear()
         for key, value in loss_dict.items():
             self.writer.add_scalar(f"Loss/{key}", value, it)

@@ -260,13 +260,19 @@ class TensorDict:
         return self.apply(lambda t: t.flatten(s, e), batch_size=new_batch)
 
     def view(self, *shape: Any) -> TensorDict:
+        return self._reshape(shape, copy_ok=False)
+
+    def reshape(self, *shape: Any) -> TensorDict:
+        return self._reshape(shape, copy_ok=True)
+
+    def _reshape(self, shape: tuple, copy_ok: bool) -> TensorDict:
         if len(shape) == 1 and isinstance(shape[0], (tuple, list, torch.Size)):
             shape = tuple(shape[0])
-        probe = torch.empty(self._batch_size, device="meta").view(*shape)
+        probe = torch.empty(self._batch_size, device="meta").reshape(*shape)
         nb = len(self._batch_size)
+        if copy_ok:
+            return self.apply(lambda t: t.reshape(*probe.shape, *t.shape[nb:]), batch_size=probe.shape)
         return self.apply(lambda t: t.view(*probe.shape, *t.shape[nb:]), batch_size=probe.shape)
-
-    reshape = view
 
     def transpose(self, dim0: int, dim1: int) -> TensorDict:
         nb = len(self._batch_size)
