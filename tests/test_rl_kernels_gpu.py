@@ -270,7 +270,7 @@ def test_normalizer_update_matches_module():
         part = torch.zeros(2 * chunks * D, dtype=torch.float64, device=dev)
         C().colstats(x, rows, D, D, part)
         C().norm_update(part, chunks, rows, D, mine._mean.view(-1), mine._var.view(-1), mine._std.view(-1), mine.count,
-                        -1, None)
+                        -1, None, False)
     torch.cuda.synchronize()
     assert int(mine.count) == int(ref.count)
     torch.testing.assert_close(mine._mean, ref._mean, atol=1e-5, rtol=1e-5)
