@@ -161,7 +161,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--total-envs", type=int, default=TOTAL_ENVS,
+                    help="environments over all ranks (default: the BASELINE configuration; smaller for profiling)")
     args = ap.parse_args()
+    total_envs = args.total_envs
     world, rank, local_rank = dist_info()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -185,7 +188,7 @@ def main() -> None:
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device(device),
                                              timeout=datetime.timedelta(seconds=120))
     torch.manual_seed(1 + rank)
-    n_local = TOTAL_ENVS // world
+    n_local = total_envs // world
 
     env = make_env(n_local, device, host_noise=False, seed=rank)
     runner = build_runner(args.impl, env, device)
@@ -195,7 +198,7 @@ def main() -> None:
     s_per_iter = timed_learn(runner, args.steps, args.warmup, world)
     if sampler:
         sampler.__exit__()
-    samples = TOTAL_ENVS * T_STEPS
+    samples = total_envs * T_STEPS
     value = samples / s_per_iter
 
     e2e = None
@@ -229,7 +232,7 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded linear-Gaussian env), random-init weights",
             "config": {"model": "PPO MLP actor-critic [512,256,128] ELU, obs 96/99, 29 actions",
-                       "global_batch": samples, "seq_len": T_STEPS, "num_envs_total": TOTAL_ENVS,
+                       "global_batch": samples, "seq_len": T_STEPS, "num_envs_total": total_envs,
                        "epochs": 5, "minibatches": 4, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (rollout arena >> 126 MB)"},
             "e2e": e2e,

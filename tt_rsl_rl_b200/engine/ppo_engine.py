@@ -64,8 +64,8 @@ class PPOEngine:
         dist = actor.distribution
         if not isinstance(dist, (GaussianDistribution, HeteroscedasticGaussianDistribution)):
             return "actor distribution is not Gaussian"
-        if dist.output_dim > 64:
-            return "more than 64 actions"
+        if dist.output_dim > 32:
+            return "more than 32 actions"
         if critic.distribution is not None:
             return "critic has a distribution"
         if critic.mlp.linears[-1].out_features != 1:

@@ -1,13 +1,15 @@
 // tcgen05 GEMM for sm_100a: TMA -> shared memory (128-byte swizzle) -> tcgen05.mma (fp32 accumulators in TMEM)
 // -> tcgen05.ld epilogue with the MLP's fused elementwise work.
 //
-// One CTA computes one 128 x BN output tile (split-K partials along blockIdx.z). Warp roles:
-//   warp 0      : TMA producer (one elected lane), multi-stage ring of shared-memory stages
+// Persistent kernel, one CTA per SM, static round-robin tile schedule (N tiles fastest, then M tiles, then split-K
+// slices). TMEM holds two 128 x BN fp32 accumulators so the epilogue of tile j overlaps the MMAs of tile j + 1, and
+// the TMA producer streams operand tiles through a ring of shared-memory stages across tile boundaries.
+//   warp 0      : TMA producer (one elected lane)
 //   warp 1      : TMEM allocator + MMA issuer (one elected lane)
 //   warps 2..9  : epilogue; warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32) = output rows of its quadrant, the two
 //                 warps of a quadrant splitting the column chunks
-// Short-K layers run two CTAs per SM (TMEM 2 x BN <= 512 columns) so that one CTA's epilogue overlaps the other's
-// main loop.
+// Barriers: full/empty per ring stage (TMA <-> MMA), acc_full/acc_empty per accumulator (MMA <-> epilogue). Every
+// wait is bounded (%globaltimer); a timeout records the site in the status word and the kernel unwinds.
 // No load uses cluster multicast: every CTA fetches its own tiles from this GPU's memory.
 //
 // The MLP layers of rsl_rl (rsl_rl/modules/mlp.py:91-95, Linear+ELU stacks) map onto three uses:
@@ -27,52 +29,78 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle atom row
-constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, splitting the column chunks
+constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMNBoxBytes = 64 * kBK * 2;  // one {64 MN x 64 K} box
 constexpr int kStageWords = 32 * 33;       // per-warp 32 x 32-word staging tile (+1 word padding per row)
+constexpr int kSmemLimit = 227 * 1024;
+
+// Resident CTAs per SM: the data-gradient epilogue also streams the ELU activations in, so it runs two CTAs per SM
+// (BN <= 128, TMEM 2 x 2 x 128 columns) to keep 16 epilogue warps per SM; the others run one CTA with BN up to 256.
+template <int EPI>
+struct CtasPerSm {
+  static constexpr int value = EPI == kEpiDgradElu ? 2 : 1;
+};
 
 template <int BN, int EPI>
 struct Cfg {
-  // Short-K layers (forward, data gradient) keep two CTAs per SM so one CTA's epilogue overlaps the other's
-  // main loop; the long-K weight-gradient GEMM uses a deeper pipeline with one CTA per SM.
-  static constexpr bool kLongK = EPI == kEpiPartialF32;
-  static constexpr int kStages = kLongK ? (BN == 256 ? 4 : 6) : (BN == 256 ? 2 : BN == 128 ? 3 : 4);
-  static constexpr int kMinBlocks = kLongK ? 1 : 2;
+  static constexpr int kMinBlocks = CtasPerSm<EPI>::value;
+  static constexpr int kSmemBudget = kMinBlocks == 1 ? kSmemLimit : (228 * 1024) / 2 - 1024;
   static constexpr int kBBytes = BN * kBK * 2;
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr bool kStaged = !(EPI == kEpiF32 || EPI == kEpiPartialF32);  // bf16 outputs go through smem
+  static constexpr int kStagingBytes = kStaged ? kEpiWarps * kStageWords * 4 : 0;
+  static constexpr int kColsumBytes = EPI == kEpiDgradElu ? 2 * 4 * BN * 4 : 0;  // double-buffered by tile parity
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kColsumBytes = 4 * BN * 4;
-  static constexpr int kPipeBytes = kStages * (kABytes + kBBytes);
-  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + kPipeBytes + kBarrierBytes + kColsumBytes;
-  static_assert(kPipeBytes >= kEpiWarps * 2 * kStageWords * 4, "epilogue staging must fit in the pipeline buffers");
+  static constexpr int kFixed = 1024 /*alignment slack*/ + kStagingBytes + kColsumBytes + kBarrierBytes;
+  static constexpr int kStagesFit = (kSmemBudget - kFixed) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators
+  static constexpr int kSmemBytes = kFixed + kStages * kStageBytes;
+  static_assert(kStages >= 2, "pipeline needs at least two stages");
+  static_assert(kTmemCols * kMinBlocks <= 512, "TMEM holds 512 columns per SM");
 };
 
+struct TileCoord {
+  int m0, n0, m_tile, split, kb_begin, kb_end;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(int t, int n_tiles, int m_tiles, int splits, int num_kb, int BN) {
+  TileCoord c;
+  const int n_tile = t % n_tiles;
+  const int rest = t / n_tiles;
+  c.m_tile = rest % m_tiles;
+  c.split = rest / m_tiles;
+  c.m0 = c.m_tile * kBM;
+  c.n0 = n_tile * BN;
+  c.kb_begin = static_cast<int>((static_cast<long long>(c.split) * num_kb) / splits);
+  c.kb_end = static_cast<int>((static_cast<long long>(c.split + 1) * num_kb) / splits);
+  return c;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
+__global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmParams p, int num_kb) {
+                   const GemmParams p, int num_kb, int n_tiles, int m_tiles, int splits) {
   using C = Cfg<BN, EPI>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * C::kBBytes);
+  uint32_t* staging = reinterpret_cast<uint32_t*>(sB + S * C::kBBytes);
+  float* colsum_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(staging) + C::kStagingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(colsum_s) + C::kColsumBytes);
   uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  float* colsum_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + C::kBarrierBytes);
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM;
-  const int n0 = blockIdx.y * BN;
-  const int splits = gridDim.z;
-  const int kb_begin = static_cast<int>((static_cast<long long>(blockIdx.z) * num_kb) / splits);
-  const int kb_end = static_cast<int>((static_cast<long long>(blockIdx.z + 1) * num_kb) / splits);
-  const int nkb = kb_end - kb_begin;
+  const int num_tiles = n_tiles * m_tiles * splits;
 
   if (threadIdx.x == 0) {
 #pragma unroll
@@ -80,7 +108,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -97,45 +128,51 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1)) {
-          report_error(p.status, kTimeoutSmemEmpty, 1);
-          break;
-        }
-        const int kc = (kb_begin + i) * kBK;
-        uint32_t bytes = 0;
-        if (!A_MN) {
-          bytes += kABytes;
-        } else {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
+        for (int kb = tc.kb_begin; kb < tc.kb_end; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1)) {
+            report_error(p.status, kTimeoutSmemEmpty, 1);
+            ok = false;
+            break;
+          }
+          const int kc = kb * kBK;
+          uint32_t bytes = 0;
+          if (!A_MN) {
+            bytes += kABytes;
+          } else {
 #pragma unroll
-          for (int j = 0; j < kBM / 64; ++j)
-            if (m0 + 64 * j < p.M) bytes += kMNBoxBytes;
-        }
-        if (!B_MN) {
-          bytes += C::kBBytes;
-        } else {
+            for (int j = 0; j < kBM / 64; ++j)
+              if (tc.m0 + 64 * j < p.M) bytes += kMNBoxBytes;
+          }
+          if (!B_MN) {
+            bytes += C::kBBytes;
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            if (n0 + 64 * j < p.N) bytes += kMNBoxBytes;
-        }
-        mbar_arrive_expect_tx(&full[s], bytes);
-        uint8_t* a_dst = sA + s * kABytes;
-        uint8_t* b_dst = sB + s * C::kBBytes;
-        if (!A_MN) {
-          tma_load_2d(a_dst, &tmA, &full[s], kc, m0);
-        } else {
+            for (int j = 0; j < BN / 64; ++j)
+              if (tc.n0 + 64 * j < p.N) bytes += kMNBoxBytes;
+          }
+          mbar_arrive_expect_tx(&full[s], bytes);
+          uint8_t* a_dst = sA + s * kABytes;
+          uint8_t* b_dst = sB + s * C::kBBytes;
+          if (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[s], kc, tc.m0);
+          } else {
 #pragma unroll
-          for (int j = 0; j < kBM / 64; ++j)
-            if (m0 + 64 * j < p.M) tma_load_2d(a_dst + j * kMNBoxBytes, &tmA, &full[s], m0 + 64 * j, kc);
-        }
-        if (!B_MN) {
-          tma_load_2d(b_dst, &tmB, &full[s], kc, n0);
-        } else {
+            for (int j = 0; j < kBM / 64; ++j)
+              if (tc.m0 + 64 * j < p.M) tma_load_2d(a_dst + j * kMNBoxBytes, &tmA, &full[s], tc.m0 + 64 * j, kc);
+          }
+          if (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[s], kc, tc.n0);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            if (n0 + 64 * j < p.N) tma_load_2d(b_dst + j * kMNBoxBytes, &tmB, &full[s], n0 + 64 * j, kc);
+            for (int j = 0; j < BN / 64; ++j)
+              if (tc.n0 + 64 * j < p.N) tma_load_2d(b_dst + j * kMNBoxBytes, &tmB, &full[s], tc.n0 + 64 * j, kc);
+          }
         }
       }
     }
@@ -143,59 +180,79 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = umma_idesc_bf16_f32(kBM, BN, A_MN, B_MN);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(&full[s], ph)) {
-          report_error(p.status, kTimeoutTmaFull, 2);
+      uint32_t g = 0;
+      bool ok = true;
+      int j = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++j) {
+        const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
+        const int b = j & 1;
+        const uint32_t use = static_cast<uint32_t>(j >> 1);
+        if (!mbar_wait(&acc_empty[b], (use & 1) ^ 1)) {
+          report_error(p.status, kTimeoutAccum, 4);
           break;
         }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + s * kABytes);
-        const uint32_t b_base = smem_u32(sB + s * C::kBBytes);
+        const uint32_t d = tmem + static_cast<uint32_t>(b * C::kAccCols);
+        for (int kb = tc.kb_begin; kb < tc.kb_end; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!mbar_wait(&full[s], ph)) {
+            report_error(p.status, kTimeoutTmaFull, 2);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * kABytes);
+          const uint32_t b_base = smem_u32(sB + s * C::kBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint64_t ad = A_MN ? umma_desc_sw128(a_base + kk * 2048, kMNBoxBytes, 1024)
-                                   : umma_desc_sw128(a_base + kk * 32, 16, 1024);
-          const uint64_t bd = B_MN ? umma_desc_sw128(b_base + kk * 2048, kMNBoxBytes, 1024)
-                                   : umma_desc_sw128(b_base + kk * 32, 16, 1024);
-          mma_bf16_ss(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? umma_desc_sw128(a_base + kk * 2048, kMNBoxBytes, 1024)
+                                     : umma_desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? umma_desc_sw128(b_base + kk * 2048, kMNBoxBytes, 1024)
+                                     : umma_desc_sw128(b_base + kk * 32, 16, 1024);
+            mma_bf16_ss(d, ad, bd, idesc, (kb > tc.kb_begin || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
+        mma_commit(&acc_full[b]);
       }
-      mma_commit(accum);
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
-    // Warp w may only read TMEM lanes [32 * (w % 4), +32): its quadrant q owns output rows m0 + 32q .. +31, one row
-    // per lane. The two warps of a quadrant take alternate column chunks. The pipeline buffers are idle once the
-    // accumulator is complete, so each warp stages its chunks there to make global loads/stores row-contiguous.
     const int ew = warp - 2;
-    const int q = warp & 3;
+    const int q = warp & 3;  // TMEM lane quadrant: hardware rule warp % 4
     const int half = ew >> 2;
-    const int row_base = m0 + q * 32;
-    const int row = row_base + lane;
-    const bool row_ok = row < p.M;
-    uint32_t* stage_aux = reinterpret_cast<uint32_t*>(smem) + ew * 2 * kStageWords;
-    uint32_t* stage_out = stage_aux + kStageWords;
-    uint32_t ok = 1;
-    if (lane == 0) ok = mbar_wait(accum, 0) ? 1u : 0u;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (!ok && lane == 0) report_error(p.status, kTimeoutAccum, 3);
-    tc_fence_after();
+    uint32_t* stage = staging + ew * kStageWords;
     constexpr int CW = BN >= 64 ? 64 : 32;  // columns per chunk (64 bf16 = one 128-byte line per row)
     constexpr int WPR = CW / 2;             // 32-bit words per row of a bf16 chunk
     constexpr int LPR = WPR / 4;            // lanes per row for 16-byte accesses
     constexpr int RPP = 32 / LPR;           // rows per pass
-    if (ok && nkb > 0) {
+    int j = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
+      const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
+      const int b = j & 1;
+      const uint32_t use = static_cast<uint32_t>(j >> 1);
+      uint32_t ok = 1;
+      if (lane == 0) ok = mbar_wait(&acc_full[b], use & 1) ? 1u : 0u;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) report_error(p.status, kTimeoutAccum, 3);
+        break;
+      }
+      tc_fence_after();
+      const int row_base = tc.m0 + q * 32;
+      const int row = row_base + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
+      float* cs = colsum_s + b * 4 * BN;
 #pragma unroll 1
       for (int c = half * CW; c < BN; c += 2 * CW) {
-        const int nb = n0 + c;
+        const int nb = tc.n0 + c;
         if (nb >= p.N) break;
         const int valid = min(CW, p.N - nb);
         const bool full_cols = valid == CW;
         if constexpr (EPI == kEpiDgradElu) {
-          // coalesced load of the aux (ELU output) chunk, RPP rows per pass
+          // coalesced load of the aux (ELU output) chunk into the staging tile, RPP rows per pass
           const __nv_bfloat16* aux = static_cast<const __nv_bfloat16*>(p.aux);
           const int lr = lane / LPR, lw = (lane % LPR) * 4;
           const bool vec = full_cols && (p.ld_aux % 8) == 0;
@@ -223,66 +280,69 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
               }
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) stage_aux[r * 33 + lw + i] = w4[i];
+            for (int i = 0; i < 4; ++i) stage[r * 33 + lw + i] = w4[i];
           }
           __syncwarp();
         }
 #pragma unroll
         for (int sub = 0; sub < CW; sub += 32) {
           float v[32];
-          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c + sub), v);
+          tmem_ld_32x32b_x32(acc + static_cast<uint32_t>(c + sub), v);
           tmem_wait_ld();
           const int sb = nb + sub;
           if constexpr (EPI == kEpiF32 || EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16) {
             if (p.bias != nullptr) {
+              // lane l holds bias[sb + l]; element j takes it by shuffle
+              const float my_bias = (sb + lane < p.N) ? __ldg(p.bias + sb + lane) : 0.f;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += (sb + j < p.N) ? __ldg(p.bias + sb + j) : 0.f;
+              for (int jj = 0; jj < 32; ++jj) v[jj] += __shfl_sync(0xffffffffu, my_bias, jj);
             }
           }
           if constexpr (EPI == kEpiBiasEluBf16) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.f ? v[j] : __expf(v[j]) - 1.0f;
+            for (int jj = 0; jj < 32; ++jj) v[jj] = v[jj] > 0.f ? v[jj] : __expf(v[jj]) - 1.0f;
           }
           if constexpr (EPI == kEpiDgradElu) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const uint32_t w = stage_aux[lane * 33 + (sub + j) / 2];
+            for (int jj = 0; jj < 32; jj += 2) {
+              const uint32_t w = stage[lane * 33 + (sub + jj) / 2];
               __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w);
-              v[j] *= elu_grad_from_out(__low2float(h2));
-              v[j + 1] *= elu_grad_from_out(__high2float(h2));
+              v[jj] *= elu_grad_from_out(__low2float(h2));
+              v[jj + 1] *= elu_grad_from_out(__high2float(h2));
             }
             if (!row_ok) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+              for (int jj = 0; jj < 32; ++jj) v[jj] = 0.f;
             }
           }
           if constexpr (EPI == kEpiF32 || EPI == kEpiPartialF32) {
-            float* o = static_cast<float*>(p.out) + (EPI == kEpiPartialF32 ? blockIdx.z * p.split_stride : 0ll) +
+            float* o = static_cast<float*>(p.out) +
+                       (EPI == kEpiPartialF32 ? static_cast<long long>(tc.split) * p.split_stride : 0ll) +
                        static_cast<size_t>(row) * p.ldo + sb;
             if (row_ok) {
               if (sb + 32 <= p.N && (p.ldo % 4) == 0) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                  *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                for (int jj = 0; jj < 32; jj += 4)
+                  *reinterpret_cast<float4*>(o + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
               } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (sb + j < p.N) o[j] = v[j];
+                for (int jj = 0; jj < 32; ++jj)
+                  if (sb + jj < p.N) o[jj] = v[jj];
               }
             }
           } else {
+            // each lane rewrites the words of its own row that it has just read (aux), so one tile suffices
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) stage_out[lane * 33 + (sub + j) / 2] = pack_bf16x2(v[j], v[j + 1]);
+            for (int jj = 0; jj < 32; jj += 2) stage[lane * 33 + (sub + jj) / 2] = pack_bf16x2(v[jj], v[jj + 1]);
           }
           if constexpr (EPI == kEpiDgradElu) {
             if (p.colsum != nullptr) {
-              // per-column sums; columns at or past N are never written out
-              const float s = warp_transpose_reduce32(v);
-              colsum_s[q * BN + c + sub + lane] = s;
+              const float sum = warp_transpose_reduce32(v);  // per-column sums over this warp's 32 rows
+              cs[q * BN + c + sub + lane] = sum;
             }
           }
         }
-        if constexpr (EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16 || EPI == kEpiDgradElu) {
+        if constexpr (C::kStaged) {
           __syncwarp();
           __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(p.out);
           const int lr = lane / LPR, lw = (lane % LPR) * 4;
@@ -293,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
             const int gr = row_base + r;
             if (gr < p.M) {
               __nv_bfloat16* dst = outp + static_cast<size_t>(gr) * p.ldo + nb + 2 * lw;
-              const uint32_t* src = stage_out + r * 33 + lw;
+              const uint32_t* src = stage + r * 33 + lw;
               if (vec) {
                 *reinterpret_cast<uint4*>(dst) = make_uint4(src[0], src[1], src[2], src[3]);
               } else {
@@ -310,15 +370,19 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN, EPI>::kMinBlocks)
           __syncwarp();
         }
       }
-    }
-    if constexpr (EPI == kEpiDgradElu) {
-      if (p.colsum != nullptr) {
-        named_barrier_sync(1, kEpiWarps * 32);
-        const int t = threadIdx.x - 64;
-        for (int n = t; n < BN; n += kEpiWarps * 32) {
-          if (n0 + n < p.N) {
-            const float s = colsum_s[n] + colsum_s[BN + n] + colsum_s[2 * BN + n] + colsum_s[3 * BN + n];
-            p.colsum[static_cast<size_t>(blockIdx.x) * p.N + n0 + n] = s;
+      // accumulator b fully read by this warp: hand it back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if constexpr (EPI == kEpiDgradElu) {
+        if (p.colsum != nullptr) {
+          named_barrier_sync(1, kEpiWarps * 32);
+          const int tt = threadIdx.x - 64;
+          for (int n = tt; n < BN; n += kEpiWarps * 32) {
+            if (tc.n0 + n < p.N) {
+              const float sum = cs[n] + cs[BN + n] + cs[2 * BN + n] + cs[3 * BN + n];
+              p.colsum[static_cast<size_t>(tc.m_tile) * p.N + tc.n0 + n] = sum;
+            }
           }
         }
       }
@@ -364,6 +428,17 @@ bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
   return r == CUDA_SUCCESS;
 }
 
+int sm_count() {
+  static int n = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  });
+  return n;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN, EPI>;
@@ -379,8 +454,13 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   ok = ok && (B_MN ? make_map(&tb, p.b, p.N, p.K, p.ldb, 64, 64) : make_map(&tb, p.b, p.K, p.N, p.ldb, 64, BN));
   if (!ok) return cudaErrorInvalidValue;
   const int num_kb = (p.K + kBK - 1) / kBK;
-  dim3 grid((p.M + kBM - 1) / kBM, (p.N + BN - 1) / BN, p.splits);
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p, num_kb);
+  const int m_tiles = (p.M + kBM - 1) / kBM;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const long long tiles = static_cast<long long>(m_tiles) * n_tiles * p.splits;
+  if (tiles > (1ll << 31) - 1) return cudaErrorInvalidValue;
+  const long long slots = static_cast<long long>(sm_count()) * C::kMinBlocks;
+  const int grid = static_cast<int>(tiles < slots ? tiles : slots);
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p, num_kb, n_tiles, m_tiles, p.splits);
   return cudaGetLastError();
 }
 
@@ -388,8 +468,9 @@ template <bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_bn(const GemmParams& p, cudaStream_t stream) {
   if (!B_MN && p.N <= 32) return launch_t<32, A_MN, B_MN, EPI>(p, stream);
   if (p.N <= 64) return launch_t<64, A_MN, B_MN, EPI>(p, stream);
-  if (p.N <= 128) return launch_t<128, A_MN, B_MN, EPI>(p, stream);
-  return launch_t<256, A_MN, B_MN, EPI>(p, stream);
+  if (p.N <= 128 || EPI == kEpiDgradElu) return launch_t<128, A_MN, B_MN, EPI>(p, stream);
+  if constexpr (EPI != kEpiDgradElu) return launch_t<256, A_MN, B_MN, EPI>(p, stream);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace
