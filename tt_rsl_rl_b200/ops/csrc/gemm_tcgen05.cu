@@ -36,11 +36,12 @@ constexpr int kMNBoxBytes = 64 * kBK * 2;  // one {64 MN x 64 K} box
 constexpr int kStageWords = 32 * 33;       // per-warp 32 x 32-word staging tile (+1 word padding per row)
 constexpr int kSmemLimit = 227 * 1024;
 
-// Resident CTAs per SM: the data-gradient epilogue also streams the ELU activations in, so it runs two CTAs per SM
-// (BN <= 128, TMEM 2 x 2 x 128 columns) to keep 16 epilogue warps per SM; the others run one CTA with BN up to 256.
+// Resident CTAs per SM: the bf16-output epilogues (forward activations, data gradients that also stream the ELU
+// activations in) run two CTAs per SM (BN <= 128, TMEM 2 x 2 x 128 columns) to keep 16 epilogue warps per SM; the
+// fp32-output epilogues run one CTA with BN up to 256.
 template <int EPI>
 struct CtasPerSm {
-  static constexpr int value = EPI == kEpiDgradElu ? 2 : 1;
+  static constexpr int value = (EPI == kEpiDgradElu || EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16) ? 2 : 1;
 };
 
 template <int BN, int EPI>
@@ -468,8 +469,8 @@ template <bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_bn(const GemmParams& p, cudaStream_t stream) {
   if (!B_MN && p.N <= 32) return launch_t<32, A_MN, B_MN, EPI>(p, stream);
   if (p.N <= 64) return launch_t<64, A_MN, B_MN, EPI>(p, stream);
-  if (p.N <= 128 || EPI == kEpiDgradElu) return launch_t<128, A_MN, B_MN, EPI>(p, stream);
-  if constexpr (EPI != kEpiDgradElu) return launch_t<256, A_MN, B_MN, EPI>(p, stream);
+  if (p.N <= 128 || CtasPerSm<EPI>::value == 2) return launch_t<128, A_MN, B_MN, EPI>(p, stream);
+  if constexpr (CtasPerSm<EPI>::value == 1) return launch_t<256, A_MN, B_MN, EPI>(p, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -320,10 +320,10 @@ __global__ void __launch_bounds__(256) gather_minibatch_kernel(const GatherArgs 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// PPO loss: one thread per minibatch row (A <= 32), 128 rows per block. Each thread walks its row's actions with
+// PPO loss: one thread per minibatch row (A <= 32), 64 rows per block. Each thread walks its row's actions with
 // independent loads; per-column block sums (bias / std gradients) use the transposing warp reduction.
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kLossThreads = 128;
+constexpr int kLossThreads = 64;
 constexpr int kLossMaxA = 32;
 
 // torch.max(a, b) backward: the larger input gets the gradient, ties split it in halves.
@@ -336,14 +336,30 @@ __global__ void __launch_bounds__(kLossThreads) ppo_loss_kernel(const PpoLossArg
   __shared__ float s_raw[kLossMaxA];
   __shared__ float s_cols[kLossThreads / 32][3][32];  // per warp: mean grads, std grads (param or hetero head)
   __shared__ float s_sc[kLossThreads / 32][5];
+  // per warp: its 32 rows of stored actions / old means / old stds, gathered with coalesced row loads
+  __shared__ float s_rows[kLossThreads / 32][3][32][kLossMaxA + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x < a.A) s_raw[threadIdx.x] = a.hetero ? 0.f : a.std_param[threadIdx.x];
-  __syncthreads();
   const float invB = 1.0f / static_cast<float>(a.B);
   const int A = a.A;
   const int head_cols = a.hetero ? 2 * A : A;
   const int i = blockIdx.x * kLossThreads + threadIdx.x;
   const bool valid = i < a.B;
+  {
+    // lane r of the warp owns row (warp base + r); lanes load one row at a time, one column per lane
+    const int my_src = valid ? __ldg(a.idx + i) : 0;
+    const int row_base = blockIdx.x * kLossThreads + warp * 32;
+    for (int r = 0; r < 32; ++r) {
+      const int src = __shfl_sync(0xffffffffu, my_src, r);
+      if (row_base + r < a.B && lane < A) {
+        const size_t o = static_cast<size_t>(src) * A + lane;
+        s_rows[warp][0][r][lane] = __ldg(a.st_actions + o);
+        s_rows[warp][1][r][lane] = __ldg(a.st_mean + o);
+        s_rows[warp][2][r][lane] = __ldg(a.st_std + o);
+      }
+    }
+  }
+  __syncthreads();
   float g_mu[kLossMaxA], g_sd[kLossMaxA];
 #pragma unroll
   for (int j = 0; j < kLossMaxA; ++j) g_mu[j] = g_sd[j] = 0.f;
@@ -351,9 +367,9 @@ __global__ void __launch_bounds__(kLossThreads) ppo_loss_kernel(const PpoLossArg
   if (valid) {
     const int src = __ldg(a.idx + i);
     const float* h = a.head + static_cast<size_t>(i) * a.ld_head;
-    const float* act = a.st_actions + static_cast<size_t>(src) * A;
-    const float* om = a.st_mean + static_cast<size_t>(src) * A;
-    const float* os = a.st_std + static_cast<size_t>(src) * A;
+    const float* act = s_rows[warp][0][lane];
+    const float* om = s_rows[warp][1][lane];
+    const float* os = s_rows[warp][2][lane];
     float lp = 0.f, ent = 0.f, kl = 0.f;
 #pragma unroll
     for (int j = 0; j < kLossMaxA; ++j) {
@@ -361,7 +377,7 @@ __global__ void __launch_bounds__(kLossThreads) ppo_loss_kernel(const PpoLossArg
         const float mu = h[j];
         const float raw = a.hetero ? h[A + j] : s_raw[j];
         const float sd = head_std(raw, a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
-        const float x = __ldg(act + j), omu = __ldg(om + j), osd = __ldg(os + j);
+        const float x = act[j], omu = om[j], osd = os[j];
         const float inv_sd = 1.0f / sd;
         const float z = (x - mu) * inv_sd;
         const float lsd = logf(sd);
@@ -409,7 +425,7 @@ __global__ void __launch_bounds__(kLossThreads) ppo_loss_kernel(const PpoLossArg
         const float mu = h[j];
         const float raw = a.hetero ? h[A + j] : s_raw[j];
         const float sd = head_std(raw, a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
-        const float x = __ldg(act + j);
+        const float x = act[j];
         const float inv_sd = 1.0f / sd;
         const float diff = x - mu;
         const float dmu = d_lp * diff * inv_sd * inv_sd;
