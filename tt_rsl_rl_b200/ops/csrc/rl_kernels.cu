@@ -320,11 +320,12 @@ __global__ void __launch_bounds__(256) gather_minibatch_kernel(const GatherArgs 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// PPO loss: one thread per minibatch row (A <= 32), 64 rows per block. Each thread walks its row's actions with
-// independent loads; per-column block sums (bias / std gradients) use the transposing warp reduction.
+// PPO loss: one warp per row (lane j handles actions j and j + 32); 16 warps x 4 rows per block
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kLossThreads = 64;
-constexpr int kLossMaxA = 32;
+constexpr int kLossWarps = 16;
+constexpr int kLossRowsPerWarp = 4;
+constexpr int kLossRowsPerBlock = kLossWarps * kLossRowsPerWarp;
+constexpr int kLossMaxA = 64;
 
 // torch.max(a, b) backward: the larger input gets the gradient, ties split it in halves.
 __device__ __forceinline__ void max_grad_split(float a, float b, float& ga, float& gb) {
@@ -332,76 +333,67 @@ __device__ __forceinline__ void max_grad_split(float a, float b, float& ga, floa
   gb = b > a ? 1.f : (a == b ? 0.5f : 0.f);
 }
 
-__global__ void __launch_bounds__(kLossThreads) ppo_loss_kernel(const PpoLossArgs a) {
-  __shared__ float s_raw[kLossMaxA];
-  __shared__ float s_cols[kLossThreads / 32][3][32];  // per warp: mean grads, std grads (param or hetero head)
-  __shared__ float s_sc[kLossThreads / 32][5];
-  // per warp: its 32 rows of stored actions / old means / old stds, gathered with coalesced row loads
-  __shared__ float s_rows[kLossThreads / 32][3][32][kLossMaxA + 1];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x < a.A) s_raw[threadIdx.x] = a.hetero ? 0.f : a.std_param[threadIdx.x];
+__global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLossArgs a) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const float invB = 1.0f / static_cast<float>(a.B);
-  const int A = a.A;
-  const int head_cols = a.hetero ? 2 * A : A;
-  const int i = blockIdx.x * kLossThreads + threadIdx.x;
-  const bool valid = i < a.B;
-  {
-    // lane r of the warp owns row (warp base + r); lanes load one row at a time, one column per lane
-    const int my_src = valid ? __ldg(a.idx + i) : 0;
-    const int row_base = blockIdx.x * kLossThreads + warp * 32;
-    for (int r = 0; r < 32; ++r) {
-      const int src = __shfl_sync(0xffffffffu, my_src, r);
-      if (row_base + r < a.B && lane < A) {
-        const size_t o = static_cast<size_t>(src) * A + lane;
-        s_rows[warp][0][r][lane] = __ldg(a.st_actions + o);
-        s_rows[warp][1][r][lane] = __ldg(a.st_mean + o);
-        s_rows[warp][2][r][lane] = __ldg(a.st_std + o);
-      }
-    }
-  }
-  __syncthreads();
-  float g_mu[kLossMaxA], g_sd[kLossMaxA];
-#pragma unroll
-  for (int j = 0; j < kLossMaxA; ++j) g_mu[j] = g_sd[j] = 0.f;
-  float sc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};  // surrogate, value loss, entropy, kl, d value
-  if (valid) {
-    const int src = __ldg(a.idx + i);
+  const int head_cols = a.hetero ? 2 * a.A : a.A;
+  // per-lane accumulators: columns lane and lane + 32 of the head gradient, std gradient
+  float acc_dh[4] = {0.f, 0.f, 0.f, 0.f};  // head cols lane, lane+32, lane+64, lane+96
+  float acc_dstd[2] = {0.f, 0.f};
+  float acc_surr = 0.f, acc_val = 0.f, acc_ent = 0.f, acc_kl = 0.f, acc_dv = 0.f;
+
+  const int row0 = blockIdx.x * kLossRowsPerBlock + warp * kLossRowsPerWarp;
+  for (int rr = 0; rr < kLossRowsPerWarp; ++rr) {
+    const int i = row0 + rr;
+    if (i >= a.B) break;
+    const int src = a.idx[i];
     const float* h = a.head + static_cast<size_t>(i) * a.ld_head;
-    const float* act = s_rows[warp][0][lane];
-    const float* om = s_rows[warp][1][lane];
-    const float* os = s_rows[warp][2][lane];
+    float mu[2], sd[2], raw[2], act[2], omu[2], osd[2];
     float lp = 0.f, ent = 0.f, kl = 0.f;
 #pragma unroll
-    for (int j = 0; j < kLossMaxA; ++j) {
-      if (j < A) {
-        const float mu = h[j];
-        const float raw = a.hetero ? h[A + j] : s_raw[j];
-        const float sd = head_std(raw, a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
-        const float x = act[j], omu = om[j], osd = os[j];
-        const float inv_sd = 1.0f / sd;
-        const float z = (x - mu) * inv_sd;
-        const float lsd = logf(sd);
+    for (int k = 0; k < 2; ++k) {
+      const int j = lane + 32 * k;
+      mu[k] = sd[k] = raw[k] = act[k] = omu[k] = osd[k] = 0.f;
+      if (j < a.A) {
+        mu[k] = h[j];
+        raw[k] = a.hetero ? h[a.A + j] : a.std_param[j];
+        sd[k] = head_std(raw[k], a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
+        const size_t o = static_cast<size_t>(src) * a.A + j;
+        act[k] = a.st_actions[o];
+        omu[k] = a.st_mean[o];
+        osd[k] = a.st_std[o];
+        const float z = (act[k] - mu[k]) / sd[k];
+        const float lsd = logf(sd[k]);
         lp += -0.5f * z * z - lsd - kLogSqrt2Pi;
         ent += 0.5f + kLogSqrt2Pi + lsd;
         // KL(old || new) for diagonal Gaussians
-        const float r = osd * inv_sd;
-        const float t = (omu - mu) * inv_sd;
-        kl += 0.5f * (r * r + t * t - 1.0f) - logf(r);
+        const float vr = (osd[k] / sd[k]) * (osd[k] / sd[k]);
+        const float t1 = ((omu[k] - mu[k]) / sd[k]) * ((omu[k] - mu[k]) / sd[k]);
+        kl += 0.5f * (vr + t1 - 1.0f - logf(vr));
       }
     }
-    // clipped surrogate
-    const float adv = a.adv_override ? a.adv_override[i] : __ldg(a.st_adv + src);
-    const float ratio = expf(lp - __ldg(a.st_logp + src));
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      lp += __shfl_xor_sync(0xffffffffu, lp, off);
+      ent += __shfl_xor_sync(0xffffffffu, ent, off);
+      kl += __shfl_xor_sync(0xffffffffu, kl, off);
+    }
+    // surrogate (identical on every lane)
+    const float adv = a.adv_override ? a.adv_override[i] : a.st_adv[src];
+    const float ratio = expf(lp - a.st_logp[src]);
     const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
     const float rc = fminf(fmaxf(ratio, lo), hi);
     const float s1 = -adv * ratio, s2 = -adv * rc;
     float g1, g2;
     max_grad_split(s1, s2, g1, g2);
     const float in_rng = (ratio >= lo && ratio <= hi) ? 1.f : 0.f;
-    const float d_lp = (g1 * -adv + g2 * -adv * in_rng) * invB * ratio;
-    // clipped value loss
+    const float d_ratio = (g1 * -adv + g2 * -adv * in_rng) * invB;
+    const float d_lp = d_ratio * ratio;
+    // value loss
     const float v = a.value[static_cast<size_t>(i) * a.ld_value];
-    const float ret = __ldg(a.st_ret + src), vold = __ldg(a.st_val + src);
+    const float ret = a.st_ret[src];
+    const float vold = a.st_val[src];
     float vloss, dv;
     if (a.clipped_value) {
       const float dvv = v - vold;
@@ -417,85 +409,90 @@ __global__ void __launch_bounds__(kLossThreads) ppo_loss_kernel(const PpoLossArg
       dv = 2.f * (v - ret);
     }
     dv *= a.value_coef * invB;
-    // gradients w.r.t. the head outputs
+    // gradients w.r.t. mean and std of each action
     __nv_bfloat16* dh = static_cast<__nv_bfloat16*>(a.d_head) + static_cast<size_t>(i) * a.ld_dhead;
 #pragma unroll
-    for (int j = 0; j < kLossMaxA; ++j) {
-      if (j < A) {
-        const float mu = h[j];
-        const float raw = a.hetero ? h[A + j] : s_raw[j];
-        const float sd = head_std(raw, a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
-        const float x = act[j];
-        const float inv_sd = 1.0f / sd;
-        const float diff = x - mu;
-        const float dmu = d_lp * diff * inv_sd * inv_sd;
-        const float dsd = d_lp * (diff * diff * inv_sd * inv_sd - 1.0f) * inv_sd - a.entropy_coef * invB * inv_sd;
+    for (int k = 0; k < 2; ++k) {
+      const int j = lane + 32 * k;
+      if (j < a.A) {
+        const float inv_var = 1.0f / (sd[k] * sd[k]);
+        const float diff = act[k] - mu[k];
+        const float dmu = d_lp * diff * inv_var;
+        const float dsd = d_lp * (diff * diff * inv_var / sd[k] - 1.0f / sd[k]) - a.entropy_coef * invB / sd[k];
         // chain through the std parameterisation (clamp passes the gradient on [lo, hi] inclusive)
         float dsd_raw;
         if (a.log_std) {
-          const float in = (raw >= a.log_std_lo && raw <= a.log_std_hi) ? 1.f : 0.f;
-          dsd_raw = dsd * sd * in;
+          const float in = (raw[k] >= a.log_std_lo && raw[k] <= a.log_std_hi) ? 1.f : 0.f;
+          dsd_raw = dsd * sd[k] * in;
         } else {
-          const float in = (raw >= a.std_lo && raw <= a.std_hi) ? 1.f : 0.f;
+          const float in = (raw[k] >= a.std_lo && raw[k] <= a.std_hi) ? 1.f : 0.f;
           dsd_raw = dsd * in;
         }
-        g_mu[j] = dmu;
-        g_sd[j] = dsd_raw;
+        dh[j] = __float2bfloat16_rn(dmu);
+        acc_dh[k] += dmu;
+        if (a.hetero) {
+          dh[a.A + j] = __float2bfloat16_rn(dsd_raw);
+          acc_dh[2 + k] += dsd_raw;
+        } else {
+          acc_dstd[k] += dsd_raw;
+        }
       }
     }
-    // bf16 gradient row: [dmean | dstd (hetero) | zero padding]
-#pragma unroll
-    for (int j = 0; j < kLossMaxA; ++j) {
-      if (j < A) {
-        dh[j] = __float2bfloat16_rn(g_mu[j]);
-        if (a.hetero) dh[A + j] = __float2bfloat16_rn(g_sd[j]);
-      }
+    // zero the padding columns of the head gradient
+    for (int c = head_cols + lane; c < a.ld_dhead; c += 32) dh[c] = __float2bfloat16_rn(0.f);
+    if (lane == 0) {
+      __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.d_value) + static_cast<size_t>(i) * a.ld_dvalue;
+      dvp[0] = __float2bfloat16_rn(dv);
+      for (int c = 1; c < a.ld_dvalue; ++c) dvp[c] = __float2bfloat16_rn(0.f);
+      acc_surr += fmaxf(s1, s2) * invB;
+      acc_val += vloss * invB;
+      acc_ent += ent * invB;
+      acc_kl += kl * invB;
+      acc_dv += dv;
     }
-    for (int c = head_cols; c < a.ld_dhead; ++c) dh[c] = __float2bfloat16_rn(0.f);
-    __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.d_value) + static_cast<size_t>(i) * a.ld_dvalue;
-    dvp[0] = __float2bfloat16_rn(dv);
-    for (int c = 1; c < a.ld_dvalue; ++c) dvp[c] = __float2bfloat16_rn(0.f);
-    sc[0] = fmaxf(s1, s2) * invB;
-    sc[1] = vloss * invB;
-    sc[2] = ent * invB;
-    sc[3] = kl * invB;
-    sc[4] = dv;
   }
-  // ---- deterministic block reduction ----
-  const float smu = warp_transpose_reduce32(g_mu);  // lane L: column L summed over the warp's 32 rows
-  const float ssd = warp_transpose_reduce32(g_sd);
-  s_cols[warp][0][lane] = smu;
-  s_cols[warp][1][lane] = ssd;
+  // ---- block reduction in fixed warp order ----
+  __shared__ float sh_dh[kLossWarps][4][32];
+  __shared__ float sh_dstd[kLossWarps][2][32];
+  __shared__ float sh_sc[kLossWarps][5];
 #pragma unroll
-  for (int k = 0; k < 5; ++k) {
-#pragma unroll
-    for (int off = 16; off; off >>= 1) sc[k] += __shfl_xor_sync(0xffffffffu, sc[k], off);
+  for (int k = 0; k < 4; ++k) sh_dh[warp][k][lane] = acc_dh[k];
+  sh_dstd[warp][0][lane] = acc_dstd[0];
+  sh_dstd[warp][1][lane] = acc_dstd[1];
+  if (lane == 0) {
+    sh_sc[warp][0] = acc_surr;
+    sh_sc[warp][1] = acc_val;
+    sh_sc[warp][2] = acc_ent;
+    sh_sc[warp][3] = acc_kl;
+    sh_sc[warp][4] = acc_dv;
   }
-  if (lane == 0)
-    for (int k = 0; k < 5; ++k) s_sc[warp][k] = sc[k];
   __syncthreads();
   const int t = threadIdx.x;
-  if (t < 32) {
-    float m = 0.f, d = 0.f;
-    for (int w = 0; w < kLossThreads / 32; ++w) {
-      m += s_cols[w][0][t];
-      d += s_cols[w][1][t];
+  if (t < 64) {
+    // mean-gradient column sums (cols 0..A-1) and hetero std columns (A..2A-1)
+    const int k = t >> 5, l = t & 31;
+    const int j = 32 * k + l;
+    float s = 0.f, sstd = 0.f, sraw = 0.f;
+    for (int w = 0; w < kLossWarps; ++w) {
+      s += sh_dh[w][k][l];
+      sstd += sh_dstd[w][k][l];
+      sraw += sh_dh[w][2 + k][l];
     }
-    if (t < A) {
-      a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + t] = m;
+    if (j < a.A) {
+      a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + j] = s;
       if (a.hetero)
-        a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + A + t] = d;
+        a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + a.A + j] = sraw;
       else if (a.dstd_partial)
-        a.dstd_partial[static_cast<size_t>(blockIdx.x) * A + t] = d;
+        a.dstd_partial[static_cast<size_t>(blockIdx.x) * a.A + j] = sstd;
     }
-  } else if (t < 37) {
-    const int k = t - 32;
-    float v = 0.f;
-    for (int w = 0; w < kLossThreads / 32; ++w) v += s_sc[w][k];
-    if (k < 4)
-      a.stats_partial[static_cast<size_t>(blockIdx.x) * 4 + k] = v;
+  } else if (t < 69) {
+    const int q = t - 64;
+    float s = 0.f;
+    for (int w = 0; w < kLossWarps; ++w) s += sh_sc[w][q];
+    if (q < 4)
+      a.stats_partial[static_cast<size_t>(blockIdx.x) * 4 + q] = s;
     else
-      a.dvalue_colsum[blockIdx.x] = v;
+      a.dvalue_colsum[blockIdx.x] = s;
   }
 }
 
@@ -874,11 +871,11 @@ cudaError_t gather_minibatch(const GatherArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-int ppo_loss_blocks(int B) { return (B + kLossThreads - 1) / kLossThreads; }
+int ppo_loss_blocks(int B) { return (B + kLossRowsPerBlock - 1) / kLossRowsPerBlock; }
 
 cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
   if (a.A > kLossMaxA || a.B <= 0) return cudaErrorInvalidValue;
-  ppo_loss_kernel<<<ppo_loss_blocks(a.B), kLossThreads, 0, s>>>(a);
+  ppo_loss_kernel<<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 
