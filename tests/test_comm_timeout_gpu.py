@@ -31,7 +31,8 @@ def test_adam_exchange_times_out_on_missing_peer():
     step = torch.zeros(1, dtype=torch.int64, device=dev)
     C.adam_step(flat, send, send, grads, m, v, tens, chunks, nch, [1.0], [0.9], [0.999], [1e-8], [0], lr, None, step,
                 False, None, 0.01, 1e-5, 1e-2, 2, 0, peer_send, peer_flags, epoch, 200 * 10**6,
-                torch.zeros(grid * 4, device=dev), torch.zeros(4, dtype=torch.int32, device=dev), status, None, grid)
+                torch.zeros(grid * 4, device=dev), torch.zeros(4, dtype=torch.int32, device=dev), status, None, grid,
+                [0, n], n + 4)
     torch.cuda.synchronize()
     st = status.tolist()
     assert st[0] == 4  # peer-flag timeout

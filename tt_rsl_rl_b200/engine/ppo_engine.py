@@ -138,7 +138,12 @@ class PPOEngine:
         for p, o in zip(self.params, self.offsets):
             self.flat[o : o + p.numel()].copy_(p.data.reshape(-1))
             p.data = self.flat[o : o + p.numel()].view_as(p)
-        n_ex = self.n_params + _TAIL
+        n_ex = (self.n_params + _TAIL + 3) // 4 * 4  # exchanged floats: parameters + statistics, float4 granules
+        self.n_ex = n_ex
+        n_actor = sum(p.numel() for p, g in zip(self.params, self.param_group) if g == _GROUP_ACTOR)
+        if self.param_group != sorted(self.param_group):
+            raise RuntimeError("fused engine: actor parameters must precede critic parameters")
+        self.group_ranges = [0, n_actor, n_actor, self.n_params]
         self.exp_avg = torch.zeros(self.n_params, **f32)
         self.exp_avg_sq = torch.zeros(self.n_params, **f32)
         # ---- data parallel: symmetric send buffers shared with the peers (CUDA IPC) ----
@@ -408,7 +413,8 @@ class PPOEngine:
                     [alg.max_grad_norm, alg.max_grad_norm], [self.betas[0]] * 2, [self.betas[1]] * 2,
                     [self.adam_eps] * 2, [0, 0], self.lr, None, self.step, adaptive, kl,
                     float(alg.desired_kl or 0.0), 1e-5, 1e-2, self.world, self.rank, peers, flags, self.epoch,
-                    self.timeout_ns, self.norm_partial, self.barrier, self.status, self.out_norms, self.adam_grid)
+                    self.timeout_ns, self.norm_partial, self.barrier, self.status, self.out_norms, self.adam_grid,
+                    self.group_ranges, self.n_ex)
         self.loss_acc.add_(self.grads[self.n_params : self.n_params + _TAIL])
 
     def _normalizer_updates(self) -> None:

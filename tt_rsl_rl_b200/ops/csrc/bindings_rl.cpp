@@ -310,6 +310,27 @@ std::tuple<Tensor, Tensor, int64_t> make_adam_plan(const std::vector<int64_t>& o
     ts[i].cols = static_cast<int>(cols[i]);
     ts[i].shadow = P<void>(shadows[i]);
     ts[i].shadow_ld = static_cast<int>(shadow_lds[i]);
+    // Division by the invariant column count (Granlund & Montgomery, "Division by invariant integers using
+    // multiplication", PLDI 1994): for d > 1, l = ceil(log2 d), m = ceil(2^(31 + l) / d) < 2^32 and
+    // idx / d == umulhi(idx, m) >> (l - 1) for every idx < 2^31. d == 1 is flagged with shift 32.
+    {
+      const uint64_t d = static_cast<uint64_t>(cols[i] > 0 ? cols[i] : 1);
+      if (d == 1) {
+        ts[i].cols_magic = 0;
+        ts[i].cols_shift = 32;
+      } else {
+        unsigned int l = 0;
+        while ((1ull << l) < d) ++l;
+        ts[i].cols_magic = static_cast<unsigned int>(((1ull << (31 + l)) + d - 1) / d);
+        ts[i].cols_shift = l - 1;
+        const uint64_t probes[6] = {0ull, 1ull, d - 1, d, d + 1, static_cast<uint64_t>(numels[i] - 1)};
+        for (uint64_t n : probes) {
+          const uint64_t q = ((n * ts[i].cols_magic) >> 32) >> ts[i].cols_shift;
+          TORCH_CHECK(q == n / d, "make_adam_plan: division constant check failed");
+        }
+      }
+      TORCH_CHECK(numels[i] < (1ll << 31), "make_adam_plan: tensor too large");
+    }
     if (ts[i].shadow) {
       TORCH_CHECK(shadows[i]->scalar_type() == torch::kBFloat16 && shadows[i]->numel() >= rows[i] * shadow_lds[i] &&
                       rows[i] * cols[i] == numels[i],
@@ -338,7 +359,7 @@ void adam_step(const Tensor& params, const Tensor& send0, const Tensor& send1, c
                bool adaptive, const OptT& kl_mean, double desired_kl, double lr_min, double lr_max, int64_t world,
                int64_t rank, const OptT& peer_send, const OptT& peer_flags, const Tensor& epoch, int64_t timeout_ns,
                const Tensor& norm_partial, const Tensor& barrier, const OptT& status, const OptT& out_norms,
-               int64_t grid) {
+               int64_t grid, const std::vector<int64_t>& group_ranges, int64_t exchange_len) {
   for (const Tensor* t : {&params, &send0, &send1, &grads, &exp_avg, &exp_avg_sq}) check_f32(*t, "adam buffer");
   const size_t ng = max_norm.size();
   TORCH_CHECK(ng >= 1 && ng <= rlb::kAdamMaxGroups && beta1.size() == ng && beta2.size() == ng && eps.size() == ng,
@@ -388,6 +409,20 @@ void adam_step(const Tensor& params, const Tensor& send0, const Tensor& send1, c
   a.barrier = reinterpret_cast<unsigned int*>(barrier.data_ptr());
   a.status = P<unsigned int>(status);
   a.out_norms = P<float>(out_norms);
+  TORCH_CHECK(group_ranges.size() == 2 * ng, "adam_step: group_ranges must hold [begin, end) per group");
+  for (size_t g = 0; g < ng; ++g) {
+    a.group_begin[g] = group_ranges[2 * g];
+    a.group_end[g] = group_ranges[2 * g + 1];
+  }
+  TORCH_CHECK(exchange_len % 4 == 0 && send0.numel() >= exchange_len && send1.numel() >= exchange_len &&
+                  grads.numel() >= exchange_len,
+              "adam_step: exchange_len must be a multiple of 4 within the buffers");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(send0.data_ptr()) % 16) == 0 &&
+                  (reinterpret_cast<uintptr_t>(send1.data_ptr()) % 16) == 0 &&
+                  (reinterpret_cast<uintptr_t>(grads.data_ptr()) % 16) == 0,
+              "adam_step: exchange buffers must be 16-byte aligned");
+  TORCH_CHECK(world <= 8, "adam_step: at most 8 ranks");
+  a.exchange_len = exchange_len;
   ok(rlb::adam_step(a, static_cast<int>(grid), cur()), "adam_step");
 }
 

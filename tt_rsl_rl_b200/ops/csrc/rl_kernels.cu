@@ -209,14 +209,31 @@ __global__ void gae_kernel(const GaeArgs a) {
 
 __global__ void adv_normalize_kernel(float* adv, long long n, const double* partial, int parts) {
   __shared__ float stats[2];
+  __shared__ double red[2][32];
+  // every block reduces the per-block GAE partials in the same fixed tree order
+  double s = 0.0, ss = 0.0;
+  for (int i = threadIdx.x; i < parts; i += blockDim.x) {
+    s += partial[2 * i];
+    ss += partial[2 * i + 1];
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, off);
+    ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = s;
+    red[1][threadIdx.x >> 5] = ss;
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    double s = 0, ss = 0;
-    for (int i = 0; i < parts; ++i) {
-      s += partial[2 * i];
-      ss += partial[2 * i + 1];
+    double ts = 0, tss = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      ts += red[0][w];
+      tss += red[1][w];
     }
-    const double mean = s / static_cast<double>(n);
-    const double var = n > 1 ? fmax((ss - s * mean) / static_cast<double>(n - 1), 0.0) : 0.0;
+    const double mean = ts / static_cast<double>(n);
+    const double var = n > 1 ? fmax((tss - ts * mean) / static_cast<double>(n - 1), 0.0) : 0.0;
     stats[0] = static_cast<float>(mean);
     stats[1] = static_cast<float>(1.0 / (sqrt(var) + 1e-8));
   }
@@ -499,10 +516,10 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
 // ---------------------------------------------------------------------------------------------------------------
 // segment reduction (sum of partial slabs in fixed order, fp64 accumulation)
 // ---------------------------------------------------------------------------------------------------------------
-// Block = 32 columns x 8 part-lanes: lane y sums parts y, y + 8, ... of its column (coalesced 128-byte rows), then the
-// 8 lane sums are combined in a fixed order. Deterministic for a given launch configuration.
+// Block = 32 columns x 32 part-lanes: lane y sums parts y, y + 32, ... of its column (coalesced 128-byte rows), then the
+// 32 lane sums are combined in a fixed order. Deterministic for a given launch configuration.
 constexpr int kReduceCols = 32;
-constexpr int kReduceLanes = 8;
+constexpr int kReduceLanes = 32;
 __global__ void __launch_bounds__(kReduceCols* kReduceLanes)
     reduce_segments_kernel(const ReduceSegment* segs, int nseg, float* send0, float* send1, const unsigned int* epoch) {
   const int chunk = blockIdx.x;
@@ -578,6 +595,7 @@ __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) 
 //          coefficients and the adapted learning rate, and applies Adam to its chunks.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kAdamThreads = 256;
+constexpr int kMaxWorldAdam = 8;
 
 __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs a) {
   __shared__ float red[kAdamThreads / 32][kAdamMaxGroups];
@@ -628,25 +646,46 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
   const bool exchange_ok = peers_ok != 0;
 
   // ---- phase 1: rank-ordered sum, squared norms ----
+  // float4 grid-stride over the whole exchanged vector; the peer loads of all ranks are issued before they are
+  // summed (in rank order, so every rank obtains the same bits)
   float sq[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
   const float inv_world = 1.0f / static_cast<float>(a.world);
   const unsigned int parity = epoch & 1u;
-  const float* mine = a.send[parity];
-  for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
-    const AdamChunk ch = a.chunks[c];
-    const AdamTensor T = a.tensors[ch.tensor];
-    for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
-      const long long e = T.offset + ch.start + k;
-      float g;
-      if (a.world > 1 && exchange_ok) {
-        g = 0.f;
-        for (int r = 0; r < a.world; ++r) g += a.peer_send[parity * a.world + r][e];
-        g *= inv_world;
-      } else {
-        g = mine[e];
+  const float4* mine4 = reinterpret_cast<const float4*>(a.send[parity]);
+  const long long n4 = a.exchange_len / 4;
+  for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < n4;
+       v += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 g;
+    if (a.world > 1 && exchange_ok) {
+      float4 part[kMaxWorldAdam];
+#pragma unroll
+      for (int r = 0; r < kMaxWorldAdam; ++r)
+        if (r < a.world) part[r] = __ldcv(reinterpret_cast<const float4*>(a.peer_send[parity * a.world + r]) + v);
+      g = part[0];
+#pragma unroll
+      for (int r = 1; r < kMaxWorldAdam; ++r) {
+        if (r < a.world) {
+          g.x += part[r].x;
+          g.y += part[r].y;
+          g.z += part[r].z;
+          g.w += part[r].w;
+        }
       }
-      a.grads[e] = g;
-      if (T.group >= 0) sq[T.group] += g * g;
+      g.x *= inv_world;
+      g.y *= inv_world;
+      g.z *= inv_world;
+      g.w *= inv_world;
+    } else {
+      g = mine4[v];
+    }
+    reinterpret_cast<float4*>(a.grads)[v] = g;
+    const long long e = 4 * v;
+    const float comp[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+      for (int gr = 0; gr < kAdamMaxGroups; ++gr)
+        if (gr < a.ngroups && e + c >= a.group_begin[gr] && e + c < a.group_end[gr]) sq[gr] += comp[c] * comp[c];
     }
   }
 #pragma unroll
@@ -667,10 +706,27 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
   const bool all_ok = *reinterpret_cast<volatile unsigned int*>(a.barrier + 2) != epoch;
 
   // ---- phase 2: norms, clip coefficients, learning rate ----
+  // every block reduces the per-block partials with all of its threads (fixed tree order: identical in every block)
+  {
+    float part[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x) {
+#pragma unroll
+      for (int g = 0; g < kAdamMaxGroups; ++g) part[g] += a.norm_partial[static_cast<size_t>(b) * kAdamMaxGroups + g];
+    }
+#pragma unroll
+    for (int g = 0; g < kAdamMaxGroups; ++g) {
+#pragma unroll
+      for (int off = 16; off; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+    }
+    __syncthreads();  // red[] is reused
+    if (lane == 0)
+      for (int g = 0; g < kAdamMaxGroups; ++g) red[warp][g] = part[g];
+    __syncthreads();
+  }
   if (threadIdx.x < a.ngroups) {
     const int g = threadIdx.x;
     float s = 0.f;
-    for (int b = 0; b < static_cast<int>(gridDim.x); ++b) s += a.norm_partial[static_cast<size_t>(b) * kAdamMaxGroups + g];
+    for (int w = 0; w < kAdamThreads / 32; ++w) s += red[w][g];
     const float norm = sqrtf(s);
     float cf = 1.0f;
     if (a.max_norm[g] > 0.f) cf = fminf(a.max_norm[g] / (norm + 1e-6f), 1.0f);
@@ -691,17 +747,25 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     if (blockIdx.x == 0 && threadIdx.x == 0) *a.epoch = epoch;
     return;
   }
+  // per-group Adam constants, once per block (bias corrections in double, as torch computes them on the host)
+  __shared__ float step_size_s[kAdamMaxGroups], bc2_sqrt_s[kAdamMaxGroups];
+  if (threadIdx.x < a.ngroups) {
+    const int g = threadIdx.x;
+    const double step = static_cast<double>(step_s[g] + 1);
+    const double bc1 = 1.0 - pow(static_cast<double>(a.beta1[g]), step);
+    const double bc2 = 1.0 - pow(static_cast<double>(a.beta2[g]), step);
+    step_size_s[g] = static_cast<float>(static_cast<double>(lr_s[a.lr_index[g]]) / bc1);
+    bc2_sqrt_s[g] = static_cast<float>(sqrt(bc2));
+  }
+  __syncthreads();
   for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
     const AdamChunk ch = a.chunks[c];
     const AdamTensor T = a.tensors[ch.tensor];
     const int g = T.group;
     if (g < 0) continue;  // exchanged statistics (e.g. the KL mean), not parameters
-    const double step = static_cast<double>(step_s[g] + 1);
-    const double bc1 = 1.0 - pow(static_cast<double>(a.beta1[g]), step);
-    const double bc2 = 1.0 - pow(static_cast<double>(a.beta2[g]), step);
-    const float step_size = static_cast<float>(static_cast<double>(lr_s[a.lr_index[g]]) / bc1);
-    const float bc2_sqrt = static_cast<float>(sqrt(bc2));
+    const float step_size = step_size_s[g], bc2_sqrt = bc2_sqrt_s[g];
     const float b1 = a.beta1[g], b2 = a.beta2[g], eps = a.eps[g], cf = coef[g];
+    // chunks start on row boundaries of 2-D weights when cols divides the chunk; track (row, col) incrementally
     for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
       const long long e = T.offset + ch.start + k;
       const float grad = a.grads[e] * cf;
@@ -714,8 +778,9 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
       a.exp_avg_sq[e] = v;
       a.params[e] = p;
       if (T.shadow) {
-        const int idx = ch.start + k;
-        const int r = idx / T.cols, col = idx - r * T.cols;
+        const unsigned int idx = static_cast<unsigned int>(ch.start + k);
+        const unsigned int r = T.cols_shift == 32 ? idx : __umulhi(idx, T.cols_magic) >> T.cols_shift;  // idx / cols
+        const unsigned int col = idx - r * static_cast<unsigned int>(T.cols);
         static_cast<__nv_bfloat16*>(T.shadow)[static_cast<size_t>(r) * T.shadow_ld + col] = __float2bfloat16_rn(p);
       }
     }
@@ -762,10 +827,13 @@ __global__ void colstats_kernel(const ColStatsArgs a) {
   }
 }
 
-__global__ void norm_update_kernel(const NormUpdateArgs a) {
+// One block of 32 x 32 threads: for each 32-column stripe, lane y sums chunks y, y + 32, ... of its column, the 32
+// partial sums are combined in a fixed order, then the running statistics of that stripe are updated.
+__global__ void __launch_bounds__(1024) norm_update_kernel(const NormUpdateArgs a) {
   __shared__ long long count0;
   __shared__ int skip;
-  if (threadIdx.x == 0) {
+  __shared__ double red[2][32][33];
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
     count0 = *a.count;
     skip = (a.until >= 0 && count0 >= a.until && !a.reduce_only) ? 1 : 0;
   }
@@ -774,29 +842,44 @@ __global__ void norm_update_kernel(const NormUpdateArgs a) {
   const double n = static_cast<double>(a.rows);
   const double new_count = static_cast<double>(count0) + n;
   const float rate = static_cast<float>(n / new_count);
-  for (int c = threadIdx.x; c < a.dim; c += blockDim.x) {
+  for (int c0 = 0; c0 < a.dim; c0 += 32) {
+    const int c = c0 + threadIdx.x;
     double s = 0, ss = 0;
-    for (int k = 0; k < a.chunks; ++k) {
-      s += a.partial[(static_cast<size_t>(k) * 2) * a.dim + c];
-      ss += a.partial[(static_cast<size_t>(k) * 2 + 1) * a.dim + c];
+    if (c < a.dim) {
+      for (int k = threadIdx.y; k < a.chunks; k += 32) {
+        s += a.partial[(static_cast<size_t>(k) * 2) * a.dim + c];
+        ss += a.partial[(static_cast<size_t>(k) * 2 + 1) * a.dim + c];
+      }
     }
-    if (a.moments_out) {
-      a.moments_out[2 + c] = s;
-      a.moments_out[2 + a.dim + c] = ss;
+    red[0][threadIdx.y][threadIdx.x] = s;
+    red[1][threadIdx.y][threadIdx.x] = ss;
+    __syncthreads();
+    if (threadIdx.y == 0 && c < a.dim) {
+      double ts = 0, tss = 0;
+      for (int y = 0; y < 32; ++y) {
+        ts += red[0][y][threadIdx.x];
+        tss += red[1][y][threadIdx.x];
+      }
+      if (a.moments_out) {
+        a.moments_out[2 + c] = ts;
+        a.moments_out[2 + a.dim + c] = tss;
+      }
+      if (!a.reduce_only) {
+        const double bm = ts / n;
+        const double bv = fmax(tss / n - bm * bm, 0.0);
+        const float batch_mean = static_cast<float>(bm), batch_var = static_cast<float>(bv);
+        const float old_mean = a.mean[c];
+        const float delta = batch_mean - old_mean;
+        const float new_mean = old_mean + rate * delta;
+        const float new_var = a.var[c] + rate * (batch_var - a.var[c] + delta * (batch_mean - new_mean));
+        a.mean[c] = new_mean;
+        a.var[c] = new_var;
+        a.std[c] = sqrtf(new_var);
+      }
     }
-    if (a.reduce_only) continue;
-    const double bm = s / n;
-    const double bv = fmax(ss / n - bm * bm, 0.0);
-    const float batch_mean = static_cast<float>(bm), batch_var = static_cast<float>(bv);
-    const float old_mean = a.mean[c];
-    const float delta = batch_mean - old_mean;
-    const float new_mean = old_mean + rate * delta;
-    const float new_var = a.var[c] + rate * (batch_var - a.var[c] + delta * (batch_mean - new_mean));
-    a.mean[c] = new_mean;
-    a.var[c] = new_var;
-    a.std[c] = sqrtf(new_var);
+    __syncthreads();
   }
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
     if (a.moments_out) a.moments_out[0] = n;
     if (!a.reduce_only) *a.count = count0 + a.rows;
   }
@@ -910,7 +993,7 @@ cudaError_t colstats(const ColStatsArgs& a, cudaStream_t s) {
 }
 
 cudaError_t norm_update(const NormUpdateArgs& a, cudaStream_t s) {
-  norm_update_kernel<<<1, 256, 0, s>>>(a);
+  norm_update_kernel<<<1, dim3(32, 32), 0, s>>>(a);
   return cudaGetLastError();
 }
 

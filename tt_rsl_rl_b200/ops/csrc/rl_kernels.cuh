@@ -167,6 +167,7 @@ struct AdamTensor {
   int rows, cols;    // logical 2-D shape of weights (cols = fan-in) for the bf16 shadow
   void* shadow;      // bf16 [rows, shadow_ld] or null
   int shadow_ld;
+  unsigned int cols_magic, cols_shift;  // idx / cols == umulhi(idx, cols_magic) >> cols_shift (shift 32: cols == 1)
 };
 struct AdamChunk {
   int tensor;
@@ -185,6 +186,8 @@ struct AdamArgs {
   const AdamChunk* chunks;
   int nchunks;
   int ngroups;
+  long long group_begin[kAdamMaxGroups], group_end[kAdamMaxGroups];  // contiguous flat range of each clip group
+  long long exchange_len;  // floats exchanged (multiple of 4, buffers 16-byte aligned): parameters + statistics
   float max_norm[kAdamMaxGroups];   // <= 0: no clipping
   float beta1[kAdamMaxGroups], beta2[kAdamMaxGroups], eps[kAdamMaxGroups];
   int lr_index[kAdamMaxGroups];     // learning-rate slot of each group (groups of one torch optimizer share slot 0)
@@ -200,7 +203,6 @@ struct AdamArgs {
   float* const* peer_send;          // [2 * world] device pointers: peer_send[parity * world + r]
   unsigned int* const* peer_flags;  // [world] flag arrays of every rank (each [world] uint32)
   unsigned int* epoch;              // device exchange counter (incremented by this kernel)
-  long long exchange_len;           // number of floats exchanged (gradients + tail statistics)
   uint64_t timeout_ns;
   // scratch
   float* norm_partial;              // [gridDim, ngroups]
