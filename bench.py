@@ -38,7 +38,71 @@ T_STEPS = 24
 BASELINE_VALUE = None  # BASELINE.md publishes no NVIDIA number for this configuration
 
 
-def train_cfg(impl: str) -> dict:
+# BASELINE.json configurations: (total envs or None, envs per GPU or None, env kwargs, description)
+CONFIGS = {
+    "1": dict(total=65536, per_gpu=None, env={}, desc="PPO MLP actor-critic [512,256,128] ELU, obs 96/99, 29 actions"),
+    "2": dict(total=65536, per_gpu=None, env={},
+              desc="config 1 + RND [256,256]->16 on critic obs (weight 0.5) + symmetry (2 copies, mirror loss 1.0)"),
+    "3": dict(total=None, per_gpu=16384, env={"reset_prob": 0.01},
+              desc="recurrent PPO: GRU 256 + MLP head [256,128], obs 96, 29 actions, done p=0.01"),
+    "3lstm": dict(total=None, per_gpu=16384, env={"reset_prob": 0.01},
+                  desc="recurrent PPO: LSTM 256 + MLP head [256,128], obs 96, 29 actions, done p=0.01"),
+    "4a": dict(total=65536, per_gpu=None, env={},
+               desc="distillation: teacher [512,256,128] obs 99 -> student [256,256,128] obs 96, MSE, 8 steps/rollout"),
+    "4b": dict(total=None, per_gpu=32768, env={},
+               desc="PPO heteroscedastic Gaussian, MLPs [1024,1024,512], 262144 envs at 8 GPUs (weak scaling)"),
+}
+
+
+def mirror_maps(seed: int = 7):
+    """Seeded signed-permutation mirror: an involution on the 96 state features (pairs swapped, signs flipped) and
+    on the 29 actions; the 3 privileged critic features are symmetric."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+
+    def involution(n):
+        perm = torch.arange(n)
+        order = torch.randperm(n, generator=g)
+        for i in range(0, n - 1, 2):
+            a, b = int(order[i]), int(order[i + 1])
+            perm[a], perm[b] = b, a
+        sign = torch.where(torch.rand(n, generator=g) < 0.5, -1.0, 1.0)
+        sign = torch.minimum(sign, sign[perm])  # consistent sign on each pair keeps the map an involution
+        return perm, sign
+
+    return involution(96), involution(29)
+
+
+_MIRROR = None
+
+
+def mirror_obs_actions(env=None, obs=None, actions=None):
+    """Symmetry augmentation function of config 2: returns [original; mirrored] observations / actions."""
+    import torch
+
+    global _MIRROR
+    if _MIRROR is None:
+        _MIRROR = mirror_maps()
+    (ps, ss), (pa, sa) = _MIRROR
+    out_obs = out_act = None
+    if obs is not None:
+        groups = {}
+        for k, v in obs.items():
+            m = v.clone()
+            m[:, :96] = v[:, ps.to(v.device)] * ss.to(v.device)
+            groups[k] = torch.cat([v, m])
+        out_obs = type(obs)(groups, batch_size=[2 * obs.batch_size[0]])
+    if actions is not None:
+        out_act = torch.cat([actions, actions[:, pa.to(actions.device)] * sa.to(actions.device)])
+    return out_obs, out_act
+
+
+def train_cfg(impl: str, config: str = "1") -> dict:
+    if config in ("3", "3lstm"):
+        return _recurrent_cfg(impl, "gru" if config == "3" else "lstm")
+    if config == "4a":
+        return _distill_cfg(impl)
     alg = {
         "class_name": "PPO", "num_learning_epochs": 5, "num_mini_batches": 4, "clip_param": 0.2, "gamma": 0.99,
         "lam": 0.95, "value_loss_coef": 1.0, "entropy_coef": 0.01, "learning_rate": 1e-3, "max_grad_norm": 1.0,
@@ -55,7 +119,56 @@ def train_cfg(impl: str) -> dict:
                   "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
         "critic": {"class_name": "MLPModel", "hidden_dims": [512, 256, 128], "activation": "elu",
                    "obs_normalization": True},
+    } if config != "4b" else _hetero_wide_cfg(alg)
+
+
+def _apply_config_2(cfg: dict) -> dict:
+    cfg["algorithm"]["rnd_cfg"] = {"num_outputs": 16, "predictor_hidden_dims": [256, 256],
+                                   "target_hidden_dims": [256, 256], "weight": 0.5}
+    cfg["algorithm"]["symmetry_cfg"] = {"data_augmentation_func": mirror_obs_actions, "use_data_augmentation": True,
+                                        "use_mirror_loss": True, "mirror_loss_coeff": 1.0}
+    cfg["obs_groups"]["rnd_state"] = ["critic"]
+    return cfg
+
+
+def _hetero_wide_cfg(alg: dict) -> dict:
+    return {
+        "num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
+        "obs_groups": {"actor": ["policy"], "critic": ["critic"]},
+        "algorithm": alg,
+        "actor": {"class_name": "MLPModel", "hidden_dims": [1024, 1024, 512], "activation": "elu",
+                  "obs_normalization": True,
+                  "distribution_cfg": {"class_name": "HeteroscedasticGaussianDistribution", "init_std": 1.0}},
+        "critic": {"class_name": "MLPModel", "hidden_dims": [1024, 1024, 512], "activation": "elu",
+                   "obs_normalization": True},
     }
+
+
+def _recurrent_cfg(impl: str, rnn_type: str) -> dict:
+    alg = {"class_name": "PPO", "num_learning_epochs": 5, "num_mini_batches": 4, "learning_rate": 1e-3,
+           "schedule": "adaptive", "desired_kl": 0.01, "max_grad_norm": 1.0}
+    if impl == "reference":
+        alg["use_mixed_precision"] = True
+    model = {"class_name": "RNNModel", "hidden_dims": [256, 128], "activation": "elu", "obs_normalization": True,
+             "rnn_type": rnn_type, "rnn_hidden_dim": 256, "rnn_num_layers": 1}
+    actor = dict(model, distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
+    return {"num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
+            "obs_groups": {"actor": ["policy"], "critic": ["policy"]}, "algorithm": alg, "actor": actor,
+            "critic": dict(model)}
+
+
+def _distill_cfg(impl: str) -> dict:
+    alg = {"class_name": "Distillation", "num_learning_epochs": 1, "gradient_length": 3, "learning_rate": 1e-3,
+           "max_grad_norm": 1.0, "loss_type": "mse"}
+    if impl == "reference":
+        alg["use_mixed_precision"] = True
+    return {"num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
+            "obs_groups": {"student": ["policy"], "teacher": ["critic"]}, "algorithm": alg,
+            "student": {"class_name": "MLPModel", "hidden_dims": [256, 256, 128], "activation": "elu",
+                        "obs_normalization": True,
+                        "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+            "teacher": {"class_name": "MLPModel", "hidden_dims": [512, 256, 128], "activation": "elu",
+                        "obs_normalization": True}}
 
 
 class ClockSampler:
@@ -110,10 +223,10 @@ def dist_info() -> tuple[int, int, int]:
                                                                                                       "0"))
 
 
-def make_env(num_envs: int, device: str, host_noise: bool, seed: int):
+def make_env(num_envs: int, device: str, host_noise: bool, seed: int, **env_kw):
     from tt_rsl_rl_b200.env import humanoid_like
 
-    return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise)
+    return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise, **env_kw)
 
 
 def timed_learn(runner, steps: int, warmup: int, world: int) -> float:
@@ -141,17 +254,26 @@ def timed_learn(runner, steps: int, warmup: int, world: int) -> float:
     return ms / 1000.0
 
 
-def build_runner(impl: str, env, device: str):
-    import copy
-
-    cfg = copy.deepcopy(train_cfg(impl))
+def build_runner(impl: str, env, device: str, config: str = "1"):
+    cfg = train_cfg(impl, config)
+    if config == "2":
+        cfg = _apply_config_2(cfg)
+    distill = config == "4a"
     if impl == "reference":
-        from rsl_rl.runners import OnPolicyRunner as RefRunner  # noqa: the unmodified reference
-
-        return RefRunner(env, cfg, log_dir=None, device=device)
-    from tt_rsl_rl_b200.runners import OnPolicyRunner
-
-    return OnPolicyRunner(env, cfg, log_dir=None, device=device)
+        if distill:
+            from rsl_rl.runners import DistillationRunner as RefRunner  # noqa: the unmodified reference
+        else:
+            from rsl_rl.runners import OnPolicyRunner as RefRunner  # noqa: the unmodified reference
+        runner = RefRunner(env, cfg, log_dir=None, device=device)
+    else:
+        if distill:
+            from tt_rsl_rl_b200.runners import DistillationRunner as Runner
+        else:
+            from tt_rsl_rl_b200.runners import OnPolicyRunner as Runner
+        runner = Runner(env, cfg, log_dir=None, device=device)
+    if distill:
+        runner.alg.teacher_loaded = True  # random-init frozen teacher (no checkpoint is available offline)
+    return runner
 
 
 def main() -> None:
@@ -161,10 +283,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--total-envs", type=int, default=TOTAL_ENVS,
+    ap.add_argument("--total-envs", type=int, default=None,
                     help="environments over all ranks (default: the BASELINE configuration; smaller for profiling)")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="1", help="BASELINE.json configuration")
     args = ap.parse_args()
-    total_envs = args.total_envs
+    conf = CONFIGS[args.config]
     world, rank, local_rank = dist_info()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -188,10 +311,17 @@ def main() -> None:
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device(device),
                                              timeout=datetime.timedelta(seconds=120))
     torch.manual_seed(1 + rank)
+    if args.total_envs is not None:
+        total_envs = args.total_envs
+    elif conf["total"] is not None:
+        total_envs = conf["total"]
+    else:
+        total_envs = conf["per_gpu"] * world
     n_local = total_envs // world
+    env_kw = conf["env"]
 
-    env = make_env(n_local, device, host_noise=False, seed=rank)
-    runner = build_runner(args.impl, env, device)
+    env = make_env(n_local, device, host_noise=False, seed=rank, **env_kw)
+    runner = build_runner(args.impl, env, device, args.config)
     sampler = ClockSampler([local_rank]) if local_rank == 0 else None
     if sampler:
         sampler.__enter__()
@@ -203,8 +333,8 @@ def main() -> None:
 
     e2e = None
     if not args.no_e2e:
-        env2 = make_env(n_local, device, host_noise=True, seed=rank)
-        runner2 = build_runner(args.impl, env2, device)
+        env2 = make_env(n_local, device, host_noise=True, seed=rank, **env_kw)
+        runner2 = build_runner(args.impl, env2, device, args.config)
         e2e_s = timed_learn(runner2, args.steps, args.warmup, world)
         h2d = T_STEPS * n_local * 96 * 4
         e2e = {"value": samples / e2e_s, "unit": "samples/s", "ms_per_step": e2e_s * 1e3,
@@ -214,7 +344,7 @@ def main() -> None:
     launches = None
     if args.impl == "ours":
         eng = getattr(runner.alg, "engine", None)
-        launches = kernel_launches_per_iteration(eng) if eng is not None else 0
+        launches = kernel_launches_per_iteration(eng) if eng is not None and hasattr(eng, "plan_c") else 0
 
     if rank == 0:
         line = {
@@ -227,11 +357,11 @@ def main() -> None:
             "ms_per_step": s_per_iter * 1e3,
             "s_per_iter": s_per_iter,
             "higher_is_better": True,
-            "scaling": "strong",
+            "scaling": "strong" if conf["total"] is not None and args.total_envs is None else "weak",
             "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
             "dtype": "bf16",
             "data": "synthetic (seeded linear-Gaussian env), random-init weights",
-            "config": {"model": "PPO MLP actor-critic [512,256,128] ELU, obs 96/99, 29 actions",
+            "config": {"model": conf["desc"], "baseline_config": args.config,
                        "global_batch": samples, "seq_len": T_STEPS, "num_envs_total": total_envs,
                        "epochs": 5, "minibatches": 4, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (rollout arena >> 126 MB)"},
