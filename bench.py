@@ -108,8 +108,8 @@ def train_cfg(impl: str, config: str = "1") -> dict:
         "lam": 0.95, "value_loss_coef": 1.0, "entropy_coef": 0.01, "learning_rate": 1e-3, "max_grad_norm": 1.0,
         "schedule": "adaptive", "desired_kl": 0.01, "use_clipped_value_loss": True,
     }
-    if impl == "reference":
-        alg["use_mixed_precision"] = True  # bf16 autocast GEMMs on the reference arm
+    # bf16 GEMMs on both arms: autocast on the reference arm and on any PyTorch-path fallback of this framework
+    alg["use_mixed_precision"] = True
     return {
         "num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
         "obs_groups": {"actor": ["policy"], "critic": ["critic"]},
@@ -146,9 +146,7 @@ def _hetero_wide_cfg(alg: dict) -> dict:
 
 def _recurrent_cfg(impl: str, rnn_type: str) -> dict:
     alg = {"class_name": "PPO", "num_learning_epochs": 5, "num_mini_batches": 4, "learning_rate": 1e-3,
-           "schedule": "adaptive", "desired_kl": 0.01, "max_grad_norm": 1.0}
-    if impl == "reference":
-        alg["use_mixed_precision"] = True
+           "schedule": "adaptive", "desired_kl": 0.01, "max_grad_norm": 1.0, "use_mixed_precision": True}
     model = {"class_name": "RNNModel", "hidden_dims": [256, 128], "activation": "elu", "obs_normalization": True,
              "rnn_type": rnn_type, "rnn_hidden_dim": 256, "rnn_num_layers": 1}
     actor = dict(model, distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
@@ -159,9 +157,7 @@ def _recurrent_cfg(impl: str, rnn_type: str) -> dict:
 
 def _distill_cfg(impl: str) -> dict:
     alg = {"class_name": "Distillation", "num_learning_epochs": 1, "gradient_length": 3, "learning_rate": 1e-3,
-           "max_grad_norm": 1.0, "loss_type": "mse"}
-    if impl == "reference":
-        alg["use_mixed_precision"] = True
+           "max_grad_norm": 1.0, "loss_type": "mse", "use_mixed_precision": True}
     return {"num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
             "obs_groups": {"student": ["policy"], "teacher": ["critic"]}, "algorithm": alg,
             "student": {"class_name": "MLPModel", "hidden_dims": [256, 256, 128], "activation": "elu",

@@ -1,0 +1,188 @@
+"""The fused CUDA distillation engine: loss-gradient kernel against autograd, whole update against the PyTorch path
+of the same algorithm on identical data, graph replay against eager execution, and the runner with checkpoints."""
+
+import copy
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("huber", [False, True])
+@pytest.mark.parametrize("head_cols", [12, 24])
+def test_mse_grad_matches_autograd(huber, head_cols):
+    from tt_rsl_rl_b200.ops import ext
+
+    C = ext()
+    torch.manual_seed(0)
+    rows, A = 3000, 12
+    pred = torch.randn(rows, head_cols, device="cuda")
+    target = torch.randn(rows, 16, device="cuda") * 1.5
+    ld_grad = (head_cols + 7) // 8 * 8
+    grad = torch.full((rows, ld_grad), 7.0, dtype=torch.bfloat16, device="cuda")
+    blocks = C.mse_blocks(rows)
+    loss_partial = torch.zeros(blocks, device="cuda")
+    colsum = torch.zeros(blocks, head_cols, device="cuda")
+    loss_acc = torch.full((1,), 0.25, device="cuda")
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for _ in range(2):  # the ticket must re-arm itself
+        C.mse_grad(pred, head_cols, target, 16, rows, A, huber, grad, ld_grad, head_cols, loss_partial, colsum,
+                   loss_acc, ticket)
+    p = pred[:, :A].clone().requires_grad_(True)
+    fn = torch.nn.functional.huber_loss if huber else torch.nn.functional.mse_loss
+    loss = fn(p, target[:, :A])
+    loss.backward()
+    torch.testing.assert_close(grad[:, :A].float(), p.grad, rtol=1e-2, atol=1e-7)
+    assert (grad[:, A:].float() == 0).all()
+    torch.testing.assert_close(colsum.sum(0)[:A], p.grad.sum(0), rtol=1e-4, atol=1e-7)
+    assert (colsum[:, A:] == 0).all()
+    torch.testing.assert_close(loss_acc[0], 0.25 + 2 * loss.detach(), rtol=1e-5, atol=1e-6)
+    assert int(ticket.item()) == 0
+
+
+def _make(env, T, engine, gl=3, epochs=1, loss_type="mse", graphs=False, student=None, teacher=None):
+    from tt_rsl_rl_b200.algorithms import Distillation
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    obs = env.get_observations()
+    groups = {"student": ["policy"], "teacher": ["critic"]}
+    if student is None:
+        student = MLPModel(obs, groups, "student", env.num_actions, hidden_dims=[256, 128], obs_normalization=True,
+                           distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
+        teacher = MLPModel(obs, groups, "teacher", env.num_actions, hidden_dims=[256, 128, 64],
+                           obs_normalization=True)
+    storage = RolloutStorage("distillation", env.num_envs, T, obs, [env.num_actions], "cuda")
+    b200 = {"engine": engine, "graphs": graphs}
+    return Distillation(student, teacher, storage, num_learning_epochs=epochs, gradient_length=gl,
+                        learning_rate=1e-3, max_grad_norm=1.0, loss_type=loss_type, device="cuda", b200_cfg=b200)
+
+
+@pytest.mark.parametrize("loss_type", ["mse", "huber"])
+def test_distillation_update_matches_torch_path(loss_type):
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+
+    torch.manual_seed(0)
+    T, N = 8, 2048
+    env = LinearGaussianVecEnv(N, obs_dim=48, num_actions=12, privileged_dim=3, device="cuda")
+    alg_t = _make(env, T, "torch", gl=3, epochs=2, loss_type=loss_type)
+    # teacher normaliser with non-trivial statistics, and an untrained teacher output scale
+    obs = env.get_observations()
+    alg_t.teacher.obs_normalizer.update(torch.cat([obs["critic"]] * 4) * 2.0 + 0.5)
+    alg_e = _make(env, T, "cuda", gl=3, epochs=2, loss_type=loss_type,
+                  student=copy.deepcopy(alg_t.student), teacher=copy.deepcopy(alg_t.teacher))
+    assert alg_e.engine is not None
+    alg_e.engine.sync_from_torch()
+    with torch.inference_mode():
+        for _ in range(T):
+            actions = alg_t.act(obs)
+            obs, rew, dones, extras = env.step(actions)
+            alg_t.process_env_step(obs, rew, dones, extras)
+    st = alg_t.storage
+    alg_e.engine.load_rollout(st)
+    probe = st.observations.flatten(0, 1)[:4096]
+    with torch.no_grad():
+        old = alg_t.student(probe).clone()
+    obs_all = st.observations.flatten(0, 1)["policy"].clone()
+    loss_t = alg_t.update()
+    loss_e = alg_e.update()
+    assert abs(loss_e["behavior"] - loss_t["behavior"]) <= 2e-2 * abs(loss_t["behavior"])
+    # the normaliser saw the same raw observations (it is applied after the update on both paths)
+    nt, ne = alg_t.student.obs_normalizer, alg_e.student.obs_normalizer
+    torch.testing.assert_close(ne._mean, nt._mean, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(ne._var, nt._var, rtol=1e-4, atol=1e-6)
+    assert int(ne.count) == int(nt.count) == obs_all.shape[0]
+    # function-space parity: deviation relative to the size of the update (bf16 GEMM operands on the engine path)
+    with torch.no_grad():
+        nt.eval()
+        ne.eval()
+        new_t = alg_t.student(probe)
+        new_e = alg_e.student(probe)
+    dev = (new_e - new_t).norm() / (new_t - old).norm()
+    assert dev < 0.15, dev
+    # two windows of three steps were applied per epoch... (2 epochs x 8 steps = 16 steps -> 5 Adam steps)
+    assert int(alg_e.engine.step[0].item()) == 5
+    # the std parameter gets no gradient and stays put, as with torch.optim.Adam and grad=None
+    torch.testing.assert_close(alg_e.student.distribution.std_param, alg_t.student.distribution.std_param)
+
+
+def test_distillation_graph_replay_equals_eager():
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.models import MLPModel
+
+    T, N = 6, 1024
+    results = []
+    for graphs in (False, True):
+        torch.manual_seed(3)
+        env = LinearGaussianVecEnv(N, obs_dim=40, num_actions=10, privileged_dim=3, device="cuda")
+        obs = env.get_observations()
+        groups = {"student": ["policy"], "teacher": ["critic"]}
+        student = MLPModel(obs, groups, "student", env.num_actions, hidden_dims=[128, 64], obs_normalization=True,
+                           distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
+        teacher = MLPModel(obs, groups, "teacher", env.num_actions, hidden_dims=[128, 64], obs_normalization=True)
+        alg = _make(env, T, "cuda", gl=2, graphs=graphs, student=student, teacher=teacher)
+        losses = []
+        for _ in range(3):
+            with torch.inference_mode():
+                for _ in range(T):
+                    actions = alg.act(obs)
+                    obs, rew, dones, extras = env.step(actions)
+                    alg.process_env_step(obs, rew, dones, extras)
+            losses.append(alg.update()["behavior"])
+        results.append((alg.engine.flat.clone(), losses, alg.student.obs_normalizer._mean.clone()))
+    assert torch.equal(results[0][0], results[1][0])
+    assert results[0][1] == results[1][1]
+    assert torch.equal(results[0][2], results[1][2])
+
+
+def test_distillation_runner_teacher_from_ppo_checkpoint(tmp_path):
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.runners import DistillationRunner, OnPolicyRunner
+
+    torch.manual_seed(0)
+    env = LinearGaussianVecEnv(512, obs_dim=32, num_actions=8, privileged_dim=3, device="cuda")
+    ppo_cfg = {
+        "num_steps_per_env": 4, "save_interval": 1000, "obs_groups": {"actor": ["policy"], "critic": ["critic"]},
+        "algorithm": {"class_name": "PPO", "num_learning_epochs": 1, "num_mini_batches": 2},
+        "actor": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True,
+                  "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+        "critic": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True},
+    }
+    ppo = OnPolicyRunner(env, ppo_cfg, log_dir=None, device="cuda")
+    ppo.learn(2)
+    teacher_path = str(tmp_path / "teacher.pt")
+    ppo.save(teacher_path)
+    cfg = {
+        "num_steps_per_env": 6, "save_interval": 1000, "obs_groups": {"student": ["policy"], "teacher": ["policy"]},
+        "algorithm": {"class_name": "Distillation", "num_learning_epochs": 1, "gradient_length": 3,
+                      "b200_cfg": {"engine": "cuda"}},
+        "student": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True,
+                    "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 0.5}},
+        "teacher": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True,
+                    "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+    }
+    runner = DistillationRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    assert runner.alg.engine is not None
+    runner.load(teacher_path)
+    assert runner.alg.teacher_loaded
+    # the engine's teacher shadows were refreshed: the teacher targets equal the loaded actor's means
+    obs = env.get_observations()
+    with torch.inference_mode():
+        runner.alg.act(obs)
+        expect = ppo.alg.actor(obs)
+    eng = runner.alg.engine
+    torch.testing.assert_close(eng.targets[: env.num_envs, :8], expect, rtol=2e-2, atol=2e-2)
+    eng.t = 0
+    runner.learn(3)
+    path = str(tmp_path / "student.pt")
+    runner.save(path)
+    sd = torch.load(path, weights_only=False)
+    assert sd["optimizer_state_dict"]["state"], "optimizer state missing"
+    runner2 = DistillationRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    runner2.load(path)
+    for (k, a), b in zip(runner.alg.student.state_dict().items(), runner2.alg.student.state_dict().values()):
+        assert torch.equal(a, b), k
+    torch.testing.assert_close(runner2.alg.engine.exp_avg, runner.alg.engine.exp_avg)
+    assert int(runner2.alg.engine.step[0].item()) == int(runner.alg.engine.step[0].item()) == 6
+    runner2.learn(1)

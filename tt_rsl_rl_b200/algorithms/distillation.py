@@ -52,6 +52,7 @@ class Distillation:
         self.teacher = teacher.to(device)
         self._raw_student = self.student
         self._raw_teacher = self.teacher
+        self.optimizer_name = optimizer
         self.optimizer = resolve_optimizer(optimizer)(self.student.parameters(), lr=learning_rate)
         self.storage = storage
         self.transition = RolloutStorage.Transition()
@@ -87,12 +88,17 @@ class Distillation:
                 raise ValueError(f"The fused CUDA distillation engine does not support this configuration: {reason}")
 
     def act(self, obs) -> torch.Tensor:
+        if self.engine is not None:
+            return self.engine.act(obs)
         self.transition.actions = self.student(obs, stochastic_output=True).detach()
         self.transition.privileged_actions = self.teacher(obs).detach()
         self.transition.observations = obs
         return self.transition.actions
 
     def process_env_step(self, obs, rewards: torch.Tensor, dones: torch.Tensor, extras: dict) -> None:
+        if self.engine is not None:
+            self.engine.process_env_step(obs, rewards, dones, extras)
+            return
         self.transition.rewards = rewards
         self.transition.dones = dones
         self.storage.add_transition(self.transition)
@@ -150,6 +156,8 @@ class Distillation:
         self.teacher.eval()
 
     def save(self) -> dict:
+        if self.engine is not None:
+            self.engine.sync_to_torch()
         return {
             "student_state_dict": self._raw_student.state_dict(),
             "teacher_state_dict": self._raw_teacher.state_dict(),
@@ -157,6 +165,14 @@ class Distillation:
         }
 
     def load(self, loaded_dict: dict, load_cfg: dict | None, strict: bool) -> bool:
+        if self.engine is not None:
+            self.engine.sync_to_torch()
+        resume = self._load(loaded_dict, load_cfg, strict)
+        if self.engine is not None:
+            self.engine.sync_from_torch()
+        return resume
+
+    def _load(self, loaded_dict: dict, load_cfg: dict | None, strict: bool) -> bool:
         if load_cfg is None:
             if any("actor_state_dict" in k for k in loaded_dict):
                 load_cfg = {"teacher": True, "iteration": False}
@@ -202,6 +218,9 @@ class Distillation:
         return alg
 
     def broadcast_parameters(self) -> None:
+        if self.engine is not None:
+            self.engine.broadcast_parameters()
+            return
         for model in (self._raw_student, self._raw_teacher):
             for tensor in model.state_dict().values():
                 torch.distributed.broadcast(tensor, src=0)

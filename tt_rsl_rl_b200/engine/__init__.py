@@ -1,5 +1,6 @@
 """Fused CUDA execution engines for the algorithms (device-resident state, sm_100a kernels, CUDA graphs)."""
 
+from .distillation_engine import DistillationEngine
 from .ppo_engine import PPOEngine
 
-__all__ = ["PPOEngine"]
+__all__ = ["DistillationEngine", "PPOEngine"]

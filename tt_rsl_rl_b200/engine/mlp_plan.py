@@ -97,13 +97,13 @@ class MLPPlan:
                        bias=lin.bias.data, status=status)
 
     # ---- backward ---------------------------------------------------------------------------------------------------
-    def backward(self, rows: int, status: torch.Tensor | None = None) -> None:
+    def backward(self, rows: int, status: torch.Tensor | None = None, x: torch.Tensor | None = None) -> None:
         """Weight gradients (split partials) of every layer and data gradients down to layer 1.
 
         Requires ``d_head`` (gradient of the head output, padding columns zero) and the cached activations of the
-        training forward pass.
+        training forward pass; ``x`` is that pass's input when it was not ``x_train``.
         """
-        inputs = [self.x_train] + self.h_train  # input of layer l is inputs[l]
+        inputs = [self.x_train if x is None else x] + self.h_train  # input of layer l is inputs[l]
         dz_l = self.d_head
         for l in range(self.L - 1, -1, -1):
             lin = self.linears[l]

@@ -24,8 +24,9 @@ from itertools import chain
 import torch
 import torch.nn as nn
 
-from ..modules import EmpiricalNormalization, GaussianDistribution, HeteroscedasticGaussianDistribution
+from ..modules import GaussianDistribution, HeteroscedasticGaussianDistribution
 from ..ops import ext
+from .base import EngineBase, elu_mlp_reason
 from .mlp_plan import MLPPlan, pad8
 
 _GROUP_ACTOR = 0
@@ -33,19 +34,7 @@ _GROUP_CRITIC = 1
 _TAIL = 4  # exchanged statistics after the parameters: surrogate, value, entropy, kl (each a minibatch mean)
 
 
-def _elu_mlp(model) -> str | None:
-    mlp = getattr(model, "mlp", None)
-    if mlp is None:
-        return "model has no MLP head"
-    for m in mlp:
-        if isinstance(m, nn.Linear) or isinstance(m, nn.Unflatten):
-            continue
-        if not isinstance(m, nn.ELU) or m.alpha != 1.0:
-            return f"activation {type(m).__name__} is not fused (ELU only)"
-    return None
-
-
-class PPOEngine:
+class PPOEngine(EngineBase):
     # ---- capability checks ------------------------------------------------------------------------------------------
     @staticmethod
     def supports_models(actor, critic, alg_cfg: dict) -> str | None:
@@ -56,7 +45,7 @@ class PPOEngine:
                 if isinstance(m, CNNModel):
                     return f"{name} is a CNNModel"
                 return f"{name} type {type(m).__name__} is not fused"
-            reason = _elu_mlp(m)
+            reason = elu_mlp_reason(m)
             if reason:
                 return f"{name}: {reason}"
             if m.obs_dim > 1024:
@@ -272,23 +261,13 @@ class PPOEngine:
             raise ValueError("fused Adam supports weight_decay=0 and amsgrad=False")
 
         # ---- normaliser statistics scratch ----
-        self.stats_chunks = ext().colstats_chunks(self.total)
-        self.colstats_partial = {
-            "actor": torch.zeros(2 * self.stats_chunks * self.Da, dtype=torch.float64, device=dev),
-            "critic": torch.zeros(2 * self.stats_chunks * self.Dc, dtype=torch.float64, device=dev),
-        }
-
-        self.moments_local = {k: torch.zeros(2 + 2 * D, dtype=torch.float64, device=dev)
-                              for k, D in (("actor", self.Da), ("critic", self.Dc))}
-        self.moments_global = {k: torch.zeros_like(v) for k, v in self.moments_local.items()}
+        self._alloc_norm_scratch("actor", self.total, self.Da)
+        self._alloc_norm_scratch("critic", self.total, self.Dc)
         self.use_graphs = bool(alg.b200_cfg["graphs"])
         self._update_graph = None
         self._updates_done = 0
         self.perm_override: torch.Tensor | None = None  # int32 [T*N]: explicit sample order (tests, reproducibility)
-        self._rollout_graph = None
-        self._rollout_calls = 0
-        self._rollout_obs = None
-        self._rollout_delta = None
+        self._init_base()
 
     # ---- learning rate -----------------------------------------------------------------------------------------------
     def learning_rate(self) -> float:
@@ -303,17 +282,6 @@ class PPOEngine:
         if self.hetero:
             return self.st_std.mean(dim=0)
         return dist.current_std().detach()
-
-    # ---- normaliser views --------------------------------------------------------------------------------------------
-    @staticmethod
-    def _norm_tensors(model):
-        norm = model.obs_normalizer
-        if isinstance(norm, EmpiricalNormalization):
-            return norm._mean.view(-1), norm._std.view(-1), norm.eps
-        return None, None, 0.0
-
-    def _group_tensors(self, obs, groups):
-        return [obs[g] if obs[g].is_contiguous() else obs[g].contiguous() for g in groups]
 
     # ---- rollout ------------------------------------------------------------------------------------------------------
     def act(self, obs) -> torch.Tensor:
@@ -351,14 +319,6 @@ class PPOEngine:
         ext().process_step(rewards.reshape(-1).float(), None, dones.reshape(-1), timeouts, self.st_values[rows],
                            self.alg.gamma, self.st_rewards[rows], self.st_dones[rows], self.nonfinite)
         self.t += 1
-
-    def check_finite(self, obs, rewards) -> None:
-        """Non-finite rewards are flagged on the device by ``process_step``; nothing to do per step."""
-
-    def raise_if_nonfinite(self) -> None:
-        if int(self.nonfinite.item()) != 0:
-            self.nonfinite.zero_()
-            raise ValueError("The rewards returned by the environment contain NaN or Inf values.")
 
     def compute_returns(self, obs) -> None:
         C = ext()
@@ -403,7 +363,7 @@ class PPOEngine:
         pa.backward(B, self.status)
         pc.backward(B, self.status)
         C.reduce_segments(self.reduce_plan, self.reduce_nseg, self.reduce_chunks, self.send[0], self.send[1],
-                          self.epoch)
+                          self.epoch, False)
         adaptive = alg.desired_kl is not None and alg.schedule == "adaptive"
         kl = self.grads[self.n_params + 3 : self.n_params + 4]
         peers = self.comm.peer_send if self.comm is not None else None
@@ -418,25 +378,8 @@ class PPOEngine:
         self.loss_acc.add_(self.grads[self.n_params : self.n_params + _TAIL])
 
     def _normalizer_updates(self) -> None:
-        C = ext()
-        for name, model, obs, D in (("actor", self.actor, self.obs_a, self.Da), ("critic", self.critic, self.obs_c,
-                                                                                  self.Dc)):
-            norm = model.obs_normalizer
-            if not isinstance(norm, EmpiricalNormalization) or not model.obs_normalization or not norm.training:
-                continue
-            partial = self.colstats_partial[name]
-            C.colstats(obs, self.total, obs.shape[1], D, partial)
-            until = -1 if norm.until is None else int(norm.until)
-            mean, var, std = norm._mean.view(-1), norm._var.view(-1), norm._std.view(-1)
-            if self.comm is None:
-                C.norm_update(partial, self.stats_chunks, self.total, D, mean, var, std, norm.count, until, None,
-                              False)
-                continue
-            # global statistics: per-rank column sums, rank-ordered peer all-reduce, then the running update
-            local, glob = self.moments_local[name], self.moments_global[name]
-            C.norm_update(partial, self.stats_chunks, self.total, D, mean, var, std, norm.count, until, local, True)
-            self.comm.allreduce_f64(local, glob, self.status)
-            C.norm_update(glob[2:], 1, self.total * self.world, D, mean, var, std, norm.count, until, None, False)
+        self._normalizer_update("actor", self.actor, self.obs_a, self.total, self.Da)
+        self._normalizer_update("critic", self.critic, self.obs_c, self.total, self.Dc)
 
     def _update_body(self) -> None:
         ext().counter_add(self.perm_key, 1)
@@ -457,25 +400,6 @@ class PPOEngine:
         stats = (self.loss_acc / float(self.E * self.M)).tolist()
         self._check_status()
         return {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
-
-    def _capture(self, fn):
-        torch.cuda.synchronize(self.device)
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream(device=self.device)
-        s.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(g, stream=s):
-                fn()
-        torch.cuda.current_stream(self.device).wait_stream(s)
-        return g
-
-    def _check_status(self) -> None:
-        st = self.status.tolist()
-        if st[0] != 0:
-            self.status.zero_()
-            from ..parallel import CommTimeoutError
-
-            raise CommTimeoutError(f"device status error code={st[0]} site={st[1]} block={st[2]} count={st[3]}")
 
     # ---- rollout import (tests / external collectors) -------------------------------------------------------------------
     def load_rollout(self, storage) -> None:
@@ -547,49 +471,6 @@ class PPOEngine:
                     torch.distributed.broadcast(t, src=0)
         self.plan_a.refresh_shadows()
         self.plan_c.refresh_shadows()
-
-    # ---- captured rollout (graph-capturable environments) -------------------------------------------------------------
-    def can_capture_rollout(self, env, cfg) -> bool:
-        """A rollout can be one CUDA graph when the environment only enqueues device work (``graph_capturable``)."""
-        return self.use_graphs and bool(getattr(env, "graph_capturable", False))
-
-    def _rollout_steps(self, env, logger, cfg):
-        obs = env.get_observations()
-        for _ in range(self.T):
-            actions = self.act(obs)
-            obs, rewards, dones, extras = env.step(actions)
-            self.process_env_step(obs, rewards, dones, extras)
-            logger.process_env_step(rewards, dones, extras, None)
-        return obs
-
-    def run_captured_rollout(self, env, logger, cfg):
-        """Run ``T`` x (act, env step, store, episode bookkeeping); from the second call on as one graph replay.
-
-        The graph replays exactly the captured work: the environment must keep returning the same observation,
-        reward and done tensors (updated in place), as ``graph_capturable`` environments do. Host-side counters of
-        the logger are advanced by the captured amount after each replay.
-        """
-        if self._rollout_calls == 0:
-            obs = self._rollout_steps(env, logger, cfg)
-        else:
-            if self._rollout_graph is None:
-                before = logger.host_state()
-                t0 = self.t
-                holder = {}
-                self._rollout_graph = self._capture(lambda: holder.setdefault("obs", self._rollout_steps(env, logger,
-                                                                                                         cfg)))
-                self._rollout_obs = holder["obs"]
-                self._rollout_delta = (before, logger.host_state())
-                logger.set_host_state(before)
-                self.t = t0
-            self._rollout_graph.replay()
-            logger.advance_host_state(*self._rollout_delta)
-            self.t += self.T
-            obs = self._rollout_obs
-        self._rollout_calls += 1
-        if cfg.get("check_for_nan", True):
-            self.raise_if_nonfinite()
-        return obs
 
 
 __all__ = ["PPOEngine"]

@@ -281,13 +281,35 @@ std::tuple<Tensor, int64_t, int64_t> make_reduce_plan(const std::vector<Tensor>&
 }
 
 void reduce_segments(const Tensor& plan, int64_t nseg, int64_t chunks, const Tensor& send0, const Tensor& send1,
-                     const OptT& epoch) {
+                     const OptT& epoch, bool accumulate) {
   check_f32(send0, "send0");
   check_f32(send1, "send1");
   ok(rlb::reduce_segments(reinterpret_cast<const rlb::ReduceSegment*>(plan.data_ptr()), static_cast<int>(nseg),
                           static_cast<int>(chunks), P<float>(send0), P<float>(send1), P<const unsigned int>(epoch),
-                          cur()),
+                          accumulate ? 1 : 0, cur()),
      "reduce_segments");
+}
+
+int64_t mse_blocks(int64_t rows) { return rlb::mse_blocks(static_cast<int>(rows)); }
+
+void mse_grad(const Tensor& pred, int64_t ld_pred, const Tensor& target, int64_t ld_target, int64_t rows, int64_t A,
+              bool huber, const Tensor& grad, int64_t ld_grad, int64_t head_cols, const Tensor& loss_partial,
+              const Tensor& colsum_partial, const Tensor& loss_acc, const Tensor& ticket) {
+  check_f32(pred, "pred");
+  check_f32(target, "target");
+  check_bf16(grad, "grad");
+  check_f32(loss_acc, "loss_acc");
+  const int64_t blocks = rlb::mse_blocks(static_cast<int>(rows));
+  TORCH_CHECK(pred.numel() >= (rows - 1) * ld_pred + A && target.numel() >= (rows - 1) * ld_target + A &&
+                  grad.numel() >= rows * ld_grad && ld_grad >= A && head_cols >= A,
+              "mse_grad: sizes");
+  TORCH_CHECK(loss_partial.numel() >= blocks && colsum_partial.numel() >= blocks * head_cols, "mse_grad: partials");
+  TORCH_CHECK(ticket.scalar_type() == at::kInt && ticket.is_cuda(), "mse_grad: ticket must be int32 on the device");
+  rlb::MseArgs a{P<const float>(pred), static_cast<int>(ld_pred), P<const float>(target), static_cast<int>(ld_target),
+                 static_cast<int>(rows), static_cast<int>(A), huber ? 1 : 0, grad.data_ptr(),
+                 static_cast<int>(ld_grad), static_cast<int>(head_cols), P<float>(loss_partial),
+                 P<float>(colsum_partial), P<float>(loss_acc), reinterpret_cast<unsigned int*>(ticket.data_ptr())};
+  ok(rlb::mse_grad(a, cur()), "mse_grad");
 }
 
 // ---- Adam plan -------------------------------------------------------------------------------------------------
@@ -483,6 +505,8 @@ void rlb_register_kernels(pybind11::module& m) {
   m.def("ppo_loss", &ppo_loss);
   m.def("make_reduce_plan", &make_reduce_plan);
   m.def("reduce_segments", &reduce_segments);
+  m.def("mse_blocks", &mse_blocks);
+  m.def("mse_grad", &mse_grad);
   m.def("make_adam_plan", &make_adam_plan);
   m.def("adam_grid", &adam_grid);
   m.def("adam_step", &adam_step);

@@ -514,6 +514,79 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Behaviour-cloning loss gradient: one warp per row (lane j: columns j, j + 32), 8 warps x 4 rows per block
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kMseWarps = 8;
+constexpr int kMseRowsPerWarp = 4;
+constexpr int kMseRowsPerBlock = kMseWarps * kMseRowsPerWarp;
+
+__global__ void __launch_bounds__(kMseWarps * 32) mse_grad_kernel(const MseArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float inv_n = 1.0f / (static_cast<float>(a.rows) * static_cast<float>(a.A));
+  float col[2] = {0.f, 0.f};
+  float loss = 0.f;
+  const int row0 = blockIdx.x * kMseRowsPerBlock + warp * kMseRowsPerWarp;
+  for (int r = 0; r < kMseRowsPerWarp; ++r) {
+    const int i = row0 + r;
+    if (i >= a.rows) break;
+    __nv_bfloat16* g = static_cast<__nv_bfloat16*>(a.grad) + static_cast<size_t>(i) * a.ld_grad;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int j = lane + 32 * k;
+      if (j < a.A) {
+        const float d = a.pred[static_cast<size_t>(i) * a.ld_pred + j] - a.target[static_cast<size_t>(i) * a.ld_target + j];
+        float gd;
+        if (a.huber) {  // torch huber_loss, delta = 1: 0.5 d^2 inside |d| < 1, |d| - 0.5 outside
+          const float ad = fabsf(d);
+          loss += ad < 1.f ? 0.5f * d * d : ad - 0.5f;
+          gd = fminf(fmaxf(d, -1.f), 1.f) * inv_n;
+        } else {
+          loss += d * d;
+          gd = 2.f * d * inv_n;
+        }
+        g[j] = __float2bfloat16_rn(gd);
+        col[k] += gd;
+      } else if (j < a.ld_grad) {
+        g[j] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) loss += __shfl_xor_sync(0xffffffffu, loss, off);
+  __shared__ float s_col[kMseWarps][64];
+  __shared__ float s_loss[kMseWarps];
+  __shared__ bool s_last;
+  s_col[warp][lane] = col[0];
+  s_col[warp][lane + 32] = col[1];
+  if (lane == 0) s_loss[warp] = loss;
+  __syncthreads();
+  if (threadIdx.x < a.head_cols) {
+    float c = 0.f;
+    for (int w = 0; w < kMseWarps; ++w) c += s_col[w][threadIdx.x];
+    a.colsum_partial[static_cast<size_t>(blockIdx.x) * a.head_cols + threadIdx.x] = c;
+  }
+  if (threadIdx.x == 0) {
+    float l = 0.f;
+    for (int w = 0; w < kMseWarps; ++w) l += s_loss[w];
+    a.loss_partial[blockIdx.x] = l;
+    __threadfence();
+    s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last || warp != 0) return;
+  // last block: fixed-order sum of the block partials (lane-strided, then a butterfly)
+  __threadfence();
+  float t = 0.f;
+  for (int b = lane; b < static_cast<int>(gridDim.x); b += 32) t += __ldcg(a.loss_partial + b);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+  if (lane == 0) {
+    *a.loss_acc += t * inv_n;
+    *a.ticket = 0u;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // segment reduction (sum of partial slabs in fixed order, fp64 accumulation)
 // ---------------------------------------------------------------------------------------------------------------
 // Block = 32 columns x 32 part-lanes: lane y sums parts y, y + 32, ... of its column (coalesced 128-byte rows), then the
@@ -521,7 +594,8 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
 constexpr int kReduceCols = 32;
 constexpr int kReduceLanes = 32;
 __global__ void __launch_bounds__(kReduceCols* kReduceLanes)
-    reduce_segments_kernel(const ReduceSegment* segs, int nseg, float* send0, float* send1, const unsigned int* epoch) {
+    reduce_segments_kernel(const ReduceSegment* segs, int nseg, float* send0, float* send1, const unsigned int* epoch,
+                           int accumulate) {
   const int chunk = blockIdx.x;
   int s = 0;
   while (s + 1 < nseg && segs[s + 1].first_chunk <= chunk) ++s;
@@ -540,7 +614,7 @@ __global__ void __launch_bounds__(kReduceCols* kReduceLanes)
     double t = 0.0;
 #pragma unroll
     for (int y = 0; y < kReduceLanes; ++y) t += sh[y][threadIdx.x];
-    dst[e] = static_cast<float>(t);
+    dst[e] = accumulate ? dst[e] + static_cast<float>(t) : static_cast<float>(t);
   }
 }
 
@@ -963,9 +1037,19 @@ cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
 }
 
 cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_chunks, float* send0, float* send1,
-                            const unsigned int* epoch, cudaStream_t s) {
+                            const unsigned int* epoch, int accumulate, cudaStream_t s) {
   if (nseg <= 0 || total_chunks <= 0) return cudaErrorInvalidValue;
-  reduce_segments_kernel<<<total_chunks, dim3(kReduceCols, kReduceLanes), 0, s>>>(segs_dev, nseg, send0, send1, epoch);
+  reduce_segments_kernel<<<total_chunks, dim3(kReduceCols, kReduceLanes), 0, s>>>(segs_dev, nseg, send0, send1, epoch,
+                                                                                    accumulate);
+  return cudaGetLastError();
+}
+
+int mse_blocks(int rows) { return (rows + kMseRowsPerBlock - 1) / kMseRowsPerBlock; }
+
+cudaError_t mse_grad(const MseArgs& a, cudaStream_t s) {
+  if (a.A > 64 || a.rows <= 0 || a.ld_grad > 64 || a.head_cols > 64 || a.head_cols < a.A || a.ld_grad < a.A)
+    return cudaErrorInvalidValue;
+  mse_grad_kernel<<<mse_blocks(a.rows), kMseWarps * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 

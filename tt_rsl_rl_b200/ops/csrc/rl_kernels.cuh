@@ -156,7 +156,29 @@ struct ReduceSegment {
   int first_chunk;      // prefix of chunk counts
 };
 cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_chunks, float* send0, float* send1,
-                            const unsigned int* epoch, cudaStream_t s);
+                            const unsigned int* epoch, int accumulate, cudaStream_t s);
+
+// Behaviour-cloning loss (distillation), ``mse`` or ``huber`` (delta 1) averaged over rows x A. Writes the bf16
+// gradient of the mean loss into grad [rows, ld_grad] (columns A .. ld_grad zero), per-block column sums of that
+// gradient over head_cols columns (the output-layer bias gradient; columns >= A are zero) and adds the loss to
+// *loss_acc (per-block partials summed by the last block in a fixed order, so the value is deterministic).
+struct MseArgs {
+  const float* pred;
+  int ld_pred;
+  const float* target;
+  int ld_target;
+  int rows, A;
+  int huber;
+  void* grad;
+  int ld_grad;
+  int head_cols;
+  float* loss_partial;    // [blocks]
+  float* colsum_partial;  // [blocks, head_cols]
+  float* loss_acc;        // [1], accumulated
+  unsigned int* ticket;   // [1], zero between launches
+};
+int mse_blocks(int rows);
+cudaError_t mse_grad(const MseArgs& a, cudaStream_t s);
 constexpr int kReduceChunk = 32;  // columns per block of the reduction kernel
 
 // Fused (all-reduce over peers) + per-group global-norm clip + adaptive learning rate + Adam + bf16 weight shadows.
