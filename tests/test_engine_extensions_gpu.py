@@ -1,0 +1,189 @@
+"""RND and symmetry on the fused PPO engine against the PyTorch path of the same algorithm on identical data."""
+
+import copy
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _mirror(dims: dict, A: int, seed: int = 0):
+    """A signed-permutation augmentation (two copies) in the shape upstream symmetry functions have."""
+    from tt_rsl_rl_b200.utils.tensordict import TensorDict
+
+    gen = torch.Generator().manual_seed(seed)
+    maps = {}
+    for g, D in dims.items():
+        maps[g] = (torch.randperm(D, generator=gen), torch.where(torch.rand(D, generator=gen) < 0.3, -1.0, 1.0))
+    act = (torch.randperm(A, generator=gen), torch.where(torch.rand(A, generator=gen) < 0.3, -1.0, 1.0))
+
+    def fn(env=None, obs=None, actions=None):
+        out_obs = out_act = None
+        if obs is not None:
+            data = {}
+            for g in obs.keys():
+                x = obs[g]
+                p, s = maps[g]
+                data[g] = torch.cat([x, x[:, p.to(x.device)] * s.to(x.device)])
+            out_obs = TensorDict(data, batch_size=[2 * obs.batch_size[0]], device=obs.device)
+        if actions is not None:
+            p, s = act
+            out_act = torch.cat([actions, actions[:, p.to(actions.device)] * s.to(actions.device)])
+        return out_obs, out_act
+
+    return fn
+
+
+def _pair(env, T, hidden, M=4, E=2, rnd=False, sym=None):
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    obs = env.get_observations()
+    groups = {"actor": ["policy"], "critic": ["critic"], "rnd_state": ["critic"]}
+    dist = {"class_name": "GaussianDistribution", "init_std": 1.0}
+    actor = MLPModel(obs, groups, "actor", env.num_actions, hidden_dims=hidden, obs_normalization=True,
+                     distribution_cfg=dist)
+    critic = MLPModel(obs, groups, "critic", 1, hidden_dims=hidden, obs_normalization=True)
+    kw = dict(num_learning_epochs=E, num_mini_batches=M)
+    if rnd:
+        kw["rnd_cfg"] = {"num_states": obs["critic"].shape[1], "obs_groups": groups, "num_outputs": 16,
+                         "predictor_hidden_dims": [128, 64], "target_hidden_dims": [128, 64], "weight": 0.5}
+    if sym is not None:
+        kw["symmetry_cfg"] = dict(sym, env=env)
+    storage = RolloutStorage("rl", env.num_envs, T, obs, [env.num_actions], "cuda")
+    alg_t = PPO(actor, critic, storage, device="cuda", b200_cfg={"engine": "torch"}, **copy.deepcopy(kw))
+    alg_e = PPO(copy.deepcopy(actor), copy.deepcopy(critic), None, device="cuda",
+                b200_cfg={"engine": "cuda", "graphs": False}, num_steps_per_env=T, num_envs=env.num_envs,
+                obs_template=obs, **copy.deepcopy(kw))
+    assert alg_e.engine is not None
+    if rnd:
+        alg_e.rnd.load_state_dict(alg_t.rnd.state_dict())
+        alg_e.engine.sync_from_torch()
+    return alg_t, alg_e
+
+
+def _rollout_and_share(alg_t, alg_e, env, T, N):
+    obs = env.get_observations()
+    with torch.inference_mode():
+        for _ in range(T):
+            actions = alg_t.act(obs)
+            obs, rew, dones, extras = env.step(actions)
+            alg_t.process_env_step(obs, rew, dones, extras)
+        alg_t.compute_returns(obs)
+    st = alg_t.storage
+    eng = alg_e.engine
+    eng.load_rollout(st)
+    perm = torch.randperm(T * N, device="cuda")
+    eng.perm_override = perm.int()
+    st.mini_batch_generator = (lambda orig: (lambda M, E: orig(M, E, indices=perm)))(st.mini_batch_generator)
+    return st.observations.flatten(0, 1)[:4096]
+
+
+def _dev(new_e, new_t, old):
+    return ((new_e - new_t).norm() / (new_t - old).norm()).item()
+
+
+@pytest.mark.parametrize("aug,mirror", [(True, True), (False, True), (True, False)])
+def test_engine_symmetry_matches_torch_path(aug, mirror):
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+
+    torch.manual_seed(0)
+    T, N = 8, 1024
+    env = LinearGaussianVecEnv(N, obs_dim=40, num_actions=10, privileged_dim=3, device="cuda")
+    dims = {g: env.get_observations()[g].shape[1] for g in env.get_observations().keys()}
+    sym = {"data_augmentation_func": _mirror(dims, 10), "use_data_augmentation": aug, "use_mirror_loss": mirror,
+           "mirror_loss_coeff": 0.5}
+    alg_t, alg_e = _pair(env, T, [128, 64], sym=sym)
+    assert alg_e.engine.K == 2
+    probe = _rollout_and_share(alg_t, alg_e, env, T, N)
+    with torch.no_grad():
+        m_old, v_old = alg_t.actor(probe).clone(), alg_t.critic(probe).clone()
+    loss_t = alg_t.update()
+    loss_e = alg_e.update()
+    with torch.no_grad():
+        assert _dev(alg_e.actor(probe), alg_t.actor(probe), m_old) < 0.15
+        assert _dev(alg_e.critic(probe), alg_t.critic(probe), v_old) < 0.15
+    for k in ("value", "surrogate", "entropy", "symmetry"):
+        assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=2e-3), (k, loss_e[k], loss_t[k])
+    assert alg_e.learning_rate == pytest.approx(alg_t.learning_rate, rel=1e-6)
+
+
+def test_engine_rnd_matches_torch_path():
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+
+    torch.manual_seed(1)
+    T, N = 8, 1024
+    env = LinearGaussianVecEnv(N, obs_dim=40, num_actions=10, privileged_dim=3, device="cuda")
+    alg_t, alg_e = _pair(env, T, [128, 64], rnd=True)
+    # intrinsic reward of one fused step against the PyTorch networks on the same observations
+    obs = env.get_observations()
+    with torch.inference_mode():
+        actions = alg_e.act(obs)
+        obs2, rew, dones, extras = env.step(actions)
+        alg_e.process_env_step(obs2, rew, dones, extras)
+        s = obs2["critic"]
+        ref = torch.linalg.norm(alg_t.rnd.target(s) - alg_t.rnd.predictor(s), dim=1) * alg_t.rnd.initial_weight
+    torch.testing.assert_close(alg_e.engine.intrinsic, ref, rtol=3e-2, atol=3e-2 * ref.abs().mean().item())
+    assert alg_e.rnd.update_counter == T  # the schedule advanced by one rollout
+    alg_e.engine.t = 0
+    probe = _rollout_and_share(alg_t, alg_e, env, T, N)
+    with torch.no_grad():
+        m_old, v_old = alg_t.actor(probe).clone(), alg_t.critic(probe).clone()
+        s = probe["critic"]
+        p_old = alg_t.rnd.predictor(s).clone()
+    loss_t = alg_t.update()
+    loss_e = alg_e.update()
+    with torch.no_grad():
+        assert _dev(alg_e.actor(probe), alg_t.actor(probe), m_old) < 0.15
+        assert _dev(alg_e.critic(probe), alg_t.critic(probe), v_old) < 0.15
+        assert _dev(alg_e.rnd.predictor(s), alg_t.rnd.predictor(s), p_old) < 0.15
+    for k in ("value", "surrogate", "entropy", "rnd"):
+        assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=2e-3), (k, loss_e[k], loss_t[k])
+    # the predictor has its own optimizer: step count and learning rate are separate from PPO's
+    assert int(alg_e.engine.step[2].item()) == 2 * 4
+    alg_e.engine.sync_to_torch()
+    st = alg_e.rnd.optimizer.state
+    assert len(st) == len(list(alg_e.rnd.predictor.parameters()))
+    assert all(float(v["step"]) == 8 for v in st.values())
+
+
+def test_runner_with_rnd_and_symmetry_captured(tmp_path):
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    torch.manual_seed(2)
+    env = LinearGaussianVecEnv(512, obs_dim=32, num_actions=8, privileged_dim=3, device="cuda")
+    dims = {g: env.get_observations()[g].shape[1] for g in env.get_observations().keys()}
+    cfg = {
+        "num_steps_per_env": 6, "save_interval": 1000,
+        "obs_groups": {"actor": ["policy"], "critic": ["critic"], "rnd_state": ["critic"]},
+        "algorithm": {"class_name": "PPO", "num_learning_epochs": 2, "num_mini_batches": 2,
+                      "b200_cfg": {"engine": "cuda"},
+                      "rnd_cfg": {"num_outputs": 8, "predictor_hidden_dims": [64], "target_hidden_dims": [64],
+                                  "weight": 1.0, "state_normalization": True},
+                      "symmetry_cfg": {"data_augmentation_func": _mirror(dims, 8), "use_data_augmentation": True,
+                                       "use_mirror_loss": True, "mirror_loss_coeff": 1.0}},
+        "actor": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True,
+                  "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+        "critic": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True},
+    }
+    runner = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir=str(tmp_path), device="cuda")
+    eng = runner.alg.engine
+    assert eng is not None and eng.rnd is not None and eng.K == 2
+    runner.learn(4)
+    assert runner.alg.rnd.update_counter == 4 * 6
+    assert torch.isfinite(eng.flat).all()
+    assert int(runner.alg.rnd.state_normalizer.count) == 4 * 6 * 512
+    path = str(tmp_path / "m.pt")
+    runner.save(path)
+    ck = torch.load(path, weights_only=False)
+    assert ck["rnd_update_counter"] == 24
+    assert ck["rnd_optimizer_state_dict"]["state"]
+    runner2 = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    runner2.load(path)
+    torch.testing.assert_close(runner2.alg.engine.flat, eng.flat)
+    torch.testing.assert_close(runner2.alg.engine.exp_avg, eng.exp_avg)
+    assert runner2.alg.engine.step.tolist() == eng.step.tolist()
+    runner2.learn(1)

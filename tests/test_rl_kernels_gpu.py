@@ -88,13 +88,14 @@ def test_ppo_loss_matches_autograd(hetero, log_std):
     blocks = C().ppo_loss_blocks(B)
     d_head = torch.zeros(B, (hc + 7) // 8 * 8, device=dev, dtype=torch.bfloat16)
     d_value = torch.zeros(B, 8, device=dev, dtype=torch.bfloat16)
-    stats = torch.zeros(blocks, 4, device=dev)
+    stats = torch.zeros(blocks, 5, device=dev)
     dh_col = torch.zeros(blocks, hc, device=dev)
     dv_col = torch.zeros(blocks, 1, device=dev)
     dstd = torch.zeros(blocks, A, device=dev)
     C().ppo_loss(B, A, hetero, log_std, head, hc, value, 1, None if hetero else std_raw, 1e-6, 1e6, math.log(1e-6),
                  math.log(1e6), idx, st_actions, st_mean, st_std, st_logp, st_adv, st_ret, st_val, None, clip, vc, ec,
-                 True, d_head, d_head.shape[1], d_value, 8, stats, dh_col, dv_col, None if hetero else dstd)
+                 True, d_head, d_head.shape[1], d_value, 8, stats, dh_col, dv_col, None if hetero else dstd, 1, False,
+                 None, None, 0.0)
     torch.cuda.synchronize()
     scale = ref["dhead"].abs().max().item()
     torch.testing.assert_close(d_head[:, :hc].float(), ref["dhead"], atol=1e-2 * scale, rtol=1e-2)
@@ -159,7 +160,7 @@ def test_gather_feistel_permutation_and_normalisation():
         xa = torch.zeros(B, 96, device=dev, dtype=torch.bfloat16)
         xc = torch.zeros(B, 104, device=dev, dtype=torch.bfloat16)
         C().gather_minibatch(B, start, total, key, hb, None, idx, [obs_a, obs_c], [mean_a, None], [std_a, None], 1e-2,
-                             [xa, xc], [96, 104], None)
+                             [xa, xc], [96, 104], None, 1, [B, B], [None, None], [None, None])
         torch.cuda.synchronize()
         il = idx.long()
         seen.append(il)

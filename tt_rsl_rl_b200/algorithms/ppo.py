@@ -115,6 +115,7 @@ class PPO:
         self.normalize_advantage_per_mini_batch = normalize_advantage_per_mini_batch
         self.use_mixed_precision = use_mixed_precision
         self.intrinsic_rewards: torch.Tensor | None = None
+        self._obs_template = obs_template
 
         self.engine = None
         if self._engine_requested():

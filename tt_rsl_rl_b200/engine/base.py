@@ -12,7 +12,11 @@ from ..ops import ext
 
 def elu_mlp_reason(model) -> str | None:
     """None if ``model.mlp`` is a Linear/ELU(alpha=1) stack the fused GEMM epilogues cover, else the reason."""
-    mlp = getattr(model, "mlp", None)
+    return elu_stack_reason(getattr(model, "mlp", None))
+
+
+def elu_stack_reason(mlp) -> str | None:
+    """None if the sequential ``mlp`` holds only Linear, ELU(alpha=1) and Unflatten layers, else the reason."""
     if mlp is None:
         return "model has no MLP head"
     for m in mlp:
@@ -40,7 +44,10 @@ class EngineBase:
     # ---- normaliser views --------------------------------------------------------------------------------------------
     @staticmethod
     def _norm_tensors(model):
-        norm = model.obs_normalizer
+        return EngineBase._norm_views(model.obs_normalizer)
+
+    @staticmethod
+    def _norm_views(norm):
         if isinstance(norm, EmpiricalNormalization):
             return norm._mean.view(-1), norm._std.view(-1), norm.eps
         return None, None, 0.0
@@ -61,12 +68,14 @@ class EngineBase:
     def _normalizer_update(self, name: str, model, obs: torch.Tensor, rows: int, D: int) -> None:
         """Running-moment update of ``model``'s normaliser from ``obs[:rows, :D]`` (global over ranks when
         data-parallel: per-rank column sums, rank-ordered peer all-reduce, then the running update)."""
-        norm = model.obs_normalizer
-        if not isinstance(norm, EmpiricalNormalization) or not model.obs_normalization or not norm.training:
+        self._norm_module_update(name, model.obs_normalizer, model.obs_normalization, obs, rows, D)
+
+    def _norm_module_update(self, name: str, norm, enabled: bool, obs: torch.Tensor, rows: int, D: int) -> None:
+        if not isinstance(norm, EmpiricalNormalization) or not enabled or not norm.training:
             return
         C = ext()
         partial = self.colstats_partial[name]
-        C.colstats(obs, rows, obs.shape[1], D, partial)
+        C.colstats(obs, rows, obs.stride(0), D, partial)
         until = -1 if norm.until is None else int(norm.until)
         mean, var, std = norm._mean.view(-1), norm._var.view(-1), norm._std.view(-1)
         if self.comm is None:
@@ -116,7 +125,7 @@ class EngineBase:
             actions = self.act(obs)
             obs, rewards, dones, extras = env.step(actions)
             self.process_env_step(obs, rewards, dones, extras)
-            logger.process_env_step(rewards, dones, extras, None)
+            logger.process_env_step(rewards, dones, extras, getattr(self, "intrinsic_for_logger", None))
         return obs
 
     def run_captured_rollout(self, env, logger, cfg):
@@ -139,6 +148,7 @@ class EngineBase:
                 self._rollout_delta = (before, logger.host_state())
                 logger.set_host_state(before)
                 self.t = t0
+            self._before_replay()
             self._rollout_graph.replay()
             logger.advance_host_state(*self._rollout_delta)
             self.t += self.T
@@ -147,6 +157,9 @@ class EngineBase:
         if cfg.get("check_for_nan", True):
             self.raise_if_nonfinite()
         return obs
+
+    def _before_replay(self) -> None:
+        """Host-side preparation of a replayed rollout (e.g. per-step schedules written to device buffers)."""
 
     # overridden by the engines
     def act(self, obs):  # pragma: no cover - abstract

@@ -34,7 +34,7 @@ def wgrad_splits(out_f: int, in_f: int, rows: int, sm_count: int) -> int:
 
 class MLPPlan:
     def __init__(self, mlp: nn.Module, in_dim: int, rows_roll: int, rows_train: int, device: torch.device,
-                 sm_count: int, train: bool = True) -> None:
+                 sm_count: int, train: bool = True, grads: bool = True) -> None:
         self.linears: list[nn.Linear] = [m for m in mlp if isinstance(m, nn.Linear)]
         self.L = len(self.linears)
         self.widths = [in_dim] + [lin.out_features for lin in self.linears]
@@ -59,6 +59,9 @@ class MLPPlan:
         self.x_train = torch.zeros(B, pad8(in_dim), **bf)
         self.h_train = [torch.zeros(B, pad8(w), **bf) for w in self.widths[1:-1]]
         self.out_train = torch.zeros(B, self.head_cols, **f32)
+        self.grads = grads
+        if not grads:  # inference-only training-size buffers (a frozen network evaluated on minibatches)
+            return
         # gradient of the head output (written by the loss kernel) and of hidden pre-activations
         self.d_head = torch.zeros(B, pad8(self.head_cols), **bf)
         self.dz = [torch.zeros(B, pad8(w), **bf) for w in self.widths[1:-1]]
@@ -110,7 +113,9 @@ class MLPPlan:
             out_f, in_f = lin.out_features, lin.in_features
             h_in = inputs[l]
             part = self.wgrad_partial[l]
-            splits = self.splits[l]
+            splits = min(self.splits[l], (rows + 63) // 64)
+            if splits < self.splits[l]:  # a shorter minibatch: unused split partials must not keep stale sums
+                part[splits:].zero_()
             # dW_l = dZ_l^T H_{l-1}: both operands read MN-major from row-major [rows, features] buffers
             G.gemm(dz_l, dz_l.shape[1], True, h_in, h_in.shape[1], True, out_f, in_f, rows, G.EPI_PARTIAL_F32, part,
                    in_f, splits=splits, split_stride=out_f * in_f, status=status)
@@ -119,8 +124,12 @@ class MLPPlan:
             # dZ_{l-1} = (dZ_l W_l) * elu'(H_{l-1}); W_l [out, pad8(in)] read MN-major
             w = self.w_bf16[l]
             dz_prev = self.dz[l - 1]
+            colsum = self.bias_partial[l - 1]
+            used = G.m_tiles(rows)
+            if used < self.m_tiles:
+                colsum[used:].zero_()
             G.gemm(dz_l, dz_l.shape[1], False, w, w.shape[1], True, rows, in_f, out_f, G.EPI_DGRAD_ELU, dz_prev,
-                   dz_prev.shape[1], aux=h_in, ld_aux=h_in.shape[1], colsum=self.bias_partial[l - 1], status=status)
+                   dz_prev.shape[1], aux=h_in, ld_aux=h_in.shape[1], colsum=colsum, status=status)
             dz_l = dz_prev
 
     # ---- gradient reduction segments ----------------------------------------------------------------------------------

@@ -13,6 +13,12 @@ buffers. Per iteration:
   then the observation normaliser update. From the second call on the whole update is one CUDA graph replay and the
   only host synchronisation is the read of the loss statistics at the end.
 
+Extensions: with RND (``rsl_rl/extensions/rnd.py``) the target and predictor MLPs run on the same GEMMs, the intrinsic
+reward is added on the device during the rollout and the predictor is a third parameter group of the fused optimizer
+launch (its own learning rate, no clipping). With symmetry (``rsl_rl/extensions/symmetry.py``) the augmentation
+function is probed once as per-copy signed permutations; the gather kernel writes the mirrored observation copies and
+the loss kernel mirrors the actions and adds the mirror-loss gradient.
+
 Semantics follow ``rsl_rl/algorithms/ppo.py`` (see the kernels' comments for the exact rules). The random number
 streams differ from PyTorch's (Philox in-kernel sampling, Feistel permutation instead of ``torch.randperm``).
 """
@@ -26,12 +32,45 @@ import torch.nn as nn
 
 from ..modules import GaussianDistribution, HeteroscedasticGaussianDistribution
 from ..ops import ext
-from .base import EngineBase, elu_mlp_reason
+from .base import EngineBase, elu_mlp_reason, elu_stack_reason
 from .mlp_plan import MLPPlan, pad8
 
 _GROUP_ACTOR = 0
 _GROUP_CRITIC = 1
-_TAIL = 4  # exchanged statistics after the parameters: surrogate, value, entropy, kl (each a minibatch mean)
+_GROUP_RND = 2
+_TAIL = 5  # exchanged statistics after the parameters: surrogate, value, entropy, kl, symmetry (minibatch means)
+_MAX_COPIES = 8
+
+
+def _rnd_reason(rnd) -> str | None:
+    if getattr(rnd, "reward_normalization", False):
+        return "RND reward normalisation runs on the PyTorch path"
+    for name in ("predictor", "target"):
+        reason = elu_stack_reason(getattr(rnd, name))
+        if reason:
+            return f"RND {name}: {reason}"
+    if rnd.num_outputs > 64 or rnd.num_states > 1024:
+        return "RND network too wide"
+    return None
+
+
+def _padded_rows(rows: int, dim: int, device) -> torch.Tensor:
+    """A [rows, dim] fp32 view of a zero buffer whose row pitch is dim rounded up to 4 floats (16 bytes)."""
+    return torch.zeros(rows, (dim + 3) // 4 * 4, dtype=torch.float32, device=device)[:, :dim]
+
+
+def _model_maps(obs_maps: dict, groups: list[str], K: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Concatenate per-group signed permutations into the model's input columns: (perm [K, D] int32, sign [K, D])."""
+    perms, signs, off = [], [], 0
+    for g in groups:
+        perm, sign = obs_maps[g]
+        if perm.shape[0] != K:
+            raise ValueError("symmetry: every observation group needs the same number of copies")
+        perms.append(perm + off)
+        signs.append(sign)
+        off += perm.shape[1]
+    return (torch.cat(perms, 1).to(device=device, dtype=torch.int32).contiguous(),
+            torch.cat(signs, 1).to(device=device, dtype=torch.float32).contiguous())
 
 
 class PPOEngine(EngineBase):
@@ -59,10 +98,12 @@ class PPOEngine(EngineBase):
             return "critic has a distribution"
         if critic.mlp.linears[-1].out_features != 1:
             return "critic output is not scalar"
-        if alg_cfg.get("rnd_cfg"):
-            return "RND extension runs on the PyTorch path"
-        if alg_cfg.get("symmetry_cfg"):
-            return "symmetry extension runs on the PyTorch path"
+        rnd_cfg = alg_cfg.get("rnd_cfg")
+        if isinstance(rnd_cfg, dict):
+            if rnd_cfg.get("reward_normalization", False):
+                return "RND reward normalisation runs on the PyTorch path"
+            if str(rnd_cfg.get("activation", "elu")).lower() != "elu":
+                return "RND activation is not fused (ELU only)"
         if alg_cfg.get("normalize_advantage_per_mini_batch"):
             return "per-minibatch advantage normalisation runs on the PyTorch path"
         if str(alg_cfg.get("optimizer", "adam")).lower() != "adam":
@@ -72,12 +113,33 @@ class PPOEngine(EngineBase):
     @staticmethod
     def unsupported_reason(alg) -> str | None:
         cfg = {
-            "rnd_cfg": alg.rnd is not None,
-            "symmetry_cfg": alg.symmetry is not None,
             "normalize_advantage_per_mini_batch": alg.normalize_advantage_per_mini_batch,
             "optimizer": getattr(alg, "optimizer_name", "adam"),
         }
-        return PPOEngine.supports_models(alg.actor, alg.critic, cfg)
+        reason = PPOEngine.supports_models(alg.actor, alg.critic, cfg)
+        if reason is not None:
+            return reason
+        if alg.rnd is not None:
+            reason = _rnd_reason(alg.rnd)
+            if reason is not None:
+                return reason
+        if alg.symmetry is not None:
+            template = getattr(alg, "_obs_template", None)
+            if template is None:
+                return "symmetry needs the observation template to probe the augmentation"
+            A = alg.actor.distribution.output_dim
+            maps = alg.symmetry.probe_signed_permutations(template, A)
+            if maps is None:
+                return "symmetry augmentation is not a per-copy signed permutation"
+            obs_maps, act_maps = maps
+            K = int(act_maps[0].shape[0])
+            if not 2 <= K <= _MAX_COPIES:
+                return f"symmetry with {K} copies"
+            groups = set(alg.actor.obs_groups) | set(alg.critic.obs_groups)
+            if any(obs_maps[g][0].shape[0] != K for g in groups):
+                return "symmetry copies differ between observation groups and actions"
+            alg._symmetry_maps = maps
+        return None
 
     # ---- construction -------------------------------------------------------------------------------------------------
     def __init__(self, alg, num_steps_per_env: int, num_envs: int, obs_template) -> None:
@@ -113,10 +175,31 @@ class PPOEngine(EngineBase):
         self.Dc = self.critic.obs_dim
         self.shared_obs = self.groups_a == self.groups_c
 
+        # ---- symmetry: K copies of every minibatch row (copy 0 = the sample) ----
+        self.sym = alg.symmetry
+        self.K, self.aug, self.mirror_coef = 1, False, 0.0
+        self.perm_a = self.sign_a = self.perm_c = self.sign_c = self.act_perm = self.act_sign = None
+        if self.sym is not None:
+            obs_maps, act_maps = alg._symmetry_maps
+            self.K = int(act_maps[0].shape[0])
+            self.aug = bool(self.sym.use_data_augmentation)
+            self.mirror_coef = float(self.sym.mirror_loss_coeff) if self.sym.use_mirror_loss else 0.0
+            self.perm_a, self.sign_a = _model_maps(obs_maps, self.groups_a, self.K, dev)
+            self.perm_c, self.sign_c = _model_maps(obs_maps, self.groups_c, self.K, dev)
+            self.act_perm = act_maps[0].to(device=dev, dtype=torch.int32).contiguous()
+            self.act_sign = act_maps[1].to(device=dev, dtype=torch.float32).contiguous()
+        self.rows_a_max = self.K * self.B_max
+        self.rows_c_max = self.rows_a_max if self.aug else self.B_max
+        self.rnd = alg.rnd
+
         # ---- flat parameter arena (views installed into the nn.Parameters) ----
         self.params = list(dict.fromkeys(chain(self.actor.parameters(), self.critic.parameters())))
         actor_ids = {id(p) for p in self.actor.parameters()}
         self.param_group = [_GROUP_ACTOR if id(p) in actor_ids else _GROUP_CRITIC for p in self.params]
+        if self.rnd is not None:
+            rnd_params = list(self.rnd.predictor.parameters())
+            self.params += rnd_params
+            self.param_group += [_GROUP_RND] * len(rnd_params)
         self.offsets = []
         off = 0
         for p in self.params:
@@ -130,9 +213,12 @@ class PPOEngine(EngineBase):
         n_ex = (self.n_params + _TAIL + 3) // 4 * 4  # exchanged floats: parameters + statistics, float4 granules
         self.n_ex = n_ex
         n_actor = sum(p.numel() for p, g in zip(self.params, self.param_group) if g == _GROUP_ACTOR)
+        n_ac = sum(p.numel() for p, g in zip(self.params, self.param_group) if g != _GROUP_RND)
         if self.param_group != sorted(self.param_group):
             raise RuntimeError("fused engine: actor parameters must precede critic parameters")
-        self.group_ranges = [0, n_actor, n_actor, self.n_params]
+        self.group_ranges = [0, n_actor, n_actor, n_ac]
+        if self.rnd is not None:
+            self.group_ranges += [n_ac, self.n_params]
         self.exp_avg = torch.zeros(self.n_params, **f32)
         self.exp_avg_sq = torch.zeros(self.n_params, **f32)
         # ---- data parallel: symmetric send buffers shared with the peers (CUDA IPC) ----
@@ -143,7 +229,9 @@ class PPOEngine(EngineBase):
         if self.world > 1:
             from ..parallel import PeerExchange
 
-            small = max(4 * self.n_params, 8 * (2 + 2 * max(self.Da, self.Dc)), 4096)
+            big = max((t.numel() for t in self.rnd.state_dict().values()), default=0) if self.rnd is not None else 0
+            dmax = max(self.Da, self.Dc, self.rnd.num_states if self.rnd is not None else 0)
+            small = max(4 * self.n_params, 4 * big, 8 * (2 + 2 * dmax), 4096)
             self.comm = PeerExchange.create(n_ex, small, rank=self.rank, world=self.world, device=dev,
                                             timeout_ms=alg.b200_cfg["comm_timeout_ms"])
             self.send = self.comm.send
@@ -151,8 +239,10 @@ class PPOEngine(EngineBase):
             buf = torch.zeros(n_ex, **f32)
             self.send = [buf, buf]
         self.grads = torch.zeros(n_ex, **f32)
-        self.lr = torch.tensor([alg._learning_rate, alg._learning_rate], **f32)
-        self.step = torch.zeros(2, dtype=torch.int64, device=dev)
+        # learning-rate slots: 0 = PPO optimizer (adaptive), 2 = RND predictor optimizer; one step counter per group
+        lr_rnd = self.rnd.optimizer.param_groups[0]["lr"] if self.rnd is not None else 0.0
+        self.lr = torch.tensor([alg._learning_rate, alg._learning_rate, lr_rnd], **f32)
+        self.step = torch.zeros(3, dtype=torch.int64, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = torch.zeros(4, dtype=torch.int32, device=dev)
         self.barrier = torch.zeros(4, dtype=torch.int32, device=dev)
@@ -166,16 +256,25 @@ class PPOEngine(EngineBase):
             raise ValueError("rollout batch too large for the fused engine")
 
         # ---- MLP plans ----
-        self.plan_a = MLPPlan(self.actor.mlp, self.Da, self.N, self.B_max, dev, self.sm_count)
-        self.plan_c = MLPPlan(self.critic.mlp, self.Dc, self.N, self.B_max, dev, self.sm_count)
+        self.plan_a = MLPPlan(self.actor.mlp, self.Da, self.N, self.rows_a_max, dev, self.sm_count)
+        self.plan_c = MLPPlan(self.critic.mlp, self.Dc, self.N, self.rows_c_max, dev, self.sm_count)
         self.head_cols = self.plan_a.head_cols
-        self.plan_a.refresh_shadows()
-        self.plan_c.refresh_shadows()
+        self.plans = [self.plan_a, self.plan_c]
+        if self.rnd is not None:
+            self.Dr = self.rnd.num_states
+            self.R = self.rnd.num_outputs
+            self.groups_r = list(self.rnd.obs_groups["rnd_state"])
+            self.plan_rp = MLPPlan(self.rnd.predictor, self.Dr, self.N, self.B_max, dev, self.sm_count)
+            self.plan_rt = MLPPlan(self.rnd.target, self.Dr, self.N, self.B_max, dev, self.sm_count, grads=False)
+            self.plans += [self.plan_rp, self.plan_rt]
+        for plan in self.plans:
+            plan.refresh_shadows()
 
         # ---- rollout arena ----
         T, N, A = self.T, self.N, self.A
-        self.obs_a = torch.zeros(T * N, self.Da, **f32)
-        self.obs_c = self.obs_a if self.shared_obs else torch.zeros(T * N, self.Dc, **f32)
+        # observation arenas: rows padded to 16 bytes so the minibatch gather reads them with 16-byte loads
+        self.obs_a = _padded_rows(T * N, self.Da, dev)
+        self.obs_c = self.obs_a if self.shared_obs else _padded_rows(T * N, self.Dc, dev)
         self.st_actions = torch.zeros(T * N, A, **f32)
         self.st_mean = torch.zeros(T * N, A, **f32)
         self.st_std = torch.zeros(T * N, A, **f32)
@@ -189,13 +288,33 @@ class PPOEngine(EngineBase):
         self.last_values = torch.zeros(N, **f32)
         self.gae_partial = torch.zeros(2 * ext().gae_blocks(N), dtype=torch.float64, device=dev)
         self.t = 0
+        self.intrinsic_for_logger = None
+        if self.rnd is not None:
+            if self.groups_r == self.groups_a:
+                self.obs_r = self.obs_a
+            elif self.groups_r == self.groups_c:
+                self.obs_r = self.obs_c
+            else:
+                self.obs_r = _padded_rows(T * N, self.Dr, dev)
+            self.intrinsic = torch.zeros(N, **f32)
+            self.intrinsic_for_logger = self.intrinsic
+            alg.intrinsic_rewards = self.intrinsic
+            self.rnd_w = torch.zeros(T, **f32)  # per-step intrinsic weight of the current rollout
+            self.rnd_tout_roll = torch.zeros(N, self.R, **f32)
+            self.rnd_pout_roll = torch.zeros(N, self.R, **f32)
+            self.rnd_tout_train = torch.zeros(self.B_max, self.R, **f32)
+            self.rnd_blocks = ext().mse_blocks(self.B_max)
+            self.rnd_loss_partial = torch.zeros(self.rnd_blocks, **f32)
+            self.rnd_colsum = torch.zeros(self.rnd_blocks, self.R, **f32)
+            self.rnd_loss_acc = torch.zeros(1, **f32)
+            self.rnd_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
 
         # ---- minibatch buffers ----
         B = self.B_max
         self.idx = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.value_train = torch.zeros(B, 1, **f32)
-        self.d_value = self.plan_c.d_head  # gradient of the scalar value head, [B, 8] bf16 (7 zero padding columns)
-        self.loss_blocks = ext().ppo_loss_blocks(B)
+        self.value_train = torch.zeros(self.rows_c_max, 1, **f32)
+        self.d_value = self.plan_c.d_head  # gradient of the scalar value head, [rows, 8] bf16 (7 zero padding columns)
+        self.loss_blocks = ext().ppo_loss_blocks(self.rows_a_max)
         self.stats_partial = torch.zeros(self.loss_blocks, _TAIL, **f32)
         self.dhead_colsum = torch.zeros(self.loss_blocks, self.head_cols, **f32)
         self.dvalue_colsum = torch.zeros(self.loss_blocks, 1, **f32)
@@ -206,6 +325,8 @@ class PPOEngine(EngineBase):
         seg = {}
         seg.update(self.plan_a.reduce_segments(self.dhead_colsum, self.loss_blocks))
         seg.update(self.plan_c.reduce_segments(self.dvalue_colsum, self.loss_blocks))
+        if self.rnd is not None:
+            seg.update(self.plan_rp.reduce_segments(self.rnd_colsum, self.rnd_blocks))
         if not self.hetero:
             std_p = dist.std_param if dist.std_type == "scalar" else dist.log_std_param
             seg[id(std_p)] = (self.dstd_partial, self.loss_blocks, A)
@@ -226,7 +347,9 @@ class PPOEngine(EngineBase):
 
         # ---- Adam plan ----
         shadows = {}
-        for plan in (self.plan_a, self.plan_c):
+        for plan in self.plans:
+            if not plan.train or not plan.grads:
+                continue
             for lin, wb in zip(plan.linears, plan.w_bf16):
                 shadows[id(lin.weight)] = wb
         t_off, t_num, t_grp, t_rows, t_cols, t_sh, t_ld = [], [], [], [], [], [], []
@@ -259,10 +382,27 @@ class PPOEngine(EngineBase):
         self.adam_eps = float(group0.get("eps", 1e-8))
         if float(group0.get("weight_decay", 0.0)) != 0.0 or group0.get("amsgrad", False):
             raise ValueError("fused Adam supports weight_decay=0 and amsgrad=False")
+        ng = 3 if self.rnd is not None else 2
+        self.adam_max_norm = [alg.max_grad_norm, alg.max_grad_norm] + [0.0] * (ng - 2)
+        self.adam_beta1 = [self.betas[0]] * 2
+        self.adam_beta2 = [self.betas[1]] * 2
+        self.adam_eps_g = [self.adam_eps] * 2
+        self.adam_lr_index = [0, 0]
+        if self.rnd is not None:
+            rg = self.rnd.optimizer.param_groups[0]
+            rb1, rb2 = rg.get("betas", (0.9, 0.999))
+            if float(rg.get("weight_decay", 0.0)) != 0.0 or rg.get("amsgrad", False):
+                raise ValueError("fused Adam supports weight_decay=0 and amsgrad=False")
+            self.adam_beta1.append(float(rb1))
+            self.adam_beta2.append(float(rb2))
+            self.adam_eps_g.append(float(rg.get("eps", 1e-8)))
+            self.adam_lr_index.append(2)
 
         # ---- normaliser statistics scratch ----
         self._alloc_norm_scratch("actor", self.total, self.Da)
         self._alloc_norm_scratch("critic", self.total, self.Dc)
+        if self.rnd is not None:
+            self._alloc_norm_scratch("rnd", self.total, self.Dr)
         self.use_graphs = bool(alg.b200_cfg["graphs"])
         self._update_graph = None
         self._updates_done = 0
@@ -290,12 +430,19 @@ class PPOEngine(EngineBase):
         N, t = self.N, self.t
         rows = slice(t * N, (t + 1) * N)
         C = ext()
+        if self.rnd is not None and t == 0 and not torch.cuda.is_current_stream_capturing():
+            self._rnd_prepare()
+        if self.rnd is not None and self.obs_r is not self.obs_a and self.obs_r is not self.obs_c:
+            # the RND state groups are stored on their own (normalised copy goes to a scratch buffer)
+            C.prep_obs(self._group_tensors(obs, self.groups_r), self.obs_r[rows], self.obs_r.stride(0),
+                       self.plan_rp.x_roll,
+                       self.plan_rp.x_roll.shape[1], None, None, 0.0)
         mean_a, std_a, eps_a = self._norm_tensors(self.actor)
-        C.prep_obs(self._group_tensors(obs, self.groups_a), self.obs_a[rows], self.Da, self.plan_a.x_roll,
+        C.prep_obs(self._group_tensors(obs, self.groups_a), self.obs_a[rows], self.obs_a.stride(0), self.plan_a.x_roll,
                    self.plan_a.x_roll.shape[1], mean_a, std_a, eps_a)
         mean_c, std_c, eps_c = self._norm_tensors(self.critic)
         store_c = None if self.shared_obs else self.obs_c[rows]
-        C.prep_obs(self._group_tensors(obs, self.groups_c), store_c, self.Dc, self.plan_c.x_roll,
+        C.prep_obs(self._group_tensors(obs, self.groups_c), store_c, self.obs_c.stride(0), self.plan_c.x_roll,
                    self.plan_c.x_roll.shape[1], mean_c, std_c, eps_c)
         pa = self.plan_a
         pa.forward(pa.x_roll, pa.h_roll, N, pa.out_roll, pa.out_roll.shape[1], self.status)
@@ -316,9 +463,40 @@ class PPOEngine(EngineBase):
         timeouts = extras.get("time_outs") if isinstance(extras, dict) else None
         if timeouts is not None:
             timeouts = timeouts.to(self.device).reshape(-1)
-        ext().process_step(rewards.reshape(-1).float(), None, dones.reshape(-1), timeouts, self.st_values[rows],
+        intrinsic = None
+        if self.rnd is not None:
+            self._rnd_intrinsic(obs, t)
+            intrinsic = self.intrinsic
+        ext().process_step(rewards.reshape(-1).float(), intrinsic, dones.reshape(-1), timeouts, self.st_values[rows],
                            self.alg.gamma, self.st_rewards[rows], self.st_dones[rows], self.nonfinite)
         self.t += 1
+
+    # ---- RND -----------------------------------------------------------------------------------------------------------
+    def _rnd_prepare(self) -> None:
+        """Advance the host-side RND step counter by one rollout and upload the per-step intrinsic weights."""
+        r = self.rnd
+        weights = []
+        for _ in range(self.T):
+            r.update_counter += 1
+            r.weight = r.current_weight(r.update_counter)
+            weights.append(float(r.weight))
+        self.rnd_w.copy_(torch.tensor(weights, dtype=torch.float32))
+
+    def _before_replay(self) -> None:
+        if self.rnd is not None:
+            self._rnd_prepare()
+
+    def _rnd_intrinsic(self, obs, t: int) -> None:
+        """Intrinsic reward of the post-step observations: weight * || target(s) - predictor(s) ||."""
+        C = ext()
+        pr, pt = self.plan_rp, self.plan_rt
+        mean_r, std_r, eps_r = self._norm_views(self.rnd.state_normalizer)
+        C.prep_obs(self._group_tensors(obs, self.groups_r), None, self.Dr, pr.x_roll, pr.x_roll.shape[1], mean_r,
+                   std_r, eps_r)
+        pt.forward(pr.x_roll, pt.h_roll, self.N, self.rnd_tout_roll, self.R, self.status)
+        pr.forward(pr.x_roll, pr.h_roll, self.N, self.rnd_pout_roll, self.R, self.status)
+        C.rnd_intrinsic(self.rnd_tout_roll, self.R, self.rnd_pout_roll, self.R, self.N, self.R,
+                        self.rnd_w[t : t + 1], self.intrinsic)
 
     def compute_returns(self, obs) -> None:
         C = ext()
@@ -334,22 +512,55 @@ class PPOEngine(EngineBase):
         self.t = 0
 
     # ---- update -------------------------------------------------------------------------------------------------------
+    def _zero_partial_tails(self, B: int) -> None:
+        """A minibatch shorter than the largest one launches fewer loss blocks: clear the unused partial rows."""
+        C = ext()
+        used = C.ppo_loss_blocks(self.K * B)
+        if used < self.loss_blocks:
+            for buf in (self.stats_partial, self.dhead_colsum, self.dvalue_colsum, self.dstd_partial):
+                buf[used:].zero_()
+        if self.rnd is not None:
+            used = C.mse_blocks(B)
+            if used < self.rnd_blocks:
+                self.rnd_loss_partial[used:].zero_()
+                self.rnd_colsum[used:].zero_()
+
     def _minibatch(self, i: int) -> None:
         C = ext()
         start = i * self.total // self.M
         B = (i + 1) * self.total // self.M - start
+        if B < self.B_max:
+            self._zero_partial_tails(B)
+        rows_a = self.K * B
+        rows_c = rows_a if self.aug else B
         pa, pc = self.plan_a, self.plan_c
         mean_a, std_a, eps_a = self._norm_tensors(self.actor)
         mean_c, std_c, eps_c = self._norm_tensors(self.critic)
-        if eps_a != eps_c and mean_a is not None and mean_c is not None:
-            raise ValueError("actor and critic normalisers must share eps")
-        eps = eps_a if mean_a is not None else eps_c
+        eps_all = {e for m, e in ((mean_a, eps_a), (mean_c, eps_c)) if m is not None}
+        obs_l, mean_l, std_l = [self.obs_a, self.obs_c], [mean_a, mean_c], [std_a, std_c]
+        x_l, ld_l, rows_l = [pa.x_train, pc.x_train], [pa.x_train.shape[1], pc.x_train.shape[1]], [rows_a, rows_c]
+        perm_l = [self.perm_a, self.perm_c if self.aug else None]
+        sign_l = [self.sign_a, self.sign_c if self.aug else None]
+        if self.rnd is not None:
+            mean_r, std_r, eps_r = self._norm_views(self.rnd.state_normalizer)
+            if mean_r is not None:
+                eps_all.add(eps_r)
+            obs_l.append(self.obs_r)
+            mean_l.append(mean_r)
+            std_l.append(std_r)
+            x_l.append(self.plan_rp.x_train)
+            ld_l.append(self.plan_rp.x_train.shape[1])
+            rows_l.append(B)
+            perm_l.append(None)
+            sign_l.append(None)
+        if len(eps_all) > 1:
+            raise ValueError("all fused observation normalisers must share eps")
+        eps = eps_all.pop() if eps_all else 0.0
         idx_in = None if self.perm_override is None else self.perm_override[start : start + B]
-        C.gather_minibatch(B, start, self.total, self.perm_key, self.half_bits, idx_in, self.idx,
-                           [self.obs_a, self.obs_c], [mean_a, mean_c], [std_a, std_c], eps,
-                           [pa.x_train, pc.x_train], [pa.x_train.shape[1], pc.x_train.shape[1]], self.status)
-        pa.forward(pa.x_train, pa.h_train, B, pa.out_train, pa.out_train.shape[1], self.status)
-        pc.forward(pc.x_train, pc.h_train, B, self.value_train, 1, self.status)
+        C.gather_minibatch(B, start, self.total, self.perm_key, self.half_bits, idx_in, self.idx, obs_l, mean_l, std_l,
+                           eps, x_l, ld_l, self.status, self.K, rows_l, perm_l, sign_l)
+        pa.forward(pa.x_train, pa.h_train, rows_a, pa.out_train, pa.out_train.shape[1], self.status)
+        pc.forward(pc.x_train, pc.h_train, rows_c, self.value_train, 1, self.status)
         dist = self.actor.distribution
         std_param = None if self.hetero else (dist.std_param if dist.std_type == "scalar" else dist.log_std_param)
         alg = self.alg
@@ -359,9 +570,18 @@ class PPOEngine(EngineBase):
                    self.st_logp, self.st_adv, self.st_returns, self.st_values, None, alg.clip_param,
                    alg.value_loss_coef, alg.entropy_coef, alg.use_clipped_value_loss, pa.d_head, pa.d_head.shape[1],
                    self.d_value, self.d_value.shape[1], self.stats_partial, self.dhead_colsum, self.dvalue_colsum,
-                   None if self.hetero else self.dstd_partial)
-        pa.backward(B, self.status)
-        pc.backward(B, self.status)
+                   None if self.hetero else self.dstd_partial, self.K, self.aug, self.act_perm, self.act_sign,
+                   self.mirror_coef)
+        pa.backward(rows_a, self.status)
+        pc.backward(rows_c, self.status)
+        if self.rnd is not None:
+            pr, pt = self.plan_rp, self.plan_rt
+            pt.forward(pr.x_train, pt.h_train, B, self.rnd_tout_train, self.R, self.status)
+            pr.forward(pr.x_train, pr.h_train, B, pr.out_train, self.R, self.status)
+            C.mse_grad(pr.out_train, self.R, self.rnd_tout_train, self.R, B, self.R, False, pr.d_head,
+                       pr.d_head.shape[1], self.R, self.rnd_loss_partial, self.rnd_colsum, self.rnd_loss_acc,
+                       self.rnd_ticket)
+            pr.backward(B, self.status)
         C.reduce_segments(self.reduce_plan, self.reduce_nseg, self.reduce_chunks, self.send[0], self.send[1],
                           self.epoch, False)
         adaptive = alg.desired_kl is not None and alg.schedule == "adaptive"
@@ -369,9 +589,8 @@ class PPOEngine(EngineBase):
         peers = self.comm.peer_send if self.comm is not None else None
         flags = self.comm.peer_flags if self.comm is not None else None
         C.adam_step(self.flat, self.send[0], self.send[1], self.grads, self.exp_avg, self.exp_avg_sq,
-                    self.adam_tensors, self.adam_chunks, self.adam_nchunks,
-                    [alg.max_grad_norm, alg.max_grad_norm], [self.betas[0]] * 2, [self.betas[1]] * 2,
-                    [self.adam_eps] * 2, [0, 0], self.lr, None, self.step, adaptive, kl,
+                    self.adam_tensors, self.adam_chunks, self.adam_nchunks, self.adam_max_norm, self.adam_beta1,
+                    self.adam_beta2, self.adam_eps_g, self.adam_lr_index, self.lr, None, self.step, adaptive, kl,
                     float(alg.desired_kl or 0.0), 1e-5, 1e-2, self.world, self.rank, peers, flags, self.epoch,
                     self.timeout_ns, self.norm_partial, self.barrier, self.status, self.out_norms, self.adam_grid,
                     self.group_ranges, self.n_ex)
@@ -380,10 +599,15 @@ class PPOEngine(EngineBase):
     def _normalizer_updates(self) -> None:
         self._normalizer_update("actor", self.actor, self.obs_a, self.total, self.Da)
         self._normalizer_update("critic", self.critic, self.obs_c, self.total, self.Dc)
+        if self.rnd is not None:
+            self._norm_module_update("rnd", self.rnd.state_normalizer, self.rnd.state_normalization, self.obs_r,
+                                     self.total, self.Dr)
 
     def _update_body(self) -> None:
         ext().counter_add(self.perm_key, 1)
         self.loss_acc.zero_()
+        if self.rnd is not None:
+            self.rnd_loss_acc.zero_()
         for _ in range(self.E):
             for i in range(self.M):
                 self._minibatch(i)
@@ -397,9 +621,15 @@ class PPOEngine(EngineBase):
         else:
             self._update_body()
         self._updates_done += 1
-        stats = (self.loss_acc / float(self.E * self.M)).tolist()
+        n = float(self.E * self.M)
+        stats = (self.loss_acc / n).tolist()
         self._check_status()
-        return {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
+        out = {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
+        if self.rnd is not None:
+            out["rnd"] = float(self.rnd_loss_acc.item()) / n
+        if self.sym is not None:
+            out["symmetry"] = stats[4]
+        return out
 
     # ---- rollout import (tests / external collectors) -------------------------------------------------------------------
     def load_rollout(self, storage) -> None:
@@ -421,56 +651,70 @@ class PPOEngine(EngineBase):
         self.st_adv.copy_(storage.advantages.reshape(-1))
 
     # ---- checkpoints --------------------------------------------------------------------------------------------------
+    def _optimizer_of(self, g: int):
+        return self.rnd.optimizer if g == _GROUP_RND else self.alg.optimizer
+
     def sync_to_torch(self) -> None:
-        """Expose the device optimizer state through the ``torch.optim.Adam`` object (parameters are already views)."""
-        opt = self.alg.optimizer
+        """Expose the device optimizer state through the ``torch.optim.Adam`` objects (parameters are already views)."""
         steps = self.step.tolist()
         for p, o, g in zip(self.params, self.offsets, self.param_group):
             n = p.numel()
-            opt.state[p] = {
+            if steps[g] == 0:
+                continue
+            self._optimizer_of(g).state[p] = {
                 "step": torch.tensor(float(steps[g])),
                 "exp_avg": self.exp_avg[o : o + n].view_as(p),
                 "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p),
             }
-        lr = self.learning_rate()
-        for group in opt.param_groups:
-            group["lr"] = lr
-        self.alg._learning_rate = lr
+        lrs = self.lr.tolist()
+        for group in self.alg.optimizer.param_groups:
+            group["lr"] = lrs[0]
+        self.alg._learning_rate = lrs[0]
+        if self.rnd is not None:
+            for group in self.rnd.optimizer.param_groups:
+                group["lr"] = lrs[2]
 
     def sync_from_torch(self) -> None:
         """Pull loaded weights / optimizer state into the device arena and refresh the bf16 shadows."""
-        opt = self.alg.optimizer
-        for p, o in zip(self.params, self.offsets):
+        for p, o, g in zip(self.params, self.offsets, self.param_group):
             n = p.numel()
             if p.data.data_ptr() != self.flat[o : o + n].data_ptr():
                 self.flat[o : o + n].copy_(p.data.reshape(-1))
                 p.data = self.flat[o : o + n].view_as(p)
+            opt = self._optimizer_of(g)
             st = opt.state.get(p)
             if st:
                 self.exp_avg[o : o + n].copy_(st["exp_avg"].reshape(-1))
                 self.exp_avg_sq[o : o + n].copy_(st["exp_avg_sq"].reshape(-1))
-                self.step.fill_(int(float(st["step"])))
+                self.step[g] = int(float(st["step"]))
                 opt.state[p] = {"step": st["step"], "exp_avg": self.exp_avg[o : o + n].view_as(p),
                                 "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p)}
-        self.lr.fill_(float(opt.param_groups[0]["lr"]))
-        self.plan_a.refresh_shadows()
-        self.plan_c.refresh_shadows()
+        self.lr[0:2].fill_(float(self.alg.optimizer.param_groups[0]["lr"]))
+        if self.rnd is not None:
+            self.lr[2] = float(self.rnd.optimizer.param_groups[0]["lr"])
+        for plan in self.plans:
+            plan.refresh_shadows()
 
     # ---- data parallel ------------------------------------------------------------------------------------------------
     def broadcast_parameters(self) -> None:
         """Make every rank start from rank 0's parameters and normaliser buffers."""
+        extra = [] if self.rnd is None else [self.rnd.target, self.rnd.state_normalizer, self.rnd.reward_normalizer]
         if self.comm is not None:
             self.comm.broadcast_(self.flat, status=self.status)
-            for model in (self.actor, self.critic):
+            for model in [self.actor, self.critic] + ([self.rnd.predictor] if self.rnd is not None else []):
                 for b in model.buffers():
                     self.comm.broadcast_(b, status=self.status)
+            for m in extra:
+                for t in m.state_dict().values():
+                    self.comm.broadcast_(t, status=self.status)
             self._check_status()
         else:
-            for model in (self.actor, self.critic):
+            models = [self.actor, self.critic] + ([self.rnd] if self.rnd is not None else [])
+            for model in models:
                 for t in model.state_dict().values():
                     torch.distributed.broadcast(t, src=0)
-        self.plan_a.refresh_shadows()
-        self.plan_c.refresh_shadows()
+        for plan in self.plans:
+            plan.refresh_shadows()
 
 
 __all__ = ["PPOEngine"]

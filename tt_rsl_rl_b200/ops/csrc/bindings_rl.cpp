@@ -29,6 +29,11 @@ T* P(const Tensor& t) {
 void check_f32(const Tensor& t, const char* n) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32, n, " must be a CUDA float32 tensor");
 }
+// Elements addressable from t's first element to the end of its storage (row-padded views may address past numel()).
+int64_t avail(const Tensor& t) {
+  return static_cast<int64_t>(t.storage().nbytes() / t.element_size()) - t.storage_offset();
+}
+
 void check_bf16(const Tensor& t, const char* n) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16, n, " must be a CUDA bfloat16 tensor");
 }
@@ -60,7 +65,7 @@ void prep_obs(const std::vector<Tensor>& srcs, const OptT& store, int64_t ld_sto
   }
   TORCH_CHECK(ld_x >= D && x.numel() >= (a.rows - 1) * ld_x + D, "prep_obs: x too small");
   a.store = P<float>(store);
-  if (a.store) TORCH_CHECK(ld_store >= D && store->numel() >= (a.rows - 1) * ld_store + D, "prep_obs: store too small");
+  if (a.store) TORCH_CHECK(ld_store >= D && avail(*store) >= (a.rows - 1) * ld_store + D, "prep_obs: store too small");
   a.ld_store = static_cast<int>(ld_store);
   a.x = x.data_ptr();
   a.ld_x = static_cast<int>(ld_x);
@@ -159,10 +164,15 @@ int64_t feistel_permute(int64_t i, int64_t n, int64_t half_bits, int64_t key) {
 void gather_minibatch(int64_t B, int64_t offset, int64_t total, const OptT& key, int64_t half_bits, const OptT& idx_in,
                       const Tensor& idx_out, const std::vector<Tensor>& obs, const std::vector<OptT>& means,
                       const std::vector<OptT>& stds, double eps, const std::vector<Tensor>& xs,
-                      const std::vector<int64_t>& ld_xs, const OptT& status) {
-  TORCH_CHECK(obs.size() >= 1 && obs.size() <= 2 && xs.size() == obs.size() && ld_xs.size() == obs.size() &&
-                  means.size() == obs.size() && stds.size() == obs.size(),
-              "gather_minibatch: 1 or 2 models");
+                      const std::vector<int64_t>& ld_xs, const OptT& status, int64_t copies,
+                      const std::vector<int64_t>& rows, const std::vector<OptT>& perms,
+                      const std::vector<OptT>& signs) {
+  const size_t nm = obs.size();
+  TORCH_CHECK(nm >= 1 && nm <= static_cast<size_t>(rlb::kGatherModels) && xs.size() == nm && ld_xs.size() == nm &&
+                  means.size() == nm && stds.size() == nm && rows.size() == nm && perms.size() == nm &&
+                  signs.size() == nm,
+              "gather_minibatch: 1 to 3 models with one entry per model in every list");
+  TORCH_CHECK(copies >= 1, "gather_minibatch: copies >= 1");
   TORCH_CHECK(idx_out.scalar_type() == torch::kInt32 && idx_out.numel() >= B, "gather_minibatch: idx_out");
   TORCH_CHECK(total < (1ll << 31), "gather_minibatch: rollout too large");
   rlb::GatherArgs a{};
@@ -173,19 +183,42 @@ void gather_minibatch(int64_t B, int64_t offset, int64_t total, const OptT& key,
   a.half_bits = static_cast<int>(half_bits);
   a.idx_in = P<const int>(idx_in);
   a.idx_out = P<int>(idx_out);
-  a.models = static_cast<int>(obs.size());
-  for (size_t m = 0; m < obs.size(); ++m) {
+  a.copies = static_cast<int>(copies);
+  a.models = static_cast<int>(nm);
+  for (size_t m = 0; m < nm; ++m) {
     check_f32(obs[m], "obs");
     check_bf16(xs[m], "x");
     TORCH_CHECK(obs[m].dim() == 2 && obs[m].size(0) >= total, "gather_minibatch: obs must be [rows, dim]");
     a.obs[m] = P<const float>(obs[m]);
     a.obs_ld[m] = static_cast<int>(obs[m].stride(0));
     a.dim[m] = static_cast<int>(obs[m].size(1));
+    a.rows[m] = static_cast<int>(rows[m]);
+    TORCH_CHECK(rows[m] >= 1 && rows[m] <= copies * B, "gather_minibatch: rows per model in [1, copies * B]");
     a.mean[m] = P<const float>(means[m]);
     a.std[m] = P<const float>(stds[m]);
     a.x[m] = xs[m].data_ptr();
     a.ld_x[m] = static_cast<int>(ld_xs[m]);
-    TORCH_CHECK(xs[m].numel() >= (B - 1) * ld_xs[m] + a.dim[m], "gather_minibatch: x too small");
+    // bf16 rows are written in 4-column (8-byte) groups up to the next multiple of 4 columns
+    TORCH_CHECK(ld_xs[m] % 4 == 0 && ld_xs[m] >= (a.dim[m] + 3) / 4 * 4 &&
+                    (reinterpret_cast<uintptr_t>(xs[m].data_ptr()) % 8) == 0,
+                "gather_minibatch: x pitch must be a multiple of 4 covering dim rounded up to 4, 8-byte aligned");
+    TORCH_CHECK(xs[m].numel() >= (rows[m] - 1) * ld_xs[m] + (a.dim[m] + 3) / 4 * 4, "gather_minibatch: x too small");
+    TORCH_CHECK(obs[m].stride(1) == 1, "gather_minibatch: obs rows must be contiguous");
+    // 16-byte loads read whole 4-column groups: the last group of the last row must lie inside the storage
+    a.vec4[m] = (a.obs_ld[m] % 4 == 0 && (reinterpret_cast<uintptr_t>(obs[m].data_ptr()) % 16) == 0 &&
+                 avail(obs[m]) >= (total - 1) * a.obs_ld[m] + (a.dim[m] + 3) / 4 * 4)
+                    ? 1
+                    : 0;
+    if (perms[m].has_value()) {
+      TORCH_CHECK(signs[m].has_value(), "gather_minibatch: perm without sign");
+      TORCH_CHECK(perms[m]->scalar_type() == torch::kInt32 && perms[m]->numel() >= copies * a.dim[m] &&
+                      perms[m]->is_contiguous(),
+                  "gather_minibatch: perm must be int32 [copies, dim]");
+      check_f32(*signs[m], "sign");
+      TORCH_CHECK(signs[m]->numel() >= copies * a.dim[m], "gather_minibatch: sign must be [copies, dim]");
+      a.perm[m] = P<const int>(perms[m]);
+      a.sign[m] = P<const float>(signs[m]);
+    }
   }
   a.eps = static_cast<float>(eps);
   a.status = P<unsigned int>(status);
@@ -201,22 +234,39 @@ void ppo_loss(int64_t B, int64_t A, bool hetero, bool log_std, const Tensor& hea
               const OptT& adv_override, double clip, double value_coef, double entropy_coef, bool clipped_value,
               const Tensor& d_head, int64_t ld_dhead, const Tensor& d_value, int64_t ld_dvalue,
               const Tensor& stats_partial, const Tensor& dhead_colsum, const Tensor& dvalue_colsum,
-              const OptT& dstd_partial) {
+              const OptT& dstd_partial, int64_t copies, bool aug, const OptT& act_perm, const OptT& act_sign,
+              double mirror_coef) {
+  // B: original samples of the minibatch; the actor rows are copies * B (symmetry copies after the originals)
   check_f32(head, "head");
   check_f32(value, "value");
   check_bf16(d_head, "d_head");
   check_bf16(d_value, "d_value");
+  TORCH_CHECK(copies >= 1, "ppo_loss: copies >= 1");
+  const int64_t rows = copies * B;
+  const int64_t value_rows = aug ? rows : B;
   TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.numel() >= B, "ppo_loss: idx");
-  const int64_t blocks = rlb::ppo_loss_blocks(static_cast<int>(B));
+  const int64_t blocks = rlb::ppo_loss_blocks(static_cast<int>(rows));
   const int64_t head_cols = hetero ? 2 * A : A;
-  TORCH_CHECK(ld_dhead >= head_cols && d_head.numel() >= B * ld_dhead, "ppo_loss: d_head too small");
-  TORCH_CHECK(d_value.numel() >= B * ld_dvalue, "ppo_loss: d_value too small");
-  TORCH_CHECK(stats_partial.numel() >= blocks * 4 && dhead_colsum.numel() >= blocks * head_cols &&
+  TORCH_CHECK(ld_dhead >= head_cols && d_head.numel() >= rows * ld_dhead, "ppo_loss: d_head too small");
+  TORCH_CHECK(head.numel() >= (rows - 1) * ld_head + head_cols, "ppo_loss: head too small");
+  TORCH_CHECK(d_value.numel() >= value_rows * ld_dvalue && value.numel() >= (value_rows - 1) * ld_value + 1,
+              "ppo_loss: value / d_value too small");
+  TORCH_CHECK(stats_partial.numel() >= blocks * rlb::kLossStats && dhead_colsum.numel() >= blocks * head_cols &&
                   dvalue_colsum.numel() >= blocks,
               "ppo_loss: partial buffers too small");
   TORCH_CHECK(hetero || (std_param.has_value() && dstd_partial.has_value()), "ppo_loss: std_param/dstd_partial");
+  TORCH_CHECK(copies == 1 || (act_perm.has_value() && act_sign.has_value() &&
+                              act_perm->scalar_type() == torch::kInt32 && act_perm->numel() >= copies * A &&
+                              act_sign->numel() >= copies * A),
+              "ppo_loss: symmetry copies need int32 act_perm and act_sign [copies, A]");
   rlb::PpoLossArgs a{};
-  a.B = static_cast<int>(B);
+  a.B = static_cast<int>(rows);
+  a.n0 = static_cast<int>(B);
+  a.copies = static_cast<int>(copies);
+  a.aug = aug ? 1 : 0;
+  a.act_perm = copies > 1 ? P<const int>(act_perm) : nullptr;
+  a.act_sign = copies > 1 ? P<const float>(act_sign) : nullptr;
+  a.mirror_coef = static_cast<float>(mirror_coef);
   a.A = static_cast<int>(A);
   a.hetero = hetero;
   a.log_std = log_std;
@@ -288,6 +338,21 @@ void reduce_segments(const Tensor& plan, int64_t nseg, int64_t chunks, const Ten
                           static_cast<int>(chunks), P<float>(send0), P<float>(send1), P<const unsigned int>(epoch),
                           accumulate ? 1 : 0, cur()),
      "reduce_segments");
+}
+
+void rnd_intrinsic(const Tensor& target, int64_t ld_target, const Tensor& pred, int64_t ld_pred, int64_t rows,
+                   int64_t dim, const Tensor& weight, const Tensor& out) {
+  check_f32(target, "target");
+  check_f32(pred, "pred");
+  check_f32(weight, "weight");
+  check_f32(out, "out");
+  TORCH_CHECK(dim <= 64 && out.numel() >= rows && target.numel() >= (rows - 1) * ld_target + dim &&
+                  pred.numel() >= (rows - 1) * ld_pred + dim,
+              "rnd_intrinsic: sizes");
+  ok(rlb::rnd_intrinsic(P<const float>(target), static_cast<int>(ld_target), P<const float>(pred),
+                        static_cast<int>(ld_pred), static_cast<int>(rows), static_cast<int>(dim), P<const float>(weight),
+                        P<float>(out), cur()),
+     "rnd_intrinsic");
 }
 
 int64_t mse_blocks(int64_t rows) { return rlb::mse_blocks(static_cast<int>(rows)); }
@@ -454,7 +519,7 @@ void colstats(const Tensor& x, int64_t rows, int64_t ld, int64_t dim, const Tens
   check_f32(x, "x");
   const int chunks = rlb::colstats_chunks(rows);
   TORCH_CHECK(partial.scalar_type() == torch::kFloat64 && partial.numel() >= 2LL * chunks * dim, "colstats: partial");
-  TORCH_CHECK(x.numel() >= (rows - 1) * ld + dim, "colstats: x too small");
+  TORCH_CHECK(avail(x) >= (rows - 1) * ld + dim, "colstats: x too small");
   rlb::ColStatsArgs a{P<const float>(x), rows, static_cast<int>(ld), static_cast<int>(dim), P<double>(partial), chunks};
   ok(rlb::colstats(a, cur()), "colstats");
 }
@@ -507,6 +572,7 @@ void rlb_register_kernels(pybind11::module& m) {
   m.def("reduce_segments", &reduce_segments);
   m.def("mse_blocks", &mse_blocks);
   m.def("mse_grad", &mse_grad);
+  m.def("rnd_intrinsic", &rnd_intrinsic);
   m.def("make_adam_plan", &make_adam_plan);
   m.def("adam_grid", &adam_grid);
   m.def("adam_step", &adam_step);

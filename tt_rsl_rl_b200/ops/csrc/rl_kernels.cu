@@ -282,54 +282,99 @@ __host__ __device__ __forceinline__ uint32_t feistel_permute(uint32_t i, uint32_
 }
 
 constexpr int kGatherMaxD = 1024;
-constexpr int kGatherRows = 4;  // rows per warp iteration (their loads are issued together)
-// One warp gathers kGatherRows rows at a time: lanes 0..R-1 compute the permuted source rows, then every lane loads
-// its columns of all R rows before converting and storing, so each warp keeps several row loads in flight.
-__global__ void __launch_bounds__(256) gather_minibatch_kernel(const GatherArgs a) {
-  __shared__ float s_mean[2][kGatherMaxD];
-  __shared__ float s_inv[2][kGatherMaxD];
-  for (int m = 0; m < a.models; ++m)
-    for (int c = threadIdx.x; c < a.dim[m]; c += blockDim.x) {
-      s_mean[m][c] = a.mean[m] ? a.mean[m][c] : 0.f;
-      s_inv[m][c] = a.mean[m] ? 1.0f / (a.std[m][c] + a.eps) : 1.f;
+constexpr int kGatherRows = 8;  // rows per warp iteration (their loads are issued together)
+// One warp gathers kGatherRows rows at a time: lanes 0..R-1 compute the permuted source rows (and symmetry copies),
+// then lane l handles columns [4l, 4l + 4) of every row of the batch (128 columns per pass): a 16-byte load per row
+// when the source row pitch allows it (identity copies), else four scalar loads through the copy's column map. All
+// R rows' loads are issued before any conversion, so each warp keeps R 16-byte loads in flight.
+__global__ void __launch_bounds__(256, 3) gather_minibatch_kernel(const GatherArgs a) {
+  __shared__ __align__(16) float s_mean[kGatherModels][kGatherMaxD];
+  __shared__ __align__(16) float s_inv[kGatherModels][kGatherMaxD];
+  int max_rows = 0;
+  for (int m = 0; m < a.models; ++m) {
+    max_rows = max(max_rows, a.rows[m]);
+    for (int c = threadIdx.x; c < kGatherMaxD; c += blockDim.x) {
+      const bool in = c < a.dim[m];
+      s_mean[m][c] = (in && a.mean[m]) ? a.mean[m][c] : 0.f;
+      s_inv[m][c] = (in && a.mean[m]) ? 1.0f / (a.std[m][c] + a.eps) : 1.f;
     }
+  }
   __syncthreads();
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t key = a.key_ptr ? *a.key_ptr : 0u;
-  for (int i0 = (blockIdx.x * warps + (threadIdx.x >> 5)) * kGatherRows; i0 < a.B;
+  for (int i0 = (blockIdx.x * warps + (threadIdx.x >> 5)) * kGatherRows; i0 < max_rows;
        i0 += gridDim.x * warps * kGatherRows) {
-    int my_src = 0;
-    if (lane < kGatherRows && i0 + lane < a.B) {
+    // row i is copy i / B of original sample i % B (computed once per row by lanes 0..R-1)
+    int my_src = 0, my_copy = 0;
+    if (lane < kGatherRows && i0 + lane < max_rows) {
       const int i = i0 + lane;
+      my_copy = a.copies > 1 ? i / a.B : 0;
+      const int o = i - my_copy * a.B;
       if (a.idx_in) {
-        my_src = a.idx_in[i];
+        my_src = a.idx_in[o];
       } else {
         bool overflow = false;
-        my_src = static_cast<int>(feistel_permute(static_cast<uint32_t>(a.offset + i), static_cast<uint32_t>(a.total),
+        my_src = static_cast<int>(feistel_permute(static_cast<uint32_t>(a.offset + o), static_cast<uint32_t>(a.total),
                                                   a.half_bits, key, &overflow));
         if (overflow) report_error(a.status, kBadShape, 40);
       }
-      if (a.idx_out) a.idx_out[i] = my_src;
+      if (a.idx_out && i < a.B) a.idx_out[i] = my_src;
     }
-    int src[kGatherRows];
+    int src[kGatherRows], cp[kGatherRows];
 #pragma unroll
-    for (int r = 0; r < kGatherRows; ++r) src[r] = __shfl_sync(0xffffffffu, my_src, r);
+    for (int r = 0; r < kGatherRows; ++r) {
+      src[r] = __shfl_sync(0xffffffffu, my_src, r);
+      cp[r] = __shfl_sync(0xffffffffu, my_copy, r);
+    }
     for (int m = 0; m < a.models; ++m) {
       const int D = a.dim[m];
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        const int c = c0 + lane;
-        float v[kGatherRows];
+      const int rows_m = a.rows[m];
+      if (i0 >= rows_m) continue;
+      const int* perm = a.perm[m];
+      const float* sign = a.sign[m];
+      const float* obs = a.obs[m];
+      const int ld = a.obs_ld[m];
+      const bool vec = a.vec4[m] != 0;
+      for (int c = 4 * lane; c < D; c += 128) {
+        float4 v[kGatherRows];
 #pragma unroll
-        for (int r = 0; r < kGatherRows; ++r)
-          v[r] = (c < D && i0 + r < a.B) ? __ldg(a.obs[m] + static_cast<size_t>(src[r]) * a.obs_ld[m] + c) : 0.f;
-        if (c < D) {
-          const float mu = s_mean[m][c], inv = s_inv[m][c];
+        for (int r = 0; r < kGatherRows; ++r) {
+          v[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (i0 + r < rows_m) {
+            const float* row = obs + static_cast<size_t>(src[r]) * ld;
+            if (perm != nullptr && cp[r] > 0) {  // mirrored copy: signed column permutation of the raw observation
+              const int* pc = perm + cp[r] * D + c;
+              const float* sc = sign + cp[r] * D + c;
+              v[r].x = __ldg(sc) * __ldg(row + __ldg(pc));
+              if (c + 1 < D) v[r].y = __ldg(sc + 1) * __ldg(row + __ldg(pc + 1));
+              if (c + 2 < D) v[r].z = __ldg(sc + 2) * __ldg(row + __ldg(pc + 2));
+              if (c + 3 < D) v[r].w = __ldg(sc + 3) * __ldg(row + __ldg(pc + 3));
+            } else if (vec) {  // the row pitch is a multiple of 4 floats: columns past D are in-row padding
+              v[r] = __ldg(reinterpret_cast<const float4*>(row + c));
+            } else {
+              v[r].x = __ldg(row + c);
+              if (c + 1 < D) v[r].y = __ldg(row + c + 1);
+              if (c + 2 < D) v[r].z = __ldg(row + c + 2);
+              if (c + 3 < D) v[r].w = __ldg(row + c + 3);
+            }
+          }
+        }
+        const float4 mu = *reinterpret_cast<const float4*>(&s_mean[m][c]);
+        float4 inv = *reinterpret_cast<const float4*>(&s_inv[m][c]);
+        // columns at or past D are written as zeros (the padding of the bf16 row)
+        if (c + 1 >= D) inv.y = 0.f;
+        if (c + 2 >= D) inv.z = 0.f;
+        if (c + 3 >= D) inv.w = 0.f;
 #pragma unroll
-          for (int r = 0; r < kGatherRows; ++r)
-            if (i0 + r < a.B)
-              static_cast<__nv_bfloat16*>(a.x[m])[static_cast<size_t>(i0 + r) * a.ld_x[m] + c] =
-                  __float2bfloat16_rn((v[r] - mu) * inv);
+        for (int r = 0; r < kGatherRows; ++r) {
+          if (i0 + r < rows_m) {
+            uint2 w;
+            w.x = pack_bf16x2((v[r].x - mu.x) * inv.x, (v[r].y - mu.y) * inv.y);
+            w.y = pack_bf16x2((v[r].z - mu.z) * inv.z, (v[r].w - mu.w) * inv.w);
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.x[m]) + static_cast<size_t>(i0 + r) * a.ld_x[m] +
+                                      c) = w;
+          }
         }
       }
     }
@@ -350,44 +395,65 @@ __device__ __forceinline__ void max_grad_split(float a, float b, float& ga, floa
   gb = b > a ? 1.f : (a == b ? 0.5f : 0.f);
 }
 
-__global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLossArgs a) {
+// Row i of the minibatch is symmetry copy i / n0 of original sample i % n0 (copy 0: the sample itself). Terms:
+//   surrogate and value: rows of every copy with data augmentation (mean over B), else copy 0 (mean over n0);
+//   entropy and KL: copy 0 only (mean over n0), as upstream evaluates them on the original samples;
+//   mirror loss: copies >= 1, MSE between the row's mean and the mirrored mean of its original (target detached).
+// kSym = false compiles the plain path (one copy) without the symmetry branches and their registers.
+template <bool kSym>
+__global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoLossArgs a) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const float invB = 1.0f / static_cast<float>(a.B);
+  const float invP = 1.0f / static_cast<float>(a.aug ? a.B : a.n0);
+  const float invE = 1.0f / static_cast<float>(a.n0);
+  const float invM = a.copies > 1 ? 1.0f / (static_cast<float>(a.B - a.n0) * static_cast<float>(a.A)) : 0.f;
   const int head_cols = a.hetero ? 2 * a.A : a.A;
   // per-lane accumulators: columns lane and lane + 32 of the head gradient, std gradient
   float acc_dh[4] = {0.f, 0.f, 0.f, 0.f};  // head cols lane, lane+32, lane+64, lane+96
   float acc_dstd[2] = {0.f, 0.f};
-  float acc_surr = 0.f, acc_val = 0.f, acc_ent = 0.f, acc_kl = 0.f, acc_dv = 0.f;
+  float acc_surr = 0.f, acc_val = 0.f, acc_ent = 0.f, acc_kl = 0.f, acc_sym = 0.f, acc_dv = 0.f;
 
   const int row0 = blockIdx.x * kLossRowsPerBlock + warp * kLossRowsPerWarp;
   for (int rr = 0; rr < kLossRowsPerWarp; ++rr) {
     const int i = row0 + rr;
     if (i >= a.B) break;
-    const int src = a.idx[i];
+    const int copy = kSym ? i / a.n0 : 0;
+    const int o = i - copy * a.n0;
+    const bool ppo_row = a.aug || copy == 0;
+    const int src = a.idx[o];
     const float* h = a.head + static_cast<size_t>(i) * a.ld_head;
-    float mu[2], sd[2], raw[2], act[2], omu[2], osd[2];
-    float lp = 0.f, ent = 0.f, kl = 0.f;
+    float mu[2], sd[2], raw[2], act[2], mt[2];
+    float lp = 0.f, ent = 0.f, kl = 0.f, sym = 0.f;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int j = lane + 32 * k;
-      mu[k] = sd[k] = raw[k] = act[k] = omu[k] = osd[k] = 0.f;
+      mu[k] = sd[k] = raw[k] = act[k] = mt[k] = 0.f;
       if (j < a.A) {
         mu[k] = h[j];
         raw[k] = a.hetero ? h[a.A + j] : a.std_param[j];
         sd[k] = head_std(raw[k], a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
-        const size_t o = static_cast<size_t>(src) * a.A + j;
-        act[k] = a.st_actions[o];
-        omu[k] = a.st_mean[o];
-        osd[k] = a.st_std[o];
+        int aj = j;
+        float asg = 1.f;
+        if (copy > 0) {  // the copy's action and mirror target: signed permutation of the original's columns
+          aj = a.act_perm[copy * a.A + j];
+          asg = a.act_sign[copy * a.A + j];
+          mt[k] = asg * a.head[static_cast<size_t>(o) * a.ld_head + aj];
+          const float dm = mu[k] - mt[k];
+          sym += dm * dm;
+        }
+        act[k] = asg * a.st_actions[static_cast<size_t>(src) * a.A + aj];
         const float z = (act[k] - mu[k]) / sd[k];
         const float lsd = logf(sd[k]);
         lp += -0.5f * z * z - lsd - kLogSqrt2Pi;
-        ent += 0.5f + kLogSqrt2Pi + lsd;
-        // KL(old || new) for diagonal Gaussians
-        const float vr = (osd[k] / sd[k]) * (osd[k] / sd[k]);
-        const float t1 = ((omu[k] - mu[k]) / sd[k]) * ((omu[k] - mu[k]) / sd[k]);
-        kl += 0.5f * (vr + t1 - 1.0f - logf(vr));
+        if (copy == 0) {
+          const size_t so = static_cast<size_t>(src) * a.A + j;
+          const float omu = a.st_mean[so], osd = a.st_std[so];
+          ent += 0.5f + kLogSqrt2Pi + lsd;
+          // KL(old || new) for diagonal Gaussians
+          const float vr = (osd / sd[k]) * (osd / sd[k]);
+          const float t1 = ((omu - mu[k]) / sd[k]) * ((omu - mu[k]) / sd[k]);
+          kl += 0.5f * (vr + t1 - 1.0f - logf(vr));
+        }
       }
     }
 #pragma unroll
@@ -395,37 +461,43 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
       lp += __shfl_xor_sync(0xffffffffu, lp, off);
       ent += __shfl_xor_sync(0xffffffffu, ent, off);
       kl += __shfl_xor_sync(0xffffffffu, kl, off);
+      sym += __shfl_xor_sync(0xffffffffu, sym, off);
     }
-    // surrogate (identical on every lane)
-    const float adv = a.adv_override ? a.adv_override[i] : a.st_adv[src];
-    const float ratio = expf(lp - a.st_logp[src]);
-    const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
-    const float rc = fminf(fmaxf(ratio, lo), hi);
-    const float s1 = -adv * ratio, s2 = -adv * rc;
-    float g1, g2;
-    max_grad_split(s1, s2, g1, g2);
-    const float in_rng = (ratio >= lo && ratio <= hi) ? 1.f : 0.f;
-    const float d_ratio = (g1 * -adv + g2 * -adv * in_rng) * invB;
-    const float d_lp = d_ratio * ratio;
-    // value loss
-    const float v = a.value[static_cast<size_t>(i) * a.ld_value];
-    const float ret = a.st_ret[src];
-    const float vold = a.st_val[src];
-    float vloss, dv;
-    if (a.clipped_value) {
-      const float dvv = v - vold;
-      const float vc = vold + fminf(fmaxf(dvv, -a.clip), a.clip);
-      const float l1 = (v - ret) * (v - ret), l2 = (vc - ret) * (vc - ret);
-      float q1, q2;
-      max_grad_split(l1, l2, q1, q2);
-      const float vin = (dvv >= -a.clip && dvv <= a.clip) ? 1.f : 0.f;
-      vloss = fmaxf(l1, l2);
-      dv = q1 * 2.f * (v - ret) + q2 * 2.f * (vc - ret) * vin;
-    } else {
-      vloss = (ret - v) * (ret - v);
-      dv = 2.f * (v - ret);
+    float d_lp = 0.f, dv = 0.f, surr = 0.f, vloss = 0.f;
+    if (ppo_row) {
+      // surrogate (identical on every lane)
+      const float adv = a.adv_override ? a.adv_override[o] : a.st_adv[src];
+      const float ratio = expf(lp - a.st_logp[src]);
+      const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
+      const float rc = fminf(fmaxf(ratio, lo), hi);
+      const float s1 = -adv * ratio, s2 = -adv * rc;
+      float g1, g2;
+      max_grad_split(s1, s2, g1, g2);
+      const float in_rng = (ratio >= lo && ratio <= hi) ? 1.f : 0.f;
+      const float d_ratio = (g1 * -adv + g2 * -adv * in_rng) * invP;
+      d_lp = d_ratio * ratio;
+      surr = fmaxf(s1, s2);
+      // value loss
+      const float v = a.value[static_cast<size_t>(i) * a.ld_value];
+      const float ret = a.st_ret[src];
+      const float vold = a.st_val[src];
+      if (a.clipped_value) {
+        const float dvv = v - vold;
+        const float vc = vold + fminf(fmaxf(dvv, -a.clip), a.clip);
+        const float l1 = (v - ret) * (v - ret), l2 = (vc - ret) * (vc - ret);
+        float q1, q2;
+        max_grad_split(l1, l2, q1, q2);
+        const float vin = (dvv >= -a.clip && dvv <= a.clip) ? 1.f : 0.f;
+        vloss = fmaxf(l1, l2);
+        dv = q1 * 2.f * (v - ret) + q2 * 2.f * (vc - ret) * vin;
+      } else {
+        vloss = (ret - v) * (ret - v);
+        dv = 2.f * (v - ret);
+      }
+      dv *= a.value_coef * invP;
     }
-    dv *= a.value_coef * invB;
+    const float ent_w = copy == 0 ? a.entropy_coef * invE : 0.f;
+    const float mir_w = copy > 0 ? 2.f * a.mirror_coef * invM : 0.f;
     // gradients w.r.t. mean and std of each action
     __nv_bfloat16* dh = static_cast<__nv_bfloat16*>(a.d_head) + static_cast<size_t>(i) * a.ld_dhead;
 #pragma unroll
@@ -434,8 +506,8 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
       if (j < a.A) {
         const float inv_var = 1.0f / (sd[k] * sd[k]);
         const float diff = act[k] - mu[k];
-        const float dmu = d_lp * diff * inv_var;
-        const float dsd = d_lp * (diff * diff * inv_var / sd[k] - 1.0f / sd[k]) - a.entropy_coef * invB / sd[k];
+        const float dmu = d_lp * diff * inv_var + mir_w * (mu[k] - mt[k]);
+        const float dsd = d_lp * (diff * diff * inv_var / sd[k] - 1.0f / sd[k]) - ent_w / sd[k];
         // chain through the std parameterisation (clamp passes the gradient on [lo, hi] inclusive)
         float dsd_raw;
         if (a.log_std) {
@@ -458,20 +530,25 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
     // zero the padding columns of the head gradient
     for (int c = head_cols + lane; c < a.ld_dhead; c += 32) dh[c] = __float2bfloat16_rn(0.f);
     if (lane == 0) {
-      __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.d_value) + static_cast<size_t>(i) * a.ld_dvalue;
-      dvp[0] = __float2bfloat16_rn(dv);
-      for (int c = 1; c < a.ld_dvalue; ++c) dvp[c] = __float2bfloat16_rn(0.f);
-      acc_surr += fmaxf(s1, s2) * invB;
-      acc_val += vloss * invB;
-      acc_ent += ent * invB;
-      acc_kl += kl * invB;
-      acc_dv += dv;
+      if (ppo_row) {
+        __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.d_value) + static_cast<size_t>(i) * a.ld_dvalue;
+        dvp[0] = __float2bfloat16_rn(dv);
+        for (int c = 1; c < a.ld_dvalue; ++c) dvp[c] = __float2bfloat16_rn(0.f);
+        acc_surr += surr * invP;
+        acc_val += vloss * invP;
+        acc_dv += dv;
+      }
+      if (copy == 0) {
+        acc_ent += ent * invE;
+        acc_kl += kl * invE;
+      }
+      acc_sym += sym * invM;
     }
   }
   // ---- block reduction in fixed warp order ----
   __shared__ float sh_dh[kLossWarps][4][32];
   __shared__ float sh_dstd[kLossWarps][2][32];
-  __shared__ float sh_sc[kLossWarps][5];
+  __shared__ float sh_sc[kLossWarps][kLossStats + 1];
 #pragma unroll
   for (int k = 0; k < 4; ++k) sh_dh[warp][k][lane] = acc_dh[k];
   sh_dstd[warp][0][lane] = acc_dstd[0];
@@ -481,7 +558,8 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
     sh_sc[warp][1] = acc_val;
     sh_sc[warp][2] = acc_ent;
     sh_sc[warp][3] = acc_kl;
-    sh_sc[warp][4] = acc_dv;
+    sh_sc[warp][4] = acc_sym;
+    sh_sc[warp][5] = acc_dv;
   }
   __syncthreads();
   const int t = threadIdx.x;
@@ -502,12 +580,12 @@ __global__ void __launch_bounds__(kLossWarps * 32) ppo_loss_kernel(const PpoLoss
       else if (a.dstd_partial)
         a.dstd_partial[static_cast<size_t>(blockIdx.x) * a.A + j] = sstd;
     }
-  } else if (t < 69) {
+  } else if (t < 64 + kLossStats + 1) {
     const int q = t - 64;
     float s = 0.f;
     for (int w = 0; w < kLossWarps; ++w) s += sh_sc[w][q];
-    if (q < 4)
-      a.stats_partial[static_cast<size_t>(blockIdx.x) * 4 + q] = s;
+    if (q < kLossStats)
+      a.stats_partial[static_cast<size_t>(blockIdx.x) * kLossStats + q] = s;
     else
       a.dvalue_colsum[blockIdx.x] = s;
   }
@@ -1023,8 +1101,13 @@ uint32_t feistel_permute_host(uint32_t i, uint32_t n, uint32_t half_bits, uint32
 }
 
 cudaError_t gather_minibatch(const GatherArgs& a, cudaStream_t s) {
-  if (a.B <= 0 || a.dim[0] > kGatherMaxD || (a.models > 1 && a.dim[1] > kGatherMaxD)) return cudaErrorInvalidValue;
-  gather_minibatch_kernel<<<grid_for(a.B, 8 * kGatherRows, 148 * 16), 256, 0, s>>>(a);
+  if (a.B <= 0 || a.models < 1 || a.models > kGatherModels || a.copies < 1) return cudaErrorInvalidValue;
+  int max_rows = 0;
+  for (int m = 0; m < a.models; ++m) {
+    if (a.dim[m] > kGatherMaxD || a.rows[m] < 1 || a.rows[m] > a.copies * a.B) return cudaErrorInvalidValue;
+    max_rows = max(max_rows, a.rows[m]);
+  }
+  gather_minibatch_kernel<<<grid_for(max_rows, 8 * kGatherRows, 148 * 16), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -1032,7 +1115,11 @@ int ppo_loss_blocks(int B) { return (B + kLossRowsPerBlock - 1) / kLossRowsPerBl
 
 cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
   if (a.A > kLossMaxA || a.B <= 0) return cudaErrorInvalidValue;
-  ppo_loss_kernel<<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
+  if (a.copies < 1 || a.n0 <= 0 || a.B != a.copies * a.n0) return cudaErrorInvalidValue;
+  if (a.copies > 1)
+    ppo_loss_kernel<true><<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
+  else
+    ppo_loss_kernel<false><<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -1041,6 +1128,32 @@ cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_c
   if (nseg <= 0 || total_chunks <= 0) return cudaErrorInvalidValue;
   reduce_segments_kernel<<<total_chunks, dim3(kReduceCols, kReduceLanes), 0, s>>>(segs_dev, nseg, send0, send1, epoch,
                                                                                     accumulate);
+  return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256) rnd_intrinsic_kernel(const float* __restrict__ target, int ld_target,
+                                                            const float* __restrict__ pred, int ld_pred, int rows,
+                                                            int dim, const float* __restrict__ weight,
+                                                            float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const float w = *weight;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < rows; i += (gridDim.x * blockDim.x) >> 5) {
+    float s = 0.f;
+    for (int j = lane; j < dim; j += 32) {
+      const float d = target[static_cast<size_t>(i) * ld_target + j] - pred[static_cast<size_t>(i) * ld_pred + j];
+      s += d * d;
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) out[i] = w * sqrtf(s);
+  }
+}
+
+cudaError_t rnd_intrinsic(const float* target, int ld_target, const float* pred, int ld_pred, int rows, int dim,
+                          const float* weight, float* out, cudaStream_t s) {
+  if (rows <= 0 || dim <= 0) return cudaErrorInvalidValue;
+  rnd_intrinsic_kernel<<<grid_for(rows, 8, 148 * 16), 256, 0, s>>>(target, ld_target, pred, ld_pred, rows, dim,
+                                                                    weight, out);
   return cudaGetLastError();
 }
 

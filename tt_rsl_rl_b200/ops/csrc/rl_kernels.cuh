@@ -84,24 +84,30 @@ cudaError_t gae(const GaeArgs& a, cudaStream_t s);
 // advantages = (adv - mean) / (std_unbiased + 1e-8) over all T*N values; each block re-reduces `partial`.
 cudaError_t adv_normalize(float* adv, long long n, const double* partial, int parts, cudaStream_t s);
 
+constexpr int kGatherModels = 3;
 // Minibatch gather: for rows i in [0, B) take storage row idx = perm(offset + i) (Feistel bijection of [0, total) keyed
 // by *key_ptr) or idx_in[i]; write idx_out[i] and the normalised bf16 observations of up to two models.
 struct GatherArgs {
-  int B;
+  int B;               // original minibatch rows (n0)
   long long offset;
   long long total;
   const uint32_t* key_ptr;
   int half_bits;
   const int* idx_in;  // optional explicit permutation slice
   int* idx_out;
-  const float* obs[2];
-  int obs_ld[2];
-  int dim[2];
-  const float* mean[2];
-  const float* std[2];
+  int copies;          // symmetry copies K >= 1: row r of a model is copy r / B of sample r % B
+  const float* obs[kGatherModels];
+  int obs_ld[kGatherModels];
+  int dim[kGatherModels];
+  int rows[kGatherModels];          // rows written for each model: B or K * B
+  const float* mean[kGatherModels];
+  const float* std[kGatherModels];
+  const int* perm[kGatherModels];   // [K, dim] source column of each output column per copy (null: identity)
+  const float* sign[kGatherModels]; // [K, dim]
+  int vec4[kGatherModels];          // 1: obs rows 16-byte aligned with a pitch that is a multiple of 4 floats
   float eps;
-  void* x[2];  // bf16
-  int ld_x[2];
+  void* x[kGatherModels];  // bf16
+  int ld_x[kGatherModels];
   int models;
   unsigned int* status;
 };
@@ -112,17 +118,23 @@ uint32_t feistel_permute_host(uint32_t i, uint32_t n, uint32_t half_bits, uint32
 // PPO loss terms and gradients with respect to the model outputs (upstream ppo.py:241-294), with per-block partial
 // sums (deterministic) for the loss statistics, bias gradients of both heads and the std-parameter gradient.
 struct PpoLossArgs {
-  int B;
+  int B;       // actor rows = copies * n0
+  int n0;      // original samples of the minibatch
+  int copies;  // symmetry copies (1: none)
+  int aug;     // 1: surrogate/value terms over all B rows (data augmentation); 0: rows < n0 only
+  const int* act_perm;    // [copies, A] action column maps (copy 0 identity); null when copies == 1
+  const float* act_sign;  // [copies, A]
+  float mirror_coef;      // gradient weight of the mirror loss (0: statistics only)
   int A;
   int hetero;
   int log_std;
   const float* head;  // actor last-layer output [B, ld_head]
   int ld_head;
-  const float* value;  // critic output [B, ld_value]
+  const float* value;  // critic output [rows, ld_value] (rows = B if aug else n0)
   int ld_value;
   const float* std_param;
   float std_lo, std_hi, log_std_lo, log_std_hi;
-  const int* idx;  // storage row per minibatch row
+  const int* idx;  // storage row per original minibatch row
   const float* st_actions;
   const float* st_mean;
   const float* st_std;
@@ -130,18 +142,19 @@ struct PpoLossArgs {
   const float* st_adv;
   const float* st_ret;
   const float* st_val;
-  const float* adv_override;  // optional per-minibatch normalised advantages [B] (normalize_advantage_per_mini_batch)
+  const float* adv_override;  // optional per-minibatch normalised advantages [n0] (normalize_advantage_per_mini_batch)
   float clip, value_coef, entropy_coef;
   int clipped_value;
   void* d_head;  // bf16 [B, ld_dhead]
   int ld_dhead;
-  void* d_value;  // bf16 [B, ld_dvalue]
+  void* d_value;  // bf16 [rows, ld_dvalue]
   int ld_dvalue;
-  float* stats_partial;   // [blocks, 4]: surrogate, value, entropy, kl (each already divided by B)
+  float* stats_partial;   // [blocks, kLossStats]: surrogate, value, entropy, kl, symmetry (each a mean)
   float* dhead_colsum;    // [blocks, head_cols]
   float* dvalue_colsum;   // [blocks, 1]
   float* dstd_partial;    // [blocks, A] (non-hetero)
 };
+constexpr int kLossStats = 5;
 int ppo_loss_blocks(int B);
 cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s);
 
@@ -178,6 +191,10 @@ struct MseArgs {
   unsigned int* ticket;   // [1], zero between launches
 };
 int mse_blocks(int rows);
+
+// RND intrinsic reward: out[i] = weight[step] * || target[i] - pred[i] ||_2 over dim columns.
+cudaError_t rnd_intrinsic(const float* target, int ld_target, const float* pred, int ld_pred, int rows, int dim,
+                          const float* weight, float* out, cudaStream_t s);
 cudaError_t mse_grad(const MseArgs& a, cudaStream_t s);
 constexpr int kReduceChunk = 32;  // columns per block of the reduction kernel
 
