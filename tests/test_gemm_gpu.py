@@ -71,6 +71,50 @@ def test_dgrad_elu_colsum(M, Nin, Kout):
     torch.testing.assert_close(colsum.sum(0), ref.sum(0), atol=1e-2 * M ** 0.5, rtol=1e-3)
 
 
+@pytest.mark.parametrize("M,Nin,Kout", [(333, 40, 64), (130, 72, 29), (200, 36, 64)])
+def test_dgrad_elu_padded_pitches(M, Nin, Kout):
+    """Output and activation buffers with different padded row pitches: padding columns are left untouched."""
+    from tt_rsl_rl_b200.ops import gemm as G
+
+    torch.manual_seed(5)
+    kp = G.pad8(Kout)
+    dz = torch.zeros(M, kp, device="cuda", dtype=torch.bfloat16)
+    dz[:, :Kout] = _bf16((M, Kout))
+    w = _bf16((Kout, G.pad8(Nin) + 8), 0.1)
+    h = torch.zeros(M, G.pad8(Nin) + 8, device="cuda", dtype=torch.bfloat16)
+    h[:, :Nin] = torch.nn.functional.elu(torch.randn(M, Nin, device="cuda")).to(torch.bfloat16)
+    out = torch.full((M, G.pad8(Nin) + 16), 7.0, device="cuda", dtype=torch.bfloat16)
+    colsum = torch.zeros(G.m_tiles(M), Nin, device="cuda")
+    G.gemm(dz, kp, False, w, w.shape[1], True, M, Nin, Kout, G.EPI_DGRAD_ELU, out, out.shape[1], aux=h,
+           ld_aux=h.shape[1], colsum=colsum)
+    torch.cuda.synchronize()
+    hf = h[:, :Nin].float()
+    grad = torch.where(hf > 0, torch.ones_like(hf), hf + 1)
+    ref = (dz[:, :Kout].float() @ w[:, :Nin].float()) * grad
+    torch.testing.assert_close(out[:, :Nin].float(), ref, atol=3e-2, rtol=2e-2)
+    assert (out[:, Nin : G.pad8(Nin)].float() == 0.0).all()
+    assert (out[:, G.pad8(Nin) :].float() == 7.0).all()
+    torch.testing.assert_close(colsum.sum(0), ref.sum(0), atol=1e-2 * M ** 0.5, rtol=1e-3)
+
+
+def test_forward_bias_elu_leaves_padding():
+    from tt_rsl_rl_b200.ops import gemm as G
+
+    torch.manual_seed(6)
+    M, N, K = 200, 36, 64
+    x = _bf16((M, K))
+    w = _bf16((N, K), 0.1)
+    bias = torch.randn(N, device="cuda") * 0.1
+    out = torch.full((M, 48), 5.0, device="cuda", dtype=torch.bfloat16)
+    G.gemm(x, K, False, w, K, False, M, N, K, G.EPI_BIAS_ELU_BF16, out, 48, bias=bias)
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.elu(_ref(x, w) + bias)
+    torch.testing.assert_close(out[:, :N].float(), ref, atol=3e-2, rtol=2e-2)
+    # bf16 outputs are stored in 16-byte column groups: [N, pad8(N)) receives zeros, columns past it are untouched
+    assert (out[:, N : G.pad8(N)].float() == 0.0).all()
+    assert (out[:, G.pad8(N) :].float() == 5.0).all()
+
+
 @pytest.mark.parametrize("rows,out_f,in_f,splits", [(4096, 256, 512, 4), (3000, 29, 128, 3), (8192, 512, 96, 8),
                                                     (1000, 1, 256, 2)])
 def test_wgrad_split_partials(rows, out_f, in_f, splits):

@@ -10,6 +10,9 @@
 //                 warps of a quadrant splitting the column chunks
 // Barriers: full/empty per ring stage (TMA <-> MMA), acc_full/acc_empty per accumulator (MMA <-> epilogue). Every
 // wait is bounded (%globaltimer); a timeout records the site in the status word and the kernel unwinds.
+// bf16-output epilogues work in 32-row x 32-column steps through two 2 KB buffers per warp (64-byte swizzle, so the
+// row-per-thread 16-byte shared accesses are conflict-free): the data-gradient epilogue TMA-loads the next step's
+// ELU-output tile while it computes the current one, and every step leaves through a TMA store.
 // No load uses cluster multicast: every CTA fetches its own tiles from this GPU's memory.
 //
 // The MLP layers of rsl_rl (rsl_rl/modules/mlp.py:91-95, Linear+ELU stacks) map onto three uses:
@@ -33,7 +36,7 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMNBoxBytes = 64 * kBK * 2;  // one {64 MN x 64 K} box
-constexpr int kStageWords = 32 * 33;       // per-warp 32 x 32-word staging tile (+1 word padding per row)
+constexpr int kEpiBufBytes = 32 * 32 * 2;  // one epilogue step: 32 rows x 32 bf16 columns (64-byte rows)
 constexpr int kSmemLimit = 227 * 1024;
 
 // Resident CTAs per SM: the bf16-output epilogues (forward activations, data gradients that also stream the ELU
@@ -51,10 +54,11 @@ struct Cfg {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr bool kStaged = !(EPI == kEpiF32 || EPI == kEpiPartialF32);  // bf16 outputs go through smem
-  static constexpr int kStagingBytes = kStaged ? kEpiWarps * kStageWords * 4 : 0;
+  static constexpr int kStagingBytes = kStaged ? kEpiWarps * 2 * kEpiBufBytes : 0;
+  static constexpr int kBiasBytes = kStaged ? kEpiWarps * 32 * 4 : 0;
   static constexpr int kColsumBytes = EPI == kEpiDgradElu ? 2 * 4 * BN * 4 : 0;  // double-buffered by tile parity
-  static constexpr int kBarrierBytes = 256;
-  static constexpr int kFixed = 1024 /*alignment slack*/ + kStagingBytes + kColsumBytes + kBarrierBytes;
+  static constexpr int kBarrierBytes = 512;
+  static constexpr int kFixed = 1024 /*alignment slack*/ + kStagingBytes + kBiasBytes + kColsumBytes + kBarrierBytes;
   static constexpr int kStagesFit = (kSmemBudget - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
   static constexpr int kAccCols = BN < 32 ? 32 : BN;
@@ -84,6 +88,7 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int n_tiles, int m_tiles
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmX,
                    const GemmParams p, int num_kb, int n_tiles, int m_tiles, int splits) {
   using C = Cfg<BN, EPI>;
   constexpr int S = C::kStages;
@@ -91,13 +96,15 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * kABytes;
-  uint32_t* staging = reinterpret_cast<uint32_t*>(sB + S * C::kBBytes);
-  float* colsum_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(staging) + C::kStagingBytes);
+  uint8_t* staging = sB + S * C::kBBytes;  // 1024-byte aligned: stage sizes are multiples of 1 KB
+  float* bias_smem = reinterpret_cast<float*>(staging + C::kStagingBytes);
+  float* colsum_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bias_smem) + C::kBiasBytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(colsum_s) + C::kColsumBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* aux_bar = acc_empty + 2;  // two per epilogue warp (data-gradient epilogue)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 2 * kEpiWarps);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -113,9 +120,12 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kEpiWarps);
     }
+    for (int b = 0; b < 2 * kEpiWarps; ++b) mbar_init(&aux_bar[b], 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (C::kStaged) tma_prefetch_desc(&tmO);
+    if constexpr (EPI == kEpiDgradElu) tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -218,16 +228,165 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
         mma_commit(&acc_full[b]);
       }
     }
-  } else {
-    // ---------------- epilogue (warps 2..9) ----------------
+  } else if constexpr (C::kStaged) {
+    // ---------------- bf16-output epilogue (warps 2..9), 32 x 32 steps through two swizzled buffers -------------
     const int ew = warp - 2;
     const int q = warp & 3;  // TMEM lane quadrant: hardware rule warp % 4
     const int half = ew >> 2;
-    uint32_t* stage = staging + ew * kStageWords;
-    constexpr int CW = BN >= 64 ? 64 : 32;  // columns per chunk (64 bf16 = one 128-byte line per row)
-    constexpr int WPR = CW / 2;             // 32-bit words per row of a bf16 chunk
-    constexpr int LPR = WPR / 4;            // lanes per row for 16-byte accesses
-    constexpr int RPP = 32 / LPR;           // rows per pass
+    uint8_t* ebuf = staging + ew * 2 * kEpiBufBytes;
+    float* bias_s = bias_smem + ew * 32;
+    uint64_t* xbar = aux_bar + 2 * ew;
+    // 64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3); each thread owns row `lane`
+    const int swz = (lane >> 1) & 3;
+    // next (tile, 32-column step) of this warp whose aux tile is still to be loaded (data-gradient epilogue)
+    int pt = blockIdx.x, psc = half;
+    int issued = 0, consumed = 0;
+    auto seek = [&](int& t, int& sc) {
+      while (t < num_tiles) {
+        const int n0 = (t % n_tiles) * BN;
+        if (sc * 32 < BN && n0 + sc * 32 < p.N) return;
+        t += gridDim.x;
+        sc = half;
+      }
+    };
+    auto issue_aux = [&]() {  // lane 0 only
+      if (pt >= num_tiles) return;
+      const TileCoord pc = decode_tile(pt, n_tiles, m_tiles, splits, num_kb, BN);
+      uint8_t* dst = ebuf + (issued & 1) * kEpiBufBytes;
+      bulk_wait_group_read<0>();  // the store that last read this buffer is done with it
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&xbar[issued & 1], kEpiBufBytes);
+      tma_load_2d(dst, &tmX, &xbar[issued & 1], pc.n0 + psc * 32, pc.m0 + q * 32);
+      ++issued;
+      psc += 2;
+      seek(pt, psc);
+    };
+    if constexpr (EPI == kEpiDgradElu) {
+      seek(pt, psc);
+      if (lane == 0) issue_aux();
+    }
+    // After a timeout the warp keeps walking the tile schedule without waiting or computing, so every epilogue warp
+    // still reaches each tile's column-sum barrier (a named barrier cannot time out) and the kernel unwinds.
+    bool failed = false;
+    int j = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
+      const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
+      const int b = j & 1;
+      const uint32_t use = static_cast<uint32_t>(j >> 1);
+      if (!failed) {
+        uint32_t ok = 1;
+        if (lane == 0) ok = mbar_wait(&acc_full[b], use & 1) ? 1u : 0u;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          if (lane == 0) report_error(p.status, kTimeoutAccum, 3);
+          failed = true;
+        }
+      }
+      tc_fence_after();
+      const int row_base = tc.m0 + q * 32;
+      const bool row_ok = row_base + lane < p.M;
+      const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
+      float* cs = colsum_s + b * 4 * BN;
+#pragma unroll 1
+      for (int sc = half; !failed && sc * 32 < BN && tc.n0 + sc * 32 < p.N; sc += 2, ++consumed) {
+        const int sb = tc.n0 + sc * 32;
+        uint8_t* buf = ebuf + (consumed & 1) * kEpiBufBytes;
+        float v[32];
+        tmem_ld_32x32b_x32(acc + static_cast<uint32_t>(sc * 32), v);
+        if constexpr (EPI == kEpiDgradElu) {
+          if (lane == 0) issue_aux();  // next step's ELU-output tile, one step ahead
+        } else {
+          if (lane == 0) bulk_wait_group_read<1>();  // the store issued two steps ago has read this buffer
+          bias_s[lane] = (p.bias != nullptr && sb + lane < p.N) ? __ldg(p.bias + sb + lane) : 0.f;
+        }
+        __syncwarp();
+        tmem_wait_ld();
+        uint4* rowp = reinterpret_cast<uint4*>(buf + lane * 64);
+        if constexpr (EPI == kEpiDgradElu) {
+          uint32_t ok2 = mbar_wait(&xbar[consumed & 1], (consumed >> 1) & 1) ? 1u : 0u;
+          if (!__all_sync(0xffffffffu, ok2)) {
+            if (lane == 0) report_error(p.status, kTimeoutTmaFull, 5);
+            failed = true;
+            ++consumed;  // this step's aux tile is accounted for (drained below if it lands late)
+            break;
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 w = rowp[c ^ swz];
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&ws[i]);
+              v[8 * c + 2 * i] *= elu_grad_from_out(__low2float(h2));
+              v[8 * c + 2 * i + 1] *= elu_grad_from_out(__high2float(h2));
+            }
+          }
+          if (!row_ok) {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) v[jj] = 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 bb = reinterpret_cast<const float4*>(bias_s)[c];  // broadcast read
+            v[4 * c] += bb.x;
+            v[4 * c + 1] += bb.y;
+            v[4 * c + 2] += bb.z;
+            v[4 * c + 3] += bb.w;
+          }
+          if constexpr (EPI == kEpiBiasEluBf16) {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) v[jj] = v[jj] > 0.f ? v[jj] : __expf(v[jj]) - 1.0f;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          rowp[c ^ swz] = make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                                     pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+        if constexpr (EPI == kEpiDgradElu) {
+          if (p.colsum != nullptr) {
+            const float sum = warp_transpose_reduce32(v);  // per-column sums over this warp's 32 rows
+            cs[q * BN + sc * 32 + lane] = sum;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (row_base < p.M) tma_store_2d(&tmO, buf, sb, row_base);
+          bulk_commit_group();
+        }
+      }
+      // accumulator b fully read by this warp: hand it back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && !failed) mbar_arrive(&acc_empty[b]);
+      if constexpr (EPI == kEpiDgradElu) {
+        if (p.colsum != nullptr) {
+          named_barrier_sync(1, kEpiWarps * 32);
+          const int tt = threadIdx.x - 64;
+          for (int n = tt; n < BN; n += kEpiWarps * 32) {
+            if (tc.n0 + n < p.N) {
+              const float sum = cs[n] + cs[BN + n] + cs[2 * BN + n] + cs[3 * BN + n];
+              p.colsum[static_cast<size_t>(tc.m_tile) * p.N + tc.n0 + n] = sum;
+            }
+          }
+        }
+      }
+    }
+    if (lane == 0) {
+      // aux tiles still in flight after an early exit land before the CTA's shared memory is released; a tile whose
+      // wait already timed out is waited for once more (bounded)
+      const int first = failed ? consumed - 1 : consumed;
+      for (int k = first < 0 ? 0 : first; k < issued; ++k) mbar_wait(&xbar[k & 1], (k >> 1) & 1);
+      bulk_wait_group<0>();  // outputs written before the kernel ends
+    }
+    __syncwarp();
+  } else {
+    // ---------------- fp32-output epilogue (warps 2..9) ----------------
+    const int ew = warp - 2;
+    const int q = warp & 3;  // TMEM lane quadrant: hardware rule warp % 4
+    const int half = ew >> 2;
+    constexpr int CW = BN >= 64 ? 64 : 32;  // columns per chunk
     int j = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
       const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
@@ -241,57 +400,20 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
         break;
       }
       tc_fence_after();
-      const int row_base = tc.m0 + q * 32;
-      const int row = row_base + lane;
+      const int row = tc.m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
-      float* cs = colsum_s + b * 4 * BN;
 #pragma unroll 1
       for (int c = half * CW; c < BN; c += 2 * CW) {
         const int nb = tc.n0 + c;
         if (nb >= p.N) break;
-        const int valid = min(CW, p.N - nb);
-        const bool full_cols = valid == CW;
-        if constexpr (EPI == kEpiDgradElu) {
-          // coalesced load of the aux (ELU output) chunk into the staging tile, RPP rows per pass
-          const __nv_bfloat16* aux = static_cast<const __nv_bfloat16*>(p.aux);
-          const int lr = lane / LPR, lw = (lane % LPR) * 4;
-          const bool vec = full_cols && (p.ld_aux % 8) == 0;
-#pragma unroll
-          for (int r0 = 0; r0 < 32; r0 += RPP) {
-            const int r = r0 + lr;
-            const int gr = row_base + r;
-            uint32_t w4[4] = {0u, 0u, 0u, 0u};
-            if (gr < p.M) {
-              const __nv_bfloat16* src = aux + static_cast<size_t>(gr) * p.ld_aux + nb + 2 * lw;
-              if (vec) {
-                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src));
-                w4[0] = raw.x;
-                w4[1] = raw.y;
-                w4[2] = raw.z;
-                w4[3] = raw.w;
-              } else {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const int col = 2 * (lw + i);
-                  const float lo = col < valid ? __bfloat162float(src[2 * i]) : 0.f;
-                  const float hi = col + 1 < valid ? __bfloat162float(src[2 * i + 1]) : 0.f;
-                  w4[i] = pack_bf16x2(lo, hi);
-                }
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) stage[r * 33 + lw + i] = w4[i];
-          }
-          __syncwarp();
-        }
 #pragma unroll
         for (int sub = 0; sub < CW; sub += 32) {
           float v[32];
           tmem_ld_32x32b_x32(acc + static_cast<uint32_t>(c + sub), v);
           tmem_wait_ld();
           const int sb = nb + sub;
-          if constexpr (EPI == kEpiF32 || EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16) {
+          if constexpr (EPI == kEpiF32) {
             if (p.bias != nullptr) {
               // lane l holds bias[sb + l]; element j takes it by shuffle
               const float my_bias = (sb + lane < p.N) ? __ldg(p.bias + sb + lane) : 0.f;
@@ -299,94 +421,26 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
               for (int jj = 0; jj < 32; ++jj) v[jj] += __shfl_sync(0xffffffffu, my_bias, jj);
             }
           }
-          if constexpr (EPI == kEpiBiasEluBf16) {
+          float* o = static_cast<float*>(p.out) +
+                     (EPI == kEpiPartialF32 ? static_cast<long long>(tc.split) * p.split_stride : 0ll) +
+                     static_cast<size_t>(row) * p.ldo + sb;
+          if (row_ok) {
+            if (sb + 32 <= p.N && (p.ldo % 4) == 0) {
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) v[jj] = v[jj] > 0.f ? v[jj] : __expf(v[jj]) - 1.0f;
-          }
-          if constexpr (EPI == kEpiDgradElu) {
+              for (int jj = 0; jj < 32; jj += 4)
+                *reinterpret_cast<float4*>(o + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
+            } else {
 #pragma unroll
-            for (int jj = 0; jj < 32; jj += 2) {
-              const uint32_t w = stage[lane * 33 + (sub + jj) / 2];
-              __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w);
-              v[jj] *= elu_grad_from_out(__low2float(h2));
-              v[jj + 1] *= elu_grad_from_out(__high2float(h2));
-            }
-            if (!row_ok) {
-#pragma unroll
-              for (int jj = 0; jj < 32; ++jj) v[jj] = 0.f;
+              for (int jj = 0; jj < 32; ++jj)
+                if (sb + jj < p.N) o[jj] = v[jj];
             }
           }
-          if constexpr (EPI == kEpiF32 || EPI == kEpiPartialF32) {
-            float* o = static_cast<float*>(p.out) +
-                       (EPI == kEpiPartialF32 ? static_cast<long long>(tc.split) * p.split_stride : 0ll) +
-                       static_cast<size_t>(row) * p.ldo + sb;
-            if (row_ok) {
-              if (sb + 32 <= p.N && (p.ldo % 4) == 0) {
-#pragma unroll
-                for (int jj = 0; jj < 32; jj += 4)
-                  *reinterpret_cast<float4*>(o + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
-              } else {
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj)
-                  if (sb + jj < p.N) o[jj] = v[jj];
-              }
-            }
-          } else {
-            // each lane rewrites the words of its own row that it has just read (aux), so one tile suffices
-#pragma unroll
-            for (int jj = 0; jj < 32; jj += 2) stage[lane * 33 + (sub + jj) / 2] = pack_bf16x2(v[jj], v[jj + 1]);
-          }
-          if constexpr (EPI == kEpiDgradElu) {
-            if (p.colsum != nullptr) {
-              const float sum = warp_transpose_reduce32(v);  // per-column sums over this warp's 32 rows
-              cs[q * BN + c + sub + lane] = sum;
-            }
-          }
-        }
-        if constexpr (C::kStaged) {
-          __syncwarp();
-          __nv_bfloat16* outp = static_cast<__nv_bfloat16*>(p.out);
-          const int lr = lane / LPR, lw = (lane % LPR) * 4;
-          const bool vec = full_cols && (p.ldo % 8) == 0;
-#pragma unroll
-          for (int r0 = 0; r0 < 32; r0 += RPP) {
-            const int r = r0 + lr;
-            const int gr = row_base + r;
-            if (gr < p.M) {
-              __nv_bfloat16* dst = outp + static_cast<size_t>(gr) * p.ldo + nb + 2 * lw;
-              const uint32_t* src = stage + r * 33 + lw;
-              if (vec) {
-                *reinterpret_cast<uint4*>(dst) = make_uint4(src[0], src[1], src[2], src[3]);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const int col = 2 * (lw + i);
-                  __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&src[i]);
-                  if (col < valid) dst[2 * i] = __low2bfloat16(h2);
-                  if (col + 1 < valid) dst[2 * i + 1] = __high2bfloat16(h2);
-                }
-              }
-            }
-          }
-          __syncwarp();
         }
       }
       // accumulator b fully read by this warp: hand it back to the MMA issuer
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
-      if constexpr (EPI == kEpiDgradElu) {
-        if (p.colsum != nullptr) {
-          named_barrier_sync(1, kEpiWarps * 32);
-          const int tt = threadIdx.x - 64;
-          for (int n = tt; n < BN; n += kEpiWarps * 32) {
-            if (tc.n0 + n < p.N) {
-              const float sum = cs[n] + cs[BN + n] + cs[2 * BN + n] + cs[3 * BN + n];
-              p.colsum[static_cast<size_t>(tc.m_tile) * p.N + tc.n0 + n] = sum;
-            }
-          }
-        }
-      }
     }
   }
 
@@ -416,7 +470,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D bf16 tensor map: dims {inner, outer}, row pitch ld elements, box {box_inner, box_outer}, 128B swizzle.
 bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
-              uint32_t box_outer) {
+              uint32_t box_outer, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -424,7 +478,7 @@ bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -453,6 +507,11 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb;
   bool ok = A_MN ? make_map(&ta, p.a, p.M, p.K, p.lda, 64, 64) : make_map(&ta, p.a, p.K, p.M, p.lda, 64, kBM);
   ok = ok && (B_MN ? make_map(&tb, p.b, p.N, p.K, p.ldb, 64, 64) : make_map(&tb, p.b, p.K, p.N, p.ldb, 64, BN));
+  // epilogue maps: bf16 output (TMA store) and ELU-output aux (TMA load), 32 x 32 boxes with 64-byte swizzle
+  CUtensorMap to = ta, tx = ta;
+  if constexpr (C::kStaged) ok = ok && make_map(&to, p.out, p.N, p.M, p.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if constexpr (EPI == kEpiDgradElu)
+    ok = ok && make_map(&tx, p.aux, p.N, p.M, p.ld_aux, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return cudaErrorInvalidValue;
   const int num_kb = (p.K + kBK - 1) / kBK;
   const int m_tiles = (p.M + kBM - 1) / kBM;
@@ -461,7 +520,7 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   if (tiles > (1ll << 31) - 1) return cudaErrorInvalidValue;
   const long long slots = static_cast<long long>(sm_count()) * C::kMinBlocks;
   const int grid = static_cast<int>(tiles < slots ? tiles : slots);
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p, num_kb, n_tiles, m_tiles, p.splits);
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, to, tx, p, num_kb, n_tiles, m_tiles, p.splits);
   return cudaGetLastError();
 }
 
@@ -484,6 +543,11 @@ cudaError_t gemm_launch(const GemmParams& p, cudaStream_t stream) {
   if (p.splits > num_kb) return cudaErrorInvalidValue;
   if (p.splits > 1 && p.epilogue != kEpiPartialF32) return cudaErrorInvalidValue;
   if (p.epilogue == kEpiDgradElu && p.aux == nullptr) return cudaErrorInvalidValue;
+  const bool staged = p.epilogue == kEpiBiasEluBf16 || p.epilogue == kEpiBiasBf16 || p.epilogue == kEpiDgradElu;
+  // TMA epilogue rules: 16-byte aligned bases, row pitches that are multiples of 16 bytes
+  if (staged && ((p.ldo % 8) != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15))) return cudaErrorInvalidValue;
+  if (p.epilogue == kEpiDgradElu && ((p.ld_aux % 8) != 0 || (reinterpret_cast<uintptr_t>(p.aux) & 15)))
+    return cudaErrorInvalidValue;
   const bool am = p.a_mn_major, bm = p.b_mn_major;
   switch (p.epilogue) {
     case kEpiF32:

@@ -12,13 +12,15 @@ namespace rlb {
 //   A K-major : A(m, k) = a[m * lda + k]          A MN-major : A(m, k) = a[k * lda + m]
 //   B K-major : B(n, k) = b[n * ldb + k]          B MN-major : B(n, k) = b[k * ldb + n]
 // The leading dimension times 2 bytes must be a multiple of 16 (TMA stride rule); extents need not be.
+// bf16 outputs (and the bf16 aux input) need 16-byte aligned bases and ldo, ld_aux multiples of 8. They leave through
+// TMA stores in 16-byte column groups: columns [N, N rounded up to 8) of each output row receive zeros (the
+// accumulator columns past N are zero), columns beyond are untouched.
 enum GemmEpilogue : int {
   kEpiF32 = 0,         // out fp32 = acc (+ bias[n])
   kEpiBiasEluBf16 = 1, // out bf16 = elu(acc + bias[n])
   kEpiBiasBf16 = 2,    // out bf16 = acc + bias[n]
   kEpiDgradElu = 3,    // out bf16 = acc * elu'(aux[m, n]) with aux = elu output (bf16); colsum partials of out
   kEpiPartialF32 = 4,  // out fp32 split partial: out[z * split_stride + m * ldo + n] = acc over split z
-  kEpiDgradF32 = 5,    // out fp32 = acc (no activation); colsum partials optional
 };
 
 struct GemmParams {
