@@ -80,4 +80,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM with fused MLP epilogues");
   rlb_register_kernels(m);
   rlb_register_p2p(m);
+  rlb_register_rnn(m);
 }

@@ -4,3 +4,4 @@
 
 void rlb_register_kernels(pybind11::module& m);
 void rlb_register_p2p(pybind11::module& m);
+void rlb_register_rnn(pybind11::module& m);
