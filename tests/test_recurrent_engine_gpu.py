@@ -1,0 +1,119 @@
+"""The fused recurrent PPO engine (GRU / LSTM, done-masked BPTT) against the PyTorch path on identical data."""
+
+import copy
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _models(obs, rnn_type, H=64, A=8):
+    from tt_rsl_rl_b200.models import RNNModel
+
+    groups = {"actor": ["policy"], "critic": ["critic"]}
+    dist = {"class_name": "GaussianDistribution", "init_std": 1.0}
+    actor = RNNModel(obs, groups, "actor", A, hidden_dims=[64, 32], obs_normalization=True, distribution_cfg=dist,
+                     rnn_type=rnn_type, rnn_hidden_dim=H)
+    critic = RNNModel(obs, groups, "critic", 1, hidden_dims=[64, 32], obs_normalization=True, rnn_type=rnn_type,
+                      rnn_hidden_dim=H)
+    return actor, critic
+
+
+def _sequence_means(actor, obs_seq, dones_seq, h0):
+    """Deterministic actor means over a stored sequence from the given initial state (PyTorch, fp32)."""
+    actor.rnn.hidden_state = h0
+    out = []
+    with torch.no_grad():
+        for t in range(obs_seq.shape[0]):
+            out.append(actor(obs_seq[t]))
+            actor.reset(dones_seq[t])
+    actor.rnn.hidden_state = None
+    return torch.stack(out)
+
+
+@pytest.mark.parametrize("rnn_type", ["gru", "lstm"])
+def test_recurrent_engine_matches_torch_path(rnn_type):
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    torch.manual_seed(0)
+    T, N = 12, 512
+    env = LinearGaussianVecEnv(N, obs_dim=24, num_actions=8, privileged_dim=3, device="cuda", reset_prob=0.05)
+    obs = env.get_observations()
+    actor, critic = _models(obs, rnn_type)
+    kw = dict(num_learning_epochs=2, num_mini_batches=4)
+    storage = RolloutStorage("rl", N, T, obs, [env.num_actions], "cuda")
+    alg_t = PPO(actor, critic, storage, device="cuda", b200_cfg={"engine": "torch"}, **kw)
+    alg_e = PPO(copy.deepcopy(actor), copy.deepcopy(critic), None, device="cuda",
+                b200_cfg={"engine": "cuda", "graphs": False}, num_steps_per_env=T, num_envs=N, **kw)
+    from tt_rsl_rl_b200.engine import RecurrentPPOEngine
+
+    assert isinstance(alg_e.engine, RecurrentPPOEngine)
+    # two rollouts on the PyTorch path; the second starts from a non-zero state
+    for it in range(2):
+        with torch.inference_mode():
+            for _ in range(T):
+                actions = alg_t.act(obs)
+                obs, rew, dones, extras = env.step(actions)
+                alg_t.process_env_step(obs, rew, dones, extras)
+            alg_t.compute_returns(obs)
+        if it == 0:
+            storage.clear()
+    st = storage
+    sa, sc = st.saved_hidden_state_a, st.saved_hidden_state_c
+    h0a, h0c = sa[0][0, 0].clone(), sc[0][0, 0].clone()
+    c0a = sa[1][0, 0].clone() if len(sa) > 1 else None
+    c0c = sc[1][0, 0].clone() if len(sc) > 1 else None
+    assert h0a.abs().sum() > 0
+    alg_e.engine.load_rollout(st, h0a, h0c, c0a, c0c)
+    obs_seq = st.observations
+    dones_seq = st.dones.squeeze(-1)
+    h0 = h0a[None] if c0a is None else (h0a[None].clone(), c0a[None].clone())
+    old = _sequence_means(alg_t.actor, obs_seq, dones_seq, h0)
+    w0 = alg_t.actor.rnn.rnn.weight_hh_l0.detach().clone()
+    loss_t = alg_t.update()
+    loss_e = alg_e.update()
+    h0 = h0a[None] if c0a is None else (h0a[None].clone(), c0a[None].clone())
+    new_t = _sequence_means(alg_t.actor, obs_seq, dones_seq, h0)
+    h0 = h0a[None] if c0a is None else (h0a[None].clone(), c0a[None].clone())
+    new_e = _sequence_means(alg_e.actor, obs_seq, dones_seq, h0)
+    dev = ((new_e - new_t).norm() / (new_t - old).norm()).item()
+    assert dev < 0.2, dev
+    for k in ("value", "surrogate", "entropy"):
+        assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=3e-3), (k, loss_e[k], loss_t[k])
+    assert alg_e.learning_rate == pytest.approx(alg_t.learning_rate, rel=1e-6)
+    # recurrent weights moved like the PyTorch path's
+    wt, we = alg_t.actor.rnn.rnn.weight_hh_l0.detach(), alg_e.actor.rnn.rnn.weight_hh_l0.detach()
+    assert ((we - wt).norm() / (wt - w0).norm()).item() < 0.25
+
+
+@pytest.mark.parametrize("rnn_type", ["gru", "lstm"])
+def test_recurrent_runner_learns_with_graphs(rnn_type, tmp_path):
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    torch.manual_seed(3)
+    env = LinearGaussianVecEnv(256, obs_dim=24, num_actions=8, privileged_dim=3, device="cuda", reset_prob=0.05)
+    cfg = {
+        "num_steps_per_env": 8, "save_interval": 1000, "obs_groups": {"actor": ["policy"], "critic": ["critic"]},
+        "algorithm": {"class_name": "PPO", "num_learning_epochs": 2, "num_mini_batches": 2,
+                      "b200_cfg": {"engine": "cuda"}},
+        "actor": {"class_name": "RNNModel", "hidden_dims": [64, 32], "obs_normalization": True, "rnn_type": rnn_type,
+                  "rnn_hidden_dim": 64, "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+        "critic": {"class_name": "RNNModel", "hidden_dims": [64, 32], "obs_normalization": True, "rnn_type": rnn_type,
+                   "rnn_hidden_dim": 64},
+    }
+    runner = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    assert runner.alg.engine is not None
+    runner.learn(4)
+    eng = runner.alg.engine
+    assert torch.isfinite(eng.flat).all()
+    assert int(eng.step[0].item()) == 4 * 2 * 2
+    path = str(tmp_path / "m.pt")
+    runner.save(path)
+    runner2 = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    runner2.load(path)
+    torch.testing.assert_close(runner2.alg.engine.flat, eng.flat)
+    runner2.learn(1)

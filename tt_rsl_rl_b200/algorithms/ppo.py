@@ -119,10 +119,9 @@ class PPO:
 
         self.engine = None
         if self._engine_requested():
-            from ..engine import PPOEngine
-
-            self.engine = PPOEngine(self, num_steps_per_env=num_steps_per_env or storage.num_transitions_per_env,
-                                    num_envs=num_envs or storage.num_envs, obs_template=obs_template)
+            engine_cls = _engine_class(self.actor)
+            self.engine = engine_cls(self, num_steps_per_env=num_steps_per_env or storage.num_transitions_per_env,
+                                     num_envs=num_envs or storage.num_envs, obs_template=obs_template)
 
     # ---- engine selection ---------------------------------------------------------------------------------------------
     def _engine_requested(self) -> bool:
@@ -131,9 +130,7 @@ class PPO:
             if mode == "cuda":
                 raise ValueError("b200_cfg.engine='cuda' requires a CUDA device")
             return False
-        from ..engine import PPOEngine
-
-        reason = PPOEngine.unsupported_reason(self)
+        reason = _engine_class(self.actor).unsupported_reason(self)
         if reason is None:
             return True
         if mode == "cuda":
@@ -412,12 +409,17 @@ class PPO:
         reduce_gradients_in_buckets(params, self.gpu_world_size, self.grad_reduce_bucket_mb)
 
 
+def _engine_class(actor):
+    """The fused engine for the actor's model family: recurrent (GRU/LSTM) or MLP."""
+    from ..engine import PPOEngine, RecurrentPPOEngine
+
+    return RecurrentPPOEngine if getattr(actor, "is_recurrent", False) else PPOEngine
+
+
 def _engine_will_run(b200: dict, device: str, actor, critic, alg_cfg: dict) -> bool:
     if b200["engine"] == "torch" or torch.device(device).type != "cuda":
         return False
-    from ..engine import PPOEngine
-
-    return PPOEngine.supports_models(actor, critic, alg_cfg) is None
+    return _engine_class(actor).supports_models(actor, critic, alg_cfg) is None
 
 
 def _upgrade_legacy_checkpoint(d: dict) -> dict:

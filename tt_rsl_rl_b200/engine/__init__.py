@@ -2,5 +2,6 @@
 
 from .distillation_engine import DistillationEngine
 from .ppo_engine import PPOEngine
+from .recurrent_engine import RecurrentPPOEngine
 
-__all__ = ["DistillationEngine", "PPOEngine"]
+__all__ = ["DistillationEngine", "PPOEngine", "RecurrentPPOEngine"]

@@ -100,11 +100,13 @@ class MLPPlan:
                        bias=lin.bias.data, status=status)
 
     # ---- backward ---------------------------------------------------------------------------------------------------
-    def backward(self, rows: int, status: torch.Tensor | None = None, x: torch.Tensor | None = None) -> None:
+    def backward(self, rows: int, status: torch.Tensor | None = None, x: torch.Tensor | None = None,
+                 dx_out: torch.Tensor | None = None) -> None:
         """Weight gradients (split partials) of every layer and data gradients down to layer 1.
 
         Requires ``d_head`` (gradient of the head output, padding columns zero) and the cached activations of the
-        training forward pass; ``x`` is that pass's input when it was not ``x_train``.
+        training forward pass; ``x`` is that pass's input when it was not ``x_train``. With ``dx_out`` (fp32
+        [rows, in_dim]) the gradient of the input, ``dZ_1 W_1``, is written as well (no activation below the input).
         """
         inputs = [self.x_train if x is None else x] + self.h_train  # input of layer l is inputs[l]
         dz_l = self.d_head
@@ -120,6 +122,10 @@ class MLPPlan:
             G.gemm(dz_l, dz_l.shape[1], True, h_in, h_in.shape[1], True, out_f, in_f, rows, G.EPI_PARTIAL_F32, part,
                    in_f, splits=splits, split_stride=out_f * in_f, status=status)
             if l == 0:
+                if dx_out is not None:
+                    w = self.w_bf16[0]
+                    G.gemm(dz_l, dz_l.shape[1], False, w, w.shape[1], True, rows, in_f, out_f, G.EPI_F32, dx_out,
+                           dx_out.stride(0), status=status)
                 break
             # dZ_{l-1} = (dZ_l W_l) * elu'(H_{l-1}); W_l [out, pad8(in)] read MN-major
             w = self.w_bf16[l]

@@ -18,6 +18,11 @@ T* ptr_or_null(const c10::optional<torch::Tensor>& t) {
   return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
 }
 
+// Elements addressable from t's first element to the end of its storage (strided row views reach past numel()).
+int64_t avail(const torch::Tensor& t) {
+  return static_cast<int64_t>(t.storage().nbytes() / t.element_size()) - t.storage_offset();
+}
+
 void raise_on(cudaError_t e, const char* what) {
   TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
 }
@@ -36,14 +41,14 @@ void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b
   // extent checks (elements reachable by the kernel)
   const int64_t a_need = a_mn ? (K - 1) * lda + M : (M - 1) * lda + K;
   const int64_t b_need = b_mn ? (K - 1) * ldb + N : (N - 1) * ldb + K;
-  TORCH_CHECK(a.numel() >= a_need, "gemm: A too small");
-  TORCH_CHECK(b.numel() >= b_need, "gemm: B too small");
-  TORCH_CHECK(out.numel() >= (splits - 1) * split_stride + (M - 1) * ldo + N, "gemm: out too small");
+  TORCH_CHECK(avail(a) >= a_need, "gemm: A too small");
+  TORCH_CHECK(avail(b) >= b_need, "gemm: B too small");
+  TORCH_CHECK(avail(out) >= (splits - 1) * split_stride + (M - 1) * ldo + N, "gemm: out too small");
   if (bias.has_value() && bias->defined()) {
     TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "gemm: bad bias");
   }
   if (aux.has_value() && aux->defined()) {
-    TORCH_CHECK(aux->scalar_type() == torch::kBFloat16 && aux->numel() >= (M - 1) * ld_aux + N, "gemm: bad aux");
+    TORCH_CHECK(aux->scalar_type() == torch::kBFloat16 && avail(*aux) >= (M - 1) * ld_aux + N, "gemm: bad aux");
   }
   if (colsum.has_value() && colsum->defined()) {
     TORCH_CHECK(colsum->scalar_type() == torch::kFloat32 && colsum->numel() >= rlb::gemm_m_tiles(M) * N,
