@@ -40,6 +40,8 @@ BASELINE_VALUE = None  # BASELINE.md publishes no NVIDIA number for this configu
 
 # BASELINE.json configurations: (total envs or None, envs per GPU or None, env kwargs, description)
 CONFIGS = {
+    "0": dict(total=1024, per_gpu=None, env={"obs_dim": 48, "num_actions": 12}, cpu=True,
+              desc="single-process CPU PPO fp32: MLPs [512,256,128] ELU, obs 48, 12 actions, 1024 envs"),
     "1": dict(total=65536, per_gpu=None, env={}, desc="PPO MLP actor-critic [512,256,128] ELU, obs 96/99, 29 actions"),
     "2": dict(total=65536, per_gpu=None, env={},
               desc="config 1 + RND [256,256]->16 on critic obs (weight 0.5) + symmetry (2 copies, mirror loss 1.0)"),
@@ -110,6 +112,15 @@ def train_cfg(impl: str, config: str = "1") -> dict:
     }
     # bf16 GEMMs on both arms: autocast on the reference arm and on any PyTorch-path fallback of this framework
     alg["use_mixed_precision"] = True
+    if config == "0":  # CPU, fp32, no observation normalisation, critic on the policy observations
+        alg["use_mixed_precision"] = False
+        return {
+            "num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
+            "obs_groups": {"actor": ["policy"], "critic": ["policy"]}, "algorithm": alg,
+            "actor": {"class_name": "MLPModel", "hidden_dims": [512, 256, 128], "activation": "elu",
+                      "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+            "critic": {"class_name": "MLPModel", "hidden_dims": [512, 256, 128], "activation": "elu"},
+        }
     return {
         "num_steps_per_env": T_STEPS, "save_interval": 10**9, "check_for_nan": True,
         "obs_groups": {"actor": ["policy"], "critic": ["critic"]},
@@ -220,15 +231,31 @@ def dist_info() -> tuple[int, int, int]:
 
 
 def make_env(num_envs: int, device: str, host_noise: bool, seed: int, **env_kw):
-    from tt_rsl_rl_b200.env import humanoid_like
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv, humanoid_like
 
+    if "obs_dim" in env_kw:  # config 0: the plain linear-Gaussian environment
+        return LinearGaussianVecEnv(num_envs, device=device, seed=seed, **env_kw)
     return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise, **env_kw)
 
 
-def timed_learn(runner, steps: int, warmup: int, world: int) -> float:
-    """Seconds per iteration (device time), max over ranks."""
+def timed_learn_cpu(runner, steps: int, warmup: int) -> float:
+    """Seconds per iteration on the host clock (CPU configuration)."""
+    runner.learn(warmup)
+    t0 = time.perf_counter()
+    runner.learn(steps)
+    return (time.perf_counter() - t0) / steps
+
+
+def timed_learn(runner, steps: int, warmup: int, world: int, counter=None) -> float:
+    """Seconds per iteration (device time), max over ranks. The first warm-up iteration runs eagerly (CUDA graphs are
+    captured from the second one on); with ``counter`` this framework's kernel launches of that iteration are counted,
+    which equals the launches of every later (replayed) iteration."""
     import torch
 
+    if counter is not None and warmup > 0:
+        with counter:
+            runner.learn(1)
+        warmup -= 1
     runner.learn(warmup)
     torch.cuda.synchronize()
     if world > 1:
@@ -298,6 +325,9 @@ def main() -> None:
 
     import torch
 
+    if conf.get("cpu"):
+        run_cpu(args, conf)
+        return
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     torch.cuda.set_device(local_rank)
     device = f"cuda:{local_rank}"
@@ -321,7 +351,12 @@ def main() -> None:
     sampler = ClockSampler([local_rank]) if local_rank == 0 else None
     if sampler:
         sampler.__enter__()
-    s_per_iter = timed_learn(runner, args.steps, args.warmup, world)
+    counter = None
+    if args.impl == "ours":
+        from tt_rsl_rl_b200.ops import count_launches
+
+        counter = count_launches()
+    s_per_iter = timed_learn(runner, args.steps, args.warmup, world, counter)
     if sampler:
         sampler.__exit__()
     samples = total_envs * T_STEPS
@@ -337,10 +372,7 @@ def main() -> None:
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 20 if args.impl == "ours" else 16,
                "input": "environment process noise copied from pinned host memory every env step"}
 
-    launches = None
-    if args.impl == "ours":
-        eng = getattr(runner.alg, "engine", None)
-        launches = kernel_launches_per_iteration(eng) if eng is not None and hasattr(eng, "plan_c") else 0
+    launches = counter.n if counter is not None else None
 
     if rank == 0:
         line = {
@@ -373,17 +405,30 @@ def main() -> None:
         torch.distributed.destroy_process_group()
 
 
-def kernel_launches_per_iteration(engine) -> int:
-    """Launches of this framework's kernels per timed iteration (counted from the engine's structure)."""
-    if engine is None:
-        return 0
-    L_a, L_c = engine.plan_a.L, engine.plan_c.L
-    per_act = 2 + L_a + 1 + L_c  # prep x2, actor GEMMs, sample, critic GEMMs
-    per_step = per_act + 1  # + process_step
-    returns = 1 + L_c + 2  # prep, critic GEMMs, gae, normalise
-    per_mb = 1 + L_a + L_c + 1 + (2 * L_a - 1) + (2 * L_c - 1) + 1 + 1  # gather, fwd, loss, bwd, reduce, adam
-    update = 1 + engine.E * engine.M * per_mb + 2 * 2  # perm key, minibatches, normaliser (2 kernels x 2 models)
-    return engine.T * per_step + returns + update
+def run_cpu(args, conf) -> None:
+    """Config 0: one process on the host CPU, fp32, timed with the host clock."""
+    import torch
+
+    if args.gpus != 1:
+        raise SystemExit("config 0 is a single-process CPU configuration")
+    torch.manual_seed(1)
+    env = make_env(conf["total"], "cpu", host_noise=False, seed=0, **conf["env"])
+    runner = build_runner(args.impl, env, "cpu", args.config)
+    s_per_iter = timed_learn_cpu(runner, args.steps, args.warmup)
+    samples = conf["total"] * T_STEPS
+    line = {
+        "metric": "PPO train samples/s (box, max over ranks)", "value": samples / s_per_iter, "unit": "samples/s",
+        "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "ms_per_step": s_per_iter * 1e3,
+        "s_per_iter": s_per_iter, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic (seeded linear-Gaussian env), random-init weights",
+        "config": {"model": conf["desc"], "baseline_config": "0", "global_batch": samples, "seq_len": T_STEPS,
+                   "num_envs_total": conf["total"], "epochs": 5, "minibatches": 4, "parallelism": "cpu",
+                   "timing": "host clock (no device)", "threads": torch.get_num_threads()},
+        "e2e": None, "gpu_launches": 0, "clocks": None,
+    }
+    if args.impl == "reference":
+        line["impl"] = "reference"
+    print(json.dumps(line))
 
 
 if __name__ == "__main__":
