@@ -103,7 +103,7 @@ def test_cell_backward_matches_autograd(lstm):
     cs_gh = None if lstm else torch.zeros(blocks, G * H, device="cuda")
     C().rnn_cell_bwd(rows, H, lstm, save, S * H, None if lstm else h.detach(), H, c.detach() if lstm else None, H,
                      dh_head, H, rec_a, rec_b, H, dc_rec, H, done, dgi, G * H, dgh, G * H, dh_direct, H, dc_prev, H,
-                     cs_gi, cs_gh)
+                     cs_gi, cs_gh, False)
     torch.cuda.synchronize()
     tol = dict(rtol=2e-2, atol=2e-2 * gi.grad.abs().max().item() / 8)
     torch.testing.assert_close(dgi.float(), gi.grad, **tol)
@@ -115,3 +115,10 @@ def test_cell_backward_matches_autograd(lstm):
         torch.testing.assert_close(dgh.float(), gh.grad, **tol)
         torch.testing.assert_close(cs_gh.sum(0), gh.grad.sum(0), rtol=1e-4, atol=1e-3)
         torch.testing.assert_close(dh_direct, h.grad, rtol=1e-4, atol=1e-4)  # dL/dh not through W_hh
+    # accumulate mode adds a second sweep step's sums onto the same rows
+    before = [t.clone() for t in (cs_gi, cs_gh) if t is not None]
+    C().rnn_cell_bwd(rows, H, lstm, save, S * H, None if lstm else h.detach(), H, c.detach() if lstm else None, H,
+                     dh_head, H, rec_a, rec_b, H, dc_rec, H, done, dgi, G * H, dgh, G * H, dh_direct, H, dc_prev, H,
+                     cs_gi, cs_gh, True)
+    for t, b in zip([t for t in (cs_gi, cs_gh) if t is not None], before):
+        torch.testing.assert_close(t, 2 * b, rtol=1e-6, atol=1e-6)

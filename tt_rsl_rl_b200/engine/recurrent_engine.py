@@ -91,8 +91,9 @@ class _RecurrentNet:
         self.dh_gemm = [torch.zeros(Be_max, H, **f32) for _ in range(2)]
         self.dc = [torch.zeros(Be_max, H, **f32) for _ in range(2)] if self.lstm else [None, None]
         self.bwd_blocks = ext().rnn_bwd_blocks(Be_max)
-        self.cs_gi = torch.zeros(T * self.bwd_blocks, GH, **f32)
-        self.cs_gh = None if self.lstm else torch.zeros(T * self.bwd_blocks, GH, **f32)
+        # bias-gradient column sums: one row per backward-cell block, accumulated over the T steps of a sweep
+        self.cs_gi = torch.zeros(self.bwd_blocks, GH, **f32)
+        self.cs_gh = None if self.lstm else torch.zeros(self.bwd_blocks, GH, **f32)
         self.splits_ih = wgrad_splits(GH, self.D, R, sm_count)
         self.splits_hh = wgrad_splits(GH, H, R, sm_count)
         self.part_ih = torch.zeros(self.splits_ih, GH, self.D, **f32)
@@ -106,7 +107,7 @@ class _RecurrentNet:
 
     def reduce_segments(self, head_bias_partial, head_parts: int) -> dict[int, tuple]:
         segs = self.head.reduce_segments(head_bias_partial, head_parts)
-        parts = self.T * self.bwd_blocks
+        parts = self.bwd_blocks
         segs[id(self.w_ih)] = (self.part_ih, self.splits_ih, self.w_ih.numel())
         segs[id(self.w_hh)] = (self.part_hh, self.splits_hh, self.w_hh.numel())
         segs[id(self.b_ih)] = (self.cs_gi, parts, self.b_ih.numel())
@@ -168,11 +169,11 @@ class _RecurrentNet:
         T, N, H, GH, S = self.T, self.N, self.H, self.GH, self.S
         R = Be * T
         nb = self.bwd_blocks
-        if C.rnn_bwd_blocks(Be) < nb:  # a shorter env range writes fewer column-sum rows per step
+        if C.rnn_bwd_blocks(Be) < nb:  # a shorter env range writes fewer column-sum rows
             used = C.rnn_bwd_blocks(Be)
             for cs in (self.cs_gi, self.cs_gh):
                 if cs is not None:
-                    cs.view(T, nb, GH)[:, used:].zero_()
+                    cs[used:].zero_()
         self.head.backward(R, status, x=self.hout_bf, dx_out=self.dh_head)
         dgh = self.dgi if self.lstm else self.dgh
         for t in range(T - 1, -1, -1):
@@ -188,9 +189,7 @@ class _RecurrentNet:
                            None if last else dones_tm[t * N + lo : t * N + lo + Be],
                            _view_from(self.dgi, t * GH), T * GH,
                            None if self.lstm else _view_from(self.dgh, t * GH), T * GH,
-                           self.dh_direct[cur], H, self.dc[cur], H,
-                           _view_from(self.cs_gi, t * nb * GH),
-                           None if self.lstm else _view_from(self.cs_gh, t * nb * GH))
+                           self.dh_direct[cur], H, self.dc[cur], H, self.cs_gi, self.cs_gh, not last)
             if t > 0:  # gradient of the step's input state through W_hh (W_hh [GH, H] read MN-major)
                 G.gemm(_view_from(dgh, t * GH), T * GH, False, self.w_hh_bf, self.w_hh_bf.shape[1], True, Be, H, GH,
                        G.EPI_F32, self.dh_gemm[cur], H, status=status)

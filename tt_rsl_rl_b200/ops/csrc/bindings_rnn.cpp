@@ -72,7 +72,7 @@ void rnn_cell_bwd(int64_t rows, int64_t H, bool lstm, const Tensor& save, int64_
                   const OptT& dh_rec_a, const OptT& dh_rec_b, int64_t ld_dh_rec, const OptT& dc_rec, int64_t ld_dc_rec,
                   const OptT& done, const Tensor& dgi, int64_t ld_dgi, const OptT& dgh, int64_t ld_dgh,
                   const OptT& dh_direct, int64_t ld_dh_direct, const OptT& dc_prev, int64_t ld_dc_prev,
-                  const OptT& colsum_gi, const OptT& colsum_gh) {
+                  const OptT& colsum_gi, const OptT& colsum_gh, bool colsum_accumulate) {
   const int64_t G = lstm ? 4 : 3, S = lstm ? 5 : 4;
   const auto f32 = torch::kFloat32, bf = torch::kBFloat16;
   const int64_t blocks = rlb::rnn_bwd_blocks(static_cast<int>(rows));
@@ -104,6 +104,7 @@ void rnn_cell_bwd(int64_t rows, int64_t H, bool lstm, const Tensor& save, int64_
   a.ld_dc_prev = ld_dc_prev;
   a.colsum_gi = ptr<float>(colsum_gi, blocks, G * H, G * H, f32, "colsum_gi");
   a.colsum_gh = ptr<float>(colsum_gh, blocks, G * H, G * H, f32, "colsum_gh");
+  a.colsum_accumulate = colsum_accumulate ? 1 : 0;
   ok(rlb::rnn_cell_bwd(a, cur()), "rnn_cell_bwd");
 }
 

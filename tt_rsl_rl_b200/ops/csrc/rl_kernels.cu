@@ -384,10 +384,25 @@ __global__ void __launch_bounds__(256, 3) gather_minibatch_kernel(const GatherAr
 // ---------------------------------------------------------------------------------------------------------------
 // PPO loss: one warp per row (lane j handles actions j and j + 32); 16 warps x 4 rows per block
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kLossWarps = 16;
+constexpr int kLossWarps = 8;
 constexpr int kLossRowsPerWarp = 4;
 constexpr int kLossRowsPerBlock = kLossWarps * kLossRowsPerWarp;
 constexpr int kLossMaxA = 64;
+constexpr int kLossGridCap = 2 * 148;  // two resident blocks per SM of a B200
+
+// Standard deviation of the head's std parameterisation and its log and reciprocal: with log-std the log is the
+// clamped raw value itself (no logarithm), with a direct std one log; one correctly rounded reciprocal replaces the
+// divisions of the log-probability, KL and gradient terms.
+__device__ __forceinline__ void std_terms(float raw, const PpoLossArgs& a, float& sd, float& lsd, float& isd) {
+  if (a.log_std) {
+    lsd = fminf(fmaxf(raw, a.log_std_lo), a.log_std_hi);
+    sd = expf(lsd);
+  } else {
+    sd = fminf(fmaxf(raw, a.std_lo), a.std_hi);
+    lsd = logf(sd);
+  }
+  isd = __frcp_rn(sd);
+}
 
 // torch.max(a, b) backward: the larger input gets the gradient, ties split it in halves.
 __device__ __forceinline__ void max_grad_split(float a, float b, float& ga, float& gb) {
@@ -400,8 +415,10 @@ __device__ __forceinline__ void max_grad_split(float a, float b, float& ga, floa
 //   entropy and KL: copy 0 only (mean over n0), as upstream evaluates them on the original samples;
 //   mirror loss: copies >= 1, MSE between the row's mean and the mirrored mean of its original (target detached).
 // kSym = false compiles the plain path (one copy) without the symmetry branches and their registers.
+// The plain path first issues every load of the warp's kLossRowsPerWarp rows (random storage rows: actions, old mean
+// and std, scalars) and only then computes, so each warp keeps its rows' loads in flight together.
 template <bool kSym>
-__global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoLossArgs a) {
+__global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel(const PpoLossArgs a) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const float invP = 1.0f / static_cast<float>(a.aug ? a.B : a.n0);
@@ -413,25 +430,74 @@ __global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoL
   float acc_dstd[2] = {0.f, 0.f};
   float acc_surr = 0.f, acc_val = 0.f, acc_ent = 0.f, acc_kl = 0.f, acc_sym = 0.f, acc_dv = 0.f;
 
-  const int row0 = blockIdx.x * kLossRowsPerBlock + warp * kLossRowsPerWarp;
+  // state-independent std (a parameter): std, log std and 1 / std of this lane's actions, once per kernel
+  float c_raw[2], c_sd[2], c_lsd[2], c_isd[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int j = lane + 32 * k;
+    c_raw[k] = (!a.hetero && j < a.A) ? a.std_param[j] : 1.f;
+    std_terms(c_raw[k], a, c_sd[k], c_lsd[k], c_isd[k]);
+  }
+  // blocks stride over groups of kLossRowsPerBlock rows: the grid (and so the number of per-block partials that the
+  // gradient reduction has to sum) is capped at kLossGridCap whatever the minibatch size
+  const int ngroups = (a.B + kLossRowsPerBlock - 1) / kLossRowsPerBlock;
+  for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
+  const int row0 = grp * kLossRowsPerBlock + warp * kLossRowsPerWarp;
+  // prefetch (plain path): storage rows of all of this warp's rows
+  constexpr int PF = kSym ? 1 : kLossRowsPerWarp;
+  float pf_act[PF][2], pf_omu[PF][2], pf_osd[PF][2], pf_mu[PF][2], pf_raw[PF][2];
+  float pf_adv[PF], pf_lp[PF], pf_ret[PF], pf_vold[PF], pf_v[PF];
+  if constexpr (!kSym) {
+#pragma unroll
+    for (int rr = 0; rr < PF; ++rr) {
+      const int i = row0 + rr;
+      const bool in = i < a.B;
+      const int src = in ? a.idx[i] : 0;
+      const float* h = a.head + static_cast<size_t>(in ? i : 0) * a.ld_head;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int j = lane + 32 * k;
+        const bool ok = in && j < a.A;
+        const size_t so = static_cast<size_t>(src) * a.A + j;
+        pf_act[rr][k] = ok ? a.st_actions[so] : 0.f;
+        pf_omu[rr][k] = ok ? a.st_mean[so] : 0.f;
+        pf_osd[rr][k] = ok ? a.st_std[so] : 1.f;
+        pf_mu[rr][k] = ok ? h[j] : 0.f;
+        pf_raw[rr][k] = (ok && a.hetero) ? h[a.A + j] : 1.f;  // non-hetero: the shared parameter, read below
+      }
+      pf_adv[rr] = in ? (a.adv_override ? a.adv_override[i] : a.st_adv[src]) : 0.f;
+      pf_lp[rr] = in ? a.st_logp[src] : 0.f;
+      pf_ret[rr] = in ? a.st_ret[src] : 0.f;
+      pf_vold[rr] = in ? a.st_val[src] : 0.f;
+      pf_v[rr] = in ? a.value[static_cast<size_t>(i) * a.ld_value] : 0.f;
+    }
+  }
+#pragma unroll
   for (int rr = 0; rr < kLossRowsPerWarp; ++rr) {
     const int i = row0 + rr;
     if (i >= a.B) break;
     const int copy = kSym ? i / a.n0 : 0;
     const int o = i - copy * a.n0;
     const bool ppo_row = a.aug || copy == 0;
-    const int src = a.idx[o];
+    const int src = kSym ? a.idx[o] : 0;
     const float* h = a.head + static_cast<size_t>(i) * a.ld_head;
-    float mu[2], sd[2], raw[2], act[2], mt[2];
+    float mu[2], sd[2], isd[2], raw[2], act[2], mt[2];
     float lp = 0.f, ent = 0.f, kl = 0.f, sym = 0.f;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int j = lane + 32 * k;
-      mu[k] = sd[k] = raw[k] = act[k] = mt[k] = 0.f;
+      mu[k] = act[k] = mt[k] = 0.f;
+      raw[k] = c_raw[k];
+      sd[k] = c_sd[k];
+      isd[k] = c_isd[k];
+      float lsd = c_lsd[k];
       if (j < a.A) {
-        mu[k] = h[j];
-        raw[k] = a.hetero ? h[a.A + j] : a.std_param[j];
-        sd[k] = head_std(raw[k], a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
+        const int pr = kSym ? 0 : rr;
+        mu[k] = kSym ? h[j] : pf_mu[pr][k];
+        if (a.hetero) {
+          raw[k] = kSym ? h[a.A + j] : pf_raw[pr][k];
+          std_terms(raw[k], a, sd[k], lsd, isd[k]);
+        }
         int aj = j;
         float asg = 1.f;
         if (copy > 0) {  // the copy's action and mirror target: signed permutation of the original's columns
@@ -441,18 +507,19 @@ __global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoL
           const float dm = mu[k] - mt[k];
           sym += dm * dm;
         }
-        act[k] = asg * a.st_actions[static_cast<size_t>(src) * a.A + aj];
-        const float z = (act[k] - mu[k]) / sd[k];
-        const float lsd = logf(sd[k]);
+        act[k] = kSym ? asg * a.st_actions[static_cast<size_t>(src) * a.A + aj] : pf_act[pr][k];
+        const float z = (act[k] - mu[k]) * isd[k];
         lp += -0.5f * z * z - lsd - kLogSqrt2Pi;
         if (copy == 0) {
           const size_t so = static_cast<size_t>(src) * a.A + j;
-          const float omu = a.st_mean[so], osd = a.st_std[so];
+          const float omu = kSym ? a.st_mean[so] : pf_omu[pr][k];
+          const float osd = kSym ? a.st_std[so] : pf_osd[pr][k];
           ent += 0.5f + kLogSqrt2Pi + lsd;
-          // KL(old || new) for diagonal Gaussians
-          const float vr = (osd / sd[k]) * (osd / sd[k]);
-          const float t1 = ((omu - mu[k]) / sd[k]) * ((omu - mu[k]) / sd[k]);
-          kl += 0.5f * (vr + t1 - 1.0f - logf(vr));
+          // KL(old || new) for diagonal Gaussians; only compared against the adaptive-LR thresholds, so the fast
+          // logarithm suffices: log(vr) = 2 log(osd / sd)
+          const float r = osd * isd[k];
+          const float t1 = (omu - mu[k]) * isd[k];
+          kl += 0.5f * (r * r + t1 * t1 - 1.0f) - __logf(r);
         }
       }
     }
@@ -465,9 +532,10 @@ __global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoL
     }
     float d_lp = 0.f, dv = 0.f, surr = 0.f, vloss = 0.f;
     if (ppo_row) {
+      const int pr = kSym ? 0 : rr;
       // surrogate (identical on every lane)
-      const float adv = a.adv_override ? a.adv_override[o] : a.st_adv[src];
-      const float ratio = expf(lp - a.st_logp[src]);
+      const float adv = kSym ? (a.adv_override ? a.adv_override[o] : a.st_adv[src]) : pf_adv[pr];
+      const float ratio = expf(lp - (kSym ? a.st_logp[src] : pf_lp[pr]));
       const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
       const float rc = fminf(fmaxf(ratio, lo), hi);
       const float s1 = -adv * ratio, s2 = -adv * rc;
@@ -478,9 +546,9 @@ __global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoL
       d_lp = d_ratio * ratio;
       surr = fmaxf(s1, s2);
       // value loss
-      const float v = a.value[static_cast<size_t>(i) * a.ld_value];
-      const float ret = a.st_ret[src];
-      const float vold = a.st_val[src];
+      const float v = kSym ? a.value[static_cast<size_t>(i) * a.ld_value] : pf_v[pr];
+      const float ret = kSym ? a.st_ret[src] : pf_ret[pr];
+      const float vold = kSym ? a.st_val[src] : pf_vold[pr];
       if (a.clipped_value) {
         const float dvv = v - vold;
         const float vc = vold + fminf(fmaxf(dvv, -a.clip), a.clip);
@@ -504,10 +572,10 @@ __global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoL
     for (int k = 0; k < 2; ++k) {
       const int j = lane + 32 * k;
       if (j < a.A) {
-        const float inv_var = 1.0f / (sd[k] * sd[k]);
+        const float inv_var = isd[k] * isd[k];
         const float diff = act[k] - mu[k];
         const float dmu = d_lp * diff * inv_var + mir_w * (mu[k] - mt[k]);
-        const float dsd = d_lp * (diff * diff * inv_var / sd[k] - 1.0f / sd[k]) - ent_w / sd[k];
+        const float dsd = (d_lp * (diff * diff * inv_var - 1.0f) - ent_w) * isd[k];
         // chain through the std parameterisation (clamp passes the gradient on [lo, hi] inclusive)
         float dsd_raw;
         if (a.log_std) {
@@ -545,6 +613,7 @@ __global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoL
       acc_sym += sym * invM;
     }
   }
+  }  // row groups
   // ---- block reduction in fixed warp order ----
   __shared__ float sh_dh[kLossWarps][4][32];
   __shared__ float sh_dstd[kLossWarps][2][32];
@@ -603,9 +672,10 @@ __global__ void __launch_bounds__(kMseWarps * 32) mse_grad_kernel(const MseArgs 
   const float inv_n = 1.0f / (static_cast<float>(a.rows) * static_cast<float>(a.A));
   float col[2] = {0.f, 0.f};
   float loss = 0.f;
-  const int row0 = blockIdx.x * kMseRowsPerBlock + warp * kMseRowsPerWarp;
+  const int ngroups = (a.rows + kMseRowsPerBlock - 1) / kMseRowsPerBlock;
+  for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x)
   for (int r = 0; r < kMseRowsPerWarp; ++r) {
-    const int i = row0 + r;
+    const int i = grp * kMseRowsPerBlock + warp * kMseRowsPerWarp + r;
     if (i >= a.rows) break;
     __nv_bfloat16* g = static_cast<__nv_bfloat16*>(a.grad) + static_cast<size_t>(i) * a.ld_grad;
 #pragma unroll
@@ -1111,7 +1181,10 @@ cudaError_t gather_minibatch(const GatherArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-int ppo_loss_blocks(int B) { return (B + kLossRowsPerBlock - 1) / kLossRowsPerBlock; }
+int ppo_loss_blocks(int B) {
+  const int groups = (B + kLossRowsPerBlock - 1) / kLossRowsPerBlock;
+  return groups < kLossGridCap ? groups : kLossGridCap;
+}
 
 cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
   if (a.A > kLossMaxA || a.B <= 0) return cudaErrorInvalidValue;
@@ -1157,7 +1230,10 @@ cudaError_t rnd_intrinsic(const float* target, int ld_target, const float* pred,
   return cudaGetLastError();
 }
 
-int mse_blocks(int rows) { return (rows + kMseRowsPerBlock - 1) / kMseRowsPerBlock; }
+int mse_blocks(int rows) {
+  const int groups = (rows + kMseRowsPerBlock - 1) / kMseRowsPerBlock;
+  return groups < 4 * 148 ? groups : 4 * 148;
+}
 
 cudaError_t mse_grad(const MseArgs& a, cudaStream_t s) {
   if (a.A > 64 || a.rows <= 0 || a.ld_grad > 64 || a.head_cols > 64 || a.head_cols < a.A || a.ld_grad < a.A)

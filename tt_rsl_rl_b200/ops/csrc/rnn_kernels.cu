@@ -143,16 +143,18 @@ __global__ void __launch_bounds__(kBwdThreads) rnn_cell_bwd_kernel(const RnnCell
   for (int k = 0; k < kMaxColIter; ++k) {
     const int j = threadIdx.x + k * kBwdThreads;
     if (j >= H) break;
+    // one partial row per block, accumulated over the steps of a BPTT sweep (steps run in stream order)
+    auto put = [&](float* o, float v) { *o = a.colsum_accumulate ? *o + v : v; };
     if (a.colsum_gi) {
       float* o = a.colsum_gi + blockIdx.x * GH;
-      for (int g = 0; g < G; ++g) o[g * H + j] = cs_gi[g][k];
+      for (int g = 0; g < G; ++g) put(o + g * H + j, cs_gi[g][k]);
     }
     if (a.colsum_gh) {
       float* o = a.colsum_gh + blockIdx.x * GH;
-      o[j] = cs_gi[0][k];
-      o[H + j] = cs_gi[1][k];
-      o[2 * H + j] = a.lstm ? cs_gi[2][k] : cs_ghn[k];
-      if (a.lstm) o[3 * H + j] = cs_gi[3][k];
+      put(o + j, cs_gi[0][k]);
+      put(o + H + j, cs_gi[1][k]);
+      put(o + 2 * H + j, a.lstm ? cs_gi[2][k] : cs_ghn[k]);
+      if (a.lstm) put(o + 3 * H + j, cs_gi[3][k]);
     }
   }
 }

@@ -69,6 +69,7 @@ struct RnnCellBwdArgs {
   long long ld_dc_prev;
   float* colsum_gi;  // [blocks, G*H] per-block column sums of dgi (bias gradient of b_ih), optional
   float* colsum_gh;  // [blocks, G*H] of dgh (GRU), optional
+  int colsum_accumulate;  // 1: add to the column sums (later steps of a BPTT sweep), 0: overwrite
 };
 
 // Rows handled by one block of the backward cell (the row count of its column-sum partials is ceil(rows / this)).
