@@ -35,7 +35,7 @@ def _mirror(dims: dict, A: int, seed: int = 0):
     return fn
 
 
-def _pair(env, T, hidden, M=4, E=2, rnd=False, sym=None):
+def _pair(env, T, hidden, M=4, E=2, rnd=False, sym=None, reward_norm=False):
     from tt_rsl_rl_b200.algorithms import PPO
     from tt_rsl_rl_b200.models import MLPModel
     from tt_rsl_rl_b200.storage import RolloutStorage
@@ -49,7 +49,8 @@ def _pair(env, T, hidden, M=4, E=2, rnd=False, sym=None):
     kw = dict(num_learning_epochs=E, num_mini_batches=M)
     if rnd:
         kw["rnd_cfg"] = {"num_states": obs["critic"].shape[1], "obs_groups": groups, "num_outputs": 16,
-                         "predictor_hidden_dims": [128, 64], "target_hidden_dims": [128, 64], "weight": 0.5}
+                         "predictor_hidden_dims": [128, 64], "target_hidden_dims": [128, 64], "weight": 0.5,
+                         "reward_normalization": reward_norm}
     if sym is not None:
         kw["symmetry_cfg"] = dict(sym, env=env)
     storage = RolloutStorage("rl", env.num_envs, T, obs, [env.num_actions], "cuda")
@@ -110,13 +111,15 @@ def test_engine_symmetry_matches_torch_path(aug, mirror):
     assert alg_e.learning_rate == pytest.approx(alg_t.learning_rate, rel=1e-6)
 
 
-def test_engine_rnd_matches_torch_path():
+@pytest.mark.parametrize("reward_norm", [False, True])
+def test_engine_rnd_matches_torch_path(reward_norm):
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv
 
     torch.manual_seed(1)
     T, N = 8, 1024
     env = LinearGaussianVecEnv(N, obs_dim=40, num_actions=10, privileged_dim=3, device="cuda")
-    alg_t, alg_e = _pair(env, T, [128, 64], rnd=True)
+    alg_t, alg_e = _pair(env, T, [128, 64], rnd=True, reward_norm=reward_norm)
+    norm_ref = copy.deepcopy(alg_t.rnd.reward_normalizer)
     # intrinsic reward of one fused step against the PyTorch networks on the same observations
     obs = env.get_observations()
     with torch.inference_mode():
@@ -124,7 +127,8 @@ def test_engine_rnd_matches_torch_path():
         obs2, rew, dones, extras = env.step(actions)
         alg_e.process_env_step(obs2, rew, dones, extras)
         s = obs2["critic"]
-        ref = torch.linalg.norm(alg_t.rnd.target(s) - alg_t.rnd.predictor(s), dim=1) * alg_t.rnd.initial_weight
+        raw = torch.linalg.norm(alg_t.rnd.target(s) - alg_t.rnd.predictor(s), dim=1)
+        ref = (norm_ref(raw) if reward_norm else raw) * alg_t.rnd.initial_weight
     torch.testing.assert_close(alg_e.engine.intrinsic, ref, rtol=3e-2, atol=3e-2 * ref.abs().mean().item())
     assert alg_e.rnd.update_counter == T  # the schedule advanced by one rollout
     alg_e.engine.t = 0

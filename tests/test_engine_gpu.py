@@ -48,14 +48,15 @@ def _collect(alg, env, T):
     return obs
 
 
-@pytest.mark.parametrize("hetero", [False, True])
-def test_engine_update_matches_torch_path(hetero):
+@pytest.mark.parametrize("hetero,per_mb", [(False, False), (True, False), (False, True)])
+def test_engine_update_matches_torch_path(hetero, per_mb):
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv
 
     torch.manual_seed(0)
     T, N = 8, 1024
     env = LinearGaussianVecEnv(N, obs_dim=48, num_actions=12, privileged_dim=3, device="cuda")
-    alg_t, alg_e = _algs(env, [256, 128, 64], T, hetero=hetero, num_learning_epochs=2, num_mini_batches=4)
+    alg_t, alg_e = _algs(env, [256, 128, 64], T, hetero=hetero, num_learning_epochs=2, num_mini_batches=4,
+                         normalize_advantage_per_mini_batch=per_mb)
     _collect(alg_t, env, T)
     # identical data and sample order for both paths
     st = alg_t.storage

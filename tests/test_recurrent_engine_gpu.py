@@ -32,8 +32,8 @@ def _sequence_means(actor, obs_seq, dones_seq, h0):
     return torch.stack(out)
 
 
-@pytest.mark.parametrize("rnn_type", ["gru", "lstm"])
-def test_recurrent_engine_matches_torch_path(rnn_type):
+@pytest.mark.parametrize("rnn_type,per_mb", [("gru", False), ("lstm", False), ("gru", True)])
+def test_recurrent_engine_matches_torch_path(rnn_type, per_mb):
     from tt_rsl_rl_b200.algorithms import PPO
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv
     from tt_rsl_rl_b200.storage import RolloutStorage
@@ -43,7 +43,7 @@ def test_recurrent_engine_matches_torch_path(rnn_type):
     env = LinearGaussianVecEnv(N, obs_dim=24, num_actions=8, privileged_dim=3, device="cuda", reset_prob=0.05)
     obs = env.get_observations()
     actor, critic = _models(obs, rnn_type)
-    kw = dict(num_learning_epochs=2, num_mini_batches=4)
+    kw = dict(num_learning_epochs=2, num_mini_batches=4, normalize_advantage_per_mini_batch=per_mb)
     storage = RolloutStorage("rl", N, T, obs, [env.num_actions], "cuda")
     alg_t = PPO(actor, critic, storage, device="cuda", b200_cfg={"engine": "torch"}, **kw)
     alg_e = PPO(copy.deepcopy(actor), copy.deepcopy(critic), None, device="cuda",

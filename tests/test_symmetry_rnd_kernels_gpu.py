@@ -137,5 +137,14 @@ def test_rnd_intrinsic_reward():
     p = torch.randn(5000, 16, device="cuda")
     w = torch.tensor([0.37, 9.0], device="cuda")
     out = torch.zeros(5000, device="cuda")
-    C().rnd_intrinsic(t, 16, p, 16, 5000, 16, w[0:1], out)
+    C().rnd_intrinsic(t, 16, p, 16, 5000, 16, w[0:1], out, None, 0.0)
     torch.testing.assert_close(out, 0.37 * torch.linalg.norm(t - p, dim=1), rtol=1e-5, atol=1e-6)
+    # normalised form: raw distance + discounted sum, then weight / std
+    disc = torch.full((5000,), 0.5, device="cuda")
+    C().rnd_intrinsic(t, 16, p, 16, 5000, 16, w[0:1], out, disc, 0.9)
+    raw = torch.linalg.norm(t - p, dim=1)
+    torch.testing.assert_close(out, raw, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(disc, 0.45 + raw, rtol=1e-5, atol=1e-6)
+    std = torch.tensor([2.5], device="cuda")
+    C().rnd_reward_scale(out, 5000, w[0:1], std)
+    torch.testing.assert_close(out, 0.37 * raw / 2.5, rtol=1e-5, atol=1e-6)

@@ -60,8 +60,10 @@ class EngineBase:
         dev = self.device
         if not hasattr(self, "colstats_partial"):
             self.colstats_partial, self.moments_local, self.moments_global = {}, {}, {}
-        self.stats_chunks = ext().colstats_chunks(rows)
-        self.colstats_partial[name] = torch.zeros(2 * self.stats_chunks * D, dtype=torch.float64, device=dev)
+        if not hasattr(self, "stats_chunks"):
+            self.stats_chunks = {}
+        self.stats_chunks[name] = ext().colstats_chunks(rows)
+        self.colstats_partial[name] = torch.zeros(2 * self.stats_chunks[name] * D, dtype=torch.float64, device=dev)
         self.moments_local[name] = torch.zeros(2 + 2 * D, dtype=torch.float64, device=dev)
         self.moments_global[name] = torch.zeros_like(self.moments_local[name])
 
@@ -78,11 +80,12 @@ class EngineBase:
         C.colstats(obs, rows, obs.stride(0), D, partial)
         until = -1 if norm.until is None else int(norm.until)
         mean, var, std = norm._mean.view(-1), norm._var.view(-1), norm._std.view(-1)
+        chunks = self.stats_chunks[name]
         if self.comm is None:
-            C.norm_update(partial, self.stats_chunks, rows, D, mean, var, std, norm.count, until, None, False)
+            C.norm_update(partial, chunks, rows, D, mean, var, std, norm.count, until, None, False)
             return
         local, glob = self.moments_local[name], self.moments_global[name]
-        C.norm_update(partial, self.stats_chunks, rows, D, mean, var, std, norm.count, until, local, True)
+        C.norm_update(partial, chunks, rows, D, mean, var, std, norm.count, until, local, True)
         self.comm.allreduce_f64(local, glob, self.status)
         C.norm_update(glob[2:], 1, rows * self.world, D, mean, var, std, norm.count, until, None, False)
 

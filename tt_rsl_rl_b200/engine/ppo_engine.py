@@ -43,8 +43,6 @@ _MAX_COPIES = 8
 
 
 def _rnd_reason(rnd) -> str | None:
-    if getattr(rnd, "reward_normalization", False):
-        return "RND reward normalisation runs on the PyTorch path"
     for name in ("predictor", "target"):
         reason = elu_stack_reason(getattr(rnd, name))
         if reason:
@@ -100,12 +98,8 @@ class PPOEngine(EngineBase):
             return "critic output is not scalar"
         rnd_cfg = alg_cfg.get("rnd_cfg")
         if isinstance(rnd_cfg, dict):
-            if rnd_cfg.get("reward_normalization", False):
-                return "RND reward normalisation runs on the PyTorch path"
             if str(rnd_cfg.get("activation", "elu")).lower() != "elu":
                 return "RND activation is not fused (ELU only)"
-        if alg_cfg.get("normalize_advantage_per_mini_batch"):
-            return "per-minibatch advantage normalisation runs on the PyTorch path"
         if str(alg_cfg.get("optimizer", "adam")).lower() != "adam":
             return "only Adam is fused"
         return None
@@ -308,6 +302,9 @@ class PPOEngine(EngineBase):
             self.rnd_colsum = torch.zeros(self.rnd_blocks, self.R, **f32)
             self.rnd_loss_acc = torch.zeros(1, **f32)
             self.rnd_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+            # reward normalisation: per-environment discounted sum of the raw intrinsic reward and its running std
+            self.rnd_reward_norm = bool(self.rnd.reward_normalization)
+            self.rnd_disc = torch.zeros(N, **f32) if self.rnd_reward_norm else None
 
         # ---- minibatch buffers ----
         B = self.B_max
@@ -320,6 +317,11 @@ class PPOEngine(EngineBase):
         self.dvalue_colsum = torch.zeros(self.loss_blocks, 1, **f32)
         self.dstd_partial = torch.zeros(self.loss_blocks, A, **f32)
         self.loss_acc = torch.zeros(_TAIL, **f32)
+        # normalize_advantage_per_mini_batch: the minibatch's advantages, normalised, replace the stored ones
+        self.adv_per_mb = bool(alg.normalize_advantage_per_mini_batch)
+        self.adv_mb = torch.zeros(B, **f32) if self.adv_per_mb else None
+        self.adv_mb_partial = (torch.zeros(2 * ext().adv_gather_blocks(B), dtype=torch.float64, device=dev)
+                               if self.adv_per_mb else None)
 
         # ---- gradient reduction plan (flat order = optimizer order) ----
         seg = {}
@@ -403,6 +405,8 @@ class PPOEngine(EngineBase):
         self._alloc_norm_scratch("critic", self.total, self.Dc)
         if self.rnd is not None:
             self._alloc_norm_scratch("rnd", self.total, self.Dr)
+            if self.rnd_reward_norm:
+                self._alloc_norm_scratch("rnd_reward", self.N, 1)
         self.use_graphs = bool(alg.b200_cfg["graphs"])
         self._update_graph = None
         self._updates_done = 0
@@ -495,8 +499,17 @@ class PPOEngine(EngineBase):
                    std_r, eps_r)
         pt.forward(pr.x_roll, pt.h_roll, self.N, self.rnd_tout_roll, self.R, self.status)
         pr.forward(pr.x_roll, pr.h_roll, self.N, self.rnd_pout_roll, self.R, self.status)
-        C.rnd_intrinsic(self.rnd_tout_roll, self.R, self.rnd_pout_roll, self.R, self.N, self.R,
-                        self.rnd_w[t : t + 1], self.intrinsic)
+        w = self.rnd_w[t : t + 1]
+        if not self.rnd_reward_norm:
+            C.rnd_intrinsic(self.rnd_tout_roll, self.R, self.rnd_pout_roll, self.R, self.N, self.R, w, self.intrinsic,
+                            None, 0.0)
+            return
+        # normalised: raw distance, discounted sum, running std of the sum (global over ranks), then weight / std
+        rn = self.rnd.reward_normalizer
+        C.rnd_intrinsic(self.rnd_tout_roll, self.R, self.rnd_pout_roll, self.R, self.N, self.R, w, self.intrinsic,
+                        self.rnd_disc, rn.disc_avg.gamma)
+        self._norm_module_update("rnd_reward", rn.emp_norm, rn.training, self.rnd_disc.view(self.N, 1), self.N, 1)
+        C.rnd_reward_scale(self.intrinsic, self.N, w, rn.emp_norm._std.view(-1))
 
     def compute_returns(self, obs) -> None:
         C = ext()
@@ -507,7 +520,7 @@ class PPOEngine(EngineBase):
         pc.forward(pc.x_roll, pc.h_roll, self.N, self.last_values.view(self.N, 1), 1, self.status)
         C.gae(self.st_rewards, self.st_dones, self.st_values, self.last_values, self.st_returns, self.st_adv, self.T,
               self.N, self.alg.gamma, self.alg.lam, self.gae_partial)
-        if self.total > 1:
+        if self.total > 1 and not self.adv_per_mb:
             C.adv_normalize(self.st_adv, self.gae_partial, ext().gae_blocks(self.N))
         self.t = 0
 
@@ -524,6 +537,15 @@ class PPOEngine(EngineBase):
             if used < self.rnd_blocks:
                 self.rnd_loss_partial[used:].zero_()
                 self.rnd_colsum[used:].zero_()
+
+    def _minibatch_advantages(self, idx: torch.Tensor, n: int):
+        """normalize_advantage_per_mini_batch: (adv[idx] - mean) / (std + 1e-8) over the minibatch, else None."""
+        if not self.adv_per_mb or n <= 1:
+            return None
+        C = ext()
+        C.adv_gather_stats(self.st_adv, idx, n, self.adv_mb, self.adv_mb_partial)
+        C.adv_normalize(self.adv_mb[:n], self.adv_mb_partial, C.adv_gather_blocks(n))
+        return self.adv_mb
 
     def _minibatch(self, i: int) -> None:
         C = ext()
@@ -559,6 +581,7 @@ class PPOEngine(EngineBase):
         idx_in = None if self.perm_override is None else self.perm_override[start : start + B]
         C.gather_minibatch(B, start, self.total, self.perm_key, self.half_bits, idx_in, self.idx, obs_l, mean_l, std_l,
                            eps, x_l, ld_l, self.status, self.K, rows_l, perm_l, sign_l)
+        adv_override = self._minibatch_advantages(self.idx, B)
         pa.forward(pa.x_train, pa.h_train, rows_a, pa.out_train, pa.out_train.shape[1], self.status)
         pc.forward(pc.x_train, pc.h_train, rows_c, self.value_train, 1, self.status)
         dist = self.actor.distribution
@@ -567,7 +590,7 @@ class PPOEngine(EngineBase):
         C.ppo_loss(B, self.A, self.hetero, self.log_std, pa.out_train, pa.out_train.shape[1], self.value_train, 1,
                    None if std_param is None else std_param.data, self.std_range[0], self.std_range[1],
                    self.log_std_range[0], self.log_std_range[1], self.idx, self.st_actions, self.st_mean, self.st_std,
-                   self.st_logp, self.st_adv, self.st_returns, self.st_values, None, alg.clip_param,
+                   self.st_logp, self.st_adv, self.st_returns, self.st_values, adv_override, alg.clip_param,
                    alg.value_loss_coef, alg.entropy_coef, alg.use_clipped_value_loss, pa.d_head, pa.d_head.shape[1],
                    self.d_value, self.d_value.shape[1], self.stats_partial, self.dhead_colsum, self.dvalue_colsum,
                    None if self.hetero else self.dstd_partial, self.K, self.aug, self.act_perm, self.act_sign,

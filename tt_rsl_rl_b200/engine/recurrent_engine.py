@@ -234,8 +234,6 @@ class RecurrentPPOEngine(EngineBase):
             return "critic output is not a scalar value"
         if alg_cfg.get("rnd_cfg"):
             return "RND with recurrent models runs on the PyTorch path"
-        if alg_cfg.get("normalize_advantage_per_mini_batch"):
-            return "per-minibatch advantage normalisation runs on the PyTorch path"
         if str(alg_cfg.get("optimizer", "adam")).lower() != "adam":
             return "only Adam is fused"
         return None
@@ -358,6 +356,10 @@ class RecurrentPPOEngine(EngineBase):
         self.dvalue_colsum = torch.zeros(self.loss_blocks, 1, **f32)
         self.dstd_partial = torch.zeros(self.loss_blocks, A, **f32)
         self.loss_acc = torch.zeros(_TAIL, **f32)
+        self.adv_per_mb = bool(alg.normalize_advantage_per_mini_batch)
+        self.adv_mb = torch.zeros(R_max, **f32) if self.adv_per_mb else None
+        self.adv_mb_partial = (torch.zeros(2 * C.adv_gather_blocks(R_max), dtype=torch.float64, device=dev)
+                               if self.adv_per_mb else None)
 
         # ---- gradient reduction plan ----
         seg = {}
@@ -489,7 +491,7 @@ class RecurrentPPOEngine(EngineBase):
         net.head.forward(net.hbf_scratch, net.head.h_roll, self.N, self.last_values.view(self.N, 1), 1, self.status)
         C.gae(self.st_rewards, self.st_dones, self.st_values, self.last_values, self.st_returns, self.st_adv, self.T,
               self.N, self.alg.gamma, self.alg.lam, self.gae_partial)
-        if self.total > 1:
+        if self.total > 1 and not self.adv_per_mb:
             C.adv_normalize(self.st_adv, self.gae_partial, C.gae_blocks(self.N))
         self.t = 0
 
@@ -508,10 +510,16 @@ class RecurrentPPOEngine(EngineBase):
         self.net_c.forward_sequence(lo, Be, self.st_dones, self.value_train, 1, self.status)
         std_param = self._std_param()
         alg = self.alg
+        adv_override = None
+        if self.adv_per_mb and R > 1:
+            C.adv_gather_stats(self.st_adv, self.mb_idx[i], R, self.adv_mb, self.adv_mb_partial)
+            C.adv_normalize(self.adv_mb[:R], self.adv_mb_partial, C.adv_gather_blocks(R))
+            adv_override = self.adv_mb
         C.ppo_loss(R, self.A, self.hetero, self.log_std, pa.out_train, pa.out_train.shape[1], self.value_train, 1,
                    None if std_param is None else std_param.data, self.std_range[0], self.std_range[1],
                    self.log_std_range[0], self.log_std_range[1], self.mb_idx[i], self.st_actions, self.st_mean,
-                   self.st_std, self.st_logp, self.st_adv, self.st_returns, self.st_values, None, alg.clip_param,
+                   self.st_std, self.st_logp, self.st_adv, self.st_returns, self.st_values, adv_override,
+                   alg.clip_param,
                    alg.value_loss_coef, alg.entropy_coef, alg.use_clipped_value_loss, pa.d_head, pa.d_head.shape[1],
                    self.d_value, self.d_value.shape[1], self.stats_partial, self.dhead_colsum, self.dvalue_colsum,
                    None if self.hetero else self.dstd_partial, 1, False, None, None, 0.0)

@@ -341,7 +341,7 @@ void reduce_segments(const Tensor& plan, int64_t nseg, int64_t chunks, const Ten
 }
 
 void rnd_intrinsic(const Tensor& target, int64_t ld_target, const Tensor& pred, int64_t ld_pred, int64_t rows,
-                   int64_t dim, const Tensor& weight, const Tensor& out) {
+                   int64_t dim, const Tensor& weight, const Tensor& out, const OptT& disc, double gamma) {
   check_f32(target, "target");
   check_f32(pred, "pred");
   check_f32(weight, "weight");
@@ -349,10 +349,35 @@ void rnd_intrinsic(const Tensor& target, int64_t ld_target, const Tensor& pred, 
   TORCH_CHECK(dim <= 64 && out.numel() >= rows && target.numel() >= (rows - 1) * ld_target + dim &&
                   pred.numel() >= (rows - 1) * ld_pred + dim,
               "rnd_intrinsic: sizes");
+  if (disc.has_value()) {
+    check_f32(*disc, "disc");
+    TORCH_CHECK(disc->numel() >= rows, "rnd_intrinsic: disc too small");
+  }
   ok(rlb::rnd_intrinsic(P<const float>(target), static_cast<int>(ld_target), P<const float>(pred),
                         static_cast<int>(ld_pred), static_cast<int>(rows), static_cast<int>(dim), P<const float>(weight),
-                        P<float>(out), cur()),
+                        P<float>(out), P<float>(disc), static_cast<float>(gamma), cur()),
      "rnd_intrinsic");
+}
+
+void rnd_reward_scale(const Tensor& out, int64_t rows, const Tensor& weight, const Tensor& std) {
+  check_f32(out, "out");
+  check_f32(weight, "weight");
+  check_f32(std, "std");
+  TORCH_CHECK(out.numel() >= rows, "rnd_reward_scale: out too small");
+  ok(rlb::rnd_reward_scale(P<float>(out), static_cast<int>(rows), P<const float>(weight), P<const float>(std), cur()),
+     "rnd_reward_scale");
+}
+
+int64_t adv_gather_blocks(int64_t n) { return rlb::adv_gather_blocks(n); }
+
+void adv_gather_stats(const Tensor& adv, const Tensor& idx, int64_t n, const Tensor& out, const Tensor& partial) {
+  check_f32(adv, "adv");
+  check_f32(out, "out");
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.numel() >= n && out.numel() >= n, "adv_gather_stats: sizes");
+  TORCH_CHECK(partial.scalar_type() == torch::kFloat64 && partial.numel() >= 2 * rlb::adv_gather_blocks(n),
+              "adv_gather_stats: partial must be float64 [2 * blocks]");
+  ok(rlb::adv_gather_stats(P<const float>(adv), P<const int>(idx), n, P<float>(out), P<double>(partial), cur()),
+     "adv_gather_stats");
 }
 
 int64_t mse_blocks(int64_t rows) { return rlb::mse_blocks(static_cast<int>(rows)); }
@@ -571,8 +596,11 @@ void rlb_register_kernels(pybind11::module& m) {
   m.def("make_reduce_plan", &make_reduce_plan);
   m.def("reduce_segments", &reduce_segments);
   m.def("mse_blocks", &mse_blocks);
+  m.def("adv_gather_blocks", &adv_gather_blocks);
+  m.def("adv_gather_stats", &adv_gather_stats);
   m.def("mse_grad", &mse_grad);
   m.def("rnd_intrinsic", &rnd_intrinsic);
+  m.def("rnd_reward_scale", &rnd_reward_scale);
   m.def("make_adam_plan", &make_adam_plan);
   m.def("adam_grid", &adam_grid);
   m.def("adam_step", &adam_step);

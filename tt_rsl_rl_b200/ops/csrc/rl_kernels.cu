@@ -244,6 +244,41 @@ __global__ void adv_normalize_kernel(float* adv, long long n, const double* part
     adv[i] = (adv[i] - mean) * inv;
 }
 
+constexpr int kAdvGatherBlocks = 148;
+
+__global__ void __launch_bounds__(256) adv_gather_stats_kernel(const float* __restrict__ adv,
+                                                                const int* __restrict__ idx, long long n,
+                                                                float* __restrict__ out, double* __restrict__ partial) {
+  __shared__ double red[2][8];
+  double s = 0.0, ss = 0.0;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float v = adv[idx[i]];
+    out[i] = v;
+    s += v;
+    ss += static_cast<double>(v) * v;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, off);
+    ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = s;
+    red[1][threadIdx.x >> 5] = ss;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ts = 0, tss = 0;
+    for (int w = 0; w < 8; ++w) {
+      ts += red[0][w];
+      tss += red[1][w];
+    }
+    partial[2 * blockIdx.x] = ts;
+    partial[2 * blockIdx.x + 1] = tss;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Feistel permutation of [0, n): 4-round balanced Feistel network on 2*half_bits bits with cycle walking. A bijection
 // of the padded domain restricted by cycle walking is a bijection of [0, n).
@@ -1181,6 +1216,18 @@ cudaError_t gather_minibatch(const GatherArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+int adv_gather_blocks(long long n) {
+  const long long b = (n + 255) / 256;
+  return static_cast<int>(b < kAdvGatherBlocks ? (b < 1 ? 1 : b) : kAdvGatherBlocks);
+}
+
+cudaError_t adv_gather_stats(const float* adv, const int* idx, long long n, float* out, double* partial,
+                             cudaStream_t s) {
+  if (n <= 0) return cudaErrorInvalidValue;
+  adv_gather_stats_kernel<<<adv_gather_blocks(n), 256, 0, s>>>(adv, idx, n, out, partial);
+  return cudaGetLastError();
+}
+
 int ppo_loss_blocks(int B) {
   const int groups = (B + kLossRowsPerBlock - 1) / kLossRowsPerBlock;
   return groups < kLossGridCap ? groups : kLossGridCap;
@@ -1207,9 +1254,10 @@ cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_c
 __global__ void __launch_bounds__(256) rnd_intrinsic_kernel(const float* __restrict__ target, int ld_target,
                                                             const float* __restrict__ pred, int ld_pred, int rows,
                                                             int dim, const float* __restrict__ weight,
-                                                            float* __restrict__ out) {
+                                                            float* __restrict__ out, float* __restrict__ disc,
+                                                            float gamma) {
   const int lane = threadIdx.x & 31;
-  const float w = *weight;
+  const float w = disc ? 1.0f : *weight;
   for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < rows; i += (gridDim.x * blockDim.x) >> 5) {
     float s = 0.f;
     for (int j = lane; j < dim; j += 32) {
@@ -1218,15 +1266,33 @@ __global__ void __launch_bounds__(256) rnd_intrinsic_kernel(const float* __restr
     }
 #pragma unroll
     for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (lane == 0) out[i] = w * sqrtf(s);
+    if (lane == 0) {
+      const float r = sqrtf(s);
+      out[i] = w * r;
+      if (disc) disc[i] = gamma * disc[i] + r;
+    }
   }
 }
 
+__global__ void __launch_bounds__(256) rnd_reward_scale_kernel(float* __restrict__ out, int rows,
+                                                               const float* __restrict__ weight,
+                                                               const float* __restrict__ std) {
+  const float sd = *std;
+  const float f = *weight / (sd > 0.f ? sd : 1.0f);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) out[i] *= f;
+}
+
 cudaError_t rnd_intrinsic(const float* target, int ld_target, const float* pred, int ld_pred, int rows, int dim,
-                          const float* weight, float* out, cudaStream_t s) {
+                          const float* weight, float* out, float* disc, float gamma, cudaStream_t s) {
   if (rows <= 0 || dim <= 0) return cudaErrorInvalidValue;
   rnd_intrinsic_kernel<<<grid_for(rows, 8, 148 * 16), 256, 0, s>>>(target, ld_target, pred, ld_pred, rows, dim,
-                                                                    weight, out);
+                                                                    weight, out, disc, gamma);
+  return cudaGetLastError();
+}
+
+cudaError_t rnd_reward_scale(float* out, int rows, const float* weight, const float* std, cudaStream_t s) {
+  if (rows <= 0) return cudaErrorInvalidValue;
+  rnd_reward_scale_kernel<<<grid_for(rows, 256, 148 * 4), 256, 0, s>>>(out, rows, weight, std);
   return cudaGetLastError();
 }
 

@@ -83,6 +83,11 @@ int gae_blocks(int N);
 cudaError_t gae(const GaeArgs& a, cudaStream_t s);
 // advantages = (adv - mean) / (std_unbiased + 1e-8) over all T*N values; each block re-reduces `partial`.
 cudaError_t adv_normalize(float* adv, long long n, const double* partial, int parts, cudaStream_t s);
+// Per-minibatch advantages: out[i] = adv[idx[i]] with per-block (sum, sum of squares) partials in fp64, the input of
+// adv_normalize (normalize_advantage_per_mini_batch). Returns the partial count through *parts.
+int adv_gather_blocks(long long n);
+cudaError_t adv_gather_stats(const float* adv, const int* idx, long long n, float* out, double* partial,
+                             cudaStream_t s);
 
 constexpr int kGatherModels = 3;
 // Minibatch gather: for rows i in [0, B) take storage row idx = perm(offset + i) (Feistel bijection of [0, total) keyed
@@ -192,9 +197,13 @@ struct MseArgs {
 };
 int mse_blocks(int rows);
 
-// RND intrinsic reward: out[i] = weight[step] * || target[i] - pred[i] ||_2 over dim columns.
+// RND intrinsic reward: out[i] = weight[step] * || target[i] - pred[i] ||_2 over dim columns. With reward
+// normalisation (disc != null) the kernel writes the unweighted distance and advances the per-environment discounted
+// sum disc[i] = gamma * disc[i] + out[i]; rnd_reward_scale then applies out[i] = weight * out[i] / std once the running
+// std of that sum has been updated (rsl_rl/modules/normalization.py EmpiricalDiscountedVariationNormalization).
 cudaError_t rnd_intrinsic(const float* target, int ld_target, const float* pred, int ld_pred, int rows, int dim,
-                          const float* weight, float* out, cudaStream_t s);
+                          const float* weight, float* out, float* disc, float gamma, cudaStream_t s);
+cudaError_t rnd_reward_scale(float* out, int rows, const float* weight, const float* std, cudaStream_t s);
 cudaError_t mse_grad(const MseArgs& a, cudaStream_t s);
 constexpr int kReduceChunk = 32;  // columns per block of the reduction kernel
 
