@@ -231,6 +231,45 @@ def test_gloo_replicas_stay_identical_only_with_reduction(reduce):
     assert same == reduce
 
 
+def _replica_worker(rank, world, port, out_dir, reduce):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "WORLD_SIZE": str(world),
+                       "RANK": str(rank), "LOCAL_RANK": str(rank)})
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from helpers import ppo_cfg as cfg_fn
+    from helpers import small_env as env_fn
+
+    from tt_rsl_rl_b200.parallel import ReplicaDivergenceError
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    torch.manual_seed(rank)
+    cfg = cfg_fn()
+    cfg["algorithm"]["b200_cfg"] = {"replica_check_interval": 1}
+    runner = OnPolicyRunner(env_fn(seed=rank), cfg, log_dir=None, device="cpu")
+    if not reduce:
+        runner.alg.reduce_parameters = lambda: None  # replicas drift apart after the first update
+    try:
+        runner.learn(2)
+        result = "ok"
+    except ReplicaDivergenceError as e:
+        result = f"diverged: {e}"
+    with open(os.path.join(out_dir, f"r{rank}"), "w") as f:
+        f.write(result)
+    torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize("reduce", [True, False])
+def test_replica_check_detects_divergence_on_every_rank(reduce):
+    out = tempfile.mkdtemp()
+    torch.multiprocessing.spawn(_replica_worker, args=(2, _free_port(), out, reduce), nprocs=2, join=True)
+    res = [open(os.path.join(out, f"r{r}")).read() for r in range(2)]
+    if reduce:
+        assert res == ["ok", "ok"], res
+    else:
+        assert all(r.startswith("diverged") and "after update 1" in r for r in res), res
+
+
 # ---- host-side failure detection ---------------------------------------------------------------------------------------
 def _wd_worker(rank, port, out_dir):
     from datetime import timedelta

@@ -77,6 +77,9 @@ class Distillation:
             raise ValueError(f"Unknown loss type: {loss_type}. Supported types are: {list(losses)}")
         self.loss_fn = losses[loss_type]
         self.num_updates = 0
+        from ..parallel import ReplicaChecker
+
+        self._replica_checker = ReplicaChecker(self.b200_cfg["replica_check_interval"], self.gpu_world_size)
         self.engine = None
         if self.b200_cfg["engine"] != "torch" and torch.device(device).type == "cuda":
             from ..engine.distillation_engine import DistillationEngine
@@ -110,6 +113,11 @@ class Distillation:
         """Distillation needs no return targets."""
 
     def update(self) -> dict[str, float]:
+        out = self._update()
+        self._replica_checker.step(list(self.student.parameters()))
+        return out
+
+    def _update(self) -> dict[str, float]:
         self.num_updates += 1
         if self.engine is not None:
             loss_dict = self.engine.update()

@@ -116,6 +116,9 @@ class PPO:
         self.use_mixed_precision = use_mixed_precision
         self.intrinsic_rewards: torch.Tensor | None = None
         self._obs_template = obs_template
+        from ..parallel import ReplicaChecker
+
+        self._replica_checker = ReplicaChecker(self.b200_cfg["replica_check_interval"], self.gpu_world_size)
 
         self.engine = None
         if self._engine_requested():
@@ -204,6 +207,17 @@ class PPO:
 
     # ---- update ---------------------------------------------------------------------------------------------------------
     def update(self) -> dict[str, float]:
+        out = self._update()
+        self._replica_checker.step(self._replicated_parameters())
+        return out
+
+    def _replicated_parameters(self):
+        params = list(self.actor.parameters()) + list(self.critic.parameters())
+        if self.rnd:
+            params += list(self.rnd.predictor.parameters())
+        return params
+
+    def _update(self) -> dict[str, float]:
         if self.engine is not None:
             return self.engine.update()
         sums = {"value": 0.0, "surrogate": 0.0, "entropy": 0.0}

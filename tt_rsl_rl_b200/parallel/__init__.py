@@ -1,9 +1,10 @@
 """Data-parallel communication: the peer-to-peer gradient exchange used inside the fused Adam kernel, parameter
 broadcast and normaliser-statistics combine, with bounded device-side waits and host-side failure reporting."""
 
-from .errors import CommTimeoutError
+from .errors import CommTimeoutError, ReplicaDivergenceError
+from .replica import ReplicaChecker
 
-__all__ = ["CommTimeoutError", "PeerExchange"]
+__all__ = ["CommTimeoutError", "PeerExchange", "ReplicaChecker", "ReplicaDivergenceError"]
 
 
 def __getattr__(name):

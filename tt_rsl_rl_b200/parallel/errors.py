@@ -7,3 +7,7 @@ class CommTimeoutError(RuntimeError):
     The kernels record the first failing site in a status word and return instead of hanging; the host reads the word
     after each update and raises this error.
     """
+
+
+class ReplicaDivergenceError(RuntimeError):
+    """Data-parallel replicas no longer hold identical parameters (raised on every rank by the replica check)."""
