@@ -352,11 +352,18 @@ def main() -> None:
     if sampler:
         sampler.__enter__()
     counter = None
+    host_reads = None
     if args.impl == "ours":
         from tt_rsl_rl_b200.ops import count_launches
+        from tt_rsl_rl_b200.utils.timer import HostTransfers
 
         counter = count_launches()
+        HostTransfers.reset()
     s_per_iter = timed_learn(runner, args.steps, args.warmup, world, counter)
+    if args.impl == "ours":
+        snap = HostTransfers.snapshot()  # over warm-up + timed iterations
+        host_reads = {"calls_per_step": snap["calls"] / (args.steps + args.warmup),
+                      "bytes_per_step": snap["bytes"] / (args.steps + args.warmup)}
     if sampler:
         sampler.__exit__()
     samples = total_envs * T_STEPS
@@ -395,6 +402,7 @@ def main() -> None:
                        "l2": "inputs larger than L2 (rollout arena >> 126 MB)"},
             "e2e": e2e,
             "gpu_launches": launches,
+            "engine_host_reads": host_reads,
             "clocks": sampler.summary() if sampler else None,
         }
         if args.impl == "reference":

@@ -112,6 +112,34 @@ def test_runner_learn_logs_saves_and_exports(tmp_path):
         torch.testing.assert_close(jit(x), runner.get_inference_policy()({"policy": x}))
 
 
+def test_section_timer_and_runner_sections(tmp_path):
+    import time
+
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+    from tt_rsl_rl_b200.utils.timer import SectionTimer
+
+    t = SectionTimer(True, "cpu")
+    with t.section("a"):
+        time.sleep(0.01)
+    with t.section("a"):
+        time.sleep(0.01)
+    with t.section("b"):
+        pass
+    out = t.resolve()
+    assert set(out) == {"a", "b"} and out["a"] >= 15.0 and t.resolve() == {}
+    off = SectionTimer(False, "cpu")
+    with off.section("x"):
+        pass
+    assert off.resolve() == {}
+    cfg = ppo_cfg(b200_cfg={"section_timing": True})
+    cfg["logger"] = {"class_name": "CsvLogWriter"}
+    runner = OnPolicyRunner(small_env(), cfg, log_dir=str(tmp_path), device="cpu")
+    runner.learn(2)
+    assert set(runner.section_timer.totals) == {"rollout", "returns", "update"}
+    csv_text = open(os.path.join(str(tmp_path), "metrics.csv")).read()
+    assert "Perf/section_update_ms" in csv_text
+
+
 def test_runner_tensorboard_default(tmp_path):
     from tt_rsl_rl_b200.runners import OnPolicyRunner
 

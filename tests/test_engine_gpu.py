@@ -165,3 +165,28 @@ def test_runner_learn_and_checkpoint_roundtrip(tmp_path):
     with torch.no_grad():
         torch.testing.assert_close(runner.get_inference_policy()(probe), runner2.get_inference_policy()(probe))
     runner2.learn(1)
+
+
+def test_engine_host_reads_per_iteration_are_few_and_small():
+    """The fused path reads only small status/statistics tensors back per iteration (no rollout-sized transfers)."""
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+    from tt_rsl_rl_b200.utils.timer import HostTransfers
+
+    cfg = {
+        "num_steps_per_env": 8, "save_interval": 100, "obs_groups": {"actor": ["policy"], "critic": ["critic"]},
+        "algorithm": {"class_name": "PPO", "num_learning_epochs": 2, "num_mini_batches": 2,
+                      "b200_cfg": {"engine": "cuda", "section_timing": True}},
+        "actor": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True,
+                  "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 1.0}},
+        "critic": {"class_name": "MLPModel", "hidden_dims": [64, 64], "obs_normalization": True},
+    }
+    env = LinearGaussianVecEnv(4096, obs_dim=48, num_actions=12, privileged_dim=3, device="cuda")
+    runner = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    runner.learn(2)  # eager + capture
+    HostTransfers.reset()
+    runner.learn(3)  # graph replays
+    snap = HostTransfers.snapshot()
+    assert snap["calls"] <= 3 * 5, dict(HostTransfers.calls)
+    assert snap["bytes"] <= 3 * 64, dict(HostTransfers.nbytes)
+    assert set(runner.section_timer.totals) == {"rollout", "returns", "update"}

@@ -8,6 +8,7 @@ import torch.nn as nn
 
 from ..modules import EmpiricalNormalization
 from ..ops import ext
+from ..utils.timer import HostTransfers
 
 
 def elu_mlp_reason(model) -> str | None:
@@ -102,7 +103,7 @@ class EngineBase:
         return g
 
     def _check_status(self) -> None:
-        st = self.status.tolist()
+        st = HostTransfers.read(self.status, "status")
         if st[0] != 0:
             self.status.zero_()
             from ..parallel import CommTimeoutError
@@ -113,7 +114,7 @@ class EngineBase:
         """Non-finite rewards are flagged on the device by ``process_step``; nothing to do per step."""
 
     def raise_if_nonfinite(self) -> None:
-        if int(self.nonfinite.item()) != 0:
+        if int(HostTransfers.read(self.nonfinite, "nonfinite")[0]) != 0:
             self.nonfinite.zero_()
             raise ValueError("The rewards returned by the environment contain NaN or Inf values.")
 

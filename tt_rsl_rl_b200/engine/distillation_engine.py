@@ -25,6 +25,7 @@ import torch
 
 from ..modules import GaussianDistribution, HeteroscedasticGaussianDistribution
 from ..ops import ext
+from ..utils.timer import HostTransfers
 from .base import EngineBase, elu_mlp_reason
 from .mlp_plan import MLPPlan, pad8
 
@@ -192,7 +193,7 @@ class DistillationEngine(EngineBase):
 
     # ---- learning rate / logging ---------------------------------------------------------------------------------------
     def learning_rate(self) -> float:
-        return float(self.lr[0].item())
+        return float(HostTransfers.read(self.lr[0:1], "learning_rate")[0])
 
     def action_std(self) -> torch.Tensor:
         if self.s_dist is None:
@@ -280,7 +281,7 @@ class DistillationEngine(EngineBase):
             self._update_body()
         self._updates_done += 1
         self.t = 0
-        loss = float(self.loss_acc.item()) / float(self.E * self.T)
+        loss = float(HostTransfers.read(self.loss_acc, "loss_stats")[0]) / float(self.E * self.T)
         self._check_status()
         return {"behavior": loss}
 

@@ -32,6 +32,7 @@ import torch.nn as nn
 
 from ..modules import GaussianDistribution, HeteroscedasticGaussianDistribution
 from ..ops import ext
+from ..utils.timer import HostTransfers
 from .base import EngineBase, elu_mlp_reason, elu_stack_reason
 from .mlp_plan import MLPPlan, pad8
 
@@ -415,7 +416,7 @@ class PPOEngine(EngineBase):
 
     # ---- learning rate -----------------------------------------------------------------------------------------------
     def learning_rate(self) -> float:
-        return float(self.lr[0].item())
+        return float(HostTransfers.read(self.lr[0:1], "learning_rate")[0])
 
     def set_learning_rate(self, value: float) -> None:
         self.lr[0].fill_(value)
@@ -645,11 +646,11 @@ class PPOEngine(EngineBase):
             self._update_body()
         self._updates_done += 1
         n = float(self.E * self.M)
-        stats = (self.loss_acc / n).tolist()
+        stats = [v / n for v in HostTransfers.read(self.loss_acc, "loss_stats")]
         self._check_status()
         out = {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
         if self.rnd is not None:
-            out["rnd"] = float(self.rnd_loss_acc.item()) / n
+            out["rnd"] = float(HostTransfers.read(self.rnd_loss_acc, "rnd_loss")[0]) / n
         if self.sym is not None:
             out["symmetry"] = stats[4]
         return out

@@ -29,6 +29,7 @@ import torch.nn as nn
 from ..modules import GaussianDistribution, HeteroscedasticGaussianDistribution
 from ..ops import ext
 from ..ops import gemm as G
+from ..utils.timer import HostTransfers
 from .base import EngineBase, elu_mlp_reason
 from .mlp_plan import MLPPlan, pad8, wgrad_splits
 
@@ -424,7 +425,7 @@ class RecurrentPPOEngine(EngineBase):
 
     # ---- learning rate / logging ---------------------------------------------------------------------------------------
     def learning_rate(self) -> float:
-        return float(self.lr[0].item())
+        return float(HostTransfers.read(self.lr[0:1], "learning_rate")[0])
 
     def set_learning_rate(self, value: float) -> None:
         self.lr[0].fill_(value)
@@ -555,7 +556,7 @@ class RecurrentPPOEngine(EngineBase):
         else:
             self._update_body()
         self._updates_done += 1
-        stats = (self.loss_acc / float(self.E * self.M)).tolist()
+        stats = [v / float(self.E * self.M) for v in HostTransfers.read(self.loss_acc, "loss_stats")]
         self._check_status()
         return {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
 

@@ -39,6 +39,10 @@ class OnPolicyRunner:
         )
         self.current_learning_iteration = 0
         self._rollout_graph = None
+        from ..utils.timer import SectionTimer
+
+        b200 = self.alg.b200_cfg if hasattr(self.alg, "b200_cfg") else {}
+        self.section_timer = SectionTimer(b200.get("section_timing", False), self.device)
 
     # ---- training loop ------------------------------------------------------------------------------------------------
     def learn(self, num_learning_iterations: int, init_at_random_ep_len: bool = False) -> None:
@@ -54,14 +58,18 @@ class OnPolicyRunner:
         start_it = self.current_learning_iteration
         total_it = start_it + num_learning_iterations
         try:
+            timer = self.section_timer
             for it in range(start_it, total_it):
                 t0 = time.time()
                 with torch.inference_mode():
-                    obs = self.rollout(obs)
+                    with timer.section("rollout"):
+                        obs = self.rollout(obs)
                     t1 = time.time()
                     collect_time = t1 - t0
-                    self.alg.compute_returns(obs)
-                loss_dict = self.alg.update()
+                    with timer.section("returns"):
+                        self.alg.compute_returns(obs)
+                with timer.section("update"):
+                    loss_dict = self.alg.update()
                 learn_time = time.time() - t1
                 self.current_learning_iteration = it
                 self.logger.log(
@@ -69,6 +77,7 @@ class OnPolicyRunner:
                     loss_dict=loss_dict, learning_rate=self.alg.learning_rate,
                     action_std=self._action_std(),
                     rnd_weight=self.alg.rnd.weight if self.cfg["algorithm"].get("rnd_cfg") else None,
+                    sections=timer.resolve() if timer.enabled else None,
                 )
                 if self.logger.writer is not None and it % self.cfg["save_interval"] == 0:
                     self.save(os.path.join(self.logger.log_dir, f"model_{it}.pt"))

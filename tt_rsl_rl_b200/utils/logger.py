@@ -173,7 +173,7 @@ class Logger:
     # ---- per iteration -------------------------------------------------------------------------------------------------
     def log(self, it: int, start_it: int, total_it: int, collect_time: float, learn_time: float, loss_dict: dict,
             learning_rate: float, action_std: torch.Tensor, rnd_weight: float | None, print_minimal: bool = False,
-            width: int = 80, pad: int = 40) -> None:
+            width: int = 80, pad: int = 40, sections: dict[str, float] | None = None) -> None:
         if self.writer is None:
             return
         self._flush_finished()
@@ -203,6 +203,8 @@ class Logger:
         self.writer.add_scalar("Perf/total_fps", fps, it)
         self.writer.add_scalar("Perf/collection_time", collect_time, it)
         self.writer.add_scalar("Perf/learning_time", learn_time, it)
+        for name, ms in (sections or {}).items():
+            self.writer.add_scalar(f"Perf/section_{name}_ms", ms, it)
         if len(self.rewbuffer) > 0:
             if self.use_rnd:
                 self.writer.add_scalar("Rnd/mean_extrinsic_reward", statistics.mean(self.erewbuffer), it)
@@ -222,6 +224,8 @@ class Logger:
               f"""{"Steps per second:":>{pad}} {fps:.0f} \n"""
               f"""{"Collection time:":>{pad}} {collect_time:.3f}s \n"""
               f"""{"Learning time:":>{pad}} {learn_time:.3f}s \n""")
+        for name, ms in (sections or {}).items():
+            s += f"""{f"Section {name}:":>{pad}} {ms:.3f}ms\n"""
         for key, value in loss_dict.items():
             s += f"""{f"Mean {key} loss:":>{pad}} {value:.4f}\n"""
         if len(self.rewbuffer) > 0:
