@@ -1,0 +1,89 @@
+"""Remote environment bridge over ZeroMQ (loopback): equality with the local environment, error replies, timeouts,
+and a runner learning through the bridge."""
+
+import threading
+
+import pytest
+import torch
+
+zmq = pytest.importorskip("zmq")
+
+
+def _server(env):
+    from tt_rsl_rl_b200.env import EnvServer
+
+    srv = EnvServer(env, "tcp://127.0.0.1:*")
+    srv.serve_in_thread()
+    return srv
+
+
+def test_bridge_steps_equal_the_local_environment():
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv, RemoteVecEnv
+
+    local = LinearGaussianVecEnv(64, obs_dim=10, num_actions=3, privileged_dim=2, seed=4, reset_prob=0.1)
+    served = LinearGaussianVecEnv(64, obs_dim=10, num_actions=3, privileged_dim=2, seed=4, reset_prob=0.1)
+    srv = _server(served)
+    remote = RemoteVecEnv(srv.address, timeout_ms=5000)
+    assert (remote.num_envs, remote.num_actions) == (64, 3)
+    assert remote.groups == {"policy": [10], "critic": [12]}
+    torch.testing.assert_close(remote.get_observations()["critic"], local.get_observations()["critic"])
+    torch.manual_seed(0)
+    for _ in range(5):
+        a = torch.randn(64, 3)
+        torch.manual_seed(1)  # the environments draw their noise from the global generator
+        o1, r1, d1, e1 = local.step(a)
+        torch.manual_seed(1)
+        o2, r2, d2, e2 = remote.step(a)
+        torch.testing.assert_close(o2["policy"], o1["policy"])
+        torch.testing.assert_close(r2, r1)
+        torch.testing.assert_close(d2, d1.float())
+        torch.testing.assert_close(remote.episode_length_buf, local.episode_length_buf)
+        if "time_outs" in e1:
+            torch.testing.assert_close(e2["time_outs"], e1["time_outs"].float())
+    remote.close()
+
+
+def test_bridge_server_survives_handler_errors():
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv, RemoteEnvError, RemoteVecEnv
+
+    srv = _server(LinearGaussianVecEnv(8, obs_dim=4, num_actions=2))
+    remote = RemoteVecEnv(srv.address, timeout_ms=5000)
+    with pytest.raises(RemoteEnvError, match="actions must have shape"):
+        remote.step(torch.zeros(8, 5))
+    obs, rew, dones, _ = remote.step(torch.zeros(8, 2))  # still serving
+    assert rew.shape == (8,) and srv.errors == 1
+    remote.close()
+
+
+def test_bridge_client_times_out_instead_of_hanging():
+    import time
+
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv, RemoteEnvTimeoutError, RemoteVecEnv
+
+    srv = _server(LinearGaussianVecEnv(8, obs_dim=4, num_actions=2))
+    remote = RemoteVecEnv(srv.address, timeout_ms=3000)
+    srv.stop()  # the server goes away: no reply to the next request
+    time.sleep(0.3)
+    remote.timeout_ms = 500
+    remote.sock.close(0)
+    remote._connect()
+    t0 = time.monotonic()
+    with pytest.raises(RemoteEnvTimeoutError):
+        remote.step(torch.zeros(8, 2))
+    assert time.monotonic() - t0 < 3.0
+
+
+def test_runner_learns_through_the_bridge(tmp_path):
+    import copy
+
+    from helpers import ppo_cfg
+
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv, RemoteVecEnv
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    srv = _server(LinearGaussianVecEnv(32, obs_dim=6, num_actions=2, privileged_dim=1))
+    remote = RemoteVecEnv(srv.address, timeout_ms=5000)
+    runner = OnPolicyRunner(remote, copy.deepcopy(ppo_cfg(T=4)), log_dir=None, device="cpu")
+    runner.learn(2)
+    assert runner.current_learning_iteration == 1
+    remote.close()

@@ -1,0 +1,216 @@
+"""Remote environment bridge: run the learner here and the simulator in another process or on another host.
+
+Transport: ZeroMQ REQ/REP. A message is a multipart list ``[header, buffer_0, buffer_1, ...]``; ``header`` is UTF-8
+JSON ``{"op": ..., "tensors": [{"key": k, "dtype": d, "shape": s}, ...], ...}`` and ``buffer_i`` holds the raw
+little-endian bytes of tensor ``i`` (C order). Keys are ``"obs/<group>"``, ``"rewards"``, ``"dones"``,
+``"actions"``, ``"time_outs"``, ``"episode_length_buf"``; scalar logging extras travel in the header (``"log"``).
+
+Operations: ``info`` (sizes and groups), ``get_observations``, ``step`` (actions in, transition out), ``close``.
+A handler error is answered with ``{"op": "error", "message": ...}`` and the server keeps serving; the client turns it
+into :class:`RemoteEnvError`. A client whose request gets no reply within ``timeout_ms`` raises
+:class:`RemoteEnvTimeoutError` instead of hanging (and rebuilds its socket, as a REQ socket cannot send twice).
+
+The reference plugin's bridge has the same roles (``rsl_rl_tt/bridge/client.py:47-132``, ``server.py:62-154``).
+"""
+
+from __future__ import annotations
+
+import json
+import threading
+
+import numpy as np
+import torch
+
+from ..utils.tensordict import TensorDict
+from .vec_env import VecEnv
+
+_DTYPES = {"float32": torch.float32, "float64": torch.float64, "int64": torch.int64, "int32": torch.int32,
+           "uint8": torch.uint8, "bool": torch.bool}
+
+
+class RemoteEnvError(RuntimeError):
+    """The environment server answered a request with an error."""
+
+
+class RemoteEnvTimeoutError(TimeoutError):
+    """The environment server did not answer within the client's timeout."""
+
+
+def pack(header: dict, tensors: dict[str, torch.Tensor]) -> list[bytes]:
+    """Encode a header and named tensors as a multipart message."""
+    meta, frames = [], []
+    for key, t in tensors.items():
+        a = t.detach().to("cpu").contiguous()
+        meta.append({"key": key, "dtype": str(a.dtype).replace("torch.", ""), "shape": list(a.shape)})
+        frames.append(a.numpy().tobytes() if a.dtype != torch.bool else a.to(torch.uint8).numpy().tobytes())
+    return [json.dumps(dict(header, tensors=meta)).encode()] + frames
+
+
+def unpack(frames: list[bytes]) -> tuple[dict, dict[str, torch.Tensor]]:
+    """Decode a multipart message into its header and named CPU tensors."""
+    header = json.loads(frames[0].decode())
+    out = {}
+    for meta, buf in zip(header.get("tensors", []), frames[1:]):
+        dt = _DTYPES[meta["dtype"]]
+        np_dt = np.uint8 if dt == torch.bool else torch.empty(0, dtype=dt).numpy().dtype
+        arr = np.frombuffer(buf, dtype=np_dt).reshape(meta["shape"])
+        t = torch.from_numpy(arr.copy())
+        out[meta["key"]] = t.to(torch.bool) if dt == torch.bool else t
+    return header, out
+
+
+def _transition(env, obs, rewards=None, dones=None, extras=None) -> tuple[dict, dict]:
+    tensors = {f"obs/{g}": obs[g] for g in obs.keys()}
+    header = {"op": "ok"}
+    if rewards is not None:
+        tensors["rewards"] = rewards.reshape(-1).float()
+        tensors["dones"] = dones.reshape(-1).float()
+        tensors["episode_length_buf"] = env.episode_length_buf
+        extras = extras or {}
+        if "time_outs" in extras:
+            tensors["time_outs"] = extras["time_outs"].reshape(-1).float()
+        log = extras.get("log") or extras.get("episode") or {}
+        header["log"] = {k: float(v.float().mean()) if isinstance(v, torch.Tensor) else float(v) for k, v in log.items()}
+    return header, tensors
+
+
+class EnvServer:
+    """Serves a :class:`VecEnv` on a ZeroMQ REP socket until a ``close`` request (or :meth:`stop`)."""
+
+    def __init__(self, env, address: str = "tcp://127.0.0.1:5555", poll_ms: int = 100) -> None:
+        import zmq
+
+        self.env = env
+        self.ctx = zmq.Context.instance()
+        self.sock = self.ctx.socket(zmq.REP)
+        self.sock.setsockopt(zmq.LINGER, 0)
+        self.sock.bind(address)
+        self.address = self.sock.getsockopt_string(zmq.LAST_ENDPOINT)
+        self.poll_ms = poll_ms
+        self._stop = threading.Event()
+        self.errors = 0
+
+    def _handle(self, header: dict, tensors: dict) -> tuple[dict, dict]:
+        env, op = self.env, header.get("op")
+        if op == "info":
+            obs = env.get_observations()
+            groups = {g: list(obs[g].shape[1:]) for g in obs.keys()}
+            return {"op": "ok", "num_envs": env.num_envs, "num_actions": env.num_actions,
+                    "max_episode_length": int(env.max_episode_length), "groups": groups,
+                    "step_dt": float(getattr(env, "step_dt", 0.0))}, {}
+        if op == "get_observations":
+            return _transition(env, env.get_observations())
+        if op == "step":
+            actions = tensors["actions"]
+            if actions.shape != (env.num_envs, env.num_actions):
+                raise ValueError(f"actions must have shape {(env.num_envs, env.num_actions)}, got {tuple(actions.shape)}")
+            obs, rew, dones, extras = env.step(actions.to(env.device))
+            return _transition(env, obs, rew, dones, extras)
+        if op == "close":
+            self._stop.set()
+            return {"op": "ok"}, {}
+        raise ValueError(f"unknown op {op!r}")
+
+    def serve(self) -> None:
+        import zmq
+
+        poller = zmq.Poller()
+        poller.register(self.sock, zmq.POLLIN)
+        while not self._stop.is_set():
+            if not dict(poller.poll(self.poll_ms)):
+                continue
+            frames = self.sock.recv_multipart()
+            try:
+                header, tensors = unpack(frames)
+                reply = pack(*self._handle(header, tensors))
+            except Exception as exc:  # the server survives handler errors and reports them
+                self.errors += 1
+                reply = pack({"op": "error", "message": f"{type(exc).__name__}: {exc}"}, {})
+            self.sock.send_multipart(reply)
+        self.sock.close(0)
+
+    def serve_in_thread(self) -> threading.Thread:
+        th = threading.Thread(target=self.serve, daemon=True)
+        th.start()
+        return th
+
+    def stop(self) -> None:
+        self._stop.set()
+
+
+class RemoteVecEnv(VecEnv):
+    """A :class:`VecEnv` whose simulator runs behind an :class:`EnvServer`."""
+
+    def __init__(self, address: str, device: str | torch.device = "cpu", timeout_ms: int = 30000) -> None:
+        import zmq
+
+        self.address = address
+        self.device = torch.device(device)
+        self.timeout_ms = int(timeout_ms)
+        self._zmq = zmq
+        self.ctx = zmq.Context.instance()
+        self._connect()
+        info, _ = self._request({"op": "info"}, {})
+        self.num_envs = int(info["num_envs"])
+        self.num_actions = int(info["num_actions"])
+        self.max_episode_length = int(info["max_episode_length"])
+        self.step_dt = float(info.get("step_dt", 0.0))
+        self.groups = info["groups"]
+        self.episode_length_buf = torch.zeros(self.num_envs, dtype=torch.long, device=self.device)
+        self.cfg = {"address": address, "num_envs": self.num_envs}
+
+    @property
+    def unwrapped(self) -> RemoteVecEnv:
+        return self
+
+    def _connect(self) -> None:
+        zmq = self._zmq
+        self.sock = self.ctx.socket(zmq.REQ)
+        self.sock.setsockopt(zmq.LINGER, 0)
+        self.sock.setsockopt(zmq.RCVTIMEO, self.timeout_ms)
+        self.sock.setsockopt(zmq.SNDTIMEO, self.timeout_ms)
+        self.sock.connect(self.address)
+
+    def _request(self, header: dict, tensors: dict) -> tuple[dict, dict]:
+        zmq = self._zmq
+        try:
+            self.sock.send_multipart(pack(header, tensors))
+            frames = self.sock.recv_multipart()
+        except zmq.error.Again as exc:
+            # a REQ socket that missed its reply cannot send again: rebuild it before reporting
+            self.sock.close(0)
+            self._connect()
+            raise RemoteEnvTimeoutError(
+                f"environment server at {self.address} did not answer {header.get('op')!r} within {self.timeout_ms} ms"
+            ) from exc
+        reply, out = unpack(frames)
+        if reply.get("op") == "error":
+            raise RemoteEnvError(reply.get("message", "remote error"))
+        return reply, out
+
+    def _obs(self, tensors: dict) -> TensorDict:
+        groups = {k[4:]: v.to(self.device) for k, v in tensors.items() if k.startswith("obs/")}
+        return TensorDict(groups, batch_size=[self.num_envs], device=self.device)
+
+    def get_observations(self):
+        _, tensors = self._request({"op": "get_observations"}, {})
+        return self._obs(tensors)
+
+    def step(self, actions: torch.Tensor):
+        reply, t = self._request({"op": "step"}, {"actions": actions.float()})
+        obs = self._obs(t)
+        rewards = t["rewards"].to(self.device)
+        dones = t["dones"].to(self.device)
+        self.episode_length_buf.copy_(t["episode_length_buf"].to(self.device))
+        extras = {}
+        if "time_outs" in t:
+            extras["time_outs"] = t["time_outs"].to(self.device)
+        if reply.get("log"):
+            extras["log"] = {k: torch.tensor(v) for k, v in reply["log"].items()}
+        return obs, rewards, dones, extras
+
+    def close(self) -> None:
+        try:
+            self._request({"op": "close"}, {})
+        finally:
+            self.sock.close(0)
