@@ -335,3 +335,21 @@ def test_watchdog_reports_a_rank_that_left():
     assert res.startswith("timeout"), res
     assert "[1]" in res
     assert float(res.split()[1]) < 5.0
+
+
+def test_parity_report_metrics():
+    from tt_rsl_rl_b200.testing import Tol, assert_parity, compare
+
+    e = torch.linspace(-1, 1, 1001)
+    rep = compare(e.clone(), e)
+    assert rep.ok and rep.rel_fro == 0 and rep.max_ulp == 0 and rep.pcc == pytest.approx(1.0)
+    a = e.clone()
+    a[500] += 0.5  # one bad element
+    rep = compare(a, e, Tol(rel_fro=1e-3))
+    assert not rep.ok and rep.worst_index == (500,) and rep.max_abs == pytest.approx(0.5)
+    nxt = torch.nextafter(e, torch.full_like(e, 2.0))
+    assert compare(nxt, e).max_ulp == 1
+    bf = e.to(torch.bfloat16).float()
+    assert_parity(bf, e, "gemm_bf16", "bf16 rounding is within the bf16 GEMM tolerance")
+    with pytest.raises(AssertionError):
+        assert_parity(bf, e, "fp64_reduced", "but not within the fp64 one")

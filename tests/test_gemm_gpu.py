@@ -31,6 +31,10 @@ def test_forward_f32_bias(M, N, K):
     torch.cuda.synchronize()
     ref = _ref(x[:, :K], w[:, :K]) + bias
     torch.testing.assert_close(out, ref, atol=2e-3 * (K ** 0.5), rtol=1e-3)
+    # same bf16 operands on both sides: only the fp32 accumulation order differs
+    from tt_rsl_rl_b200.testing import assert_parity
+
+    assert_parity(out, ref, "fp32_elementwise", f"gemm fp32 epilogue {M}x{N}x{K}")
 
 
 @pytest.mark.parametrize("M,N,K", [(300, 512, 96), (1000, 256, 512), (129, 128, 256), (77, 40, 64)])
