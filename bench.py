@@ -230,12 +230,14 @@ def dist_info() -> tuple[int, int, int]:
                                                                                                       "0"))
 
 
-def make_env(num_envs: int, device: str, host_noise: bool, seed: int, **env_kw):
+def make_env(num_envs: int, device: str, host_noise: bool, seed: int, fused: bool = False, **env_kw):
+    """The benchmark environment. ``fused`` selects this framework's fused step kernel (the same transition); the
+    reference arm always gets the PyTorch-op step so that none of this framework's kernels run on its path."""
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv, humanoid_like
 
     if "obs_dim" in env_kw:  # config 0: the plain linear-Gaussian environment
-        return LinearGaussianVecEnv(num_envs, device=device, seed=seed, **env_kw)
-    return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise, **env_kw)
+        return LinearGaussianVecEnv(num_envs, device=device, seed=seed, fused=False, **env_kw)
+    return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise, fused=fused, **env_kw)
 
 
 def timed_learn_cpu(runner, steps: int, warmup: int) -> float:
@@ -346,7 +348,8 @@ def main() -> None:
     n_local = total_envs // world
     env_kw = conf["env"]
 
-    env = make_env(n_local, device, host_noise=False, seed=rank, **env_kw)
+    fused_env = args.impl == "ours"
+    env = make_env(n_local, device, host_noise=False, seed=rank, fused=fused_env, **env_kw)
     runner = build_runner(args.impl, env, device, args.config)
     sampler = ClockSampler([local_rank]) if local_rank == 0 else None
     if sampler:
@@ -371,7 +374,7 @@ def main() -> None:
 
     e2e = None
     if not args.no_e2e:
-        env2 = make_env(n_local, device, host_noise=True, seed=rank, **env_kw)
+        env2 = make_env(n_local, device, host_noise=True, seed=rank, fused=fused_env, **env_kw)
         runner2 = build_runner(args.impl, env2, device, args.config)
         e2e_s = timed_learn(runner2, args.steps, args.warmup, world)
         h2d = T_STEPS * n_local * 96 * 4
@@ -399,7 +402,9 @@ def main() -> None:
             "config": {"model": conf["desc"], "baseline_config": args.config,
                        "global_batch": samples, "seq_len": T_STEPS, "num_envs_total": total_envs,
                        "epochs": 5, "minibatches": 4, "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2 (rollout arena >> 126 MB)"},
+                       "l2": "inputs larger than L2 (rollout arena >> 126 MB)",
+                       "env_step": "fused sm_100a kernel after two cuBLAS matmuls" if fused_env
+                       else "PyTorch ops (cuBLAS matmuls + elementwise)"},
             "e2e": e2e,
             "gpu_launches": launches,
             "engine_host_reads": host_reads,

@@ -42,7 +42,7 @@ class LinearGaussianVecEnv(VecEnv):
     def __init__(self, num_envs: int, obs_dim: int = 48, num_actions: int = 12, privileged_dim: int = 0,
                  episode_length: int = 1000, reset_prob: float = 0.005, noise_std: float = 0.05, seed: int = 0,
                  device: str | torch.device = "cpu", host_noise: bool = False, host_noise_pool_steps: int = 8,
-                 step_dt: float = 0.02) -> None:
+                 step_dt: float = 0.02, fused: bool | None = None) -> None:
         self.num_envs = num_envs
         self.num_obs = obs_dim
         self.num_actions = num_actions
@@ -81,6 +81,15 @@ class LinearGaussianVecEnv(VecEnv):
             self._host_step = 0
         self._write_obs(torch.zeros(num_envs, num_actions, device=self.device))
         self._obs = self._make_obs_dict()
+        # fused device step (everything after the two matmuls in one kernel); None: on CUDA when the framework's
+        # extension is available. The PyTorch-op step below is the specification and the CPU path.
+        if fused is None:
+            fused = self.device.type == "cuda" and _extension_available()
+        self.fused = bool(fused)
+        if self.fused:
+            self._env_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
+            self._env_ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._env_seed = (seed * 0x9E3779B97F4A7C15 + 0x5851F42D4C957F2D) % (2**63)
 
     # ---- VecEnv -----------------------------------------------------------------------------------------------------
     @property
@@ -119,6 +128,8 @@ class LinearGaussianVecEnv(VecEnv):
 
     def step(self, actions: torch.Tensor):
         a = actions.to(self.device)
+        if self.fused:
+            return self._fused_step(a)
         self._draw_noise()
         # s' = A s + B a + sigma * eps
         torch.addmm(torch.mm(self.state, self.At), a, self.Bt, out=self._next)
@@ -141,6 +152,34 @@ class LinearGaussianVecEnv(VecEnv):
         self._write_obs(a)
         extras = {"time_outs": self.time_outs, "log": {"/state_norm": self.rewards}}
         return self._obs, self.rewards, self.dones, extras
+
+
+    def _fused_step(self, a: torch.Tensor):
+        """Same transition on the device: the matmuls on cuBLAS, the rest in one kernel with Philox noise."""
+        torch.addmm(torch.mm(self.state, self.At), a, self.Bt, out=self._next)
+        noise = None
+        if self.host_noise:
+            self._draw_noise()
+            noise = self._noise
+        from ..ops import ext
+
+        a = a if a.stride(1) == 1 else a.contiguous()
+        ext().lg_env_step(self._next, self.state, a, noise, self.noise_std, self.reset_prob,
+                                int(self.max_episode_length), self.episode_length_buf, self.rewards, self.dones,
+                                self.time_outs, self._policy_obs, self._critic_obs, self.privileged_dim,
+                                self._env_seed, self._env_counter, self._env_ticket)
+        extras = {"time_outs": self.time_outs, "log": {"/state_norm": self.rewards}}
+        return self._obs, self.rewards, self.dones, extras
+
+
+def _extension_available() -> bool:
+    try:
+        from ..ops import ext
+
+        ext()
+        return True
+    except Exception:  # pragma: no cover - depends on the build
+        return False
 
 
 def humanoid_like(num_envs: int, device: str | torch.device = "cpu", seed: int = 0, **kw) -> LinearGaussianVecEnv:

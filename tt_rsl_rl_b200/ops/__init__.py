@@ -17,9 +17,10 @@ _COUNTER: list[int] | None = None
 
 # Entry points that launch kernels (the rest are host-side planning, sizing and IPC helpers).
 LAUNCHING = frozenset({
-    "adam_step", "adv_gather_stats", "adv_normalize", "colstats", "counter_add", "gae", "gather_minibatch", "gaussian_sample", "gemm",
-    "mse_grad", "norm_update", "p2p_allreduce_f64", "p2p_broadcast_f32", "ppo_loss", "prep_obs", "process_step",
-    "reduce_segments", "rnd_intrinsic", "rnd_reward_scale", "rnn_cell_bwd", "rnn_cell_fwd", "rnn_mask", "to_bf16_padded",
+    "adam_step", "adv_gather_stats", "adv_normalize", "colstats", "counter_add", "gae", "gather_minibatch",
+    "gaussian_sample", "gemm", "lg_env_step", "mse_grad", "norm_update", "p2p_allreduce_f64", "p2p_broadcast_f32",
+    "ppo_loss", "prep_obs", "process_step", "reduce_segments", "rnd_intrinsic", "rnd_reward_scale", "rnn_cell_bwd",
+    "rnn_cell_fwd", "rnn_mask", "to_bf16_padded",
 })
 
 

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "kernels.cuh"
+#include "env_kernels.cuh"
 #include "rl_kernels.cuh"
 
 namespace {
@@ -368,6 +369,51 @@ void rnd_reward_scale(const Tensor& out, int64_t rows, const Tensor& weight, con
      "rnd_reward_scale");
 }
 
+void lg_env_step(const Tensor& next, const Tensor& state, const Tensor& actions, const OptT& noise, double noise_std,
+                 double reset_prob, int64_t max_len, const Tensor& ep_len, const Tensor& rewards, const Tensor& dones,
+                 const Tensor& time_outs, const Tensor& obs_policy, const OptT& obs_critic, int64_t priv, int64_t seed,
+                 const Tensor& counter, const Tensor& ticket) {
+  for (const Tensor* t : {&next, &state, &actions, &rewards, &dones, &time_outs, &obs_policy}) check_f32(*t, "env");
+  const int64_t N = state.size(0), S = state.size(1), A = actions.size(1);
+  TORCH_CHECK(next.is_contiguous() && state.is_contiguous() && obs_policy.is_contiguous() && actions.stride(1) == 1,
+              "lg_env_step: contiguous rows expected");
+  TORCH_CHECK(next.numel() == N * S && obs_policy.numel() == N * S && rewards.numel() == N && dones.numel() == N &&
+                  time_outs.numel() == N && ep_len.numel() == N && ep_len.scalar_type() == torch::kInt64,
+              "lg_env_step: sizes");
+  if (noise.has_value()) {
+    check_f32(*noise, "noise");
+    TORCH_CHECK(noise->is_contiguous() && noise->numel() == N * S, "lg_env_step: noise");
+  }
+  if (obs_critic.has_value()) {
+    check_f32(*obs_critic, "obs_critic");
+    TORCH_CHECK(obs_critic->is_contiguous() && obs_critic->numel() == N * (S + priv), "lg_env_step: critic obs");
+  }
+  TORCH_CHECK(counter.scalar_type() == torch::kInt64 && ticket.scalar_type() == torch::kInt32, "counter/ticket");
+  rlb::LgEnvArgs a{};
+  a.N = static_cast<int>(N);
+  a.S = static_cast<int>(S);
+  a.A = static_cast<int>(A);
+  a.P = static_cast<int>(priv);
+  a.next = P<const float>(next);
+  a.state = P<float>(state);
+  a.actions = P<const float>(actions);
+  a.ld_act = static_cast<int>(actions.stride(0));
+  a.noise = P<const float>(noise);
+  a.noise_std = static_cast<float>(noise_std);
+  a.reset_prob = static_cast<float>(reset_prob);
+  a.max_len = max_len;
+  a.ep_len = reinterpret_cast<long long*>(ep_len.data_ptr());
+  a.rewards = P<float>(rewards);
+  a.dones = P<float>(dones);
+  a.time_outs = P<float>(time_outs);
+  a.obs_policy = P<float>(obs_policy);
+  a.obs_critic = P<float>(obs_critic);
+  a.seed = static_cast<uint64_t>(seed);
+  a.counter = reinterpret_cast<uint64_t*>(counter.data_ptr());
+  a.ticket = reinterpret_cast<unsigned int*>(ticket.data_ptr());
+  ok(rlb::lg_env_step(a, cur()), "lg_env_step");
+}
+
 int64_t adv_gather_blocks(int64_t n) { return rlb::adv_gather_blocks(n); }
 
 void adv_gather_stats(const Tensor& adv, const Tensor& idx, int64_t n, const Tensor& out, const Tensor& partial) {
@@ -597,6 +643,7 @@ void rlb_register_kernels(pybind11::module& m) {
   m.def("reduce_segments", &reduce_segments);
   m.def("mse_blocks", &mse_blocks);
   m.def("adv_gather_blocks", &adv_gather_blocks);
+  m.def("lg_env_step", &lg_env_step);
   m.def("adv_gather_stats", &adv_gather_stats);
   m.def("mse_grad", &mse_grad);
   m.def("rnd_intrinsic", &rnd_intrinsic);
