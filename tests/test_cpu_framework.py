@@ -353,3 +353,82 @@ def test_parity_report_metrics():
     assert_parity(bf, e, "gemm_bf16", "bf16 rounding is within the bf16 GEMM tolerance")
     with pytest.raises(AssertionError):
         assert_parity(bf, e, "fp64_reduced", "but not within the fp64 one")
+
+
+@pytest.mark.parametrize("rnn_type", ["gru", "lstm"])
+def test_recurrent_minibatches_equal_a_done_masked_scan(rnn_type):
+    """Upstream's split-and-pad trajectory minibatches (re-run from the state stored at each trajectory start) compute
+    the same outputs as a time scan over the whole rollout whose input state is zeroed after every done: the basis of
+    the fused recurrent engine's layout."""
+    from tt_rsl_rl_b200.modules import RNN
+    from tt_rsl_rl_b200.utils.utils import split_and_pad_trajectories
+
+    torch.manual_seed(0)
+    T, N, D, H = 12, 7, 5, 8
+    rnn = RNN(D, H, 1, rnn_type)
+    obs = torch.randn(T, N, D)
+    dones = (torch.rand(T, N) < 0.2).float()
+    h0 = torch.randn(1, N, H)
+    c0 = torch.randn(1, N, H)
+    # scan with masked state
+    h, c = h0.clone(), c0.clone()
+    scan = []
+    with torch.no_grad():
+        for t in range(T):
+            if rnn_type == "gru":
+                out, h = rnn.rnn(obs[t : t + 1], h)
+            else:
+                out, (h, c) = rnn.rnn(obs[t : t + 1], (h, c))
+            scan.append(out[0])
+            keep = (1 - dones[t])[None, :, None]
+            h, c = h * keep, c * keep
+    scan = torch.stack(scan)
+    # trajectories: start state = rollout-start state for those starting at t = 0, reset (zero) state after a done
+    padded, masks = split_and_pad_trajectories(obs, dones.unsqueeze(-1))
+    starts = torch.zeros(T, N, dtype=torch.bool)
+    starts[0] = True
+    starts[1:] = dones[:-1].bool()
+    hs, cs = [], []
+    for n in range(N):  # trajectories are ordered env by env, then in time
+        for t in range(T):
+            if starts[t, n]:
+                hs.append(h0[0, n] if t == 0 else torch.zeros(H))
+                cs.append(c0[0, n] if t == 0 else torch.zeros(H))
+    hid = torch.stack(hs)[None]
+    state = hid if rnn_type == "gru" else (hid, torch.stack(cs)[None])
+    with torch.no_grad():
+        batched = rnn(padded, masks, state)
+    torch.testing.assert_close(batched, scan, rtol=1e-5, atol=1e-6)
+
+
+def test_normaliser_distributed_combine_with_a_fake_all_reduce(monkeypatch):
+    """The three-all-reduce combine (count, sum, spread around the global mean) equals the statistics of the union
+    of the ranks' batches; a second rank is simulated inside a fake ``all_reduce``."""
+    from tt_rsl_rl_b200.modules import EmpiricalNormalization
+
+    torch.manual_seed(1)
+    x = torch.randn(50, 4) * 2 + 1  # this rank
+    y = torch.randn(70, 4) - 3  # the simulated peer
+    calls = []
+    gmean = {}
+
+    def fake_all_reduce(t, op=None):
+        k = len(calls)
+        calls.append(k)
+        if k == 0:
+            t += len(y)
+        elif k == 1:
+            t += y.mean(0, keepdim=True) * len(y)
+            gmean["v"] = t / (len(x) + len(y))
+        else:
+            t += len(y) * (y.var(0, unbiased=False, keepdim=True) + (y.mean(0, keepdim=True) - gmean["v"]).square())
+
+    monkeypatch.setattr(torch.distributed, "is_initialized", lambda: True)
+    monkeypatch.setattr(torch.distributed, "all_reduce", fake_all_reduce)
+    norm = EmpiricalNormalization(4)
+    norm.train()
+    norm.update(x)
+    u = torch.cat([x, y])
+    assert len(calls) == 3 and int(norm.count) == 120
+    torch.testing.assert_close(norm._mean.squeeze(0), u.mean(0), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(norm._var.squeeze(0), u.var(0, unbiased=False), rtol=1e-5, atol=1e-6)
