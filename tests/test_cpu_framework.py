@@ -432,3 +432,70 @@ def test_normaliser_distributed_combine_with_a_fake_all_reduce(monkeypatch):
     assert len(calls) == 3 and int(norm.count) == 120
     torch.testing.assert_close(norm._mean.squeeze(0), u.mean(0), rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(norm._var.squeeze(0), u.var(0, unbiased=False), rtol=1e-5, atol=1e-6)
+
+
+# ---- N ranks vs 1 rank on the union minibatch ------------------------------------------------------------------------
+def _union_data(seed, N, T, D, A):
+    g = torch.Generator().manual_seed(seed)
+    return {
+        "obs": torch.randn(T, N, D, generator=g), "actions": torch.randn(T, N, A, generator=g),
+        "values": torch.randn(T, N, 1, generator=g), "mean": 0.1 * torch.randn(T, N, A, generator=g),
+        "returns": torch.randn(T, N, 1, generator=g), "advantages": torch.randn(T, N, 1, generator=g),
+    }
+
+
+def _union_alg(data, multi_gpu_cfg=None):
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.storage import RolloutStorage
+    from tt_rsl_rl_b200.utils.tensordict import TensorDict
+
+    T, N, D = data["obs"].shape
+    A = data["actions"].shape[2]
+    template = TensorDict({"policy": data["obs"][0]}, batch_size=[N])
+    groups = {"actor": ["policy"], "critic": ["policy"]}
+    torch.manual_seed(0)  # identical initial models everywhere
+    actor = MLPModel(template, groups, "actor", A, hidden_dims=[32, 32], obs_normalization=True,
+                     distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
+    critic = MLPModel(template, groups, "critic", 1, hidden_dims=[32, 32], obs_normalization=True)
+    st = RolloutStorage("rl", N, T, template, [A], "cpu")
+    dist = torch.distributions.Normal(data["mean"], torch.ones_like(data["mean"]))
+    logp = dist.log_prob(data["actions"]).sum(-1, keepdim=True)
+    for t in range(T):
+        tr = RolloutStorage.Transition()
+        tr.observations = TensorDict({"policy": data["obs"][t]}, batch_size=[N])
+        tr.actions, tr.values, tr.actions_log_prob = data["actions"][t], data["values"][t], logp[t]
+        tr.rewards, tr.dones = torch.zeros(N), torch.zeros(N)
+        tr.distribution_params = (data["mean"][t], torch.ones(N, A))
+        st.add_transition(tr)
+    st.returns.copy_(data["returns"])
+    st.advantages.copy_(data["advantages"])
+    return PPO(actor, critic, st, num_learning_epochs=1, num_mini_batches=1, device="cpu",
+               multi_gpu_cfg=multi_gpu_cfg, b200_cfg={"engine": "torch"})
+
+
+def _union_worker(rank, world, port, out_dir):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "WORLD_SIZE": str(world),
+                       "RANK": str(rank), "LOCAL_RANK": str(rank)})
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    alg = _union_alg(_union_data(10 + rank, 64, 6, 5, 3), {"global_rank": rank, "local_rank": rank,
+                                                            "world_size": world})
+    alg.update()
+    torch.save({"actor": alg.actor.state_dict(), "critic": alg.critic.state_dict(), "lr": alg.learning_rate},
+               os.path.join(out_dir, f"r{rank}.pt"))
+    torch.distributed.destroy_process_group()
+
+
+def test_two_ranks_equal_one_rank_on_the_union_minibatch():
+    out = tempfile.mkdtemp()
+    torch.multiprocessing.spawn(_union_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    parts = [_union_data(10 + r, 64, 6, 5, 3) for r in range(2)]
+    union = {k: torch.cat([parts[0][k], parts[1][k]], dim=1) for k in parts[0]}
+    alg = _union_alg(union)
+    alg.update()
+    for r in range(2):
+        got = torch.load(os.path.join(out, f"r{r}.pt"))
+        assert got["lr"] == pytest.approx(alg.learning_rate, rel=1e-6)
+        for name, model in (("actor", alg.actor), ("critic", alg.critic)):
+            for k, v in model.state_dict().items():
+                torch.testing.assert_close(got[name][k], v, rtol=1e-5, atol=1e-6, msg=f"rank {r} {name}.{k}")
