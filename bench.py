@@ -1,7 +1,7 @@
 #!/usr/bin/env python
-"""Benchmark: PPO training throughput (samples/s) of one learn() iteration on the BASELINE configuration.
+"""Benchmark: PPO training throughput (samples/s) of one learn() iteration on the headline configuration.
 
-Configuration: 65536 environments in total split evenly across ranks, synthetic
+Configuration 1 (the default): 65536 environments in total split evenly across ranks, synthetic
 linear-Gaussian environment (actor obs 96, critic obs 99, 29 actions), actor and critic MLPs [512, 256, 128] ELU with
 empirical observation normalisation, 24 steps per environment, 5 epochs x 4 minibatches, bf16 GEMM operands with fp32
 master weights and Adam. Data: synthetic, seeded; weights: random init.
@@ -35,10 +35,10 @@ sys.path.insert(0, HERE)
 
 TOTAL_ENVS = 65536
 T_STEPS = 24
-BASELINE_VALUE = None  # BASELINE.md publishes no NVIDIA number for this configuration
+BASELINE_VALUE = None  # no published number exists for this configuration (the reference ships no GPU results)
 
 
-# BASELINE.json configurations: (total envs or None, envs per GPU or None, env kwargs, description)
+# Benchmark configurations: (total envs or None, envs per GPU or None, env kwargs, description)
 CONFIGS = {
     "0": dict(total=1024, per_gpu=None, env={"obs_dim": 48, "num_actions": 12}, cpu=True,
               desc="single-process CPU PPO fp32: MLPs [512,256,128] ELU, obs 48, 12 actions, 1024 envs"),
@@ -309,8 +309,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--total-envs", type=int, default=None,
-                    help="environments over all ranks (default: the BASELINE configuration; smaller for profiling)")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="1", help="BASELINE.json configuration")
+                    help="environments over all ranks (default: the configuration's; smaller for profiling)")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="1", help="benchmark configuration")
     args = ap.parse_args()
     conf = CONFIGS[args.config]
     world, rank, local_rank = dist_info()
