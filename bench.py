@@ -279,10 +279,12 @@ def timed_learn(runner, steps: int, warmup: int, world: int, counter=None) -> fl
     return ms / 1000.0
 
 
-def build_runner(impl: str, env, device: str, config: str = "1"):
+def build_runner(impl: str, env, device: str, config: str = "1", sections: bool = False):
     cfg = train_cfg(impl, config)
     if config == "2":
         cfg = _apply_config_2(cfg)
+    if sections and impl == "ours":
+        cfg["algorithm"].setdefault("b200_cfg", {})["section_timing"] = True
     distill = config == "4a"
     if impl == "reference":
         if distill:
@@ -311,6 +313,8 @@ def main() -> None:
     ap.add_argument("--total-envs", type=int, default=None,
                     help="environments over all ranks (default: the configuration's; smaller for profiling)")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="1", help="benchmark configuration")
+    ap.add_argument("--sections", action="store_true",
+                    help="also report rollout / returns / update device milliseconds (CUDA events; ours only)")
     args = ap.parse_args()
     conf = CONFIGS[args.config]
     world, rank, local_rank = dist_info()
@@ -350,7 +354,7 @@ def main() -> None:
 
     fused_env = args.impl == "ours"
     env = make_env(n_local, device, host_noise=False, seed=rank, fused=fused_env, **env_kw)
-    runner = build_runner(args.impl, env, device, args.config)
+    runner = build_runner(args.impl, env, device, args.config, sections=args.sections)
     sampler = ClockSampler([local_rank]) if local_rank == 0 else None
     if sampler:
         sampler.__enter__()
@@ -383,6 +387,11 @@ def main() -> None:
                "input": "environment process noise copied from pinned host memory every env step"}
 
     launches = counter.n if counter is not None else None
+    sections = None
+    timer = getattr(runner, "section_timer", None)
+    if args.sections and timer is not None and timer.enabled:
+        n_it = args.steps + args.warmup
+        sections = {k: v / n_it for k, v in timer.totals.items()}  # ms per iteration, warm-up included
 
     if rank == 0:
         line = {
@@ -408,6 +417,7 @@ def main() -> None:
             "e2e": e2e,
             "gpu_launches": launches,
             "engine_host_reads": host_reads,
+            "sections_ms": sections,
             "clocks": sampler.summary() if sampler else None,
         }
         if args.impl == "reference":
