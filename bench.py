@@ -259,6 +259,9 @@ def timed_learn(runner, steps: int, warmup: int, world: int, counter=None) -> fl
             runner.learn(1)
         warmup -= 1
     runner.learn(warmup)
+    timer = getattr(runner, "section_timer", None)
+    if timer is not None:
+        timer.totals.clear()  # section times of the timed iterations only (capture iterations bracket host time)
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -390,8 +393,7 @@ def main() -> None:
     sections = None
     timer = getattr(runner, "section_timer", None)
     if args.sections and timer is not None and timer.enabled:
-        n_it = args.steps + args.warmup
-        sections = {k: v / n_it for k, v in timer.totals.items()}  # ms per iteration, warm-up included
+        sections = {k: v / args.steps for k, v in timer.totals.items()}  # ms per timed iteration
 
     if rank == 0:
         line = {
