@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_tcgen05.cuh"
@@ -32,8 +33,6 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle atom row
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMNBoxBytes = 64 * kBK * 2;  // one {64 MN x 64 K} box
 constexpr int kEpiBufBytes = 32 * 32 * 2;  // one epilogue step: 32 rows x 32 bf16 columns (64-byte rows)
@@ -47,9 +46,19 @@ struct CtasPerSm {
   static constexpr int value = (EPI == kEpiDgradElu || EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16) ? 2 : 1;
 };
 
-template <int BN, int EPI>
+// WIDE: one CTA per SM with 16 epilogue warps (four per TMEM lane quadrant) and the whole shared memory for a deeper
+// operand ring; otherwise CtasPerSm CTAs with 8 epilogue warps each.
+template <int EPI, bool WIDE>
+struct Shape {
+  static constexpr int kMinBlocks = WIDE ? 1 : CtasPerSm<EPI>::value;
+  static constexpr int kEpiWarps = WIDE ? 16 : 8;
+  static constexpr int kThreads = 64 + kEpiWarps * 32;
+};
+
+template <int BN, int EPI, bool WIDE>
 struct Cfg {
-  static constexpr int kMinBlocks = CtasPerSm<EPI>::value;
+  static constexpr int kMinBlocks = Shape<EPI, WIDE>::kMinBlocks;
+  static constexpr int kEpiWarps = Shape<EPI, WIDE>::kEpiWarps;
   static constexpr int kSmemBudget = kMinBlocks == 1 ? kSmemLimit : (228 * 1024) / 2 - 1024;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -85,13 +94,15 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int n_tiles, int m_tiles
   return c;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
+template <int BN, bool A_MN, bool B_MN, int EPI, bool WIDE>
+__global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::kMinBlocks)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmX,
                    const GemmParams p, int num_kb, int n_tiles, int m_tiles, int splits) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, WIDE>;
   constexpr int S = C::kStages;
+  constexpr int kEpiWarps = C::kEpiWarps;
+  constexpr int kPerQuad = kEpiWarps / 4;  // epilogue warps sharing a TMEM lane quadrant
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -232,21 +243,21 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
     // ---------------- bf16-output epilogue (warps 2..9), 32 x 32 steps through two swizzled buffers -------------
     const int ew = warp - 2;
     const int q = warp & 3;  // TMEM lane quadrant: hardware rule warp % 4
-    const int half = ew >> 2;
+    const int slot = ew >> 2;  // this warp takes the quadrant's 32-column steps slot, slot + kPerQuad, ...
     uint8_t* ebuf = staging + ew * 2 * kEpiBufBytes;
     float* bias_s = bias_smem + ew * 32;
     uint64_t* xbar = aux_bar + 2 * ew;
     // 64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3); each thread owns row `lane`
     const int swz = (lane >> 1) & 3;
     // next (tile, 32-column step) of this warp whose aux tile is still to be loaded (data-gradient epilogue)
-    int pt = blockIdx.x, psc = half;
+    int pt = blockIdx.x, psc = slot;
     int issued = 0, consumed = 0;
     auto seek = [&](int& t, int& sc) {
       while (t < num_tiles) {
         const int n0 = (t % n_tiles) * BN;
         if (sc * 32 < BN && n0 + sc * 32 < p.N) return;
         t += gridDim.x;
-        sc = half;
+        sc = slot;
       }
     };
     auto issue_aux = [&]() {  // lane 0 only
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
       mbar_arrive_expect_tx(&xbar[issued & 1], kEpiBufBytes);
       tma_load_2d(dst, &tmX, &xbar[issued & 1], pc.n0 + psc * 32, pc.m0 + q * 32);
       ++issued;
-      psc += 2;
+      psc += kPerQuad;
       seek(pt, psc);
     };
     if constexpr (EPI == kEpiDgradElu) {
@@ -288,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
       const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
       float* cs = colsum_s + b * 4 * BN;
 #pragma unroll 1
-      for (int sc = half; !failed && sc * 32 < BN && tc.n0 + sc * 32 < p.N; sc += 2, ++consumed) {
+      for (int sc = slot; !failed && sc * 32 < BN && tc.n0 + sc * 32 < p.N; sc += kPerQuad, ++consumed) {
         const int sb = tc.n0 + sc * 32;
         uint8_t* buf = ebuf + (consumed & 1) * kEpiBufBytes;
         float v[32];
@@ -385,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
     // ---------------- fp32-output epilogue (warps 2..9) ----------------
     const int ew = warp - 2;
     const int q = warp & 3;  // TMEM lane quadrant: hardware rule warp % 4
-    const int half = ew >> 2;
+    const int slot = ew >> 2;
     constexpr int CW = BN >= 64 ? 64 : 32;  // columns per chunk
     int j = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
@@ -404,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<EPI>::value)
       const bool row_ok = row < p.M;
       const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
 #pragma unroll 1
-      for (int c = half * CW; c < BN; c += 2 * CW) {
+      for (int c = slot * CW; c < BN; c += kPerQuad * CW) {
         const int nb = tc.n0 + c;
         if (nb >= p.N) break;
 #pragma unroll
@@ -494,10 +505,10 @@ int sm_count() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool WIDE>
 cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
-  using C = Cfg<BN, EPI>;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  using C = Cfg<BN, EPI, WIDE>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI, WIDE>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -520,17 +531,47 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   if (tiles > (1ll << 31) - 1) return cudaErrorInvalidValue;
   const long long slots = static_cast<long long>(sm_count()) * C::kMinBlocks;
   const int grid = static_cast<int>(tiles < slots ? tiles : slots);
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, to, tx, p, num_kb, n_tiles, m_tiles, p.splits);
+  kern<<<grid, Shape<EPI, WIDE>::kThreads, C::kSmemBytes, stream>>>(ta, tb, to, tx, p, num_kb, n_tiles, m_tiles,
+                                                                    p.splits);
   return cudaGetLastError();
+}
+
+// Layout choice for the bf16-output epilogues. Measured on the benchmark shapes (393,216 rows): the one-CTA,
+// 16-epilogue-warp layout (deeper operand ring, 256-column tiles) is faster for wide outputs (forward 96->512 and
+// 512->256, data gradient 256->512: 4-12%) and slower for narrow ones (outputs of 128 or 256 columns in the data
+// gradient, 128 in the forward pass: 5-20%). RLB_GEMM_WIDE=0 / 1 in the environment forces one layout (read once).
+int wide_override() {
+  static const int v = [] {
+    const char* e = std::getenv("RLB_GEMM_WIDE");
+    return e == nullptr ? -1 : (e[0] == '1' ? 1 : 0);
+  }();
+  return v;
+}
+
+template <int EPI>
+bool use_wide(int N) {
+  const int o = wide_override();
+  if (o >= 0) return o == 1;
+  return EPI == kEpiDgradElu ? N >= 512 : N >= 256;
+}
+
+template <bool A_MN, bool B_MN, int EPI, bool WIDE>
+cudaError_t launch_bn_t(const GemmParams& p, cudaStream_t stream) {
+  constexpr bool one_cta = Shape<EPI, WIDE>::kMinBlocks == 1;
+  if (!B_MN && p.N <= 32) return launch_t<32, A_MN, B_MN, EPI, WIDE>(p, stream);
+  if (p.N <= 64) return launch_t<64, A_MN, B_MN, EPI, WIDE>(p, stream);
+  if (p.N <= 128 || !one_cta) return launch_t<128, A_MN, B_MN, EPI, WIDE>(p, stream);
+  if constexpr (one_cta) return launch_t<256, A_MN, B_MN, EPI, WIDE>(p, stream);
+  return cudaErrorInvalidValue;
 }
 
 template <bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_bn(const GemmParams& p, cudaStream_t stream) {
-  if (!B_MN && p.N <= 32) return launch_t<32, A_MN, B_MN, EPI>(p, stream);
-  if (p.N <= 64) return launch_t<64, A_MN, B_MN, EPI>(p, stream);
-  if (p.N <= 128 || CtasPerSm<EPI>::value == 2) return launch_t<128, A_MN, B_MN, EPI>(p, stream);
-  if constexpr (CtasPerSm<EPI>::value == 1) return launch_t<256, A_MN, B_MN, EPI>(p, stream);
-  return cudaErrorInvalidValue;
+  constexpr bool staged = EPI == kEpiDgradElu || EPI == kEpiBiasEluBf16 || EPI == kEpiBiasBf16;
+  if constexpr (staged) {
+    if (use_wide<EPI>(p.N)) return launch_bn_t<A_MN, B_MN, EPI, true>(p, stream);
+  }
+  return launch_bn_t<A_MN, B_MN, EPI, false>(p, stream);
 }
 
 }  // namespace
