@@ -1,9 +1,9 @@
 """Environment interface, the synthetic benchmark environment and the remote environment bridge."""
 
 from .bridge import EnvServer, RemoteEnvError, RemoteEnvTimeoutError, RemoteVecEnv
-from .classic import BatchedCartPole, BatchedCartPolePO, BatchedPendulum, Tracking12
+from .classic import ENV_CLASSES, BatchedCartPole, BatchedCartPolePO, BatchedPendulum, Tracking12, make_env
 from .linear_gaussian import LinearGaussianVecEnv, humanoid_like
 from .vec_env import VecEnv
 
-__all__ = ["BatchedCartPole", "BatchedCartPolePO", "BatchedPendulum", "EnvServer", "LinearGaussianVecEnv",
-           "RemoteEnvError", "RemoteEnvTimeoutError", "RemoteVecEnv", "Tracking12", "VecEnv", "humanoid_like"]
+__all__ = ["ENV_CLASSES", "BatchedCartPole", "BatchedCartPolePO", "BatchedPendulum", "EnvServer", "LinearGaussianVecEnv",
+           "RemoteEnvError", "RemoteEnvTimeoutError", "RemoteVecEnv", "Tracking12", "VecEnv", "humanoid_like", "make_env"]

@@ -27,6 +27,7 @@ from .vec_env import VecEnv
 class _SeededBatchEnv(VecEnv):
     num_actions: int = 1
     time_out_steps: int = 500
+    step_dt: float = 0.02  # simulated seconds per step (RND scales its weight by it)
     obs_groups_cfg: dict = {"actor": ["policy"], "critic": ["policy"]}
 
     def __init__(self, num_envs: int, seed: int = 0, device: str | torch.device = "cpu") -> None:
@@ -76,6 +77,7 @@ class BatchedCartPole(_SeededBatchEnv):
     num_actions = 1
     time_out_steps = 500
     G, M_CART, M_POLE, HALF_LEN, FORCE, TAU = 9.8, 1.0, 0.1, 0.5, 10.0, 0.02
+    step_dt = TAU
     X_LIMIT, THETA_LIMIT = 2.4, 12.0 * math.pi / 180.0
 
     def _reset(self, mask: torch.Tensor) -> None:
@@ -114,6 +116,7 @@ class BatchedPendulum(_SeededBatchEnv):
     num_actions = 1
     time_out_steps = 200
     G, MASS, LEN, DT, MAX_SPEED, MAX_TORQUE = 10.0, 1.0, 1.0, 0.05, 8.0, 2.0
+    step_dt = DT
 
     def _reset(self, mask):
         th = self._uniform(self.num_envs, lo=-math.pi, hi=math.pi)
@@ -145,6 +148,7 @@ class Tracking12(_SeededBatchEnv):
     time_out_steps = 400
     obs_groups_cfg = {"actor": ["policy"], "critic": ["policy", "privileged"]}
     DT, DAMPING, ACC_LIMIT, LOST = 0.05, 0.5, 4.0, 3.0
+    step_dt = DT
 
     def _reset(self, mask):
         N, D = self.num_envs, 12
@@ -184,4 +188,22 @@ class Tracking12(_SeededBatchEnv):
         return TensorDict({"policy": policy, "privileged": privileged}, batch_size=[self.num_envs], device=self.device)
 
 
-__all__ = ["BatchedCartPole", "BatchedCartPolePO", "BatchedPendulum", "Tracking12"]
+ENV_CLASSES = {"cartpole": BatchedCartPole, "cartpole_po": BatchedCartPolePO, "pendulum": BatchedPendulum,
+               "tracking12": Tracking12}
+
+
+def env_class(name: str) -> type[_SeededBatchEnv]:
+    """The test environment class registered under ``name`` (a key of :data:`ENV_CLASSES`)."""
+    try:
+        return ENV_CLASSES[name]
+    except KeyError:
+        raise KeyError(f"unknown test environment {name!r}; known: {sorted(ENV_CLASSES)}") from None
+
+
+def make_env(name: str, num_envs: int, seed: int = 0, device: str | torch.device = "cpu") -> _SeededBatchEnv:
+    """Build the seeded test environment ``name`` with ``num_envs`` environments on ``device``."""
+    return env_class(name)(num_envs, seed=seed, device=device)
+
+
+__all__ = ["ENV_CLASSES", "BatchedCartPole", "BatchedCartPolePO", "BatchedPendulum", "Tracking12", "env_class",
+           "make_env"]

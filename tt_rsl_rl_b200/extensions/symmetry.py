@@ -80,7 +80,32 @@ class Symmetry:
         action_maps = _signed_perm_from_images(a_out.view(K, num_actions, num_actions))
         if action_maps is None:
             return None
+        if any(perm.shape[0] != K for perm, _ in obs_maps.values()):
+            return None  # every group and the actions must have the same number of copies
+        if not self._maps_reproduce(obs_template, num_actions, obs_maps, action_maps):
+            return None
         return obs_maps, action_maps
+
+    def _maps_reproduce(self, obs_template, num_actions: int, obs_maps: dict, action_maps, rows: int = 5) -> bool:
+        """Check the derived maps against the function on random inputs of every group at once.
+
+        Basis vectors alone cannot see a map that reads another group (each group is probed with the others at zero)
+        or a nonlinear map that agrees with a signed permutation on 0/1 inputs (``x -> -x**3``)."""
+        device = next(iter(obs_template.values())).device
+        gen = torch.Generator().manual_seed(0x5EED)
+        x = {g: torch.randn(rows, obs_template[g].shape[-1], generator=gen).to(device) for g in obs_template.keys()}
+        a = torch.randn(rows, num_actions, generator=gen).to(device)
+        out_obs, out_act = self.data_augmentation_func(env=self.env, obs=TensorDict(x, batch_size=[rows], device=device),
+                                                       actions=a)
+
+        def matches(got, src, perm, sign):
+            want = torch.cat([src[:, perm[k]] * sign[k] for k in range(perm.shape[0])], dim=0)
+            return got is not None and got.shape == want.shape and bool(
+                torch.allclose(got.float(), want, rtol=1e-3, atol=1e-5))
+
+        if out_obs is None or not all(matches(out_obs[g], x[g], *obs_maps[g]) for g in obs_maps):
+            return False
+        return matches(out_act, a, *action_maps)
 
 
 def _signed_perm_from_images(images: torch.Tensor):

@@ -28,6 +28,13 @@ class OnPolicyRunner:
         self.env = env
         self.cfg = train_cfg
         self.device = device
+        self.gpu_session = None
+        guard = self.cfg.get("device_guard")
+        if guard and torch.device(device).type == "cuda":
+            # opt-in: device checks and an exclusive per-GPU lock before anything touches the GPU
+            from ..device import acquire_gpu
+
+            self.gpu_session = acquire_gpu(torch.device(device).index or 0, **(guard if isinstance(guard, dict) else {}))
         self._configure_multi_gpu()
         obs = self.env.get_observations()
         alg_class = resolve_callable(self.cfg["algorithm"]["class_name"])

@@ -1,0 +1,179 @@
+"""Golden learning curves of the seeded test environments and the acceptance rule applied to them.
+
+The golden curves are recorded with the upstream rsl_rl runner on the CPU (:func:`record`, one CSV per environment and
+seed plus ``summary.json``). A run of this framework passes on an environment when the mean over its seeds of the final
+reward (mean of ``Train/mean_reward`` over the last ``FINAL_WINDOW`` iterations) is finite and at least
+
+    golden mean - max(golden std over seeds, 5 % of |golden mean|).
+
+The reference plugin applies the same rule to its own golden runs (``rsl_rl_tt/testing/golden.py:28-60``).
+
+Command line::
+
+    python -m tt_rsl_rl_b200.testing.golden record --envs cartpole pendulum --seeds 0 1 2
+    python -m tt_rsl_rl_b200.testing.golden summarize --envs cartpole     # statistics from the CSVs in place
+    python -m tt_rsl_rl_b200.testing.golden check --envs cartpole --seeds 0 1 2 --device cuda:0
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import json
+import math
+import os
+import statistics
+import sys
+import tempfile
+from pathlib import Path
+
+GOLDEN_DIR = Path(__file__).resolve().parent / "golden"
+FINAL_WINDOW = 10
+SEEDS = (0, 1, 2)
+REWARD = "Train/mean_reward"
+# columns kept in the committed curves
+KEEP = ("iteration", "Train/mean_reward", "Train/mean_episode_length", "Loss/value", "Loss/surrogate", "Loss/entropy",
+        "Loss/learning_rate", "Policy/mean_std")
+
+
+def read_curve(path: str | Path) -> list[dict[str, float | None]]:
+    """Rows of a metrics CSV; empty cells become ``None``."""
+    with open(path, newline="") as f:
+        return [{k: (float(v) if v not in ("", None) else None) for k, v in row.items()} for row in csv.DictReader(f)]
+
+
+def write_curve(path: str | Path, rows: list[dict], columns=KEEP) -> None:
+    with open(path, "w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=list(columns), extrasaction="ignore", restval="")
+        w.writeheader()
+        for r in rows:
+            w.writerow({k: ("" if r.get(k) is None else r[k]) for k in columns})
+
+
+def final_reward(rows: list[dict], window: int = FINAL_WINDOW) -> float:
+    """Mean of the last ``window`` logged rewards (NaN when the run never finished an episode)."""
+    vals = [r[REWARD] for r in rows if r.get(REWARD) is not None][-window:]
+    return statistics.mean(vals) if vals else float("nan")
+
+
+def threshold(mean: float, std: float) -> float:
+    """Lowest passing final reward for golden seeds of mean ``mean`` and standard deviation ``std``."""
+    return mean - max(std, 0.05 * abs(mean))
+
+
+def summarize(finals: list[float]) -> dict:
+    return {"final_rewards": finals, "final_reward_mean": statistics.mean(finals),
+            "final_reward_std": statistics.stdev(finals) if len(finals) > 1 else 0.0}
+
+
+def load_summary(golden_dir: str | Path = GOLDEN_DIR) -> dict:
+    return json.loads((Path(golden_dir) / "summary.json").read_text())
+
+
+def verdict(env_name: str, finals: list[float], curves_finite: bool = True, summary: dict | None = None) -> dict:
+    """Apply the acceptance rule to the final rewards of a run's seeds."""
+    ref = (summary or load_summary())["envs"][env_name]
+    thr = threshold(ref["final_reward_mean"], ref["final_reward_std"])
+    finite = curves_finite and bool(finals) and all(math.isfinite(x) for x in finals)
+    mean = statistics.mean(finals) if finals else float("nan")
+    return {"env": env_name, "final_rewards": finals, "mean": mean, "golden_mean": ref["final_reward_mean"],
+            "golden_std": ref["final_reward_std"], "threshold": thr, "all_finite": finite,
+            "passes": bool(finite and mean >= thr)}
+
+
+def _curve_finite(rows: list[dict]) -> bool:
+    return all(v is None or math.isfinite(v) for r in rows for v in r.values())
+
+
+def record(envs, seeds=SEEDS, out_dir: str | Path = GOLDEN_DIR, iterations: int | None = None,
+           num_threads: int | None = None) -> dict:
+    """Train every environment with upstream rsl_rl on the CPU and write the curves and ``summary.json``."""
+    from .reference import SPECS, train
+
+    out_dir = Path(out_dir)
+    summary_path = out_dir / "summary.json"
+    summary = json.loads(summary_path.read_text()) if summary_path.exists() else {"envs": {}}
+    summary.update({"final_window": FINAL_WINDOW, "impl": "upstream rsl_rl (CPU)"})
+    for env_name in envs:
+        (out_dir / env_name).mkdir(parents=True, exist_ok=True)
+        finals, runs = [], []
+        for seed in seeds:
+            with tempfile.TemporaryDirectory() as tmp:
+                info = train(env_name, seed, tmp, impl="upstream", iterations=iterations, num_threads=num_threads)
+                rows = read_curve(os.path.join(tmp, "metrics.csv"))
+            write_curve(out_dir / env_name / f"seed{seed}.csv", rows)
+            finals.append(final_reward(rows))
+            runs.append({"seed": seed, "wall_s": round(info["wall_s"], 1), "iterations": info["iterations"]})
+        spec = SPECS[env_name]
+        summary["envs"][env_name] = {**summarize(finals), "runs": runs, "num_envs": spec.num_envs,
+                                     "num_steps": spec.num_steps, "hidden": list(spec.hidden)}
+        summary_path.write_text(json.dumps(summary, indent=1))
+    return summary
+
+
+def summarize_dir(envs, seeds=SEEDS, golden_dir: str | Path = GOLDEN_DIR) -> dict:
+    """Rebuild the final-reward statistics of ``summary.json`` from the curves already in ``golden_dir`` (per-run
+    metadata recorded earlier is kept)."""
+    from .reference import SPECS
+
+    golden_dir = Path(golden_dir)
+    path = golden_dir / "summary.json"
+    summary = json.loads(path.read_text()) if path.exists() else {"envs": {}}
+    summary.update({"final_window": FINAL_WINDOW, "impl": "upstream rsl_rl (CPU)"})
+    for env_name in envs:
+        finals = [final_reward(read_curve(golden_dir / env_name / f"seed{s}.csv")) for s in seeds]
+        spec = SPECS[env_name]
+        prev = summary["envs"].get(env_name, {})
+        summary["envs"][env_name] = {**prev, **summarize(finals), "seeds": list(seeds), "num_envs": spec.num_envs,
+                                     "num_steps": spec.num_steps, "hidden": list(spec.hidden),
+                                     "iterations": spec.iterations}
+    path.write_text(json.dumps(summary, indent=1))
+    return summary
+
+
+def check(envs, seeds=SEEDS, device: str = "cpu", iterations: int | None = None, log_root: str | None = None,
+          golden_dir: str | Path = GOLDEN_DIR, num_threads: int | None = None) -> list[dict]:
+    """Train every environment with this framework on ``device`` and apply the acceptance rule."""
+    from .reference import train
+
+    summary = load_summary(golden_dir)
+    out = []
+    for env_name in envs:
+        finals, finite = [], True
+        for seed in seeds:
+            with tempfile.TemporaryDirectory() as tmp:
+                log_dir = os.path.join(log_root, env_name, f"seed{seed}") if log_root else tmp
+                train(env_name, seed, log_dir, impl="b200", device=device, iterations=iterations,
+                      num_threads=num_threads)
+                rows = read_curve(os.path.join(log_dir, "metrics.csv"))
+            finals.append(final_reward(rows))
+            finite &= _curve_finite(rows)
+        out.append(verdict(env_name, finals, finite, summary))
+    return out
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("mode", choices=("record", "summarize", "check"))
+    ap.add_argument("--envs", nargs="+", default=["cartpole", "pendulum", "tracking12", "cartpole_po"])
+    ap.add_argument("--seeds", nargs="+", type=int, default=list(SEEDS))
+    ap.add_argument("--device", default="cpu", help="check only: device of this framework's run")
+    ap.add_argument("--iterations", type=int, default=None, help="override the spec's iteration count")
+    ap.add_argument("--threads", type=int, default=None)
+    ap.add_argument("--golden-dir", default=str(GOLDEN_DIR))
+    ap.add_argument("--log-root", default=None, help="check only: keep the curves of the run under this folder")
+    args = ap.parse_args(argv)
+    if args.mode == "record":
+        print(json.dumps(record(args.envs, args.seeds, args.golden_dir, args.iterations, args.threads), indent=1))
+        return 0
+    if args.mode == "summarize":
+        print(json.dumps(summarize_dir(args.envs, args.seeds, args.golden_dir), indent=1))
+        return 0
+    results = check(args.envs, args.seeds, args.device, args.iterations, args.log_root, args.golden_dir, args.threads)
+    for r in results:
+        print(json.dumps(r))
+    return 0 if all(r["passes"] for r in results) else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -6,6 +6,7 @@ import csv
 import json
 import os
 import pathlib
+import time
 from abc import ABC, abstractmethod
 
 
@@ -35,35 +36,43 @@ class LogWriter(ABC):
 
 
 class CsvLogWriter(LogWriter):
-    """One CSV row per iteration (``metrics.csv``) plus ``config.json`` in ``log_dir`` (no external service)."""
+    """One CSV row per iteration (``metrics.csv``) plus ``config.json`` in ``log_dir`` (no external service).
 
-    def __init__(self, log_dir: str, filename: str = "metrics.csv") -> None:
+    Columns are ``iteration``, ``wall_s`` (seconds since the writer was made) and then every tag in order of first
+    appearance; a tag that starts late (``Train/mean_reward`` appears once the first episode ends) gets its own column
+    and empty cells before. The file is rewritten whenever an iteration completes, so an interrupted run still leaves
+    a valid CSV. Time-indexed duplicates (``*/time`` tags, stepped by seconds rather than iterations, which a logger
+    emits for writers of other kinds) are skipped: ``wall_s`` carries the time."""
+
+    def __init__(self, log_dir: str, filename: str = "metrics.csv", **kwargs) -> None:
         self.log_dir = log_dir
         os.makedirs(log_dir, exist_ok=True)
         self.path = os.path.join(log_dir, filename)
-        self._row: dict[str, float] = {}
+        self._t0 = time.time()
+        self._rows: dict[int, dict[str, float]] = {}
+        self._columns: list[str] = []
         self._step: int | None = None
-        self._columns: list[str] | None = None
 
     def add_scalar(self, tag: str, scalar_value: float, global_step: int) -> None:
+        if tag.endswith("/time"):
+            return
         if self._step is not None and global_step != self._step:
             self._flush()
         self._step = global_step
-        self._row[tag] = float(scalar_value)
+        row = self._rows.setdefault(global_step, {"iteration": global_step,
+                                                  "wall_s": round(time.time() - self._t0, 3)})
+        row[tag] = float(scalar_value)
+        if tag not in self._columns:
+            self._columns.append(tag)
 
     def _flush(self) -> None:
-        if self._step is None:
+        if not self._rows:
             return
-        row = {"iteration": self._step, **self._row}
-        new = self._columns is None
-        if new:
-            self._columns = list(row)
-        with open(self.path, "a", newline="") as f:
-            w = csv.DictWriter(f, fieldnames=self._columns, extrasaction="ignore")
-            if new:
-                w.writeheader()
-            w.writerow(row)
-        self._row = {}
+        with open(self.path, "w", newline="") as f:
+            w = csv.DictWriter(f, fieldnames=["iteration", "wall_s", *self._columns], restval="")
+            w.writeheader()
+            for step in sorted(self._rows):
+                w.writerow(self._rows[step])
 
     def store_config(self, env_cfg: dict | object, train_cfg: dict) -> None:
         def default(o):
@@ -75,4 +84,3 @@ class CsvLogWriter(LogWriter):
 
     def stop(self) -> None:
         self._flush()
-        self._step = None
