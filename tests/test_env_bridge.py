@@ -87,3 +87,33 @@ def test_runner_learns_through_the_bridge(tmp_path):
     runner.learn(2)
     assert runner.current_learning_iteration == 1
     remote.close()
+
+
+def test_training_through_the_bridge_equals_local_training():
+    """Loopback equality: the same seeds give bit-identical parameters whether the environment is local or behind the
+    bridge (the transport moves raw float32 bytes, nothing is re-encoded)."""
+    import copy
+
+    from helpers import ppo_cfg
+
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv, RemoteVecEnv
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    def make_env():
+        return LinearGaussianVecEnv(32, obs_dim=6, num_actions=2, privileged_dim=1, seed=4)
+
+    def train(env):
+        torch.manual_seed(9)
+        runner = OnPolicyRunner(env, copy.deepcopy(ppo_cfg(T=4)), log_dir=None, device="cpu")
+        runner.learn(3)
+        return [p.detach().clone() for p in runner.alg.actor.parameters()]
+
+    local = train(make_env())
+    srv = _server(make_env())
+    remote = RemoteVecEnv(srv.address, timeout_ms=5000)
+    try:
+        bridged = train(remote)
+    finally:
+        remote.close()
+    for a, b in zip(local, bridged):
+        assert torch.equal(a, b)

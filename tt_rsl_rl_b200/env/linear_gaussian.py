@@ -37,8 +37,6 @@ def make_system_matrices(state_dim: int, action_dim: int, seed: int, rho: float 
 
 
 class LinearGaussianVecEnv(VecEnv):
-    graph_capturable = True
-
     def __init__(self, num_envs: int, obs_dim: int = 48, num_actions: int = 12, privileged_dim: int = 0,
                  episode_length: int = 1000, reset_prob: float = 0.005, noise_std: float = 0.05, seed: int = 0,
                  device: str | torch.device = "cpu", host_noise: bool = False, host_noise_pool_steps: int = 8,
@@ -86,10 +84,20 @@ class LinearGaussianVecEnv(VecEnv):
         if fused is None:
             fused = self.device.type == "cuda" and _extension_available()
         self.fused = bool(fused)
+        if not self.fused:
+            # the PyTorch-op step alternates between two observation buffers: the observations a policy acted on stay
+            # intact until the algorithm has stored them after the next step (rsl_rl keeps a reference to them)
+            self._spare_obs = (torch.zeros_like(self._policy_obs),
+                               None if self._critic_obs is None else torch.zeros_like(self._critic_obs))
         if self.fused:
             self._env_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
             self._env_ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
             self._env_seed = (seed * 0x9E3779B97F4A7C15 + 0x5851F42D4C957F2D) % (2**63)
+
+    @property
+    def graph_capturable(self) -> bool:
+        """The fused step only enqueues device work into fixed buffers, so a rollout can be one CUDA graph."""
+        return self.fused
 
     # ---- VecEnv -----------------------------------------------------------------------------------------------------
     @property
@@ -149,6 +157,10 @@ class LinearGaussianVecEnv(VecEnv):
         self._reset_noise.normal_()
         self.state.copy_(torch.where(done.unsqueeze(1), self._reset_noise, self._next))
         self.episode_length_buf.masked_fill_(done, 0)
+        spare = self._spare_obs
+        self._spare_obs = (self._policy_obs, self._critic_obs)
+        self._policy_obs, self._critic_obs = spare
+        self._obs = self._make_obs_dict()
         self._write_obs(a)
         extras = {"time_outs": self.time_outs, "log": {"/state_norm": self.rewards}}
         return self._obs, self.rewards, self.dones, extras
