@@ -1,0 +1,150 @@
+"""Reference-run harness: mirror functions of the test environments and the signed-permutation probe, run specs and
+config builders on both implementations, the CSV writer, and the golden acceptance rule."""
+
+import math
+import os
+
+import pytest
+import torch
+
+from tt_rsl_rl_b200.env import make_env
+from tt_rsl_rl_b200.extensions import Symmetry
+from tt_rsl_rl_b200.testing import golden
+from tt_rsl_rl_b200.testing import reference as R
+from tt_rsl_rl_b200.testing import symmetry as S
+
+
+def _probe(env_name, func):
+    env = make_env(env_name, 4, seed=0)
+    sym = Symmetry(env, func, use_data_augmentation=True)
+    return sym.probe_signed_permutations(env.get_observations(), env.num_actions)
+
+
+@pytest.mark.parametrize("env_name,func,K", [
+    ("cartpole", S.cartpole_mirror, 2), ("cartpole_po", S.cartpole_mirror, 2), ("pendulum", S.pendulum_mirror, 2),
+    ("tracking12", S.tracking12_sign_mirror, 2), ("tracking12", S.tracking12_dihedral_mirror, 4),
+])
+def test_mirrors_are_signed_permutations_and_symmetries(env_name, func, K):
+    maps = _probe(env_name, func)
+    assert maps is not None
+    obs_maps, act_maps = maps
+    assert act_maps[0].shape[0] == K and all(p.shape[0] == K for p, _ in obs_maps.values())
+    # a true symmetry: mirrored states evolve into mirrored states with equal rewards
+    a, b = make_env(env_name, 8, seed=2), make_env(env_name, 8, seed=2)
+    if env_name == "tracking12":
+        for k in ("p", "v", "a_prev", "amp", "omega", "phase"):
+            getattr(b, k).copy_(getattr(a, k))
+        b.p.neg_(), b.v.neg_(), b.a_prev.neg_()
+        b.phase.add_(math.pi)
+    elif env_name == "pendulum":
+        b.th, b.thd = -a.th.clone(), -a.thd.clone()
+    else:
+        b.s = -a.s.clone()
+    acts = torch.randn(8, a.num_actions) * 0.3
+    for _ in range(5):
+        oa, ra, _, _ = a.step(acts)
+        ob, rb, _, _ = b.step(-acts)
+        mirrored, _ = S.MIRRORS[env_name](obs=oa)
+        for g in oa.keys():
+            torch.testing.assert_close(ob[g], mirrored[g][8:], atol=1e-4, rtol=1e-4)
+        torch.testing.assert_close(ra, rb, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("func", [S.tracking12_affine_mirror, S.tracking12_mixing_mirror, S.tracking12_cubic_mirror])
+def test_probe_refuses_maps_that_are_not_signed_permutations(func):
+    assert _probe("tracking12", func) is None
+
+
+def test_config_builders():
+    spec = R.with_symmetry("tracking12", R.with_rnd("tracking12", R.SPECS["tracking12"]))
+    cfg = R.train_cfg("tracking12", spec)
+    alg = cfg["algorithm"]
+    assert alg["rnd_cfg"]["weight"] == R.RND_WEIGHT["tracking12"]
+    assert alg["symmetry_cfg"]["data_augmentation_func"].endswith(":tracking12_sign_mirror")
+    assert cfg["obs_groups"] == {"actor": ["policy"], "critic": ["policy", "privileged"]}
+    rnn = R.train_cfg("cartpole", R.with_rnn(R.SPECS["cartpole"], "lstm", critic=False))
+    assert rnn["actor"]["class_name"] == "RNNModel" and rnn["actor"]["rnn_type"] == "lstm"
+    assert rnn["critic"]["class_name"] == "MLPModel"
+    t = R.teacher_train_cfg("tracking12")
+    assert t["obs_groups"]["actor"] == ["policy", "privileged"]
+    d = R.distill_cfg("tracking12")
+    assert d["obs_groups"]["student"] == ["policy"] and d["algorithm"]["class_name"] == "Distillation"
+    with pytest.raises(ValueError):
+        R.build_runner("cartpole", 0, impl="upstream", device="cuda:0")
+
+
+def _small(spec, **kw):
+    import dataclasses
+
+    return dataclasses.replace(spec, num_envs=64, num_steps=8, **kw)
+
+
+@pytest.mark.parametrize("impl", ["b200", "upstream"])
+@pytest.mark.parametrize("variant", ["plain", "rnd_symmetry", "gru"])
+def test_runs_of_both_implementations_log_the_same_columns(ref, tmp_path, impl, variant):
+    env_name = "cartpole_po" if variant == "gru" else "tracking12"
+    spec = _small(R.SPECS[env_name])
+    if variant == "rnd_symmetry":
+        spec = R.with_symmetry(env_name, R.with_rnd(env_name, spec))
+    out = R.train(env_name, 0, str(tmp_path), impl=impl, iterations=3, spec=spec)
+    assert out["iterations"] == 3
+    rows = golden.read_curve(tmp_path / "metrics.csv")
+    assert [r["iteration"] for r in rows] == [0, 1, 2]
+    assert all(math.isfinite(r["Loss/value"]) for r in rows)
+    if variant == "rnd_symmetry":
+        assert "Loss/rnd" in rows[0] and "Loss/symmetry" in rows[0]
+
+
+@pytest.mark.parametrize("impl", ["b200", "upstream"])
+def test_teacher_checkpoint_and_distillation(ref, tmp_path, impl):
+    ckpt = R.make_teacher_checkpoint("tracking12", str(tmp_path / "teacher.pt"), iterations=2, num_envs=64,
+                                     impl=impl)
+    assert os.path.exists(ckpt)
+    out = R.train_distillation("tracking12", 0, str(tmp_path / "d"), ckpt, impl=impl, iterations=2)
+    assert out["iterations"] == 2
+    rows = golden.read_curve(tmp_path / "d" / "metrics.csv")
+    assert len(rows) == 2 and "Loss/behavior" in rows[0]
+
+
+def test_csv_writer_keeps_late_columns(tmp_path):
+    from tt_rsl_rl_b200.utils.log_writer import CsvLogWriter
+
+    w = CsvLogWriter(str(tmp_path))
+    w.add_scalar("Loss/value", 1.0, 0)
+    w.add_scalar("Train/mean_reward/time", 5.0, 17)  # time-indexed: skipped
+    w.add_scalar("Loss/value", 2.0, 1)
+    w.add_scalar("Train/mean_reward", 3.0, 1)
+    w.stop()
+    rows = golden.read_curve(tmp_path / "metrics.csv")
+    assert [r["iteration"] for r in rows] == [0, 1]
+    assert rows[0]["Train/mean_reward"] is None and rows[1]["Train/mean_reward"] == 3.0
+
+
+def test_golden_rule(tmp_path):
+    rows = [{"iteration": i, "Train/mean_reward": float(i)} for i in range(30)]
+    assert golden.final_reward(rows) == pytest.approx(sum(range(20, 30)) / 10)
+    assert math.isnan(golden.final_reward([{"iteration": 0, "Train/mean_reward": None}]))
+    summary = {"envs": {"x": {"final_reward_mean": 100.0, "final_reward_std": 2.0}}}
+    assert golden.threshold(100.0, 2.0) == 95.0 and golden.threshold(-10.0, 2.0) == -12.0
+    assert golden.verdict("x", [96.0, 95.0], summary=summary)["passes"]
+    assert not golden.verdict("x", [94.0, 95.0], summary=summary)["passes"]
+    assert not golden.verdict("x", [float("nan"), 200.0], summary=summary)["passes"]
+    assert not golden.verdict("x", [99.0], curves_finite=False, summary=summary)["passes"]
+    golden.write_curve(tmp_path / "c.csv", rows)
+    assert golden.read_curve(tmp_path / "c.csv")[5]["Train/mean_reward"] == 5.0
+
+
+def test_committed_golden_curves_are_consistent():
+    summary = golden.load_summary()
+    assert set(summary["envs"]) >= {"cartpole", "pendulum", "tracking12", "cartpole_po"}
+    for env_name, ref in summary["envs"].items():
+        finals = [golden.final_reward(golden.read_curve(golden.GOLDEN_DIR / env_name / f"seed{s}.csv"))
+                  for s in golden.SEEDS]
+        assert finals == pytest.approx(ref["final_rewards"])
+
+
+def test_this_framework_passes_the_golden_rule_on_cartpole():
+    """One seed of the cart-pole spec on the CPU path against the upstream golden curves."""
+    (res,) = golden.check(["cartpole"], seeds=(0,))
+    assert res["all_finite"]
+    assert res["mean"] >= res["threshold"], res
