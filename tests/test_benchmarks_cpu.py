@@ -31,3 +31,44 @@ def test_bridge_bench_round_trips(transport):
 
     res = measure(transport, 64, steps=5, warmup=2)
     assert res["ms_per_step"] > 0 and res["bytes_per_step"] == sum(step_bytes(64, {"policy": 36, "privileged": 48}, 12))
+
+
+def test_op_profiler_times_launching_entry_points(monkeypatch):
+    from tt_rsl_rl_b200 import ops
+
+    class FakeExt:
+        def gae(self, x):
+            return x + 1
+
+        def gemm(self, x):
+            return x * 2
+
+        def plan_sizes(self):
+            return "host helper"
+
+    class FakeEvent:
+        clock = [0.0]
+
+        def record(self):
+            FakeEvent.clock[0] += 0.5
+            self.t = FakeEvent.clock[0]
+
+        def elapsed_time(self, end):
+            return end.t - self.t
+
+    monkeypatch.setattr(ops, "_EXT", FakeExt())
+    capturing = {"on": False}
+    with ops.count_launches() as cnt, ops.profile_ops(FakeEvent, lambda: None, lambda: capturing["on"]) as prof:
+        assert ops.ext().gae(1) == 2 and ops.ext().gae(2) == 3 and ops.ext().gemm(3) == 6
+        assert ops.ext().plan_sizes() == "host helper"  # not a launching entry point: neither counted nor timed
+        capturing["on"] = True
+        ops.ext().gemm(1)  # inside a graph capture: counted, not timed
+    assert cnt.n == 4
+    assert prof.stats == {"gae": [2, 1.0], "gemm": [1, 0.5]}
+    rows = prof.table()
+    assert rows[0]["op"] == "gae" and rows[0]["mean_us"] == 500.0 and abs(sum(r["share"] for r in rows) - 1) < 1e-6
+    assert ops._PROFILER is None and ops.ext() is ops._EXT  # instrumentation ends with the block
+    with pytest.raises(RuntimeError):
+        with ops.profile_ops(FakeEvent, lambda: None, lambda: False), ops.profile_ops(FakeEvent):
+            pass
+    assert ops._PROFILER is None

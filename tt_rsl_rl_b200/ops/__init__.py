@@ -14,6 +14,7 @@ import torch
 _EXT = None
 _EXT_ERROR: Exception | None = None
 _COUNTER: list[int] | None = None
+_PROFILER: profile_ops | None = None
 
 # Entry points that launch kernels (the rest are host-side planning, sizing and IPC helpers).
 LAUNCHING = frozenset({
@@ -25,7 +26,8 @@ LAUNCHING = frozenset({
 
 
 class _CountingModule:
-    """Forwards to the extension and counts calls of kernel-launching entry points."""
+    """Forwards to the extension; counts (and, under :class:`profile_ops`, times) calls of kernel-launching entry
+    points."""
 
     def __init__(self, mod) -> None:
         self._mod = mod
@@ -38,6 +40,9 @@ class _CountingModule:
         def counted(*args, **kwargs):
             if _COUNTER is not None:
                 _COUNTER[0] += 1
+            prof = _PROFILER
+            if prof is not None:
+                return prof._timed(name, fn, args, kwargs)
             return fn(*args, **kwargs)
 
         return counted
@@ -64,6 +69,60 @@ class count_launches:
         _COUNTER = None
 
 
+class profile_ops:
+    """Context manager timing every kernel-launching entry point called from Python.
+
+    Each call is bracketed by CUDA events on the current stream; the events are resolved when the block exits (one
+    synchronisation, no per-call host wait), so a time is the device time of that call's kernels. ``.stats[name] =
+    [calls, total_ms]``; :meth:`table` lists them by total time. Calls made while a CUDA graph is being captured are
+    not timed (a replay is one graph launch): profile eager iterations (``b200_cfg["graphs"] = False``, or the first
+    iteration of a captured path). The reference plugin's op profiler has the same role with a device
+    synchronisation around every op (``scripts/profile_ops.py``).
+    """
+
+    def __init__(self, event_factory=None, synchronize=None, capturing=None) -> None:
+        self._event = event_factory or (lambda: torch.cuda.Event(enable_timing=True))
+        self._sync = synchronize or torch.cuda.synchronize
+        self._capturing = capturing or torch.cuda.is_current_stream_capturing
+        self._pending: list = []
+        self.stats: dict[str, list] = {}
+
+    def _timed(self, name: str, fn, args, kwargs):
+        if self._capturing():
+            return fn(*args, **kwargs)
+        start, end = self._event(), self._event()
+        start.record()
+        out = fn(*args, **kwargs)
+        end.record()
+        self._pending.append((name, start, end))
+        return out
+
+    def __enter__(self) -> profile_ops:
+        global _PROFILER
+        if _PROFILER is not None:
+            raise RuntimeError("profile_ops blocks do not nest")
+        self._pending = []
+        _PROFILER = self
+        return self
+
+    def __exit__(self, *exc) -> None:
+        global _PROFILER
+        _PROFILER = None
+        self._sync()
+        for name, start, end in self._pending:
+            entry = self.stats.setdefault(name, [0, 0.0])
+            entry[0] += 1
+            entry[1] += start.elapsed_time(end)
+        self._pending = []
+
+    def table(self) -> list[dict]:
+        """One row per entry point: calls, total milliseconds, mean microseconds, share of the total."""
+        total = sum(ms for _, ms in self.stats.values()) or 1.0
+        rows = [{"op": k, "calls": c, "total_ms": round(ms, 4), "mean_us": round(1e3 * ms / c, 2),
+                 "share": round(ms / total, 4)} for k, (c, ms) in self.stats.items()]
+        return sorted(rows, key=lambda r: -r["total_ms"])
+
+
 def ext():
     """Return the compiled extension module, raising a clear error if it is not built."""
     global _EXT, _EXT_ERROR
@@ -76,7 +135,7 @@ def ext():
         raise RuntimeError(
             "tt_rsl_rl_b200._C is not built; run `python setup.py build_ext --inplace` in the repository root"
         ) from _EXT_ERROR
-    if _COUNTER is not None:
+    if _COUNTER is not None or _PROFILER is not None:
         return _CountingModule(_EXT)
     return _EXT
 

@@ -47,12 +47,15 @@ def make_cfg(hidden: list[int], steps: int, mini_batches: int = 4, epochs: int =
 
 
 def build(impl: str, device: str, num_envs: int, hidden: list[int], steps: int = 24, mini_batches: int = 4,
-          epochs: int = 5, shape: str = "humanoid", seed: int = 0):
-    """``(algorithm, env)`` of a runner of ``impl`` ("b200" or "upstream") on a null environment."""
+          epochs: int = 5, shape: str = "humanoid", seed: int = 0, b200_cfg: dict | None = None):
+    """``(algorithm, env)`` of a runner of ``impl`` ("b200" or "upstream") on a null environment; ``b200_cfg`` goes
+    to this framework's algorithm section."""
     groups, num_actions = SHAPES[shape]
     torch.manual_seed(seed)
     env = NullVecEnv(num_envs, groups, num_actions, seed=seed, device=device)
     cfg = make_cfg(hidden, steps, mini_batches, epochs)
+    if b200_cfg and impl == "b200":
+        cfg["algorithm"]["b200_cfg"] = dict(b200_cfg)
     if impl == "upstream":
         if torch.device(device).type != "cpu":
             raise ValueError("the upstream runner is measured on the CPU here")
