@@ -1,0 +1,76 @@
+"""Invariants of the source tree, checked on the host: no cluster-multicast loads, no traps or device asserts, no
+batched-copy calls, no compatibility layers, build notes not named from code, every kernel wait bounded."""
+
+import pathlib
+import re
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+PKG = ROOT / "tt_rsl_rl_b200"
+CSRC = PKG / "ops" / "csrc"
+CODE_EXT = {".py", ".cu", ".cuh", ".cpp", ".h", ".c"}
+
+
+def _code_files():
+    roots = [PKG, ROOT / "tests", ROOT / "baseline" / "compat"]
+    files = [p for r in roots for p in r.rglob("*") if p.suffix in CODE_EXT and "__pycache__" not in p.parts]
+    files += [ROOT / n for n in ("bench.py", "__graft_entry__.py", "setup.py") if (ROOT / n).exists()]
+    return files
+
+
+def _offenders(pattern, files):
+    rx = re.compile(pattern)
+    return [f"{p.relative_to(ROOT)}:{i}" for p in files for i, line in enumerate(p.read_text(errors="replace").splitlines(), 1)
+            if rx.search(line)]
+
+
+def test_no_cluster_multicast_anywhere():
+    # the same kernels run in multi-GPU jobs, where a multicast load could read another GPU's memory
+    token = re.escape("multicast" + "::" + "cluster")
+    assert _offenders(token, _code_files()) == []
+
+
+def test_no_traps_or_device_asserts():
+    kernels = [p for p in CSRC.rglob("*") if p.suffix in {".cu", ".cuh"}]
+    assert kernels
+    assert _offenders(r"\b__" + "trap" + r"\b|asm[^;]*\btrap\b", kernels) == []
+    assert _offenders(r"(?<![_\w])assert\s*\(", kernels) == []  # static_assert is fine
+
+
+def test_no_batched_copy_calls():
+    assert _offenders(r"[Cc]u(da)?Memcpy(3D)?" + "Batch", _code_files()) == []
+
+
+def test_no_compatibility_layers_on_the_compute_path():
+    pkg = [p for p in PKG.rglob("*.py")]
+    assert _offenders(r"^\s*(import|from)\s+(triton|tilelang)\b", pkg) == []
+    # torch.compile only behind the user's opt-in wrapper
+    assert _offenders(r"torch\.compile\(", pkg) == ["tt_rsl_rl_b200/utils/utils.py:" + str(
+        next(i for i, line in enumerate((PKG / "utils" / "utils.py").read_text().splitlines(), 1)
+             if "torch.compile(" in line))]
+
+
+def test_code_names_no_build_notes():
+    notes = [p.stem for p in ROOT.glob("*.md") if p.name != "README.md"]
+    assert notes
+    pattern = r"\b(" + "|".join(re.escape(n) for n in notes) + r")(\.md)?\b"
+    assert _offenders(pattern, _code_files()) == []
+
+
+def test_every_kernel_wait_loop_is_bounded():
+    """Each loop that polls memory written by another thread, block or GPU (acquire loads, mbarrier try-waits, a
+    barrier generation) also reads the global timer and gives up after a deadline."""
+    polling = re.compile(r"ld_acquire|try_wait|\*gen\b|volatile")
+    bounded = re.compile(r"globaltimer|timeout")
+    found = 0
+    for p in CSRC.rglob("*"):
+        if p.suffix not in {".cu", ".cuh"}:
+            continue
+        lines = p.read_text().splitlines()
+        for i, line in enumerate(lines):
+            if not re.search(r"\bwhile\s*\(|\bfor\s*\(\s*;\s*;", line):
+                continue
+            window = "\n".join(lines[i: i + 12])
+            if polling.search(window):
+                found += 1
+                assert bounded.search(window), f"unbounded wait at {p.relative_to(ROOT)}:{i + 1}"
+    assert found >= 4  # the peer-flag waits, the grid barrier and the mbarrier wait
