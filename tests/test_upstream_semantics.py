@@ -416,3 +416,74 @@ def test_reduce_parameters_on_one_rank_is_the_identity():
     assert sum(calls) == sum(p.numel() for p in alg.actor.parameters()) + sum(
         p.numel() for p in alg.critic.parameters() if p.grad is not None)
     assert all(bool((p.grad == 0.5).all()) for p in alg.actor.parameters())
+
+
+# ---- loss tables, mixed precision, shared encoders ------------------------------------------------------------------------
+def _direct_ppo(**kw):
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.models import MLPModel
+
+    torch.manual_seed(0)
+    N, T, A = 8, 4, 3
+    obs = TensorDict({"policy": torch.randn(N, 5)}, batch_size=[N])
+    groups = {"actor": ["policy"], "critic": ["policy"]}
+    actor = MLPModel(obs, groups, "actor", A, hidden_dims=[16],
+                     distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
+    critic = MLPModel(obs, groups, "critic", 1, hidden_dims=[16])
+    ppo = PPO(actor, critic, RolloutStorage("rl", N, T, obs, [A]), **kw)
+    ppo.train_mode()
+    for _ in range(T):
+        ppo.act(obs)
+        ppo.process_env_step(obs, torch.randn(N), torch.zeros(N), {})
+    ppo.compute_returns(obs)
+    return ppo
+
+
+@pytest.mark.parametrize("advantage,ratio,expected", [(1.0, 1.5, -1.2), (-1.0, 0.5, 0.8), (1.0, 0.5, -0.5)])
+def test_surrogate_clipping_table(advantage, ratio, expected):
+    """-min(A r, A clip(r, 0.8, 1.2)) for ratios outside the clip range, positive and negative advantages."""
+    ppo = _direct_ppo(num_learning_epochs=1, num_mini_batches=1, schedule="fixed")
+    ppo.storage.actions_log_prob.sub_(math.log(ratio))
+    ppo.storage.advantages.fill_(advantage)
+    assert ppo.update()["surrogate"] == pytest.approx(expected, rel=1e-5)
+
+
+@pytest.mark.parametrize("clipped,offset,expected", [(True, 0.0, 0.64), (False, 0.0, 0.0), (True, -1.0, 1.0)])
+def test_value_clipping_table(clipped, offset, expected):
+    """Old values 1 below the prediction: the clipped estimate moves only 0.2 towards it."""
+    ppo = _direct_ppo(num_learning_epochs=1, num_mini_batches=1, schedule="fixed", use_clipped_value_loss=clipped)
+    ppo.storage.returns.copy_(ppo.storage.values + offset)
+    ppo.storage.values.sub_(1.0)
+    assert ppo.update()["value"] == pytest.approx(expected, abs=1e-5)
+
+
+def test_mixed_precision_is_opt_in_and_updates():
+    assert _direct_ppo().use_mixed_precision is False
+    ppo = _direct_ppo(use_mixed_precision=True, schedule="fixed")
+    before = [p.clone() for p in ppo.actor.parameters()]
+    losses = ppo.update()
+    assert all(math.isfinite(v) for v in losses.values())
+    assert any(not torch.equal(b, a) for b, a in zip(before, ppo.actor.parameters()))
+
+
+def test_shared_cnn_encoder_is_stepped_once():
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.models import CNNModel
+
+    obs = TensorDict({"policy": torch.randn(4, 3), "image": torch.randn(4, 1, 8, 8)}, batch_size=[4])
+    groups = {"actor": ["policy", "image"], "critic": ["policy", "image"]}
+    cnn_cfg = {"image": {"output_channels": [4], "kernel_size": 3, "stride": 1, "activation": "elu"}}
+    actor = CNNModel(obs, groups, "actor", 2, hidden_dims=[8], cnn_cfg=cnn_cfg,
+                     distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
+    critic = CNNModel(obs, groups, "critic", 1, hidden_dims=[8], cnns=actor.cnns)
+    ppo = PPO(actor, critic, RolloutStorage("rl", 4, 2, obs, [2]), learning_rate=1e-3)
+    params = ppo.optimizer.param_groups[0]["params"]
+    assert len(params) == len({id(p) for p in params})
+    shared = next(actor.cnns.parameters())
+    assert any(shared is p for p in critic.parameters())
+    before = shared.detach().clone()
+    for p in params:
+        p.grad = torch.ones_like(p)
+    ppo.optimizer.step()
+    assert int(ppo.optimizer.state[shared]["step"]) == 1
+    assert (before - shared.detach()).abs().max().item() == pytest.approx(1e-3, abs=1e-6)  # one Adam step of lr
