@@ -103,7 +103,8 @@ def record(envs, seeds=SEEDS, out_dir: str | Path = GOLDEN_DIR, iterations: int 
                 rows = read_curve(os.path.join(tmp, "metrics.csv"))
             write_curve(out_dir / env_name / f"seed{seed}.csv", rows)
             finals.append(final_reward(rows))
-            runs.append({"seed": seed, "wall_s": round(info["wall_s"], 1), "iterations": info["iterations"]})
+            runs.append({"seed": seed, "wall_s": round(info["wall_s"], 1), "iterations": info["iterations"],
+                         "num_threads": info["num_threads"]})  # the thread count sets the matmul summation order
         spec = SPECS[env_name]
         summary["envs"][env_name] = {**summarize(finals), "runs": runs, "num_envs": spec.num_envs,
                                      "num_steps": spec.num_steps, "hidden": list(spec.hidden)}
