@@ -138,8 +138,9 @@ def test_committed_golden_curves_are_consistent():
     summary = golden.load_summary()
     assert set(summary["envs"]) >= {"cartpole", "pendulum", "tracking12", "cartpole_po"}
     for env_name, ref in summary["envs"].items():
+        assert tuple(ref["seeds"]) == golden.seeds_for(env_name)
         finals = [golden.final_reward(golden.read_curve(golden.GOLDEN_DIR / env_name / f"seed{s}.csv"))
-                  for s in golden.SEEDS]
+                  for s in ref["seeds"]]
         assert finals == pytest.approx(ref["final_rewards"])
 
 
@@ -148,3 +149,23 @@ def test_this_framework_passes_the_golden_rule_on_cartpole():
     (res,) = golden.check(["cartpole"], seeds=(0,))
     assert res["all_finite"]
     assert res["mean"] >= res["threshold"], res
+
+
+def test_cpu_path_reproduces_the_upstream_curve_exactly():
+    """Same seed, same environment: the PyTorch path logs the same numbers as upstream rsl_rl did for the golden
+    curve (the first 10 iterations of cart-pole seed 0), not just a statistically equivalent curve."""
+    import tempfile
+
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)  # the thread count of the recording
+    try:
+        with tempfile.TemporaryDirectory() as tmp:
+            R.train("cartpole", 0, tmp, iterations=10)
+            ours = golden.read_curve(os.path.join(tmp, "metrics.csv"))
+    finally:
+        torch.set_num_threads(threads)
+    gold = golden.read_curve(golden.GOLDEN_DIR / "cartpole" / "seed0.csv")[:10]
+    for g, o in zip(gold, ours):
+        for k, v in g.items():
+            if v is not None:
+                assert o[k] == v, (g["iteration"], k, v, o[k])

@@ -1,5 +1,10 @@
 """Pieces shared by the fused engines: normaliser views, CUDA-graph capture, device status checks, the observation
-normaliser update (local or over the peer exchange) and the captured rollout of graph-capturable environments."""
+normaliser update (local or over the peer exchange) and the captured rollout of graph-capturable environments.
+
+The rollout step replaces ``PPO.act`` / ``process_env_step`` (``rsl_rl/algorithms/ppo.py:124-164``); the normaliser
+update is ``EmpiricalNormalization.update`` with its distributed combine (``rsl_rl/modules/normalization.py:51-78``);
+capture-once / replay plays the role of the reference plugin's trace mixin (``rsl_rl_tt/traced.py:15-47``) with CUDA
+graphs."""
 
 from __future__ import annotations
 

@@ -10,7 +10,9 @@ privileged features (|s|^2 / S, |a_prev|^2 / A, episode progress, then zeros) wh
 
 ``step`` performs only asynchronous device work (no host synchronisation), so it can be captured in a CUDA graph. With ``host_noise=True`` the process noise is read from a pinned host pool and copied
 to the device every step (the input of an end-to-end measurement). The same class serves the CPU path, the CUDA path
-and the unmodified-reference benchmark arm; it depends only on torch and a TensorDict class.
+and the unmodified-reference benchmark arm; it depends only on torch and a TensorDict class. It implements rsl_rl's
+environment interface (``rsl_rl/env/vec_env.py:14-102``); the reference plugin benchmarks with a null environment
+instead (``scripts/bench_matrix.py:34-51``), which this package also has (``env/null.py``).
 """
 
 from __future__ import annotations

@@ -3,7 +3,8 @@ and column sums) for one minibatch of ``--rows`` rows.
 
 Run ``python -m tt_rsl_rl_b200.ops.bench_gemm`` and again with ``RLB_GEMM_WIDE=0`` / ``RLB_GEMM_WIDE=1`` in the
 environment to compare the two CTA layouts of the bf16-output epilogues; prints one JSON line of microseconds per
-launch (CUDA events around ``--iters`` launches after 3 warm-up launches) and the achieved bandwidth.
+launch (CUDA events around ``--iters`` launches after 3 warm-up launches) and the achieved bandwidth. The shapes are
+those of ``rsl_rl/modules/mlp.py:16-95`` in the benchmark model.
 """
 
 from __future__ import annotations

@@ -1,6 +1,9 @@
 """Thin Python wrappers around the tcgen05 GEMM (``csrc/gemm_tcgen05.cu``).
 
 All matrices are row-major with a leading dimension (row pitch) in elements; bf16 pitches must be multiples of 8.
+The three roles (forward with bias + ELU, data gradient with ELU', weight gradient) are the ``nn.Linear`` + ELU
+stack of ``rsl_rl/modules/mlp.py:16-95`` and its autograd backward; the reference plugin writes the same VJP by hand
+(``rsl_rl_tt/modules.py:160-262``).
 """
 
 from __future__ import annotations

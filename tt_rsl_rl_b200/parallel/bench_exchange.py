@@ -8,7 +8,8 @@ Reported (rank 0, one JSON line): device time per step (CUDA events around a CUD
 max over ranks; the eager per-launch time is reported as well),
 the roofline time = max(local HBM bytes / measured HBM bandwidth, peer bytes / 770 GB/s per direction), the achieved
 fraction of that roofline, and for comparison the time of the baseline path (NCCL all-reduce of the flat gradient +
-two clip_grad_norm_ + torch.optim.Adam, as upstream rsl_rl does it).
+two clip_grad_norm_ + torch.optim.Adam, as upstream rsl_rl does it: ``rsl_rl/algorithms/ppo.py:304-311`` with the
+bucketed all-reduce of ``rsl_rl/utils/utils.py:345-392``).
 """
 
 from __future__ import annotations

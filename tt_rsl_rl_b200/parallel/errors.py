@@ -1,4 +1,5 @@
-"""Errors raised by the communicator and the device status word."""
+"""Errors raised by the communicator and the device status word. The replica check mirrors the reference plugin's
+(``rsl_rl_tt/ppo.py:678-698``); upstream rsl_rl raises neither."""
 
 
 class CommTimeoutError(RuntimeError):
