@@ -1,8 +1,6 @@
 """Remote environment bridge over ZeroMQ (loopback): equality with the local environment, error replies, timeouts,
 and a runner learning through the bridge."""
 
-import threading
-
 import pytest
 import torch
 

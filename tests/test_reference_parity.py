@@ -114,7 +114,6 @@ def _rollout_into(alg, env, T):
 def _make_ppo_pair(ref, T=8, **kw):
     from rsl_rl.algorithms import PPO as RefPPO
     from rsl_rl.storage import RolloutStorage as RefStorage
-    from rsl_rl.utils import resolve_obs_groups  # noqa: F401
 
     from tt_rsl_rl_b200.algorithms import PPO
     from tt_rsl_rl_b200.storage import RolloutStorage

@@ -28,13 +28,12 @@ from __future__ import annotations
 from itertools import chain
 
 import torch
-import torch.nn as nn
 
 from ..modules import GaussianDistribution, HeteroscedasticGaussianDistribution
 from ..ops import ext
 from ..utils.timer import HostTransfers
 from .base import EngineBase, elu_mlp_reason, elu_stack_reason
-from .mlp_plan import MLPPlan, pad8
+from .mlp_plan import MLPPlan
 
 _GROUP_ACTOR = 0
 _GROUP_CRITIC = 1
