@@ -2,7 +2,9 @@
 
 Transport: ZeroMQ REQ/REP. A message is a multipart list ``[header, buffer_0, buffer_1, ...]``; ``header`` is UTF-8
 JSON ``{"op": ..., "tensors": [{"key": k, "dtype": d, "shape": s}, ...], ...}`` and ``buffer_i`` holds the raw
-little-endian bytes of tensor ``i`` (C order). Keys are ``"obs/<group>"``, ``"rewards"``, ``"dones"``,
+little-endian bytes of tensor ``i`` (C order). Tensor parts are sent from the tensors' own memory and received
+without an intermediate copy (ZeroMQ's zero-copy mode; it copies parts below its threshold itself), so a tensor is
+copied once on each side. Keys are ``"obs/<group>"``, ``"rewards"``, ``"dones"``,
 ``"actions"``, ``"time_outs"``, ``"episode_length_buf"``; scalar logging extras travel in the header (``"log"``).
 
 Operations: ``info`` (sizes and groups), ``get_observations``, ``step`` (actions in, transition out), ``close``.
@@ -36,24 +38,33 @@ class RemoteEnvTimeoutError(TimeoutError):
     """The environment server did not answer within the client's timeout."""
 
 
-def pack(header: dict, tensors: dict[str, torch.Tensor]) -> list[bytes]:
-    """Encode a header and named tensors as a multipart message."""
+def pack(header: dict, tensors: dict[str, torch.Tensor]) -> list:
+    """Encode a header and named tensors as a multipart message: the header's bytes, then one buffer per tensor that
+    views the (CPU, contiguous) tensor's memory, so a zero-copy send moves it without an intermediate bytes copy."""
     meta, frames = [], []
     for key, t in tensors.items():
-        a = t.detach().to("cpu").contiguous()
-        meta.append({"key": key, "dtype": str(a.dtype).replace("torch.", ""), "shape": list(a.shape)})
-        frames.append(a.numpy().tobytes() if a.dtype != torch.bool else a.to(torch.uint8).numpy().tobytes())
+        a = t.detach().to("cpu")
+        if a.dtype == torch.bool:
+            a = a.to(torch.uint8)
+        a = a.contiguous()
+        meta.append({"key": key, "dtype": str(t.dtype).replace("torch.", ""), "shape": list(a.shape)})
+        frames.append(memoryview(a.numpy()).cast("B"))
     return [json.dumps(dict(header, tensors=meta)).encode()] + frames
 
 
-def unpack(frames: list[bytes]) -> tuple[dict, dict[str, torch.Tensor]]:
-    """Decode a multipart message into its header and named CPU tensors."""
-    header = json.loads(frames[0].decode())
+def _buffer(frame):
+    """The bytes of a received part: a ``zmq.Frame`` (zero-copy receive) or any bytes-like object."""
+    return frame.buffer if hasattr(frame, "buffer") else frame
+
+
+def unpack(frames: list) -> tuple[dict, dict[str, torch.Tensor]]:
+    """Decode a multipart message into its header and named CPU tensors (one copy out of the message buffers)."""
+    header = json.loads(bytes(_buffer(frames[0])).decode())
     out = {}
-    for meta, buf in zip(header.get("tensors", []), frames[1:]):
+    for meta, frame in zip(header.get("tensors", []), frames[1:]):
         dt = _DTYPES[meta["dtype"]]
         np_dt = np.uint8 if dt == torch.bool else torch.empty(0, dtype=dt).numpy().dtype
-        arr = np.frombuffer(buf, dtype=np_dt).reshape(meta["shape"])
+        arr = np.frombuffer(_buffer(frame), dtype=np_dt).reshape(meta["shape"])
         t = torch.from_numpy(arr.copy())
         out[meta["key"]] = t.to(torch.bool) if dt == torch.bool else t
     return header, out
@@ -119,14 +130,14 @@ class EnvServer:
         while not self._stop.is_set():
             if not dict(poller.poll(self.poll_ms)):
                 continue
-            frames = self.sock.recv_multipart()
+            frames = self.sock.recv_multipart(copy=False)
             try:
                 header, tensors = unpack(frames)
                 reply = pack(*self._handle(header, tensors))
             except Exception as exc:  # the server survives handler errors and reports them
                 self.errors += 1
                 reply = pack({"op": "error", "message": f"{type(exc).__name__}: {exc}"}, {})
-            self.sock.send_multipart(reply)
+            self.sock.send_multipart(reply, copy=False)
         self.sock.close(0)
 
     def serve_in_thread(self) -> threading.Thread:
@@ -174,8 +185,8 @@ class RemoteVecEnv(VecEnv):
     def _request(self, header: dict, tensors: dict) -> tuple[dict, dict]:
         zmq = self._zmq
         try:
-            self.sock.send_multipart(pack(header, tensors))
-            frames = self.sock.recv_multipart()
+            self.sock.send_multipart(pack(header, tensors), copy=False)
+            frames = self.sock.recv_multipart(copy=False)
         except zmq.error.Again as exc:
             # a REQ socket that missed its reply cannot send again: rebuild it before reporting
             self.sock.close(0)
