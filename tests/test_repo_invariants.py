@@ -74,3 +74,10 @@ def test_every_kernel_wait_loop_is_bounded():
                 found += 1
                 assert bounded.search(window), f"unbounded wait at {p.relative_to(ROOT)}:{i + 1}"
     assert found >= 4  # the peer-flag waits, the grid barrier and the mbarrier wait
+
+
+def test_engines_read_device_data_only_through_named_transfers():
+    """Every device-to-host read of the fused engines goes through ``HostTransfers.read`` with a tag, so the
+    benchmark's count of reads per iteration is complete."""
+    files = [p for p in (PKG / "engine").glob("*.py")] + [PKG / "parallel" / "peer_exchange.py"]
+    assert _offenders(r"\.(item|tolist|cpu|numpy)\(\)", files) == []

@@ -300,7 +300,7 @@ class DistillationEngine(EngineBase):
     def sync_to_torch(self) -> None:
         """Expose the device Adam state through the ``torch.optim`` object (parameters are already views)."""
         opt = self.alg.optimizer
-        step = float(self.step[0].item())
+        step = float(HostTransfers.read(self.step[0:1], "adam_step")[0])
         for p, o in zip(self.params, self.offsets):
             n = p.numel()
             if step > 0:

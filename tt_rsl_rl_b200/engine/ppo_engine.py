@@ -679,7 +679,7 @@ class PPOEngine(EngineBase):
 
     def sync_to_torch(self) -> None:
         """Expose the device optimizer state through the ``torch.optim.Adam`` objects (parameters are already views)."""
-        steps = self.step.tolist()
+        steps = HostTransfers.read(self.step, "adam_step")
         for p, o, g in zip(self.params, self.offsets, self.param_group):
             n = p.numel()
             if steps[g] == 0:
@@ -689,7 +689,7 @@ class PPOEngine(EngineBase):
                 "exp_avg": self.exp_avg[o : o + n].view_as(p),
                 "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p),
             }
-        lrs = self.lr.tolist()
+        lrs = HostTransfers.read(self.lr, "learning_rate")
         for group in self.alg.optimizer.param_groups:
             group["lr"] = lrs[0]
         self.alg._learning_rate = lrs[0]

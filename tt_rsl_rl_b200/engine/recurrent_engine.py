@@ -593,7 +593,7 @@ class RecurrentPPOEngine(EngineBase):
     # ---- checkpoints --------------------------------------------------------------------------------------------------
     def sync_to_torch(self) -> None:
         opt = self.alg.optimizer
-        steps = self.step.tolist()
+        steps = HostTransfers.read(self.step, "adam_step")
         for p, o, g in zip(self.params, self.offsets, self.param_group):
             if steps[g] == 0:
                 continue
