@@ -7,7 +7,10 @@ One step sends the actions (``num_envs x A`` float32) and returns the observatio
 * ``zmq-tcp`` / ``zmq-ipc``: the bridge (:class:`~tt_rsl_rl_b200.env.bridge.RemoteVecEnv` against
   :class:`~tt_rsl_rl_b200.env.bridge.EnvServer`): JSON header plus raw tensor frames;
 * ``zmq-pickle``: ZeroMQ ``send_pyobj`` of the tensors, the naive alternative;
-* ``raw-tcp``: a plain TCP socket carrying the same bytes with a length prefix and no encoding, the loopback floor.
+* ``raw-tcp``: a plain TCP socket carrying the same bytes with a length prefix and no encoding, the loopback floor;
+* ``reference-zmq-tcp``: the reference plugin's own bridge (``rsl_rl_tt/bridge``, importable from an install of the
+  reference) serving the same environment, for a same-machine comparison (its payload differs slightly: it sends
+  dones as bytes and no episode lengths; the bytes it moved are reported).
 
 ::
 
@@ -32,7 +35,7 @@ import time
 import torch
 
 SHAPES = {"tracking12": ({"policy": 36, "privileged": 48}, 12), "humanoid": ({"policy": 96, "critic": 99}, 29)}
-TRANSPORTS = ("zmq-tcp", "zmq-ipc", "zmq-pickle", "raw-tcp")
+TRANSPORTS = ("zmq-tcp", "zmq-ipc", "zmq-pickle", "raw-tcp", "reference-zmq-tcp")
 
 
 def step_bytes(num_envs: int, groups: dict[str, int], num_actions: int) -> tuple[int, int]:
@@ -72,6 +75,27 @@ def _serve_pickle(address, num_envs, shape, ready):
         obs, rew, dones, extras = env.step(msg)
         sock.send_pyobj(({k: obs[k] for k in obs.keys()}, rew, dones, extras["time_outs"], env.episode_length_buf))
     sock.close(0)
+
+
+def _reference_bridge():
+    """The reference plugin's bridge package (``rsl_rl_tt.bridge``), from an install of the reference."""
+    import importlib
+
+    try:
+        return importlib.import_module("rsl_rl_tt.bridge.server"), importlib.import_module("rsl_rl_tt.bridge.client")
+    except ImportError:
+        import baseline
+
+        if not baseline.reference_available():
+            raise
+        baseline.add_reference_to_path()
+        return importlib.import_module("rsl_rl_tt.bridge.server"), importlib.import_module("rsl_rl_tt.bridge.client")
+
+
+def _serve_reference(address, num_envs, shape, ready):
+    server, _ = _reference_bridge()
+    ready.put(address)
+    server.serve(_null_env(num_envs, shape), address, log=lambda m: None)
 
 
 def _recv_exact(conn, n):
@@ -132,6 +156,12 @@ def measure(transport: str, num_envs: int, steps: int = 200, warmup: int = 20, s
         proc = ctx.Process(target=target, args=(address, num_envs, shape, ready), daemon=True)
     elif transport == "raw-tcp":
         proc = ctx.Process(target=_serve_raw, args=(num_envs, shape, ready), daemon=True)
+    elif transport == "reference-zmq-tcp":
+        with socket.socket() as probe:
+            probe.bind(("127.0.0.1", 0))
+            port = probe.getsockname()[1]
+        proc = ctx.Process(target=_serve_reference, args=(f"tcp://127.0.0.1:{port}", num_envs, shape, ready),
+                           daemon=True)
     else:
         raise ValueError(f"unknown transport {transport!r}; known: {TRANSPORTS}")
     proc.start()
@@ -165,6 +195,12 @@ def measure(transport: str, num_envs: int, steps: int = 200, warmup: int = 20, s
             sock.send_pyobj(None)
             sock.recv_pyobj()
             sock.close(0)
+        elif transport == "reference-zmq-tcp":
+            _, client = _reference_bridge()
+            env = client.RemoteVecEnv(endpoint, timeout_s=60)
+            times = _time_steps(lambda: env.step(actions), steps, warmup)
+            moved = (env.stats.sent_bytes + env.stats.received_bytes) // max(1, len(env.stats.step_rtt_s))
+            env.close()
         else:
             from .bridge import RemoteVecEnv
 
@@ -178,6 +214,8 @@ def measure(transport: str, num_envs: int, steps: int = 200, warmup: int = 20, s
             proc.join()
         shutil.rmtree(tmp, ignore_errors=True)
     sent, received = step_bytes(num_envs, groups, A)
+    if transport == "reference-zmq-tcp":
+        sent, received = moved, 0  # measured by the reference client (includes its info / header bytes)
     med = statistics.median(times)
     return {"transport": transport, "num_envs": num_envs, "shape": shape, "steps": steps,
             "ms_per_step": round(med * 1e3, 4), "p90_ms": round(sorted(times)[int(0.9 * (len(times) - 1))] * 1e3, 4),
