@@ -72,3 +72,10 @@ def test_op_profiler_times_launching_entry_points(monkeypatch):
         with ops.profile_ops(FakeEvent, lambda: None, lambda: False), ops.profile_ops(FakeEvent):
             pass
     assert ops._PROFILER is None
+
+
+def test_bridge_bench_runs_the_reference_bridge(ref):
+    from tt_rsl_rl_b200.env.bench_bridge import measure
+
+    res = measure("reference-zmq-tcp", 64, steps=5, warmup=2)
+    assert res["ms_per_step"] > 0 and res["bytes_per_step"] > 64 * 4 * (36 + 48)
