@@ -384,3 +384,78 @@ def test_symmetry_matches_reference_and_probe(ref):
     (p, s), (ap, as_) = maps[0]["policy"], maps[1]
     assert torch.equal(p[1], perm) and torch.equal(s[1], sign)
     assert torch.equal(ap[1], torch.tensor([2, 1, 0])) and torch.equal(as_[1], -torch.ones(3))
+
+
+@pytest.mark.parametrize("cnn_cfg", [
+    {"output_channels": [4, 8], "kernel_size": 3, "stride": [1, 2], "padding": "zeros", "norm": "batch",
+     "max_pool": [True, False], "activation": "elu"},
+    {"output_channels": [6], "kernel_size": 5, "stride": 1, "norm": "layer", "global_pool": "avg",
+     "activation": "relu"},
+])
+def test_cnn_model_state_dict_and_outputs(ref, cnn_cfg):
+    """CNN encoders + MLP head: same parameter names and shapes as upstream, same outputs after loading its weights
+    (batch norm in train and eval mode)."""
+    from rsl_rl.models import CNNModel as RefCNN
+
+    from tt_rsl_rl_b200.models import CNNModel
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    import tensordict as ref_tdm
+
+    torch.manual_seed(0)
+    data = {"policy": torch.randn(6, 5), "image": torch.rand(6, 2, 12, 12)}
+    groups = {"actor": ["policy", "image"]}
+    dist = {"class_name": "GaussianDistribution", "init_std": 0.8}
+    ours = CNNModel(TensorDict(dict(data), batch_size=[6]), groups, "actor", 3, hidden_dims=[16], cnn_cfg=dict(cnn_cfg),
+                    obs_normalization=True, distribution_cfg=dist)
+    theirs = RefCNN(ref_tdm.TensorDict(dict(data), batch_size=[6]), groups, "actor", 3, hidden_dims=[16],
+                    cnn_cfg=dict(cnn_cfg), obs_normalization=True, distribution_cfg=dist)
+    sd_o, sd_r = ours.state_dict(), theirs.state_dict()
+    assert list(sd_o) == list(sd_r)
+    assert all(sd_o[k].shape == sd_r[k].shape for k in sd_o)
+    ours.load_state_dict(sd_r)
+    for mode in ("train", "eval"):
+        getattr(ours, mode)()
+        getattr(theirs, mode)()
+        a = ours(TensorDict(dict(data), batch_size=[6]))
+        b = theirs(ref_tdm.TensorDict(dict(data), batch_size=[6]))
+        torch.testing.assert_close(a, b, **TOL)
+
+
+@pytest.mark.parametrize("where,values", [("obs", [float("nan")]), ("obs", [float("nan"), float("inf")]),
+                                          ("rewards", [float("inf")]), ("dones", [float("nan")]), ("none", [])])
+def test_check_nan_messages_match_reference(ref, where, values):
+    from rsl_rl.utils import check_nan as ref_check
+
+    from tt_rsl_rl_b200.utils.utils import check_nan
+
+    obs = {"policy": torch.zeros(4, 3)}
+    rewards, dones = torch.zeros(4), torch.zeros(4)
+    target = {"obs": obs["policy"].view(-1), "rewards": rewards, "dones": dones}.get(where)
+    for i, v in enumerate(values):
+        target[i] = v
+    outcomes = []
+    for fn in (check_nan, ref_check):
+        try:
+            fn(obs, rewards, dones)
+            outcomes.append(None)
+        except ValueError as exc:
+            outcomes.append(str(exc))
+    assert outcomes[0] == outcomes[1]
+    assert (outcomes[0] is None) == (where == "none")
+
+
+@pytest.mark.parametrize("mode", ["reduce-overhead", "max-autotune"])
+def test_compile_model_rejects_cuda_graph_modes_like_reference(ref, mode):
+    from rsl_rl.utils import compile_model as ref_compile
+
+    from tt_rsl_rl_b200.utils.utils import compile_model
+
+    m = torch.nn.Linear(2, 2)
+    assert compile_model(m, None) is m
+    msgs = []
+    for fn in (compile_model, ref_compile):
+        with pytest.raises(ValueError) as err:
+            fn(m, mode)
+        msgs.append(str(err.value))
+    assert msgs[0] == msgs[1]
