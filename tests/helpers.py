@@ -7,6 +7,7 @@ import copy
 import torch
 
 from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+from tt_rsl_rl_b200.utils.log_writer import LogWriter
 
 
 def small_env(num_envs: int = 64, obs_dim: int = 10, num_actions: int = 3, privileged_dim: int = 2, seed: int = 0,
@@ -41,3 +42,33 @@ def ref_obs(obs, ref_td_cls):
 
 def seed_all(s: int) -> None:
     torch.manual_seed(s)
+
+
+class RecordingWriter(LogWriter):
+    """A LogWriter that records the calls it receives (class-level log, for runner lifecycle tests)."""
+
+    events: list = []
+
+    def __init__(self, log_dir: str, **kwargs) -> None:
+        RecordingWriter.events.append(("init", log_dir))
+
+    def add_scalar(self, tag, scalar_value, global_step):
+        RecordingWriter.events.append(("scalar", tag, global_step))
+
+    def store_config(self, env_cfg, train_cfg):
+        RecordingWriter.events.append(("config",))
+
+    def save_model(self, model_path, it):
+        RecordingWriter.events.append(("model", it))
+
+    def save_file(self, path):
+        RecordingWriter.events.append(("file", path))
+
+    def save_video(self, video, it):
+        RecordingWriter.events.append(("video", str(video), it))
+
+    def stop(self):
+        RecordingWriter.events.append(("stop",))
+
+    def abort(self):
+        RecordingWriter.events.append(("abort",))

@@ -487,3 +487,39 @@ def test_shared_cnn_encoder_is_stepped_once():
     ppo.optimizer.step()
     assert int(ppo.optimizer.state[shared]["step"]) == 1
     assert (before - shared.detach()).abs().max().item() == pytest.approx(1e-3, abs=1e-6)  # one Adam step of lr
+
+
+# ---- writer lifecycle ----------------------------------------------------------------------------------------------------
+def test_writer_lifecycle_on_success_and_on_failure(tmp_path):
+    from helpers import RecordingWriter
+
+    cfg = ppo_cfg(T=4)
+    cfg["logger"] = {"class_name": "helpers:RecordingWriter"}
+    cfg["save_interval"] = 2
+    RecordingWriter.events.clear()
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    runner = OnPolicyRunner(small_env(8), copy.deepcopy(cfg), log_dir=str(tmp_path / "a"), device="cpu")
+    runner.learn(3)
+    kinds = [e[0] for e in RecordingWriter.events]
+    assert kinds[0] == "init" and kinds.count("config") == 1 and kinds[-1] == "stop" and "abort" not in kinds
+    assert [e[1] for e in RecordingWriter.events if e[0] == "model"] == [0, 2, 2]  # interval saves + the final one
+    assert {e[2] for e in RecordingWriter.events if e[0] == "scalar"} == {0, 1, 2}
+
+    class Failing(type(small_env(8))):
+        calls = 0
+
+        def step(self, actions):
+            Failing.calls += 1
+            if Failing.calls > 5:
+                raise RuntimeError("simulator crashed")
+            return super().step(actions)
+
+    RecordingWriter.events.clear()
+    env = small_env(8)
+    env.__class__ = Failing
+    runner = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir=str(tmp_path / "b"), device="cpu")
+    with pytest.raises(RuntimeError, match="simulator crashed"):
+        runner.learn(3)
+    kinds = [e[0] for e in RecordingWriter.events]
+    assert kinds[-1] == "abort" and "stop" not in kinds
