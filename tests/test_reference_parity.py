@@ -18,32 +18,34 @@ def _obs(env):
     return env.get_observations()
 
 
-def _ref_models(ref, obs, groups, A, hidden, hetero=False):
+def _ref_models(ref, obs, groups, A, hidden, hetero=False, std_type="scalar"):
     from rsl_rl.models import MLPModel as RefMLP
 
-    dist = {"class_name": "HeteroscedasticGaussianDistribution" if hetero else "GaussianDistribution", "init_std": 1.0}
+    dist = {"class_name": "HeteroscedasticGaussianDistribution" if hetero else "GaussianDistribution", "init_std": 1.0,
+            "std_type": std_type}
     a = RefMLP(obs, groups, "actor", A, hidden_dims=hidden, obs_normalization=True, distribution_cfg=dist)
     c = RefMLP(obs, groups, "critic", 1, hidden_dims=hidden, obs_normalization=True)
     return a, c
 
 
-def _our_models(obs, groups, A, hidden, hetero=False):
+def _our_models(obs, groups, A, hidden, hetero=False, std_type="scalar"):
     from tt_rsl_rl_b200.models import MLPModel
 
-    dist = {"class_name": "HeteroscedasticGaussianDistribution" if hetero else "GaussianDistribution", "init_std": 1.0}
+    dist = {"class_name": "HeteroscedasticGaussianDistribution" if hetero else "GaussianDistribution", "init_std": 1.0,
+            "std_type": std_type}
     a = MLPModel(obs, groups, "actor", A, hidden_dims=hidden, obs_normalization=True, distribution_cfg=dist)
     c = MLPModel(obs, groups, "critic", 1, hidden_dims=hidden, obs_normalization=True)
     return a, c
 
 
-@pytest.mark.parametrize("hetero", [False, True])
-def test_mlp_model_state_dict_and_outputs(ref, hetero):
+@pytest.mark.parametrize("hetero,std_type", [(False, "scalar"), (True, "scalar"), (False, "log"), (True, "log")])
+def test_mlp_model_state_dict_and_outputs(ref, hetero, std_type):
     env = small_env()
     obs = _obs(env)
     groups = {"actor": ["policy"], "critic": ["critic"]}
     torch.manual_seed(0)
-    ra, rc = _ref_models(ref, obs, groups, 3, [16, 8], hetero)
-    oa, oc = _our_models(obs, groups, 3, [16, 8], hetero)
+    ra, rc = _ref_models(ref, obs, groups, 3, [16, 8], hetero, std_type)
+    oa, oc = _our_models(obs, groups, 3, [16, 8], hetero, std_type)
     assert list(ra.state_dict()) == list(oa.state_dict())
     assert list(rc.state_dict()) == list(oc.state_dict())
     oa.load_state_dict(ra.state_dict())
@@ -111,7 +113,7 @@ def _rollout_into(alg, env, T):
         alg.compute_returns(obs)
 
 
-def _make_ppo_pair(ref, T=8, **kw):
+def _make_ppo_pair(ref, T=8, std_type="scalar", **kw):
     from rsl_rl.algorithms import PPO as RefPPO
     from rsl_rl.storage import RolloutStorage as RefStorage
 
@@ -122,8 +124,8 @@ def _make_ppo_pair(ref, T=8, **kw):
     obs = _obs(env)
     groups = {"actor": ["policy"], "critic": ["critic"]}
     torch.manual_seed(3)
-    ra, rc = _ref_models(ref, obs, groups, 3, [32, 16])
-    oa, oc = _our_models(obs, groups, 3, [32, 16])
+    ra, rc = _ref_models(ref, obs, groups, 3, [32, 16], std_type=std_type)
+    oa, oc = _our_models(obs, groups, 3, [32, 16], std_type=std_type)
     oa.load_state_dict(ra.state_dict())
     oc.load_state_dict(rc.state_dict())
     rs = RefStorage("rl", 32, T, obs, [3], "cpu")
@@ -150,9 +152,10 @@ def test_gae_returns_match_reference(ref):
     torch.testing.assert_close(st_o.advantages, st_r.advantages, **TOL)
 
 
-@pytest.mark.parametrize("clipped", [True, False])
-def test_full_ppo_update_matches_reference(ref, clipped):
-    env, rp, op = _make_ppo_pair(ref, num_learning_epochs=3, num_mini_batches=4, use_clipped_value_loss=clipped)
+@pytest.mark.parametrize("clipped,std_type", [(True, "scalar"), (False, "scalar"), (True, "log")])
+def test_full_ppo_update_matches_reference(ref, clipped, std_type):
+    env, rp, op = _make_ppo_pair(ref, std_type=std_type, num_learning_epochs=3, num_mini_batches=4,
+                                 use_clipped_value_loss=clipped)
     torch.manual_seed(5)
     _rollout_into(rp, env, 8)
     st_r, st_o = rp.storage, op.storage
