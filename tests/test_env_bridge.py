@@ -115,3 +115,67 @@ def test_training_through_the_bridge_equals_local_training():
         remote.close()
     for a, b in zip(local, bridged):
         assert torch.equal(a, b)
+
+
+def test_agent_cfg_conversion_and_loading(tmp_path):
+    import json
+
+    import yaml
+
+    from helpers import ppo_cfg
+
+    from tt_rsl_rl_b200.env import b200_agent_cfg, load_agent_cfg
+
+    host = ppo_cfg()
+    host["class_name"] = "OnPolicyRunner"
+    host["algorithm"]["class_name"] = "rsl_rl.algorithms:PPO"
+    host["actor"]["class_name"] = "rsl_rl.models.MLPModel"
+    host["actor"]["distribution_cfg"]["class_name"] = "rsl_rl.modules:GaussianDistribution"
+    before = json.dumps(host, sort_keys=True)
+    cfg = b200_agent_cfg(host, device="cuda:1", graphs=False, csv_log=True, extra_b200_cfg={"section_timing": True})
+    assert json.dumps(host, sort_keys=True) == before  # the argument is not modified
+    assert cfg["algorithm"]["class_name"] == "PPO" and cfg["actor"]["class_name"] == "MLPModel"
+    assert cfg["actor"]["distribution_cfg"]["class_name"] == "GaussianDistribution"
+    assert cfg["algorithm"]["b200_cfg"] == {"engine": "auto", "graphs": False, "section_timing": True}
+    assert cfg["device"] == "cuda:1" and cfg["logger"]["class_name"].endswith(":CsvLogWriter")
+    assert cfg["actor"]["hidden_dims"] == host["actor"]["hidden_dims"] and cfg["obs_groups"] == host["obs_groups"]
+    with pytest.raises(NotImplementedError):
+        b200_agent_cfg({**host, "class_name": "OffPolicyRunner"})
+    with pytest.raises(NotImplementedError):
+        b200_agent_cfg({**host, "algorithm": {"class_name": "SAC"}})
+    with pytest.raises(ValueError, match="critic"):
+        b200_agent_cfg({k: v for k, v in host.items() if k != "critic"})
+    dist = {"class_name": "DistillationRunner", "obs_groups": {}, "student": {}, "teacher": {},
+            "algorithm": {"class_name": "rsl_rl.algorithms:Distillation"}}
+    assert b200_agent_cfg(dist)["algorithm"]["class_name"] == "Distillation"
+    # JSON and YAML (Isaac Lab dumps tuples with a Python tag)
+    (tmp_path / "agent.json").write_text(json.dumps(host))
+    assert load_agent_cfg(tmp_path / "agent.json") == host
+    (tmp_path / "agent.yaml").write_text(yaml.dump({**host, "clip_actions": (1.0, 2.0)}))
+    loaded = load_agent_cfg(tmp_path / "agent.yaml")
+    assert loaded["clip_actions"] == (1.0, 2.0) and loaded["actor"] == host["actor"]
+    (tmp_path / "bad.json").write_text("[1, 2]")
+    with pytest.raises(ValueError):
+        load_agent_cfg(tmp_path / "bad.json")
+
+
+def test_server_hands_its_agent_cfg_to_the_learner():
+    import copy
+
+    from helpers import ppo_cfg
+
+    from tt_rsl_rl_b200.env import EnvServer, LinearGaussianVecEnv, RemoteVecEnv, b200_agent_cfg
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    host_cfg = ppo_cfg(T=4)
+    srv = EnvServer(LinearGaussianVecEnv(16, obs_dim=6, num_actions=2, privileged_dim=1), "tcp://127.0.0.1:*",
+                    agent_cfg=host_cfg)
+    srv.serve_in_thread()
+    remote = RemoteVecEnv(srv.address, timeout_ms=5000)
+    try:
+        assert remote.agent_cfg == host_cfg
+        cfg = b200_agent_cfg(remote.agent_cfg, device="cpu")
+        runner = OnPolicyRunner(remote, copy.deepcopy(cfg), log_dir=None, device=cfg["device"])
+        runner.learn(1)
+    finally:
+        remote.close()

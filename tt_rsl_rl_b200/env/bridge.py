@@ -7,7 +7,8 @@ without an intermediate copy (ZeroMQ's zero-copy mode; it copies parts below its
 copied once on each side. Keys are ``"obs/<group>"``, ``"rewards"``, ``"dones"``,
 ``"actions"``, ``"time_outs"``, ``"episode_length_buf"``; scalar logging extras travel in the header (``"log"``).
 
-Operations: ``info`` (sizes and groups), ``get_observations``, ``step`` (actions in, transition out), ``close``.
+Operations: ``info`` (sizes, groups and the host's agent configuration if it has one), ``get_observations``, ``step``
+(actions in, transition out), ``close``.
 A handler error is answered with ``{"op": "error", "message": ...}`` and the server keeps serving; the client turns it
 into :class:`RemoteEnvError`. A client whose request gets no reply within ``timeout_ms`` raises
 :class:`RemoteEnvTimeoutError` instead of hanging (and rebuilds its socket, as a REQ socket cannot send twice).
@@ -88,10 +89,13 @@ def _transition(env, obs, rewards=None, dones=None, extras=None) -> tuple[dict, 
 class EnvServer:
     """Serves a :class:`VecEnv` on a ZeroMQ REP socket until a ``close`` request (or :meth:`stop`)."""
 
-    def __init__(self, env, address: str = "tcp://127.0.0.1:5555", poll_ms: int = 100) -> None:
+    def __init__(self, env, address: str = "tcp://127.0.0.1:5555", poll_ms: int = 100,
+                 agent_cfg: dict | None = None) -> None:
         import zmq
 
         self.env = env
+        # the host's training configuration (JSON-serialisable), handed to the learner with "info"
+        self.agent_cfg = None if agent_cfg is None else json.loads(json.dumps(agent_cfg, default=repr))
         self.ctx = zmq.Context.instance()
         self.sock = self.ctx.socket(zmq.REP)
         self.sock.setsockopt(zmq.LINGER, 0)
@@ -108,7 +112,7 @@ class EnvServer:
             groups = {g: list(obs[g].shape[1:]) for g in obs.keys()}
             return {"op": "ok", "num_envs": env.num_envs, "num_actions": env.num_actions,
                     "max_episode_length": int(env.max_episode_length), "groups": groups,
-                    "step_dt": float(getattr(env, "step_dt", 0.0))}, {}
+                    "step_dt": float(getattr(env, "step_dt", 0.0)), "agent_cfg": self.agent_cfg}, {}
         if op == "get_observations":
             return _transition(env, env.get_observations())
         if op == "step":
@@ -167,6 +171,7 @@ class RemoteVecEnv(VecEnv):
         self.max_episode_length = int(info["max_episode_length"])
         self.step_dt = float(info.get("step_dt", 0.0))
         self.groups = info["groups"]
+        self.agent_cfg = info.get("agent_cfg")  # the server's training configuration, if it sent one
         self.episode_length_buf = torch.zeros(self.num_envs, dtype=torch.long, device=self.device)
         self.cfg = {"address": address, "num_envs": self.num_envs}
 
