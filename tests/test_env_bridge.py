@@ -179,3 +179,58 @@ def test_server_hands_its_agent_cfg_to_the_learner():
         runner.learn(1)
     finally:
         remote.close()
+
+
+def test_episode_lengths_reset_protocol_and_stats():
+    import copy
+
+    from helpers import ppo_cfg
+
+    from tt_rsl_rl_b200.env import EnvServer, LinearGaussianVecEnv, RemoteEnvError, RemoteVecEnv
+    from tt_rsl_rl_b200.env import bridge as B
+    from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+    class ResettableEnv(LinearGaussianVecEnv):
+        resets = 0
+
+        def reset(self):
+            ResettableEnv.resets += 1
+            self.episode_length_buf.zero_()
+            return self.get_observations(), {"log": {"resets": torch.tensor(float(ResettableEnv.resets))}}
+
+    local = ResettableEnv(16, obs_dim=6, num_actions=2, privileged_dim=1, episode_length=50)
+    srv = EnvServer(local, "tcp://127.0.0.1:*")
+    srv.serve_in_thread()
+    remote = RemoteVecEnv(srv.address, timeout_ms=5000)
+    try:
+        assert remote.has_reset
+        # the runner's random start lengths reach the simulator
+        runner = OnPolicyRunner(remote, copy.deepcopy(ppo_cfg(T=4)), log_dir=None, device="cpu")
+        runner.learn(1, init_at_random_ep_len=True)
+        assert int(local.episode_length_buf.max()) > 4 and torch.equal(remote.episode_length_buf,
+                                                                      local.episode_length_buf)
+        obs, extras = remote.reset()
+        assert ResettableEnv.resets == 1 and extras["log"]["resets"] == 1.0
+        assert int(remote.episode_length_buf.sum()) == 0 and obs["policy"].shape == (16, 6)
+        s = remote.stats.summary()
+        assert s["step"]["calls"] == 4 and s["set_episode_length_buf"]["calls"] == 1 and s["reset"]["calls"] == 1
+        assert s["received_bytes"] > s["sent_bytes"] > 0
+    finally:
+        remote.close()
+    # a server of another protocol version is refused
+    srv2 = EnvServer(LinearGaussianVecEnv(4, obs_dim=3, num_actions=1), "tcp://127.0.0.1:*")
+    inner = srv2._handle
+
+    def older_server(header, tensors):
+        out = inner(header, tensors)
+        if header.get("op") == "info":
+            out[0]["protocol"] = B.PROTOCOL_VERSION - 1
+        return out
+
+    srv2._handle = older_server
+    srv2.serve_in_thread()
+    try:
+        with pytest.raises(RemoteEnvError, match="protocol"):
+            RemoteVecEnv(srv2.address, timeout_ms=5000)
+    finally:
+        srv2.stop()

@@ -7,8 +7,10 @@ without an intermediate copy (ZeroMQ's zero-copy mode; it copies parts below its
 copied once on each side. Keys are ``"obs/<group>"``, ``"rewards"``, ``"dones"``,
 ``"actions"``, ``"time_outs"``, ``"episode_length_buf"``; scalar logging extras travel in the header (``"log"``).
 
-Operations: ``info`` (sizes, groups and the host's agent configuration if it has one), ``get_observations``, ``step``
-(actions in, transition out), ``close``.
+Operations: ``info`` (protocol version, sizes, groups and the host's agent configuration if it has one),
+``get_observations``, ``reset`` (when the environment has one), ``step`` (actions in, transition out, episode lengths
+included), ``set_episode_length_buf`` (the runner's random start lengths reach the simulator), ``close``. The client
+keeps per-operation call counts, seconds and bytes (``RemoteVecEnv.stats``).
 A handler error is answered with ``{"op": "error", "message": ...}`` and the server keeps serving; the client turns it
 into :class:`RemoteEnvError`. A client whose request gets no reply within ``timeout_ms`` raises
 :class:`RemoteEnvTimeoutError` instead of hanging (and rebuilds its socket, as a REQ socket cannot send twice).
@@ -20,12 +22,15 @@ from __future__ import annotations
 
 import json
 import threading
+import time
 
 import numpy as np
 import torch
 
 from ..utils.tensordict import TensorDict
 from .vec_env import VecEnv
+
+PROTOCOL_VERSION = 1
 
 _DTYPES = {"float32": torch.float32, "float64": torch.float64, "int64": torch.int64, "int32": torch.int32,
            "uint8": torch.uint8, "bool": torch.bool}
@@ -110,11 +115,29 @@ class EnvServer:
         if op == "info":
             obs = env.get_observations()
             groups = {g: list(obs[g].shape[1:]) for g in obs.keys()}
-            return {"op": "ok", "num_envs": env.num_envs, "num_actions": env.num_actions,
-                    "max_episode_length": int(env.max_episode_length), "groups": groups,
-                    "step_dt": float(getattr(env, "step_dt", 0.0)), "agent_cfg": self.agent_cfg}, {}
+            return {"op": "ok", "protocol": PROTOCOL_VERSION, "num_envs": env.num_envs,
+                    "num_actions": env.num_actions, "max_episode_length": int(env.max_episode_length),
+                    "groups": groups, "step_dt": float(getattr(env, "step_dt", 0.0)), "agent_cfg": self.agent_cfg,
+                    "has_reset": callable(getattr(env, "reset", None))}, {"episode_length_buf": env.episode_length_buf}
         if op == "get_observations":
             return _transition(env, env.get_observations())
+        if op == "reset":
+            reset = getattr(env, "reset", None)
+            if not callable(reset):
+                raise ValueError("the environment has no reset()")
+            out = reset()
+            obs, extras = out if isinstance(out, tuple) else (out, {})
+            header, tensors = _transition(env, obs)
+            log = (extras or {}).get("log") or {}
+            header["log"] = {k: float(v.float().mean()) if isinstance(v, torch.Tensor) else float(v) for k, v in log.items()}
+            tensors["episode_length_buf"] = env.episode_length_buf
+            return header, tensors
+        if op == "set_episode_length_buf":
+            buf = tensors["episode_length_buf"]
+            if buf.shape != (env.num_envs,):
+                raise ValueError(f"episode_length_buf must have shape ({env.num_envs},), got {tuple(buf.shape)}")
+            env.episode_length_buf = buf.to(dtype=torch.long, device=env.episode_length_buf.device)
+            return {"op": "ok"}, {}
         if op == "step":
             actions = tensors["actions"]
             if actions.shape != (env.num_envs, env.num_actions):
@@ -153,6 +176,30 @@ class EnvServer:
         self._stop.set()
 
 
+class BridgeStats:
+    """Per-operation call count, seconds and payload bytes seen by a client."""
+
+    def __init__(self) -> None:
+        self.calls: dict[str, int] = {}
+        self.seconds: dict[str, float] = {}
+        self.sent_bytes = 0
+        self.received_bytes = 0
+
+    def add(self, op: str, seconds: float, sent: int, received: int) -> None:
+        self.calls[op] = self.calls.get(op, 0) + 1
+        self.seconds[op] = self.seconds.get(op, 0.0) + seconds
+        self.sent_bytes += sent
+        self.received_bytes += received
+
+    def summary(self) -> dict:
+        return {op: {"calls": n, "ms_per_call": 1e3 * self.seconds[op] / n} for op, n in self.calls.items()} | {
+            "sent_bytes": self.sent_bytes, "received_bytes": self.received_bytes}
+
+
+def _nbytes(frames) -> int:
+    return sum(len(_buffer(f)) if not isinstance(f, memoryview) else f.nbytes for f in frames)
+
+
 class RemoteVecEnv(VecEnv):
     """A :class:`VecEnv` whose simulator runs behind an :class:`EnvServer`."""
 
@@ -164,15 +211,20 @@ class RemoteVecEnv(VecEnv):
         self.timeout_ms = int(timeout_ms)
         self._zmq = zmq
         self.ctx = zmq.Context.instance()
+        self.stats = BridgeStats()
         self._connect()
-        info, _ = self._request({"op": "info"}, {})
+        info, t = self._request({"op": "info"}, {})
+        if info.get("protocol") != PROTOCOL_VERSION:
+            raise RemoteEnvError(f"the server speaks bridge protocol {info.get('protocol')}, this client "
+                                 f"{PROTOCOL_VERSION}")
+        self.has_reset = bool(info.get("has_reset", False))
         self.num_envs = int(info["num_envs"])
         self.num_actions = int(info["num_actions"])
         self.max_episode_length = int(info["max_episode_length"])
         self.step_dt = float(info.get("step_dt", 0.0))
         self.groups = info["groups"]
         self.agent_cfg = info.get("agent_cfg")  # the server's training configuration, if it sent one
-        self.episode_length_buf = torch.zeros(self.num_envs, dtype=torch.long, device=self.device)
+        self._episode_length_buf = t["episode_length_buf"].to(self.device)
         self.cfg = {"address": address, "num_envs": self.num_envs}
 
     @property
@@ -187,10 +239,24 @@ class RemoteVecEnv(VecEnv):
         self.sock.setsockopt(zmq.SNDTIMEO, self.timeout_ms)
         self.sock.connect(self.address)
 
+    @property
+    def episode_length_buf(self) -> torch.Tensor:
+        """Episode lengths of the remote environments (refreshed by every step)."""
+        return self._episode_length_buf
+
+    @episode_length_buf.setter
+    def episode_length_buf(self, value: torch.Tensor) -> None:
+        """Set the remote environments' episode lengths (the runner's random start lengths)."""
+        value = torch.as_tensor(value, dtype=torch.long).reshape(self.num_envs)
+        self._request({"op": "set_episode_length_buf"}, {"episode_length_buf": value})
+        self._episode_length_buf = value.to(self.device)
+
     def _request(self, header: dict, tensors: dict) -> tuple[dict, dict]:
         zmq = self._zmq
+        t0 = time.perf_counter()
         try:
-            self.sock.send_multipart(pack(header, tensors), copy=False)
+            request = pack(header, tensors)
+            self.sock.send_multipart(request, copy=False)
             frames = self.sock.recv_multipart(copy=False)
         except zmq.error.Again as exc:
             # a REQ socket that missed its reply cannot send again: rebuild it before reporting
@@ -200,6 +266,7 @@ class RemoteVecEnv(VecEnv):
                 f"environment server at {self.address} did not answer {header.get('op')!r} within {self.timeout_ms} ms"
             ) from exc
         reply, out = unpack(frames)
+        self.stats.add(header.get("op", "?"), time.perf_counter() - t0, _nbytes(request), _nbytes(frames))
         if reply.get("op") == "error":
             raise RemoteEnvError(reply.get("message", "remote error"))
         return reply, out
@@ -212,12 +279,19 @@ class RemoteVecEnv(VecEnv):
         _, tensors = self._request({"op": "get_observations"}, {})
         return self._obs(tensors)
 
+    def reset(self):
+        """Reset every remote environment (when the server's environment has ``reset()``)."""
+        reply, t = self._request({"op": "reset"}, {})
+        self._episode_length_buf = t["episode_length_buf"].to(self.device)
+        extras = {"log": {k: torch.tensor(v) for k, v in reply["log"].items()}} if reply.get("log") else {}
+        return self._obs(t), extras
+
     def step(self, actions: torch.Tensor):
         reply, t = self._request({"op": "step"}, {"actions": actions.float()})
         obs = self._obs(t)
         rewards = t["rewards"].to(self.device)
         dones = t["dones"].to(self.device)
-        self.episode_length_buf.copy_(t["episode_length_buf"].to(self.device))
+        self._episode_length_buf = t["episode_length_buf"].to(self.device)
         extras = {}
         if "time_outs" in t:
             extras["time_outs"] = t["time_outs"].to(self.device)
