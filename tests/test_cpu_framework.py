@@ -499,3 +499,62 @@ def test_two_ranks_equal_one_rank_on_the_union_minibatch():
         for name, model in (("actor", alg.actor), ("critic", alg.critic)):
             for k, v in model.state_dict().items():
                 torch.testing.assert_close(got[name][k], v, rtol=1e-5, atol=1e-6, msg=f"rank {r} {name}.{k}")
+
+
+# ---- distillation: N ranks vs 1 rank on the union batch -------------------------------------------------------------
+def _distill_union_data(seed, N, T, D, A):
+    g = torch.Generator().manual_seed(seed)
+    return {"obs": torch.randn(T, N, D, generator=g), "teacher": torch.randn(T, N, A, generator=g)}
+
+
+def _distill_union_alg(data, multi_gpu_cfg=None):
+    from tt_rsl_rl_b200.algorithms import Distillation
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.storage import RolloutStorage
+    from tt_rsl_rl_b200.utils.tensordict import TensorDict
+
+    T, N, D = data["obs"].shape
+    A = data["teacher"].shape[2]
+    template = TensorDict({"policy": data["obs"][0]}, batch_size=[N])
+    groups = {"student": ["policy"], "teacher": ["policy"]}
+    torch.manual_seed(0)
+    student = MLPModel(template, groups, "student", A, hidden_dims=[32, 32], obs_normalization=True,
+                       distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0})
+    teacher = MLPModel(template, groups, "teacher", A, hidden_dims=[32, 32])
+    st = RolloutStorage("distillation", N, T, template, [A], "cpu")
+    for t in range(T):
+        tr = RolloutStorage.Transition()
+        tr.observations = TensorDict({"policy": data["obs"][t]}, batch_size=[N])
+        tr.actions = torch.zeros(N, A)
+        tr.privileged_actions = data["teacher"][t]
+        tr.rewards, tr.dones = torch.zeros(N), torch.zeros(N)
+        st.add_transition(tr)
+    return Distillation(student, teacher, st, num_learning_epochs=2, gradient_length=3, max_grad_norm=1.0,
+                        device="cpu", multi_gpu_cfg=multi_gpu_cfg, b200_cfg={"engine": "torch"})
+
+
+def _distill_union_worker(rank, world, port, out_dir):
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "WORLD_SIZE": str(world),
+                       "RANK": str(rank), "LOCAL_RANK": str(rank)})
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    alg = _distill_union_alg(_distill_union_data(20 + rank, 32, 6, 5, 3),
+                             {"global_rank": rank, "local_rank": rank, "world_size": world})
+    alg.update()
+    torch.save(alg.student.state_dict(), os.path.join(out_dir, f"d{rank}.pt"))
+    torch.distributed.destroy_process_group()
+
+
+def test_distillation_two_ranks_equal_one_rank_on_the_union_batch():
+    """Rank-averaged gradients of equal-sized local batches equal the gradient of the union batch, and the student
+    normaliser's global statistics equal the union's (the reference plugin's distillation equivalence test has the
+    same design: ``rsl_rl_tt/testing/distill_equiv.py:32-81``)."""
+    out = tempfile.mkdtemp()
+    torch.multiprocessing.spawn(_distill_union_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    parts = [_distill_union_data(20 + r, 32, 6, 5, 3) for r in range(2)]
+    union = {k: torch.cat([parts[0][k], parts[1][k]], dim=1) for k in parts[0]}
+    alg = _distill_union_alg(union)
+    alg.update()
+    for r in range(2):
+        got = torch.load(os.path.join(out, f"d{r}.pt"))
+        for k, v in alg.student.state_dict().items():
+            torch.testing.assert_close(got[k], v, rtol=1e-5, atol=1e-6, msg=f"rank {r} student.{k}")
