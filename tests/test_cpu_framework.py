@@ -444,7 +444,33 @@ def _union_data(seed, N, T, D, A):
     }
 
 
-def _union_alg(data, multi_gpu_cfg=None):
+def _union_mirror(env=None, obs=None, actions=None):
+    """Two copies: the observation vector reversed with alternating signs, the actions negated."""
+    from tt_rsl_rl_b200.utils.tensordict import TensorDict
+
+    out_obs = out_act = None
+    if obs is not None:
+        x = obs["policy"]
+        sign = torch.ones(x.shape[1])
+        sign[1::2] = -1.0
+        out_obs = TensorDict({"policy": torch.cat([x, x.flip(1) * sign])}, batch_size=[2 * x.shape[0]])
+    if actions is not None:
+        out_act = torch.cat([actions, -actions])
+    return out_obs, out_act
+
+
+def _union_extensions(variant, D):
+    if variant == "rnd":
+        return {"rnd_cfg": {"num_states": D, "obs_groups": {"rnd_state": ["policy"]}, "num_outputs": 4,
+                            "predictor_hidden_dims": [16], "target_hidden_dims": [16], "weight": 1.0,
+                            "state_normalization": True}}
+    if variant == "symmetry":
+        return {"symmetry_cfg": {"env": None, "data_augmentation_func": _union_mirror, "use_data_augmentation": True,
+                                 "use_mirror_loss": True, "mirror_loss_coeff": 0.5}}
+    return {}
+
+
+def _union_alg(data, multi_gpu_cfg=None, variant="plain"):
     from tt_rsl_rl_b200.algorithms import PPO
     from tt_rsl_rl_b200.models import MLPModel
     from tt_rsl_rl_b200.storage import RolloutStorage
@@ -471,32 +497,41 @@ def _union_alg(data, multi_gpu_cfg=None):
     st.returns.copy_(data["returns"])
     st.advantages.copy_(data["advantages"])
     return PPO(actor, critic, st, num_learning_epochs=1, num_mini_batches=1, device="cpu",
-               multi_gpu_cfg=multi_gpu_cfg, b200_cfg={"engine": "torch"})
+               multi_gpu_cfg=multi_gpu_cfg, b200_cfg={"engine": "torch"}, **_union_extensions(variant, D))
 
 
-def _union_worker(rank, world, port, out_dir):
+def _models_of(alg):
+    models = {"actor": alg.actor, "critic": alg.critic}
+    if alg.rnd is not None:
+        models["rnd_predictor"] = alg.rnd.predictor
+        models["rnd_state_normalizer"] = alg.rnd.state_normalizer
+    return models
+
+
+def _union_worker(rank, world, port, out_dir, variant):
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "WORLD_SIZE": str(world),
                        "RANK": str(rank), "LOCAL_RANK": str(rank)})
     torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
     alg = _union_alg(_union_data(10 + rank, 64, 6, 5, 3), {"global_rank": rank, "local_rank": rank,
-                                                            "world_size": world})
-    alg.update()
-    torch.save({"actor": alg.actor.state_dict(), "critic": alg.critic.state_dict(), "lr": alg.learning_rate},
-               os.path.join(out_dir, f"r{rank}.pt"))
+                                                            "world_size": world}, variant)
+    losses = alg.update()
+    torch.save({**{k: m.state_dict() for k, m in _models_of(alg).items()}, "lr": alg.learning_rate,
+                "losses": losses}, os.path.join(out_dir, f"r{rank}.pt"))
     torch.distributed.destroy_process_group()
 
 
-def test_two_ranks_equal_one_rank_on_the_union_minibatch():
+@pytest.mark.parametrize("variant", ["plain", "rnd", "symmetry"])
+def test_two_ranks_equal_one_rank_on_the_union_minibatch(variant):
     out = tempfile.mkdtemp()
-    torch.multiprocessing.spawn(_union_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    torch.multiprocessing.spawn(_union_worker, args=(2, _free_port(), out, variant), nprocs=2, join=True)
     parts = [_union_data(10 + r, 64, 6, 5, 3) for r in range(2)]
     union = {k: torch.cat([parts[0][k], parts[1][k]], dim=1) for k in parts[0]}
-    alg = _union_alg(union)
+    alg = _union_alg(union, variant=variant)
     alg.update()
     for r in range(2):
         got = torch.load(os.path.join(out, f"r{r}.pt"))
         assert got["lr"] == pytest.approx(alg.learning_rate, rel=1e-6)
-        for name, model in (("actor", alg.actor), ("critic", alg.critic)):
+        for name, model in _models_of(alg).items():
             for k, v in model.state_dict().items():
                 torch.testing.assert_close(got[name][k], v, rtol=1e-5, atol=1e-6, msg=f"rank {r} {name}.{k}")
 
