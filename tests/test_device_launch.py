@@ -1,5 +1,6 @@
 """Device guard (checks, per-GPU lock, close hooks) with fake system calls, and the job launcher (locks, records,
-time limit with interrupt then kill) with host-only child processes."""
+time limit with interrupt then kill, restart of a failed job that resumes from its newest checkpoint) with host-only
+child processes."""
 
 import json
 import os
@@ -173,3 +174,51 @@ def test_launch_refuses_a_locked_gpu_and_records_running_jobs(tmp_path):
     out = subprocess.run([sys.executable, "-m", "tt_rsl_rl_b200.launch", "--list", "--run-dir", jobs,
                           "--lock-dir", locks], capture_output=True, text=True, check=True)
     assert json.loads(out.stdout)["jobs"] == []
+
+
+def test_failed_job_is_restarted_and_resumes_from_its_newest_checkpoint(tmp_path):
+    """Attempt 0 crashes in its third iteration (after checkpoints of iterations 0 and 1); attempt 1 resumes from the
+    newest one and finishes the run."""
+    logs = tmp_path / "run"
+    script = _script(tmp_path, f"""
+        import copy, json, os, sys
+        sys.path.insert(0, {os.path.join(os.getcwd(), "tests")!r})
+        sys.path.insert(0, {os.getcwd()!r})
+        import torch
+        from helpers import ppo_cfg, small_env
+        from tt_rsl_rl_b200.runners import OnPolicyRunner
+
+        attempt = int(os.environ["TT_RSL_RL_ATTEMPT"])
+        env = small_env(8)
+        if attempt == 0:
+            step = env.step
+            calls = [0]
+
+            def failing(actions):
+                calls[0] += 1
+                if calls[0] > 2 * 4 + 1:  # inside the third iteration (4 steps each)
+                    raise RuntimeError("simulator crashed")
+                return step(actions)
+
+            env.step = failing
+        cfg = ppo_cfg(T=4)
+        cfg["save_interval"] = 1
+        cfg["logger"] = {{"class_name": "CsvLogWriter"}}
+        runner = OnPolicyRunner(env, copy.deepcopy(cfg), log_dir={str(logs)!r}, device="cpu")
+        resumed = runner.resume_latest()
+        with open(os.path.join({str(tmp_path)!r}, f"attempt{{attempt}}.json"), "w") as f:
+            json.dump({{"resumed": resumed, "start": runner.current_learning_iteration}}, f)
+        runner.learn(4 - runner.current_learning_iteration)
+    """)
+    rc = launch.run_job([script], gpus=[], torchrun=False, retries=2, run_dir=str(tmp_path / "jobs"),
+                        lock_dir=str(tmp_path / "locks"), timeout=300)
+    assert rc == 0
+    a0 = json.loads((tmp_path / "attempt0.json").read_text())
+    a1 = json.loads((tmp_path / "attempt1.json").read_text())
+    assert a0 == {"resumed": None, "start": 0}
+    assert a1["resumed"].endswith("model_1.pt") and a1["start"] == 1
+    assert not (tmp_path / "attempt2.json").exists()
+    from tt_rsl_rl_b200.runners import latest_checkpoint
+
+    assert latest_checkpoint(str(logs)).endswith("model_3.pt")
+    assert latest_checkpoint(str(tmp_path / "missing")) is None

@@ -17,9 +17,11 @@ What it does:
 * the job runs in its own process group. At the time limit the group gets SIGINT (Python raises KeyboardInterrupt,
   so ``finally`` blocks release graphs and process groups), then SIGKILL after ``--grace`` seconds; the exit code is
   then 124, as for ``timeout``. SIGINT / SIGTERM sent to the launcher are passed on the same way.
-* a record ``<run dir>/<tag>-<pid>.json`` (launcher PID, process group, GPUs, command, start time) exists while the
-  job runs; ``--list`` prints the records and the lock holders, ``--stop-mine`` stops the recorded process groups of
-  this user (exact group IDs from the records, never a name pattern).
+* a record ``<run dir>/<tag>-<pid>.json`` (launcher PID, process group, GPUs, command, attempt, start time) exists
+  while the job runs; ``--list`` prints the records and the lock holders, ``--stop-mine`` stops the recorded process
+  groups of this user (exact group IDs from the records, never a name pattern).
+* ``--retries N`` restarts a job that failed (not one that hit the limit or was stopped) with its GPUs still locked;
+  the job reads its attempt number from ``TT_RSL_RL_ATTEMPT`` and resumes from its newest checkpoint.
 
 The reference plugin's job wrapper has the same roles for Tenstorrent trays (``scripts/tt_run.sh``: lock, PID
 record, device isolation, ``timeout`` with SIGINT then SIGKILL; ``scripts/kill_my_jobs.sh``).
@@ -39,6 +41,7 @@ import time
 from .device import LOCKS_HELD_ENV, DeviceGuardError, GpuLock, default_lock_dir, lock_path
 
 RUN_DIR_ENV = "TT_RSL_RL_RUN_DIR"
+ATTEMPT_ENV = "TT_RSL_RL_ATTEMPT"
 EXIT_REFUSED = 3
 EXIT_TIMEOUT = 124
 
@@ -77,39 +80,15 @@ def _signal_group(pgid: int, sig: int) -> None:
         pass
 
 
-def run_job(script: list[str], *, gpus: list[int], nproc: int | None = None, timeout: float | None = None,
-            grace: float = 30.0, tag: str = "job", run_dir: str | None = None, lock_dir: str | None = None,
-            master_port: int | None = None, torchrun: bool = True, env: dict | None = None) -> int:
-    """Run one job as described in the module docstring and return its exit code."""
-    nproc = nproc or max(len(gpus), 1)
-    if gpus and nproc != len(gpus):
-        raise ValueError(f"{len(gpus)} GPUs selected but {nproc} processes requested")
-    lock_dir = lock_dir or default_lock_dir()
-    run_dir = run_dir or default_run_dir()
-    locks: list[GpuLock] = []
-    try:
-        for g in gpus:
-            lk = GpuLock(lock_path(g, lock_dir))
-            lk.acquire()
-            locks.append(lk)
-    except DeviceGuardError as exc:
-        for lk in locks:
-            lk.release()
-        print(f"launch: refused: {exc}", file=sys.stderr)
-        return EXIT_REFUSED
-    child_env = dict(os.environ if env is None else env)
-    if gpus:
-        child_env["CUDA_VISIBLE_DEVICES"] = ",".join(str(g) for g in gpus)
-        child_env[LOCKS_HELD_ENV] = ",".join(str(g) for g in gpus)
-    cmd = build_command(script, nproc, master_port or free_port(), torchrun)
-    os.makedirs(run_dir, exist_ok=True)
-    record = os.path.join(run_dir, f"{tag}-{os.getpid()}.json")
+def _supervise(cmd: list[str], child_env: dict, *, tag: str, gpus: list[int], record: str, timeout: float | None,
+               grace: float, attempt: int) -> tuple[int, str]:
+    """Run ``cmd`` in its own process group under the time limit; returns (exit code, "done" | "timeout" |
+    "stopping")."""
     proc = subprocess.Popen(cmd, env=child_env, start_new_session=True)
     pgid = proc.pid  # a new session: the child leads its own process group
     with open(record, "w") as f:
         json.dump({"tag": tag, "launcher_pid": os.getpid(), "pgid": pgid, "uid": os.getuid(), "gpus": gpus,
-                   "command": cmd, "start": time.time()}, f)
-
+                   "command": cmd, "attempt": attempt, "start": time.time()}, f)
     stopping = {"sig": None}
 
     def forward(signum, _frame):
@@ -139,13 +118,61 @@ def run_job(script: list[str], *, gpus: list[int], nproc: int | None = None, tim
     finally:
         for s, h in old.items():
             signal.signal(s, h)
+    if state == "running" and stopping["sig"] is not None:
+        state = "stopping"
+    return rc, ("done" if state == "running" else state)
+
+
+def run_job(script: list[str], *, gpus: list[int], nproc: int | None = None, timeout: float | None = None,
+            grace: float = 30.0, tag: str = "job", run_dir: str | None = None, lock_dir: str | None = None,
+            master_port: int | None = None, torchrun: bool = True, env: dict | None = None,
+            retries: int = 0) -> int:
+    """Run one job as described in the module docstring and return its exit code.
+
+    ``retries`` restarts a job that failed (non-zero exit, neither the time limit nor a stop request) up to that many
+    times, with the GPUs still locked; the job sees its attempt number in ``TT_RSL_RL_ATTEMPT`` and can resume from
+    its newest checkpoint (``OnPolicyRunner.resume_latest``). The time limit applies to each attempt."""
+    nproc = nproc or max(len(gpus), 1)
+    if gpus and nproc != len(gpus):
+        raise ValueError(f"{len(gpus)} GPUs selected but {nproc} processes requested")
+    lock_dir = lock_dir or default_lock_dir()
+    run_dir = run_dir or default_run_dir()
+    locks: list[GpuLock] = []
+    try:
+        for g in gpus:
+            lk = GpuLock(lock_path(g, lock_dir))
+            lk.acquire()
+            locks.append(lk)
+    except DeviceGuardError as exc:
+        for lk in locks:
+            lk.release()
+        print(f"launch: refused: {exc}", file=sys.stderr)
+        return EXIT_REFUSED
+    child_env = dict(os.environ if env is None else env)
+    if gpus:
+        child_env["CUDA_VISIBLE_DEVICES"] = ",".join(str(g) for g in gpus)
+        child_env[LOCKS_HELD_ENV] = ",".join(str(g) for g in gpus)
+    os.makedirs(run_dir, exist_ok=True)
+    record = os.path.join(run_dir, f"{tag}-{os.getpid()}.json")
+    try:
+        for attempt in range(retries + 1):
+            child_env[ATTEMPT_ENV] = str(attempt)
+            cmd = build_command(script, nproc, master_port or free_port(), torchrun)
+            rc, how = _supervise(cmd, child_env, tag=tag, gpus=gpus, record=record, timeout=timeout, grace=grace,
+                                 attempt=attempt)
+            if how == "timeout":
+                return EXIT_TIMEOUT
+            if rc == 0 or how == "stopping" or attempt == retries:
+                return rc
+            print(f"launch: {tag} attempt {attempt} failed with exit code {rc}; restarting", file=sys.stderr)
+        return rc
+    finally:
         for lk in locks:
             lk.release()
         try:
             os.remove(record)
         except OSError:
             pass
-    return EXIT_TIMEOUT if state == "timeout" else rc
 
 
 def list_jobs(run_dir: str | None = None) -> list[dict]:
@@ -204,6 +231,7 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--nproc", type=int, default=None, help="processes when no GPU is selected")
     ap.add_argument("--timeout", type=float, default=None, help="seconds before the job is interrupted")
     ap.add_argument("--grace", type=float, default=30.0, help="seconds between the interrupt and SIGKILL")
+    ap.add_argument("--retries", type=int, default=0, help="restart a failed job up to this many times")
     ap.add_argument("--tag", default="job")
     ap.add_argument("--master-port", type=int, default=None)
     ap.add_argument("--no-torchrun", action="store_true", help="run the script directly (one process)")
@@ -223,7 +251,7 @@ def main(argv: list[str] | None = None) -> int:
         ap.error("give the job after '--'")
     return run_job(script, gpus=_parse_gpus(args.gpus), nproc=args.nproc, timeout=args.timeout, grace=args.grace,
                    tag=args.tag, run_dir=args.run_dir, lock_dir=args.lock_dir, master_port=args.master_port,
-                   torchrun=not args.no_torchrun)
+                   torchrun=not args.no_torchrun, retries=args.retries)
 
 
 if __name__ == "__main__":

@@ -12,6 +12,7 @@ store, episode bookkeeping)) is captured once and replayed as a single CUDA grap
 from __future__ import annotations
 
 import os
+import re
 import time
 
 import torch
@@ -19,6 +20,18 @@ import torch
 from ..algorithms import PPO
 from ..utils.logger import Logger
 from ..utils.utils import check_nan, resolve_callable
+
+
+def latest_checkpoint(log_dir: str | None) -> str | None:
+    """The ``model_<iteration>.pt`` with the highest iteration in ``log_dir``, or None."""
+    if not log_dir or not os.path.isdir(log_dir):
+        return None
+    best, best_it = None, -1
+    for name in os.listdir(log_dir):
+        m = re.fullmatch(r"model_(\d+)\.pt", name)
+        if m and int(m.group(1)) > best_it:
+            best, best_it = os.path.join(log_dir, name), int(m.group(1))
+    return best
 
 
 class OnPolicyRunner:
@@ -140,6 +153,14 @@ class OnPolicyRunner:
         if self.alg.load(loaded, load_cfg, strict):
             self.current_learning_iteration = loaded["iter"]
         return loaded.get("infos")
+
+    def resume_latest(self, log_dir: str | None = None, **load_kwargs) -> str | None:
+        """Load the newest ``model_<iteration>.pt`` of ``log_dir`` (default: this run's log folder) if there is one:
+        the recovery path after a failed job (``python -m tt_rsl_rl_b200.launch --retries``). Returns the path."""
+        path = latest_checkpoint(log_dir or self.logger.log_dir)
+        if path is not None:
+            self.load(path, **load_kwargs)
+        return path
 
     def get_inference_policy(self, device: str | None = None):
         self.alg.eval_mode()
