@@ -523,3 +523,88 @@ def test_writer_lifecycle_on_success_and_on_failure(tmp_path):
         runner.learn(3)
     kinds = [e[0] for e in RecordingWriter.events]
     assert kinds[-1] == "abort" and "stop" not in kinds
+
+
+# ---- W&B / Neptune writers with fake client modules ------------------------------------------------------------------------
+def _fake_wandb(calls):
+    import types
+
+    m = types.ModuleType("wandb")
+    m.init = lambda **kw: calls.append(("init", kw))
+    m.log = lambda data, step=None: calls.append(("log", data, step))
+    m.save = lambda path, base_path=None: calls.append(("save", path))
+    m.finish = lambda exit_code=0: calls.append(("finish", exit_code))
+    m.Video = lambda path, format=None: ("video-object", path)
+    m.config = types.SimpleNamespace(update=lambda d: calls.append(("config", d)))
+    return m
+
+
+class _FakeNeptuneRun:
+    def __init__(self, calls):
+        self.calls = calls
+
+    def __getitem__(self, key):
+        calls, outer = self.calls, self
+
+        class Field:
+            def log(self, value, step=None):
+                calls.append(("log", key, value, step))
+
+            def upload(self, path):
+                calls.append(("upload", key, path))
+
+        return Field()
+
+    def __setitem__(self, key, value):
+        self.calls.append(("set", key, value))
+
+    def stop(self):
+        self.calls.append(("stop",))
+
+
+def test_wandb_and_neptune_writers_with_fake_clients(tmp_path, monkeypatch):
+    import dataclasses
+    import sys
+    import types
+
+    from tt_rsl_rl_b200.utils import NeptuneLogWriter, WandbLogWriter
+
+    @dataclasses.dataclass
+    class EnvCfg:
+        dt: float = 0.02
+
+    calls = []
+    monkeypatch.setitem(sys.modules, "wandb", _fake_wandb(calls))
+    monkeypatch.setenv("WANDB_USERNAME", "someone")
+    w = WandbLogWriter(str(tmp_path / "wb" / "run_7"), project_name="proj")
+    w.add_scalar("Loss/value", 1.5, 3)
+    w.store_config(EnvCfg(), {"num_steps_per_env": 24})
+    w.save_video(tmp_path / "v.mp4", 4)
+    w.stop()
+    init = calls[0][1]
+    assert init["project"] == "proj" and init["entity"] == "someone" and init["name"] == "run_7"
+    assert ("log", {"Loss/value": 1.5}, 3) in calls
+    assert ("config", {"train_cfg": {"num_steps_per_env": 24}}) in calls and ("config", {"env_cfg": {"dt": 0.02}}) in calls
+    assert any(c[0] == "log" and "video" in c[1] for c in calls) and calls[-1] == ("finish", 0)
+    assert any(p.name.startswith("events.out.tfevents") for p in (tmp_path / "wb" / "run_7").iterdir())  # TensorBoard copy
+
+    calls.clear()
+    neptune = types.ModuleType("neptune")
+    neptune.init_run = lambda project, api_token, **kw: (calls.append(("init", project, api_token)), _FakeNeptuneRun(calls))[1]
+    monkeypatch.setitem(sys.modules, "neptune", neptune)
+    monkeypatch.delenv("NEPTUNE_API_TOKEN", raising=False)
+    with pytest.raises(KeyError, match="NEPTUNE_API_TOKEN"):
+        NeptuneLogWriter(str(tmp_path / "nep" / "run_8"), project_name="proj")
+    monkeypatch.setenv("NEPTUNE_API_TOKEN", "tok")
+    monkeypatch.setenv("NEPTUNE_USERNAME", "me")
+    n = NeptuneLogWriter(str(tmp_path / "nep" / "run_8"), project_name="proj")
+    n.add_scalar("Train/mean_reward/time", 2.0, 5)
+    n.store_config({"a": 1}, {"b": 2})
+    n.save_model(str(tmp_path / "model_5.pt"), 5)
+    n.save_file(str(tmp_path / "repo.diff"))
+    n.stop()
+    assert ("init", "me/proj", "tok") in calls and ("log", "log_dir", "run_8", None) in calls
+    assert ("log", "Train/mean_reward_time", 2.0, 5) in calls
+    assert ("set", "train_cfg", {"b": 2}) in calls and ("set", "env_cfg", {"a": 1}) in calls
+    assert ("upload", "model/saved_model_5", str(tmp_path / "model_5.pt")) in calls
+    assert ("upload", "git_diff/repo", str(tmp_path / "repo.diff")) in calls and calls[-1] == ("stop",)
