@@ -169,3 +169,21 @@ def test_cpu_path_reproduces_the_upstream_curve_exactly():
         for k, v in g.items():
             if v is not None:
                 assert o[k] == v, (g["iteration"], k, v, o[k])
+
+
+def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
+    """``extras["log"]`` means (here the cart-pole's pole angle) appear in every iteration's log with upstream's
+    values (to float32 rounding: they are summed step by step on the device, where upstream concatenates the steps'
+    values and takes one mean)."""
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        rows = {}
+        for impl in ("b200", "upstream"):
+            R.train("cartpole", 0, str(tmp_path / impl), impl=impl, iterations=3)
+            rows[impl] = golden.read_curve(tmp_path / impl / "metrics.csv")
+    finally:
+        torch.set_num_threads(threads)
+    ours, theirs = ([r.get("Episode/pole_angle") for r in rows[k]] for k in ("b200", "upstream"))
+    assert len(ours) == 3 and all(v is not None for v in ours)
+    assert ours == pytest.approx(theirs, rel=1e-6)

@@ -97,10 +97,11 @@ class Logger:
         if info:
             for key, value in info.items():
                 if key not in self._extras_sum:
-                    self._extras_order.append(key)
                     with torch.inference_mode(False):  # a normal tensor: it is also reset outside inference mode
                         self._extras_sum[key] = torch.zeros((), device=self.device)
                     self._extras_cnt[key] = 0
+                if key not in self._extras_order:  # keys seen in this iteration, in order of first appearance
+                    self._extras_order.append(key)
                 v = value if isinstance(value, torch.Tensor) else torch.tensor(float(value))
                 v = v.to(self.device, torch.float32).reshape(-1)
                 self._extras_sum[key] += v.sum()
