@@ -187,3 +187,41 @@ def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
     ours, theirs = ([r.get("Episode/pole_angle") for r in rows[k]] for k in ("b200", "upstream"))
     assert len(ours) == 3 and all(v is not None for v in ours)
     assert ours == pytest.approx(theirs, rel=1e-6)
+
+
+@pytest.mark.parametrize("variant", ["rnd_symmetry", "gru", "lstm", "hetero"])
+def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
+    """Same seeds, same thread count: every logged column except timings (and the float32 rounding of episode
+    extras) is equal to upstream's, iteration by iteration."""
+    import dataclasses
+
+    small = dict(num_envs=64, num_steps=8)
+    if variant == "rnd_symmetry":
+        env_name = "tracking12"
+        spec = R.with_symmetry(env_name, R.with_rnd(env_name, dataclasses.replace(R.SPECS[env_name], **small)))
+    elif variant == "gru":
+        env_name, spec = "cartpole_po", dataclasses.replace(R.SPECS["cartpole_po"], **small)
+    elif variant == "lstm":
+        env_name = "tracking12"
+        spec = R.with_rnn(dataclasses.replace(R.SPECS[env_name], **small), "lstm", 32)
+    else:
+        env_name = "pendulum"
+        spec = dataclasses.replace(R.SPECS[env_name], distribution="HeteroscedasticGaussianDistribution", **small)
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        rows = {}
+        for impl in ("b200", "upstream"):
+            R.train(env_name, 0, str(tmp_path / impl), impl=impl, iterations=3, spec=spec)
+            rows[impl] = golden.read_curve(tmp_path / impl / "metrics.csv")
+    finally:
+        torch.set_num_threads(threads)
+    cols = {k for r in rows["upstream"] for k in r} | {k for r in rows["b200"] for k in r}
+    for c in sorted(cols):
+        if c.startswith("Perf/") or c == "wall_s":
+            continue
+        ours, theirs = [r.get(c) for r in rows["b200"]], [r.get(c) for r in rows["upstream"]]
+        if c.startswith("Episode/"):
+            assert ours == pytest.approx(theirs, rel=1e-6), c
+        else:
+            assert ours == theirs, c
