@@ -462,3 +462,38 @@ def test_compile_model_rejects_cuda_graph_modes_like_reference(ref, mode):
             fn(m, mode)
         msgs.append(str(err.value))
     assert msgs[0] == msgs[1]
+
+
+def test_public_api_signatures_and_defaults_match_reference(ref):
+    """Every public class and function of upstream's packages exists here with the same parameters and defaults
+    (constructors and methods), so user code and configurations carry over."""
+    import importlib
+    import inspect
+
+    checked = 0
+    for pkg in ("algorithms", "models", "modules", "storage", "extensions", "utils", "runners", "env"):
+        theirs, ours = importlib.import_module(f"rsl_rl.{pkg}"), importlib.import_module(f"tt_rsl_rl_b200.{pkg}")
+        for name in dir(theirs):
+            obj = getattr(theirs, name)
+            if name.startswith("_") or inspect.ismodule(obj) or not callable(obj):
+                continue
+            assert hasattr(ours, name), f"{pkg}.{name} missing"
+            mine = getattr(ours, name)
+            pairs = [(obj.__init__, mine.__init__)] if inspect.isclass(obj) else [(obj, mine)]
+            if inspect.isclass(obj):
+                pairs += [(getattr(obj, m), getattr(mine, m)) for m in vars(obj)
+                          if not m.startswith("_") and callable(getattr(obj, m)) and hasattr(mine, m)]
+            for fa, fb in pairs:
+                try:
+                    sa, sb = inspect.signature(fa), inspect.signature(fb)
+                except (TypeError, ValueError):
+                    continue
+                var_kw = any(q.kind == q.VAR_KEYWORD for q in sb.parameters.values())
+                for p, v in sa.parameters.items():
+                    if p == "self" or v.kind in (v.VAR_POSITIONAL, v.VAR_KEYWORD):
+                        continue
+                    assert p in sb.parameters or var_kw, f"{pkg}.{name}: parameter {p} missing"
+                    if p in sb.parameters and v.default is not inspect.Parameter.empty:
+                        assert sb.parameters[p].default == v.default, f"{pkg}.{name}: default of {p}"
+                checked += 1
+    assert checked > 50
