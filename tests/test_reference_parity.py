@@ -497,3 +497,40 @@ def test_public_api_signatures_and_defaults_match_reference(ref):
                         assert sb.parameters[p].default == v.default, f"{pkg}.{name}: default of {p}"
                 checked += 1
     assert checked > 50
+
+
+@pytest.mark.parametrize("kind", ["mlp", "hetero", "gru", "lstm"])
+def test_jit_exported_policies_match_reference(ref, kind):
+    """The scripted inference policy (``as_jit``) computes what upstream's scripted policy computes, hidden state
+    included, for the same weights."""
+    from rsl_rl.models import MLPModel as RefMLP
+    from rsl_rl.models import RNNModel as RefRNN
+
+    from tt_rsl_rl_b200.models import MLPModel, RNNModel
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    import tensordict as ref_tdm
+
+    torch.manual_seed(0)
+    data = {"policy": torch.randn(4, 6)}
+    groups = {"actor": ["policy"]}
+    dist = {"class_name": "HeteroscedasticGaussianDistribution" if kind == "hetero" else "GaussianDistribution"}
+    kw = dict(hidden_dims=[16], obs_normalization=True, distribution_cfg=dist)
+    if kind in ("gru", "lstm"):
+        kw.update(rnn_type=kind, rnn_hidden_dim=8)
+        ours = RNNModel(TensorDict(dict(data), batch_size=[4]), groups, "actor", 3, **kw)
+        theirs = RefRNN(ref_tdm.TensorDict(dict(data), batch_size=[4]), groups, "actor", 3, **kw)
+    else:
+        ours = MLPModel(TensorDict(dict(data), batch_size=[4]), groups, "actor", 3, **kw)
+        theirs = RefMLP(ref_tdm.TensorDict(dict(data), batch_size=[4]), groups, "actor", 3, **kw)
+    theirs.obs_normalizer.update(torch.randn(50, 6) * 3 + 1)
+    ours.load_state_dict(theirs.state_dict())
+    ja, jb = torch.jit.script(ours.as_jit()), torch.jit.script(theirs.as_jit())
+    for _ in range(4):
+        x = torch.randn(1, 6)
+        torch.testing.assert_close(ja(x), jb(x), rtol=0, atol=0)
+    if kind in ("gru", "lstm"):
+        ja.reset()
+        jb.reset()
+        x = torch.randn(1, 6)
+        torch.testing.assert_close(ja(x), jb(x), rtol=0, atol=0)
