@@ -189,7 +189,8 @@ def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
     assert ours == pytest.approx(theirs, rel=1e-6)
 
 
-@pytest.mark.parametrize("variant", ["rnd_symmetry", "gru", "lstm", "hetero"])
+@pytest.mark.parametrize("variant", ["rnd_symmetry", "gru", "lstm", "hetero", "per_minibatch_fixed_lr", "beta",
+                                     "log_std_unclipped"])
 def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
     """Same seeds, same thread count: every logged column except timings (and the float32 rounding of episode
     extras) is equal to upstream's, iteration by iteration."""
@@ -204,9 +205,21 @@ def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
     elif variant == "lstm":
         env_name = "tracking12"
         spec = R.with_rnn(dataclasses.replace(R.SPECS[env_name], **small), "lstm", 32)
-    else:
+    elif variant == "hetero":
         env_name = "pendulum"
         spec = dataclasses.replace(R.SPECS[env_name], distribution="HeteroscedasticGaussianDistribution", **small)
+    elif variant == "per_minibatch_fixed_lr":
+        env_name = "cartpole"
+        alg = {**R.SPECS[env_name].algorithm, "normalize_advantage_per_mini_batch": True, "schedule": "fixed"}
+        spec = dataclasses.replace(R.SPECS[env_name], algorithm=alg, **small)
+    elif variant == "beta":
+        env_name = "pendulum"
+        spec = dataclasses.replace(R.SPECS[env_name], distribution="BetaDistribution", **small)
+    else:
+        env_name = "tracking12"
+        alg = {**R.SPECS[env_name].algorithm, "use_clipped_value_loss": False, "entropy_coef": 0.01}
+        spec = dataclasses.replace(R.SPECS[env_name], algorithm=alg, model={"distribution_cfg": {
+            "class_name": "GaussianDistribution", "init_std": 1.0, "std_type": "log"}}, critic_model={}, **small)
     threads = torch.get_num_threads()
     torch.set_num_threads(2)
     try:

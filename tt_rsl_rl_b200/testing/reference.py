@@ -115,10 +115,18 @@ def with_rnn(spec: RunSpec, rnn_type: str = "gru", hidden_dim: int = 64, num_lay
     return dataclasses.replace(spec, model=model if actor else {}, critic_model=model if critic else {})
 
 
+def _dist_cfg(spec: RunSpec) -> dict:
+    """``distribution_cfg`` of the spec (Gaussian families take an initial std, the Beta policy has none)."""
+    dist = {"class_name": spec.distribution}
+    if "Gaussian" in spec.distribution:
+        dist["init_std"] = spec.init_std
+    return dist
+
+
 def train_cfg(env_name: str, spec: RunSpec | None = None, logger: dict | None = CSV_LOGGER) -> dict:
     """``OnPolicyRunner`` configuration of ``spec`` (default: the environment's own) on ``env_name``."""
     spec = spec or SPECS[env_name]
-    dist = {"class_name": spec.distribution, "init_std": spec.init_std}
+    dist = _dist_cfg(spec)
     mlp = {"class_name": "MLPModel", "hidden_dims": list(spec.hidden), "activation": "elu",
            "obs_normalization": spec.obs_normalization}
     critic_extra = (spec.model or {}) if spec.critic_model is None else spec.critic_model
@@ -161,7 +169,7 @@ def distill_cfg(env_name: str, spec: RunSpec | None = None, logger: dict | None 
     spec = spec or SPECS[env_name]
     model = {"class_name": "MLPModel", "hidden_dims": list(spec.hidden), "activation": "elu",
              "obs_normalization": spec.obs_normalization,
-             "distribution_cfg": {"class_name": spec.distribution, "init_std": spec.init_std}}
+             "distribution_cfg": _dist_cfg(spec)}
     cfg = {
         "num_steps_per_env": spec.num_steps,
         "save_interval": 10_000,
