@@ -283,3 +283,29 @@ def test_checkpoints_after_training_equal_upstream(ref, tmp_path, variant):
         if key in ("actor_state_dict", "critic_state_dict", "rnd_state_dict"):
             assert list(ours[key]) == list(theirs[key]), key  # same names in the same order
         _equal_state(ours[key], theirs[key], key)
+
+
+@pytest.mark.parametrize("loss_type", ["mse", "huber"])
+def test_distillation_logs_equal_upstream(ref, tmp_path, loss_type):
+    """Distillation from the same teacher checkpoint: every logged scalar equals upstream's (episode extras to float32
+    rounding)."""
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        ckpt = R.make_teacher_checkpoint("tracking12", str(tmp_path / "t.pt"), iterations=2, num_envs=64,
+                                         impl="upstream")
+        rows = {}
+        for impl in ("b200", "upstream"):
+            R.train_distillation("tracking12", 0, str(tmp_path / impl), ckpt, impl=impl, iterations=3,
+                                 algorithm={"loss_type": loss_type})
+            rows[impl] = golden.read_curve(tmp_path / impl / "metrics.csv")
+    finally:
+        torch.set_num_threads(threads)
+    for c in sorted({k for r in rows["upstream"] for k in r}):
+        if c.startswith("Perf/") or c == "wall_s":
+            continue
+        ours, theirs = [r.get(c) for r in rows["b200"]], [r.get(c) for r in rows["upstream"]]
+        if c.startswith("Episode/"):
+            assert ours == pytest.approx(theirs, rel=1e-6), c
+        else:
+            assert ours == theirs, c
