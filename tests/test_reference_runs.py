@@ -285,8 +285,8 @@ def test_checkpoints_after_training_equal_upstream(ref, tmp_path, variant):
         _equal_state(ours[key], theirs[key], key)
 
 
-@pytest.mark.parametrize("loss_type", ["mse", "huber"])
-def test_distillation_logs_equal_upstream(ref, tmp_path, loss_type):
+@pytest.mark.parametrize("loss_type,student", [("mse", None), ("huber", None), ("mse", "gru"), ("huber", "lstm")])
+def test_distillation_logs_equal_upstream(ref, tmp_path, loss_type, student):
     """Distillation from the same teacher checkpoint: every logged scalar equals upstream's (episode extras to float32
     rounding)."""
     threads = torch.get_num_threads()
@@ -296,8 +296,10 @@ def test_distillation_logs_equal_upstream(ref, tmp_path, loss_type):
                                          impl="upstream")
         rows = {}
         for impl in ("b200", "upstream"):
+            student_model = None if student is None else {"class_name": "RNNModel", "rnn_type": student,
+                                                          "rnn_hidden_dim": 32}
             R.train_distillation("tracking12", 0, str(tmp_path / impl), ckpt, impl=impl, iterations=3,
-                                 algorithm={"loss_type": loss_type})
+                                 algorithm={"loss_type": loss_type}, student_model=student_model)
             rows[impl] = golden.read_curve(tmp_path / impl / "metrics.csv")
     finally:
         torch.set_num_threads(threads)

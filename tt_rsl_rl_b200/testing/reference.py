@@ -164,8 +164,9 @@ def teacher_train_cfg(env_name: str, logger: dict | None = CSV_LOGGER) -> dict:
 
 
 def distill_cfg(env_name: str, spec: RunSpec | None = None, logger: dict | None = CSV_LOGGER,
-                algorithm: dict | None = None) -> dict:
-    """``DistillationRunner`` configuration: student and teacher MLPs of the spec's size."""
+                algorithm: dict | None = None, student_model: dict | None = None) -> dict:
+    """``DistillationRunner`` configuration: student and teacher MLPs of the spec's size; ``student_model`` adds keys
+    to the student's model config (e.g. a recurrent student: ``{"class_name": "RNNModel", "rnn_type": "gru"}``)."""
     spec = spec or SPECS[env_name]
     model = {"class_name": "MLPModel", "hidden_dims": list(spec.hidden), "activation": "elu",
              "obs_normalization": spec.obs_normalization,
@@ -175,7 +176,7 @@ def distill_cfg(env_name: str, spec: RunSpec | None = None, logger: dict | None 
         "save_interval": 10_000,
         "check_for_nan": True,
         "obs_groups": copy.deepcopy(DISTILL_GROUPS[env_name]),
-        "student": copy.deepcopy(model),
+        "student": {**copy.deepcopy(model), **copy.deepcopy(student_model or {})},
         "teacher": copy.deepcopy(model),
         "algorithm": {**DISTILLATION_ALGORITHM, **(algorithm or {})},
     }
@@ -294,14 +295,15 @@ def make_teacher_checkpoint(env_name: str, path: str, seed: int = 0, iterations:
 
 def build_distillation_runner(env_name: str, seed: int, log_dir: str | None, teacher_ckpt: str, *,
                               impl: str = "b200", device: str = "cpu", spec: RunSpec | None = None,
-                              num_envs: int | None = None, algorithm: dict | None = None):
+                              num_envs: int | None = None, algorithm: dict | None = None,
+                              student_model: dict | None = None):
     """Seed, build the environment and a ``DistillationRunner`` of ``impl``, load the teacher from an RL checkpoint.
     Returns ``(runner, env, spec)``."""
     _check_impl(impl, device)
     spec = spec or SPECS[env_name]
     torch.manual_seed(seed)
     env = make_env(env_name, num_envs or spec.num_envs, seed=seed, device=device)
-    cfg = distill_cfg(env_name, spec, CSV_LOGGER if log_dir else None, algorithm)
+    cfg = distill_cfg(env_name, spec, CSV_LOGGER if log_dir else None, algorithm, student_model)
     if impl == "upstream":
         _, runner_cls, td_cls = upstream_runners()
         runner = runner_cls(UpstreamEnvAdapter(env, td_cls), cfg, log_dir=log_dir, device="cpu")
@@ -314,11 +316,12 @@ def build_distillation_runner(env_name: str, seed: int, log_dir: str | None, tea
 
 
 def train_distillation(env_name: str, seed: int, log_dir: str, teacher_ckpt: str, *, impl: str = "b200",
-                       device: str = "cpu", iterations: int | None = None, algorithm: dict | None = None) -> dict:
+                       device: str = "cpu", iterations: int | None = None, algorithm: dict | None = None,
+                       student_model: dict | None = None) -> dict:
     """Distil ``teacher_ckpt`` into a student; metrics in ``log_dir/metrics.csv``. Returns a summary."""
     os.makedirs(log_dir, exist_ok=True)
     runner, _, spec = build_distillation_runner(env_name, seed, log_dir, teacher_ckpt, impl=impl, device=device,
-                                                algorithm=algorithm)
+                                                algorithm=algorithm, student_model=student_model)
     n_it = DISTILL_ITERATIONS[env_name] if iterations is None else iterations
     t0 = time.time()
     runner.learn(num_learning_iterations=n_it, init_at_random_ep_len=True)
