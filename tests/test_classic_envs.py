@@ -7,9 +7,11 @@ import torch
 
 
 def test_seeded_and_shaped():
-    from tt_rsl_rl_b200.env.classic import BatchedCartPole, BatchedCartPolePO, BatchedPendulum, Tracking12
+    from tt_rsl_rl_b200.env.classic import (BatchedCartPole, BatchedCartPoleImage, BatchedCartPolePO, BatchedPendulum,
+                                            Tracking12)
 
     for cls, dims in ((BatchedCartPole, {"policy": 4}), (BatchedCartPolePO, {"policy": 2}),
+                      (BatchedCartPoleImage, {"policy": 2, "image": 1}),
                       (BatchedPendulum, {"policy": 3}), (Tracking12, {"policy": 36, "privileged": 48})):
         a, b, c = cls(16, seed=3), cls(16, seed=3), cls(16, seed=4)
         obs = a.get_observations()

@@ -190,7 +190,7 @@ def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
 
 
 @pytest.mark.parametrize("variant", ["rnd_symmetry", "gru", "lstm", "hetero", "per_minibatch_fixed_lr", "beta",
-                                     "log_std_unclipped"])
+                                     "log_std_unclipped", "cnn"])
 def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
     """Same seeds, same thread count: every logged column except timings (and the float32 rounding of episode
     extras) is equal to upstream's, iteration by iteration."""
@@ -212,6 +212,11 @@ def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
         env_name = "cartpole"
         alg = {**R.SPECS[env_name].algorithm, "normalize_advantage_per_mini_batch": True, "schedule": "fixed"}
         spec = dataclasses.replace(R.SPECS[env_name], algorithm=alg, **small)
+    elif variant == "cnn":
+        env_name = "cartpole_image"
+        cnn = {"class_name": "CNNModel", "cnn_cfg": {"output_channels": [4, 8], "kernel_size": 3, "stride": [1, 2],
+                                                     "norm": "batch", "activation": "elu"}}
+        spec = dataclasses.replace(R.SPECS["cartpole"], hidden=(32,), model=cnn, **small)
     elif variant == "beta":
         env_name = "pendulum"
         spec = dataclasses.replace(R.SPECS[env_name], distribution="BetaDistribution", **small)

@@ -1,6 +1,6 @@
 """Seeded batched test environments for learning checks (the reference plugin's harness has the same roles:
-``rsl_rl_tt/testing/envs.py``): cart-pole, a partially observed cart-pole (positions only, for recurrent policies),
-pendulum swing-up, and a 12-D trajectory-tracking task with a privileged critic group, terminations, time-outs and
+``rsl_rl_tt/testing/envs.py``): cart-pole, a partially observed cart-pole (positions only, for recurrent policies), a
+cart-pole with a 2-D observation map (for convolutional encoders), pendulum swing-up, and a 12-D trajectory-tracking task with a privileged critic group, terminations, time-outs and
 ``extras["log"]``. All state lives in device tensors; resets and noise come from a per-environment generator.
 
 Dynamics (standard formulations, written from their physics):
@@ -112,6 +112,23 @@ class BatchedCartPolePO(BatchedCartPole):
         return TensorDict({"policy": self.s[:, [0, 2]].clone()}, batch_size=[self.num_envs], device=self.device)
 
 
+class BatchedCartPoleImage(BatchedCartPole):
+    """Cart-pole with a 2-D observation group for convolutional encoders: ``"image"`` is a 1 x 12 x 12 map holding a
+    Gaussian bump at (cart position, pole angle) on a grid spanning the termination limits; ``"policy"`` keeps the
+    velocities."""
+
+    GRID = 12
+    obs_groups_cfg = {"actor": ["policy", "image"], "critic": ["policy", "image"]}
+
+    def _observe(self):
+        g = torch.linspace(-1.0, 1.0, self.GRID, device=self.device)
+        px = (self.s[:, 0] / self.X_LIMIT)[:, None, None]
+        pt = (self.s[:, 2] / self.THETA_LIMIT)[:, None, None]
+        image = torch.exp(-((g[None, :, None] - px) ** 2 + (g[None, None, :] - pt) ** 2) / 0.05)
+        return TensorDict({"policy": self.s[:, [1, 3]].clone(), "image": image.unsqueeze(1)},
+                          batch_size=[self.num_envs], device=self.device)
+
+
 class BatchedPendulum(_SeededBatchEnv):
     num_actions = 1
     time_out_steps = 200
@@ -188,8 +205,8 @@ class Tracking12(_SeededBatchEnv):
         return TensorDict({"policy": policy, "privileged": privileged}, batch_size=[self.num_envs], device=self.device)
 
 
-ENV_CLASSES = {"cartpole": BatchedCartPole, "cartpole_po": BatchedCartPolePO, "pendulum": BatchedPendulum,
-               "tracking12": Tracking12}
+ENV_CLASSES = {"cartpole": BatchedCartPole, "cartpole_po": BatchedCartPolePO, "cartpole_image": BatchedCartPoleImage,
+               "pendulum": BatchedPendulum, "tracking12": Tracking12}
 
 
 def env_class(name: str) -> type[_SeededBatchEnv]:
@@ -205,5 +222,5 @@ def make_env(name: str, num_envs: int, seed: int = 0, device: str | torch.device
     return env_class(name)(num_envs, seed=seed, device=device)
 
 
-__all__ = ["ENV_CLASSES", "BatchedCartPole", "BatchedCartPolePO", "BatchedPendulum", "Tracking12", "env_class",
-           "make_env"]
+__all__ = ["ENV_CLASSES", "BatchedCartPole", "BatchedCartPoleImage", "BatchedCartPolePO", "BatchedPendulum",
+           "Tracking12", "env_class", "make_env"]
