@@ -316,3 +316,26 @@ def test_distillation_logs_equal_upstream(ref, tmp_path, loss_type, student):
             assert ours == pytest.approx(theirs, rel=1e-6), c
         else:
             assert ours == theirs, c
+
+
+def test_tensorboard_runs_convert_and_compare(tmp_path):
+    from torch.utils.tensorboard import SummaryWriter
+
+    for seed, level in ((0, 100.0), (1, 104.0)):
+        w = SummaryWriter(str(tmp_path / f"tb{seed}"))
+        for it in range(20):
+            w.add_scalar("Train/mean_reward", level * it / 19, it)
+            w.add_scalar("Loss/value", 1.0 / (it + 1), it)
+            w.add_scalar("Train/mean_reward/time", 0.0, 1000 + it)  # time-indexed duplicates are dropped
+        w.close()
+        assert golden.tb_to_csv(tmp_path / f"tb{seed}", tmp_path / f"ref{seed}.csv") == 20
+    rows = golden.read_curve(tmp_path / "ref0.csv")
+    assert rows[19]["Train/mean_reward"] == pytest.approx(100.0) and "Train/mean_reward/time" not in rows[0]
+    good = [{"iteration": i, "Train/mean_reward": 100.0} for i in range(20)]
+    bad = [{"iteration": i, "Train/mean_reward": 50.0} for i in range(20)]
+    golden.write_curve(tmp_path / "good.csv", good)
+    golden.write_curve(tmp_path / "bad.csv", bad)
+    refs = [tmp_path / "ref0.csv", tmp_path / "ref1.csv"]
+    assert golden.compare_runs(refs, [tmp_path / "good.csv"])["passes"]
+    assert not golden.compare_runs(refs, [tmp_path / "bad.csv"])["passes"]
+    assert golden.main(["compare", "--ref", *map(str, refs), "--run", str(tmp_path / "good.csv")]) == 0

@@ -13,6 +13,12 @@ Command line::
     python -m tt_rsl_rl_b200.testing.golden record --envs cartpole pendulum --seeds 0 1 2
     python -m tt_rsl_rl_b200.testing.golden summarize --envs cartpole     # statistics from the CSVs in place
     python -m tt_rsl_rl_b200.testing.golden check --envs cartpole --seeds 0 1 2 --device cuda:0
+    python -m tt_rsl_rl_b200.testing.golden tb2csv --tb-dir logs/rsl_rl/cartpole/<run> --out gpu_seed0.csv
+    python -m tt_rsl_rl_b200.testing.golden compare --ref gpu_seed0.csv gpu_seed1.csv --run a/metrics.csv b/metrics.csv
+
+The last two compare any run logged by TensorBoard (an upstream run on a GPU, for instance) with this framework's runs
+under the same rule, as the reference plugin does for its own runs (``scripts/tb_to_csv.py``,
+``scripts/compare_curves.py``).
 """
 
 from __future__ import annotations
@@ -164,9 +170,41 @@ def check(envs, seeds=None, device: str = "cpu", iterations: int | None = None, 
     return out
 
 
+def tb_to_csv(run_dir: str | Path, out: str | Path) -> int:
+    """Scalars of the TensorBoard event files under ``run_dir`` (the default writer of a run, e.g. an Isaac Lab GPU
+    run) as a CSV of this package's layout: ``iteration`` then one column per tag. Returns the number of rows."""
+    from tensorboard.backend.event_processing.event_accumulator import EventAccumulator
+
+    acc = EventAccumulator(str(run_dir), size_guidance={"scalars": 0})  # 0: keep every event
+    acc.Reload()
+    tags = [t for t in acc.Tags()["scalars"] if not t.endswith("/time")]
+    if not tags:
+        raise ValueError(f"no scalar events under {run_dir}")
+    table: dict[int, dict[str, float]] = {}
+    for tag in tags:
+        for ev in acc.Scalars(tag):
+            table.setdefault(int(ev.step), {"iteration": int(ev.step)})[tag] = float(ev.value)
+    rows = [table[k] for k in sorted(table)]
+    write_curve(out, rows, columns=["iteration", *tags])
+    return len(rows)
+
+
+def compare_runs(reference: list[str | Path], runs: list[str | Path]) -> dict:
+    """The acceptance rule between two sets of curves (CSV files; e.g. a GPU reference run converted with
+    :func:`tb_to_csv` against this framework's runs). With one reference seed only the 5 % margin applies."""
+    ref_finals = [final_reward(read_curve(p)) for p in reference]
+    run_curves = [read_curve(p) for p in runs]
+    summary = {"envs": {"runs": summarize(ref_finals)}}
+    return verdict("runs", [final_reward(c) for c in run_curves], all(_curve_finite(c) for c in run_curves), summary)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("mode", choices=("record", "summarize", "check"))
+    ap.add_argument("mode", choices=("record", "summarize", "check", "compare", "tb2csv"))
+    ap.add_argument("--ref", nargs="+", default=None, help="compare: reference curves (CSV)")
+    ap.add_argument("--run", nargs="+", default=None, help="compare: curves of the run under test (CSV)")
+    ap.add_argument("--tb-dir", default=None, help="tb2csv: folder with TensorBoard event files")
+    ap.add_argument("--out", default=None, help="tb2csv: CSV to write")
     ap.add_argument("--envs", nargs="+", default=["cartpole", "pendulum", "tracking12", "cartpole_po"])
     ap.add_argument("--seeds", nargs="+", type=int, default=None, help="default: the environment's golden seeds")
     ap.add_argument("--device", default="cpu", help="check only: device of this framework's run")
@@ -181,6 +219,17 @@ def main(argv=None) -> int:
     if args.mode == "summarize":
         print(json.dumps(summarize_dir(args.envs, args.seeds, args.golden_dir), indent=1))
         return 0
+    if args.mode == "tb2csv":
+        if not (args.tb_dir and args.out):
+            ap.error("tb2csv needs --tb-dir and --out")
+        print(json.dumps({"rows": tb_to_csv(args.tb_dir, args.out), "out": args.out}))
+        return 0
+    if args.mode == "compare":
+        if not (args.ref and args.run):
+            ap.error("compare needs --ref and --run")
+        result = compare_runs(args.ref, args.run)
+        print(json.dumps(result))
+        return 0 if result["passes"] else 1
     results = check(args.envs, args.seeds, args.device, args.iterations, args.log_root, args.golden_dir, args.threads)
     for r in results:
         print(json.dumps(r))
