@@ -339,3 +339,12 @@ def test_tensorboard_runs_convert_and_compare(tmp_path):
     assert golden.compare_runs(refs, [tmp_path / "good.csv"])["passes"]
     assert not golden.compare_runs(refs, [tmp_path / "bad.csv"])["passes"]
     assert golden.main(["compare", "--ref", *map(str, refs), "--run", str(tmp_path / "good.csv")]) == 0
+
+
+def test_stability_measures():
+    rise = [{"iteration": i, "Train/mean_reward": min(500.0, 50.0 * i)} for i in range(15)]
+    s = golden.stability(rise)
+    assert s["first_at_level"] == 10 and s["min_after"] == 500.0 and not s["collapsed"]
+    dip = rise + [{"iteration": 15, "Train/mean_reward": 300.0}, {"iteration": 16, "Train/mean_reward": 500.0}]
+    assert golden.stability(dip)["collapsed"]
+    assert golden.stability([{"iteration": 0, "Train/mean_reward": 10.0}])["first_at_level"] is None

@@ -198,6 +198,18 @@ def compare_runs(reference: list[str | Path], runs: list[str | Path]) -> dict:
     return verdict("runs", [final_reward(c) for c in run_curves], all(_curve_finite(c) for c in run_curves), summary)
 
 
+def stability(rows: list[dict], reach: float = 499.0, collapse: float = 450.0) -> dict:
+    """Whether a run that reached ``reach`` (cart-pole's maximum) later fell below ``collapse``: the first iteration
+    at the level, the lowest reward after it and the final reward (the reference plugin's stability study has the
+    same measures: ``scripts/stability_cartpole.py``)."""
+    rewards = [(r["iteration"], r[REWARD]) for r in rows if r.get(REWARD) is not None]
+    first = next((it for it, v in rewards if v >= reach), None)
+    after = [v for it, v in rewards if first is not None and it >= first]
+    low = min(after) if after else None
+    return {"first_at_level": first, "min_after": low, "final": final_reward(rows),
+            "collapsed": bool(low is not None and low < collapse)}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("mode", choices=("record", "summarize", "check", "compare", "tb2csv"))
