@@ -234,3 +234,34 @@ def test_episode_lengths_reset_protocol_and_stats():
             RemoteVecEnv(srv2.address, timeout_ms=5000)
     finally:
         srv2.stop()
+
+
+def test_command_line_serve_and_train(tmp_path):
+    """The environment host serves a test environment with its run spec; the learner trains against it with the
+    configuration the server sent, writes metrics and checkpoints, and closing the client stops the server."""
+    import socket
+    import subprocess
+    import sys
+
+    from tt_rsl_rl_b200.env import bridge
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    server = subprocess.Popen([sys.executable, "-m", "tt_rsl_rl_b200.env.bridge", "serve", "--local-env", "cartpole",
+                               "--num-envs", "32", "--address", f"tcp://127.0.0.1:{port}"],
+                              stdout=subprocess.PIPE, text=True)
+    try:
+        assert "serving" in server.stdout.readline()
+        rc = bridge.main(["train", "--address", f"tcp://127.0.0.1:{port}", "--iterations", "2",
+                          "--log-dir", str(tmp_path), "--device", "cpu", "--timeout-ms", "30000"])
+        assert rc == 0
+        assert server.wait(timeout=30) == 0
+    finally:
+        if server.poll() is None:
+            server.kill()
+            server.wait()
+    import csv
+
+    rows = list(csv.DictReader(open(tmp_path / "metrics.csv")))
+    assert [r["iteration"] for r in rows] == ["0", "1"] and (tmp_path / "model_1.pt").exists()

@@ -304,3 +304,96 @@ class RemoteVecEnv(VecEnv):
             self._request({"op": "close"}, {})
         finally:
             self.sock.close(0)
+
+
+# ---- command line: serve an environment on one host, train against it on another --------------------------------------
+def _make_served_env(args):
+    if args.local_env:
+        from .classic import make_env
+
+        return make_env(args.local_env, args.num_envs, seed=args.seed, device=args.env_device)
+    from ..utils.utils import resolve_callable
+
+    return resolve_callable(args.env)(**json.loads(args.env_kwargs or "{}"))
+
+
+def serve_main(args) -> int:
+    """Serve an environment until a client closes it (the environment host's side)."""
+    from .agent_cfg import load_agent_cfg
+
+    env = _make_served_env(args)
+    agent_cfg = load_agent_cfg(args.agent_cfg) if args.agent_cfg else None
+    if agent_cfg is None and args.local_env:
+        from ..testing.reference import train_cfg
+
+        agent_cfg = train_cfg(args.local_env, logger=None)  # the test environment's own run spec
+    server = EnvServer(env, args.address, agent_cfg=agent_cfg)
+    print(json.dumps({"serving": server.address, "num_envs": int(env.num_envs)}), flush=True)
+    server.serve()
+    return 0
+
+
+def train_main(args) -> int:
+    """Train against a served environment with the server's (or a saved) agent configuration."""
+    from ..runners import OnPolicyRunner
+    from .agent_cfg import b200_agent_cfg, load_agent_cfg
+
+    env = RemoteVecEnv(args.address, device=args.device, timeout_ms=args.timeout_ms)
+    try:
+        agent_cfg = load_agent_cfg(args.agent_cfg) if args.agent_cfg else env.agent_cfg
+        if agent_cfg is None:
+            raise SystemExit("the server sent no agent configuration; give one with --agent-cfg")
+        cfg = b200_agent_cfg(agent_cfg, device=args.device, engine=args.engine, csv_log=True)
+        runner = OnPolicyRunner(env, cfg, log_dir=args.log_dir, device=cfg["device"])
+        if args.resume:
+            runner.resume_latest()
+        runner.learn(args.iterations, init_at_random_ep_len=True)
+        print(json.dumps({"iterations": args.iterations, "log_dir": args.log_dir, "bridge": env.stats.summary()}))
+    finally:
+        env.close()
+    return 0
+
+
+def main(argv=None) -> int:
+    """``serve`` on the environment host, ``train`` on the learner host::
+
+        python -m tt_rsl_rl_b200.env.bridge serve --local-env tracking12 --num-envs 2048 --address tcp://*:5555
+        python -m tt_rsl_rl_b200.env.bridge serve --env my_pkg.envs:make --env-kwargs '{"num_envs": 4096}' \\
+            --agent-cfg params/agent.yaml --address tcp://*:5555
+        python -m tt_rsl_rl_b200.env.bridge train --address tcp://env-host:5555 --iterations 300 --log-dir logs/run
+
+    The reference plugin splits the same roles over two scripts (``scripts/isaac_env_server.py``,
+    ``scripts/train_isaac.py``)."""
+    import argparse
+
+    ap = argparse.ArgumentParser(prog="python -m tt_rsl_rl_b200.env.bridge", description=main.__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    s = sub.add_parser("serve", help="serve an environment")
+    s.add_argument("--address", default="tcp://127.0.0.1:5555")
+    s.add_argument("--local-env", default=None, help="a seeded test environment of this package")
+    s.add_argument("--env", default=None, help="'module:callable' returning a VecEnv")
+    s.add_argument("--env-kwargs", default=None, help="JSON keyword arguments of --env")
+    s.add_argument("--num-envs", type=int, default=1024)
+    s.add_argument("--seed", type=int, default=0)
+    s.add_argument("--env-device", default="cpu")
+    s.add_argument("--agent-cfg", default=None, help="JSON / YAML agent configuration handed to the learner")
+    t = sub.add_parser("train", help="train against a served environment")
+    t.add_argument("--address", required=True)
+    t.add_argument("--iterations", type=int, default=100)
+    t.add_argument("--log-dir", default=None)
+    t.add_argument("--device", default="cuda:0" if torch.cuda.is_available() else "cpu")
+    t.add_argument("--engine", default="auto", choices=("auto", "torch", "cuda"))
+    t.add_argument("--agent-cfg", default=None, help="override the server's agent configuration")
+    t.add_argument("--timeout-ms", type=int, default=60_000)
+    t.add_argument("--resume", action="store_true", help="continue from the newest checkpoint in --log-dir")
+    args = ap.parse_args(argv)
+    if args.cmd == "serve":
+        if bool(args.local_env) == bool(args.env):
+            ap.error("serve needs exactly one of --local-env and --env")
+        return serve_main(args)
+    return train_main(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
