@@ -608,3 +608,26 @@ def test_wandb_and_neptune_writers_with_fake_clients(tmp_path, monkeypatch):
     assert ("set", "train_cfg", {"b": 2}) in calls and ("set", "env_cfg", {"a": 1}) in calls
     assert ("upload", "model/saved_model_5", str(tmp_path / "model_5.pt")) in calls
     assert ("upload", "git_diff/repo", str(tmp_path / "repo.diff")) in calls and calls[-1] == ("stop",)
+
+
+def test_play_evaluates_the_newest_checkpoint(tmp_path):
+    from tt_rsl_rl_b200.runners import play
+    from tt_rsl_rl_b200.testing import reference as R
+
+    import dataclasses
+
+    spec = dataclasses.replace(R.SPECS["cartpole"], num_envs=64, num_steps=8)
+    R.train("cartpole", 0, str(tmp_path), iterations=2, spec=spec)
+    runner, _, _ = R.build_runner("cartpole", 0, None, spec)  # a checkpoint the CSV run did not write
+    runner.save(str(tmp_path / "model_7.pt"))
+    import contextlib
+    import io
+    import json
+
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        assert play.main(["--run-dir", str(tmp_path), "--env", "cartpole", "--num-envs", "32", "--steps", "300",
+                          "--device", "cpu", "--export-jit", str(tmp_path / "exported")]) == 0
+    out = json.loads(buf.getvalue().strip().splitlines()[-1])
+    assert out["checkpoint"].endswith("model_7.pt") and out["episodes"] > 0 and out["mean_length"] > 0
+    assert (tmp_path / "exported" / "policy.pt").exists()
