@@ -593,3 +593,35 @@ def test_distillation_two_ranks_equal_one_rank_on_the_union_batch():
         got = torch.load(os.path.join(out, f"d{r}.pt"))
         for k, v in alg.student.state_dict().items():
             torch.testing.assert_close(got[k], v, rtol=1e-5, atol=1e-6, msg=f"rank {r} student.{k}")
+
+
+# ---- host-side GEMM planning of the fused engines (no device work) --------------------------------------------------------
+@pytest.mark.parametrize("in_dim,hidden,A,rows", [(96, [512, 256, 128], 29, 98304), (99, [1024, 1024, 512], 1, 4096),
+                                                   (5, [32], 3, 100)])
+def test_mlp_plan_buffers_and_reduction_segments(in_dim, hidden, A, rows):
+    """Buffers of the per-MLP GEMM plan obey the 16-byte row-pitch rule of TMA, the split-K factor fills the GPU once
+    without exceeding the k-blocks, and every weight and bias has a partial-sum segment of the right size."""
+    from tt_rsl_rl_b200.engine.mlp_plan import MLPPlan, pad8, wgrad_splits
+    from tt_rsl_rl_b200.modules.mlp import MLP
+
+    mlp = MLP(in_dim, A, hidden, "elu")
+    sm = 148
+    plan = MLPPlan(mlp, in_dim, rows_roll=rows // 4, rows_train=rows, device=torch.device("cpu"), sm_count=sm)
+    bf16 = [plan.x_roll, plan.x_train, plan.d_head, *plan.h_roll, *plan.h_train, *plan.dz, *plan.w_bf16]
+    assert all(t.dtype == torch.bfloat16 and t.shape[-1] % 8 == 0 for t in bf16)  # 16-byte pitches
+    assert plan.widths == [in_dim, *hidden, A]
+    for lin, s, part in zip(plan.linears, plan.splits, plan.wgrad_partial):
+        kb = (rows + 63) // 64
+        assert 1 <= s <= kb and part.shape == (s, lin.out_features, lin.in_features)
+        assert s == wgrad_splits(lin.out_features, lin.in_features, rows, sm)
+    head = torch.zeros(7, A)
+    segs = plan.reduce_segments(head, 7)
+    for l, lin in enumerate(plan.linears):
+        buf, parts, n = segs[id(lin.weight)]
+        assert n == lin.weight.numel() and buf.numel() == parts * n
+        buf, parts, n = segs[id(lin.bias)]
+        assert n == lin.bias.numel() and buf.numel() == parts * n
+        if l == plan.L - 1:
+            assert buf is head
+    assert len(segs) == 2 * plan.L
+    assert pad8(1) == 8 and pad8(8) == 8 and pad8(29) == 32
