@@ -625,3 +625,43 @@ def test_mlp_plan_buffers_and_reduction_segments(in_dim, hidden, A, rows):
             assert buf is head
     assert len(segs) == 2 * plan.L
     assert pad8(1) == 8 and pad8(8) == 8 and pad8(29) == 32
+
+
+def test_which_configurations_the_fused_engines_take():
+    """The engines' own checks (host-side, no device): what runs fused and why the rest stays on the PyTorch path."""
+    from tt_rsl_rl_b200.engine import PPOEngine, RecurrentPPOEngine
+    from tt_rsl_rl_b200.models import CNNModel, MLPModel, RNNModel
+    from tt_rsl_rl_b200.utils.tensordict import TensorDict
+
+    obs = TensorDict({"policy": torch.zeros(2, 8), "image": torch.zeros(2, 1, 8, 8)}, batch_size=[2])
+    g = {"actor": ["policy"], "critic": ["policy"]}
+    gauss = {"class_name": "GaussianDistribution"}
+
+    def mlp(role, out, act="elu", dist=None, hidden=(32, 32)):
+        return MLPModel(obs, g, role, out, hidden_dims=list(hidden), activation=act, distribution_cfg=dist)
+
+    ok = PPOEngine.supports_models(mlp("actor", 3, dist=gauss), mlp("critic", 1), {})
+    assert ok is None
+    hetero = {"class_name": "HeteroscedasticGaussianDistribution"}
+    assert PPOEngine.supports_models(mlp("actor", 3, dist=hetero), mlp("critic", 1), {}) is None
+    assert "ELU" in PPOEngine.supports_models(mlp("actor", 3, act="relu", dist=gauss), mlp("critic", 1), {})
+    assert "Gaussian" in PPOEngine.supports_models(mlp("actor", 3, dist={"class_name": "BetaDistribution"}),
+                                                   mlp("critic", 1), {})
+    assert "32 actions" in PPOEngine.supports_models(mlp("actor", 40, dist=gauss), mlp("critic", 1), {})
+    assert "Adam" in PPOEngine.supports_models(mlp("actor", 3, dist=gauss), mlp("critic", 1), {"optimizer": "sgd"})
+    cnn_g = {"actor": ["policy", "image"], "critic": ["policy", "image"]}
+    cnn = CNNModel(obs, cnn_g, "actor", 3, hidden_dims=[16], distribution_cfg=gauss,
+                   cnn_cfg={"output_channels": [4], "kernel_size": 3})
+    assert "CNN" in PPOEngine.supports_models(cnn, mlp("critic", 1), {})
+
+    def rnn(role, out, dist=None, rnn_type="gru", hidden=32, layers=1):
+        return RNNModel(obs, g, role, out, hidden_dims=[16], distribution_cfg=dist, rnn_type=rnn_type,
+                        rnn_hidden_dim=hidden, rnn_num_layers=layers)
+
+    assert RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss), rnn("critic", 1), {}) is None
+    assert RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss, "lstm"), rnn("critic", 1, None, "lstm"), {}) is None
+    assert "single-layer" in RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss, layers=2), rnn("critic", 1), {})
+    assert "multiple of 32" in RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss, hidden=20),
+                                                                  rnn("critic", 1), {})
+    assert "RND" in RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss), rnn("critic", 1), {"rnd_cfg": True})
+    assert "not fused" in PPOEngine.supports_models(rnn("actor", 3, gauss), rnn("critic", 1), {})
