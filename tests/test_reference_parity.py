@@ -536,7 +536,7 @@ def test_jit_exported_policies_match_reference(ref, kind):
         torch.testing.assert_close(ja(x), jb(x), rtol=0, atol=0)
 
 
-def _dp_parity_worker(rank, world, port, out_dir):
+def _dp_parity_worker(rank, world, port, out_dir, variant="plain"):
     import os
 
     import baseline
@@ -545,44 +545,68 @@ def _dp_parity_worker(rank, world, port, out_dir):
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
     torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
     mg = {"global_rank": rank, "local_rank": rank, "world_size": world}
-    env, rp, op = _make_ppo_pair(None, num_learning_epochs=2, num_mini_batches=2, multi_gpu_cfg=mg)
+    extra = {}
+    if variant == "rnd":
+        extra["rnd_cfg"] = {"num_states": 10, "obs_groups": {"rnd_state": ["policy"]}, "num_outputs": 4,
+                            "predictor_hidden_dims": [16], "target_hidden_dims": [16], "weight": 0.5,
+                            "state_normalization": True, "reward_normalization": True}
+    env, rp, op = _make_ppo_pair(None, num_learning_epochs=2, num_mini_batches=2, multi_gpu_cfg=mg, **extra)
     torch.manual_seed(50 + rank)  # each rank collects its own rollout
-    _rollout_into(rp, env, 8)
-    st_r, st_o = rp.storage, op.storage
-    for name in ("actions", "rewards", "dones", "values", "actions_log_prob", "returns", "advantages"):
-        getattr(st_o, name).copy_(getattr(st_r, name))
-    st_o.distribution_params = tuple(p.clone() for p in st_r.distribution_params)
-    st_o.observations.copy_(st_r.observations)
-    st_o.step = st_r.step
+    if variant == "rnd":
+        op.rnd.load_state_dict(rp.rnd.state_dict())  # the two constructors drew different initial weights
+        # both implementations collect the same rollout: intrinsic rewards and their globally normalised scale
+        _rollout_into(rp, env, 8)
+        torch.manual_seed(50 + rank)
+        _rollout_into(op, small_env(num_envs=32), 8)
+        torch.testing.assert_close(op.storage.rewards, rp.storage.rewards, rtol=1e-5, atol=1e-6)
+        for name, v in rp.rnd.state_dict().items():  # the reward normaliser's global statistics agree
+            torch.testing.assert_close(op.rnd.state_dict()[name], v, rtol=1e-5, atol=1e-6)
+        for name in ("actions", "values", "actions_log_prob", "returns", "advantages"):
+            torch.testing.assert_close(getattr(op.storage, name), getattr(rp.storage, name), rtol=1e-5, atol=1e-6)
+    else:
+        _rollout_into(rp, env, 8)
+        st_r, st_o = rp.storage, op.storage
+        for name in ("actions", "rewards", "dones", "values", "actions_log_prob", "returns", "advantages"):
+            getattr(st_o, name).copy_(getattr(st_r, name))
+        st_o.distribution_params = tuple(p.clone() for p in st_r.distribution_params)
+        st_o.observations.copy_(st_r.observations)
+        st_o.step = st_r.step
     torch.manual_seed(6)
     loss_r = rp.update()
     torch.manual_seed(6)
     loss_o = op.update()
-    torch.save({"ref": {"actor": rp.actor.state_dict(), "critic": rp.critic.state_dict(), "lr": rp.learning_rate,
-                        "loss": loss_r},
-                "ours": {"actor": op.actor.state_dict(), "critic": op.critic.state_dict(), "lr": op.learning_rate,
-                         "loss": loss_o}}, os.path.join(out_dir, f"{rank}.pt"))
+    def models(alg):
+        out = {"actor": alg.actor.state_dict(), "critic": alg.critic.state_dict()}
+        if alg.rnd is not None:
+            out["rnd"] = alg.rnd.state_dict()
+        return out
+
+    torch.save({"ref": {**models(rp), "lr": rp.learning_rate, "loss": loss_r},
+                "ours": {**models(op), "lr": op.learning_rate, "loss": loss_o}}, os.path.join(out_dir, f"{rank}.pt"))
     torch.distributed.destroy_process_group()
 
 
-def test_data_parallel_update_matches_reference_over_gloo(ref, tmp_path):
+@pytest.mark.parametrize("variant", ["plain", "rnd"])
+def test_data_parallel_update_matches_reference_over_gloo(ref, tmp_path, variant):
     """Two gloo ranks with different rollouts: the data-parallel update (rank-averaged KL and learning rate, bucketed
-    gradient mean, global normaliser statistics) gives the same parameters as upstream's, and replicas agree."""
+    gradient mean, global normaliser statistics; with RND the predictor's gradients and its normalisers too) gives the
+    same parameters as upstream's, and replicas agree."""
     import socket
 
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    torch.multiprocessing.spawn(_dp_parity_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    torch.multiprocessing.spawn(_dp_parity_worker, args=(2, port, str(tmp_path), variant), nprocs=2, join=True)
     res = [torch.load(tmp_path / f"{r}.pt", weights_only=False) for r in range(2)]
     for r in range(2):
         ours, theirs = res[r]["ours"], res[r]["ref"]
         assert ours["lr"] == pytest.approx(theirs["lr"], rel=1e-6)
         for k in theirs["loss"]:
             assert ours["loss"][k] == pytest.approx(theirs["loss"][k], rel=1e-5, abs=1e-7)
-        for model in ("actor", "critic"):
+        models = ("actor", "critic", "rnd") if variant == "rnd" else ("actor", "critic")
+        for model in models:
             for name, v in theirs[model].items():
                 torch.testing.assert_close(ours[model][name], v, atol=1e-5, rtol=1e-4, msg=f"rank {r} {model}.{name}")
-    for model in ("actor", "critic"):
+    for model in models:
         for name, v in res[0]["ours"][model].items():
             assert torch.equal(v, res[1]["ours"][model][name]), f"replicas differ: {model}.{name}"
