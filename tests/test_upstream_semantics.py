@@ -631,3 +631,19 @@ def test_play_evaluates_the_newest_checkpoint(tmp_path):
     out = json.loads(buf.getvalue().strip().splitlines()[-1])
     assert out["checkpoint"].endswith("model_7.pt") and out["episodes"] > 0 and out["mean_length"] > 0
     assert (tmp_path / "exported" / "policy.pt").exists()
+
+
+def test_checkpoint_loads_after_a_rollout_with_rnd_reward_normalisation(tmp_path):
+    """The RND reward normaliser is updated inside the rollout (inference mode); its buffers stay ordinary tensors, so
+    loading a checkpoint into a runner that has already trained works."""
+    cfg = ppo_cfg(T=4)
+    cfg["algorithm"]["rnd_cfg"] = {"weight": 1.0, "num_outputs": 4, "predictor_hidden_dims": [8],
+                                   "target_hidden_dims": [8], "reward_normalization": True,
+                                   "state_normalization": True}
+    r = _runner(cfg)
+    r.learn(2)
+    assert not r.alg.rnd.reward_normalizer.emp_norm._std.is_inference()
+    r.save(str(tmp_path / "m.pt"))
+    r.learn(1)
+    r.load(str(tmp_path / "m.pt"))
+    assert r.current_learning_iteration == 1

@@ -57,7 +57,9 @@ class EmpiricalNormalization(nn.Module):
         delta = batch_mean - self._mean
         self._mean += rate * delta
         self._var += rate * (batch_var - self._var + delta * (batch_mean - self._mean))
-        self._std = torch.sqrt(self._var)
+        # in place: an update inside inference mode (the RND reward normaliser runs in the rollout) keeps the buffer
+        # a normal tensor, so a later load_state_dict can still write it
+        self._std.copy_(torch.sqrt(self._var))
 
     @torch.jit.unused
     def inverse(self, y: torch.Tensor) -> torch.Tensor:
