@@ -536,6 +536,16 @@ def test_jit_exported_policies_match_reference(ref, kind):
         torch.testing.assert_close(ja(x), jb(x), rtol=0, atol=0)
 
 
+def _dp_mirror(env=None, obs=None, actions=None):
+    """Two copies: every observation group and the actions negated."""
+    out_obs = out_act = None
+    if obs is not None:
+        out_obs = type(obs)({g: torch.cat([obs[g], -obs[g]]) for g in obs.keys()}, batch_size=[2 * obs.batch_size[0]])
+    if actions is not None:
+        out_act = torch.cat([actions, -actions])
+    return out_obs, out_act
+
+
 def _dp_parity_worker(rank, world, port, out_dir, variant="plain"):
     import os
 
@@ -550,6 +560,9 @@ def _dp_parity_worker(rank, world, port, out_dir, variant="plain"):
         extra["rnd_cfg"] = {"num_states": 10, "obs_groups": {"rnd_state": ["policy"]}, "num_outputs": 4,
                             "predictor_hidden_dims": [16], "target_hidden_dims": [16], "weight": 0.5,
                             "state_normalization": True, "reward_normalization": True}
+    if variant == "symmetry":
+        extra["symmetry_cfg"] = {"env": None, "data_augmentation_func": _dp_mirror, "use_data_augmentation": True,
+                                 "use_mirror_loss": True, "mirror_loss_coeff": 0.5}
     env, rp, op = _make_ppo_pair(None, num_learning_epochs=2, num_mini_batches=2, multi_gpu_cfg=mg, **extra)
     torch.manual_seed(50 + rank)  # each rank collects its own rollout
     if variant == "rnd":
@@ -586,7 +599,7 @@ def _dp_parity_worker(rank, world, port, out_dir, variant="plain"):
     torch.distributed.destroy_process_group()
 
 
-@pytest.mark.parametrize("variant", ["plain", "rnd"])
+@pytest.mark.parametrize("variant", ["plain", "rnd", "symmetry"])
 def test_data_parallel_update_matches_reference_over_gloo(ref, tmp_path, variant):
     """Two gloo ranks with different rollouts: the data-parallel update (rank-averaged KL and learning rate, bucketed
     gradient mean, global normaliser statistics; with RND the predictor's gradients and its normalisers too) gives the
