@@ -623,3 +623,69 @@ def test_data_parallel_update_matches_reference_over_gloo(ref, tmp_path, variant
     for model in models:
         for name, v in res[0]["ours"][model].items():
             assert torch.equal(v, res[1]["ours"][model][name]), f"replicas differ: {model}.{name}"
+
+
+def _dp_distill_worker(rank, world, port, out_dir):
+    import os
+
+    import baseline
+
+    baseline.add_reference_to_path()
+    from rsl_rl.algorithms import Distillation as RefDist
+    from rsl_rl.models import MLPModel as RefMLP
+    from rsl_rl.storage import RolloutStorage as RefStorage
+
+    from tt_rsl_rl_b200.algorithms import Distillation
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    mg = {"global_rank": rank, "local_rank": rank, "world_size": world}
+    env = small_env(num_envs=16)
+    obs = _obs(env)
+    groups = {"student": ["policy"], "teacher": ["critic"]}
+    torch.manual_seed(10)
+    dist = {"class_name": "GaussianDistribution"}
+    rs_ = RefMLP(obs, groups, "student", 3, hidden_dims=[16, 16], obs_normalization=True, distribution_cfg=dist)
+    rt = RefMLP(obs, groups, "teacher", 3, hidden_dims=[16, 16])
+    os_ = MLPModel(obs, groups, "student", 3, hidden_dims=[16, 16], obs_normalization=True, distribution_cfg=dist)
+    ot = MLPModel(obs, groups, "teacher", 3, hidden_dims=[16, 16])
+    os_.load_state_dict(rs_.state_dict())
+    ot.load_state_dict(rt.state_dict())
+    T = 6
+    rd = RefDist(rs_, rt, RefStorage("distillation", 16, T, obs, [3], "cpu"), gradient_length=3, max_grad_norm=1.0,
+                 multi_gpu_cfg=mg)
+    od = Distillation(os_, ot, RolloutStorage("distillation", 16, T, obs, [3], "cpu"), gradient_length=3,
+                      max_grad_norm=1.0, multi_gpu_cfg=mg)
+    for alg in (rd, od):
+        e = small_env(num_envs=16, seed=4 + rank)  # each rank its own data
+        torch.manual_seed(11 + rank)
+        o = e.get_observations()
+        with torch.inference_mode():
+            for _ in range(T):
+                a = alg.act(o)
+                o, r, d, x = e.step(a)
+                alg.process_env_step(o, r, d, x)
+    loss_r, loss_o = rd.update(), od.update()
+    torch.save({"ref": rd.student.state_dict(), "ours": od.student.state_dict(), "loss_r": loss_r, "loss_o": loss_o},
+               os.path.join(out_dir, f"d{rank}.pt"))
+    torch.distributed.destroy_process_group()
+
+
+def test_data_parallel_distillation_matches_reference_over_gloo(ref, tmp_path):
+    """Two gloo ranks with their own data: the data-parallel distillation update (bucketed gradient mean, global
+    student normaliser) gives the same student as upstream's, and replicas agree."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    torch.multiprocessing.spawn(_dp_distill_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    res = [torch.load(tmp_path / f"d{r}.pt", weights_only=False) for r in range(2)]
+    for r in range(2):
+        assert res[r]["loss_o"]["behavior"] == pytest.approx(res[r]["loss_r"]["behavior"], rel=1e-5)
+        for name, v in res[r]["ref"].items():
+            torch.testing.assert_close(res[r]["ours"][name], v, atol=1e-6, rtol=1e-5, msg=f"rank {r} {name}")
+    for name, v in res[0]["ours"].items():
+        assert torch.equal(v, res[1]["ours"][name]), name
