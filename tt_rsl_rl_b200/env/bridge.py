@@ -34,6 +34,9 @@ PROTOCOL_VERSION = 1
 
 _DTYPES = {"float32": torch.float32, "float64": torch.float64, "int64": torch.int64, "int32": torch.int32,
            "uint8": torch.uint8, "bool": torch.bool}
+# wire dtype name -> numpy dtype of the frame (booleans travel as bytes)
+_NP_DTYPES = {"float32": np.float32, "float64": np.float64, "int64": np.int64, "int32": np.int32, "uint8": np.uint8,
+              "bool": np.uint8}
 
 
 class RemoteEnvError(RuntimeError):
@@ -69,8 +72,7 @@ def unpack(frames: list) -> tuple[dict, dict[str, torch.Tensor]]:
     out = {}
     for meta, frame in zip(header.get("tensors", []), frames[1:]):
         dt = _DTYPES[meta["dtype"]]
-        np_dt = np.uint8 if dt == torch.bool else torch.empty(0, dtype=dt).numpy().dtype
-        arr = np.frombuffer(_buffer(frame), dtype=np_dt).reshape(meta["shape"])
+        arr = np.frombuffer(_buffer(frame), dtype=_NP_DTYPES[meta["dtype"]]).reshape(meta["shape"])
         t = torch.from_numpy(arr.copy())
         out[meta["key"]] = t.to(torch.bool) if dt == torch.bool else t
     return header, out
