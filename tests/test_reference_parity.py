@@ -674,7 +674,7 @@ def _dp_distill_worker(rank, world, port, out_dir):
 
 def test_data_parallel_distillation_matches_reference_over_gloo(ref, tmp_path):
     """Two gloo ranks with their own data: the data-parallel distillation update (bucketed gradient mean, global
-    student normaliser) gives the same student as upstream's, and replicas agree."""
+    student normaliser) gives bit for bit the student upstream's gives, and replicas agree."""
     import socket
 
     with socket.socket() as s:
@@ -683,8 +683,8 @@ def test_data_parallel_distillation_matches_reference_over_gloo(ref, tmp_path):
     torch.multiprocessing.spawn(_dp_distill_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     res = [torch.load(tmp_path / f"d{r}.pt", weights_only=False) for r in range(2)]
     for r in range(2):
-        assert res[r]["loss_o"]["behavior"] == pytest.approx(res[r]["loss_r"]["behavior"], rel=1e-5)
+        assert res[r]["loss_o"] == res[r]["loss_r"]
         for name, v in res[r]["ref"].items():
-            torch.testing.assert_close(res[r]["ours"][name], v, atol=1e-6, rtol=1e-5, msg=f"rank {r} {name}")
+            assert torch.equal(res[r]["ours"][name], v), f"rank {r} {name}"
     for name, v in res[0]["ours"].items():
         assert torch.equal(v, res[1]["ours"][name]), name
