@@ -647,3 +647,38 @@ def test_checkpoint_loads_after_a_rollout_with_rnd_reward_normalisation(tmp_path
     r.learn(1)
     r.load(str(tmp_path / "m.pt"))
     assert r.current_learning_iteration == 1
+
+
+def test_torch_path_stores_the_observations_it_acted_on_with_an_in_place_environment():
+    """An environment that rewrites its observation tensors in place (as graph-capturable ones do) still gives the
+    PyTorch path's storage the observations each action was computed from."""
+    from tt_rsl_rl_b200.env.vec_env import VecEnv
+
+    class InPlaceEnv(VecEnv):
+        graph_capturable = True
+        num_envs, num_actions, max_episode_length = 4, 2, 100
+
+        def __init__(self):
+            self.device = "cpu"
+            self.cfg = {}
+            self.episode_length_buf = torch.zeros(4, dtype=torch.long)
+            self.t = 0
+            self.buf = torch.zeros(4, 3)
+            self.obs = TensorDict({"policy": self.buf, "critic": self.buf}, batch_size=[4])
+            self.seen = []
+
+        def get_observations(self):
+            return self.obs
+
+        def step(self, actions):
+            self.t += 1
+            self.buf.fill_(float(self.t))  # in place
+            return self.obs, torch.zeros(4), torch.zeros(4), {"time_outs": torch.zeros(4)}
+
+    env = InPlaceEnv()
+    r = _runner(ppo_cfg(T=4), env=env)
+    r.alg.update = lambda: {}  # keep the stored rollout
+    r.alg.storage.clear = lambda: None
+    r.learn(1)
+    stored = r.alg.storage.observations["policy"][:, 0, 0]
+    assert stored.tolist() == [0.0, 1.0, 2.0, 3.0]  # step t stores the observation of step t, not t + 1

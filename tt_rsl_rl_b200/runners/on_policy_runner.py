@@ -115,8 +115,12 @@ class OnPolicyRunner:
             return engine.run_captured_rollout(self.env, self.logger, self.cfg)
         check = self.cfg.get("check_for_nan", True)
         use_rnd = bool(self.cfg["algorithm"].get("rnd_cfg"))
+        # a graph-capturable environment rewrites its observation tensors in place every step, while the PyTorch path
+        # keeps a reference to the observations it acted on until the next step is stored (as rsl_rl does): give it a
+        # copy. The fused engines copy observations into their own buffers and need none.
+        copy_obs = engine is None and bool(getattr(self.env, "graph_capturable", False))
         for _ in range(self.cfg["num_steps_per_env"]):
-            actions = self.alg.act(obs)
+            actions = self.alg.act(obs.clone() if copy_obs else obs)
             obs, rewards, dones, extras = self.env.step(actions.to(self.env.device))
             if check and engine is None:
                 check_nan(obs, rewards, dones)
