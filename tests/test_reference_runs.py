@@ -173,8 +173,7 @@ def test_cpu_path_reproduces_the_upstream_curve_exactly():
 
 def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
     """``extras["log"]`` means (here the cart-pole's pole angle) appear in every iteration's log with upstream's
-    values (to float32 rounding: they are summed step by step on the device, where upstream concatenates the steps'
-    values and takes one mean)."""
+    values."""
     threads = torch.get_num_threads()
     torch.set_num_threads(2)
     try:
@@ -186,14 +185,14 @@ def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
         torch.set_num_threads(threads)
     ours, theirs = ([r.get("Episode/pole_angle") for r in rows[k]] for k in ("b200", "upstream"))
     assert len(ours) == 3 and all(v is not None for v in ours)
-    assert ours == pytest.approx(theirs, rel=1e-6)
+    assert ours == theirs
 
 
 @pytest.mark.parametrize("variant", ["rnd_symmetry", "gru", "lstm", "hetero", "per_minibatch_fixed_lr", "beta",
                                      "log_std_unclipped", "cnn"])
 def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
-    """Same seeds, same thread count: every logged column except timings (and the float32 rounding of episode
-    extras) is equal to upstream's, iteration by iteration."""
+    """Same seeds, same thread count: every logged column except timings is equal to upstream's, iteration by
+    iteration."""
     import dataclasses
 
     small = dict(num_envs=64, num_steps=8)
@@ -239,10 +238,7 @@ def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
         if c.startswith("Perf/") or c == "wall_s":
             continue
         ours, theirs = [r.get(c) for r in rows["b200"]], [r.get(c) for r in rows["upstream"]]
-        if c.startswith("Episode/"):
-            assert ours == pytest.approx(theirs, rel=1e-6), c
-        else:
-            assert ours == theirs, c
+        assert ours == theirs, c
 
 
 def _equal_state(a, b, where):
@@ -292,8 +288,7 @@ def test_checkpoints_after_training_equal_upstream(ref, tmp_path, variant):
 
 @pytest.mark.parametrize("loss_type,student", [("mse", None), ("huber", None), ("mse", "gru"), ("huber", "lstm")])
 def test_distillation_logs_equal_upstream(ref, tmp_path, loss_type, student):
-    """Distillation from the same teacher checkpoint: every logged scalar equals upstream's (episode extras to float32
-    rounding)."""
+    """Distillation from the same teacher checkpoint: every logged scalar equals upstream's."""
     threads = torch.get_num_threads()
     torch.set_num_threads(2)
     try:
@@ -312,10 +307,7 @@ def test_distillation_logs_equal_upstream(ref, tmp_path, loss_type, student):
         if c.startswith("Perf/") or c == "wall_s":
             continue
         ours, theirs = [r.get(c) for r in rows["b200"]], [r.get(c) for r in rows["upstream"]]
-        if c.startswith("Episode/"):
-            assert ours == pytest.approx(theirs, rel=1e-6), c
-        else:
-            assert ours == theirs, c
+        assert ours == theirs, c
 
 
 def test_tensorboard_runs_convert_and_compare(tmp_path):

@@ -61,6 +61,9 @@ class Logger:
         self._extras_sum: dict[str, torch.Tensor] = {}
         self._extras_cnt: dict[str, int] = {}
         self._extras_order: list[str] = []
+        # per-step values of eager steps (none are kept while a rollout is being captured into a CUDA graph): their
+        # mean is taken over the concatenation, in one reduction, as rsl_rl does; replayed rollouts use the sums
+        self._extras_vals: dict[str, list[torch.Tensor]] = {}
 
     # ---- writer lifecycle ----------------------------------------------------------------------------------------------
     def init_logging_writer(self) -> None:
@@ -106,6 +109,8 @@ class Logger:
                 v = v.to(self.device, torch.float32).reshape(-1)
                 self._extras_sum[key] += v.sum()
                 self._extras_cnt[key] += v.numel()
+                if not (torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()):
+                    self._extras_vals.setdefault(key, []).append(v.clone())
         rewards = rewards.to(self.device).view(-1)
         if intrinsic_rewards is not None:
             self.cur_ereward_sum += rewards
@@ -184,7 +189,11 @@ class Logger:
         self.tot_time += iteration_time
         extras_string = ""
         for key in self._extras_order:
-            value = (self._extras_sum[key] / max(1, self._extras_cnt[key])).item()
+            vals = self._extras_vals.get(key)
+            if vals and sum(v.numel() for v in vals) == self._extras_cnt[key]:  # every step of the iteration was eager
+                value = torch.mean(torch.cat(vals)).item()
+            else:
+                value = (self._extras_sum[key] / max(1, self._extras_cnt[key])).item()
             if "/" in key:
                 self.writer.add_scalar(key, value, it)
                 extras_string += f"""{f"{key}:":>{pad}} {value:.4f}\n"""
@@ -195,6 +204,7 @@ class Logger:
             v.zero_()  # persistent accumulators (captured rollouts add into them)
         self._extras_cnt = {k: 0 for k in self._extras_cnt}
         self._extras_order.clear()
+        self._extras_vals.clear()
         for key, value in loss_dict.items():
             self.writer.add_scalar(f"Loss/{key}", value, it)
         self.writer.add_scalar("Loss/learning_rate", learning_rate, it)
