@@ -256,16 +256,27 @@ def _equal_state(a, b, where):
         assert a == b, where
 
 
-@pytest.mark.parametrize("variant", ["plain", "rnd_symmetry", "gru"])
+@pytest.mark.parametrize("variant", ["plain", "rnd_symmetry", "gru", "lstm", "cnn", "hetero_log_std", "beta"])
 def test_checkpoints_after_training_equal_upstream(ref, tmp_path, variant):
     """Three iterations from the same seed: the saved checkpoints (models, normalisers, Adam state, RND networks and
     counters, iteration) of this framework and of upstream are equal tensor by tensor."""
     import dataclasses
 
-    env_name = "cartpole_po" if variant == "gru" else "tracking12"
-    spec = dataclasses.replace(R.SPECS[env_name], num_envs=64, num_steps=8)
+    env_name = {"gru": "cartpole_po", "cnn": "cartpole_image", "beta": "pendulum"}.get(variant, "tracking12")
+    base = R.SPECS["cartpole"] if env_name == "cartpole_image" else R.SPECS[env_name]
+    spec = dataclasses.replace(base, num_envs=64, num_steps=8)
     if variant == "rnd_symmetry":
         spec = R.with_symmetry(env_name, R.with_rnd(env_name, spec))
+    elif variant == "lstm":
+        spec = R.with_rnn(spec, "lstm", 32)
+    elif variant == "cnn":
+        spec = dataclasses.replace(spec, hidden=(32,), model={"class_name": "CNNModel", "cnn_cfg": {
+            "output_channels": [4], "kernel_size": 3, "norm": "batch", "activation": "elu"}})
+    elif variant == "hetero_log_std":
+        spec = dataclasses.replace(spec, model={"distribution_cfg": {
+            "class_name": "HeteroscedasticGaussianDistribution", "init_std": 1.0, "std_type": "log"}}, critic_model={})
+    elif variant == "beta":
+        spec = dataclasses.replace(spec, distribution="BetaDistribution")
     threads = torch.get_num_threads()
     torch.set_num_threads(2)
     saved = {}
