@@ -351,3 +351,24 @@ def test_stability_measures():
     dip = rise + [{"iteration": 15, "Train/mean_reward": 300.0}, {"iteration": 16, "Train/mean_reward": 500.0}]
     assert golden.stability(dip)["collapsed"]
     assert golden.stability([{"iteration": 0, "Train/mean_reward": 10.0}])["first_at_level"] is None
+
+
+def test_distillation_checkpoints_after_training_equal_upstream(ref, tmp_path):
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    saved = {}
+    try:
+        ckpt = R.make_teacher_checkpoint("tracking12", str(tmp_path / "t.pt"), iterations=2, num_envs=64,
+                                         impl="upstream")
+        for impl in ("b200", "upstream"):
+            runner, _, _ = R.build_distillation_runner("tracking12", 0, None, ckpt, impl=impl, num_envs=64,
+                                                       student_model={"class_name": "RNNModel", "rnn_type": "gru",
+                                                                      "rnn_hidden_dim": 32})
+            runner.learn(3, init_at_random_ep_len=True)
+            runner.save(str(tmp_path / f"{impl}.pt"))
+            saved[impl] = torch.load(tmp_path / f"{impl}.pt", weights_only=False)
+    finally:
+        torch.set_num_threads(threads)
+    assert sorted(saved["b200"]) == sorted(saved["upstream"])
+    for key in saved["upstream"]:
+        _equal_state(saved["b200"][key], saved["upstream"][key], key)
