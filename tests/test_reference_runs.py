@@ -372,3 +372,35 @@ def test_distillation_checkpoints_after_training_equal_upstream(ref, tmp_path):
     assert sorted(saved["b200"]) == sorted(saved["upstream"])
     for key in saved["upstream"]:
         _equal_state(saved["b200"][key], saved["upstream"][key], key)
+
+
+def test_resumed_training_equals_upstream(ref, tmp_path):
+    """Save after two iterations, load into a fresh runner and train two more: iteration numbers, logged scalars and
+    the final checkpoint equal upstream's doing the same."""
+    import dataclasses
+
+    spec = dataclasses.replace(R.SPECS["tracking12"], num_envs=64, num_steps=8)
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    out = {}
+    try:
+        for impl in ("b200", "upstream"):
+            first, _, _ = R.build_runner("tracking12", 0, None, spec, impl=impl)
+            first.learn(2, init_at_random_ep_len=True)
+            first.save(str(tmp_path / f"{impl}_a.pt"))
+            log_dir = str(tmp_path / impl)
+            second, _, _ = R.build_runner("tracking12", 1, log_dir, spec, impl=impl)
+            second.load(str(tmp_path / f"{impl}_a.pt"))
+            second.learn(2)
+            second.logger.writer.stop()
+            out[impl] = (golden.read_curve(tmp_path / impl / "metrics.csv"),
+                         torch.load(os.path.join(log_dir, "model_2.pt"), weights_only=False))
+    finally:
+        torch.set_num_threads(threads)
+    (rows_o, ck_o), (rows_u, ck_u) = out["b200"], out["upstream"]
+    assert [r["iteration"] for r in rows_o] == [r["iteration"] for r in rows_u] == [1, 2]
+    for c in rows_u[0]:
+        if not c.startswith("Perf/") and c != "wall_s":
+            assert [r.get(c) for r in rows_o] == [r.get(c) for r in rows_u], c
+    for key in ck_u:
+        _equal_state(ck_o[key], ck_u[key], key)
