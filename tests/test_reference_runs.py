@@ -189,7 +189,7 @@ def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
 
 
 @pytest.mark.parametrize("variant", ["rnd_symmetry", "gru", "lstm", "hetero", "per_minibatch_fixed_lr", "beta",
-                                     "log_std_unclipped", "cnn"])
+                                     "log_std_unclipped", "cnn", "mixed_precision"])
 def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
     """Same seeds, same thread count: every logged column except timings is equal to upstream's, iteration by
     iteration."""
@@ -216,6 +216,10 @@ def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
         cnn = {"class_name": "CNNModel", "cnn_cfg": {"output_channels": [4, 8], "kernel_size": 3, "stride": [1, 2],
                                                      "norm": "batch", "activation": "elu"}}
         spec = dataclasses.replace(R.SPECS["cartpole"], hidden=(32,), model=cnn, **small)
+    elif variant == "mixed_precision":
+        env_name = "tracking12"
+        alg = {**R.SPECS[env_name].algorithm, "use_mixed_precision": True}
+        spec = dataclasses.replace(R.SPECS[env_name], algorithm=alg, **small)
     elif variant == "beta":
         env_name = "pendulum"
         spec = dataclasses.replace(R.SPECS[env_name], distribution="BetaDistribution", **small)
