@@ -189,7 +189,8 @@ def test_episode_extras_are_logged_every_iteration_like_upstream(ref, tmp_path):
 
 
 @pytest.mark.parametrize("variant", ["rnd_symmetry", "gru", "lstm", "hetero", "per_minibatch_fixed_lr", "beta",
-                                     "log_std_unclipped", "cnn", "mixed_precision"])
+                                     "log_std_unclipped", "cnn", "mixed_precision", "mirror_loss_only",
+                                     "rnd_linear_schedule", "sgd", "rmsprop", "adamw"])
 def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
     """Same seeds, same thread count: every logged column except timings is equal to upstream's, iteration by
     iteration."""
@@ -216,6 +217,19 @@ def test_every_logged_scalar_equals_upstream(ref, tmp_path, variant):
         cnn = {"class_name": "CNNModel", "cnn_cfg": {"output_channels": [4, 8], "kernel_size": 3, "stride": [1, 2],
                                                      "norm": "batch", "activation": "elu"}}
         spec = dataclasses.replace(R.SPECS["cartpole"], hidden=(32,), model=cnn, **small)
+    elif variant == "mirror_loss_only":
+        env_name = "tracking12"
+        spec = R.with_symmetry(env_name, dataclasses.replace(R.SPECS[env_name], **small), data_augmentation=False)
+    elif variant == "rnd_linear_schedule":
+        env_name = "tracking12"
+        spec = R.with_rnd(env_name, dataclasses.replace(R.SPECS[env_name], **small))
+        rnd = {**spec.algorithm["rnd_cfg"], "weight_schedule": {"mode": "linear", "initial_step": 4,
+                                                                "final_step": 20, "final_value": 0.0}}
+        spec = dataclasses.replace(spec, algorithm={**spec.algorithm, "rnd_cfg": rnd})
+    elif variant in ("sgd", "rmsprop", "adamw"):
+        env_name = "cartpole"
+        alg = {**R.SPECS[env_name].algorithm, "optimizer": variant}
+        spec = dataclasses.replace(R.SPECS[env_name], algorithm=alg, **small)
     elif variant == "mixed_precision":
         env_name = "tracking12"
         alg = {**R.SPECS[env_name].algorithm, "use_mixed_precision": True}
