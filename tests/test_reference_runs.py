@@ -422,3 +422,44 @@ def test_resumed_training_equals_upstream(ref, tmp_path):
             assert [r.get(c) for r in rows_o] == [r.get(c) for r in rows_u], c
     for key in ck_u:
         _equal_state(ck_o[key], ck_u[key], key)
+
+
+PARITY_DRAWS = int(os.environ.get("RLB_PARITY_DRAWS", "6"))  # more draws for a longer sweep
+
+
+@pytest.mark.parametrize("draw", range(PARITY_DRAWS))
+def test_random_configurations_log_exactly_what_upstream_logs(ref, tmp_path, draw):
+    """Randomly drawn algorithm settings (epochs, minibatches, clip, discounting, KL target or a fixed learning rate,
+    gradient-norm limits, loss weights, network sizes, normalisation): every logged scalar equals upstream's."""
+    import dataclasses
+    import random
+
+    rng = random.Random(1000 + draw)
+    env_name = rng.choice(["cartpole", "pendulum", "tracking12"])
+    schedule = rng.choice(["adaptive", "fixed"])
+    alg = {**R.PPO_ALGORITHM,
+           "num_learning_epochs": rng.randint(1, 4), "num_mini_batches": rng.choice([1, 2, 3, 4, 7]),
+           "clip_param": rng.choice([0.1, 0.2, 0.3]), "gamma": rng.choice([0.9, 0.99, 0.999]),
+           "lam": rng.choice([0.9, 0.95, 1.0]), "value_loss_coef": rng.choice([0.5, 1.0, 2.0]),
+           "entropy_coef": rng.choice([0.0, 0.005, 0.02]), "learning_rate": rng.choice([3e-4, 1e-3, 3e-3]),
+           "max_grad_norm": rng.choice([0.5, 1.0, 10.0]), "schedule": schedule,
+           "desired_kl": rng.choice([0.005, 0.01, 0.02]) if schedule == "adaptive" else None,
+           "use_clipped_value_loss": rng.choice([True, False]),
+           "normalize_advantage_per_mini_batch": rng.choice([True, False])}
+    hidden = tuple(rng.choice([16, 32, 64]) for _ in range(rng.randint(1, 3)))
+    spec = dataclasses.replace(R.SPECS[env_name], num_envs=rng.choice([16, 48, 64]), num_steps=rng.choice([4, 8, 12]),
+                               hidden=hidden, algorithm=alg, obs_normalization=rng.choice([True, False]),
+                               init_std=rng.choice([0.5, 1.0]))
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        rows = {}
+        for impl in ("b200", "upstream"):
+            R.train(env_name, draw, str(tmp_path / impl), impl=impl, iterations=3, spec=spec)
+            rows[impl] = golden.read_curve(tmp_path / impl / "metrics.csv")
+    finally:
+        torch.set_num_threads(threads)
+    cols = {k for r in rows["upstream"] for k in r} | {k for r in rows["b200"] for k in r}
+    for c in sorted(cols):
+        if not c.startswith("Perf/") and c != "wall_s":
+            assert [r.get(c) for r in rows["b200"]] == [r.get(c) for r in rows["upstream"]], (c, spec)
