@@ -463,3 +463,50 @@ def test_random_configurations_log_exactly_what_upstream_logs(ref, tmp_path, dra
     for c in sorted(cols):
         if not c.startswith("Perf/") and c != "wall_s":
             assert [r.get(c) for r in rows["b200"]] == [r.get(c) for r in rows["upstream"]], (c, spec)
+
+
+@pytest.mark.parametrize("draw", range(PARITY_DRAWS))
+def test_random_models_and_extensions_log_exactly_what_upstream_logs(ref, tmp_path, draw):
+    """Randomly drawn model families (MLP, GRU / LSTM, layer counts), policies (Gaussian scalar / log std,
+    heteroscedastic, Beta) and extensions (RND with and without normalisation, symmetry modes)."""
+    import dataclasses
+    import random
+
+    rng = random.Random(5000 + draw)
+    env_name = rng.choice(["cartpole", "pendulum", "tracking12", "cartpole_po"])
+    spec = dataclasses.replace(R.SPECS[env_name], num_envs=rng.choice([16, 32]), num_steps=rng.choice([4, 8]),
+                               hidden=tuple(rng.choice([16, 32]) for _ in range(rng.randint(1, 2))),
+                               distribution=rng.choice(["GaussianDistribution", "HeteroscedasticGaussianDistribution",
+                                                        "BetaDistribution"]),
+                               algorithm={**R.SPECS[env_name].algorithm,
+                                          "num_learning_epochs": rng.randint(1, 3),
+                                          "num_mini_batches": rng.choice([1, 2, 4])})
+    recurrent = env_name == "cartpole_po" or rng.random() < 0.3
+    if recurrent:
+        spec = R.with_rnn(spec, rng.choice(["gru", "lstm"]), rng.choice([16, 32]), rng.choice([1, 2]),
+                          critic=rng.random() < 0.7)
+    elif spec.distribution == "GaussianDistribution" and rng.random() < 0.5:
+        spec = dataclasses.replace(spec, model={"distribution_cfg": {"class_name": "GaussianDistribution",
+                                                                     "init_std": 1.0, "std_type": "log"}},
+                                   critic_model={})
+    if rng.random() < 0.5:
+        spec = R.with_rnd(env_name, spec)
+        rnd = {**spec.algorithm["rnd_cfg"], "state_normalization": rng.random() < 0.5,
+               "reward_normalization": rng.random() < 0.5}
+        spec = dataclasses.replace(spec, algorithm={**spec.algorithm, "rnd_cfg": rnd})
+    if not recurrent and rng.random() < 0.5:
+        aug, mirror = rng.choice([(True, True), (True, False), (False, True)])
+        spec = R.with_symmetry(env_name, spec, data_augmentation=aug, mirror_loss=mirror)
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        rows = {}
+        for impl in ("b200", "upstream"):
+            R.train(env_name, draw, str(tmp_path / impl), impl=impl, iterations=3, spec=spec)
+            rows[impl] = golden.read_curve(tmp_path / impl / "metrics.csv")
+    finally:
+        torch.set_num_threads(threads)
+    cols = {k for r in rows["upstream"] for k in r} | {k for r in rows["b200"] for k in r}
+    for c in sorted(cols):
+        if not c.startswith("Perf/") and c != "wall_s":
+            assert [r.get(c) for r in rows["b200"]] == [r.get(c) for r in rows["upstream"]], (c, spec)
