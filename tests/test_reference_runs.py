@@ -510,3 +510,31 @@ def test_random_models_and_extensions_log_exactly_what_upstream_logs(ref, tmp_pa
     for c in sorted(cols):
         if not c.startswith("Perf/") and c != "wall_s":
             assert [r.get(c) for r in rows["b200"]] == [r.get(c) for r in rows["upstream"]], (c, spec)
+
+
+@pytest.mark.parametrize("draw", range(PARITY_DRAWS // 2))
+def test_random_distillation_settings_log_exactly_what_upstream_logs(ref, tmp_path, draw):
+    """Randomly drawn distillation settings (student family, loss, window length, epochs, clipping, learning rate)."""
+    import random
+
+    rng = random.Random(9000 + draw)
+    student = rng.choice([None, {"class_name": "RNNModel", "rnn_type": "gru", "rnn_hidden_dim": 16},
+                          {"class_name": "RNNModel", "rnn_type": "lstm", "rnn_hidden_dim": 16}])
+    alg = {"loss_type": rng.choice(["mse", "huber"]), "gradient_length": rng.choice([1, 2, 3, 8]),
+           "num_learning_epochs": rng.randint(1, 3), "max_grad_norm": rng.choice([None, 0.5, 1.0]),
+           "learning_rate": rng.choice([3e-4, 1e-3])}
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        ckpt = R.make_teacher_checkpoint("tracking12", str(tmp_path / "t.pt"), iterations=1, num_envs=32,
+                                         impl="upstream")
+        rows = {}
+        for impl in ("b200", "upstream"):
+            R.train_distillation("tracking12", draw, str(tmp_path / impl), ckpt, impl=impl, iterations=3,
+                                 algorithm=alg, student_model=student)
+            rows[impl] = golden.read_curve(tmp_path / impl / "metrics.csv")
+    finally:
+        torch.set_num_threads(threads)
+    for c in sorted({k for r in rows["upstream"] for k in r}):
+        if not c.startswith("Perf/") and c != "wall_s":
+            assert [r.get(c) for r in rows["b200"]] == [r.get(c) for r in rows["upstream"]], (c, alg, student)
