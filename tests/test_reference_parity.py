@@ -688,3 +688,49 @@ def test_data_parallel_distillation_matches_reference_over_gloo(ref, tmp_path):
             assert torch.equal(res[r]["ours"][name], v), f"rank {r} {name}"
     for name, v in res[0]["ours"].items():
         assert torch.equal(v, res[1]["ours"][name]), name
+
+
+@pytest.mark.parametrize("draw", range(40))
+def test_random_cnn_encoders_match_reference(ref, draw):
+    """Randomly drawn convolutional encoders (channels, kernel sizes, strides, dilations, padding modes, norms,
+    pooling, activations): same parameter names and shapes as upstream's, same outputs for the same weights."""
+    import random
+
+    from rsl_rl.modules import CNN as RefCNN
+
+    from tt_rsl_rl_b200.modules import CNN
+
+    rng = random.Random(300 + draw)
+    n = rng.randint(1, 3)
+    cfg = {"output_channels": [rng.choice([2, 4, 8]) for _ in range(n)],
+           "kernel_size": [rng.choice([1, 3, 5]) for _ in range(n)],
+           "stride": [rng.choice([1, 2]) for _ in range(n)],
+           "dilation": [rng.choice([1, 1, 2]) for _ in range(n)],
+           "padding": rng.choice(["none", "zeros", "reflect", "replicate", "circular"]),
+           "norm": [rng.choice(["none", "batch", "layer"]) for _ in range(n)],
+           "activation": rng.choice(["elu", "relu", "tanh", "lrelu"]),
+           "max_pool": [rng.random() < 0.3 for _ in range(n)],
+           "global_pool": rng.choice(["none", "avg", "max"])}
+    shape = (rng.choice([12, 16]), rng.choice([12, 16]))
+    torch.manual_seed(draw)
+    try:
+        theirs = RefCNN(shape, 2, **cfg)
+    except Exception as exc:  # a combination upstream refuses must be refused here too
+        with pytest.raises(type(exc)):
+            CNN(shape, 2, **cfg)
+        return
+    ours = CNN(shape, 2, **cfg)
+    assert [(k, v.shape) for k, v in ours.state_dict().items()] == [(k, v.shape) for k, v in theirs.state_dict().items()]
+    assert ours.output_dim == theirs.output_dim
+    ours.load_state_dict(theirs.state_dict())
+    x = torch.randn(5, 2, *shape)
+    for mode in ("train", "eval"):
+        getattr(ours, mode)()
+        getattr(theirs, mode)()
+        try:
+            want = theirs(x)
+        except RuntimeError:  # a degenerate layout (padding beyond the map) fails in upstream and here alike
+            with pytest.raises(RuntimeError):
+                ours(x)
+            continue
+        torch.testing.assert_close(ours(x), want, rtol=0, atol=0)
