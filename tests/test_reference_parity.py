@@ -734,3 +734,56 @@ def test_random_cnn_encoders_match_reference(ref, draw):
                 ours(x)
             continue
         torch.testing.assert_close(ours(x), want, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("name", ["elu", "selu", "relu", "crelu", "lrelu", "tanh", "sigmoid", "softplus", "gelu",
+                                  "swish", "mish", "identity", "ELU", "bogus"])
+def test_activation_names_resolve_like_reference(ref, name):
+    from rsl_rl.utils import resolve_nn_activation as theirs
+
+    from tt_rsl_rl_b200.utils import resolve_nn_activation as ours
+
+    try:
+        want = theirs(name)
+    except ValueError:
+        with pytest.raises(ValueError):
+            ours(name)
+        return
+    got = ours(name)
+    assert type(got) is type(want)
+    x = torch.linspace(-3, 3, 13)
+    torch.testing.assert_close(got(x), want(x), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("draw", range(20))
+def test_random_mlps_match_reference(ref, draw):
+    """Randomly drawn MLPs (depths, widths, activations, tuple outputs, init scales): same modules, same init for the
+    same seed, same outputs."""
+    import random
+
+    from rsl_rl.modules import MLP as RefMLP
+
+    from tt_rsl_rl_b200.modules import MLP
+
+    rng = random.Random(700 + draw)
+    hidden = [rng.choice([4, 16, 33]) for _ in range(rng.randint(1, 4))]
+    out = rng.choice([1, 3, (2, 3)])
+    act = rng.choice(["elu", "relu", "tanh", "gelu", "identity"])
+    last = rng.choice([None, "tanh", "sigmoid"])
+    torch.manual_seed(draw)
+    theirs = RefMLP(7, out, hidden, act, last)
+    torch.manual_seed(draw)
+    ours = MLP(7, out, hidden, act, last)
+    assert [type(m) for m in ours] == [type(m) for m in theirs]
+    for (k1, v1), (k2, v2) in zip(ours.state_dict().items(), theirs.state_dict().items()):
+        assert k1 == k2 and torch.equal(v1, v2)
+    # a scale per module of the sequence (upstream indexes the scales by module position) or one for all
+    scales = rng.choice([[rng.choice([0.5, 1.0, 2.0]) for _ in range(len(theirs))], rng.choice([0.01, 1.0])])
+    torch.manual_seed(draw)
+    theirs.init_weights(scales)
+    torch.manual_seed(draw)
+    ours.init_weights(scales)
+    for v1, v2 in zip(ours.state_dict().values(), theirs.state_dict().values()):
+        assert torch.equal(v1, v2)
+    x = torch.randn(4, 7)
+    assert torch.equal(ours(x), theirs(x))
