@@ -787,3 +787,67 @@ def test_random_mlps_match_reference(ref, draw):
         assert torch.equal(v1, v2)
     x = torch.randn(4, 7)
     assert torch.equal(ours(x), theirs(x))
+
+
+@pytest.mark.parametrize("draw", range(20))
+def test_random_storages_yield_the_reference_minibatches(ref, draw):
+    """Random rollout shapes, done patterns, minibatch counts and hidden-state layouts (GRU tensor, LSTM pair, several
+    layers): both generators yield exactly upstream's minibatches, every field."""
+    import random
+
+    from rsl_rl.storage import RolloutStorage as RefStorage
+
+    from tt_rsl_rl_b200.storage import RolloutStorage
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    rng = random.Random(1300 + draw)
+    N, T, A = rng.choice([3, 8, 17]), rng.choice([1, 4, 7]), rng.choice([1, 3])
+    p_done, layers, lstm = rng.choice([0.0, 0.2, 0.7]), rng.choice([1, 2]), rng.random() < 0.5
+    g = torch.Generator().manual_seed(draw)
+    obs = TensorDict({"policy": torch.zeros(N, 4), "extra": torch.zeros(N, 2)}, batch_size=[N])
+    rs, os_ = RefStorage("rl", N, T, obs, [A], "cpu"), RolloutStorage("rl", N, T, obs, [A], "cpu")
+    for t in range(T):
+        tr = type(rs).Transition()
+        tr.observations = TensorDict({"policy": torch.randn(N, 4, generator=g), "extra": torch.randn(N, 2, generator=g)},
+                                     batch_size=[N])
+        tr.actions = torch.randn(N, A, generator=g)
+        tr.rewards = torch.randn(N, generator=g)
+        tr.dones = (torch.rand(N, generator=g) < p_done).float()
+        tr.values = torch.randn(N, 1, generator=g)
+        tr.actions_log_prob = torch.randn(N, generator=g)
+        tr.distribution_params = (torch.randn(N, A, generator=g), torch.rand(N, A, generator=g))
+        h = torch.randn(layers, N, 5, generator=g)
+        c = torch.randn(layers, N, 5, generator=g)
+        tr.hidden_states = ((h, c) if lstm else h, (h.clone(), c.clone()) if lstm else h.clone())
+        rs.add_transition(tr)
+        os_.add_transition(tr)
+    for name in ("returns", "advantages"):
+        getattr(rs, name).copy_(torch.randn(T, N, 1, generator=g))
+        getattr(os_, name).copy_(getattr(rs, name))
+    M = rng.randint(1, min(N, 5))
+    E = rng.randint(1, 3)
+
+    def same(x, y, where):
+        if isinstance(x, (tuple, list)):
+            assert len(x) == len(y), where
+            for i, (a, b) in enumerate(zip(x, y)):
+                same(a, b, f"{where}[{i}]")
+        elif x is None:
+            assert y is None, where
+        elif hasattr(x, "keys"):
+            for k in x.keys():
+                assert torch.equal(x[k], y[k]), f"{where}.{k}"
+        else:
+            assert torch.equal(x, y), where
+
+    fields = ("observations", "actions", "values", "advantages", "returns", "old_actions_log_prob",
+              "old_distribution_params", "hidden_states", "masks")
+    for gen in ("mini_batch_generator", "recurrent_mini_batch_generator"):
+        torch.manual_seed(draw)
+        theirs = list(getattr(rs, gen)(M, E))
+        torch.manual_seed(draw)
+        ours = list(getattr(os_, gen)(M, E))
+        assert len(ours) == len(theirs) == M * E
+        for i, (x, y) in enumerate(zip(theirs, ours)):
+            for f in fields:
+                same(getattr(x, f), getattr(y, f), f"{gen}[{i}].{f}")
