@@ -851,3 +851,46 @@ def test_random_storages_yield_the_reference_minibatches(ref, draw):
         for i, (x, y) in enumerate(zip(theirs, ours)):
             for f in fields:
                 same(getattr(x, f), getattr(y, f), f"{gen}[{i}].{f}")
+
+
+@pytest.mark.parametrize("draw", range(24))
+def test_random_distributions_match_reference(ref, draw):
+    """Random Gaussian (scalar / log std, std ranges that clamp, fixed std), heteroscedastic and Beta distributions:
+    parameters, samples for the same seed, log-probabilities, entropies, KL divergences and deterministic outputs
+    equal upstream's."""
+    import random
+
+    import rsl_rl.modules.distribution as RD
+
+    import tt_rsl_rl_b200.modules.distribution as OD
+
+    rng = random.Random(2100 + draw)
+    kind = rng.choice(["GaussianDistribution", "HeteroscedasticGaussianDistribution", "BetaDistribution"])
+    A = rng.choice([1, 3, 6])
+    if kind == "BetaDistribution":
+        kw = {"action_range": rng.choice([(-1.0, 1.0), (0.0, 2.0), (-3.0, 0.5)])}
+    else:
+        kw = {"init_std": rng.choice([0.1, 1.0, 3.0]), "std_type": rng.choice(["scalar", "log"]),
+              "std_range": rng.choice([(1e-6, 1e6), (0.2, 0.8), (0.5, 2.0)])}
+        if kind == "GaussianDistribution":
+            kw["learn_std"] = rng.random() < 0.8
+    theirs, ours = getattr(RD, kind)(A, **kw), getattr(OD, kind)(A, **kw)
+    assert [(k, v.shape) for k, v in ours.state_dict().items()] == [(k, v.shape) for k, v in theirs.state_dict().items()]
+    ours.load_state_dict(theirs.state_dict())
+    assert ours.input_dim == theirs.input_dim
+    dims = theirs.input_dim if isinstance(theirs.input_dim, list) else [theirs.input_dim]
+    g = torch.Generator().manual_seed(draw)
+    head = torch.randn(5, *dims, generator=g)
+    theirs.update(head)
+    ours.update(head)
+    for name in ("mean", "std", "entropy"):
+        assert torch.equal(getattr(ours, name), getattr(theirs, name)), name
+    torch.manual_seed(draw)
+    s_t = theirs.sample()
+    torch.manual_seed(draw)
+    s_o = ours.sample()
+    assert torch.equal(s_o, s_t)
+    assert torch.equal(ours.log_prob(s_t), theirs.log_prob(s_t))
+    assert torch.equal(ours.deterministic_output(head), theirs.deterministic_output(head))
+    old = tuple(p.detach() + 0.01 for p in theirs.params)
+    assert torch.equal(ours.kl_divergence(old, ours.params), theirs.kl_divergence(old, theirs.params))
