@@ -894,3 +894,45 @@ def test_random_distributions_match_reference(ref, draw):
     assert torch.equal(ours.deterministic_output(head), theirs.deterministic_output(head))
     old = tuple(p.detach() + 0.01 for p in theirs.params)
     assert torch.equal(ours.kl_divergence(old, ours.params), theirs.kl_divergence(old, theirs.params))
+
+
+@pytest.mark.parametrize("draw", range(12))
+def test_random_normaliser_histories_match_reference(ref, draw):
+    """Random update histories (batch sizes, an `until` limit, train / eval switches) of the empirical normaliser and
+    the discounted reward normaliser: buffers, outputs and inverses equal upstream's."""
+    import random
+
+    from rsl_rl.modules import EmpiricalDiscountedVariationNormalization as RefDisc
+    from rsl_rl.modules import EmpiricalNormalization as RefNorm
+
+    from tt_rsl_rl_b200.modules import EmpiricalDiscountedVariationNormalization, EmpiricalNormalization
+
+    rng = random.Random(4100 + draw)
+    g = torch.Generator().manual_seed(draw)
+    D = rng.choice([1, 4])
+    until = rng.choice([None, 30, 200])
+    gamma = rng.choice([0.9, 0.99])
+    pairs = [(RefNorm([D], until=until), EmpiricalNormalization([D], until=until)),
+             (RefDisc([], gamma=gamma, until=until), EmpiricalDiscountedVariationNormalization([], gamma=gamma,
+                                                                                              until=until))]
+    envs = rng.choice([1, 6])  # the discounted normaliser keeps one running sum per environment
+    for step in range(rng.randint(3, 8)):
+        n = rng.choice([1, 5, 40])
+        x = torch.randn(n, D, generator=g) * 3 + 1
+        r = torch.randn(envs, generator=g)
+        if rng.random() < 0.2:
+            for a, b in pairs:
+                a.eval(), b.eval()
+        else:
+            for a, b in pairs:
+                a.train(), b.train()
+        (a0, b0), (a1, b1) = pairs
+        assert torch.equal(b0(x), a0(x))
+        assert torch.equal(b1(r), a1(r))
+        a0.update(x), b0.update(x)
+        for (k, v), (k2, v2) in zip(a0.state_dict().items(), b0.state_dict().items()):
+            assert k == k2 and torch.equal(v, v2), k
+        for (k, v), (k2, v2) in zip(a1.state_dict().items(), b1.state_dict().items()):
+            assert k == k2 and torch.equal(v, v2), k
+    y = torch.randn(3, D, generator=g)
+    assert torch.equal(pairs[0][1].inverse(y), pairs[0][0].inverse(y))
