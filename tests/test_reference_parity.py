@@ -936,3 +936,43 @@ def test_random_normaliser_histories_match_reference(ref, draw):
             assert k == k2 and torch.equal(v, v2), k
     y = torch.randn(3, D, generator=g)
     assert torch.equal(pairs[0][1].inverse(y), pairs[0][0].inverse(y))
+
+
+@pytest.mark.parametrize("draw", range(12))
+def test_random_rnd_modules_match_reference(ref, draw):
+    """Randomly configured RND modules (network sizes, activations, state / reward normalisation, weight schedules):
+    intrinsic rewards, losses and state over a sequence of steps and normaliser updates equal upstream's."""
+    import random
+
+    import tensordict as ref_tdm
+    from rsl_rl.extensions import RandomNetworkDistillation as RefRND
+
+    from tt_rsl_rl_b200.extensions import RandomNetworkDistillation
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    rng = random.Random(6100 + draw)
+    schedule = rng.choice([None, {"mode": "constant"}, {"mode": "step", "final_step": 4, "final_value": 0.2},
+                           {"mode": "linear", "initial_step": 2, "final_step": 7, "final_value": 0.0}])
+    kw = dict(num_states=6, obs_groups={"rnd_state": ["a", "b"]}, num_outputs=rng.choice([1, 4, 8]),
+              predictor_hidden_dims=[rng.choice([8, 16]) for _ in range(rng.randint(1, 2))],
+              target_hidden_dims=[rng.choice([8, 16]) for _ in range(rng.randint(1, 2))],
+              activation=rng.choice(["elu", "relu", "tanh"]), state_normalization=rng.random() < 0.5,
+              reward_normalization=rng.random() < 0.5, weight=rng.choice([0.1, 1.0]), weight_schedule=schedule)
+    torch.manual_seed(draw)
+    theirs = RefRND(**kw)
+    torch.manual_seed(draw)
+    ours = RandomNetworkDistillation(**kw)
+    ours.load_state_dict(theirs.state_dict())
+    g = torch.Generator().manual_seed(draw)
+    for step in range(8):
+        a, b = torch.randn(5, 4, generator=g), torch.randn(5, 2, generator=g)
+        o = TensorDict({"a": a, "b": b}, batch_size=[5])
+        t = ref_tdm.TensorDict({"a": a, "b": b}, batch_size=[5])
+        assert torch.equal(ours.get_intrinsic_reward(o), theirs.get_intrinsic_reward(t)), step
+        assert ours.weight == theirs.weight
+        assert torch.equal(ours.compute_loss(o), theirs.compute_loss(t))
+        if step % 3 == 2:
+            ours.update_normalization(o)
+            theirs.update_normalization(t)
+    for (k, v), (k2, v2) in zip(ours.state_dict().items(), theirs.state_dict().items()):
+        assert k == k2 and torch.equal(v, v2), k

@@ -111,8 +111,9 @@ class RandomNetworkDistillation(nn.Module):
             return self.initial_weight
         if step > final_step:
             return final_value
-        frac = (step - initial_step) / (final_step - initial_step)
-        return self.initial_weight + (final_value - self.initial_weight) * frac
+        # product before quotient, in upstream's order, so the weight is the same double
+        return self.initial_weight + (final_value - self.initial_weight) * (step - initial_step) / (
+            final_step - initial_step)
 
 
 def resolve_rnd_config(alg_cfg: dict, obs, obs_groups: dict[str, list[str]], env) -> dict:
