@@ -976,3 +976,43 @@ def test_random_rnd_modules_match_reference(ref, draw):
             theirs.update_normalization(t)
     for (k, v), (k2, v2) in zip(ours.state_dict().items(), theirs.state_dict().items()):
         assert k == k2 and torch.equal(v, v2), k
+
+
+@pytest.mark.parametrize("draw", range(16))
+def test_random_trajectory_splits_and_rnn_batches_match_reference(ref, draw):
+    """Random done patterns: split-and-pad, unpad and the RNN module's masked batch pass (GRU / LSTM, layers) equal
+    upstream's; so do rollout-mode steps with per-environment resets."""
+    import random
+
+    from rsl_rl.modules import RNN as RefRNN
+    from rsl_rl.utils import split_and_pad_trajectories as ref_split
+    from rsl_rl.utils import unpad_trajectories as ref_unpad
+
+    from tt_rsl_rl_b200.modules import RNN
+    from tt_rsl_rl_b200.utils import split_and_pad_trajectories, unpad_trajectories
+
+    rng = random.Random(7100 + draw)
+    g = torch.Generator().manual_seed(draw)
+    T, N, D = rng.choice([1, 3, 8]), rng.choice([1, 4, 9]), 3
+    dones = (torch.rand(T, N, 1, generator=g) < rng.choice([0.0, 0.3, 0.8])).float()
+    x = torch.randn(T, N, D, generator=g)
+    pa, ma = split_and_pad_trajectories(x, dones)
+    pb, mb = ref_split(x, dones)
+    assert torch.equal(pa, pb) and torch.equal(ma, mb)
+    assert torch.equal(unpad_trajectories(pa, ma), ref_unpad(pb, mb))
+    kind, layers, H = rng.choice(["gru", "lstm"]), rng.choice([1, 2]), rng.choice([4, 8])
+    torch.manual_seed(draw)
+    theirs = RefRNN(D, hidden_dim=H, num_layers=layers, type=kind)
+    ours = RNN(D, hidden_dim=H, num_layers=layers, type=kind)
+    ours.load_state_dict(theirs.state_dict())
+    traj = pa.shape[1]
+    h = torch.randn(layers, traj, H, generator=g)
+    hs = (h, torch.randn(layers, traj, H, generator=g)) if kind == "lstm" else h
+    assert torch.equal(ours(pa, ma, hs), theirs(pb, mb, hs))
+    for t in range(T):  # rollout mode with resets of done environments
+        assert torch.equal(ours(x[t]), theirs(x[t]))
+        ours.reset(dones[t, :, 0])
+        theirs.reset(dones[t, :, 0])
+    st_o, st_t = ours.hidden_state, theirs.hidden_state
+    for a, b in (zip(st_o, st_t) if kind == "lstm" else [(st_o, st_t)]):
+        assert torch.equal(a, b)
