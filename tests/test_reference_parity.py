@@ -1016,3 +1016,34 @@ def test_random_trajectory_splits_and_rnn_batches_match_reference(ref, draw):
     st_o, st_t = ours.hidden_state, theirs.hidden_state
     for a, b in (zip(st_o, st_t) if kind == "lstm" else [(st_o, st_t)]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("draw", range(20))
+def test_random_observation_group_configs_resolve_like_reference(ref, draw):
+    """Random observation-set configurations (missing sets, unknown groups, empty lists, extra sets): the resolved
+    sets, or the error raised, equal upstream's."""
+    import random
+    import warnings
+
+    import tensordict as ref_tdm
+    from rsl_rl.utils import resolve_obs_groups as theirs
+
+    from tt_rsl_rl_b200.utils import TensorDict
+    from tt_rsl_rl_b200.utils import resolve_obs_groups as ours
+
+    rng = random.Random(8100 + draw)
+    names = ["policy", "critic", "privileged", "teacher"][: rng.randint(1, 4)]
+    data = {n: torch.zeros(2, 3) for n in names}
+    sets = rng.sample(["actor", "critic", "student", "teacher", "rnd_state"], rng.randint(0, 3))
+    cfg = {s: rng.sample(names + ["missing"], rng.randint(0, 2)) for s in sets}
+    defaults = rng.choice([["actor", "critic"], ["student", "teacher"], ["actor", "critic", "rnd_state"]])
+    outcomes = []
+    for fn, td in ((ours, TensorDict(dict(data), batch_size=[2])), (theirs, ref_tdm.TensorDict(dict(data),
+                                                                                              batch_size=[2]))):
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            try:
+                outcomes.append(("ok", fn(td, {k: list(v) for k, v in cfg.items()}, list(defaults))))
+            except Exception as exc:  # the same kind of refusal
+                outcomes.append(("error", type(exc).__name__))
+    assert outcomes[0] == outcomes[1], (cfg, defaults)
