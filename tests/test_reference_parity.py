@@ -1047,3 +1047,61 @@ def test_random_observation_group_configs_resolve_like_reference(ref, draw):
             except Exception as exc:  # the same kind of refusal
                 outcomes.append(("error", type(exc).__name__))
     assert outcomes[0] == outcomes[1], (cfg, defaults)
+
+
+@pytest.mark.parametrize("draw", range(12))
+def test_random_symmetry_modules_match_reference(ref, draw):
+    """Random signed-permutation mirror functions with K copies and the three usage modes: augmented batches and
+    mirror losses equal upstream's."""
+    import random
+
+    import tensordict as ref_tdm
+    from rsl_rl.extensions import Symmetry as RefSym
+
+    from tt_rsl_rl_b200.extensions import Symmetry
+    from tt_rsl_rl_b200.models import MLPModel
+    from tt_rsl_rl_b200.utils import TensorDict
+
+    rng = random.Random(9100 + draw)
+    g = torch.Generator().manual_seed(draw)
+    K, D, A, B = rng.choice([2, 3, 4]), 6, 3, 5
+    maps = [(torch.randperm(D, generator=g), torch.where(torch.rand(D, generator=g) < 0.5, -1.0, 1.0),
+             torch.randperm(A, generator=g), torch.where(torch.rand(A, generator=g) < 0.5, -1.0, 1.0))
+            for _ in range(K - 1)]
+
+    def mirror(env=None, obs=None, actions=None):
+        o = a = None
+        if obs is not None:
+            x = obs["policy"]
+            o = type(obs)({"policy": torch.cat([x] + [x[:, p] * s for p, s, _, _ in maps])},
+                          batch_size=[K * x.shape[0]])
+        if actions is not None:
+            a = torch.cat([actions] + [actions[:, p] * s for _, _, p, s in maps])
+        return o, a
+
+    aug, loss = rng.choice([(True, True), (True, False), (False, True)])
+    kw = dict(env=None, data_augmentation_func=mirror, use_data_augmentation=aug, use_mirror_loss=loss,
+              mirror_loss_coeff=0.5)
+    x = torch.randn(B, D, generator=g)
+    obs_o, obs_t = TensorDict({"policy": x}, batch_size=[B]), ref_tdm.TensorDict({"policy": x}, batch_size=[B])
+    torch.manual_seed(draw)
+    actor = MLPModel(obs_o, {"actor": ["policy"]}, "actor", A, hidden_dims=[8],
+                     distribution_cfg={"class_name": "GaussianDistribution"})
+
+    class Batch:
+        pass
+
+    batches = []
+    for obs in (obs_o, obs_t):
+        b = Batch()
+        b.observations, b.actions = obs, torch.randn(B, A, generator=torch.Generator().manual_seed(draw))
+        for name in ("old_actions_log_prob", "values", "advantages", "returns"):
+            setattr(b, name, torch.randn(B, 1, generator=torch.Generator().manual_seed(len(name))))
+        batches.append(b)
+    ours_s, theirs_s = Symmetry(**kw), RefSym(**kw)
+    ours_s.augment_batch(batches[0], B)
+    theirs_s.augment_batch(batches[1], B)
+    for name in ("actions", "old_actions_log_prob", "values", "advantages", "returns"):
+        assert torch.equal(getattr(batches[0], name), getattr(batches[1], name)), name
+    assert torch.equal(batches[0].observations["policy"], batches[1].observations["policy"])
+    assert torch.equal(ours_s.compute_loss(actor, batches[0], B), theirs_s.compute_loss(actor, batches[1], B))
