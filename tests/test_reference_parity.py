@@ -1105,3 +1105,61 @@ def test_random_symmetry_modules_match_reference(ref, draw):
         assert torch.equal(getattr(batches[0], name), getattr(batches[1], name)), name
     assert torch.equal(batches[0].observations["policy"], batches[1].observations["policy"])
     assert torch.equal(ours_s.compute_loss(actor, batches[0], B), theirs_s.compute_loss(actor, batches[1], B))
+
+
+@pytest.mark.parametrize("draw", range(12))
+def test_random_logger_streams_match_reference(ref, tmp_path, draw):
+    """Random step streams into the training logger (rewards, dones, intrinsic rewards, extras that are floats,
+    0-d or per-environment tensors, keys that come and go, "episode" or "log" dictionaries): every scalar written
+    equals upstream's, over several iterations."""
+    import contextlib
+    import io
+    import random
+
+    from rsl_rl.utils.logger import Logger as RefLogger
+
+    from tt_rsl_rl_b200.utils.logger import Logger
+
+    class Rec:
+        def __init__(self):
+            self.rows = []
+
+        def add_scalar(self, tag, value, step, *args, **kwargs):
+            if not tag.startswith("Perf/") and not tag.endswith("/time"):
+                self.rows.append((tag, float(value), int(step)))
+
+    rng = random.Random(11000 + draw)
+    g = torch.Generator().manual_seed(draw)
+    N = rng.choice([1, 4, 9])
+    rnd = rng.random() < 0.5
+    cfg = {"num_steps_per_env": 4, "algorithm": {"rnd_cfg": {"weight": 1.0} if rnd else None}}
+    writers = []
+    loggers = []
+    for cls in (Logger, RefLogger):
+        lg = cls(log_dir=str(tmp_path), cfg=dict(cfg), env_cfg={}, num_envs=N, is_distributed=False, gpu_world_size=1,
+                 gpu_global_rank=0, device="cpu")
+        lg.writer = Rec()
+        writers.append(lg.writer)
+        loggers.append(lg)
+    key_sets = [["a"], ["a", "b"], ["b", "c/d"], []]
+    for it in range(3):
+        for step in range(4):
+            rew = torch.randn(N, generator=g)
+            dones = (torch.rand(N, generator=g) < 0.4).float()
+            intr = torch.rand(N, generator=g) if rnd else None
+            keys = rng.choice(key_sets)
+            info = {}
+            for k in keys:
+                kind = rng.choice(["float", "0d", "vec"])
+                v = torch.randn(N, generator=g)
+                info[k] = float(v[0]) if kind == "float" else (v[0].clone() if kind == "0d" else v)
+            extras = {rng.choice(["episode", "log"]): info} if info else {}
+            for lg in loggers:
+                lg.process_env_step(rew.clone(), dones.clone(), {k: dict(v) for k, v in extras.items()},
+                                    None if intr is None else intr.clone())
+        with contextlib.redirect_stdout(io.StringIO()):
+            for lg in loggers:
+                lg.log(it=it, start_it=0, total_it=3, collect_time=0.1, learn_time=0.2,
+                       loss_dict={"value": 1.0 + it}, learning_rate=1e-3, action_std=torch.ones(2),
+                       rnd_weight=0.5 if rnd else None)
+    assert writers[0].rows == writers[1].rows
