@@ -538,3 +538,32 @@ def test_random_distillation_settings_log_exactly_what_upstream_logs(ref, tmp_pa
     for c in sorted({k for r in rows["upstream"] for k in r}):
         if not c.startswith("Perf/") and c != "wall_s":
             assert [r.get(c) for r in rows["b200"]] == [r.get(c) for r in rows["upstream"]], (c, alg, student)
+
+
+@pytest.mark.parametrize("draw", range(8))
+def test_selective_checkpoint_loading_matches_upstream(ref, tmp_path, draw):
+    """Random ``load_cfg`` selections (actor, critic, optimizer, iteration, RND) of an upstream checkpoint into
+    freshly built runners of both implementations: the resulting checkpoints and iteration counters are equal."""
+    import dataclasses
+    import random
+
+    rng = random.Random(12000 + draw)
+    spec = R.with_rnd("tracking12", dataclasses.replace(R.SPECS["tracking12"], num_envs=32, num_steps=4))
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        src, _, _ = R.build_runner("tracking12", 0, None, spec, impl="upstream")
+        src.learn(2)
+        src.save(str(tmp_path / "src.pt"))
+        load_cfg = {k: rng.random() < 0.5 for k in ("actor", "critic", "optimizer", "iteration", "rnd")}
+        saved = {}
+        for impl in ("b200", "upstream"):
+            dst, _, _ = R.build_runner("tracking12", 1, None, spec, impl=impl)
+            dst.load(str(tmp_path / "src.pt"), load_cfg=dict(load_cfg))
+            dst.save(str(tmp_path / f"{impl}.pt"))
+            saved[impl] = (dst.current_learning_iteration, torch.load(tmp_path / f"{impl}.pt", weights_only=False))
+    finally:
+        torch.set_num_threads(threads)
+    assert saved["b200"][0] == saved["upstream"][0]
+    for key in saved["upstream"][1]:
+        _equal_state(saved["b200"][1][key], saved["upstream"][1][key], f"{key} with {load_cfg}")
