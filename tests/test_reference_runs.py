@@ -567,3 +567,28 @@ def test_selective_checkpoint_loading_matches_upstream(ref, tmp_path, draw):
     assert saved["b200"][0] == saved["upstream"][0]
     for key in saved["upstream"][1]:
         _equal_state(saved["b200"][1][key], saved["upstream"][1][key], f"{key} with {load_cfg}")
+
+
+def test_distillation_checkpoint_resumes_like_upstream(ref, tmp_path):
+    """A distillation checkpoint (student, teacher, optimizer) of upstream loads into both implementations, which then
+    train on identically."""
+    threads = torch.get_num_threads()
+    torch.set_num_threads(2)
+    try:
+        teacher = R.make_teacher_checkpoint("tracking12", str(tmp_path / "t.pt"), iterations=1, num_envs=32,
+                                            impl="upstream")
+        src, _, _ = R.build_distillation_runner("tracking12", 0, None, teacher, impl="upstream", num_envs=32)
+        src.learn(2)
+        src.save(str(tmp_path / "distill.pt"))
+        saved = {}
+        for impl in ("b200", "upstream"):
+            runner, _, _ = R.build_distillation_runner("tracking12", 3, None, teacher, impl=impl, num_envs=32)
+            runner.load(str(tmp_path / "distill.pt"))
+            runner.learn(2)
+            runner.save(str(tmp_path / f"{impl}.pt"))
+            saved[impl] = torch.load(tmp_path / f"{impl}.pt", weights_only=False)
+    finally:
+        torch.set_num_threads(threads)
+    assert saved["b200"]["iter"] == saved["upstream"]["iter"]
+    for key in saved["upstream"]:
+        _equal_state(saved["b200"][key], saved["upstream"][key], key)
