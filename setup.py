@@ -10,6 +10,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("tt_rsl_rl_b200", "ops", "csrc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# TT_RSL_RL_DEBUG_BOUNDS=1: kernels check the indices they read from memory and report bad ones in their status word
+DEBUG = ["-DRL_DEBUG_BOUNDS"] if os.environ.get("TT_RSL_RL_DEBUG_BOUNDS") == "1" else []
 
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
@@ -24,7 +26,7 @@ setup(
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={
                 "cxx": ["-O3", "-std=c++17"],
-                "nvcc": ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", *ARCH],
+                "nvcc": ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", *ARCH, *DEBUG],
             },
         )
     ],

@@ -1,0 +1,53 @@
+"""Bounds-checked debug builds: the status code a bad index reports, its host-side error, and the build switch.
+
+Kernels that read indices from memory check them with ``RL_CHECK_INDEX`` when built with ``-DRL_DEBUG_BOUNDS``; an
+index outside its tensor is recorded in the status word and replaced by 0. The GPU side is a compile-time switch, so
+these host tests check the mapping of the status word and that release builds define the check away.
+"""
+
+from __future__ import annotations
+
+import os
+import re
+import types
+
+import pytest
+import torch
+
+from tt_rsl_rl_b200.engine.base import EngineBase
+from tt_rsl_rl_b200.parallel import CommTimeoutError
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PRIMS = os.path.join(ROOT, "tt_rsl_rl_b200", "ops", "csrc", "sm100_primitives.cuh")
+
+
+def _engine_with_status(words):
+    eng = types.SimpleNamespace(status=torch.tensor(words, dtype=torch.int64))
+    return eng
+
+
+def test_bad_index_status_raises_index_error_and_clears_the_word():
+    eng = _engine_with_status([8, 41, 3, 2])
+    with pytest.raises(IndexError, match="site=41 block=3 count=2"):
+        EngineBase._check_status(eng)
+    assert int(eng.status.abs().sum()) == 0
+
+
+def test_timeouts_still_raise_comm_timeout():
+    eng = _engine_with_status([4, 60, 0, 1])
+    with pytest.raises(CommTimeoutError):
+        EngineBase._check_status(eng)
+    EngineBase._check_status(_engine_with_status([0, 0, 0, 0]))  # a clean word raises nothing
+
+
+def test_status_code_of_bad_index_matches_the_host_mapping():
+    src = open(PRIMS).read()
+    assert re.search(r"kBadIndex\s*=\s*8\b", src)
+    # the release branch of the macro is empty: default builds carry no check
+    release = src.split("#else", 1)[1].split("#endif", 1)[0]
+    assert "RL_CHECK_INDEX" in release and "report_error" not in release
+
+
+def test_setup_adds_the_define_only_when_asked(monkeypatch):
+    text = open(os.path.join(ROOT, "setup.py")).read()
+    assert 'os.environ.get("TT_RSL_RL_DEBUG_BOUNDS") == "1"' in text and "-DRL_DEBUG_BOUNDS" in text

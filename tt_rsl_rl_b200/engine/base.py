@@ -111,6 +111,9 @@ class EngineBase:
         st = HostTransfers.read(self.status, "status")
         if st[0] != 0:
             self.status.zero_()
+            if st[0] == 8:  # kBadIndex, reported by builds with -DRL_DEBUG_BOUNDS
+                raise IndexError(f"a kernel read an index outside its tensor: site={st[1]} block={st[2]} "
+                                 f"count={st[3]} (the access was redirected to index 0)")
             from ..parallel import CommTimeoutError
 
             raise CommTimeoutError(f"device status error code={st[0]} site={st[1]} block={st[2]} count={st[3]}")

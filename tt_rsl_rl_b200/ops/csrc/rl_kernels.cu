@@ -316,6 +316,7 @@ __global__ void __launch_bounds__(256, 3) gather_minibatch_kernel(const GatherAr
       const int o = i - my_copy * a.B;
       if (a.idx_in) {
         my_src = a.idx_in[o];
+        RL_CHECK_INDEX(my_src, a.total, a.status, 41);
       } else {
         bool overflow = false;
         my_src = static_cast<int>(feistel_permute(static_cast<uint32_t>(a.offset + o), static_cast<uint32_t>(a.total),

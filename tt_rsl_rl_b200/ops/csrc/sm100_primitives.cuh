@@ -22,6 +22,7 @@ enum StatusCode : unsigned int {
   kTimeoutGridBarrier = 5,
   kBadShape = 6,
   kNonFinite = 7,
+  kBadIndex = 8,  // an index read from memory lies outside its tensor (checked in RL_DEBUG_BOUNDS builds)
 };
 
 __device__ __forceinline__ void report_error(unsigned int* status, unsigned int code, unsigned int site) {
@@ -32,6 +33,24 @@ __device__ __forceinline__ void report_error(unsigned int* status, unsigned int 
   }
   atomicAdd(status + 3, 1u);
 }
+
+// Bounds checks of indices that kernels read from memory (permutations, sample indices) before those indices address a
+// tensor. Built with -DRL_DEBUG_BOUNDS (TT_RSL_RL_DEBUG_BOUNDS=1 python setup.py build_ext --inplace), an index outside
+// [0, n) is recorded in the kernel's status word (kBadIndex, the site, the block) and replaced by 0, so the access stays
+// inside the tensor and the host raises after the launch. Release builds compile the check away.
+#ifdef RL_DEBUG_BOUNDS
+#define RL_CHECK_INDEX(idx, n, status, site)              \
+  do {                                                    \
+    if ((idx) < 0 || (idx) >= (n)) {                      \
+      ::rlb::report_error((status), ::rlb::kBadIndex, (site)); \
+      (idx) = 0;                                          \
+    }                                                     \
+  } while (0)
+#else
+#define RL_CHECK_INDEX(idx, n, status, site) \
+  do {                                       \
+  } while (0)
+#endif
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
