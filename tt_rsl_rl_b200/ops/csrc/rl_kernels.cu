@@ -290,6 +290,13 @@ constexpr int kGatherRows = 8;  // rows per warp iteration (their loads are issu
 // then lane l handles columns [4l, 4l + 4) of every row of the batch (128 columns per pass): a 16-byte load per row
 // when the source row pitch allows it (identity copies), else four scalar loads through the copy's column map. All
 // R rows' loads are issued before any conversion, so each warp keeps R 16-byte loads in flight.
+// Source column of a mirrored copy (a host-probed signed permutation); checked in RL_DEBUG_BOUNDS builds (site 42).
+__device__ __forceinline__ int perm_col(const int* p, int n, unsigned int* status) {
+  int j = __ldg(p);
+  RL_CHECK_INDEX(j, n, status, 42);
+  return j;
+}
+
 __global__ void __launch_bounds__(256, 3) gather_minibatch_kernel(const GatherArgs a) {
   __shared__ __align__(16) float s_mean[kGatherModels][kGatherMaxD];
   __shared__ __align__(16) float s_inv[kGatherModels][kGatherMaxD];
@@ -350,10 +357,10 @@ __global__ void __launch_bounds__(256, 3) gather_minibatch_kernel(const GatherAr
             if (perm != nullptr && cp[r] > 0) {  // mirrored copy: signed column permutation of the raw observation
               const int* pc = perm + cp[r] * D + c;
               const float* sc = sign + cp[r] * D + c;
-              v[r].x = __ldg(sc) * __ldg(row + __ldg(pc));
-              if (c + 1 < D) v[r].y = __ldg(sc + 1) * __ldg(row + __ldg(pc + 1));
-              if (c + 2 < D) v[r].z = __ldg(sc + 2) * __ldg(row + __ldg(pc + 2));
-              if (c + 3 < D) v[r].w = __ldg(sc + 3) * __ldg(row + __ldg(pc + 3));
+              v[r].x = __ldg(sc) * __ldg(row + perm_col(pc, D, a.status));
+              if (c + 1 < D) v[r].y = __ldg(sc + 1) * __ldg(row + perm_col(pc + 1, D, a.status));
+              if (c + 2 < D) v[r].z = __ldg(sc + 2) * __ldg(row + perm_col(pc + 2, D, a.status));
+              if (c + 3 < D) v[r].w = __ldg(sc + 3) * __ldg(row + perm_col(pc + 3, D, a.status));
             } else if (vec) {  // the row pitch is a multiple of 4 floats: columns past D are in-row padding
               v[r] = __ldg(reinterpret_cast<const float4*>(row + c));
             } else {
