@@ -13,7 +13,7 @@
 // bf16-output epilogues work in 32-row x 32-column steps through two 2 KB buffers per warp (64-byte swizzle, so the
 // row-per-thread 16-byte shared accesses are conflict-free): the data-gradient epilogue TMA-loads the next step's
 // ELU-output tile while it computes the current one, and every step leaves through a TMA store.
-// No load uses cluster multicast: every CTA fetches its own tiles from this GPU's memory.
+// Every CTA fetches its own tiles from this GPU's memory; no tile load is shared between CTAs.
 //
 // The MLP layers of rsl_rl (rsl_rl/modules/mlp.py:91-95, Linear+ELU stacks) map onto three uses:
 //   forward : H_l   = elu(H_{l-1} W_l^T + b_l)      A = H_{l-1} (K-major), B = W_l (K-major)

@@ -1,7 +1,7 @@
 // Peer-to-peer collectives over NVLink / NVSwitch for the data-parallel engine.
 //
 // Buffers are plain cudaMalloc allocations shared between the ranks of one node through CUDA IPC handles; each
-// rank maps every peer's buffer once, so kernels read peer memory with ordinary loads (no TMA, no multicast).
+// rank maps every peer's buffer once, so kernels read peer memory with ordinary loads (no TMA on peer memory).
 // Synchronisation uses monotonically increasing epochs: a rank publishes `epoch` into slot `rank` of every peer's
 // flag array (st.release.sys) and waits (ld.acquire.sys, bounded by %globaltimer) until every slot of its own
 // array has reached `epoch`. On timeout the kernel records the failing peer in the status word and returns.
