@@ -230,14 +230,22 @@ def dist_info() -> tuple[int, int, int]:
                                                                                                       "0"))
 
 
-def make_env(num_envs: int, device: str, host_noise: bool, seed: int, fused: bool = False, **env_kw):
-    """The benchmark environment. ``fused`` selects this framework's fused step kernel (the same transition); the
-    reference arm always gets the PyTorch-op step so that none of this framework's kernels run on its path."""
+ENV_STEP = "PyTorch ops (cuBLAS matmuls + elementwise), the same step code on both arms"
+
+
+def make_env(num_envs: int, device: str, host_noise: bool, seed: int, inplace_obs: bool = False, **env_kw):
+    """The benchmark environment: the PyTorch-op step of the synthetic environment on both arms (none of this
+    framework's kernels run inside it). ``inplace_obs`` rewrites the observations in place instead of alternating two
+    buffers (same device work); this framework's engines copy observations when they act, which lets its runner
+    capture the whole rollout, environment step included, as one CUDA graph. The unmodified reference keeps a
+    reference to the observations it acted on, so its arm gets the alternating buffers. Host noise copies are
+    double-buffered on a copy stream on both arms."""
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv, humanoid_like
 
     if "obs_dim" in env_kw:  # config 0: the plain linear-Gaussian environment
         return LinearGaussianVecEnv(num_envs, device=device, seed=seed, fused=False, **env_kw)
-    return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise, fused=fused, **env_kw)
+    return humanoid_like(num_envs, device=device, seed=seed, host_noise=host_noise, fused=False,
+                         inplace_obs=inplace_obs, rollout_steps=T_STEPS if host_noise else None, **env_kw)
 
 
 def timed_learn_cpu(runner, steps: int, warmup: int) -> float:
@@ -355,8 +363,8 @@ def main() -> None:
     n_local = total_envs // world
     env_kw = conf["env"]
 
-    fused_env = args.impl == "ours"
-    env = make_env(n_local, device, host_noise=False, seed=rank, fused=fused_env, **env_kw)
+    inplace_obs = args.impl == "ours"
+    env = make_env(n_local, device, host_noise=False, seed=rank, inplace_obs=inplace_obs, **env_kw)
     runner = build_runner(args.impl, env, device, args.config, sections=args.sections)
     sampler = ClockSampler([local_rank]) if local_rank == 0 else None
     if sampler:
@@ -381,7 +389,7 @@ def main() -> None:
 
     e2e = None
     if not args.no_e2e:
-        env2 = make_env(n_local, device, host_noise=True, seed=rank, fused=fused_env, **env_kw)
+        env2 = make_env(n_local, device, host_noise=True, seed=rank, inplace_obs=inplace_obs, **env_kw)
         runner2 = build_runner(args.impl, env2, device, args.config)
         e2e_s = timed_learn(runner2, args.steps, args.warmup, world)
         h2d = T_STEPS * n_local * 96 * 4
@@ -414,8 +422,7 @@ def main() -> None:
                        "global_batch": samples, "seq_len": T_STEPS, "num_envs_total": total_envs,
                        "epochs": 5, "minibatches": 4, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (rollout arena >> 126 MB)",
-                       "env_step": "fused sm_100a kernel after two cuBLAS matmuls" if fused_env
-                       else "PyTorch ops (cuBLAS matmuls + elementwise)"},
+                       "env_step": ENV_STEP},
             "e2e": e2e,
             "gpu_launches": launches,
             "engine_host_reads": host_reads,

@@ -8,11 +8,22 @@ Episodes terminate at random with probability ``reset_prob`` per step (a termina
 Observations: group ``"policy"`` is the state ``s`` (S values); group ``"critic"`` appends ``privileged_dim``
 privileged features (|s|^2 / S, |a_prev|^2 / A, episode progress, then zeros) when ``privileged_dim > 0``.
 
-``step`` performs only asynchronous device work (no host synchronisation), so it can be captured in a CUDA graph. With ``host_noise=True`` the process noise is read from a pinned host pool and copied
-to the device every step (the input of an end-to-end measurement). The same class serves the CPU path, the CUDA path
-and the unmodified-reference benchmark arm; it depends only on torch and a TensorDict class. It implements rsl_rl's
-environment interface (``rsl_rl/env/vec_env.py:14-102``); the reference plugin benchmarks with a null environment
-instead (``scripts/bench_matrix.py:34-51``), which this package also has (``env/null.py``).
+``step`` performs only asynchronous device work (no host synchronisation), so it can be captured in a CUDA graph.
+
+Observation buffers: by default the PyTorch-op step alternates between two observation buffers, because rsl_rl keeps a
+reference to the observations a policy acted on and copies them into its storage after the next step. With
+``inplace_obs=True`` the observations are rewritten in place every step (the consumer copies them when it acts, as
+this framework's engines do); such an environment on CUDA is ``graph_capturable``. Both modes do the same device work.
+
+With ``host_noise=True`` the process noise is read from a pinned host pool and copied to the device every step (the
+input of an end-to-end measurement). With ``rollout_steps=T`` on CUDA the copy of step ``k + 1``'s noise runs on a
+side stream while step ``k`` computes (double buffer); the first step of every window of ``T`` steps copies in line,
+so a window that is captured as one CUDA graph joins every copy it forks. ``T`` must then equal the rollout length.
+
+The same class serves the CPU path, the CUDA path and the unmodified-reference benchmark arm; it depends only on torch
+and a TensorDict class. It implements rsl_rl's environment interface (``rsl_rl/env/vec_env.py:14-102``); the
+reference plugin benchmarks with a null environment instead (``scripts/bench_matrix.py:34-51``), which this package
+also has (``env/null.py``).
 """
 
 from __future__ import annotations
@@ -42,7 +53,8 @@ class LinearGaussianVecEnv(VecEnv):
     def __init__(self, num_envs: int, obs_dim: int = 48, num_actions: int = 12, privileged_dim: int = 0,
                  episode_length: int = 1000, reset_prob: float = 0.005, noise_std: float = 0.05, seed: int = 0,
                  device: str | torch.device = "cpu", host_noise: bool = False, host_noise_pool_steps: int = 8,
-                 step_dt: float = 0.02, fused: bool | None = None) -> None:
+                 step_dt: float = 0.02, fused: bool | None = None, inplace_obs: bool = False,
+                 rollout_steps: int | None = None) -> None:
         self.num_envs = num_envs
         self.num_obs = obs_dim
         self.num_actions = num_actions
@@ -74,11 +86,18 @@ class LinearGaussianVecEnv(VecEnv):
         crit_dim = obs_dim + privileged_dim
         self._critic_obs = torch.zeros(num_envs, crit_dim, device=self.device) if privileged_dim > 0 else None
         self.host_noise = host_noise
+        self._copy_stream = None
         if host_noise:
             pin = self.device.type == "cuda"
             pool = torch.randn(host_noise_pool_steps, num_envs, obs_dim, generator=gen)
             self._host_pool = pool.pin_memory() if pin else pool
             self._host_step = 0
+            if pin and rollout_steps is not None and rollout_steps > 1:
+                # double-buffered prefetch of the next step's noise on a copy stream
+                self._prefetch_window = int(rollout_steps)
+                self._copy_stream = torch.cuda.Stream(device=self.device)
+                self._noise_slots = (self._noise, torch.zeros_like(self._noise))
+                self._noise_ready = None
         self._write_obs(torch.zeros(num_envs, num_actions, device=self.device))
         self._obs = self._make_obs_dict()
         # fused device step (everything after the two matmuls in one kernel); None: on CUDA when the framework's
@@ -86,7 +105,8 @@ class LinearGaussianVecEnv(VecEnv):
         if fused is None:
             fused = self.device.type == "cuda" and _extension_available()
         self.fused = bool(fused)
-        if not self.fused:
+        self.inplace_obs = bool(inplace_obs) and not self.fused
+        if not self.fused and not self.inplace_obs:
             # the PyTorch-op step alternates between two observation buffers: the observations a policy acted on stay
             # intact until the algorithm has stored them after the next step (rsl_rl keeps a reference to them)
             self._spare_obs = (torch.zeros_like(self._policy_obs),
@@ -98,8 +118,9 @@ class LinearGaussianVecEnv(VecEnv):
 
     @property
     def graph_capturable(self) -> bool:
-        """The fused step only enqueues device work into fixed buffers, so a rollout can be one CUDA graph."""
-        return self.fused
+        """The fused step and the in-place PyTorch-op step on CUDA only enqueue device work into fixed buffers, so a
+        rollout can be one CUDA graph."""
+        return self.fused or (self.inplace_obs and self.device.type == "cuda")
 
     # ---- VecEnv -----------------------------------------------------------------------------------------------------
     @property
@@ -115,13 +136,34 @@ class LinearGaussianVecEnv(VecEnv):
             groups["critic"] = self._critic_obs
         return TensorDict(groups, batch_size=[self.num_envs], device=self.device)
 
-    def _draw_noise(self) -> None:
-        if self.host_noise:
-            src = self._host_pool[self._host_step % self._host_pool.shape[0]]
-            self._host_step += 1
-            self._noise.copy_(src, non_blocking=True)
-        else:
+    def _draw_noise(self) -> torch.Tensor:
+        """This step's process noise: drawn on the device, or copied from the pinned host pool."""
+        if not self.host_noise:
             self._noise.normal_()
+            return self._noise
+        k = self._host_step
+        self._host_step += 1
+        pool = self._host_pool
+        if self._copy_stream is None:
+            self._noise.copy_(pool[k % pool.shape[0]], non_blocking=True)
+            return self._noise
+        cur = torch.cuda.current_stream(self.device)
+        phase = k % self._prefetch_window
+        slot = self._noise_slots[k % 2]
+        if phase == 0 or self._noise_ready is None:
+            slot.copy_(pool[k % pool.shape[0]], non_blocking=True)
+        else:
+            cur.wait_event(self._noise_ready)  # the copy that step k - 1 started
+        self._noise_ready = None
+        if phase + 1 < self._prefetch_window:
+            # slot (k + 1) % 2 was last read by step k - 1, whose work is already on the current stream
+            self._copy_stream.wait_stream(cur)
+            with torch.cuda.stream(self._copy_stream):
+                self._noise_slots[(k + 1) % 2].copy_(pool[(k + 1) % pool.shape[0]], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(self._copy_stream)
+            self._noise_ready = ready
+        return slot
 
     def _write_obs(self, actions: torch.Tensor) -> None:
         self._policy_obs.copy_(self.state)
@@ -140,10 +182,10 @@ class LinearGaussianVecEnv(VecEnv):
         a = actions.to(self.device)
         if self.fused:
             return self._fused_step(a)
-        self._draw_noise()
+        noise = self._draw_noise()
         # s' = A s + B a + sigma * eps
         torch.addmm(torch.mm(self.state, self.At), a, self.Bt, out=self._next)
-        self._next.add_(self._noise, alpha=self.noise_std)
+        self._next.add_(noise, alpha=self.noise_std)
         # reward on the new state and the applied action
         torch.sum(self._next.square(), dim=1, out=self.rewards)
         self.rewards.add_(a.square().sum(dim=1), alpha=0.01).neg_()
@@ -159,10 +201,11 @@ class LinearGaussianVecEnv(VecEnv):
         self._reset_noise.normal_()
         self.state.copy_(torch.where(done.unsqueeze(1), self._reset_noise, self._next))
         self.episode_length_buf.masked_fill_(done, 0)
-        spare = self._spare_obs
-        self._spare_obs = (self._policy_obs, self._critic_obs)
-        self._policy_obs, self._critic_obs = spare
-        self._obs = self._make_obs_dict()
+        if not self.inplace_obs:
+            spare = self._spare_obs
+            self._spare_obs = (self._policy_obs, self._critic_obs)
+            self._policy_obs, self._critic_obs = spare
+            self._obs = self._make_obs_dict()
         self._write_obs(a)
         extras = {"time_outs": self.time_outs, "log": {"/state_norm": self.rewards}}
         return self._obs, self.rewards, self.dones, extras
@@ -171,10 +214,7 @@ class LinearGaussianVecEnv(VecEnv):
     def _fused_step(self, a: torch.Tensor):
         """Same transition on the device: the matmuls on cuBLAS, the rest in one kernel with Philox noise."""
         torch.addmm(torch.mm(self.state, self.At), a, self.Bt, out=self._next)
-        noise = None
-        if self.host_noise:
-            self._draw_noise()
-            noise = self._noise
+        noise = self._draw_noise() if self.host_noise else None
         from ..ops import ext
 
         a = a if a.stride(1) == 1 else a.contiguous()
