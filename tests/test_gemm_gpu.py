@@ -65,7 +65,7 @@ def test_dgrad_elu_colsum(M, Nin, Kout):
     w = _bf16((Kout, Nin), 0.1)
     h = torch.nn.functional.elu(torch.randn(M, Nin, device="cuda")).to(torch.bfloat16)
     out = torch.zeros(M, Nin, device="cuda", dtype=torch.bfloat16)
-    colsum = torch.zeros(G.m_tiles(M), Nin, device="cuda")
+    colsum = torch.full((G.colsum_rows(), Nin), float("nan"), device="cuda")  # every row is written
     G.gemm(dz, kp, False, w, Nin, True, M, Nin, Kout, G.EPI_DGRAD_ELU, out, Nin, aux=h, ld_aux=Nin, colsum=colsum)
     torch.cuda.synchronize()
     hf = h.float()
@@ -88,7 +88,7 @@ def test_dgrad_elu_padded_pitches(M, Nin, Kout):
     h = torch.zeros(M, G.pad8(Nin) + 8, device="cuda", dtype=torch.bfloat16)
     h[:, :Nin] = torch.nn.functional.elu(torch.randn(M, Nin, device="cuda")).to(torch.bfloat16)
     out = torch.full((M, G.pad8(Nin) + 16), 7.0, device="cuda", dtype=torch.bfloat16)
-    colsum = torch.zeros(G.m_tiles(M), Nin, device="cuda")
+    colsum = torch.full((G.colsum_rows(), Nin), float("nan"), device="cuda")  # every row is written
     G.gemm(dz, kp, False, w, w.shape[1], True, M, Nin, Kout, G.EPI_DGRAD_ELU, out, out.shape[1], aux=h,
            ld_aux=h.shape[1], colsum=colsum)
     torch.cuda.synchronize()

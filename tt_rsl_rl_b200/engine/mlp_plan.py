@@ -4,7 +4,7 @@ For a model ``MLPModel.mlp`` with layers ``W_1 .. W_L`` it owns bf16 weight shad
 batch and a training minibatch, and the partial-gradient buffers, and issues:
 
 * forward      ``H_l = elu(H_{l-1} W_l^T + b_l)`` (bf16 activations kept for backward), last layer fp32;
-* backward     data gradients ``dZ_{l-1} = (dZ_l W_l) * elu'(H_{l-1})`` with per-tile column sums (bias gradients)
+* backward     data gradients ``dZ_{l-1} = (dZ_l W_l) * elu'(H_{l-1})`` with per-CTA column sums (bias gradients)
                and weight gradients ``dW_l = dZ_l^T H_{l-1}`` as split-K fp32 partials.
 
 Row pitches of all bf16 buffers are padded to multiples of 8 elements (16 bytes, the TMA stride rule).
@@ -65,9 +65,9 @@ class MLPPlan:
         # gradient of the head output (written by the loss kernel) and of hidden pre-activations
         self.d_head = torch.zeros(B, pad8(self.head_cols), **bf)
         self.dz = [torch.zeros(B, pad8(w), **bf) for w in self.widths[1:-1]]
-        self.m_tiles = G.m_tiles(B)
-        # bias-gradient partials of hidden layers: colsums from the data-gradient GEMM of the next layer
-        self.bias_partial = [torch.zeros(self.m_tiles, w, **f32) for w in self.widths[1:-1]]
+        # bias-gradient partials of hidden layers: per-CTA column sums from the data-gradient GEMM of the next layer
+        self.colsum_rows = int(ext().gemm_colsum_rows(sm_count))
+        self.bias_partial = [torch.zeros(self.colsum_rows, w, **f32) for w in self.widths[1:-1]]
         self.splits = []
         self.wgrad_partial = []
         for lin in self.linears:
@@ -130,10 +130,7 @@ class MLPPlan:
             # dZ_{l-1} = (dZ_l W_l) * elu'(H_{l-1}); W_l [out, pad8(in)] read MN-major
             w = self.w_bf16[l]
             dz_prev = self.dz[l - 1]
-            colsum = self.bias_partial[l - 1]
-            used = G.m_tiles(rows)
-            if used < self.m_tiles:
-                colsum[used:].zero_()
+            colsum = self.bias_partial[l - 1]  # every row written by the launch (unused CTAs' rows cleared)
             G.gemm(dz_l, dz_l.shape[1], False, w, w.shape[1], True, rows, in_f, out_f, G.EPI_DGRAD_ELU, dz_prev,
                    dz_prev.shape[1], aux=h_in, ld_aux=h_in.shape[1], colsum=colsum, status=status)
             dz_l = dz_prev
@@ -145,7 +142,7 @@ class MLPPlan:
         for l, lin in enumerate(self.linears):
             segs[id(lin.weight)] = (self.wgrad_partial[l], self.splits[l], lin.weight.numel())
             if l < self.L - 1:
-                segs[id(lin.bias)] = (self.bias_partial[l], self.m_tiles, lin.bias.numel())
+                segs[id(lin.bias)] = (self.bias_partial[l], self.colsum_rows, lin.bias.numel())
             else:
                 segs[id(lin.bias)] = (head_bias_partial, head_parts, lin.bias.numel())
         return segs

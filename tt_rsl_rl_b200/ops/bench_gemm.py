@@ -53,7 +53,7 @@ def main() -> None:
     for Kout, Nin in ((256, 512), (128, 256), (32, 128)):
         dz, w, h = bf(B, Kout), bf(Kout, Nin), bf(B, Nin)
         y = torch.empty(B, Nin, device=dev, dtype=torch.bfloat16)
-        cs = torch.empty(G.m_tiles(B), Nin, device=dev)
+        cs = torch.empty(G.colsum_rows(dev), Nin, device=dev)
         timeit(f"data gradient {Kout}->{Nin}",
                lambda: G.gemm(dz, Kout, False, w, Nin, True, B, Nin, Kout, G.EPI_DGRAD_ELU, y, Nin, aux=h,
                               ld_aux=Nin, colsum=cs), 2 * B * (Kout + 2 * Nin))

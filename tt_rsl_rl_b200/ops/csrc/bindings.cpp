@@ -50,9 +50,14 @@ void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b
   if (aux.has_value() && aux->defined()) {
     TORCH_CHECK(aux->scalar_type() == torch::kBFloat16 && avail(*aux) >= (M - 1) * ld_aux + N, "gemm: bad aux");
   }
+  int64_t colsum_rows = 0;
   if (colsum.has_value() && colsum->defined()) {
-    TORCH_CHECK(colsum->scalar_type() == torch::kFloat32 && colsum->numel() >= rlb::gemm_m_tiles(M) * N,
-                "gemm: colsum too small");
+    // one row of N column sums per CTA: [rows, N] with rows >= the launch's CTA count (checked by the launcher)
+    TORCH_CHECK(colsum->scalar_type() == torch::kFloat32 && colsum->dim() == 2 && colsum->is_contiguous() &&
+                    colsum->size(1) == N,
+                "gemm: colsum must be a contiguous fp32 [rows, N] tensor");
+    TORCH_CHECK(N <= rlb::kColsumMaxN, "gemm: column sums need N <= ", rlb::kColsumMaxN);
+    colsum_rows = colsum->size(0);
   }
   const at::cuda::CUDAGuard guard(a.device());
   rlb::GemmParams p;
@@ -74,6 +79,7 @@ void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b
   p.aux = ptr_or_null<const void>(aux);
   p.ld_aux = static_cast<int>(ld_aux);
   p.colsum = ptr_or_null<float>(colsum);
+  p.colsum_rows = static_cast<int>(colsum_rows);
   p.status = ptr_or_null<unsigned int>(status);
   raise_on(rlb::gemm_launch(p, at::cuda::getCurrentCUDAStream()), "gemm");
 }
@@ -83,6 +89,7 @@ void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of tt_rsl_rl_b200";
   m.def("gemm", &gemm, "tcgen05 GEMM with fused MLP epilogues");
+  m.def("gemm_colsum_rows", [](int64_t sms) { return static_cast<int64_t>(rlb::gemm_colsum_rows(static_cast<int>(sms))); });
   rlb_register_kernels(m);
   rlb_register_p2p(m);
   rlb_register_rnn(m);

@@ -66,8 +66,10 @@ struct Cfg {
   static constexpr int kStagingBytes = kStaged ? kEpiWarps * 2 * kEpiBufBytes : 0;
   static constexpr int kBiasBytes = kStaged ? kEpiWarps * 32 * 4 : 0;
   static constexpr int kColsumBytes = EPI == kEpiDgradElu ? 2 * 4 * BN * 4 : 0;  // double-buffered by tile parity
+  static constexpr int kColAccBytes = EPI == kEpiDgradElu ? kColsumMaxN * 4 : 0;   // the CTA's running column sums
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kFixed = 1024 /*alignment slack*/ + kStagingBytes + kBiasBytes + kColsumBytes + kBarrierBytes;
+  static constexpr int kFixed = 1024 /*alignment slack*/ + kStagingBytes + kBiasBytes + kColsumBytes + kColAccBytes +
+                                kBarrierBytes;
   static constexpr int kStagesFit = (kSmemBudget - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
   static constexpr int kAccCols = BN < 32 ? 32 : BN;
@@ -110,7 +112,8 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
   uint8_t* staging = sB + S * C::kBBytes;  // 1024-byte aligned: stage sizes are multiples of 1 KB
   float* bias_smem = reinterpret_cast<float*>(staging + C::kStagingBytes);
   float* colsum_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bias_smem) + C::kBiasBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(colsum_s) + C::kColsumBytes);
+  float* colacc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(colsum_s) + C::kColsumBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(colacc) + C::kColAccBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
@@ -275,6 +278,9 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
     if constexpr (EPI == kEpiDgradElu) {
       seek(pt, psc);
       if (lane == 0) issue_aux();
+      // the CTA's running column sums start at zero (made visible by the first tile's named barrier)
+      if (p.colsum != nullptr)
+        for (int n = threadIdx.x - 64; n < p.N; n += kEpiWarps * 32) colacc[n] = 0.f;
     }
     // After a timeout the warp keeps walking the tile schedule without waiting or computing, so every epilogue warp
     // still reaches each tile's column-sum barrier (a named barrier cannot time out) and the kernel unwinds.
@@ -376,11 +382,21 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
           named_barrier_sync(1, kEpiWarps * 32);
           const int tt = threadIdx.x - 64;
           for (int n = tt; n < BN; n += kEpiWarps * 32) {
-            if (tc.n0 + n < p.N) {
-              const float sum = cs[n] + cs[BN + n] + cs[2 * BN + n] + cs[3 * BN + n];
-              p.colsum[static_cast<size_t>(tc.m_tile) * p.N + tc.n0 + n] = sum;
-            }
+            if (tc.n0 + n < p.N) colacc[tc.n0 + n] += (cs[n] + cs[BN + n]) + (cs[2 * BN + n] + cs[3 * BN + n]);
           }
+        }
+      }
+    }
+    if constexpr (EPI == kEpiDgradElu) {
+      // one partial row per CTA (tiles of this CTA summed in schedule order); rows of CTAs that this launch does not
+      // have are cleared by CTA 0, so the reduction over all colsum_rows rows never sums stale values
+      if (p.colsum != nullptr) {
+        named_barrier_sync(1, kEpiWarps * 32);
+        const int tt = threadIdx.x - 64;
+        for (int n = tt; n < p.N; n += kEpiWarps * 32) {
+          p.colsum[static_cast<size_t>(blockIdx.x) * p.N + n] = colacc[n];
+          if (blockIdx.x == 0)
+            for (int r = gridDim.x; r < p.colsum_rows; ++r) p.colsum[static_cast<size_t>(r) * p.N + n] = 0.f;
         }
       }
     }
@@ -531,6 +547,7 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   if (tiles > (1ll << 31) - 1) return cudaErrorInvalidValue;
   const long long slots = static_cast<long long>(sm_count()) * C::kMinBlocks;
   const int grid = static_cast<int>(tiles < slots ? tiles : slots);
+  if (EPI == kEpiDgradElu && p.colsum != nullptr && grid > p.colsum_rows) return cudaErrorInvalidValue;
   kern<<<grid, Shape<EPI, WIDE>::kThreads, C::kSmemBytes, stream>>>(ta, tb, to, tx, p, num_kb, n_tiles, m_tiles,
                                                                     p.splits);
   return cudaGetLastError();
@@ -584,6 +601,8 @@ cudaError_t gemm_launch(const GemmParams& p, cudaStream_t stream) {
   if (p.splits > num_kb) return cudaErrorInvalidValue;
   if (p.splits > 1 && p.epilogue != kEpiPartialF32) return cudaErrorInvalidValue;
   if (p.epilogue == kEpiDgradElu && p.aux == nullptr) return cudaErrorInvalidValue;
+  if (p.epilogue == kEpiDgradElu && p.colsum != nullptr && (p.N > kColsumMaxN || p.colsum_rows < 1))
+    return cudaErrorInvalidValue;
   const bool staged = p.epilogue == kEpiBiasEluBf16 || p.epilogue == kEpiBiasBf16 || p.epilogue == kEpiDgradElu;
   // TMA epilogue rules: 16-byte aligned bases, row pitches that are multiples of 16 bytes
   if (staged && ((p.ldo % 8) != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15))) return cudaErrorInvalidValue;

@@ -39,14 +39,21 @@ struct GemmParams {
   const float* bias = nullptr;
   const void* aux = nullptr;  // bf16 [M, ld_aux]
   int ld_aux = 0;
-  float* colsum = nullptr;    // fp32 [gridDim.x, N]: per-M-tile column sums of the stored output (bias gradients)
+  float* colsum = nullptr;    // fp32 [colsum_rows, N]: per-CTA column sums of the stored output (bias gradients)
+  int colsum_rows = 0;        // rows of colsum (>= the launch's CTA count, gemm_colsum_rows()); N <= kColsumMaxN
   unsigned int* status = nullptr;
 };
+
+// Widest output whose column sums the data-gradient epilogue accumulates per CTA (shared memory, fp32).
+constexpr int kColsumMaxN = 1024;
 
 // Returns cudaSuccess or the launch error. Host-side validation failures return cudaErrorInvalidValue.
 cudaError_t gemm_launch(const GemmParams& p, cudaStream_t stream);
 
-// Number of M tiles (rows of the colsum partial buffer) used for a given M.
+// Number of 128-row M tiles used for a given M.
 inline int gemm_m_tiles(int M) { return (M + 127) / 128; }
+
+// Rows of a column-sum partial buffer: one per CTA of the largest data-gradient launch (two CTAs per SM).
+inline int gemm_colsum_rows(int sm_count) { return 2 * sm_count; }
 
 }  // namespace rlb

@@ -672,6 +672,223 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// PPO loss without symmetry copies (the common path): eight lanes per row, four rows per warp
+// ---------------------------------------------------------------------------------------------------------------
+// Lane l8 = lane % 8 of row group g = lane / 8 holds actions 4 l8 .. 4 l8 + 3 (A <= 32). The row's scalar terms
+// (ratio, clipped surrogate, clipped value loss) are evaluated once per eight lanes instead of once per 32, the
+// per-row sums need three shuffle rounds, and every load of a row is issued before its arithmetic. Same formulas and
+// tie rules as ppo_loss_kernel; the per-block partials have the same layout (grid = ppo_loss_blocks(B)).
+constexpr int kLoss8Warps = 8;
+static_assert(kLoss8Warps * 4 == kLossRowsPerBlock, "row groups of the two loss kernels must match");
+
+__global__ void __launch_bounds__(kLoss8Warps * 32, 2) ppo_loss_rows8_kernel(const PpoLossArgs a) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 3;   // row of the warp's four
+  const int l8 = lane & 7;   // action group
+  const float invP = 1.0f / static_cast<float>(a.n0);
+  const float invE = invP;
+  const int A = a.A;
+  const int head_cols = a.hetero ? 2 * A : A;
+  float acc_dh[4] = {0.f, 0.f, 0.f, 0.f}, acc_ds[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc_surr = 0.f, acc_val = 0.f, acc_ent = 0.f, acc_kl = 0.f, acc_dv = 0.f;
+  // state-independent std of this lane's actions (a parameter), once per kernel
+  float c_raw[4], c_sd[4], c_lsd[4], c_isd[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int j = 4 * l8 + k;
+    c_raw[k] = (!a.hetero && j < A) ? a.std_param[j] : 1.f;
+    std_terms(c_raw[k], a, c_sd[k], c_lsd[k], c_isd[k]);
+  }
+  const int ngroups = (a.B + kLossRowsPerBlock - 1) / kLossRowsPerBlock;
+  for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
+    const int i = grp * kLossRowsPerBlock + warp * 4 + g;
+    const bool in = i < a.B;  // rows past B still take part in the warp's shuffles, with neutral values
+    const int src = in ? a.idx[i] : 0;
+    const float* h = a.head + static_cast<size_t>(in ? i : 0) * a.ld_head;
+    // ---- loads ----
+    float act[4], omu[4], osd[4], mu[4], raw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * l8 + k;
+      const bool ok = in && j < A;
+      const size_t so = static_cast<size_t>(src) * A + j;
+      act[k] = ok ? a.st_actions[so] : 0.f;
+      omu[k] = ok ? a.st_mean[so] : 0.f;
+      osd[k] = ok ? a.st_std[so] : 1.f;
+      mu[k] = ok ? h[j] : 0.f;
+      raw[k] = (ok && a.hetero) ? h[A + j] : c_raw[k];
+    }
+    const float adv = !in ? 0.f : (a.adv_override ? a.adv_override[i] : a.st_adv[src]);
+    const float lp_old = in ? a.st_logp[src] : 0.f;
+    const float ret = in ? a.st_ret[src] : 0.f;
+    const float vold = in ? a.st_val[src] : 0.f;
+    const float v = in ? a.value[static_cast<size_t>(i) * a.ld_value] : 0.f;
+    // ---- per-action terms ----
+    float sd[4], isd[4], lp = 0.f, ent = 0.f, kl = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * l8 + k;
+      sd[k] = c_sd[k];
+      isd[k] = c_isd[k];
+      float lsd = c_lsd[k];
+      if (a.hetero) std_terms(raw[k], a, sd[k], lsd, isd[k]);
+      if (in && j < A) {
+        const float z = (act[k] - mu[k]) * isd[k];
+        lp += -0.5f * z * z - lsd - kLogSqrt2Pi;
+        ent += 0.5f + kLogSqrt2Pi + lsd;
+        const float r = osd[k] * isd[k];
+        const float t1 = (omu[k] - mu[k]) * isd[k];
+        kl += 0.5f * (r * r + t1 * t1 - 1.0f) - __logf(r);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      lp += __shfl_xor_sync(0xffffffffu, lp, off);
+      ent += __shfl_xor_sync(0xffffffffu, ent, off);
+      kl += __shfl_xor_sync(0xffffffffu, kl, off);
+    }
+    // ---- row terms (identical on the row's eight lanes) ----
+    const float ratio = expf(lp - lp_old);
+    const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
+    const float rc = fminf(fmaxf(ratio, lo), hi);
+    const float s1 = -adv * ratio, s2 = -adv * rc;
+    float g1, g2;
+    max_grad_split(s1, s2, g1, g2);
+    const float in_rng = (ratio >= lo && ratio <= hi) ? 1.f : 0.f;
+    const float d_lp = (g1 * -adv + g2 * -adv * in_rng) * invP * ratio;
+    const float surr = fmaxf(s1, s2);
+    float dv, vloss;
+    if (a.clipped_value) {
+      const float dvv = v - vold;
+      const float vc = vold + fminf(fmaxf(dvv, -a.clip), a.clip);
+      const float l1 = (v - ret) * (v - ret), l2 = (vc - ret) * (vc - ret);
+      float q1, q2;
+      max_grad_split(l1, l2, q1, q2);
+      const float vin = (dvv >= -a.clip && dvv <= a.clip) ? 1.f : 0.f;
+      vloss = fmaxf(l1, l2);
+      dv = q1 * 2.f * (v - ret) + q2 * 2.f * (vc - ret) * vin;
+    } else {
+      vloss = (ret - v) * (ret - v);
+      dv = 2.f * (v - ret);
+    }
+    dv *= a.value_coef * invP;
+    const float ent_w = a.entropy_coef * invE;
+    // ---- gradients w.r.t. mean and std ----
+    float dmu[4], dsr[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * l8 + k;
+      dmu[k] = dsr[k] = 0.f;
+      if (in && j < A) {
+        const float inv_var = isd[k] * isd[k];
+        const float diff = act[k] - mu[k];
+        dmu[k] = d_lp * diff * inv_var;
+        const float dsd = (d_lp * (diff * diff * inv_var - 1.0f) - ent_w) * isd[k];
+        if (a.log_std) {
+          const float in = (raw[k] >= a.log_std_lo && raw[k] <= a.log_std_hi) ? 1.f : 0.f;
+          dsr[k] = dsd * sd[k] * in;
+        } else {
+          const float in = (raw[k] >= a.std_lo && raw[k] <= a.std_hi) ? 1.f : 0.f;
+          dsr[k] = dsd * in;
+        }
+        acc_dh[k] += dmu[k];
+        acc_ds[k] += dsr[k];
+      }
+    }
+    if (!in) continue;  // past this point only the row's own stores and accumulators
+    __nv_bfloat16* dh = static_cast<__nv_bfloat16*>(a.d_head) + static_cast<size_t>(i) * a.ld_dhead;
+    if (!a.hetero) {
+      // columns 4 l8 .. 4 l8 + 3 in one 8-byte store (zeros past A: the padding columns of the row)
+      if (4 * l8 < a.ld_dhead)
+        *reinterpret_cast<uint2*>(dh + 4 * l8) = make_uint2(pack_bf16x2(dmu[0], dmu[1]), pack_bf16x2(dmu[2], dmu[3]));
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int j = 4 * l8 + k;
+        if (j < A) {
+          dh[j] = __float2bfloat16_rn(dmu[k]);
+          dh[A + j] = __float2bfloat16_rn(dsr[k]);
+        }
+      }
+    }
+    for (int c = (a.hetero ? head_cols : 32) + l8; c < a.ld_dhead; c += 8) dh[c] = __float2bfloat16_rn(0.f);
+    if (l8 == 0) {
+      __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.d_value) + static_cast<size_t>(i) * a.ld_dvalue;
+      if (a.ld_dvalue == 8) {
+        *reinterpret_cast<uint4*>(dvp) = make_uint4(pack_bf16x2(dv, 0.f), 0u, 0u, 0u);
+      } else {
+        dvp[0] = __float2bfloat16_rn(dv);
+        for (int c = 1; c < a.ld_dvalue; ++c) dvp[c] = __float2bfloat16_rn(0.f);
+      }
+      acc_surr += surr * invP;
+      acc_val += vloss * invP;
+      acc_dv += dv;
+      acc_ent += ent * invE;
+      acc_kl += kl * invE;
+    }
+  }
+  // ---- block reduction in a fixed order: row groups of a warp, then warps ----
+#pragma unroll
+  for (int off = 8; off < 32; off <<= 1) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      acc_dh[k] += __shfl_xor_sync(0xffffffffu, acc_dh[k], off);
+      acc_ds[k] += __shfl_xor_sync(0xffffffffu, acc_ds[k], off);
+    }
+    acc_surr += __shfl_xor_sync(0xffffffffu, acc_surr, off);
+    acc_val += __shfl_xor_sync(0xffffffffu, acc_val, off);
+    acc_ent += __shfl_xor_sync(0xffffffffu, acc_ent, off);
+    acc_kl += __shfl_xor_sync(0xffffffffu, acc_kl, off);
+    acc_dv += __shfl_xor_sync(0xffffffffu, acc_dv, off);
+  }
+  __shared__ float sh_dh[kLoss8Warps][32];
+  __shared__ float sh_ds[kLoss8Warps][32];
+  __shared__ float sh_sc[kLoss8Warps][kLossStats + 1];
+  if (lane < 8) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      sh_dh[warp][4 * lane + k] = acc_dh[k];
+      sh_ds[warp][4 * lane + k] = acc_ds[k];
+    }
+  }
+  if (lane == 0) {
+    sh_sc[warp][0] = acc_surr;
+    sh_sc[warp][1] = acc_val;
+    sh_sc[warp][2] = acc_ent;
+    sh_sc[warp][3] = acc_kl;
+    sh_sc[warp][4] = 0.f;  // no mirror loss without copies
+    sh_sc[warp][5] = acc_dv;
+  }
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < 32) {
+    float sdh = 0.f, sds = 0.f;
+#pragma unroll
+    for (int w = 0; w < kLoss8Warps; ++w) {
+      sdh += sh_dh[w][t];
+      sds += sh_ds[w][t];
+    }
+    if (t < A) {
+      a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + t] = sdh;
+      if (a.hetero)
+        a.dhead_colsum[static_cast<size_t>(blockIdx.x) * head_cols + A + t] = sds;
+      else if (a.dstd_partial)
+        a.dstd_partial[static_cast<size_t>(blockIdx.x) * A + t] = sds;
+    }
+  } else if (t < 32 + kLossStats + 1) {
+    const int q = t - 32;
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kLoss8Warps; ++w) sum += sh_sc[w][q];
+    if (q < kLossStats)
+      a.stats_partial[static_cast<size_t>(blockIdx.x) * kLossStats + q] = sum;
+    else
+      a.dvalue_colsum[blockIdx.x] = sum;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // Behaviour-cloning loss gradient: one warp per row (lane j: columns j, j + 32), 8 warps x 4 rows per block
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kMseWarps = 8;
@@ -748,32 +965,37 @@ __global__ void __launch_bounds__(kMseWarps * 32) mse_grad_kernel(const MseArgs 
 // ---------------------------------------------------------------------------------------------------------------
 // segment reduction (sum of partial slabs in fixed order, fp64 accumulation)
 // ---------------------------------------------------------------------------------------------------------------
-// Block = 32 columns x 32 part-lanes: lane y sums parts y, y + 32, ... of its column (coalesced 128-byte rows), then the
-// 32 lane sums are combined in a fixed order. Deterministic for a given launch configuration.
-constexpr int kReduceCols = 32;
-constexpr int kReduceLanes = 32;
-__global__ void __launch_bounds__(kReduceCols* kReduceLanes)
-    reduce_segments_kernel(const ReduceSegment* segs, int nseg, float* send0, float* send1, const unsigned int* epoch,
-                           int accumulate) {
-  const int chunk = blockIdx.x;
+// One warp per chunk of 32 columns (lane = column, coalesced 128-byte rows), warps striding over the chunks of all
+// segments. A lane keeps 8 loads of its column in flight (parts p .. p + 7) and adds them into four fp64 partial
+// sums in a fixed order, so the result is deterministic for any launch configuration; a GPU-wide grid of such warps
+// keeps enough bytes in flight to stream the partial slabs at HBM bandwidth.
+constexpr int kReduceWarps = 8;
+__global__ void __launch_bounds__(kReduceWarps * 32)
+    reduce_segments_kernel(const ReduceSegment* __restrict__ segs, int nseg, int total_chunks, float* send0,
+                           float* send1, const unsigned int* epoch, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  float* dst_base = (((epoch ? *epoch : 0u) + 1u) & 1u) ? send1 : send0;
+  const int warps = gridDim.x * kReduceWarps;
   int s = 0;
-  while (s + 1 < nseg && segs[s + 1].first_chunk <= chunk) ++s;
-  const ReduceSegment g = segs[s];
-  float* dst = (((epoch ? *epoch : 0u) + 1u) & 1u) ? send1 : send0;
-  dst += g.dst_offset;
-  const long long e = static_cast<long long>(chunk - g.first_chunk) * kReduceCols + threadIdx.x;
-  double acc = 0.0;
-  if (e < g.n) {
-    for (int p = threadIdx.y; p < g.parts; p += kReduceLanes) acc += g.src[static_cast<size_t>(p) * g.n + e];
-  }
-  __shared__ double sh[kReduceLanes][kReduceCols];
-  sh[threadIdx.y][threadIdx.x] = acc;
-  __syncthreads();
-  if (threadIdx.y == 0 && e < g.n) {
-    double t = 0.0;
+  for (int chunk = blockIdx.x * kReduceWarps + (threadIdx.x >> 5); chunk < total_chunks; chunk += warps) {
+    while (s + 1 < nseg && segs[s + 1].first_chunk <= chunk) ++s;  // chunks only grow along a warp's walk
+    const ReduceSegment g = segs[s];
+    const long long e = static_cast<long long>(chunk - g.first_chunk) * kReduceChunk + lane;
+    if (e >= g.n) continue;
+    const float* col = g.src + e;
+    double acc[4] = {0.0, 0.0, 0.0, 0.0};
+    int p = 0;
+    for (; p + 8 <= g.parts; p += 8) {
+      float v[8];
 #pragma unroll
-    for (int y = 0; y < kReduceLanes; ++y) t += sh[y][threadIdx.x];
-    dst[e] = accumulate ? dst[e] + static_cast<float>(t) : static_cast<float>(t);
+      for (int u = 0; u < 8; ++u) v[u] = __ldcs(col + static_cast<size_t>(p + u) * g.n);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u & 3] += v[u];
+    }
+    for (; p < g.parts; ++p) acc[0] += __ldcs(col + static_cast<size_t>(p) * g.n);
+    const float t = static_cast<float>((acc[0] + acc[1]) + (acc[2] + acc[3]));
+    float* dst = dst_base + g.dst_offset + e;
+    *dst = accumulate ? *dst + t : t;
   }
 }
 
@@ -1212,8 +1434,12 @@ int ppo_loss_blocks(int B) {
 cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
   if (a.A > kLossMaxA || a.B <= 0) return cudaErrorInvalidValue;
   if (a.copies < 1 || a.n0 <= 0 || a.B != a.copies * a.n0) return cudaErrorInvalidValue;
+  const bool aligned = (reinterpret_cast<uintptr_t>(a.d_head) & 7) == 0 && (a.ld_dhead % 4) == 0 &&
+                       (a.ld_dvalue != 8 || (reinterpret_cast<uintptr_t>(a.d_value) & 15) == 0);
   if (a.copies > 1)
     ppo_loss_kernel<true><<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
+  else if (a.A <= 32 && aligned)
+    ppo_loss_rows8_kernel<<<ppo_loss_blocks(a.B), kLoss8Warps * 32, 0, s>>>(a);
   else
     ppo_loss_kernel<false><<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
   return cudaGetLastError();
@@ -1222,8 +1448,17 @@ cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
 cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_chunks, float* send0, float* send1,
                             const unsigned int* epoch, int accumulate, cudaStream_t s) {
   if (nseg <= 0 || total_chunks <= 0) return cudaErrorInvalidValue;
-  reduce_segments_kernel<<<total_chunks, dim3(kReduceCols, kReduceLanes), 0, s>>>(segs_dev, nseg, send0, send1, epoch,
-                                                                                    accumulate);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int want = (total_chunks + kReduceWarps - 1) / kReduceWarps;
+  const int grid = want < sms * 8 ? want : sms * 8;  // up to 64 resident warps per SM
+  reduce_segments_kernel<<<grid, kReduceWarps * 32, 0, s>>>(segs_dev, nseg, total_chunks, send0, send1, epoch,
+                                                            accumulate);
   return cudaGetLastError();
 }
 

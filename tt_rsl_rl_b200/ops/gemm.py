@@ -25,8 +25,15 @@ def pad8(n: int) -> int:
 
 
 def m_tiles(m: int) -> int:
-    """Number of 128-row tiles (rows of a column-sum partial buffer)."""
+    """Number of 128-row tiles."""
     return (m + 127) // 128
+
+
+def colsum_rows(device: torch.device | int | None = None) -> int:
+    """Rows of a column-sum partial buffer of the data-gradient epilogue: one per CTA of the largest launch."""
+    dev = torch.device("cuda") if device is None else torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    return int(ext().gemm_colsum_rows(torch.cuda.get_device_properties(idx).multi_processor_count))
 
 
 def gemm(

@@ -139,7 +139,7 @@ class OnPolicyRunner:
         if engine is not None and hasattr(engine, "action_std"):
             return engine.action_std()
         policy = self.alg.get_policy()
-        if getattr(policy, "distribution", None) is None or policy.distribution._distribution is None:
+        if getattr(policy, "distribution", None) is None or not policy.distribution.ready:
             return torch.zeros(1)
         return policy.output_std
 
