@@ -44,7 +44,62 @@ def resolve_b200_cfg(cfg: dict | None) -> dict:
     return out
 
 
+# ---- the PPO objective and schedules as functions (the PyTorch path's definition; the fused kernels evaluate the same
+# formulas: ops/csrc/rl_kernels.cu ppo_loss / adam_step) ------------------------------------------------------------
+LR_FLOOR, LR_CEILING, LR_FACTOR = 1e-5, 1e-2, 1.5
+
+
+def kl_adapted_learning_rate(lr: float, kl, desired_kl: float) -> float:
+    """Adaptive-KL schedule (``rsl_rl/algorithms/ppo.py:241-266``): shrink the step when the policy moved more than
+    twice the target KL, grow it when it moved less than half of it (and at all), within [1e-5, 1e-2]."""
+    if kl > desired_kl * 2.0:
+        return max(LR_FLOOR, lr / LR_FACTOR)
+    if desired_kl / 2.0 > kl > 0.0:
+        return min(LR_CEILING, lr * LR_FACTOR)
+    return lr
+
+
+def clipped_surrogate_loss(logp: torch.Tensor, old_logp: torch.Tensor, advantages: torch.Tensor,
+                           clip: float) -> torch.Tensor:
+    """Mean of ``max(-A r, -A clamp(r, 1 - clip, 1 + clip))`` with ``r = exp(logp - old_logp)``."""
+    ratio = torch.exp(logp - old_logp.squeeze(-1))
+    neg_adv = -advantages.squeeze(-1)
+    return torch.max(neg_adv * ratio, neg_adv * torch.clamp(ratio, 1.0 - clip, 1.0 + clip)).mean()
+
+
+def value_function_loss(values: torch.Tensor, old_values: torch.Tensor, returns: torch.Tensor, clip: float,
+                        clipped: bool) -> torch.Tensor:
+    """Squared error to the returns; with ``clipped`` the pessimistic max over the prediction and its clip to
+    ``old +- clip``."""
+    if not clipped:
+        return (returns - values).pow(2).mean()
+    near_old = old_values + (values - old_values).clamp(-clip, clip)
+    return torch.max((values - returns).pow(2), (near_old - returns).pow(2)).mean()
+
+
+def standardize(x: torch.Tensor) -> torch.Tensor:
+    """``(x - mean) / (unbiased std + 1e-8)``."""
+    return (x - x.mean()) / (x.std() + 1e-8)
+
+
+def generalized_advantages(storage: RolloutStorage, last_values: torch.Tensor, gamma: float, lam: float) -> None:
+    """Fill ``storage.returns`` by the reversed GAE recursion (a done cuts bootstrapping) and set
+    ``storage.advantages = returns - values``."""
+    values, T = storage.values, storage.num_transitions_per_env
+    gae = 0
+    for t in range(T - 1, -1, -1):
+        bootstrap = last_values if t == T - 1 else values[t + 1]
+        alive = 1.0 - storage.dones[t].float()
+        delta = storage.rewards[t] + alive * gamma * bootstrap - values[t]
+        gae = delta + alive * gamma * lam * gae
+        storage.returns[t] = gae + values[t]
+    storage.advantages = storage.returns - values
+
+
 class PPO:
+    """Clipped PPO with GAE, value clipping, entropy bonus, adaptive-KL learning rate and per-model gradient
+    clipping; optional RND and symmetry extensions; data parallel over ranks."""
+
     actor: MLPModel
     critic: MLPModel
 
@@ -79,39 +134,31 @@ class PPO:
         obs_template=None,
     ) -> None:
         self.device = device
-        self.is_multi_gpu = multi_gpu_cfg is not None
-        self.gpu_global_rank = multi_gpu_cfg["global_rank"] if multi_gpu_cfg else 0
-        self.gpu_world_size = multi_gpu_cfg["world_size"] if multi_gpu_cfg else 1
-        self.grad_reduce_bucket_mb = grad_reduce_bucket_mb
         self.b200_cfg = resolve_b200_cfg(b200_cfg)
-
+        # data parallel (one process per GPU): identity of this rank
+        self.is_multi_gpu = multi_gpu_cfg is not None
+        self.gpu_global_rank = multi_gpu_cfg["global_rank"] if self.is_multi_gpu else 0
+        self.gpu_world_size = multi_gpu_cfg["world_size"] if self.is_multi_gpu else 1
+        self.grad_reduce_bucket_mb = grad_reduce_bucket_mb
+        # extensions (the RND networks draw their initial weights here, after the models')
         self.rnd = RandomNetworkDistillation(device=self.device, **rnd_cfg) if rnd_cfg else None
         if symmetry_cfg is not None and (actor.is_recurrent or critic.is_recurrent):
             raise ValueError("Symmetry augmentation is not supported for recurrent policies.")
         self.symmetry = Symmetry(**symmetry_cfg) if symmetry_cfg else None
-
-        self.actor = actor.to(self.device)
-        self.critic = critic.to(self.device)
-        self._raw_actor = self.actor
-        self._raw_critic = self.critic
-        self.optimizer = resolve_optimizer(optimizer)(
-            list(dict.fromkeys(chain(self.actor.parameters(), self.critic.parameters()))), lr=learning_rate
-        )
+        # models and the one optimizer over both (a shared module's parameters once)
+        self.actor = self._raw_actor = actor.to(self.device)
+        self.critic = self._raw_critic = critic.to(self.device)
+        params = list(dict.fromkeys(chain(self.actor.parameters(), self.critic.parameters())))
+        self.optimizer = resolve_optimizer(optimizer)(params, lr=learning_rate)
         self.optimizer_name = optimizer.lower()
         self.storage = storage
         self.transition = RolloutStorage.Transition()
-
-        self.clip_param = clip_param
-        self.num_learning_epochs = num_learning_epochs
-        self.num_mini_batches = num_mini_batches
-        self.value_loss_coef = value_loss_coef
-        self.entropy_coef = entropy_coef
-        self.gamma = gamma
-        self.lam = lam
-        self.max_grad_norm = max_grad_norm
-        self.use_clipped_value_loss = use_clipped_value_loss
-        self.desired_kl = desired_kl
-        self.schedule = schedule
+        # hyper-parameters
+        self.num_learning_epochs, self.num_mini_batches = num_learning_epochs, num_mini_batches
+        self.clip_param, self.gamma, self.lam = clip_param, gamma, lam
+        self.value_loss_coef, self.entropy_coef = value_loss_coef, entropy_coef
+        self.max_grad_norm, self.use_clipped_value_loss = max_grad_norm, use_clipped_value_loss
+        self.desired_kl, self.schedule = desired_kl, schedule
         self._learning_rate = learning_rate
         self.normalize_advantage_per_mini_batch = normalize_advantage_per_mini_batch
         self.use_mixed_precision = use_mixed_precision
@@ -120,7 +167,6 @@ class PPO:
         from ..parallel import ReplicaChecker
 
         self._replica_checker = ReplicaChecker(self.b200_cfg["replica_check_interval"], self.gpu_world_size)
-
         self.engine = None
         if self._engine_requested():
             engine_cls = _engine_class(self.actor)
@@ -159,30 +205,33 @@ class PPO:
     def act(self, obs) -> torch.Tensor:
         if self.engine is not None:
             return self.engine.act(obs)
-        self.transition.hidden_states = (self.actor.get_hidden_state(), self.critic.get_hidden_state())
-        self.transition.actions = self.actor(obs, stochastic_output=True).detach()
-        self.transition.values = self.critic(obs).detach()
-        self.transition.actions_log_prob = self.actor.get_output_log_prob(self.transition.actions).detach()
-        self.transition.distribution_params = tuple(p.detach() for p in self.actor.output_distribution_params)
-        self.transition.observations = obs
-        return self.transition.actions
+        t = self.transition
+        t.hidden_states = (self.actor.get_hidden_state(), self.critic.get_hidden_state())
+        actions = self.actor(obs, stochastic_output=True).detach()  # draws the action noise
+        t.actions = actions
+        t.values = self.critic(obs).detach()
+        t.actions_log_prob = self.actor.get_output_log_prob(actions).detach()
+        t.distribution_params = tuple(p.detach() for p in self.actor.output_distribution_params)
+        t.observations = obs
+        return actions
 
     def process_env_step(self, obs, rewards: torch.Tensor, dones: torch.Tensor, extras: dict) -> None:
+        """Store the step: reward (+ intrinsic reward, + gamma V(s) for time-outs, the bootstrap of a truncated
+        episode from the value of the state it was cut in), then reset recurrent state at dones."""
         if self.engine is not None:
             self.engine.process_env_step(obs, rewards, dones, extras)
             return
-        self.transition.rewards = rewards.clone()
-        self.transition.dones = dones
+        t = self.transition
+        t.rewards = rewards.clone()
+        t.dones = dones
         if self.rnd:
             self.intrinsic_rewards = self.rnd.get_intrinsic_reward(obs)
-            self.transition.rewards += self.intrinsic_rewards
+            t.rewards += self.intrinsic_rewards
         if "time_outs" in extras:
-            # bootstrap truncated episodes with the value of the state they were cut in
-            self.transition.rewards += self.gamma * torch.squeeze(
-                self.transition.values * extras["time_outs"].unsqueeze(1).to(self.device), 1
-            )
-        self.storage.add_transition(self.transition)
-        self.transition.clear()
+            truncated = extras["time_outs"].unsqueeze(1).to(self.device)
+            t.rewards += self.gamma * torch.squeeze(t.values * truncated, 1)
+        self.storage.add_transition(t)
+        t.clear()
         self.actor.reset(dones)
         self.critic.reset(dones)
 
@@ -190,25 +239,17 @@ class PPO:
         if self.engine is not None:
             self.engine.compute_returns(obs)
             return
-        st = self.storage
-        hidden = self.critic.get_hidden_state()
+        hidden = self.critic.get_hidden_state()  # the bootstrap value must not advance the critic's state
         last_values = self.critic(obs).detach()
         self.critic.reset(hidden_state=hidden)
-        gae = 0
-        T = st.num_transitions_per_env
-        for t in reversed(range(T)):
-            next_values = last_values if t == T - 1 else st.values[t + 1]
-            not_done = 1.0 - st.dones[t].float()
-            delta = st.rewards[t] + not_done * self.gamma * next_values - st.values[t]
-            gae = delta + not_done * self.gamma * self.lam * gae
-            st.returns[t] = gae + st.values[t]
-        st.advantages = st.returns - st.values
+        st = self.storage
+        generalized_advantages(st, last_values, self.gamma, self.lam)
         if not self.normalize_advantage_per_mini_batch and st.advantages.numel() > 1:
-            st.advantages = (st.advantages - st.advantages.mean()) / (st.advantages.std() + 1e-8)
+            st.advantages = standardize(st.advantages)
 
     # ---- update ---------------------------------------------------------------------------------------------------------
     def update(self) -> dict[str, float]:
-        out = self._update()
+        out = self.engine.update() if self.engine is not None else self._update_autograd()
         self._replica_checker.step(self._replicated_parameters())
         return out
 
@@ -218,59 +259,52 @@ class PPO:
             params += list(self.rnd.predictor.parameters())
         return params
 
-    def _update(self) -> dict[str, float]:
-        if self.engine is not None:
-            return self.engine.update()
-        sums = {"value": 0.0, "surrogate": 0.0, "entropy": 0.0}
-        if self.rnd:
-            sums["rnd"] = 0.0
-        if self.symmetry:
-            sums["symmetry"] = 0.0
-        if self.actor.is_recurrent or self.critic.is_recurrent:
-            batches = self.storage.recurrent_mini_batch_generator(self.num_mini_batches, self.num_learning_epochs)
-        else:
-            batches = self.storage.mini_batch_generator(self.num_mini_batches, self.num_learning_epochs)
-        for batch in batches:
-            terms = self._minibatch_step(batch)
-            for k, v in terms.items():
-                sums[k] += v
+    def _minibatches(self):
+        recurrent = self.actor.is_recurrent or self.critic.is_recurrent
+        gen = self.storage.recurrent_mini_batch_generator if recurrent else self.storage.mini_batch_generator
+        return gen(self.num_mini_batches, self.num_learning_epochs)
+
+    def _update_autograd(self) -> dict[str, float]:
+        keys = ["value", "surrogate", "entropy"] + (["rnd"] if self.rnd else []) + (["symmetry"] if self.symmetry
+                                                                                  else [])
+        totals = dict.fromkeys(keys, 0.0)
+        for batch in self._minibatches():
+            for key, value in self._minibatch_step(batch).items():
+                totals[key] += value
+        # observation statistics move only after every epoch has used the rollout's normalisation
         obs = self.storage.observations.flatten(0, 1)
-        self.actor.update_normalization(obs)
-        self.critic.update_normalization(obs)
-        if self.rnd:
-            self.rnd.update_normalization(obs)
-        n = self.num_learning_epochs * self.num_mini_batches
+        for model in (self.actor, self.critic) + ((self.rnd,) if self.rnd else ()):
+            model.update_normalization(obs)
+        steps = self.num_learning_epochs * self.num_mini_batches
         self.storage.clear()
-        return {k: v / n for k, v in sums.items()}
+        return {key: value / steps for key, value in totals.items()}
 
     def _adapt_learning_rate(self, batch, dist_params: tuple[torch.Tensor, ...]) -> None:
-        """Adaptive-KL schedule, evaluated every minibatch before its optimizer step (``ppo.py:241-266``)."""
+        """The adaptive-KL rule on this minibatch's mean KL (rank-averaged), before its optimizer step; rank 0
+        decides and broadcasts the result."""
         with torch.inference_mode():
             kl_mean = torch.mean(self.actor.get_kl_divergence(batch.old_distribution_params, dist_params))
             if self.is_multi_gpu:
                 torch.distributed.all_reduce(kl_mean, op=torch.distributed.ReduceOp.SUM)
                 kl_mean /= self.gpu_world_size
             if self.gpu_global_rank == 0:
-                if kl_mean > self.desired_kl * 2.0:
-                    self._learning_rate = max(1e-5, self._learning_rate / 1.5)
-                elif self.desired_kl / 2.0 > kl_mean > 0.0:
-                    self._learning_rate = min(1e-2, self._learning_rate * 1.5)
+                self._learning_rate = kl_adapted_learning_rate(self._learning_rate, kl_mean, self.desired_kl)
             if self.is_multi_gpu:
-                lr = torch.tensor(self._learning_rate, device=self.device)
-                torch.distributed.broadcast(lr, src=0)
-                self._learning_rate = lr.item()
+                shared = torch.tensor(self._learning_rate, device=self.device)
+                torch.distributed.broadcast(shared, src=0)
+                self._learning_rate = shared.item()
             for group in self.optimizer.param_groups:
                 group["lr"] = self._learning_rate
 
     def _minibatch_step(self, batch) -> dict[str, float]:
-        n0 = batch.observations.batch_size[0]
+        n0 = batch.observations.batch_size[0]  # samples before symmetry copies are appended
         if self.normalize_advantage_per_mini_batch and batch.advantages.numel() > 1:
             with torch.no_grad():
-                batch.advantages = (batch.advantages - batch.advantages.mean()) / (batch.advantages.std() + 1e-8)
+                batch.advantages = standardize(batch.advantages)
         if self.symmetry:
             self.symmetry.augment_batch(batch, n0)
-        with torch.amp.autocast(device_type=torch.device(self.device).type, enabled=self.use_mixed_precision,
-                                dtype=torch.bfloat16):
+        device_type = torch.device(self.device).type
+        with torch.amp.autocast(device_type=device_type, enabled=self.use_mixed_precision, dtype=torch.bfloat16):
             self.actor(batch.observations, masks=batch.masks, hidden_state=batch.hidden_states[0],
                        stochastic_output=True)
             logp = self.actor.get_output_log_prob(batch.actions)
@@ -279,88 +313,80 @@ class PPO:
             entropy = self.actor.output_entropy[:n0]
             if self.desired_kl is not None and self.schedule == "adaptive":
                 self._adapt_learning_rate(batch, dist_params)
-            ratio = torch.exp(logp - batch.old_actions_log_prob.squeeze(-1))
-            adv = batch.advantages.squeeze(-1)
-            surrogate_loss = torch.max(-adv * ratio,
-                                       -adv * torch.clamp(ratio, 1.0 - self.clip_param, 1.0 + self.clip_param)).mean()
-            if self.use_clipped_value_loss:
-                clipped = batch.values + (values - batch.values).clamp(-self.clip_param, self.clip_param)
-                value_loss = torch.max((values - batch.returns).pow(2), (clipped - batch.returns).pow(2)).mean()
-            else:
-                value_loss = (batch.returns - values).pow(2).mean()
-            loss = surrogate_loss + self.value_loss_coef * value_loss - self.entropy_coef * entropy.mean()
+            surrogate = clipped_surrogate_loss(logp, batch.old_actions_log_prob, batch.advantages, self.clip_param)
+            value = value_function_loss(values, batch.values, batch.returns, self.clip_param,
+                                        self.use_clipped_value_loss)
+            loss = surrogate + self.value_loss_coef * value - self.entropy_coef * entropy.mean()
             rnd_loss = self.rnd.compute_loss(batch.observations[:n0]) if self.rnd else None
-            symmetry_loss = None
-            if self.symmetry:
-                symmetry_loss = self.symmetry.compute_loss(self.actor, batch, n0)
-                if self.symmetry.use_mirror_loss:
-                    loss = loss + self.symmetry.mirror_loss_coeff * symmetry_loss
+            mirror = self.symmetry.compute_loss(self.actor, batch, n0) if self.symmetry else None
+            if mirror is not None and self.symmetry.use_mirror_loss:
+                loss = loss + self.symmetry.mirror_loss_coeff * mirror
+        self._optimizer_step(loss, rnd_loss)
+        out = {"value": value.item(), "surrogate": surrogate.item(), "entropy": entropy.mean().item()}
+        if rnd_loss is not None:
+            out["rnd"] = rnd_loss.item()
+        if mirror is not None:
+            out["symmetry"] = mirror.item()
+        return out
+
+    def _optimizer_step(self, loss: torch.Tensor, rnd_loss: torch.Tensor | None) -> None:
+        """Gradients of both losses, rank average, one clip per model (actor incl. its std, critic), the steps."""
         self.optimizer.zero_grad()
         loss.backward()
-        if self.rnd:
+        if rnd_loss is not None:
             self.rnd.optimizer.zero_grad()
             rnd_loss.backward()
         if self.is_multi_gpu:
             self.reduce_parameters()
-        nn.utils.clip_grad_norm_(self.actor.parameters(), self.max_grad_norm)
-        nn.utils.clip_grad_norm_(self.critic.parameters(), self.max_grad_norm)
+        for model in (self.actor, self.critic):
+            nn.utils.clip_grad_norm_(model.parameters(), self.max_grad_norm)
         self.optimizer.step()
-        if self.rnd:
-            self.rnd.optimizer.step()
-        out = {"value": value_loss.item(), "surrogate": surrogate_loss.item(), "entropy": entropy.mean().item()}
         if rnd_loss is not None:
-            out["rnd"] = rnd_loss.item()
-        if symmetry_loss is not None:
-            out["symmetry"] = symmetry_loss.item()
-        return out
+            self.rnd.optimizer.step()
 
     # ---- modes, checkpoints -----------------------------------------------------------------------------------------------
+    def _trained_modules(self):
+        return (self.actor, self.critic) + ((self.rnd,) if self.rnd else ())
+
     def train_mode(self) -> None:
-        self.actor.train()
-        self.critic.train()
-        if self.rnd:
-            self.rnd.train()
+        for m in self._trained_modules():
+            m.train()
 
     def eval_mode(self) -> None:
-        self.actor.eval()
-        self.critic.eval()
-        if self.rnd:
-            self.rnd.eval()
+        for m in self._trained_modules():
+            m.eval()
 
     def save(self) -> dict:
         if self.engine is not None:
             self.engine.sync_to_torch()
-        out = {
-            "actor_state_dict": self._raw_actor.state_dict(),
-            "critic_state_dict": self._raw_critic.state_dict(),
-            "optimizer_state_dict": self.optimizer.state_dict(),
-        }
+        out = {"actor_state_dict": self._raw_actor.state_dict(), "critic_state_dict": self._raw_critic.state_dict(),
+               "optimizer_state_dict": self.optimizer.state_dict()}
         if self.rnd:
-            out["rnd_state_dict"] = self.rnd.state_dict()
-            out["rnd_optimizer_state_dict"] = self.rnd.optimizer.state_dict()
-            out["rnd_update_counter"] = self.rnd.update_counter
+            out.update(rnd_state_dict=self.rnd.state_dict(), rnd_optimizer_state_dict=self.rnd.optimizer.state_dict(),
+                       rnd_update_counter=self.rnd.update_counter)
         return out
 
+    _LOAD_ALL = {"actor": True, "critic": True, "optimizer": True, "iteration": True, "rnd": True}
+
     def load(self, loaded_dict: dict, load_cfg: dict | None, strict: bool) -> bool:
+        """Load the selected parts (all by default); returns whether the runner resumes the iteration count."""
         if self.engine is not None:
             self.engine.sync_to_torch()
-        if load_cfg is None:
-            load_cfg = {"actor": True, "critic": True, "optimizer": True, "iteration": True, "rnd": True}
-        loaded_dict = _upgrade_legacy_checkpoint(loaded_dict)
-        if load_cfg.get("actor"):
-            self._raw_actor.load_state_dict(loaded_dict["actor_state_dict"], strict=strict)
-        if load_cfg.get("critic"):
-            self._raw_critic.load_state_dict(loaded_dict["critic_state_dict"], strict=strict)
-        if load_cfg.get("optimizer") and "optimizer_state_dict" in loaded_dict:
-            self.optimizer.load_state_dict(loaded_dict["optimizer_state_dict"])
+        sel = self._LOAD_ALL if load_cfg is None else load_cfg
+        ckpt = _upgrade_legacy_checkpoint(loaded_dict)
+        for part, model in (("actor", self._raw_actor), ("critic", self._raw_critic)):
+            if sel.get(part):
+                model.load_state_dict(ckpt[f"{part}_state_dict"], strict=strict)
+        if sel.get("optimizer") and "optimizer_state_dict" in ckpt:
+            self.optimizer.load_state_dict(ckpt["optimizer_state_dict"])
             self._learning_rate = self.optimizer.param_groups[0]["lr"]
-        if load_cfg.get("rnd") and self.rnd:
-            self.rnd.load_state_dict(loaded_dict["rnd_state_dict"], strict=strict)
-            self.rnd.optimizer.load_state_dict(loaded_dict["rnd_optimizer_state_dict"])
-            self.rnd.update_counter = loaded_dict.get("rnd_update_counter", 0)
+        if sel.get("rnd") and self.rnd:
+            self.rnd.load_state_dict(ckpt["rnd_state_dict"], strict=strict)
+            self.rnd.optimizer.load_state_dict(ckpt["rnd_optimizer_state_dict"])
+            self.rnd.update_counter = ckpt.get("rnd_update_counter", 0)
         if self.engine is not None:
             self.engine.sync_from_torch()
-        return load_cfg.get("iteration", False)
+        return sel.get("iteration", False)
 
     def get_policy(self) -> MLPModel:
         if self.engine is not None:
@@ -378,15 +404,13 @@ class PPO:
     # ---- construction ---------------------------------------------------------------------------------------------------
     @staticmethod
     def construct_algorithm(obs, env, cfg: dict, device: str) -> PPO:
+        """Resolve classes and observation sets, build actor, critic, extensions and storage from a runner config."""
         alg_class, alg_cfg = resolve_class(cfg["algorithm"])
+        sets = ["actor", "critic"] + (["rnd_state"] if alg_cfg.get("rnd_cfg") is not None else [])
+        cfg["obs_groups"] = resolve_obs_groups(obs, cfg["obs_groups"], sets)
+        alg_cfg = resolve_symmetry_config(resolve_rnd_config(alg_cfg, obs, cfg["obs_groups"], env), env)
         actor_class, actor_cfg = resolve_class(cfg["actor"])
         critic_class, critic_cfg = resolve_class(cfg["critic"])
-        default_sets = ["actor", "critic"]
-        if alg_cfg.get("rnd_cfg") is not None:
-            default_sets.append("rnd_state")
-        cfg["obs_groups"] = resolve_obs_groups(obs, cfg["obs_groups"], default_sets)
-        alg_cfg = resolve_rnd_config(alg_cfg, obs, cfg["obs_groups"], env)
-        alg_cfg = resolve_symmetry_config(alg_cfg, env)
         actor = actor_class(obs, cfg["obs_groups"], "actor", env.num_actions, **actor_cfg).to(device)
         print(f"Actor Model: {actor}")
         if alg_cfg.pop("share_cnn_encoders", None):
@@ -394,30 +418,33 @@ class PPO:
         critic = critic_class(obs, cfg["obs_groups"], "critic", 1, **critic_cfg).to(device)
         print(f"Critic Model: {critic}")
         b200 = resolve_b200_cfg(alg_cfg.get("b200_cfg"))
-        # The fused engine keeps its own device rollout arena; the PyTorch storage is only allocated when needed.
-        storage = None
-        if not _engine_will_run(b200, device, actor, critic, alg_cfg):
-            storage = RolloutStorage("rl", env.num_envs, cfg["num_steps_per_env"], obs, [env.num_actions], device)
-        alg = alg_class(actor, critic, storage, device=device, **alg_cfg, multi_gpu_cfg=cfg["multi_gpu"],
-                        num_steps_per_env=cfg["num_steps_per_env"], num_envs=env.num_envs, obs_template=obs)
+        T = cfg["num_steps_per_env"]
+
+        def storage():
+            return RolloutStorage("rl", env.num_envs, T, obs, [env.num_actions], device)
+
+        # the fused engine keeps its own device rollout arena: the PyTorch storage exists only when it is used
+        alg = alg_class(actor, critic, None if _engine_will_run(b200, device, actor, critic, alg_cfg) else storage(),
+                        device=device, **alg_cfg, multi_gpu_cfg=cfg["multi_gpu"], num_steps_per_env=T,
+                        num_envs=env.num_envs, obs_template=obs)
         if alg.engine is None and alg.storage is None:
-            alg.storage = RolloutStorage("rl", env.num_envs, cfg["num_steps_per_env"], obs, [env.num_actions], device)
+            alg.storage = storage()
         alg.compile(cfg.get("torch_compile_mode"))
         return alg
 
     # ---- data parallel ----------------------------------------------------------------------------------------------------
     def broadcast_parameters(self) -> None:
+        """Every rank starts from rank 0's models (and RND networks)."""
         if self.engine is not None:
             self.engine.broadcast_parameters()
             return
-        models = [self._raw_actor, self._raw_critic]
-        if self.rnd:
-            models += [self.rnd.predictor, self.rnd.target]
+        models = [self._raw_actor, self._raw_critic] + ([self.rnd.predictor, self.rnd.target] if self.rnd else [])
         for model in models:
             for tensor in model.state_dict().values():
                 torch.distributed.broadcast(tensor, src=0)
 
     def reduce_parameters(self) -> None:
+        """Average every trained parameter's gradient over the ranks (bucketed all-reduce)."""
         params = chain(self.actor.parameters(), self.critic.parameters())
         if self.rnd:
             params = chain(params, self.rnd.parameters())
