@@ -1,5 +1,7 @@
 """Bounded device-side waits: a peer flag that nothing sets makes the kernel give up, record the failing site in the
-status word and leave the parameters untouched. Both "ranks" live on one GPU; nothing faults, traps or hangs."""
+status word and leave the parameters untouched. Both "ranks" live on one GPU; nothing faults, traps or hangs. The
+two-shot exchange is also run to completion on one GPU, with the second rank's part (its flags and its averaged
+shard) prepared by the test, and compared with the PyTorch definition of the step."""
 
 import pytest
 import torch
@@ -32,7 +34,7 @@ def test_adam_exchange_times_out_on_missing_peer():
     C.adam_step(flat, send, send, grads, m, v, tens, chunks, nch, [1.0], [0.9], [0.999], [1e-8], [0], lr, None, step,
                 False, None, 0.01, 1e-5, 1e-2, 2, 0, peer_send, peer_flags, epoch, 200 * 10**6,
                 torch.zeros(grid * 4, device=dev), torch.zeros(4, dtype=torch.int32, device=dev), status, None, grid,
-                [0, n], n + 4)
+                [0, n], n + 4, None, -1)
     torch.cuda.synchronize()
     st = status.tolist()
     assert st[0] == 4  # peer-flag timeout
@@ -80,3 +82,81 @@ def test_small_collective_completes_when_peer_flag_is_set():
     assert status[0].item() == 0
     assert torch.equal(out, buf0 + buf1)
     assert int(epoch) == 2
+
+
+def _two_shot_setup(n=1000, seed=0):
+    from tt_rsl_rl_b200.ops import ext
+
+    C = ext()
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n_ex = (n + 4 + 3) // 4 * 4
+    s0 = torch.randn(n_ex, device=dev, generator=g) * 0.1  # rank 0's gradients (this process)
+    s1 = torch.randn(n_ex, device=dev, generator=g) * 0.1  # "rank 1"'s gradients
+    red0 = torch.zeros(n_ex + 8, device=dev)
+    red1 = torch.zeros(n_ex + 8, device=dev)
+    flat = torch.randn(n, device=dev, generator=g)
+    tens, chunks, nch = C.make_adam_plan([0, n], [n, 4], [0, -1], [1, 1], [n, 4], [None, None], [0, 0], flat)
+    grid = C.adam_grid(torch.cuda.current_device())
+    return C, dev, n, n_ex, s0, s1, red0, red1, flat, tens, chunks, nch, grid
+
+
+def _two_shot_call(C, dev, n, n_ex, s0, s1, red0, red1, flat, tens, chunks, nch, grid, flags0, flags1, timeout_ns,
+                   max_norm=0.5):
+    m = torch.zeros(n, device=dev)
+    v = torch.zeros(n, device=dev)
+    grads = torch.zeros(n_ex, device=dev)
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+    lr = torch.tensor([1e-3], device=dev)
+    step = torch.zeros(1, dtype=torch.int64, device=dev)
+    # parity (epoch 1) & 1 = 1 selects the second half of the send table: [s0, s1]
+    peer_send = torch.tensor([s0.data_ptr(), s1.data_ptr()] * 2, dtype=torch.int64, device=dev)
+    peer_flags = torch.tensor([flags0.data_ptr(), flags1.data_ptr()], dtype=torch.int64, device=dev)
+    peer_reduced = torch.tensor([red0.data_ptr(), red1.data_ptr()], dtype=torch.int64, device=dev)
+    C.adam_step(flat, s0, s0, grads, m, v, tens, chunks, nch, [max_norm], [0.9], [0.999], [1e-8], [0], lr, None, step,
+                False, None, 0.01, 1e-5, 1e-2, 2, 0, peer_send, peer_flags, epoch, timeout_ns,
+                torch.zeros(grid * 4, device=dev), torch.zeros(4, dtype=torch.int32, device=dev), status, None, grid,
+                [0, n], n_ex, peer_reduced, -1)
+    torch.cuda.synchronize()
+    return status, grads, m, v, epoch
+
+
+def test_two_shot_exchange_times_out_on_missing_peer():
+    C, dev, n, n_ex, s0, s1, red0, red1, flat, tens, chunks, nch, grid = _two_shot_setup()
+    before = flat.clone()
+    flags0 = torch.zeros(2, dtype=torch.int32, device=dev)  # slot 1 ("rank 1") never written
+    flags1 = torch.zeros(2, dtype=torch.int32, device=dev)
+    status, *_ = _two_shot_call(C, dev, n, n_ex, s0, s1, red0, red1, flat, tens, chunks, nch, grid, flags0, flags1,
+                                200 * 10**6)
+    assert status[0].item() == 4 and status[1].item() == 61  # round 1, waiting for rank 1
+    assert torch.equal(flat, before)
+    assert int(flags1[0]) == 2  # round 1 of exchange 1 was published to the peer
+
+
+def test_two_shot_exchange_matches_the_torch_step():
+    """Rank 0 of a two-rank two-shot exchange on one GPU: rank 1's flags (2 e, 2 e + 1) and its averaged shard with
+    its squared-norm slot are prepared as rank 1 would have written them."""
+    C, dev, n, n_ex, s0, s1, red0, red1, flat, tens, chunks, nch, grid = _two_shot_setup()
+    before = flat.clone()
+    avg = (s0 + s1) * 0.5  # rank-ordered sum, then the 1 / world factor: the kernel's arithmetic
+    n4 = n_ex // 4
+    shard = (n4 + 1) // 2 * 4  # elements of rank 0's shard
+    red1[shard:n_ex] = avg[shard:]
+    red1[n_ex] = avg[shard:n].square().sum()  # rank 1's group-0 squared norm (parameters only)
+    flags0 = torch.tensor([0, 3], dtype=torch.int32, device=dev)  # rank 1 passed rounds 1 and 2 of exchange 1
+    flags1 = torch.zeros(2, dtype=torch.int32, device=dev)
+    status, grads, m, v, epoch = _two_shot_call(C, dev, n, n_ex, s0, s1, red0, red1, flat, tens, chunks, nch, grid,
+                                                flags0, flags1, 10**9)
+    assert status.tolist() == [0, 0, 0, 0]
+    assert int(epoch) == 1 and int(flags1[0]) == 3  # both rounds published to the peer
+    assert torch.equal(red0[:shard], avg[:shard])  # the own shard, averaged in rank order
+    torch.testing.assert_close(red0[n_ex], avg[:min(shard, n)].square().sum(), rtol=1e-5, atol=1e-7)
+    assert torch.equal(grads[:n_ex], avg)  # every element's average, read from its owner
+    # the PyTorch definition: clip the averaged gradient to norm 0.5, one Adam step
+    p = torch.nn.Parameter(before.clone())
+    p.grad = avg[:n].clone()
+    torch.nn.utils.clip_grad_norm_([p], 0.5)
+    opt = torch.optim.Adam([p], lr=1e-3)
+    opt.step()
+    torch.testing.assert_close(flat, p.detach(), rtol=1e-6, atol=1e-7)

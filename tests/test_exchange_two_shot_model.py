@@ -1,19 +1,22 @@
-"""Host model of a two-shot gradient exchange (reduce-scatter, Adam on a shard, all-gather of the parameters), with
-threads as ranks: the protocol planned for the fused Adam kernel at 4-8 GPUs, where the one-shot exchange reads
-(N - 1) full gradient vectors per rank and the two-shot moves 2 (N - 1) / N of one.
+"""Host model of the two-shot gradient exchange of the fused Adam kernel (``adam_two_shot`` in
+``ops/csrc/rl_kernels.cu``), with threads as ranks.
 
-Per step, with one send buffer, one norm slot and one parameter buffer per rank:
+Per exchange ``e`` (epoch), with two send buffers per rank (alternating by parity), one reduced buffer per rank (the
+averaged shard followed by the squared-norm slot) and one flag array per rank:
 
-1. write this step's gradients into the send buffer, publish flag 1, wait for flag 1 of every rank;
-2. sum the own shard over all ranks in rank order, divide by N; square-sum per clip group into the own norm slot;
-   publish flag 2, wait for flag 2 of every rank;
-3. read every rank's norm slot in rank order (the same global norms on every rank), clip, adaptive learning rate,
-   Adam on the own shard (moments are sharded);
-4. store the updated shard into every rank's parameter buffer, publish flag 3, wait for flag 3 of every rank.
+1. write this step's gradients into send buffer ``e % 2``; publish ``2 e`` (round 1) into every rank's flag array and
+   wait until every slot of the own array holds at least ``2 e``;
+2. average the own shard over all ranks in rank order into the reduced buffer, with its squared norm in the slot;
+   publish ``2 e + 1`` (round 2) and wait for it from every rank;
+3. sum the ranks' norm slots in rank order (the same global norm on every rank), clip, and apply Adam to the whole
+   vector with each element's average read from the rank that owns its shard (parameters and moments replicated).
 
-The model checks that the three flag rounds make one buffer of each kind safe (no rank overwrites data a peer still
-reads), that every rank ends each step with bit-identical parameters, and that they equal the one-shot result up to
-the summation order of the norms.
+The model checks that two rounds make a single reduced buffer safe: a rank rewrites its reduced buffer only in step 2
+of exchange ``e + 1``, after round 1 of ``e + 1``, which every rank publishes only once it has finished reading the
+reduced buffers of exchange ``e``; that without round 2 a rank can read a shard its owner has not averaged yet; that
+replicas are bit-identical every step; and that the result equals the one-shot exchange up to the summation order of
+the norm. (The send buffers alternate by parity as the one-shot exchange needs; in the two-round protocol a rank reads
+peers' send buffers only before it publishes round 2, so even one buffer would be safe there.)
 """
 
 import threading
@@ -22,7 +25,7 @@ import time
 import numpy as np
 import pytest
 
-P = 96  # parameters (divisible by every world size tested)
+P = 96  # parameters (the shards are ceil(P / W) long, the last one shorter)
 LR, B1, B2, EPS, MAX_NORM = 1e-2, 0.9, 0.999, 1e-8, 0.5
 
 
@@ -32,29 +35,38 @@ def grads(rank: int, step: int) -> np.ndarray:
 
 
 class Fabric:
-    def __init__(self, world: int) -> None:
+    def __init__(self, world: int, send_buffers: int = 2) -> None:
         self.world = world
-        self.send = [np.zeros(P, np.float32) for _ in range(world)]
-        self.norm = [np.zeros(1, np.float32) for _ in range(world)]
-        self.params = [np.ones(P, np.float32) for _ in range(world)]
-        self.flags = [[[0] * world for _ in range(world)] for _ in range(3)]  # flags[k][dst][src]
+        self.nsend = send_buffers
+        self.send = [[np.zeros(P, np.float32) for _ in range(send_buffers)] for _ in range(world)]
+        self.reduced = [np.zeros(P + 1, np.float32) for _ in range(world)]  # shard values + norm slot at [P]
+        self.flags = [[0] * world for _ in range(world)]  # flags[dst][src]
         self.lock = threading.Lock()
         self.violations = []
 
-    def publish(self, k: int, rank: int, epoch: int) -> None:
+    def publish(self, rank: int, value: int) -> None:
         with self.lock:
             for r in range(self.world):
-                self.flags[k][r][rank] = epoch
+                self.flags[r][rank] = value
 
-    def wait(self, k: int, rank: int, epoch: int, timeout_s: float = 10.0) -> None:
+    def wait(self, rank: int, value: int, timeout_s: float = 10.0) -> None:
         t0 = time.monotonic()
         while True:
             with self.lock:
-                if all(f >= epoch for f in self.flags[k][rank]):
+                if all(f >= value for f in self.flags[rank]):
                     return
             if time.monotonic() - t0 > timeout_s:
-                raise TimeoutError(f"rank {rank} flag {k + 1} epoch {epoch}")
+                raise TimeoutError(f"rank {rank} waits for {value}")
             time.sleep(1e-4)
+
+
+def shard_bounds(world: int, rank: int) -> tuple[int, int]:
+    size = -(-P // world)
+    return min(P, rank * size), min(P, (rank + 1) * size)
+
+
+def owner(world: int, e: int) -> int:
+    return e // -(-P // world)
 
 
 def adam(p, g, m, v, step):
@@ -64,44 +76,46 @@ def adam(p, g, m, v, step):
     p -= np.float32(LR / bc1) * m / (np.sqrt(v) / np.float32(np.sqrt(bc2)) + np.float32(EPS))
 
 
-def two_shot_rank(fab: Fabric, rank: int, steps: int, out: dict, jitter, rounds: int = 3, before_store=None) -> None:
+def two_shot_rank(fab: Fabric, rank: int, steps: int, out: dict, jitter, round2: bool = True) -> None:
     W = fab.world
-    lo, hi = rank * P // W, (rank + 1) * P // W
-    m, v = np.zeros(hi - lo, np.float32), np.zeros(hi - lo, np.float32)
+    lo, hi = shard_bounds(W, rank)
+    p = np.ones(P, np.float32)
+    m, v = np.zeros(P, np.float32), np.zeros(P, np.float32)
     try:
         for step in range(steps):
             epoch = step + 1
-            fab.send[rank][:] = grads(rank, step)
-            fab.publish(0, rank, epoch)
-            fab.wait(0, rank, epoch)
+            send = fab.send[rank][epoch % fab.nsend]
+            send[:] = grads(rank, step)
+            fab.publish(rank, 2 * epoch)
+            fab.wait(rank, 2 * epoch)
             jitter()
             shard = np.zeros(hi - lo, np.float32)
-            for r in range(W):
-                got = fab.send[r][lo:hi].copy()
+            for r in range(W):  # rank order
+                got = fab.send[r][epoch % fab.nsend][lo:hi].copy()
                 if not np.array_equal(got, grads(r, step)[lo:hi]):
                     fab.violations.append(("send", rank, r, step))
                 shard += got
                 jitter()
             shard /= np.float32(W)
-            fab.norm[rank][0] = np.float32(np.sum(shard * shard, dtype=np.float32))
-            fab.publish(1, rank, epoch)
-            fab.wait(1, rank, epoch)
+            fab.reduced[rank][lo:hi] = shard
+            fab.reduced[rank][P] = np.float32(np.sum(shard * shard, dtype=np.float32))
+            fab.publish(rank, 2 * epoch + 1)
+            if round2:
+                fab.wait(rank, 2 * epoch + 1)
             total = np.float32(0.0)
             for r in range(W):
-                total += fab.norm[r][0]
+                total += fab.reduced[r][P]
                 jitter()
             coef = min(np.float32(MAX_NORM) / (np.sqrt(total) + np.float32(1e-6)), np.float32(1.0))
-            p = fab.params[rank][lo:hi].copy()
-            adam(p, shard * coef, m, v, epoch)
-            if before_store is not None:
-                before_store(rank, step)
-            for r in range(W):
-                fab.params[r][lo:hi] = p
-                jitter()
-            if rounds == 3:
-                fab.publish(2, rank, epoch)
-                fab.wait(2, rank, epoch)
-            out.setdefault(rank, []).append(fab.params[rank].copy())
+            g = np.empty(P, np.float32)
+            for e in range(P):
+                g[e] = fab.reduced[owner(W, e)][e]
+            jitter()
+            expect = np.mean(np.stack([grads(r, step) for r in range(W)]), axis=0)
+            if not np.allclose(g, expect, rtol=1e-5, atol=1e-6):
+                fab.violations.append(("reduced", rank, step))
+            adam(p, g * coef, m, v, epoch)
+            out.setdefault(rank, []).append(p.copy())
     except Exception as exc:  # reported to the test
         out[rank] = exc
 
@@ -122,23 +136,32 @@ def one_shot(world: int, steps: int) -> list[np.ndarray]:
     return hist
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_two_shot_protocol_is_race_free_and_replicas_match(world):
+def _run(world: int, steps: int, jitter, round2: bool = True):
     fab = Fabric(world)
-    rng = np.random.default_rng(world)
-    lock = threading.Lock()
-
-    def jitter():
-        with lock:
-            d = rng.uniform(0, 4e-4)
-        time.sleep(d)
-
-    out, steps = {}, 12
-    threads = [threading.Thread(target=two_shot_rank, args=(fab, r, steps, out, jitter)) for r in range(world)]
+    out = {}
+    threads = [threading.Thread(target=two_shot_rank, args=(fab, r, steps, out, jitter(r), round2))
+               for r in range(world)]
     for t in threads:
         t.start()
     for t in threads:
         t.join(timeout=120)
+    return fab, out
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_two_shot_protocol_is_race_free_and_replicas_match(world):
+    rng = np.random.default_rng(world)
+    lock = threading.Lock()
+
+    def jitter(rank):
+        def f():
+            with lock:
+                d = rng.uniform(0, 4e-4)
+            time.sleep(d)
+        return f
+
+    steps = 12
+    fab, out = _run(world, steps, jitter)
     errors = {r: v for r, v in out.items() if isinstance(v, Exception)}
     assert not errors and not fab.violations, (errors, fab.violations[:5])
     for step in range(steps):
@@ -149,21 +172,13 @@ def test_two_shot_protocol_is_race_free_and_replicas_match(world):
         np.testing.assert_allclose(out[0][step], ref[step], rtol=2e-5, atol=2e-6)
 
 
-@pytest.mark.parametrize("rounds,identical", [(3, True), (2, False)])
-def test_the_third_flag_round_is_what_keeps_parameters_complete(rounds, identical):
-    """Rank 0 is slow to store its updated shard: without the third flag round rank 1 goes on with stale
-    parameters."""
-    fab = Fabric(2)
-    out = {}
+@pytest.mark.parametrize("round2,safe", [(True, True), (False, False)])
+def test_round_two_is_what_makes_the_owners_shards_complete(round2, safe):
+    """Rank 0 averages its shard slowly: without waiting for round 2, rank 1 reads rank 0's shard before it is
+    written (stale values from the previous exchange)."""
 
-    def slow_store(rank, step):
-        if rank == 0 and step == 0:
-            time.sleep(0.05)
+    def jitter(rank):
+        return (lambda: time.sleep(2e-3)) if rank == 0 else (lambda: None)
 
-    threads = [threading.Thread(target=two_shot_rank, args=(fab, r, 1, out, lambda: None, rounds, slow_store))
-               for r in range(2)]
-    for t in threads:
-        t.start()
-    for t in threads:
-        t.join(timeout=60)
-    assert np.array_equal(out[0][0], out[1][0]) == identical
+    fab, out = _run(2, 4, jitter, round2)
+    assert (not fab.violations) == safe

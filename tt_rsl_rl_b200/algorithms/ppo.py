@@ -30,6 +30,7 @@ B200_CFG_DEFAULTS = {
     "graphs": True,  # capture act / GAE / minibatch steps in CUDA graphs
     "replica_check_interval": 0,  # >0: every k updates verify that all ranks hold bit-identical parameters
     "comm_timeout_ms": 10000,  # device-side wait limit of the peer-to-peer gradient exchange
+    "exchange": "auto",  # gradient exchange: "one_shot", "two_shot", or "auto" (two-shot from 4 ranks on)
     "gemm_dtype": "bf16",  # GEMM operand precision of the fused path ("bf16")
     "section_timing": False,  # time rollout / returns / update with CUDA events (Perf/section_*) and NVTX ranges
 }
@@ -41,7 +42,17 @@ def resolve_b200_cfg(cfg: dict | None) -> dict:
         if k not in B200_CFG_DEFAULTS:
             raise ValueError(f"Unknown b200_cfg key '{k}'. Valid keys: {list(B200_CFG_DEFAULTS)}")
         out[k] = v
+    if out["exchange"] not in ("auto", "one_shot", "two_shot"):
+        raise ValueError(f"b200_cfg.exchange must be 'auto', 'one_shot' or 'two_shot', got {out['exchange']!r}")
     return out
+
+
+def use_two_shot(b200_cfg: dict, world: int) -> bool:
+    """Whether the fused optimizer exchanges gradients in two shots (reduce-scatter, then every rank reads each
+    element's average from its owner) instead of one (every rank sums every element): fewer peer bytes per rank,
+    2 (W - 1) / W instead of W - 1 vectors, for one more flag round."""
+    mode = b200_cfg["exchange"]
+    return world > 1 and (mode == "two_shot" or (mode == "auto" and world >= 4))
 
 
 # ---- the PPO objective and schedules as functions (the PyTorch path's definition; the fused kernels evaluate the same

@@ -103,6 +103,8 @@ class DistillationEngine(EngineBase):
         self.rank = alg.gpu_global_rank
         self.timeout_ns = int(alg.b200_cfg["comm_timeout_ms"] * 1e6)
         self.comm = None
+        self._peer_reduced = None  # set for the two-shot exchange
+        self._kl_offset = -1  # index of the KL statistic in the exchanged vector
         if self.world > 1:
             from ..parallel import PeerExchange
 
@@ -110,6 +112,12 @@ class DistillationEngine(EngineBase):
             small = max(4 * self.n_params, 4 * t_max, 8 * (2 + 2 * self.Ds), 4096)
             self.comm = PeerExchange.create(self.n_ex, small, rank=self.rank, world=self.world, device=dev,
                                             timeout_ms=alg.b200_cfg["comm_timeout_ms"])
+            from ..algorithms.ppo import use_two_shot
+
+            # two-shot exchange: the ranks' reduced buffers; the KL statistic is read from its owner's shard
+            if use_two_shot(alg.b200_cfg, self.world):
+                self._peer_reduced = self.comm.peer_reduced
+
             self.send = self.comm.send
         else:
             buf = torch.zeros(self.n_ex, **f32)
@@ -261,7 +269,8 @@ class DistillationEngine(EngineBase):
                         self.adam_tensors, self.adam_chunks, self.adam_nchunks, [max_norm], [self.betas[0]],
                         [self.betas[1]], [self.adam_eps], [0], self.lr, None, self.step, False, None, 0.0, 0.0, 0.0,
                         self.world, self.rank, peers, flags, self.epoch, self.timeout_ns, self.norm_partial,
-                        self.barrier, self.status, None, self.adam_grid, [0, self.n_params], self.n_ex)
+                        self.barrier, self.status, None, self.adam_grid, [0, self.n_params], self.n_ex,
+                        self._peer_reduced, self._kl_offset)
 
     def _update_body(self) -> None:
         self.loss_acc.zero_()

@@ -220,6 +220,8 @@ class PPOEngine(EngineBase):
         self.rank = alg.gpu_global_rank
         self.timeout_ns = int(alg.b200_cfg["comm_timeout_ms"] * 1e6)
         self.comm = None
+        self._peer_reduced = None  # set for the two-shot exchange
+        self._kl_offset = self.n_params + 3  # index of the KL statistic in the exchanged vector
         if self.world > 1:
             from ..parallel import PeerExchange
 
@@ -228,6 +230,12 @@ class PPOEngine(EngineBase):
             small = max(4 * self.n_params, 4 * big, 8 * (2 + 2 * dmax), 4096)
             self.comm = PeerExchange.create(n_ex, small, rank=self.rank, world=self.world, device=dev,
                                             timeout_ms=alg.b200_cfg["comm_timeout_ms"])
+            from ..algorithms.ppo import use_two_shot
+
+            # two-shot exchange: the ranks' reduced buffers; the KL statistic is read from its owner's shard
+            if use_two_shot(alg.b200_cfg, self.world):
+                self._peer_reduced = self.comm.peer_reduced
+
             self.send = self.comm.send
         else:
             buf = torch.zeros(n_ex, **f32)
@@ -616,7 +624,7 @@ class PPOEngine(EngineBase):
                     self.adam_beta2, self.adam_eps_g, self.adam_lr_index, self.lr, None, self.step, adaptive, kl,
                     float(alg.desired_kl or 0.0), 1e-5, 1e-2, self.world, self.rank, peers, flags, self.epoch,
                     self.timeout_ns, self.norm_partial, self.barrier, self.status, self.out_norms, self.adam_grid,
-                    self.group_ranges, self.n_ex)
+                    self.group_ranges, self.n_ex, self._peer_reduced, self._kl_offset)
         self.loss_acc.add_(self.grads[self.n_params : self.n_params + _TAIL])
 
     def _normalizer_updates(self) -> None:

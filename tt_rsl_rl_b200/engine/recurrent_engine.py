@@ -294,12 +294,20 @@ class RecurrentPPOEngine(EngineBase):
         self.world, self.rank = alg.gpu_world_size, alg.gpu_global_rank
         self.timeout_ns = int(alg.b200_cfg["comm_timeout_ms"] * 1e6)
         self.comm = None
+        self._peer_reduced = None  # set for the two-shot exchange
+        self._kl_offset = self.n_params + 3  # index of the KL statistic in the exchanged vector
         if self.world > 1:
             from ..parallel import PeerExchange
 
             small = max(4 * self.n_params, 8 * (2 + 2 * max(self.Da, self.Dc)), 4096)
             self.comm = PeerExchange.create(self.n_ex, small, rank=self.rank, world=self.world, device=dev,
                                             timeout_ms=alg.b200_cfg["comm_timeout_ms"])
+            from ..algorithms.ppo import use_two_shot
+
+            # two-shot exchange: the ranks' reduced buffers; the KL statistic is read from its owner's shard
+            if use_two_shot(alg.b200_cfg, self.world):
+                self._peer_reduced = self.comm.peer_reduced
+
             self.send = self.comm.send
         else:
             buf = torch.zeros(self.n_ex, **f32)
@@ -537,7 +545,7 @@ class RecurrentPPOEngine(EngineBase):
                     [self.betas[0]] * 2, [self.betas[1]] * 2, [self.adam_eps] * 2, [0, 0], self.lr, None, self.step,
                     adaptive, kl, float(alg.desired_kl or 0.0), 1e-5, 1e-2, self.world, self.rank, peers, flags,
                     self.epoch, self.timeout_ns, self.norm_partial, self.barrier, self.status, None, self.adam_grid,
-                    self.group_ranges, self.n_ex)
+                    self.group_ranges, self.n_ex, self._peer_reduced, self._kl_offset)
         self.loss_acc.add_(self.grads[self.n_params : self.n_params + _TAIL])
 
     def _update_body(self) -> None:

@@ -517,7 +517,8 @@ void adam_step(const Tensor& params, const Tensor& send0, const Tensor& send1, c
                bool adaptive, const OptT& kl_mean, double desired_kl, double lr_min, double lr_max, int64_t world,
                int64_t rank, const OptT& peer_send, const OptT& peer_flags, const Tensor& epoch, int64_t timeout_ns,
                const Tensor& norm_partial, const Tensor& barrier, const OptT& status, const OptT& out_norms,
-               int64_t grid, const std::vector<int64_t>& group_ranges, int64_t exchange_len) {
+               int64_t grid, const std::vector<int64_t>& group_ranges, int64_t exchange_len,
+               const OptT& peer_reduced, int64_t kl_offset) {
   for (const Tensor* t : {&params, &send0, &send1, &grads, &exp_avg, &exp_avg_sq}) check_f32(*t, "adam buffer");
   const size_t ng = max_norm.size();
   TORCH_CHECK(ng >= 1 && ng <= rlb::kAdamMaxGroups && beta1.size() == ng && beta2.size() == ng && eps.size() == ng,
@@ -581,6 +582,21 @@ void adam_step(const Tensor& params, const Tensor& send0, const Tensor& send1, c
               "adam_step: exchange buffers must be 16-byte aligned");
   TORCH_CHECK(world <= 8, "adam_step: at most 8 ranks");
   a.exchange_len = exchange_len;
+  // two-shot exchange: peer table of the ranks' reduced buffers (exchange_len + 8 floats each), shards of
+  // ceil(n4 / world) float4 elements, the KL statistic read from its owner
+  a.peer_reduced = nullptr;
+  a.shard4 = 0;
+  a.kl_offset = -1;
+  if (peer_reduced.has_value() && peer_reduced->defined() && world > 1) {
+    TORCH_CHECK(peer_reduced->numel() >= world && peer_reduced->scalar_type() == torch::kInt64,
+                "adam_step: peer_reduced must hold one int64 device pointer per rank");
+    TORCH_CHECK(!adaptive || (kl_offset >= 0 && kl_offset < exchange_len),
+                "adam_step: the two-shot exchange with an adaptive schedule needs the KL statistic's offset");
+    a.peer_reduced = P<float* const>(peer_reduced);
+    const long long n4 = exchange_len / 4;
+    a.shard4 = (n4 + world - 1) / world;
+    a.kl_offset = kl_offset;
+  }
   ok(rlb::adam_step(a, static_cast<int>(grid), cur()), "adam_step");
 }
 

@@ -1041,154 +1041,69 @@ __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) 
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Threads r < world wait, in parallel, until slot r of this rank's flag array reaches `target` (a bounded wait);
+// returns false in every thread of the block if one slot did not arrive in time (site + r recorded).
+__device__ bool await_peer_flags(const unsigned int* my_flags, int world, unsigned int target, uint64_t timeout_ns,
+                                 unsigned int* status, int site, unsigned int* abort_word, unsigned int abort_tag) {
+  __shared__ int all_arrived;
+  if (threadIdx.x == 0) all_arrived = 1;
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const uint64_t t0 = globaltimer_ns();
+    while (static_cast<int>(ld_acquire_sys(my_flags + threadIdx.x) - target) < 0) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        report_error(status, kTimeoutPeerFlag, site + threadIdx.x);
+        all_arrived = 0;
+        atomicExch(abort_word, abort_tag);  // grid-wide abort of this exchange (tagged with the epoch)
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+  return all_arrived != 0;
+}
+
+// Thread r < world of the calling block stores `value` into slot `rank` of rank r's flag array (release).
+__device__ __forceinline__ void publish_flag(unsigned int* const* peer_flags, int world, int rank, unsigned int value) {
+  if (threadIdx.x < world) {
+    __threadfence_system();
+    st_release_sys(peer_flags[threadIdx.x] + rank, value);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Fused exchange + clip + adaptive LR + Adam
-// Phase 0 (world > 1): block 0 publishes this rank's epoch flag to every peer, then waits for every peer's flag.
-// Phase 1: each block sums its chunks' gradients over ranks in rank order (bit-identical on every rank), divides by
-//          the world size, writes the averaged gradient locally and accumulates per-group squared norms.
-// Phase 2 (after a grid barrier): every block reduces the norm partials in the same order, derives the clip
-//          coefficients and the adapted learning rate, and applies Adam to its chunks.
+// One-shot (world 2, or forced): every block publishes/awaits the epoch flags, then sums every element's gradient over
+//          all ranks in rank order (bit-identical on every rank), divides by the world size, accumulates per-group
+//          squared norms; after a grid barrier every block reduces the norm partials in the same order.
+// Two-shot (world >= 2 with peer_reduced): flag round 1 (gradients sent), each rank averages only its own shard of
+//          the vector over all ranks into its reduced buffer with the shard's squared norms; the last block to finish
+//          sums the blocks' norm partials into the rank's norm slots and publishes flag round 2 (shard averaged);
+//          after round 2 every rank sums the ranks' norm slots in rank order and reads each element's average from
+//          its owner while it applies Adam. Peer bytes per rank: 2 (W - 1) / W of the vector instead of (W - 1).
+// Both: the clip coefficients, the adapted learning rate and Adam follow; bf16 weight shadows are refreshed.
+// Every flag wait is bounded; the ranks' flags are polled in parallel (one thread per rank).
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kAdamThreads = 256;
 constexpr int kMaxWorldAdam = 8;
 
-__global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs a) {
-  __shared__ float red[kAdamThreads / 32][kAdamMaxGroups];
-  __shared__ float coef[kAdamMaxGroups];
-  __shared__ float lr_s[kAdamMaxGroups];
-  __shared__ long long step_s[kAdamMaxGroups];
-  __shared__ int peers_ok;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-  __shared__ unsigned int epoch_s;
-  __shared__ float lr_old[kAdamMaxGroups];
-  // Everything block 0 rewrites at the end (step, learning rates, epoch) is read here, before the grid barrier.
-  if (threadIdx.x == 0) {
-    peers_ok = 1;
-    for (int g = 0; g < a.ngroups; ++g) {
-      step_s[g] = a.step[g];
-      lr_old[g] = a.lr[g];
-    }
-    epoch_s = *a.epoch + 1u;
-  }
-  __syncthreads();
-  const unsigned int epoch = epoch_s;
-  // ---- phase 0: flags ----
-  if (a.world > 1) {
-    if (blockIdx.x == 0 && threadIdx.x < a.world) {
-      // publish: this rank's slot in every peer's flag array (release orders our gradient writes before the flag)
-      __threadfence_system();
-      st_release_sys(a.peer_flags[threadIdx.x] + a.rank, epoch);
-    }
-    if (threadIdx.x == 0) {
-      const uint64_t t0 = globaltimer_ns();
-      const unsigned int* my_flags = a.peer_flags[a.rank];
-      for (int r = 0; r < a.world; ++r) {
-        while (static_cast<int>(ld_acquire_sys(my_flags + r) - epoch) < 0) {
-          if (globaltimer_ns() - t0 > a.timeout_ns) {
-            report_error(a.status, kTimeoutPeerFlag, 60 + r);
-            peers_ok = 0;
-            atomicExch(a.barrier + 2, epoch);  // grid-wide abort of this exchange (tagged with the epoch)
-            break;
-          }
-          __nanosleep(32);
-        }
-        if (!peers_ok) break;
-      }
-    }
-  }
-  __syncthreads();
-  const bool exchange_ok = peers_ok != 0;
-
-  // ---- phase 1: rank-ordered sum, squared norms ----
-  // float4 grid-stride over the whole exchanged vector; the peer loads of all ranks are issued before they are
-  // summed (in rank order, so every rank obtains the same bits)
-  float sq[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
-  const float inv_world = 1.0f / static_cast<float>(a.world);
-  const unsigned int parity = epoch & 1u;
-  const float4* mine4 = reinterpret_cast<const float4*>(a.send[parity]);
-  const long long n4 = a.exchange_len / 4;
-  for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < n4;
-       v += static_cast<long long>(gridDim.x) * blockDim.x) {
-    float4 g;
-    if (a.world > 1 && exchange_ok) {
-      float4 part[kMaxWorldAdam];
-#pragma unroll
-      for (int r = 0; r < kMaxWorldAdam; ++r)
-        if (r < a.world) part[r] = __ldcv(reinterpret_cast<const float4*>(a.peer_send[parity * a.world + r]) + v);
-      g = part[0];
-#pragma unroll
-      for (int r = 1; r < kMaxWorldAdam; ++r) {
-        if (r < a.world) {
-          g.x += part[r].x;
-          g.y += part[r].y;
-          g.z += part[r].z;
-          g.w += part[r].w;
-        }
-      }
-      g.x *= inv_world;
-      g.y *= inv_world;
-      g.z *= inv_world;
-      g.w *= inv_world;
-    } else {
-      g = mine4[v];
-    }
-    reinterpret_cast<float4*>(a.grads)[v] = g;
-    const long long e = 4 * v;
-    const float comp[4] = {g.x, g.y, g.z, g.w};
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-#pragma unroll
-      for (int gr = 0; gr < kAdamMaxGroups; ++gr)
-        if (gr < a.ngroups && e + c >= a.group_begin[gr] && e + c < a.group_end[gr]) sq[gr] += comp[c] * comp[c];
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < kAdamMaxGroups; ++g) {
-#pragma unroll
-    for (int off = 16; off; off >>= 1) sq[g] += __shfl_xor_sync(0xffffffffu, sq[g], off);
-  }
-  if (lane == 0)
-    for (int g = 0; g < kAdamMaxGroups; ++g) red[warp][g] = sq[g];
-  __syncthreads();
-  if (threadIdx.x < kAdamMaxGroups) {
-    float s = 0.f;
-    for (int w = 0; w < kAdamThreads / 32; ++w) s += red[w][threadIdx.x];
-    a.norm_partial[static_cast<size_t>(blockIdx.x) * kAdamMaxGroups + threadIdx.x] = s;
-  }
-  if (!grid_sync(a.barrier, a.status, a.timeout_ns)) return;
-  // every block takes the same decision: the exchange failed if any block's wait gave up
-  const bool all_ok = *reinterpret_cast<volatile unsigned int*>(a.barrier + 2) != epoch;
-
-  // ---- phase 2: norms, clip coefficients, learning rate ----
-  // every block reduces the per-block partials with all of its threads (fixed tree order: identical in every block)
-  {
-    float part[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
-    for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x) {
-#pragma unroll
-      for (int g = 0; g < kAdamMaxGroups; ++g) part[g] += a.norm_partial[static_cast<size_t>(b) * kAdamMaxGroups + g];
-    }
-#pragma unroll
-    for (int g = 0; g < kAdamMaxGroups; ++g) {
-#pragma unroll
-      for (int off = 16; off; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-    }
-    __syncthreads();  // red[] is reused
-    if (lane == 0)
-      for (int g = 0; g < kAdamMaxGroups; ++g) red[warp][g] = part[g];
-    __syncthreads();
-  }
+// Clip coefficients, adapted learning rate and Adam constants from the global squared norms `norm_sq` (identical in
+// every block and on every rank), then Adam over this block's chunks with the gradient of element e given by
+// grad_of(e). With `store_grads` the rank-averaged gradient is also written to a.grads (the two-shot path, where it
+// was not materialised locally). Block 0 finally advances the step counters, learning rates and the epoch.
+template <typename GradOf>
+__device__ void adam_apply(const AdamArgs& a, const float* norm_sq, float kl, unsigned int epoch,
+                           const long long* step_s, const float* lr_old, bool exchange_ok, bool store_grads,
+                           GradOf grad_of) {
+  __shared__ float coef[kAdamMaxGroups], lr_s[kAdamMaxGroups];
+  __shared__ float step_size_s[kAdamMaxGroups], bc2_sqrt_s[kAdamMaxGroups];
   if (threadIdx.x < a.ngroups) {
     const int g = threadIdx.x;
-    float s = 0.f;
-    for (int w = 0; w < kAdamThreads / 32; ++w) s += red[w][g];
-    const float norm = sqrtf(s);
-    float cf = 1.0f;
-    if (a.max_norm[g] > 0.f) cf = fminf(a.max_norm[g] / (norm + 1e-6f), 1.0f);
-    coef[g] = cf;
+    const float norm = sqrtf(norm_sq[g]);
+    coef[g] = a.max_norm[g] > 0.f ? fminf(a.max_norm[g] / (norm + 1e-6f), 1.0f) : 1.0f;
     float lr = lr_old[g];  // slot g
     if (g == 0 && a.adaptive) {
-      const float kl = *a.kl_mean;
       if (kl > a.desired_kl * 2.0f)
         lr = fmaxf(a.lr_min, lr / 1.5f);
       else if (kl < a.desired_kl / 2.0f && kl > 0.0f)
@@ -1198,12 +1113,11 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     if (blockIdx.x == 0 && a.out_norms) a.out_norms[g] = norm;
   }
   __syncthreads();
-  if (!all_ok) {  // leave parameters untouched when the exchange failed; the status word reports it
+  if (!exchange_ok) {  // leave parameters untouched when the exchange failed; the status word reports it
     if (blockIdx.x == 0 && threadIdx.x == 0) *a.epoch = epoch;
     return;
   }
-  // per-group Adam constants, once per block (bias corrections in double, as torch computes them on the host)
-  __shared__ float step_size_s[kAdamMaxGroups], bc2_sqrt_s[kAdamMaxGroups];
+  // per-group Adam constants (bias corrections in double, as torch computes them on the host)
   if (threadIdx.x < a.ngroups) {
     const int g = threadIdx.x;
     const double step = static_cast<double>(step_s[g] + 1);
@@ -1217,13 +1131,21 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     const AdamChunk ch = a.chunks[c];
     const AdamTensor T = a.tensors[ch.tensor];
     const int g = T.group;
-    if (g < 0) continue;  // exchanged statistics (e.g. the KL mean), not parameters
+    if (g < 0) {  // exchanged statistics (e.g. the KL mean), not parameters
+      if (store_grads)
+        for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
+          const long long e = T.offset + ch.start + k;
+          a.grads[e] = grad_of(e);
+        }
+      continue;
+    }
     const float step_size = step_size_s[g], bc2_sqrt = bc2_sqrt_s[g];
     const float b1 = a.beta1[g], b2 = a.beta2[g], eps = a.eps[g], cf = coef[g];
-    // chunks start on row boundaries of 2-D weights when cols divides the chunk; track (row, col) incrementally
     for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
       const long long e = T.offset + ch.start + k;
-      const float grad = a.grads[e] * cf;
+      const float raw = grad_of(e);
+      if (store_grads) a.grads[e] = raw;
+      const float grad = raw * cf;
       float m = a.exp_avg[e];
       m = m + (1.0f - b1) * (grad - m);
       const float v = b2 * a.exp_avg_sq[e] + (1.0f - b2) * grad * grad;
@@ -1249,6 +1171,195 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     }
   }
 }
+
+// Per-group squared norms of the float4 `g` of elements 4 v .. 4 v + 3, added into sq.
+__device__ __forceinline__ void add_group_squares(const AdamArgs& a, long long v, float4 g, float* sq) {
+  const long long e = 4 * v;
+  const float comp[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+#pragma unroll
+    for (int gr = 0; gr < kAdamMaxGroups; ++gr)
+      if (gr < a.ngroups && e + c >= a.group_begin[gr] && e + c < a.group_end[gr]) sq[gr] += comp[c] * comp[c];
+  }
+}
+
+// Block sum (fixed warp order) of the per-thread group squares into red[0..kAdamMaxGroups) of thread 0's view.
+__device__ __forceinline__ void block_group_sums(float* sq, float (*red)[kAdamMaxGroups]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int g = 0; g < kAdamMaxGroups; ++g) {
+#pragma unroll
+    for (int off = 16; off; off >>= 1) sq[g] += __shfl_xor_sync(0xffffffffu, sq[g], off);
+  }
+  __syncthreads();  // red[] may still be read by a previous use
+  if (lane == 0)
+    for (int g = 0; g < kAdamMaxGroups; ++g) red[warp][g] = sq[g];
+  __syncthreads();
+}
+
+__device__ __forceinline__ float4 rank_average(const AdamArgs& a, unsigned int parity, long long v, float inv_world) {
+  float4 part[kMaxWorldAdam];
+#pragma unroll
+  for (int r = 0; r < kMaxWorldAdam; ++r)  // every rank's loads in flight before the rank-ordered sum
+    if (r < a.world) part[r] = __ldcv(reinterpret_cast<const float4*>(a.peer_send[parity * a.world + r]) + v);
+  float4 g = part[0];
+#pragma unroll
+  for (int r = 1; r < kMaxWorldAdam; ++r) {
+    if (r < a.world) {
+      g.x += part[r].x;
+      g.y += part[r].y;
+      g.z += part[r].z;
+      g.w += part[r].w;
+    }
+  }
+  g.x *= inv_world;
+  g.y *= inv_world;
+  g.z *= inv_world;
+  g.w *= inv_world;
+  return g;
+}
+
+__device__ void adam_two_shot(const AdamArgs& a, unsigned int epoch, const long long* step_s, const float* lr_old) {
+  __shared__ float red[kAdamThreads / 32][kAdamMaxGroups];
+  __shared__ float norm_sq[kAdamMaxGroups];
+  __shared__ unsigned int ticket_s;
+  const unsigned int round1 = 2u * epoch, round2 = 2u * epoch + 1u;
+  // ---- round 1: this rank's gradients are in its send buffer ----
+  if (blockIdx.x == 0) publish_flag(a.peer_flags, a.world, a.rank, round1);
+  bool ok = await_peer_flags(a.peer_flags[a.rank], a.world, round1, a.timeout_ns, a.status, 60, a.barrier + 2, epoch);
+  // ---- reduce-scatter: the own shard, averaged over the ranks in rank order ----
+  float sq[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
+  const unsigned int parity = epoch & 1u;
+  const float inv_world = 1.0f / static_cast<float>(a.world);
+  const long long n4 = a.exchange_len / 4;
+  const long long v0 = static_cast<long long>(a.rank) * a.shard4;
+  const long long v1 = v0 + a.shard4 < n4 ? v0 + a.shard4 : n4;
+  float4* mine = reinterpret_cast<float4*>(a.peer_reduced[a.rank]);
+  if (ok) {
+    for (long long v = v0 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < v1;
+         v += static_cast<long long>(gridDim.x) * blockDim.x) {
+      const float4 g = rank_average(a, parity, v, inv_world);
+      mine[v] = g;
+      add_group_squares(a, v, g, sq);
+    }
+  }
+  block_group_sums(sq, red);
+  if (threadIdx.x < kAdamMaxGroups) {
+    float t = 0.f;
+    for (int w = 0; w < kAdamThreads / 32; ++w) t += red[w][threadIdx.x];
+    a.norm_partial[static_cast<size_t>(blockIdx.x) * kAdamMaxGroups + threadIdx.x] = t;
+  }
+  // the last block to finish sums the blocks' partials (block order) into this rank's norm slots and opens round 2
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) ticket_s = atomicAdd(a.barrier + 3, 1u);
+  __syncthreads();
+  if (ticket_s == gridDim.x - 1) {
+    __threadfence();
+    if (threadIdx.x < kAdamMaxGroups) {
+      float t = 0.f;
+      for (int b = 0; b < static_cast<int>(gridDim.x); ++b)
+        t += __ldcg(a.norm_partial + static_cast<size_t>(b) * kAdamMaxGroups + threadIdx.x);
+      reinterpret_cast<float*>(mine)[a.exchange_len + threadIdx.x] = t;
+    }
+    if (threadIdx.x == 0) atomicExch(a.barrier + 3, 0u);
+    __syncthreads();
+    // a block whose round-1 wait gave up tagged the abort word before its ticket: then the shard was not averaged,
+    // round 2 is not opened, and the peers' round-2 waits give up as well
+    if (*reinterpret_cast<volatile unsigned int*>(a.barrier + 2) != epoch)
+      publish_flag(a.peer_flags, a.world, a.rank, round2);
+  }
+  // ---- round 2: every shard is averaged; global norms from the ranks' slots in rank order ----
+  if (ok)
+    ok = await_peer_flags(a.peer_flags[a.rank], a.world, round2, a.timeout_ns, a.status, 70, a.barrier + 2, epoch);
+  ok = ok && *reinterpret_cast<volatile unsigned int*>(a.barrier + 2) != epoch;
+  if (threadIdx.x < a.ngroups) {
+    float t = 0.f;
+    for (int r = 0; r < a.world; ++r) t += __ldcv(a.peer_reduced[r] + a.exchange_len + threadIdx.x);
+    norm_sq[threadIdx.x] = t;
+  }
+  // the owner of element e holds its average: shard of float4 index e / 4
+  auto grad_of = [&](long long e) -> float {
+    const long long owner = (e >> 2) / a.shard4;
+    return __ldcv(a.peer_reduced[owner] + e);
+  };
+  __shared__ float kl_s;
+  if (threadIdx.x == 0) kl_s = (a.adaptive && a.kl_offset >= 0 && ok) ? grad_of(a.kl_offset) : 0.f;
+  __syncthreads();
+  adam_apply(a, norm_sq, kl_s, epoch, step_s, lr_old, ok, true, grad_of);
+}
+
+__global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs a) {
+  __shared__ float red[kAdamThreads / 32][kAdamMaxGroups];
+  __shared__ float norm_sq[kAdamMaxGroups];
+  __shared__ long long step_s[kAdamMaxGroups];
+  __shared__ float lr_old[kAdamMaxGroups];
+  __shared__ unsigned int epoch_s;
+  __shared__ int peers_ok;
+  // Everything block 0 rewrites at the end (step, learning rates, epoch) is read here, before any block can finish.
+  if (threadIdx.x == 0) {
+    peers_ok = 1;
+    for (int g = 0; g < a.ngroups; ++g) {
+      step_s[g] = a.step[g];
+      lr_old[g] = a.lr[g];
+    }
+    epoch_s = *a.epoch + 1u;
+  }
+  __syncthreads();
+  const unsigned int epoch = epoch_s;
+  if (a.world > 1 && a.peer_reduced != nullptr) {
+    adam_two_shot(a, epoch, step_s, lr_old);
+    return;
+  }
+  // ---- one-shot: flags ----
+  if (a.world > 1) {
+    // publish: this rank's slot in every peer's flag array (release orders our gradient writes before the flag)
+    if (blockIdx.x == 0) publish_flag(a.peer_flags, a.world, a.rank, epoch);
+    if (!await_peer_flags(a.peer_flags[a.rank], a.world, epoch, a.timeout_ns, a.status, 60, a.barrier + 2, epoch))
+      peers_ok = 0;
+  }
+  __syncthreads();
+  const bool exchange_ok = peers_ok != 0;
+  // ---- rank-ordered sum of every element, squared norms ----
+  float sq[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
+  const float inv_world = 1.0f / static_cast<float>(a.world);
+  const unsigned int parity = epoch & 1u;
+  const float4* mine4 = reinterpret_cast<const float4*>(a.send[parity]);
+  const long long n4 = a.exchange_len / 4;
+  for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < n4;
+       v += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 g = (a.world > 1 && exchange_ok) ? rank_average(a, parity, v, inv_world) : mine4[v];
+    reinterpret_cast<float4*>(a.grads)[v] = g;
+    add_group_squares(a, v, g, sq);
+  }
+  block_group_sums(sq, red);
+  if (threadIdx.x < kAdamMaxGroups) {
+    float t = 0.f;
+    for (int w = 0; w < kAdamThreads / 32; ++w) t += red[w][threadIdx.x];
+    a.norm_partial[static_cast<size_t>(blockIdx.x) * kAdamMaxGroups + threadIdx.x] = t;
+  }
+  if (!grid_sync(a.barrier, a.status, a.timeout_ns)) return;
+  // every block takes the same decision: the exchange failed if any block's wait gave up
+  const bool all_ok = *reinterpret_cast<volatile unsigned int*>(a.barrier + 2) != epoch;
+  // every block reduces the per-block partials with all of its threads (fixed tree order: identical in every block)
+  {
+    float part[kAdamMaxGroups] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x) {
+#pragma unroll
+      for (int g = 0; g < kAdamMaxGroups; ++g) part[g] += a.norm_partial[static_cast<size_t>(b) * kAdamMaxGroups + g];
+    }
+    block_group_sums(part, red);
+  }
+  if (threadIdx.x < a.ngroups) {
+    float t = 0.f;
+    for (int w = 0; w < kAdamThreads / 32; ++w) t += red[w][threadIdx.x];
+    norm_sq[threadIdx.x] = t;
+  }
+  const float kl = a.adaptive ? *a.kl_mean : 0.f;
+  adam_apply(a, norm_sq, kl, epoch, step_s, lr_old, all_ok, false, [&](long long e) { return a.grads[e]; });
+}
+
 
 // ---------------------------------------------------------------------------------------------------------------
 // Column statistics + EmpiricalNormalization update

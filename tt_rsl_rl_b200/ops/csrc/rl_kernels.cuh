@@ -252,9 +252,16 @@ struct AdamArgs {
   unsigned int* const* peer_flags;  // [world] flag arrays of every rank (each [world] uint32)
   unsigned int* epoch;              // device exchange counter (incremented by this kernel)
   uint64_t timeout_ns;
+  // two-shot exchange (world >= 2 with peer_reduced): rank r averages float4 elements [r S4, (r + 1) S4) of the
+  // exchanged vector over all ranks into its `reduced` buffer (followed by kAdamMaxGroups squared-norm slots), then
+  // every rank reads each element's average from its owner. Flags carry 2 e (gradients sent) and 2 e + 1 (shard
+  // averaged) for exchange e. Null peer_reduced: one-shot (every rank sums every element over all ranks).
+  float* const* peer_reduced;       // [world] device pointers of every rank's reduced buffer (exchange_len + 8 floats)
+  long long shard4;                 // S4: float4 elements per shard
+  long long kl_offset;              // index of the KL statistic in the exchanged vector (two-shot), -1: none
   // scratch
   float* norm_partial;              // [gridDim, ngroups]
-  unsigned int* barrier;            // [4] zero-initialised: grid-barrier count, generation, abort epoch
+  unsigned int* barrier;            // [4] zero-initialised: grid-barrier count, generation, abort epoch, ticket
   unsigned int* status;
   float* out_norms;                 // [ngroups] (optional)
 };

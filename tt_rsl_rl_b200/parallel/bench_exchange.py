@@ -49,6 +49,8 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--exchange", choices=["one_shot", "two_shot"], default="one_shot",
+                    help="one-shot: every rank sums every element; two-shot: reduce-scatter, then owner reads")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -103,11 +105,14 @@ def main() -> None:
     barrier = torch.zeros(4, dtype=torch.int32, device=dev)
     status = torch.zeros(4, dtype=torch.int32, device=dev)
 
+    two_shot = args.exchange == "two_shot"
+
     def fused_step():
         C.adam_step(flat, send[0], send[1], grads, m, v, tens, chunks, nch, [1.0, 1.0], [0.9, 0.9], [0.999, 0.999],
                     [1e-8, 1e-8], [0, 0], lr, None, step, True, grads[n + 3 : n + 4], 0.01, 1e-5, 1e-2, world, rank,
                     None if comm is None else comm.peer_send, None if comm is None else comm.peer_flags, epoch,
-                    10 * 10**9, norm_partial, barrier, status, None, grid, [0, n_actor, n_actor, n], n_ex)
+                    10 * 10**9, norm_partial, barrier, status, None, grid, [0, n_actor, n_actor, n], n_ex,
+                    comm.peer_reduced if (comm is not None and two_shot) else None, n + 3)
 
     def timed(fn, steps, warmup):
         for _ in range(warmup):
@@ -166,14 +171,15 @@ def main() -> None:
 
     hbm = _hbm_gbs()
     local_bytes = 4 * n * 9 + 2 * sum(sh.numel() for sh in shadows if sh is not None)  # send,g,p,m,v rd/wr + shadows
-    peer_bytes = 4 * n_ex * (world - 1)
+    peer_bytes = 4 * n_ex * (world - 1) if not two_shot else int(2 * 4 * n_ex * (world - 1) / world)
     roof_us = max(local_bytes / (hbm * 1e3), peer_bytes / (NVLINK_GBS * 1e3))
     # lower bound of any all-reduce algorithm: 2 (N - 1) / N of the vector crosses the links per rank
     min_bytes = 2.0 * (world - 1) / world * 4 * n_ex
     roof_min_us = max(local_bytes / (hbm * 1e3), min_bytes / (NVLINK_GBS * 1e3))
     if rank == 0:
         print(json.dumps({
-            "kernel": "fused exchange + clip + adaptive LR + Adam", "world": world, "params": n,
+            "kernel": "fused exchange + clip + adaptive LR + Adam", "exchange": args.exchange, "world": world,
+            "params": n,
             "grad_bytes_per_rank": 4 * n_ex, "fused_us": fused_us, "fused_eager_launch_us": eager_us,
             "roofline_us": roof_us,
             "roofline_fraction": roof_us / fused_us, "peer_bytes_per_rank": peer_bytes, "local_hbm_bytes": local_bytes,

@@ -4,8 +4,10 @@ One process per GPU (``torchrun``). ``torch.distributed`` is used once, at const
 (``all_gather_object``); afterwards every exchange is a kernel reading peer memory over NVLink / NVSwitch:
 
 * gradient exchange: two send buffers per rank (alternating by exchange parity, so a rank never overwrites gradients a
-  slower peer may still read) and a flag array; consumed by the fused clip + Adam kernel, which sums the peers'
-  gradients in rank order, so every rank computes bit-identical parameters;
+  slower peer may still read), a reduced buffer (the rank's averaged shard and its squared norms, for the two-shot
+  exchange) and a flag array; consumed by the fused clip + Adam kernel, which sums the ranks' gradients in rank order
+  (every element on every rank in the one-shot exchange, the own shard in the two-shot one), so every rank computes
+  bit-identical parameters;
 * small collectives (normaliser moments, parameter broadcast) on a separate buffer and flag channel.
 
 Replaces ``torch.distributed`` all-reduce / broadcast at ``rsl_rl/utils/utils.py:345-392``,
@@ -35,6 +37,7 @@ class PeerExchange:
         self._bufs = {
             "send0": C.ipc_alloc(4 * n_exchange, dev),
             "send1": C.ipc_alloc(4 * n_exchange, dev),
+            "reduced": C.ipc_alloc(4 * (n_exchange + 8), dev),
             "flags": C.ipc_alloc(4 * world, dev),
             "small": C.ipc_alloc(max(64, n_small_bytes), dev),
             "small_flags": C.ipc_alloc(4 * world, dev),
@@ -59,6 +62,7 @@ class PeerExchange:
         # device pointer tables read by the fused Adam kernel
         self.peer_send = torch.tensor(ptrs["send0"] + ptrs["send1"], dtype=torch.int64, device=device)
         self.peer_flags = torch.tensor(ptrs["flags"], dtype=torch.int64, device=device)
+        self.peer_reduced = torch.tensor(ptrs["reduced"], dtype=torch.int64, device=device)
         torch.distributed.barrier()
 
     @classmethod
