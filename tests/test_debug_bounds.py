@@ -51,3 +51,18 @@ def test_status_code_of_bad_index_matches_the_host_mapping():
 def test_setup_adds_the_define_only_when_asked(monkeypatch):
     text = open(os.path.join(ROOT, "setup.py")).read()
     assert 'os.environ.get("TT_RSL_RL_DEBUG_BOUNDS") == "1"' in text and "-DRL_DEBUG_BOUNDS" in text
+
+
+def test_loaded_build_reports_its_bounds_mode():
+    """The extension says which build is loaded (release builds: no checks), so logs and tests can record it."""
+    from tt_rsl_rl_b200.ops import ext
+
+    assert ext().debug_bounds_enabled() is (os.environ.get("TT_RSL_RL_DEBUG_BOUNDS") == "1")
+
+
+def test_every_index_read_from_memory_has_a_check_site():
+    """Sites: 41 minibatch gather sample index, 42 mirrored copy source column, 43 per-minibatch advantage index,
+    44 loss kernels' storage row, 45 mirrored action column."""
+    src = open(os.path.join(ROOT, "tt_rsl_rl_b200", "ops", "csrc", "rl_kernels.cu")).read()
+    sites = sorted(int(s) for s in re.findall(r"RL_CHECK_INDEX\([^;]*,\s*(\d+)\);", src))
+    assert sorted(set(sites)) == [41, 42, 43, 44, 45]

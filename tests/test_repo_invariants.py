@@ -75,3 +75,15 @@ def test_engines_read_device_data_only_through_named_transfers():
     benchmark's count of reads per iteration is complete."""
     files = [p for p in (PKG / "engine").glob("*.py")] + [PKG / "parallel" / "peer_exchange.py"]
     assert _offenders(r"\.(item|tolist|cpu|numpy)\(\)", files) == []
+
+
+def test_noalloc_header_declares_the_definition():
+    """The C declaration in gae_noalloc.h (which callers and the GPU test's ctypes binding read) has the parameter
+    types of the definition in gae_noalloc.cu."""
+    def params(path):
+        text = (CSRC / path).read_text()
+        decl = re.search(r"int\s+rlb_gae_advantages_noalloc\s*\(([^)]*)\)", text).group(1)
+        return [" ".join(p.split()[:-1]).replace(" *", "*") for p in decl.split(",")]
+
+    assert params("gae_noalloc.h") == params("gae_noalloc.cu")
+    assert '#include "gae_noalloc.h"' in (CSRC / "gae_noalloc.cu").read_text()

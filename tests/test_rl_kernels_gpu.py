@@ -95,7 +95,7 @@ def test_ppo_loss_matches_autograd(hetero, log_std):
     C().ppo_loss(B, A, hetero, log_std, head, hc, value, 1, None if hetero else std_raw, 1e-6, 1e6, math.log(1e-6),
                  math.log(1e6), idx, st_actions, st_mean, st_std, st_logp, st_adv, st_ret, st_val, None, clip, vc, ec,
                  True, d_head, d_head.shape[1], d_value, 8, stats, dh_col, dv_col, None if hetero else dstd, 1, False,
-                 None, None, 0.0)
+                 None, None, 0.0, None)
     torch.cuda.synchronize()
     scale = ref["dhead"].abs().max().item()
     torch.testing.assert_close(d_head[:, :hc].float(), ref["dhead"], atol=1e-2 * scale, rtol=1e-2)

@@ -115,7 +115,8 @@ def test_ppo_loss_with_symmetry_matches_autograd(aug, K, coef):
     dstd = torch.zeros(blocks, A, device=dev)
     C().ppo_loss(n0, A, False, False, head.detach(), A, value.detach(), 1, std_raw.detach(), 1e-6, 1e6,
                  math.log(1e-6), math.log(1e6), idx, st_actions, st_mean, st_std, st_logp, st_adv, st_ret, st_val, None,
-                 clip, vc, ec, True, d_head, 16, d_value, 8, stats, dh_col, dv_col, dstd, K, aug, perm, sign, coef)
+                 clip, vc, ec, True, d_head, 16, d_value, 8, stats, dh_col, dv_col, dstd, K, aug, perm, sign, coef,
+                 None)
     torch.cuda.synchronize()
     scale = head.grad.abs().max().item()
     torch.testing.assert_close(d_head[:, :A].float(), head.grad, atol=1e-2 * scale, rtol=1e-2)

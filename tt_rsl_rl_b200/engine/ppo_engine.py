@@ -551,7 +551,7 @@ class PPOEngine(EngineBase):
         if not self.adv_per_mb or n <= 1:
             return None
         C = ext()
-        C.adv_gather_stats(self.st_adv, idx, n, self.adv_mb, self.adv_mb_partial)
+        C.adv_gather_stats(self.st_adv, idx, n, self.adv_mb, self.adv_mb_partial, self.status)
         C.adv_normalize(self.adv_mb[:n], self.adv_mb_partial, C.adv_gather_blocks(n))
         return self.adv_mb
 
@@ -602,7 +602,7 @@ class PPOEngine(EngineBase):
                    alg.value_loss_coef, alg.entropy_coef, alg.use_clipped_value_loss, pa.d_head, pa.d_head.shape[1],
                    self.d_value, self.d_value.shape[1], self.stats_partial, self.dhead_colsum, self.dvalue_colsum,
                    None if self.hetero else self.dstd_partial, self.K, self.aug, self.act_perm, self.act_sign,
-                   self.mirror_coef)
+                   self.mirror_coef, self.status)
         pa.backward(rows_a, self.status)
         pc.backward(rows_c, self.status)
         if self.rnd is not None:

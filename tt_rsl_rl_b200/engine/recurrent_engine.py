@@ -521,7 +521,7 @@ class RecurrentPPOEngine(EngineBase):
         alg = self.alg
         adv_override = None
         if self.adv_per_mb and R > 1:
-            C.adv_gather_stats(self.st_adv, self.mb_idx[i], R, self.adv_mb, self.adv_mb_partial)
+            C.adv_gather_stats(self.st_adv, self.mb_idx[i], R, self.adv_mb, self.adv_mb_partial, self.status)
             C.adv_normalize(self.adv_mb[:R], self.adv_mb_partial, C.adv_gather_blocks(R))
             adv_override = self.adv_mb
         C.ppo_loss(R, self.A, self.hetero, self.log_std, pa.out_train, pa.out_train.shape[1], self.value_train, 1,
@@ -531,7 +531,7 @@ class RecurrentPPOEngine(EngineBase):
                    alg.clip_param,
                    alg.value_loss_coef, alg.entropy_coef, alg.use_clipped_value_loss, pa.d_head, pa.d_head.shape[1],
                    self.d_value, self.d_value.shape[1], self.stats_partial, self.dhead_colsum, self.dvalue_colsum,
-                   None if self.hetero else self.dstd_partial, 1, False, None, None, 0.0)
+                   None if self.hetero else self.dstd_partial, 1, False, None, None, 0.0, self.status)
         self.net_a.backward_sequence(lo, Be, self.st_dones, self.status)
         self.net_c.backward_sequence(lo, Be, self.st_dones, self.status)
         C.reduce_segments(self.reduce_plan, self.reduce_nseg, self.reduce_chunks, self.send[0], self.send[1],

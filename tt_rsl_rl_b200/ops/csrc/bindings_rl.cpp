@@ -236,7 +236,7 @@ void ppo_loss(int64_t B, int64_t A, bool hetero, bool log_std, const Tensor& hea
               const Tensor& d_head, int64_t ld_dhead, const Tensor& d_value, int64_t ld_dvalue,
               const Tensor& stats_partial, const Tensor& dhead_colsum, const Tensor& dvalue_colsum,
               const OptT& dstd_partial, int64_t copies, bool aug, const OptT& act_perm, const OptT& act_sign,
-              double mirror_coef) {
+              double mirror_coef, const OptT& status) {
   // B: original samples of the minibatch; the actor rows are copies * B (symmetry copies after the originals)
   check_f32(head, "head");
   check_f32(value, "value");
@@ -301,6 +301,8 @@ void ppo_loss(int64_t B, int64_t A, bool hetero, bool log_std, const Tensor& hea
   a.dhead_colsum = P<float>(dhead_colsum);
   a.dvalue_colsum = P<float>(dvalue_colsum);
   a.dstd_partial = P<float>(dstd_partial);
+  a.total = st_actions.size(0);
+  a.status = P<unsigned int>(status);
   ok(rlb::ppo_loss(a, cur()), "ppo_loss");
 }
 
@@ -416,13 +418,15 @@ void lg_env_step(const Tensor& next, const Tensor& state, const Tensor& actions,
 
 int64_t adv_gather_blocks(int64_t n) { return rlb::adv_gather_blocks(n); }
 
-void adv_gather_stats(const Tensor& adv, const Tensor& idx, int64_t n, const Tensor& out, const Tensor& partial) {
+void adv_gather_stats(const Tensor& adv, const Tensor& idx, int64_t n, const Tensor& out, const Tensor& partial,
+                      const OptT& status) {
   check_f32(adv, "adv");
   check_f32(out, "out");
   TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.numel() >= n && out.numel() >= n, "adv_gather_stats: sizes");
   TORCH_CHECK(partial.scalar_type() == torch::kFloat64 && partial.numel() >= 2 * rlb::adv_gather_blocks(n),
               "adv_gather_stats: partial must be float64 [2 * blocks]");
-  ok(rlb::adv_gather_stats(P<const float>(adv), P<const int>(idx), n, P<float>(out), P<double>(partial), cur()),
+  ok(rlb::adv_gather_stats(P<const float>(adv), adv.numel(), P<const int>(idx), n, P<float>(out), P<double>(partial),
+                           P<unsigned int>(status), cur()),
      "adv_gather_stats");
 }
 
@@ -661,6 +665,8 @@ void rlb_register_kernels(pybind11::module& m) {
   m.def("adv_gather_blocks", &adv_gather_blocks);
   m.def("lg_env_step", &lg_env_step);
   m.def("adv_gather_stats", &adv_gather_stats);
+  m.def("debug_bounds_enabled", &rlb::debug_bounds_enabled,
+        "whether the kernels were built with RL_DEBUG_BOUNDS (indices read from memory are checked)");
   m.def("mse_grad", &mse_grad);
   m.def("rnd_intrinsic", &rnd_intrinsic);
   m.def("rnd_reward_scale", &rnd_reward_scale);

@@ -214,14 +214,17 @@ __global__ void adv_normalize_kernel(float* adv, long long n, const double* part
 
 constexpr int kAdvGatherBlocks = 148;
 
-__global__ void __launch_bounds__(256) adv_gather_stats_kernel(const float* __restrict__ adv,
+__global__ void __launch_bounds__(256) adv_gather_stats_kernel(const float* __restrict__ adv, long long n_adv,
                                                                 const int* __restrict__ idx, long long n,
-                                                                float* __restrict__ out, double* __restrict__ partial) {
+                                                                float* __restrict__ out, double* __restrict__ partial,
+                                                                unsigned int* status) {
   __shared__ double red[2][8];
   double s = 0.0, ss = 0.0;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const float v = adv[idx[i]];
+    long long src = idx[i];
+    RL_CHECK_INDEX(src, n_adv, status, 43);
+    const float v = adv[src];
     out[i] = v;
     s += v;
     ss += static_cast<double>(v) * v;
@@ -463,7 +466,8 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
     for (int rr = 0; rr < PF; ++rr) {
       const int i = row0 + rr;
       const bool in = i < a.B;
-      const int src = in ? a.idx[i] : 0;
+      int src = in ? a.idx[i] : 0;
+      RL_CHECK_INDEX(src, a.total, a.status, 44);
       const float* h = a.head + static_cast<size_t>(in ? i : 0) * a.ld_head;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
@@ -490,7 +494,8 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
     const int copy = kSym ? i / a.n0 : 0;
     const int o = i - copy * a.n0;
     const bool ppo_row = a.aug || copy == 0;
-    const int src = kSym ? a.idx[o] : 0;
+    int src = kSym ? a.idx[o] : 0;
+    RL_CHECK_INDEX(src, a.total, a.status, 44);
     const float* h = a.head + static_cast<size_t>(i) * a.ld_head;
     float mu[2], sd[2], isd[2], raw[2], act[2], mt[2];
     float lp = 0.f, ent = 0.f, kl = 0.f, sym = 0.f;
@@ -513,6 +518,7 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
         float asg = 1.f;
         if (copy > 0) {  // the copy's action and mirror target: signed permutation of the original's columns
           aj = a.act_perm[copy * a.A + j];
+          RL_CHECK_INDEX(aj, a.A, a.status, 45);
           asg = a.act_sign[copy * a.A + j];
           mt[k] = asg * a.head[static_cast<size_t>(o) * a.ld_head + aj];
           const float dm = mu[k] - mt[k];
@@ -704,7 +710,8 @@ __global__ void __launch_bounds__(kLoss8Warps * 32, 2) ppo_loss_rows8_kernel(con
   for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
     const int i = grp * kLossRowsPerBlock + warp * 4 + g;
     const bool in = i < a.B;  // rows past B still take part in the warp's shuffles, with neutral values
-    const int src = in ? a.idx[i] : 0;
+    int src = in ? a.idx[i] : 0;
+    RL_CHECK_INDEX(src, a.total, a.status, 44);
     const float* h = a.head + static_cast<size_t>(in ? i : 0) * a.ld_head;
     // ---- loads ----
     float act[4], omu[4], osd[4], mu[4], raw[4];
@@ -1530,11 +1537,19 @@ int adv_gather_blocks(long long n) {
   return static_cast<int>(b < kAdvGatherBlocks ? (b < 1 ? 1 : b) : kAdvGatherBlocks);
 }
 
-cudaError_t adv_gather_stats(const float* adv, const int* idx, long long n, float* out, double* partial,
-                             cudaStream_t s) {
+cudaError_t adv_gather_stats(const float* adv, long long n_adv, const int* idx, long long n, float* out,
+                             double* partial, unsigned int* status, cudaStream_t s) {
   if (n <= 0) return cudaErrorInvalidValue;
-  adv_gather_stats_kernel<<<adv_gather_blocks(n), 256, 0, s>>>(adv, idx, n, out, partial);
+  adv_gather_stats_kernel<<<adv_gather_blocks(n), 256, 0, s>>>(adv, n_adv, idx, n, out, partial, status);
   return cudaGetLastError();
+}
+
+bool debug_bounds_enabled() {
+#ifdef RL_DEBUG_BOUNDS
+  return true;
+#else
+  return false;
+#endif
 }
 
 int ppo_loss_blocks(int B) {

@@ -86,8 +86,10 @@ cudaError_t adv_normalize(float* adv, long long n, const double* partial, int pa
 // Per-minibatch advantages: out[i] = adv[idx[i]] with per-block (sum, sum of squares) partials in fp64, the input of
 // adv_normalize (normalize_advantage_per_mini_batch). Returns the partial count through *parts.
 int adv_gather_blocks(long long n);
-cudaError_t adv_gather_stats(const float* adv, const int* idx, long long n, float* out, double* partial,
-                             cudaStream_t s);
+cudaError_t adv_gather_stats(const float* adv, long long n_adv, const int* idx, long long n, float* out,
+                             double* partial, unsigned int* status, cudaStream_t s);
+// Whether this library was built with -DRL_DEBUG_BOUNDS (indices read from memory are checked before use).
+bool debug_bounds_enabled();
 
 constexpr int kGatherModels = 3;
 // Minibatch gather: for rows i in [0, B) take storage row idx = perm(offset + i) (Feistel bijection of [0, total) keyed
@@ -158,6 +160,8 @@ struct PpoLossArgs {
   float* dhead_colsum;    // [blocks, head_cols]
   float* dvalue_colsum;   // [blocks, 1]
   float* dstd_partial;    // [blocks, A] (non-hetero)
+  long long total;        // storage rows (bound of idx in builds with RL_DEBUG_BOUNDS)
+  unsigned int* status;   // optional status word (index errors of builds with RL_DEBUG_BOUNDS)
 };
 constexpr int kLossStats = 5;
 int ppo_loss_blocks(int B);
