@@ -11,6 +11,10 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
+# 3 x measured bf16 noise floors (see test_engine_update_matches_torch_path)
+FLOOR_MEAN = 0.12
+FLOOR_VALUE = 0.007
+
 
 def _models(obs, hidden, actor_obs="policy", critic_obs="policy", hetero=False, A=12):
     from tt_rsl_rl_b200.models import MLPModel
@@ -78,10 +82,13 @@ def test_engine_update_matches_torch_path(hetero, per_mb):
         value_e = alg_e.critic(probe)
     dev_mean = (mean_e - mean_t).norm() / (mean_t - mean_old).norm()
     dev_value = (value_e - value_t).norm() / (value_t - value_old).norm()
-    assert dev_mean < 0.15, dev_mean
-    assert dev_value < 0.15, dev_value
+    # Bounds = 3 x the bf16 noise floor measured on B200: the same update with the PyTorch path under bf16 autocast
+    # deviates from the fp32 PyTorch path by up to 0.041 (policy mean) and 0.0023 (value) over 3 seeds x these
+    # 3 configurations (the engine itself: up to 0.033 and 0.0026); loss statistics by up to 0.5 % (surrogate).
+    assert dev_mean < FLOOR_MEAN, dev_mean
+    assert dev_value < FLOOR_VALUE, dev_value
     for k in ("value", "surrogate", "entropy"):
-        assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=2e-3), (k, loss_e[k], loss_t[k])
+        assert loss_e[k] == pytest.approx(loss_t[k], rel=1.5e-2, abs=2e-4), (k, loss_e[k], loss_t[k])
     assert alg_e.learning_rate == pytest.approx(alg_t.learning_rate, rel=1e-6)
     for a, b in ((alg_t.actor, alg_e.actor), (alg_t.critic, alg_e.critic)):
         torch.testing.assert_close(a.obs_normalizer._mean, b.obs_normalizer._mean, atol=1e-5, rtol=1e-5)
@@ -105,9 +112,11 @@ def test_engine_rollout_consistent_with_model():
         value = alg_e.critic(obs)[:, 0]
         std = alg_e.actor.distribution.current_std()
         logp = torch.distributions.Normal(mean, std).log_prob(actions).sum(-1)
-    torch.testing.assert_close(eng.st_mean[:N], mean, atol=3e-2, rtol=3e-2)
-    torch.testing.assert_close(eng.st_values[:N], value, atol=3e-2, rtol=3e-2)
-    torch.testing.assert_close(eng.st_logp[:N], logp, atol=0.5, rtol=2e-2)
+    # 3 x the bf16 floor: the fp32 model under bf16 autocast differs from fp32 by up to 0.0021 (mean), 0.0025
+    # (value) and 0.0088 (log-prob, values of magnitude ~58) on these inputs; the engine by 0.0017, 0.0014, 0.0076
+    torch.testing.assert_close(eng.st_mean[:N], mean, atol=7e-3, rtol=0)
+    torch.testing.assert_close(eng.st_values[:N], value, atol=8e-3, rtol=0)
+    torch.testing.assert_close(eng.st_logp[:N], logp, atol=3e-2, rtol=0)
     torch.testing.assert_close(eng.st_actions[:N], actions)
 
 

@@ -213,7 +213,7 @@ def test_adam_with_two_clip_groups_matches_torch():
         C().adam_step(flat, send, send, grads, m, v, tens, chunks, nch, [1.0, 1.0], [0.9, 0.9], [0.999, 0.999],
                       [1e-8, 1e-8], [0, 0], lr, None, step, True, grads[n + 3 : n + 4], 0.01, 1e-5, 1e-2, 1, 0, None,
                       None, epoch, 10**9, norm_partial, barrier, status, None, grid, [0, offsets[4], offsets[4], n],
-                      n_ex)
+                      n_ex, None, -1)
         for p, g in zip(ref_params, gs):
             p.grad = g.clone()
         torch.nn.utils.clip_grad_norm_([ref_params[i] for i in range(6) if groups[i] == 0], 1.0)
@@ -249,7 +249,7 @@ def test_adaptive_learning_rate_rule():
         send[n + 3] = kl
         C().adam_step(flat, send, send, grads, m, v, tens, chunks, nch, [1.0], [0.9], [0.999], [1e-8], [0], lr, None,
                       args["step"], True, grads[n + 3 : n + 4], 0.01, 1e-5, 1e-2, 1, 0, None, None, args["epoch"],
-                      10**9, args["norm_partial"], args["barrier"], None, None, grid, [0, n], n + 4)
+                      10**9, args["norm_partial"], args["barrier"], None, None, grid, [0, n], n + 4, None, -1)
         if kl > 0.02:
             expect = max(1e-5, expect / 1.5)
         elif 0.0 < kl < 0.005:
