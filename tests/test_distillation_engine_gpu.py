@@ -100,7 +100,9 @@ def test_distillation_update_matches_torch_path(loss_type):
         new_t = alg_t.student(probe)
         new_e = alg_e.student(probe)
     dev = (new_e - new_t).norm() / (new_t - old).norm()
-    assert dev < 0.15, dev
+    # 3 x the bf16 noise floor measured on B200: the PyTorch path under bf16 autocast deviates from fp32 by up to
+    # 0.0016 of the update over 3 seeds x both losses (the engine: up to 0.0017)
+    assert dev < 5e-3, dev
     # two windows of three steps were applied per epoch... (2 epochs x 8 steps = 16 steps -> 5 Adam steps)
     assert int(alg_e.engine.step[0].item()) == 5
     # the std parameter gets no gradient and stays put, as with torch.optim.Adam and grad=None

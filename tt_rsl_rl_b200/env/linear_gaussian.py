@@ -100,10 +100,12 @@ class LinearGaussianVecEnv(VecEnv):
                 self._noise_ready = None
         self._write_obs(torch.zeros(num_envs, num_actions, device=self.device))
         self._obs = self._make_obs_dict()
-        # fused device step (everything after the two matmuls in one kernel); None: on CUDA when the framework's
-        # extension is available. The PyTorch-op step below is the specification and the CPU path.
+        # fused device step (the whole transition in one kernel; state width a multiple of 4 up to 128, at most 64
+        # actions); None: on CUDA when the framework's extension is available. The PyTorch-op step below is the
+        # specification and the CPU path.
         if fused is None:
-            fused = self.device.type == "cuda" and _extension_available()
+            fused = (self.device.type == "cuda" and obs_dim % 4 == 0 and obs_dim <= 128 and num_actions <= 64
+                     and _extension_available())
         self.fused = bool(fused)
         self.inplace_obs = bool(inplace_obs) and not self.fused
         if not self.fused and not self.inplace_obs:
@@ -212,13 +214,13 @@ class LinearGaussianVecEnv(VecEnv):
 
 
     def _fused_step(self, a: torch.Tensor):
-        """Same transition on the device: the matmuls on cuBLAS, the rest in one kernel with Philox noise."""
-        torch.addmm(torch.mm(self.state, self.At), a, self.Bt, out=self._next)
+        """Same transition in one kernel of this framework: the matrix-vector products with A and B from shared
+        memory, Philox noise, reward, resets and observation writes."""
         noise = self._draw_noise() if self.host_noise else None
         from ..ops import ext
 
         a = a if a.stride(1) == 1 else a.contiguous()
-        ext().lg_env_step(self._next, self.state, a, noise, self.noise_std, self.reset_prob,
+        ext().lg_env_step(self.At, self.Bt, self.state, a, noise, self.noise_std, self.reset_prob,
                                 int(self.max_episode_length), self.episode_length_buf, self.rewards, self.dones,
                                 self.time_outs, self._policy_obs, self._critic_obs, self.privileged_dim,
                                 self._env_seed, self._env_counter, self._env_ticket)

@@ -371,20 +371,28 @@ void rnd_reward_scale(const Tensor& out, int64_t rows, const Tensor& weight, con
      "rnd_reward_scale");
 }
 
-void lg_env_step(const Tensor& next, const Tensor& state, const Tensor& actions, const OptT& noise, double noise_std,
-                 double reset_prob, int64_t max_len, const Tensor& ep_len, const Tensor& rewards, const Tensor& dones,
-                 const Tensor& time_outs, const Tensor& obs_policy, const OptT& obs_critic, int64_t priv, int64_t seed,
-                 const Tensor& counter, const Tensor& ticket) {
-  for (const Tensor* t : {&next, &state, &actions, &rewards, &dones, &time_outs, &obs_policy}) check_f32(*t, "env");
+void lg_env_step(const Tensor& At, const Tensor& Bt, const Tensor& state, const Tensor& actions, const OptT& noise,
+                 double noise_std, double reset_prob, int64_t max_len, const Tensor& ep_len, const Tensor& rewards,
+                 const Tensor& dones, const Tensor& time_outs, const Tensor& obs_policy, const OptT& obs_critic,
+                 int64_t priv, int64_t seed, const Tensor& counter, const Tensor& ticket) {
+  for (const Tensor* t : {&At, &Bt, &state, &actions, &rewards, &dones, &time_outs, &obs_policy}) check_f32(*t, "env");
   const int64_t N = state.size(0), S = state.size(1), A = actions.size(1);
-  TORCH_CHECK(next.is_contiguous() && state.is_contiguous() && obs_policy.is_contiguous() && actions.stride(1) == 1,
+  TORCH_CHECK(At.is_contiguous() && Bt.is_contiguous() && state.is_contiguous() && obs_policy.is_contiguous() &&
+                  actions.stride(1) == 1,
               "lg_env_step: contiguous rows expected");
-  TORCH_CHECK(next.numel() == N * S && obs_policy.numel() == N * S && rewards.numel() == N && dones.numel() == N &&
-                  time_outs.numel() == N && ep_len.numel() == N && ep_len.scalar_type() == torch::kInt64,
+  TORCH_CHECK(At.numel() == S * S && Bt.numel() == A * S && S <= 128 && S % 4 == 0 && A <= 64,
+              "lg_env_step: A^T [S, S], B^T [A, S] with S <= 128, S % 4 == 0, A <= 64");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(state.data_ptr()) % 16) == 0 &&
+                  (reinterpret_cast<uintptr_t>(obs_policy.data_ptr()) % 16) == 0,
+              "lg_env_step: state and policy observations must be 16-byte aligned");
+  TORCH_CHECK(obs_policy.numel() == N * S && rewards.numel() == N && dones.numel() == N && time_outs.numel() == N &&
+                  ep_len.numel() == N && ep_len.scalar_type() == torch::kInt64,
               "lg_env_step: sizes");
   if (noise.has_value()) {
     check_f32(*noise, "noise");
-    TORCH_CHECK(noise->is_contiguous() && noise->numel() == N * S, "lg_env_step: noise");
+    TORCH_CHECK(noise->is_contiguous() && noise->numel() == N * S &&
+                    (reinterpret_cast<uintptr_t>(noise->data_ptr()) % 16) == 0,
+                "lg_env_step: noise");
   }
   if (obs_critic.has_value()) {
     check_f32(*obs_critic, "obs_critic");
@@ -396,7 +404,8 @@ void lg_env_step(const Tensor& next, const Tensor& state, const Tensor& actions,
   a.S = static_cast<int>(S);
   a.A = static_cast<int>(A);
   a.P = static_cast<int>(priv);
-  a.next = P<const float>(next);
+  a.At = P<const float>(At);
+  a.Bt = P<const float>(Bt);
   a.state = P<float>(state);
   a.actions = P<const float>(actions);
   a.ld_act = static_cast<int>(actions.stride(0));

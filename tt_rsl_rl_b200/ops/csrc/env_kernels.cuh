@@ -1,4 +1,4 @@
-// Fused step of the synthetic linear-Gaussian environment (everything after the two fp32 matmuls s A^T + a B^T).
+// Fused step of the synthetic linear-Gaussian environment (transition, noise, reward, resets, observations).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -8,8 +8,9 @@ namespace rlb {
 
 struct LgEnvArgs {
   int N, S, A, P;          // environments, state dim, action dim, privileged critic features (critic width S + P)
-  const float* next;       // [N, S] s A^T + a B^T (row pitch S)
-  float* state;            // [N, S] out: the new state (reset where done)
+  const float* At;         // [S, S] A^T (row-major: At[i * S + j] = A[j][i])
+  const float* Bt;         // [A, S] B^T
+  float* state;            // [N, S] in: s; out: the new state (reset where done). S <= 128, S % 4 == 0, A <= 64
   const float* actions;    // [N, A] row pitch ld_act
   int ld_act;
   const float* noise;      // optional [N, S] process noise supplied by the caller (else Philox normals)
@@ -27,5 +28,6 @@ struct LgEnvArgs {
 };
 
 cudaError_t lg_env_step(const LgEnvArgs& a, cudaStream_t s);
+size_t lg_env_smem_bytes(int S, int A);
 
 }  // namespace rlb

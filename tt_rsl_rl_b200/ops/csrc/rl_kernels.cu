@@ -114,6 +114,51 @@ __global__ void gaussian_sample_kernel(const SampleArgs a) {
   last_block_advance(a.counter, a.ticket);
 }
 
+// A <= 32: eight lanes per row, four rows per warp. Lane l8 of a row owns actions 4 l8 .. 4 l8 + 3, which are exactly
+// the four normals of one Philox block (counter word 1 = action group), so each block is computed once instead of by
+// four lanes; same streams and results as gaussian_sample_kernel.
+__global__ void __launch_bounds__(256) gaussian_sample_rows8_kernel(const SampleArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int l8 = lane & 7;
+  const uint64_t offset = *a.counter;
+  const int rows_per_block = (blockDim.x >> 5) * 4;
+  for (int row0 = blockIdx.x * rows_per_block; row0 < a.rows; row0 += gridDim.x * rows_per_block) {
+    const int row = row0 + (threadIdx.x >> 5) * 4 + (lane >> 3);
+    const bool in = row < a.rows;
+    float logp = 0.f;
+    if (in && 4 * l8 < a.A) {
+      const Philox rnd = philox10(static_cast<uint32_t>(row), static_cast<uint32_t>(l8),
+                                  static_cast<uint32_t>(offset), static_cast<uint32_t>(offset >> 32),
+                                  static_cast<uint32_t>(a.seed), static_cast<uint32_t>(a.seed >> 32));
+      float eps[4];
+      box_muller(rnd.c[0], rnd.c[1], eps[0], eps[1]);
+      box_muller(rnd.c[2], rnd.c[3], eps[2], eps[3]);
+      const float* h = a.head + static_cast<size_t>(row) * a.ld_head;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int j = 4 * l8 + k;
+        if (j < a.A) {
+          const float mu = h[j];
+          const float raw = a.hetero ? h[a.A + j] : a.std_param[j];
+          const float sd = head_std(raw, a.log_std, a.std_lo, a.std_hi, a.log_std_lo, a.log_std_hi);
+          const float act = mu + sd * eps[k];
+          const size_t o = static_cast<size_t>(row) * a.A + j;
+          a.actions[o] = act;
+          if (a.actions_copy) a.actions_copy[o] = act;
+          a.out_mean[o] = mu;
+          a.out_std[o] = sd;
+          const float z = (act - mu) / sd;
+          logp += -0.5f * z * z - logf(sd) - kLogSqrt2Pi;
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) logp += __shfl_xor_sync(0xffffffffu, logp, off);
+    if (in && l8 == 0) a.out_logp[row] = logp;
+  }
+  last_block_advance(a.counter, a.ticket);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // process_step
 // ---------------------------------------------------------------------------------------------------------------
@@ -1489,7 +1534,10 @@ cudaError_t prep_obs(const PrepObsArgs& a, cudaStream_t s) {
 
 cudaError_t gaussian_sample(const SampleArgs& a, cudaStream_t s) {
   if (a.A > 64 || a.rows <= 0) return cudaErrorInvalidValue;
-  gaussian_sample_kernel<<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+  if (a.A <= 32)
+    gaussian_sample_rows8_kernel<<<grid_for(a.rows, 32), 256, 0, s>>>(a);
+  else
+    gaussian_sample_kernel<<<grid_for(a.rows, 8), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
