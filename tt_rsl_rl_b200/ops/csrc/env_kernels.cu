@@ -37,11 +37,12 @@ __global__ void __launch_bounds__(kEnvWarps * 32) lg_env_step_kernel(const LgEnv
   float* At = smem;                           // [S, S]: At[i * S + j] = A[j][i]
   float* Bt = At + a.S * a.S;                 // [A, S]
   float* vec = Bt + a.A * a.S;                // per warp: the state row then the action row
+  const int vec_stride = a.S + ((a.A + 3) & ~3);  // floats per warp slot: a multiple of 4 (16-byte float4 stores)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int k = threadIdx.x; k < a.S * a.S; k += blockDim.x) At[k] = a.At[k];
   for (int k = threadIdx.x; k < a.A * a.S; k += blockDim.x) Bt[k] = a.Bt[k];
   __syncthreads();
-  float* wv = vec + warp * (a.S + a.A);
+  float* wv = vec + warp * vec_stride;
   const int S4 = a.S / 4;
   const bool own = lane < S4;
   const uint64_t step = *a.counter;
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(kEnvWarps * 32) lg_env_step_kernel(const LgEnv
 }  // namespace
 
 size_t lg_env_smem_bytes(int S, int A) {
-  return sizeof(float) * (static_cast<size_t>(S) * S + static_cast<size_t>(A) * S + kEnvWarps * (S + A));
+  return sizeof(float) * (static_cast<size_t>(S) * S + static_cast<size_t>(A) * S + kEnvWarps * (S + ((A + 3) & ~3)));
 }
 
 cudaError_t lg_env_step(const LgEnvArgs& a, cudaStream_t s) {
