@@ -592,3 +592,14 @@ def test_distillation_checkpoint_resumes_like_upstream(ref, tmp_path):
     assert saved["b200"]["iter"] == saved["upstream"]["iter"]
     for key in saved["upstream"]:
         _equal_state(saved["b200"][key], saved["upstream"][key], key)
+
+
+def test_golden_check_takes_the_execution_path(tmp_path):
+    """``golden check --engine torch`` trains the PyTorch path (here on the CPU, where it is the only path)."""
+    from tt_rsl_rl_b200.testing import golden
+
+    out = golden.check(["cartpole"], seeds=[0], iterations=2, log_root=str(tmp_path), engine="torch",
+                       mixed_precision=False)
+    assert out[0]["env"] == "cartpole" and len(out[0]["final_rewards"]) == 1
+    cfg = (tmp_path / "cartpole" / "seed0" / "config.json").read_text()
+    assert '"engine": "torch"' in cfg

@@ -150,8 +150,10 @@ def summarize_dir(envs, seeds=None, golden_dir: str | Path = GOLDEN_DIR) -> dict
 
 
 def check(envs, seeds=None, device: str = "cpu", iterations: int | None = None, log_root: str | None = None,
-          golden_dir: str | Path = GOLDEN_DIR, num_threads: int | None = None) -> list[dict]:
-    """Train every environment with this framework on ``device`` and apply the acceptance rule."""
+          golden_dir: str | Path = GOLDEN_DIR, num_threads: int | None = None, engine: str | None = None,
+          mixed_precision: bool = False) -> list[dict]:
+    """Train every environment with this framework on ``device`` and apply the acceptance rule. ``engine`` selects
+    the execution path (``"cuda"`` fused engines, ``"torch"`` the PyTorch path; default: automatic)."""
     from .reference import train
 
     summary = load_summary(golden_dir)
@@ -162,7 +164,7 @@ def check(envs, seeds=None, device: str = "cpu", iterations: int | None = None, 
             with tempfile.TemporaryDirectory() as tmp:
                 log_dir = os.path.join(log_root, env_name, f"seed{seed}") if log_root else tmp
                 train(env_name, seed, log_dir, impl="b200", device=device, iterations=iterations,
-                      num_threads=num_threads)
+                      num_threads=num_threads, engine=engine, mixed_precision=mixed_precision)
                 rows = read_curve(os.path.join(log_dir, "metrics.csv"))
             finals.append(final_reward(rows))
             finite &= _curve_finite(rows)
@@ -224,6 +226,9 @@ def main(argv=None) -> int:
     ap.add_argument("--threads", type=int, default=None)
     ap.add_argument("--golden-dir", default=str(GOLDEN_DIR))
     ap.add_argument("--log-root", default=None, help="check only: keep the curves of the run under this folder")
+    ap.add_argument("--engine", choices=("auto", "cuda", "torch"), default=None,
+                    help="check only: execution path of this framework (fused engines or the PyTorch path)")
+    ap.add_argument("--mixed-precision", action="store_true", help="check only: bf16 autocast on the PyTorch path")
     args = ap.parse_args(argv)
     if args.mode == "record":
         print(json.dumps(record(args.envs, args.seeds, args.golden_dir, args.iterations, args.threads), indent=1))
@@ -242,7 +247,8 @@ def main(argv=None) -> int:
         result = compare_runs(args.ref, args.run)
         print(json.dumps(result))
         return 0 if result["passes"] else 1
-    results = check(args.envs, args.seeds, args.device, args.iterations, args.log_root, args.golden_dir, args.threads)
+    results = check(args.envs, args.seeds, args.device, args.iterations, args.log_root, args.golden_dir, args.threads,
+                    engine=args.engine, mixed_precision=args.mixed_precision)
     for r in results:
         print(json.dumps(r))
     return 0 if all(r["passes"] for r in results) else 1

@@ -268,12 +268,23 @@ def _finish_writer(runner) -> None:
 
 
 def train(env_name: str, seed: int, log_dir: str, *, impl: str = "b200", device: str = "cpu",
-          iterations: int | None = None, spec: RunSpec | None = None, num_threads: int | None = None) -> dict:
-    """Train ``spec`` on ``env_name`` from ``seed``; the metrics land in ``log_dir/metrics.csv``. Returns a summary."""
+          iterations: int | None = None, spec: RunSpec | None = None, num_threads: int | None = None,
+          engine: str | None = None, mixed_precision: bool = False) -> dict:
+    """Train ``spec`` on ``env_name`` from ``seed``; the metrics land in ``log_dir/metrics.csv``. Returns a summary.
+
+    ``engine`` (this framework only): ``b200_cfg.engine`` of the run, e.g. ``"torch"`` for the PyTorch path on a CUDA
+    device; ``mixed_precision``: bf16 autocast on the PyTorch path."""
     if num_threads is not None:
         torch.set_num_threads(num_threads)
     os.makedirs(log_dir, exist_ok=True)
-    runner, _, spec = build_runner(env_name, seed, log_dir, spec, impl=impl, device=device)
+    cfg = None
+    if engine is not None or mixed_precision:
+        cfg = train_cfg(env_name, spec or SPECS[env_name], CSV_LOGGER if log_dir else None)
+        if engine is not None:
+            cfg["algorithm"].setdefault("b200_cfg", {})["engine"] = engine
+        if mixed_precision:
+            cfg["algorithm"]["use_mixed_precision"] = True
+    runner, _, spec = build_runner(env_name, seed, log_dir, spec, impl=impl, device=device, cfg=cfg)
     n_it = spec.iterations if iterations is None else iterations
     t0 = time.time()
     runner.learn(num_learning_iterations=n_it, init_at_random_ep_len=True)
