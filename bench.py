@@ -290,10 +290,12 @@ def timed_learn(runner, steps: int, warmup: int, world: int, counter=None) -> fl
     return ms / 1000.0
 
 
-def build_runner(impl: str, env, device: str, config: str = "1", sections: bool = False):
+def build_runner(impl: str, env, device: str, config: str = "1", sections: bool = False, b200: dict | None = None):
     cfg = train_cfg(impl, config)
     if config == "2":
         cfg = _apply_config_2(cfg)
+    if impl == "ours" and b200:
+        cfg["algorithm"].setdefault("b200_cfg", {}).update(b200)
     if sections and impl == "ours":
         cfg["algorithm"].setdefault("b200_cfg", {})["section_timing"] = True
     distill = config == "4a"
@@ -324,6 +326,8 @@ def main() -> None:
     ap.add_argument("--total-envs", type=int, default=None,
                     help="environments over all ranks (default: the configuration's; smaller for profiling)")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="1", help="benchmark configuration")
+    ap.add_argument("--b200-cfg", default=None,
+                    help="JSON object of backend options for this framework's arm (b200_cfg), e.g. '{\"model_streams\": 1}'")
     ap.add_argument("--sections", action="store_true",
                     help="also report rollout / returns / update device milliseconds (CUDA events; ours only)")
     args = ap.parse_args()
@@ -365,7 +369,8 @@ def main() -> None:
 
     inplace_obs = args.impl == "ours"
     env = make_env(n_local, device, host_noise=False, seed=rank, inplace_obs=inplace_obs, **env_kw)
-    runner = build_runner(args.impl, env, device, args.config, sections=args.sections)
+    b200 = json.loads(args.b200_cfg) if args.b200_cfg else None
+    runner = build_runner(args.impl, env, device, args.config, sections=args.sections, b200=b200)
     sampler = ClockSampler([local_rank]) if local_rank == 0 else None
     if sampler:
         sampler.__enter__()
@@ -390,7 +395,7 @@ def main() -> None:
     e2e = None
     if not args.no_e2e:
         env2 = make_env(n_local, device, host_noise=True, seed=rank, inplace_obs=inplace_obs, **env_kw)
-        runner2 = build_runner(args.impl, env2, device, args.config)
+        runner2 = build_runner(args.impl, env2, device, args.config, b200=b200)
         e2e_s = timed_learn(runner2, args.steps, args.warmup, world)
         h2d = T_STEPS * n_local * 96 * 4
         e2e = {"value": samples / e2e_s, "unit": "samples/s", "ms_per_step": e2e_s * 1e3,

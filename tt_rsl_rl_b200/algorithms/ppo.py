@@ -31,6 +31,7 @@ B200_CFG_DEFAULTS = {
     "replica_check_interval": 0,  # >0: every k updates verify that all ranks hold bit-identical parameters
     "comm_timeout_ms": 10000,  # device-side wait limit of the peer-to-peer gradient exchange
     "exchange": "auto",  # gradient exchange: "one_shot", "two_shot", or "auto" (two-shot from 4 ranks on)
+    "model_streams": 2,  # 2: actor and critic kernels on two streams where independent (fork / join); 1: serial
     "gemm_dtype": "bf16",  # GEMM operand precision of the fused path ("bf16")
     "section_timing": False,  # time rollout / returns / update with CUDA events (Perf/section_*) and NVTX ranges
 }

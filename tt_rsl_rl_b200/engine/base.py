@@ -95,6 +95,26 @@ class EngineBase:
         self.comm.allreduce_f64(local, glob, self.status)
         C.norm_update(glob[2:], 1, rows * self.world, D, mean, var, std, norm.count, until, None, False)
 
+    # ---- actor / critic concurrency ----------------------------------------------------------------------------------
+    def _init_streams(self, b200_cfg: dict) -> None:
+        """A second stream for the model whose work is independent of the other's (``b200_cfg.model_streams`` = 2)."""
+        self._side = torch.cuda.Stream(device=self.device) if int(b200_cfg.get("model_streams", 2)) > 1 else None
+
+    def _in_parallel(self, main_fn, side_fn) -> None:
+        """Run ``side_fn`` on the side stream and ``main_fn`` on the current stream, both ordered after the work
+        enqueued so far and joined before anything enqueued afterwards (a fork / join in a captured graph)."""
+        side = getattr(self, "_side", None)
+        if side is None:
+            main_fn()
+            side_fn()
+            return
+        cur = torch.cuda.current_stream(self.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            side_fn()
+        main_fn()
+        cur.wait_stream(side)
+
     # ---- graphs and status --------------------------------------------------------------------------------------------
     def _capture(self, fn):
         torch.cuda.synchronize(self.device)

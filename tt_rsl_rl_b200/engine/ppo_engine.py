@@ -420,6 +420,7 @@ class PPOEngine(EngineBase):
         self._updates_done = 0
         self.perm_override: torch.Tensor | None = None  # int32 [T*N]: explicit sample order (tests, reproducibility)
         self._init_base()
+        self._init_streams(alg.b200_cfg)
 
     # ---- learning rate -----------------------------------------------------------------------------------------------
     def learning_rate(self) -> float:
@@ -456,17 +457,21 @@ class PPOEngine(EngineBase):
         store_c = None if self.shared_obs else self.obs_c[rows]
         C.prep_obs(self._group_tensors(obs, self.groups_c), store_c, self.obs_c.stride(0), self.plan_c.x_roll,
                    self.plan_c.x_roll.shape[1], mean_c, std_c, eps_c)
-        pa = self.plan_a
-        pa.forward(pa.x_roll, pa.h_roll, N, pa.out_roll, pa.out_roll.shape[1], self.status)
+        pa, pc = self.plan_a, self.plan_c
         dist = self.actor.distribution
         std_param = None if self.hetero else (dist.std_param if dist.std_type == "scalar" else dist.log_std_param)
-        C.gaussian_sample(pa.out_roll, pa.out_roll.shape[1], N, self.A, self.hetero, self.log_std,
-                          None if std_param is None else std_param.data, self.std_range[0], self.std_range[1],
-                          self.log_std_range[0], self.log_std_range[1], self.seed, self.rng_counter, self.rng_ticket,
-                          self.st_actions[rows], self.st_mean[rows], self.st_std[rows], self.st_logp[rows],
-                          self.actions_out)
-        pc = self.plan_c
-        pc.forward(pc.x_roll, pc.h_roll, N, self.st_values[rows].view(N, 1), 1, self.status)
+
+        def actor_step():
+            pa.forward(pa.x_roll, pa.h_roll, N, pa.out_roll, pa.out_roll.shape[1], self.status)
+            C.gaussian_sample(pa.out_roll, pa.out_roll.shape[1], N, self.A, self.hetero, self.log_std,
+                              None if std_param is None else std_param.data, self.std_range[0], self.std_range[1],
+                              self.log_std_range[0], self.log_std_range[1], self.seed, self.rng_counter,
+                              self.rng_ticket, self.st_actions[rows], self.st_mean[rows], self.st_std[rows],
+                              self.st_logp[rows], self.actions_out)
+
+        # actor (with sampling) and critic are independent: two streams, joined before the actions are returned
+        self._in_parallel(actor_step,
+                          lambda: pc.forward(pc.x_roll, pc.h_roll, N, self.st_values[rows].view(N, 1), 1, self.status))
         return self.actions_out
 
     def process_env_step(self, obs, rewards, dones, extras) -> None:
@@ -590,8 +595,9 @@ class PPOEngine(EngineBase):
         C.gather_minibatch(B, start, self.total, self.perm_key, self.half_bits, idx_in, self.idx, obs_l, mean_l, std_l,
                            eps, x_l, ld_l, self.status, self.K, rows_l, perm_l, sign_l)
         adv_override = self._minibatch_advantages(self.idx, B)
-        pa.forward(pa.x_train, pa.h_train, rows_a, pa.out_train, pa.out_train.shape[1], self.status)
-        pc.forward(pc.x_train, pc.h_train, rows_c, self.value_train, 1, self.status)
+        self._in_parallel(
+            lambda: pa.forward(pa.x_train, pa.h_train, rows_a, pa.out_train, pa.out_train.shape[1], self.status),
+            lambda: pc.forward(pc.x_train, pc.h_train, rows_c, self.value_train, 1, self.status))
         dist = self.actor.distribution
         std_param = None if self.hetero else (dist.std_param if dist.std_type == "scalar" else dist.log_std_param)
         alg = self.alg
@@ -603,8 +609,7 @@ class PPOEngine(EngineBase):
                    self.d_value, self.d_value.shape[1], self.stats_partial, self.dhead_colsum, self.dvalue_colsum,
                    None if self.hetero else self.dstd_partial, self.K, self.aug, self.act_perm, self.act_sign,
                    self.mirror_coef, self.status)
-        pa.backward(rows_a, self.status)
-        pc.backward(rows_c, self.status)
+        self._in_parallel(lambda: pa.backward(rows_a, self.status), lambda: pc.backward(rows_c, self.status))
         if self.rnd is not None:
             pr, pt = self.plan_rp, self.plan_rt
             pt.forward(pr.x_train, pt.h_train, B, self.rnd_tout_train, self.R, self.status)
