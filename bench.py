@@ -352,7 +352,9 @@ def main() -> None:
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     torch.cuda.set_device(local_rank)
     device = f"cuda:{local_rank}"
-    if world > 1 and not torch.distributed.is_initialized():
+    # the unmodified reference's runner initialises the process group itself (rsl_rl/runners/on_policy_runner.py
+    # _configure_multi_gpu) and refuses an existing one; this framework's runner accepts either
+    if world > 1 and not torch.distributed.is_initialized() and args.impl != "reference":
         import datetime
 
         torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device(device),
@@ -368,7 +370,14 @@ def main() -> None:
     env_kw = conf["env"]
 
     inplace_obs = args.impl == "ours"
-    env = make_env(n_local, device, host_noise=False, seed=rank, inplace_obs=inplace_obs, **env_kw)
+    # The reference arm measures both numbers with one runner (the unmodified reference's runner initialises the
+    # process group itself and refuses a second initialisation): its environment owns the pinned noise pool from the
+    # start and switches from device noise to host noise between the two measurements. This framework's arm captures
+    # its rollout in a graph, so its end-to-end measurement gets a runner of its own.
+    one_runner = args.impl == "reference" and not args.no_e2e
+    env = make_env(n_local, device, host_noise=one_runner, seed=rank, inplace_obs=inplace_obs, **env_kw)
+    if one_runner:
+        env.host_noise = False
     b200 = json.loads(args.b200_cfg) if args.b200_cfg else None
     runner = build_runner(args.impl, env, device, args.config, sections=args.sections, b200=b200)
     sampler = ClockSampler([local_rank]) if local_rank == 0 else None
@@ -394,8 +403,12 @@ def main() -> None:
 
     e2e = None
     if not args.no_e2e:
-        env2 = make_env(n_local, device, host_noise=True, seed=rank, inplace_obs=inplace_obs, **env_kw)
-        runner2 = build_runner(args.impl, env2, device, args.config, b200=b200)
+        if one_runner:
+            env.host_noise = True
+            runner2 = runner
+        else:
+            env2 = make_env(n_local, device, host_noise=True, seed=rank, inplace_obs=inplace_obs, **env_kw)
+            runner2 = build_runner(args.impl, env2, device, args.config, b200=b200)
         e2e_s = timed_learn(runner2, args.steps, args.warmup, world)
         h2d = T_STEPS * n_local * 96 * 4
         e2e = {"value": samples / e2e_s, "unit": "samples/s", "ms_per_step": e2e_s * 1e3,

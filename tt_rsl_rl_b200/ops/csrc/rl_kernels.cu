@@ -1140,14 +1140,25 @@ __device__ __forceinline__ void publish_flag(unsigned int* const* peer_flags, in
 constexpr int kAdamThreads = 256;
 constexpr int kMaxWorldAdam = 8;
 
+// Two-shot exchange: copy elements [e0, e0 + n) of the rank-averaged gradient from their owners' reduced buffers into
+// a.grads with 16-byte peer loads (a float4 never straddles two shards); the calling block then reads them locally.
+__device__ void gather_owned(const AdamArgs& a, long long e0, long long n) {
+  const long long e1 = e0 + n;
+  const long long a0 = (e0 + 3) & ~3ll, a1 = e1 & ~3ll;  // aligned body [a0, a1)
+  for (long long e = e0 + threadIdx.x; e < (a0 < e1 ? a0 : e1); e += blockDim.x)
+    a.grads[e] = __ldcv(a.peer_reduced[(e >> 2) / a.shard4] + e);
+  for (long long v = (a0 >> 2) + threadIdx.x; v < (a1 >> 2); v += blockDim.x)
+    reinterpret_cast<float4*>(a.grads)[v] = __ldcv(reinterpret_cast<const float4*>(a.peer_reduced[v / a.shard4]) + v);
+  for (long long e = (a1 > a0 ? a1 : a0) + threadIdx.x; e < e1; e += blockDim.x)
+    a.grads[e] = __ldcv(a.peer_reduced[(e >> 2) / a.shard4] + e);
+}
+
 // Clip coefficients, adapted learning rate and Adam constants from the global squared norms `norm_sq` (identical in
-// every block and on every rank), then Adam over this block's chunks with the gradient of element e given by
-// grad_of(e). With `store_grads` the rank-averaged gradient is also written to a.grads (the two-shot path, where it
-// was not materialised locally). Block 0 finally advances the step counters, learning rates and the epoch.
-template <typename GradOf>
+// every block and on every rank), then Adam over this block's chunks reading the rank-averaged gradient from a.grads.
+// With `gather` (the two-shot exchange) each chunk's gradient is first copied there from its owners by the same
+// block. Block 0 finally advances the step counters, learning rates and the epoch.
 __device__ void adam_apply(const AdamArgs& a, const float* norm_sq, float kl, unsigned int epoch,
-                           const long long* step_s, const float* lr_old, bool exchange_ok, bool store_grads,
-                           GradOf grad_of) {
+                           const long long* step_s, const float* lr_old, bool exchange_ok, bool gather) {
   __shared__ float coef[kAdamMaxGroups], lr_s[kAdamMaxGroups];
   __shared__ float step_size_s[kAdamMaxGroups], bc2_sqrt_s[kAdamMaxGroups];
   if (threadIdx.x < a.ngroups) {
@@ -1183,21 +1194,16 @@ __device__ void adam_apply(const AdamArgs& a, const float* norm_sq, float kl, un
     const AdamChunk ch = a.chunks[c];
     const AdamTensor T = a.tensors[ch.tensor];
     const int g = T.group;
-    if (g < 0) {  // exchanged statistics (e.g. the KL mean), not parameters
-      if (store_grads)
-        for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
-          const long long e = T.offset + ch.start + k;
-          a.grads[e] = grad_of(e);
-        }
-      continue;
+    if (gather) {  // block-uniform: every thread of the block takes part before any reads the chunk
+      gather_owned(a, T.offset + ch.start, ch.count);
+      __syncthreads();
     }
+    if (g < 0) continue;  // exchanged statistics (e.g. the KL mean), not parameters
     const float step_size = step_size_s[g], bc2_sqrt = bc2_sqrt_s[g];
     const float b1 = a.beta1[g], b2 = a.beta2[g], eps = a.eps[g], cf = coef[g];
     for (int k = threadIdx.x; k < ch.count; k += blockDim.x) {
       const long long e = T.offset + ch.start + k;
-      const float raw = grad_of(e);
-      if (store_grads) a.grads[e] = raw;
-      const float grad = raw * cf;
+      const float grad = a.grads[e] * cf;
       float m = a.exp_avg[e];
       m = m + (1.0f - b1) * (grad - m);
       const float v = b2 * a.exp_avg_sq[e] + (1.0f - b2) * grad * grad;
@@ -1332,14 +1338,12 @@ __device__ void adam_two_shot(const AdamArgs& a, unsigned int epoch, const long 
     norm_sq[threadIdx.x] = t;
   }
   // the owner of element e holds its average: shard of float4 index e / 4
-  auto grad_of = [&](long long e) -> float {
-    const long long owner = (e >> 2) / a.shard4;
-    return __ldcv(a.peer_reduced[owner] + e);
-  };
   __shared__ float kl_s;
-  if (threadIdx.x == 0) kl_s = (a.adaptive && a.kl_offset >= 0 && ok) ? grad_of(a.kl_offset) : 0.f;
+  if (threadIdx.x == 0)
+    kl_s = (a.adaptive && a.kl_offset >= 0 && ok) ? __ldcv(a.peer_reduced[(a.kl_offset >> 2) / a.shard4] + a.kl_offset)
+                                                  : 0.f;
   __syncthreads();
-  adam_apply(a, norm_sq, kl_s, epoch, step_s, lr_old, ok, true, grad_of);
+  adam_apply(a, norm_sq, kl_s, epoch, step_s, lr_old, ok, true);
 }
 
 __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs a) {
@@ -1409,7 +1413,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_step_kernel(const AdamArgs 
     norm_sq[threadIdx.x] = t;
   }
   const float kl = a.adaptive ? *a.kl_mean : 0.f;
-  adam_apply(a, norm_sq, kl, epoch, step_s, lr_old, all_ok, false, [&](long long e) { return a.grads[e]; });
+  adam_apply(a, norm_sq, kl, epoch, step_s, lr_old, all_ok, false);
 }
 
 
