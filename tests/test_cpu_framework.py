@@ -663,5 +663,30 @@ def test_which_configurations_the_fused_engines_take():
     assert "single-layer" in RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss, layers=2), rnn("critic", 1), {})
     assert "multiple of 32" in RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss, hidden=20),
                                                                   rnn("critic", 1), {})
-    assert "RND" in RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss), rnn("critic", 1), {"rnd_cfg": True})
+    # RND with recurrent models runs fused (ELU networks only, as on the MLP engine)
+    assert RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss), rnn("critic", 1), {"rnd_cfg": {}}) is None
+    assert "RND" in RecurrentPPOEngine.supports_models(rnn("actor", 3, gauss), rnn("critic", 1),
+                                                       {"rnd_cfg": {"activation": "relu"}})
     assert "not fused" in PPOEngine.supports_models(rnn("actor", 3, gauss), rnn("critic", 1), {})
+
+    # distillation: MLP or recurrent students, MLP or recurrent teachers
+    from types import SimpleNamespace
+
+    from tt_rsl_rl_b200.engine import DistillationEngine, RecurrentDistillationEngine
+
+    gd = {"student": ["policy"], "teacher": ["policy"]}
+    s_rnn = RNNModel(obs, gd, "student", 3, hidden_dims=[16], distribution_cfg=gauss, rnn_type="lstm",
+                     rnn_hidden_dim=32)
+    t_rnn = RNNModel(obs, gd, "teacher", 3, hidden_dims=[16], rnn_type="gru", rnn_hidden_dim=64)
+    t_mlp = MLPModel(obs, gd, "teacher", 3, hidden_dims=[32])
+    alg = SimpleNamespace(student=s_rnn, teacher=t_rnn, loss_type="mse", optimizer_name="adam")
+    assert RecurrentDistillationEngine.unsupported_reason(alg) is None
+    alg.teacher = t_mlp
+    assert RecurrentDistillationEngine.unsupported_reason(alg) is None
+    assert "not fused" in DistillationEngine.unsupported_reason(alg)  # the MLP engine takes MLP students only
+    alg.student = MLPModel(obs, gd, "student", 3, hidden_dims=[32], distribution_cfg=gauss)
+    assert DistillationEngine.unsupported_reason(alg) is None
+    alg.teacher = t_rnn
+    assert DistillationEngine.unsupported_reason(alg) is None
+    alg.teacher = RNNModel(obs, gd, "teacher", 3, hidden_dims=[16], rnn_type="gru", rnn_hidden_dim=20)
+    assert "multiple of 32" in DistillationEngine.unsupported_reason(alg)

@@ -66,3 +66,29 @@ def test_every_index_read_from_memory_has_a_check_site():
     src = open(os.path.join(ROOT, "tt_rsl_rl_b200", "ops", "csrc", "rl_kernels.cu")).read()
     sites = sorted(int(s) for s in re.findall(r"RL_CHECK_INDEX\([^;]*,\s*(\d+)\);", src))
     assert sorted(set(sites)) == [41, 42, 43, 44, 45]
+
+
+@pytest.mark.gpu
+def test_debug_build_reports_a_bad_gather_index():
+    """Debug builds only: a sample index past the rollout is reported as site 41 and read as row 0. The storage
+    is allocated larger than the rollout, so the index stays inside the allocation even without the check."""
+    from tt_rsl_rl_b200.ops import ext
+
+    C = ext()
+    if not C.debug_bounds_enabled():
+        pytest.skip("release build: no index checks (build with TT_RSL_RL_DEBUG_BOUNDS=1)")
+    total, B, D = 64, 32, 8
+    obs = torch.randn(total + 16, D, device="cuda")
+    idx_in = torch.arange(B, dtype=torch.int32, device="cuda")
+    idx_in[5] = total + 3
+    idx_out = torch.zeros(B, dtype=torch.int32, device="cuda")
+    x = torch.zeros(B, D, dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    C.gather_minibatch(B, 0, total, None, 0, idx_in, idx_out, [obs], [None], [None], 0.0, [x], [D], status, 1, [B],
+                       [None], [None])
+    torch.cuda.synchronize()
+    st = status.tolist()
+    assert st[0] == 8 and st[1] == 41 and st[3] >= 1, st
+    torch.testing.assert_close(x[5].float(), obs[0].bfloat16().float())
+    good = [i for i in range(B) if i != 5]
+    torch.testing.assert_close(x[good].float(), obs[good].bfloat16().float())

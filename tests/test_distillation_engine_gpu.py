@@ -28,7 +28,7 @@ def test_mse_grad_matches_autograd(huber, head_cols):
     ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
     for _ in range(2):  # the ticket must re-arm itself
         C.mse_grad(pred, head_cols, target, 16, rows, A, huber, grad, ld_grad, head_cols, loss_partial, colsum,
-                   loss_acc, ticket)
+                   loss_acc, ticket, None, 0)
     p = pred[:, :A].clone().requires_grad_(True)
     fn = torch.nn.functional.huber_loss if huber else torch.nn.functional.mse_loss
     loss = fn(p, target[:, :A])
@@ -39,6 +39,35 @@ def test_mse_grad_matches_autograd(huber, head_cols):
     assert (colsum[:, A:] == 0).all()
     torch.testing.assert_close(loss_acc[0], 0.25 + 2 * loss.detach(), rtol=1e-5, atol=1e-6)
     assert int(ticket.item()) == 0
+
+
+@pytest.mark.parametrize("weight", [0.0, 37.0])
+def test_mse_grad_weighted_last_row(weight):
+    """The last row standing for ``weight`` identical rows equals autograd over the rows with that row repeated."""
+    from tt_rsl_rl_b200.ops import ext
+
+    C = ext()
+    torch.manual_seed(1)
+    rows, A, head_cols = 1001, 16, 16
+    pred = torch.randn(rows, head_cols, device="cuda")
+    target = torch.randn(rows, head_cols, device="cuda")
+    grad = torch.zeros(rows, head_cols, dtype=torch.bfloat16, device="cuda")
+    blocks = C.mse_blocks(rows)
+    loss_partial = torch.zeros(blocks, device="cuda")
+    colsum = torch.zeros(blocks, head_cols, device="cuda")
+    loss_acc = torch.zeros(1, device="cuda")
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    w = torch.full((1,), weight, device="cuda")
+    C.mse_grad(pred, head_cols, target, head_cols, rows, A, False, grad, head_cols, head_cols, loss_partial, colsum,
+               loss_acc, ticket, w, 0)
+    p = pred.clone().requires_grad_(True)
+    reps = torch.ones(rows, dtype=torch.long, device="cuda")
+    reps[-1] = int(weight)
+    loss = torch.nn.functional.mse_loss(p.repeat_interleave(reps, dim=0), target.repeat_interleave(reps, dim=0))
+    loss.backward()
+    torch.testing.assert_close(grad.float(), p.grad, rtol=1e-2, atol=1e-7)
+    torch.testing.assert_close(colsum.sum(0), p.grad.sum(0), rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(loss_acc[0], loss.detach(), rtol=1e-5, atol=1e-6)
 
 
 def _make(env, T, engine, gl=3, epochs=1, loss_type="mse", graphs=False, student=None, teacher=None):

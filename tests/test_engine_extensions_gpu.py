@@ -129,7 +129,7 @@ def test_engine_rnd_matches_torch_path(reward_norm):
         s = obs2["critic"]
         raw = torch.linalg.norm(alg_t.rnd.target(s) - alg_t.rnd.predictor(s), dim=1)
         ref = (norm_ref(raw) if reward_norm else raw) * alg_t.rnd.initial_weight
-    torch.testing.assert_close(alg_e.engine.intrinsic, ref, rtol=3e-2, atol=3e-2 * ref.abs().mean().item())
+    torch.testing.assert_close(alg_e.engine.rnd_part.intrinsic, ref, rtol=3e-2, atol=3e-2 * ref.abs().mean().item())
     assert alg_e.rnd.update_counter == T  # the schedule advanced by one rollout
     alg_e.engine.t = 0
     probe = _rollout_and_share(alg_t, alg_e, env, T, N)

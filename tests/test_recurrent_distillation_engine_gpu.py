@@ -1,0 +1,180 @@
+"""The fused distillation engine with a recurrent (GRU / LSTM) student, and with a recurrent teacher: rollout outputs
+against the PyTorch modules, one update against the PyTorch path of the same algorithm on identical data (windows of
+truncated backpropagation through time, dones inside windows, a window across the epoch boundary), graph replay
+against eager execution, and the runner with checkpoints."""
+
+import copy
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _models(obs, A, rnn_type, teacher_rnn):
+    from tt_rsl_rl_b200.models import MLPModel, RNNModel
+
+    groups = {"student": ["policy"], "teacher": ["critic"]}
+    student = RNNModel(obs, groups, "student", A, hidden_dims=[64, 32], obs_normalization=True,
+                       distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0}, rnn_type=rnn_type,
+                       rnn_hidden_dim=64)
+    if teacher_rnn:
+        teacher = RNNModel(obs, groups, "teacher", A, hidden_dims=[64, 32], obs_normalization=True,
+                           rnn_type=rnn_type, rnn_hidden_dim=96)
+    else:
+        teacher = MLPModel(obs, groups, "teacher", A, hidden_dims=[128, 64], obs_normalization=True)
+    return student, teacher
+
+
+def _alg(env, T, engine, student, teacher, gl, epochs, graphs=False, loss_type="mse"):
+    from tt_rsl_rl_b200.algorithms import Distillation
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    storage = RolloutStorage("distillation", env.num_envs, T, env.get_observations(), [env.num_actions], "cuda")
+    return Distillation(student, teacher, storage, num_learning_epochs=epochs, gradient_length=gl,
+                        learning_rate=1e-3, max_grad_norm=1.0, loss_type=loss_type, device="cuda",
+                        b200_cfg={"engine": engine, "graphs": graphs})
+
+
+def _sequence_outputs(model, obs_seq, dones_seq, state):
+    """Deterministic outputs of a recurrent model over a stored sequence from ``state`` (PyTorch, fp32)."""
+    model.reset(hidden_state=state)
+    out = []
+    with torch.no_grad():
+        for t in range(obs_seq.shape[0]):
+            out.append(model(obs_seq[t]))
+            model.reset(dones_seq[t])
+    model.reset(hidden_state=None)
+    return torch.stack(out)
+
+
+@pytest.mark.parametrize("rnn_type,teacher_rnn", [("gru", True), ("lstm", False)])
+def test_recurrent_distillation_rollout_matches_modules(rnn_type, teacher_rnn):
+    from tt_rsl_rl_b200.engine import RecurrentDistillationEngine
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+
+    torch.manual_seed(0)
+    T, N, A = 6, 512, 8
+    env = LinearGaussianVecEnv(N, obs_dim=24, num_actions=A, privileged_dim=3, device="cuda", reset_prob=0.1)
+    obs = env.get_observations()
+    student, teacher = _models(obs, A, rnn_type, teacher_rnn)
+    s_ref, t_ref = copy.deepcopy(student), copy.deepcopy(teacher)
+    alg = _alg(env, T, "cuda", student, teacher, gl=3, epochs=1)
+    assert isinstance(alg.engine, RecurrentDistillationEngine)
+    eng = alg.engine
+    for t in range(T):
+        with torch.inference_mode():
+            actions = alg.act(obs)
+            with torch.no_grad():
+                mean_ref = s_ref(obs)
+                targ_ref = t_ref(obs)
+        scale = mean_ref.abs().mean().item()
+        torch.testing.assert_close(eng.scratch_mean, mean_ref, rtol=2e-2, atol=2e-2 * scale)
+        torch.testing.assert_close(eng.targets[t * N : (t + 1) * N, :A], targ_ref, rtol=2e-2,
+                                   atol=2e-2 * targ_ref.abs().mean().item())
+        assert torch.isfinite(actions).all()
+        with torch.inference_mode():
+            obs, rew, dones, extras = env.step(actions)
+            alg.process_env_step(obs, rew, dones, extras)
+        s_ref.reset(dones)
+        t_ref.reset(dones)
+
+
+@pytest.mark.parametrize("rnn_type,gl,epochs", [("gru", 4, 2), ("lstm", 3, 2), ("gru", 5, 2)])
+def test_recurrent_distillation_update_matches_torch_path(rnn_type, gl, epochs):
+    """T = 8: gl 4 (windows inside epochs), gl 3 (a window across the epoch boundary, one leftover step), gl 5
+    (every window but the first crosses an epoch boundary or ends an epoch)."""
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+
+    torch.manual_seed(1)
+    T, N, A = 8, 1024, 8
+    env = LinearGaussianVecEnv(N, obs_dim=24, num_actions=A, privileged_dim=3, device="cuda", reset_prob=0.05)
+    obs = env.get_observations()
+    student, teacher = _models(obs, A, rnn_type, teacher_rnn=False)
+    teacher.obs_normalizer.update(torch.cat([obs["critic"]] * 4) * 2.0 + 0.5)
+    alg_t = _alg(env, T, "torch", student, teacher, gl, epochs)
+    alg_e = _alg(env, T, "cuda", copy.deepcopy(student), copy.deepcopy(teacher), gl, epochs)
+    assert alg_e.engine is not None
+    with torch.inference_mode():
+        for _ in range(T):
+            actions = alg_t.act(obs)
+            obs, rew, dones, extras = env.step(actions)
+            alg_t.process_env_step(obs, rew, dones, extras)
+    st = alg_t.storage
+    assert st.dones.sum() > 0
+    alg_e.engine.load_rollout(st)
+    obs_seq, dones_seq = st.observations, st.dones.squeeze(-1)
+    old = _sequence_outputs(alg_t.student, obs_seq, dones_seq, None)
+    loss_t = alg_t.update()
+    loss_e = alg_e.update()
+    assert abs(loss_e["behavior"] - loss_t["behavior"]) <= 2e-2 * abs(loss_t["behavior"])
+    for alg in (alg_t, alg_e):
+        alg.student.obs_normalizer.eval()
+    new_t = _sequence_outputs(alg_t.student, obs_seq, dones_seq, None)
+    new_e = _sequence_outputs(alg_e.student, obs_seq, dones_seq, None)
+    dev = ((new_e - new_t).norm() / (new_t - old).norm()).item()
+    assert dev < 2e-2, dev
+    windows = epochs * T // gl
+    assert int(alg_e.engine.step[0].item()) == windows
+    # the state the next update starts from (and the rollout continues from)
+    hs = alg_t.last_student_hidden_state
+    h_ref = hs[0] if isinstance(hs, tuple) else hs
+    torch.testing.assert_close(alg_e.engine.h_last, h_ref[0], rtol=5e-2, atol=5e-2 * h_ref.abs().mean().item())
+    torch.testing.assert_close(alg_e.engine.snet.h, alg_e.engine.h_last)
+
+
+def test_recurrent_distillation_graph_replay_equals_eager():
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+
+    T, N, A = 6, 512, 8
+    results = []
+    for graphs in (False, True):
+        torch.manual_seed(3)
+        env = LinearGaussianVecEnv(N, obs_dim=24, num_actions=A, privileged_dim=3, device="cuda", reset_prob=0.05)
+        obs = env.get_observations()
+        student, teacher = _models(obs, A, "gru", teacher_rnn=True)
+        alg = _alg(env, T, "cuda", student, teacher, gl=4, epochs=2, graphs=graphs)
+        losses = []
+        for _ in range(3):
+            with torch.inference_mode():
+                for _ in range(T):
+                    actions = alg.act(obs)
+                    obs, rew, dones, extras = env.step(actions)
+                    alg.process_env_step(obs, rew, dones, extras)
+            losses.append(alg.update()["behavior"])
+        results.append((alg.engine.flat.clone(), losses, alg.engine.h_last.clone()))
+    assert torch.equal(results[0][0], results[1][0])
+    assert results[0][1] == results[1][1]
+    assert torch.equal(results[0][2], results[1][2])
+
+
+def test_recurrent_distillation_runner_checkpoint(tmp_path):
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.runners import DistillationRunner
+
+    torch.manual_seed(0)
+    env = LinearGaussianVecEnv(512, obs_dim=24, num_actions=8, privileged_dim=3, device="cuda", reset_prob=0.02)
+    cfg = {
+        "num_steps_per_env": 8, "save_interval": 1000, "obs_groups": {"student": ["policy"], "teacher": ["critic"]},
+        "algorithm": {"class_name": "Distillation", "num_learning_epochs": 2, "gradient_length": 4,
+                      "b200_cfg": {"engine": "cuda"}},
+        "student": {"class_name": "RNNModel", "hidden_dims": [64, 32], "obs_normalization": True, "rnn_type": "lstm",
+                    "rnn_hidden_dim": 64,
+                    "distribution_cfg": {"class_name": "GaussianDistribution", "init_std": 0.5}},
+        "teacher": {"class_name": "RNNModel", "hidden_dims": [64, 32], "obs_normalization": True, "rnn_type": "gru",
+                    "rnn_hidden_dim": 64},
+    }
+    runner = DistillationRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    runner.alg.teacher_loaded = True
+    assert runner.alg.engine is not None
+    runner.learn(6)
+    eng = runner.alg.engine
+    assert torch.isfinite(eng.flat).all()
+    assert int(eng.step[0].item()) == 6 * 2 * 8 // 4
+    path = str(tmp_path / "s.pt")
+    runner.save(path)
+    runner2 = DistillationRunner(env, copy.deepcopy(cfg), log_dir=None, device="cuda")
+    runner2.load(path)
+    torch.testing.assert_close(runner2.alg.engine.flat, eng.flat)
+    torch.testing.assert_close(runner2.alg.engine.exp_avg, eng.exp_avg)
+    runner2.learn(1)

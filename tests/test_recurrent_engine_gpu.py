@@ -117,3 +117,78 @@ def test_recurrent_runner_learns_with_graphs(rnn_type, tmp_path):
     runner2.load(path)
     torch.testing.assert_close(runner2.alg.engine.flat, eng.flat)
     runner2.learn(1)
+
+
+@pytest.mark.parametrize("rnn_type", ["gru", "lstm"])
+def test_recurrent_engine_rnd_matches_torch_path(rnn_type):
+    """RND with recurrent models: the intrinsic reward of a fused rollout step, and one update against the PyTorch
+    path, whose predictor loss runs over the minibatch's zero-padded trajectories (the padded entries share the
+    normalised zero state; the engine weights one such row by their count)."""
+    from tt_rsl_rl_b200.algorithms import PPO
+    from tt_rsl_rl_b200.env import LinearGaussianVecEnv
+    from tt_rsl_rl_b200.storage import RolloutStorage
+
+    torch.manual_seed(4)
+    T, N = 12, 512
+    env = LinearGaussianVecEnv(N, obs_dim=24, num_actions=8, privileged_dim=3, device="cuda", reset_prob=0.05)
+    obs = env.get_observations()
+    actor, critic = _models(obs, rnn_type)
+    groups = {"actor": ["policy"], "critic": ["critic"], "rnd_state": ["critic"]}
+    rnd_cfg = {"num_states": obs["critic"].shape[1], "obs_groups": groups, "num_outputs": 16,
+               "predictor_hidden_dims": [64, 32], "target_hidden_dims": [64, 32], "weight": 0.5,
+               "state_normalization": True}
+    kw = dict(num_learning_epochs=2, num_mini_batches=4, rnd_cfg=rnd_cfg)
+    storage = RolloutStorage("rl", N, T, obs, [env.num_actions], "cuda")
+    alg_t = PPO(actor, critic, storage, device="cuda", b200_cfg={"engine": "torch"}, **copy.deepcopy(kw))
+    alg_e = PPO(copy.deepcopy(actor), copy.deepcopy(critic), None, device="cuda",
+                b200_cfg={"engine": "cuda", "graphs": False}, num_steps_per_env=T, num_envs=N, **copy.deepcopy(kw))
+    from tt_rsl_rl_b200.engine import RecurrentPPOEngine
+
+    assert isinstance(alg_e.engine, RecurrentPPOEngine), alg_e.engine
+    # a state normaliser away from identity, so the padded entries' normalised zero state is not zero
+    sn = alg_t.rnd.state_normalizer
+    D = sn._mean.numel()
+    sn._mean.copy_(torch.linspace(-0.5, 0.5, D, device="cuda").view_as(sn._mean))
+    sn._std.copy_(torch.linspace(0.5, 1.5, D, device="cuda").view_as(sn._std))
+    sn._var.copy_(sn._std**2)
+    alg_e.rnd.load_state_dict(alg_t.rnd.state_dict())
+    alg_e.engine.sync_from_torch()
+
+    # intrinsic reward of one fused step against the PyTorch networks on the same observations
+    with torch.inference_mode():
+        actions = alg_e.act(obs)
+        obs2, rew, dones, extras = env.step(actions)
+        alg_e.process_env_step(obs2, rew, dones, extras)
+        s = sn(obs2["critic"])
+        ref = torch.linalg.norm(alg_t.rnd.target(s) - alg_t.rnd.predictor(s), dim=1) * alg_t.rnd.initial_weight
+    torch.testing.assert_close(alg_e.engine.rnd_part.intrinsic, ref, rtol=3e-2, atol=3e-2 * ref.abs().mean().item())
+    alg_e.engine.t = 0
+
+    obs = env.get_observations()
+    for it in range(2):
+        with torch.inference_mode():
+            for _ in range(T):
+                actions = alg_t.act(obs)
+                obs, rew, dones, extras = env.step(actions)
+                alg_t.process_env_step(obs, rew, dones, extras)
+            alg_t.compute_returns(obs)
+        if it == 0:
+            storage.clear()
+    st = storage
+    assert st.dones[:-1].sum() > 0  # padded entries exist
+    sa, sc = st.saved_hidden_state_a, st.saved_hidden_state_c
+    h0a, h0c = sa[0][0, 0].clone(), sc[0][0, 0].clone()
+    c0a = sa[1][0, 0].clone() if len(sa) > 1 else None
+    c0c = sc[1][0, 0].clone() if len(sc) > 1 else None
+    alg_e.engine.load_rollout(st, h0a, h0c, c0a, c0c)
+    probe = sn(st.observations.flatten(0, 1)["critic"][:4096]).detach()
+    with torch.no_grad():
+        p_old = alg_t.rnd.predictor(probe).clone()
+    loss_t = alg_t.update()
+    loss_e = alg_e.update()
+    with torch.no_grad():
+        p_t, p_e = alg_t.rnd.predictor(probe), alg_e.rnd.predictor(probe)
+    assert ((p_e - p_t).norm() / (p_t - p_old).norm()).item() < 0.1
+    for k in ("value", "surrogate", "entropy", "rnd"):
+        assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=3e-3), (k, loss_e[k], loss_t[k])
+    assert int(alg_e.engine.step[2].item()) == 2 * 4

@@ -122,3 +122,65 @@ def test_cell_backward_matches_autograd(lstm):
                      cs_gi, cs_gh, True)
     for t, b in zip([t for t in (cs_gi, cs_gh) if t is not None], before):
         torch.testing.assert_close(t, 2 * b, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("lstm", [False, True])
+@pytest.mark.parametrize("H", [128, 256])
+def test_fused_step_matches_gemm_plus_cell(lstm, H):
+    """One launch (hidden GEMM with the cell in its epilogue) equals the tcgen05 GEMM followed by the cell kernel, on
+    env-major strided views where the next step's state goes to the next slot of the input state's buffer."""
+    from tt_rsl_rl_b200.ops import gemm as Gm
+
+    torch.manual_seed(1)
+    rows, T, t = 1000, 3, 1
+    G, S = (4, 5) if lstm else (3, 4)
+    GH = G * H
+    f32 = dict(device="cuda", dtype=torch.float32)
+    hbf_buf = (torch.randn(rows, T, H, **f32) * 0.5).bfloat16()  # input state at slot t, next state to slot t + 1
+    h_buf = torch.randn(rows, T, H, **f32) * 0.5
+    c_buf = torch.randn(rows, T, H, **f32) if lstm else None
+    gi_buf = torch.randn(rows, T, GH, **f32)
+    w = (torch.randn(GH, H, **f32) / H**0.5).bfloat16()
+    b = torch.randn(GH, **f32) * 0.1
+    done = (torch.rand(rows, device="cuda") < 0.2).float()
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+
+    def view(buf, slot):
+        return buf.view(-1)[slot * buf.shape[2] :]
+
+    outs = {}
+    for fused in (True, False):
+        hb = hbf_buf.clone()
+        hout_bf = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
+        nh = torch.zeros(rows, T, H, **f32)
+        nc = torch.zeros(rows, T, H, **f32) if lstm else None
+        save = torch.zeros(rows, S * H, **f32)
+        c_in = (view(c_buf, t), T * H) if lstm else (None, 0)
+        c_next = (view(nc, t + 1), T * H) if lstm else (None, 0)
+        if fused:
+            C().rnn_step_fused(rows, H, lstm, view(hb, t), T * H, w, H, b, view(gi_buf, t), T * GH, view(h_buf, t),
+                               T * H, *c_in, None, 0, hout_bf, H, None, 0, done, view(nh, t + 1), T * H,
+                               view(hb, t + 1), T * H, *c_next, save, S * H, status)
+        else:
+            gh = torch.zeros(rows, GH, **f32)
+            Gm.gemm(view(hb, t), T * H, False, w, H, False, rows, GH, H, Gm.EPI_F32, gh, GH, bias=b, status=status)
+            C().rnn_cell_fwd(rows, H, lstm, view(gi_buf, t), T * GH, gh, GH, view(h_buf, t), T * H, *c_in, None, 0,
+                             hout_bf, H, None, 0, done, view(nh, t + 1), T * H, view(hb, t + 1), T * H, *c_next, save,
+                             S * H)
+        torch.cuda.synchronize()
+        outs[fused] = (hout_bf.float(), nh[:, t + 1], hb[:, t + 1].float(), save, nc[:, t + 1] if lstm else None,
+                       hb[:, t].float(), hb[:, t - 1].float())
+    assert int(status[0]) == 0
+    for a_, b_ in zip(outs[True], outs[False]):
+        if a_ is not None:
+            torch.testing.assert_close(a_, b_, rtol=1e-5, atol=1e-5)
+    # against fp32 PyTorch on the same bf16 operands
+    gh_ref = hbf_buf[:, t].float() @ w.float().T + b
+    ref_h, ref_c = _step_ref(lstm, gi_buf[:, t], gh_ref, h_buf[:, t], c_buf[:, t] if lstm else None)
+    keep = (1 - done)[:, None]
+    torch.testing.assert_close(outs[True][1], ref_h * keep, rtol=1e-4, atol=1e-4)
+    if lstm:
+        torch.testing.assert_close(outs[True][4], ref_c * keep, rtol=1e-4, atol=1e-4)
+    # the input slot and the slot before it are untouched
+    torch.testing.assert_close(outs[True][5], hbf_buf[:, t].float())
+    torch.testing.assert_close(outs[True][6], hbf_buf[:, t - 1].float())

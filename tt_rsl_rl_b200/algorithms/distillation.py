@@ -11,9 +11,10 @@ window's gradient is the sum of its steps' gradients; steps that do not fill a l
 student carries its hidden state through the rollout, resets it at dones, and is detached at every window boundary
 (truncated backpropagation through time).
 
-Execution: on CUDA with MLP student and teacher :class:`tt_rsl_rl_b200.engine.DistillationEngine` runs the step in
-the framework's kernels (forward / backward GEMMs with persistent fp32 gradient sums, fused clip + Adam); otherwise
-:class:`_LossWindow` below drives autograd.
+Execution: on CUDA :class:`tt_rsl_rl_b200.engine.DistillationEngine` (MLP student) or
+:class:`tt_rsl_rl_b200.engine.RecurrentDistillationEngine` (GRU / LSTM student), with an MLP or recurrent teacher,
+runs the step in the framework's kernels (forward / backward GEMMs with persistent fp32 gradient sums, fused clip +
+Adam); otherwise :class:`_LossWindow` below drives autograd.
 """
 
 from __future__ import annotations
@@ -123,11 +124,13 @@ class Distillation:
         mode = self.b200_cfg["engine"]
         if mode == "torch" or torch.device(self.device).type != "cuda":
             return None
-        from ..engine.distillation_engine import DistillationEngine
+        from ..engine.distillation_engine import DistillationEngine, RecurrentDistillationEngine
+        from ..models import RNNModel
 
-        reason = DistillationEngine.unsupported_reason(self)
+        cls = RecurrentDistillationEngine if isinstance(self.student, RNNModel) else DistillationEngine
+        reason = cls.unsupported_reason(self)
         if reason is None:
-            return DistillationEngine(self)
+            return cls(self)
         if mode == "cuda":
             raise ValueError(f"The fused CUDA distillation engine does not support this configuration: {reason}")
         return None

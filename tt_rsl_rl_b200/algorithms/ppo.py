@@ -30,8 +30,9 @@ B200_CFG_DEFAULTS = {
     "graphs": True,  # capture act / GAE / minibatch steps in CUDA graphs
     "replica_check_interval": 0,  # >0: every k updates verify that all ranks hold bit-identical parameters
     "comm_timeout_ms": 10000,  # device-side wait limit of the peer-to-peer gradient exchange
-    "exchange": "auto",  # gradient exchange: "one_shot", "two_shot", or "auto" (two-shot from 4 ranks on)
+    "exchange": "auto",  # gradient exchange: "one_shot", "two_shot", or "auto" (one shot)
     "model_streams": 2,  # 2: actor and critic kernels on two streams where independent (fork / join); 1: serial
+    "rnn_fused_step": True,  # recurrent training steps as one launch (hidden GEMM with the cell in its epilogue)
     "gemm_dtype": "bf16",  # GEMM operand precision of the fused path ("bf16")
     "section_timing": False,  # time rollout / returns / update with CUDA events (Perf/section_*) and NVTX ranges
 }

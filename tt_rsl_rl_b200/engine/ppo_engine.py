@@ -32,24 +32,15 @@ import torch
 from ..modules import GaussianDistribution, HeteroscedasticGaussianDistribution
 from ..ops import ext
 from ..utils.timer import HostTransfers
-from .base import EngineBase, elu_mlp_reason, elu_stack_reason
+from .base import EngineBase, elu_mlp_reason
 from .mlp_plan import MLPPlan
+from .rnd_part import RndPart, rnd_reason
 
 _GROUP_ACTOR = 0
 _GROUP_CRITIC = 1
 _GROUP_RND = 2
 _TAIL = 5  # exchanged statistics after the parameters: surrogate, value, entropy, kl, symmetry (minibatch means)
 _MAX_COPIES = 8
-
-
-def _rnd_reason(rnd) -> str | None:
-    for name in ("predictor", "target"):
-        reason = elu_stack_reason(getattr(rnd, name))
-        if reason:
-            return f"RND {name}: {reason}"
-    if rnd.num_outputs > 64 or rnd.num_states > 1024:
-        return "RND network too wide"
-    return None
 
 
 def _padded_rows(rows: int, dim: int, device) -> torch.Tensor:
@@ -114,7 +105,7 @@ class PPOEngine(EngineBase):
         if reason is not None:
             return reason
         if alg.rnd is not None:
-            reason = _rnd_reason(alg.rnd)
+            reason = rnd_reason(alg.rnd)
             if reason is not None:
                 return reason
         if alg.symmetry is not None:
@@ -262,13 +253,13 @@ class PPOEngine(EngineBase):
         self.plan_c = MLPPlan(self.critic.mlp, self.Dc, self.N, self.rows_c_max, dev, self.sm_count)
         self.head_cols = self.plan_a.head_cols
         self.plans = [self.plan_a, self.plan_c]
+        self.rnd_part = None
         if self.rnd is not None:
-            self.Dr = self.rnd.num_states
-            self.R = self.rnd.num_outputs
-            self.groups_r = list(self.rnd.obs_groups["rnd_state"])
-            self.plan_rp = MLPPlan(self.rnd.predictor, self.Dr, self.N, self.B_max, dev, self.sm_count)
-            self.plan_rt = MLPPlan(self.rnd.target, self.Dr, self.N, self.B_max, dev, self.sm_count, grads=False)
-            self.plans += [self.plan_rp, self.plan_rt]
+            self.rnd_part = RndPart(self, self.rnd, self.N, self.T, self.B_max, dev, self.sm_count)
+            self.Dr = self.rnd_part.Dr
+            self.groups_r = self.rnd_part.groups
+            self.plan_rp = self.rnd_part.plan_p
+            self.plans += self.rnd_part.plans
         for plan in self.plans:
             plan.refresh_shadows()
 
@@ -298,21 +289,8 @@ class PPOEngine(EngineBase):
                 self.obs_r = self.obs_c
             else:
                 self.obs_r = _padded_rows(T * N, self.Dr, dev)
-            self.intrinsic = torch.zeros(N, **f32)
-            self.intrinsic_for_logger = self.intrinsic
-            alg.intrinsic_rewards = self.intrinsic
-            self.rnd_w = torch.zeros(T, **f32)  # per-step intrinsic weight of the current rollout
-            self.rnd_tout_roll = torch.zeros(N, self.R, **f32)
-            self.rnd_pout_roll = torch.zeros(N, self.R, **f32)
-            self.rnd_tout_train = torch.zeros(self.B_max, self.R, **f32)
-            self.rnd_blocks = ext().mse_blocks(self.B_max)
-            self.rnd_loss_partial = torch.zeros(self.rnd_blocks, **f32)
-            self.rnd_colsum = torch.zeros(self.rnd_blocks, self.R, **f32)
-            self.rnd_loss_acc = torch.zeros(1, **f32)
-            self.rnd_ticket = torch.zeros(1, dtype=torch.int32, device=dev)
-            # reward normalisation: per-environment discounted sum of the raw intrinsic reward and its running std
-            self.rnd_reward_norm = bool(self.rnd.reward_normalization)
-            self.rnd_disc = torch.zeros(N, **f32) if self.rnd_reward_norm else None
+            self.intrinsic_for_logger = self.rnd_part.intrinsic
+            alg.intrinsic_rewards = self.rnd_part.intrinsic
 
         # ---- minibatch buffers ----
         B = self.B_max
@@ -336,7 +314,7 @@ class PPOEngine(EngineBase):
         seg.update(self.plan_a.reduce_segments(self.dhead_colsum, self.loss_blocks))
         seg.update(self.plan_c.reduce_segments(self.dvalue_colsum, self.loss_blocks))
         if self.rnd is not None:
-            seg.update(self.plan_rp.reduce_segments(self.rnd_colsum, self.rnd_blocks))
+            seg.update(self.rnd_part.reduce_segments())
         if not self.hetero:
             std_p = dist.std_param if dist.std_type == "scalar" else dist.log_std_param
             seg[id(std_p)] = (self.dstd_partial, self.loss_blocks, A)
@@ -399,22 +377,15 @@ class PPOEngine(EngineBase):
         self.adam_eps_g = [self.adam_eps] * 2
         self.adam_lr_index = [0, 0]
         if self.rnd is not None:
-            rg = self.rnd.optimizer.param_groups[0]
-            rb1, rb2 = rg.get("betas", (0.9, 0.999))
-            if float(rg.get("weight_decay", 0.0)) != 0.0 or rg.get("amsgrad", False):
-                raise ValueError("fused Adam supports weight_decay=0 and amsgrad=False")
-            self.adam_beta1.append(float(rb1))
-            self.adam_beta2.append(float(rb2))
-            self.adam_eps_g.append(float(rg.get("eps", 1e-8)))
+            rb1, rb2, reps = self.rnd_part.adam_hparams()
+            self.adam_beta1.append(rb1)
+            self.adam_beta2.append(rb2)
+            self.adam_eps_g.append(reps)
             self.adam_lr_index.append(2)
 
         # ---- normaliser statistics scratch ----
         self._alloc_norm_scratch("actor", self.total, self.Da)
         self._alloc_norm_scratch("critic", self.total, self.Dc)
-        if self.rnd is not None:
-            self._alloc_norm_scratch("rnd", self.total, self.Dr)
-            if self.rnd_reward_norm:
-                self._alloc_norm_scratch("rnd_reward", self.N, 1)
         self.use_graphs = bool(alg.b200_cfg["graphs"])
         self._update_graph = None
         self._updates_done = 0
@@ -444,7 +415,7 @@ class PPOEngine(EngineBase):
         rows = slice(t * N, (t + 1) * N)
         C = ext()
         if self.rnd is not None and t == 0 and not torch.cuda.is_current_stream_capturing():
-            self._rnd_prepare()
+            self.rnd_part.prepare()
         if self.rnd is not None and self.obs_r is not self.obs_a and self.obs_r is not self.obs_c:
             # the RND state groups are stored on their own (normalised copy goes to a scratch buffer)
             C.prep_obs(self._group_tensors(obs, self.groups_r), self.obs_r[rows], self.obs_r.stride(0),
@@ -482,47 +453,14 @@ class PPOEngine(EngineBase):
             timeouts = timeouts.to(self.device).reshape(-1)
         intrinsic = None
         if self.rnd is not None:
-            self._rnd_intrinsic(obs, t)
-            intrinsic = self.intrinsic
+            intrinsic = self.rnd_part.intrinsic_reward(self, obs, t)
         ext().process_step(rewards.reshape(-1).float(), intrinsic, dones.reshape(-1), timeouts, self.st_values[rows],
                            self.alg.gamma, self.st_rewards[rows], self.st_dones[rows], self.nonfinite)
         self.t += 1
 
-    # ---- RND -----------------------------------------------------------------------------------------------------------
-    def _rnd_prepare(self) -> None:
-        """Advance the host-side RND step counter by one rollout and upload the per-step intrinsic weights."""
-        r = self.rnd
-        weights = []
-        for _ in range(self.T):
-            r.update_counter += 1
-            r.weight = r.current_weight(r.update_counter)
-            weights.append(float(r.weight))
-        self.rnd_w.copy_(torch.tensor(weights, dtype=torch.float32))
-
     def _before_replay(self) -> None:
         if self.rnd is not None:
-            self._rnd_prepare()
-
-    def _rnd_intrinsic(self, obs, t: int) -> None:
-        """Intrinsic reward of the post-step observations: weight * || target(s) - predictor(s) ||."""
-        C = ext()
-        pr, pt = self.plan_rp, self.plan_rt
-        mean_r, std_r, eps_r = self._norm_views(self.rnd.state_normalizer)
-        C.prep_obs(self._group_tensors(obs, self.groups_r), None, self.Dr, pr.x_roll, pr.x_roll.shape[1], mean_r,
-                   std_r, eps_r)
-        pt.forward(pr.x_roll, pt.h_roll, self.N, self.rnd_tout_roll, self.R, self.status)
-        pr.forward(pr.x_roll, pr.h_roll, self.N, self.rnd_pout_roll, self.R, self.status)
-        w = self.rnd_w[t : t + 1]
-        if not self.rnd_reward_norm:
-            C.rnd_intrinsic(self.rnd_tout_roll, self.R, self.rnd_pout_roll, self.R, self.N, self.R, w, self.intrinsic,
-                            None, 0.0)
-            return
-        # normalised: raw distance, discounted sum, running std of the sum (global over ranks), then weight / std
-        rn = self.rnd.reward_normalizer
-        C.rnd_intrinsic(self.rnd_tout_roll, self.R, self.rnd_pout_roll, self.R, self.N, self.R, w, self.intrinsic,
-                        self.rnd_disc, rn.disc_avg.gamma)
-        self._norm_module_update("rnd_reward", rn.emp_norm, rn.training, self.rnd_disc.view(self.N, 1), self.N, 1)
-        C.rnd_reward_scale(self.intrinsic, self.N, w, rn.emp_norm._std.view(-1))
+            self.rnd_part.prepare()
 
     def compute_returns(self, obs) -> None:
         C = ext()
@@ -546,10 +484,7 @@ class PPOEngine(EngineBase):
             for buf in (self.stats_partial, self.dhead_colsum, self.dvalue_colsum, self.dstd_partial):
                 buf[used:].zero_()
         if self.rnd is not None:
-            used = C.mse_blocks(B)
-            if used < self.rnd_blocks:
-                self.rnd_loss_partial[used:].zero_()
-                self.rnd_colsum[used:].zero_()
+            self.rnd_part.zero_tails(B)
 
     def _minibatch_advantages(self, idx: torch.Tensor, n: int):
         """normalize_advantage_per_mini_batch: (adv[idx] - mean) / (std + 1e-8) over the minibatch, else None."""
@@ -611,13 +546,7 @@ class PPOEngine(EngineBase):
                    self.mirror_coef, self.status)
         self._in_parallel(lambda: pa.backward(rows_a, self.status), lambda: pc.backward(rows_c, self.status))
         if self.rnd is not None:
-            pr, pt = self.plan_rp, self.plan_rt
-            pt.forward(pr.x_train, pt.h_train, B, self.rnd_tout_train, self.R, self.status)
-            pr.forward(pr.x_train, pr.h_train, B, pr.out_train, self.R, self.status)
-            C.mse_grad(pr.out_train, self.R, self.rnd_tout_train, self.R, B, self.R, False, pr.d_head,
-                       pr.d_head.shape[1], self.R, self.rnd_loss_partial, self.rnd_colsum, self.rnd_loss_acc,
-                       self.rnd_ticket)
-            pr.backward(B, self.status)
+            self.rnd_part.train(B, self.status)
         C.reduce_segments(self.reduce_plan, self.reduce_nseg, self.reduce_chunks, self.send[0], self.send[1],
                           self.epoch, False)
         adaptive = alg.desired_kl is not None and alg.schedule == "adaptive"
@@ -636,14 +565,13 @@ class PPOEngine(EngineBase):
         self._normalizer_update("actor", self.actor, self.obs_a, self.total, self.Da)
         self._normalizer_update("critic", self.critic, self.obs_c, self.total, self.Dc)
         if self.rnd is not None:
-            self._norm_module_update("rnd", self.rnd.state_normalizer, self.rnd.state_normalization, self.obs_r,
-                                     self.total, self.Dr)
+            self.rnd_part.normalizer_update(self, self.obs_r, self.total)
 
     def _update_body(self) -> None:
         ext().counter_add(self.perm_key, 1)
         self.loss_acc.zero_()
         if self.rnd is not None:
-            self.rnd_loss_acc.zero_()
+            self.rnd_part.loss_acc.zero_()
         for _ in range(self.E):
             for i in range(self.M):
                 self._minibatch(i)
@@ -662,7 +590,7 @@ class PPOEngine(EngineBase):
         self._check_status()
         out = {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
         if self.rnd is not None:
-            out["rnd"] = float(HostTransfers.read(self.rnd_loss_acc, "rnd_loss")[0]) / n
+            out["rnd"] = float(HostTransfers.read(self.rnd_part.loss_acc, "rnd_loss")[0]) / n
         if self.sym is not None:
             out["symmetry"] = stats[4]
         return out
@@ -734,7 +662,7 @@ class PPOEngine(EngineBase):
     # ---- data parallel ------------------------------------------------------------------------------------------------
     def broadcast_parameters(self) -> None:
         """Make every rank start from rank 0's parameters and normaliser buffers."""
-        extra = [] if self.rnd is None else [self.rnd.target, self.rnd.state_normalizer, self.rnd.reward_normalizer]
+        extra = [] if self.rnd is None else self.rnd_part.broadcast_modules()
         if self.comm is not None:
             self.comm.broadcast_(self.flat, status=self.status)
             for model in [self.actor, self.critic] + ([self.rnd.predictor] if self.rnd is not None else []):

@@ -32,8 +32,10 @@ from ..ops import gemm as G
 from ..utils.timer import HostTransfers
 from .base import EngineBase, elu_mlp_reason
 from .mlp_plan import MLPPlan, pad8, wgrad_splits
+from .rnd_part import RndPart, rnd_reason
 
 _TAIL = 5  # exchanged statistics after the parameters: surrogate, value, entropy, kl, (unused)
+_GROUP_RND = 2
 
 
 def _view_from(t: torch.Tensor, offset: int) -> torch.Tensor:
@@ -41,10 +43,32 @@ def _view_from(t: torch.Tensor, offset: int) -> torch.Tensor:
     return t.view(-1)[offset:]
 
 
+def rnn_model_reason(name: str, m) -> str | None:
+    """None if ``m`` is an RNNModel the fused recurrent kernels cover (one unidirectional GRU / LSTM layer with
+    biases, hidden size a multiple of 32 up to 1024, a Linear / ELU head), else the reason."""
+    from ..models import RNNModel
+
+    if type(m) is not RNNModel:
+        return f"{name} type {type(m).__name__} is not the recurrent model"
+    rnn = m.rnn.rnn
+    if not isinstance(rnn, (nn.GRU, nn.LSTM)):
+        return f"{name} recurrent layer {type(rnn).__name__}"
+    if rnn.num_layers != 1 or not rnn.bias or rnn.bidirectional or getattr(rnn, "proj_size", 0):
+        return f"{name}: only single-layer, unidirectional RNNs with biases are fused"
+    if rnn.hidden_size % 32 or rnn.hidden_size > 1024:
+        return f"{name}: hidden size must be a multiple of 32 up to 1024"
+    reason = elu_mlp_reason(m)
+    if reason:
+        return f"{name}: {reason}"
+    if m.obs_dim > 1024:
+        return f"{name} observation width {m.obs_dim} too large"
+    return None
+
+
 class _RecurrentNet:
     """Device plan of one RNNModel: bf16 weight shadows, rollout state, env-major minibatch buffers, the MLP head."""
 
-    def __init__(self, model, N: int, T: int, Be_max: int, device, sm_count: int) -> None:
+    def __init__(self, model, N: int, T: int, Be_max: int, device, sm_count: int, fused_step: bool = True) -> None:
         rnn = model.rnn.rnn
         self.model = model
         self.lstm = isinstance(rnn, nn.LSTM)
@@ -52,6 +76,8 @@ class _RecurrentNet:
         self.G = 4 if self.lstm else 3
         self.S = 5 if self.lstm else 4
         self.GH = self.G * H
+        # training steps as one launch: the hidden GEMM with the cell in its epilogue (H a multiple of 64)
+        self.fused_step = bool(fused_step) and H % 64 == 0
         self.D = model.obs_dim
         self.Dp = pad8(self.D)
         self.T, self.N, self.Be_max = T, N, Be_max
@@ -137,38 +163,73 @@ class _RecurrentNet:
         C.rnn_cell_fwd(N, H, self.lstm, self.gi_roll, GH, self.gh_roll, GH, self.h, H, self.c, H, h_out, H, hbf_out, H,
                        c_out, H, None, None, 0, None, 0, None, 0, None, 0)
 
-    # ---- minibatch --------------------------------------------------------------------------------------------------
+    # ---- sequences --------------------------------------------------------------------------------------------------
+    # A sequence is L steps of Be environments. Its rows are env-major (row e * L + t: PPO minibatches, contiguous env
+    # ranges of the rollout) or time-major (row t * Be + e: distillation windows, contiguous step ranges). ``at``
+    # gives the first element of step t's rows in a buffer of row width W, and the row pitch of that step.
+    @staticmethod
+    def _layout(Be: int, L: int, time_major: bool):
+        if time_major:
+            return lambda buf, t, W: (_view_from(buf, t * Be * W), W)
+        return lambda buf, t, W: (_view_from(buf, t * W), L * W)
+
     def forward_sequence(self, lo: int, Be: int, dones_tm: torch.Tensor, head_out: torch.Tensor, head_ld: int,
-                         status) -> None:
+                         status, *, L: int | None = None, t0: int = 0, time_major: bool = False, x=None, init=None,
+                         carry=None) -> None:
+        """Forward of environments ``lo .. lo + Be - 1`` over steps ``t0 .. t0 + L - 1`` (dones read at those absolute
+        steps of ``dones_tm`` [T_rollout, N]). ``x``: the sequence's normalised input rows (default: the env-major
+        rollout inputs); ``init``: (h, c) state before the first step (default: the state stored at the rollout's
+        first step); ``carry``: (h, h_bf16, c) receiving the state after the last step, masked by its dones."""
         C = ext()
-        T, N, H, GH, S = self.T, self.N, self.H, self.GH, self.S
-        R = Be * T
-        x = self.x[lo * T : (lo + Be) * T]
+        N, H, GH, S = self.N, self.H, self.GH, self.S
+        L = self.T if L is None else L
+        R = Be * L
+        at = self._layout(Be, L, time_major)
+        if x is None:
+            x = self.x[lo * L : (lo + Be) * L]
         G.gemm(x, self.Dp, False, self.w_ih_bf, self.Dp, False, R, GH, self.D, G.EPI_F32, self.gi, GH,
                bias=self.b_ih.data, status=status)
-        # rows (e, 0): the state stored at the rollout's first step
-        C.rnn_mask(Be, H, self.h0[lo : lo + Be], H, None if not self.lstm else self.c0[lo : lo + Be], H, None,
-                   self.hprev, T * H, self.hprev_bf, T * H, self.cprev, T * H)
-        for t in range(T):
-            nxt = t + 1 < T
-            G.gemm(_view_from(self.hprev_bf, t * H), T * H, False, self.w_hh_bf, self.w_hh_bf.shape[1], False, Be, GH, H,
+        if init is None:  # the state stored at the rollout's first step
+            init = (self.h0[lo : lo + Be], self.c0[lo : lo + Be] if self.lstm else None)
+        C.rnn_mask(Be, H, init[0], H, init[1] if self.lstm else None, H, None, *at(self.hprev, 0, H),
+                   *at(self.hprev_bf, 0, H), *(at(self.cprev, 0, H) if self.lstm else (None, 0)))
+        for t in range(L):
+            nxt = t + 1 < L
+            ta = (t0 + t) * N + lo
+            if nxt:
+                done_t = dones_tm[ta : ta + Be]
+                h_next, hbf_next = at(self.hprev, t + 1, H), at(self.hprev_bf, t + 1, H)
+                c_next = at(self.cprev, t + 1, H) if self.lstm else (None, 0)
+            elif carry is not None:
+                done_t = dones_tm[ta : ta + Be]
+                h_next, hbf_next = (carry[0], H), (carry[1], H)
+                c_next = (carry[2], H) if self.lstm else (None, 0)
+            else:
+                done_t, h_next, hbf_next, c_next = None, (None, 0), (None, 0), (None, 0)
+            c_in = at(self.cprev, t, H) if self.lstm else (None, 0)
+            if self.fused_step:
+                C.rnn_step_fused(Be, H, self.lstm, *at(self.hprev_bf, t, H), self.w_hh_bf, self.w_hh_bf.shape[1],
+                                 self.b_hh.data, *at(self.gi, t, GH), *at(self.hprev, t, H), *c_in, None, 0,
+                                 *at(self.hout_bf, t, H), None, 0, done_t, *h_next, *hbf_next, *c_next,
+                                 *at(self.save, t, S * H), status)
+                continue
+            G.gemm(*at(self.hprev_bf, t, H), False, self.w_hh_bf, self.w_hh_bf.shape[1], False, Be, GH, H,
                    G.EPI_F32, self.gh_step, GH, bias=self.b_hh.data, status=status)
-            done_t = dones_tm[t * N + lo : t * N + lo + Be] if nxt else None
-            C.rnn_cell_fwd(Be, H, self.lstm, _view_from(self.gi, t * GH), T * GH, self.gh_step, GH,
-                           _view_from(self.hprev, t * H), T * H,
-                           _view_from(self.cprev, t * H) if self.lstm else None, T * H,
-                           None, 0, _view_from(self.hout_bf, t * H), T * H,
-                           self.c_step, H, done_t,
-                           _view_from(self.hprev, (t + 1) * H) if nxt else None, T * H,
-                           _view_from(self.hprev_bf, (t + 1) * H) if nxt else None, T * H,
-                           _view_from(self.cprev, (t + 1) * H) if (nxt and self.lstm) else None, T * H,
-                           _view_from(self.save, t * S * H), T * S * H)
+            C.rnn_cell_fwd(Be, H, self.lstm, *at(self.gi, t, GH), self.gh_step, GH, *at(self.hprev, t, H), *c_in,
+                           None, 0, *at(self.hout_bf, t, H), self.c_step, H, done_t, *h_next, *hbf_next, *c_next,
+                           *at(self.save, t, S * H))
         self.head.forward(self.hout_bf, self.head.h_train, R, head_out, head_ld, status)
 
-    def backward_sequence(self, lo: int, Be: int, dones_tm: torch.Tensor, status) -> None:
+    def backward_sequence(self, lo: int, Be: int, dones_tm: torch.Tensor, status, *, L: int | None = None,
+                          t0: int = 0, time_major: bool = False, x=None) -> None:
+        """Backpropagation through the sequence of the last ``forward_sequence`` (same arguments): the head's
+        output gradient must be in ``head.d_head``; no gradient enters from after the last step or leaves through
+        the initial state. Leaves split-K weight-gradient partials and bias column sums for the segment reduction."""
         C = ext()
-        T, N, H, GH, S = self.T, self.N, self.H, self.GH, self.S
-        R = Be * T
+        N, H, GH, S = self.N, self.H, self.GH, self.S
+        L = self.T if L is None else L
+        R = Be * L
+        at = self._layout(Be, L, time_major)
         nb = self.bwd_blocks
         if C.rnn_bwd_blocks(Be) < nb:  # a shorter env range writes fewer column-sum rows
             used = C.rnn_bwd_blocks(Be)
@@ -177,25 +238,27 @@ class _RecurrentNet:
                     cs[used:].zero_()
         self.head.backward(R, status, x=self.hout_bf, dx_out=self.dh_head)
         dgh = self.dgi if self.lstm else self.dgh
-        for t in range(T - 1, -1, -1):
+        for t in range(L - 1, -1, -1):
             cur, prev = t & 1, (t + 1) & 1
-            last = t == T - 1
-            C.rnn_cell_bwd(Be, H, self.lstm, _view_from(self.save, t * S * H), T * S * H,
-                           None if self.lstm else _view_from(self.hprev, t * H), T * H,
-                           _view_from(self.cprev, t * H) if self.lstm else None, T * H,
-                           _view_from(self.dh_head, t * H), T * H,
+            last = t == L - 1
+            ta = (t0 + t) * N + lo
+            C.rnn_cell_bwd(Be, H, self.lstm, *at(self.save, t, S * H),
+                           *(at(self.hprev, t, H) if not self.lstm else (None, 0)),
+                           *(at(self.cprev, t, H) if self.lstm else (None, 0)),
+                           *at(self.dh_head, t, H),
                            None if (last or self.lstm) else self.dh_direct[prev],
                            None if last else self.dh_gemm[prev], H,
                            None if (last or not self.lstm) else self.dc[prev], H,
-                           None if last else dones_tm[t * N + lo : t * N + lo + Be],
-                           _view_from(self.dgi, t * GH), T * GH,
-                           None if self.lstm else _view_from(self.dgh, t * GH), T * GH,
+                           None if last else dones_tm[ta : ta + Be],
+                           *at(self.dgi, t, GH),
+                           *(at(self.dgh, t, GH) if not self.lstm else (None, 0)),
                            self.dh_direct[cur], H, self.dc[cur], H, self.cs_gi, self.cs_gh, not last)
             if t > 0:  # gradient of the step's input state through W_hh (W_hh [GH, H] read MN-major)
-                G.gemm(_view_from(dgh, t * GH), T * GH, False, self.w_hh_bf, self.w_hh_bf.shape[1], True, Be, H, GH,
+                G.gemm(*at(dgh, t, GH), False, self.w_hh_bf, self.w_hh_bf.shape[1], True, Be, H, GH,
                        G.EPI_F32, self.dh_gemm[cur], H, status=status)
-        # weight gradients over all T x Be rows: dW_ih = dgi^T x, dW_hh = dgh^T h_in (split-K partials)
-        x = self.x[lo * T : (lo + Be) * T]
+        # weight gradients over all L x Be rows: dW_ih = dgi^T x, dW_hh = dgh^T h_in (split-K partials)
+        if x is None:
+            x = self.x[lo * L : (lo + Be) * L]
         for part, splits_max, a, b, ldb, ncols in ((self.part_ih, self.splits_ih, self.dgi, x, self.Dp, self.D),
                                                    (self.part_hh, self.splits_hh, dgh, self.hprev_bf, H, H)):
             splits = min(splits_max, (R + 63) // 64)
@@ -209,23 +272,10 @@ class RecurrentPPOEngine(EngineBase):
     # ---- capability checks ------------------------------------------------------------------------------------------
     @staticmethod
     def supports_models(actor, critic, alg_cfg: dict) -> str | None:
-        from ..models import RNNModel
-
         for name, m in (("actor", actor), ("critic", critic)):
-            if type(m) is not RNNModel:
-                return f"{name} type {type(m).__name__} is not the recurrent model"
-            rnn = m.rnn.rnn
-            if not isinstance(rnn, (nn.GRU, nn.LSTM)):
-                return f"{name} recurrent layer {type(rnn).__name__}"
-            if rnn.num_layers != 1 or not rnn.bias or rnn.bidirectional or getattr(rnn, "proj_size", 0):
-                return f"{name}: only single-layer, unidirectional RNNs with biases are fused"
-            if rnn.hidden_size % 32 or rnn.hidden_size > 1024:
-                return f"{name}: hidden size must be a multiple of 32 up to 1024"
-            reason = elu_mlp_reason(m)
+            reason = rnn_model_reason(name, m)
             if reason:
-                return f"{name}: {reason}"
-            if m.obs_dim > 1024:
-                return f"{name} observation width {m.obs_dim} too large"
+                return reason
         dist = actor.distribution
         if not isinstance(dist, (GaussianDistribution, HeteroscedasticGaussianDistribution)):
             return "actor distribution is not Gaussian"
@@ -233,18 +283,21 @@ class RecurrentPPOEngine(EngineBase):
             return "more than 32 actions"
         if critic.distribution is not None or critic.mlp.linears[-1].out_features != 1:
             return "critic output is not a scalar value"
-        if alg_cfg.get("rnd_cfg"):
-            return "RND with recurrent models runs on the PyTorch path"
+        rnd_cfg = alg_cfg.get("rnd_cfg")
+        if isinstance(rnd_cfg, dict) and str(rnd_cfg.get("activation", "elu")).lower() != "elu":
+            return "RND activation is not fused (ELU only)"
         if str(alg_cfg.get("optimizer", "adam")).lower() != "adam":
             return "only Adam is fused"
         return None
 
     @staticmethod
     def unsupported_reason(alg) -> str | None:
-        cfg = {"rnd_cfg": alg.rnd is not None,
-               "normalize_advantage_per_mini_batch": alg.normalize_advantage_per_mini_batch,
+        cfg = {"normalize_advantage_per_mini_batch": alg.normalize_advantage_per_mini_batch,
                "optimizer": getattr(alg, "optimizer_name", "adam")}
-        return RecurrentPPOEngine.supports_models(alg.actor, alg.critic, cfg)
+        reason = RecurrentPPOEngine.supports_models(alg.actor, alg.critic, cfg)
+        if reason is None and alg.rnd is not None:
+            reason = rnd_reason(alg.rnd)
+        return reason
 
     # ---- construction -------------------------------------------------------------------------------------------------
     def __init__(self, alg, num_steps_per_env: int, num_envs: int, obs_template=None) -> None:
@@ -277,6 +330,11 @@ class RecurrentPPOEngine(EngineBase):
         self.param_group = [0 if id(p) in actor_ids else 1 for p in self.params]
         if self.param_group != sorted(self.param_group):
             raise RuntimeError("fused engine: actor parameters must precede critic parameters")
+        self.rnd = alg.rnd
+        if self.rnd is not None:  # the predictor: a third parameter group (own learning rate, no clipping)
+            rnd_params = list(self.rnd.predictor.parameters())
+            self.params += rnd_params
+            self.param_group += [_GROUP_RND] * len(rnd_params)
         self.offsets, off = [], 0
         for p in self.params:
             self.offsets.append(off)
@@ -287,7 +345,10 @@ class RecurrentPPOEngine(EngineBase):
             self.flat[o : o + p.numel()].copy_(p.data.reshape(-1))
             p.data = self.flat[o : o + p.numel()].view_as(p)
         n_actor = sum(p.numel() for p, g in zip(self.params, self.param_group) if g == 0)
-        self.group_ranges = [0, n_actor, n_actor, self.n_params]
+        n_ac = sum(p.numel() for p, g in zip(self.params, self.param_group) if g != _GROUP_RND)
+        self.group_ranges = [0, n_actor, n_actor, n_ac]
+        if self.rnd is not None:
+            self.group_ranges += [n_ac, self.n_params]
         self.n_ex = (self.n_params + _TAIL + 3) // 4 * 4
         self.exp_avg = torch.zeros(self.n_params, **f32)
         self.exp_avg_sq = torch.zeros(self.n_params, **f32)
@@ -299,7 +360,9 @@ class RecurrentPPOEngine(EngineBase):
         if self.world > 1:
             from ..parallel import PeerExchange
 
-            small = max(4 * self.n_params, 8 * (2 + 2 * max(self.Da, self.Dc)), 4096)
+            big = max((t.numel() for t in self.rnd.state_dict().values()), default=0) if self.rnd is not None else 0
+            dmax = max(self.Da, self.Dc, self.rnd.num_states if self.rnd is not None else 0)
+            small = max(4 * self.n_params, 4 * big, 8 * (2 + 2 * dmax), 4096)
             self.comm = PeerExchange.create(self.n_ex, small, rank=self.rank, world=self.world, device=dev,
                                             timeout_ms=alg.b200_cfg["comm_timeout_ms"])
             from ..algorithms.ppo import use_two_shot
@@ -313,8 +376,10 @@ class RecurrentPPOEngine(EngineBase):
             buf = torch.zeros(self.n_ex, **f32)
             self.send = [buf, buf]
         self.grads = torch.zeros(self.n_ex, **f32)
-        self.lr = torch.tensor([alg._learning_rate, alg._learning_rate], **f32)
-        self.step = torch.zeros(2, dtype=torch.int64, device=dev)
+        # learning-rate slots: 0 = PPO optimizer (adaptive), 2 = RND predictor optimizer; one step counter per group
+        lr_rnd = self.rnd.optimizer.param_groups[0]["lr"] if self.rnd is not None else 0.0
+        self.lr = torch.tensor([alg._learning_rate, alg._learning_rate, lr_rnd], **f32)
+        self.step = torch.zeros(3, dtype=torch.int64, device=dev)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = torch.zeros(4, dtype=torch.int32, device=dev)
         self.barrier = torch.zeros(4, dtype=torch.int32, device=dev)
@@ -324,12 +389,23 @@ class RecurrentPPOEngine(EngineBase):
         self.seed = int(torch.initial_seed() % (2**62))
 
         # ---- networks ----
-        self.net_a = _RecurrentNet(self.actor, self.N, self.T, self.Be_max, dev, self.sm_count)
-        self.net_c = _RecurrentNet(self.critic, self.N, self.T, self.Be_max, dev, self.sm_count)
+        fused = bool(alg.b200_cfg["rnn_fused_step"])
+        self.net_a = _RecurrentNet(self.actor, self.N, self.T, self.Be_max, dev, self.sm_count, fused)
+        self.net_c = _RecurrentNet(self.critic, self.N, self.T, self.Be_max, dev, self.sm_count, fused)
         self.nets = (self.net_a, self.net_c)
         for net in self.nets:
             net.refresh_shadows()
         self.head_cols = self.net_a.head.head_cols
+        # RND: the predictor trains on a minibatch's env-major rows plus one row standing for the zero-padded
+        # trajectory entries of upstream's recurrent minibatch (see _minibatch)
+        self.rnd_part = None
+        self.intrinsic_for_logger = None
+        if self.rnd is not None:
+            self.rnd_part = RndPart(self, self.rnd, self.N, self.T, self.Be_max * self.T + 1, dev, self.sm_count)
+            for plan in self.rnd_part.plans:
+                plan.refresh_shadows()
+            self.intrinsic_for_logger = self.rnd_part.intrinsic
+            alg.intrinsic_rewards = self.rnd_part.intrinsic
 
         # ---- rollout arena (time-major rows t * N + n, as the GAE kernel expects) ----
         T, N, A = self.T, self.N, self.A
@@ -348,6 +424,12 @@ class RecurrentPPOEngine(EngineBase):
         self.last_values = torch.zeros(N, **f32)
         self.gae_partial = torch.zeros(2 * C.gae_blocks(N), dtype=torch.float64, device=dev)
         self.t = 0
+        if self.rnd is not None:
+            Dr = self.rnd_part.Dr
+            # raw RND states, time-major, plus one zero row at T * N: the state of every zero-padded entry
+            self.obs_r = torch.zeros(T * N + 1, (Dr + 3) // 4 * 4, **f32)[:, :Dr]
+            self.rnd_idx_out = torch.zeros(self.Be_max * T + 1, dtype=torch.int32, device=dev)
+            self.rnd_pad = torch.zeros(1, **f32)  # padded entries of the current minibatch (weight of the zero row)
 
         # ---- minibatch: storage row of every env-major minibatch row (e, t) -> t * N + lo + e ----
         self.mb_idx = []
@@ -356,6 +438,10 @@ class RecurrentPPOEngine(EngineBase):
             e = torch.arange(lo, hi, device=dev, dtype=torch.int64)
             t = torch.arange(T, device=dev, dtype=torch.int64)
             self.mb_idx.append((t[None, :] * N + e[:, None]).reshape(-1).to(torch.int32).contiguous())
+        self.mb_idx_r = None
+        if self.rnd is not None:
+            pad_row = torch.full((1,), T * N, dtype=torch.int32, device=dev)
+            self.mb_idx_r = [torch.cat([idx, pad_row]).contiguous() for idx in self.mb_idx]
         R_max = self.Be_max * T
         self.value_train = torch.zeros(R_max, 1, **f32)
         self.d_value = self.net_c.head.d_head
@@ -374,6 +460,8 @@ class RecurrentPPOEngine(EngineBase):
         seg = {}
         seg.update(self.net_a.reduce_segments(self.dhead_colsum, self.loss_blocks))
         seg.update(self.net_c.reduce_segments(self.dvalue_colsum, self.loss_blocks))
+        if self.rnd is not None:
+            seg.update(self.rnd_part.reduce_segments())
         if not self.hetero:
             std_p = dist.std_param if dist.std_type == "scalar" else dist.log_std_param
             seg[id(std_p)] = (self.dstd_partial, self.loss_blocks, A)
@@ -396,6 +484,9 @@ class RecurrentPPOEngine(EngineBase):
         shadows = {}
         for net in self.nets:
             shadows.update(net.shadows())
+        if self.rnd is not None:
+            pp = self.rnd_part.plan_p
+            shadows.update({id(lin.weight): wb for lin, wb in zip(pp.linears, pp.w_bf16)})
         t_off, t_num, t_grp, t_rows, t_cols, t_sh, t_ld = [], [], [], [], [], [], []
         for p, o, g in zip(self.params, self.offsets, self.param_group):
             sh = shadows.get(id(p))
@@ -423,6 +514,16 @@ class RecurrentPPOEngine(EngineBase):
         self.adam_eps = float(group0.get("eps", 1e-8))
         if float(group0.get("weight_decay", 0.0)) != 0.0 or group0.get("amsgrad", False):
             raise ValueError("fused Adam supports weight_decay=0 and amsgrad=False")
+        self.adam_max_norm = [alg.max_grad_norm, alg.max_grad_norm]
+        self.adam_beta1, self.adam_beta2 = [self.betas[0]] * 2, [self.betas[1]] * 2
+        self.adam_eps_g, self.adam_lr_index = [self.adam_eps] * 2, [0, 0]
+        if self.rnd is not None:
+            rb1, rb2, reps = self.rnd_part.adam_hparams()
+            self.adam_max_norm.append(0.0)
+            self.adam_beta1.append(rb1)
+            self.adam_beta2.append(rb2)
+            self.adam_eps_g.append(reps)
+            self.adam_lr_index.append(2)
 
         self._alloc_norm_scratch("actor", self.total, self.Da)
         self._alloc_norm_scratch("critic", self.total, self.Dc)
@@ -454,6 +555,13 @@ class RecurrentPPOEngine(EngineBase):
         C = ext()
         N, T, t = self.N, self.T, self.t
         rows = slice(t * N, (t + 1) * N)
+        if self.rnd is not None:
+            if t == 0 and not torch.cuda.is_current_stream_capturing():
+                self.rnd_part.prepare()
+            # store the raw RND state (the bf16 copy in the scratch row buffer is not used)
+            rp = self.rnd_part.plan_p
+            C.prep_obs(self._group_tensors(obs, self.rnd_part.groups), self.obs_r[rows], self.obs_r.stride(0),
+                       rp.x_roll, rp.x_roll.shape[1], None, None, 0.0)
         for net, model, groups, arena in ((self.net_a, self.actor, self.groups_a, self.obs_a),
                                           (self.net_c, self.critic, self.groups_c, self.obs_c)):
             mean, std, eps = self._norm_tensors(model)
@@ -482,13 +590,18 @@ class RecurrentPPOEngine(EngineBase):
         timeouts = extras.get("time_outs") if isinstance(extras, dict) else None
         if timeouts is not None:
             timeouts = timeouts.to(self.device).reshape(-1)
-        C.process_step(rewards.reshape(-1).float(), None, dones.reshape(-1), timeouts, self.st_values[rows],
+        intrinsic = self.rnd_part.intrinsic_reward(self, obs, t) if self.rnd is not None else None
+        C.process_step(rewards.reshape(-1).float(), intrinsic, dones.reshape(-1), timeouts, self.st_values[rows],
                        self.alg.gamma, self.st_rewards[rows], self.st_dones[rows], self.nonfinite)
         done_f = self.st_dones[rows]
         for net in self.nets:  # reset the state of finished episodes
             H = net.H
             C.rnn_mask(N, H, net.h, H, net.c, H, done_f, net.h, H, net.h_bf, H, net.c, H)
         self.t += 1
+
+    def _before_replay(self) -> None:
+        if self.rnd is not None:
+            self.rnd_part.prepare()
 
     def compute_returns(self, obs) -> None:
         C = ext()
@@ -534,6 +647,8 @@ class RecurrentPPOEngine(EngineBase):
                    None if self.hetero else self.dstd_partial, 1, False, None, None, 0.0, self.status)
         self.net_a.backward_sequence(lo, Be, self.st_dones, self.status)
         self.net_c.backward_sequence(lo, Be, self.st_dones, self.status)
+        if self.rnd is not None:
+            self._rnd_minibatch(i, lo, Be)
         C.reduce_segments(self.reduce_plan, self.reduce_nseg, self.reduce_chunks, self.send[0], self.send[1],
                           self.epoch, False)
         adaptive = alg.desired_kl is not None and alg.schedule == "adaptive"
@@ -541,20 +656,41 @@ class RecurrentPPOEngine(EngineBase):
         peers = self.comm.peer_send if self.comm is not None else None
         flags = self.comm.peer_flags if self.comm is not None else None
         C.adam_step(self.flat, self.send[0], self.send[1], self.grads, self.exp_avg, self.exp_avg_sq,
-                    self.adam_tensors, self.adam_chunks, self.adam_nchunks, [alg.max_grad_norm, alg.max_grad_norm],
-                    [self.betas[0]] * 2, [self.betas[1]] * 2, [self.adam_eps] * 2, [0, 0], self.lr, None, self.step,
-                    adaptive, kl, float(alg.desired_kl or 0.0), 1e-5, 1e-2, self.world, self.rank, peers, flags,
+                    self.adam_tensors, self.adam_chunks, self.adam_nchunks, self.adam_max_norm, self.adam_beta1,
+                    self.adam_beta2, self.adam_eps_g, self.adam_lr_index, self.lr, None, self.step, adaptive, kl, float(alg.desired_kl or 0.0), 1e-5, 1e-2, self.world, self.rank, peers, flags,
                     self.epoch, self.timeout_ns, self.norm_partial, self.barrier, self.status, None, self.adam_grid,
                     self.group_ranges, self.n_ex, self._peer_reduced, self._kl_offset)
         self.loss_acc.add_(self.grads[self.n_params : self.n_params + _TAIL])
 
+    def _rnd_minibatch(self, i: int, lo: int, Be: int) -> None:
+        """Predictor step of minibatch ``i`` as upstream's ``rnd.compute_loss`` on the recurrent minibatch: its
+        observations are the padded trajectories ``[T, trajectories]``, so the MSE averages over the real entries
+        (the env range's ``Be x T`` rows) and the zero-padded ones, which all share the normalised zero state. Every
+        environment has one trajectory plus one per done before its last step, each padded to ``T`` entries: the
+        zero row's weight is ``T x`` that done count, computed on the device."""
+        C = ext()
+        part = self.rnd_part
+        rows = Be * self.T + 1
+        part.zero_tails(rows)
+        mean_r, std_r, eps_r = self._norm_views(self.rnd.state_normalizer)
+        rp = part.plan_p
+        C.gather_minibatch(rows, 0, self.total + 1, None, 0, self.mb_idx_r[i], self.rnd_idx_out, [self.obs_r],
+                           [mean_r], [std_r], eps_r if mean_r is not None else 0.0, [rp.x_train], [rp.x_train.shape[1]],
+                           self.status, 1, [rows], [None], [None])
+        C.rnn_pad_entries(self.st_dones, self.T, self.N, lo, Be, self.rnd_pad)
+        part.train(rows, self.status, self.rnd_pad)
+
     def _update_body(self) -> None:
         self.loss_acc.zero_()
+        if self.rnd is not None:
+            self.rnd_part.loss_acc.zero_()
         for _ in range(self.E):
             for i in range(self.M):
                 self._minibatch(i)
         self._normalizer_update("actor", self.actor, self.obs_a, self.total, self.Da)
         self._normalizer_update("critic", self.critic, self.obs_c, self.total, self.Dc)
+        if self.rnd is not None:
+            self.rnd_part.normalizer_update(self, self.obs_r, self.total)
 
     def update(self) -> dict[str, float]:
         if self.use_graphs and self._updates_done >= 1:
@@ -564,9 +700,13 @@ class RecurrentPPOEngine(EngineBase):
         else:
             self._update_body()
         self._updates_done += 1
-        stats = [v / float(self.E * self.M) for v in HostTransfers.read(self.loss_acc, "loss_stats")]
+        n = float(self.E * self.M)
+        stats = [v / n for v in HostTransfers.read(self.loss_acc, "loss_stats")]
         self._check_status()
-        return {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
+        out = {"value": stats[1], "surrogate": stats[0], "entropy": stats[2]}
+        if self.rnd is not None:
+            out["rnd"] = float(HostTransfers.read(self.rnd_part.loss_acc, "rnd_loss")[0]) / n
+        return out
 
     # ---- rollout import (tests) -----------------------------------------------------------------------------------------
     def load_rollout(self, storage, h0_actor: torch.Tensor, h0_critic: torch.Tensor, c0_actor=None,
@@ -587,6 +727,8 @@ class RecurrentPPOEngine(EngineBase):
             net.h0.copy_(h0)
             if net.lstm:
                 net.c0.copy_(c0)
+        if self.rnd is not None:
+            self.obs_r[: T * N].copy_(torch.cat([obs[g] for g in self.rnd_part.groups], dim=-1))
         mean, std = storage.distribution_params[0], storage.distribution_params[1]
         self.st_actions.copy_(storage.actions.reshape(T * N, -1))
         self.st_mean.copy_(mean.reshape(T * N, -1))
@@ -599,27 +741,35 @@ class RecurrentPPOEngine(EngineBase):
         self.st_adv.copy_(storage.advantages.reshape(-1))
 
     # ---- checkpoints --------------------------------------------------------------------------------------------------
+    def _optimizer_of(self, g: int):
+        return self.rnd.optimizer if g == _GROUP_RND else self.alg.optimizer
+
     def sync_to_torch(self) -> None:
-        opt = self.alg.optimizer
+        """Expose the device optimizer state through the ``torch.optim.Adam`` objects (parameters are already views)."""
         steps = HostTransfers.read(self.step, "adam_step")
         for p, o, g in zip(self.params, self.offsets, self.param_group):
             if steps[g] == 0:
                 continue
             n = p.numel()
-            opt.state[p] = {"step": torch.tensor(float(steps[g])), "exp_avg": self.exp_avg[o : o + n].view_as(p),
-                            "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p)}
-        lr = self.learning_rate()
-        for group in opt.param_groups:
-            group["lr"] = lr
-        self.alg._learning_rate = lr
+            self._optimizer_of(g).state[p] = {"step": torch.tensor(float(steps[g])),
+                                              "exp_avg": self.exp_avg[o : o + n].view_as(p),
+                                              "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p)}
+        lrs = HostTransfers.read(self.lr, "learning_rate")
+        for group in self.alg.optimizer.param_groups:
+            group["lr"] = lrs[0]
+        self.alg._learning_rate = lrs[0]
+        if self.rnd is not None:
+            for group in self.rnd.optimizer.param_groups:
+                group["lr"] = lrs[2]
 
     def sync_from_torch(self) -> None:
-        opt = self.alg.optimizer
+        """Pull loaded weights / optimizer state into the device arena and refresh the bf16 shadows."""
         for p, o, g in zip(self.params, self.offsets, self.param_group):
             n = p.numel()
             if p.data.data_ptr() != self.flat[o : o + n].data_ptr():
                 self.flat[o : o + n].copy_(p.data.reshape(-1))
                 p.data = self.flat[o : o + n].view_as(p)
+            opt = self._optimizer_of(g)
             st = opt.state.get(p)
             if st:
                 self.exp_avg[o : o + n].copy_(st["exp_avg"].reshape(-1))
@@ -627,23 +777,35 @@ class RecurrentPPOEngine(EngineBase):
                 self.step[g] = int(float(st["step"]))
                 opt.state[p] = {"step": st["step"], "exp_avg": self.exp_avg[o : o + n].view_as(p),
                                 "exp_avg_sq": self.exp_avg_sq[o : o + n].view_as(p)}
-        self.lr.fill_(float(opt.param_groups[0]["lr"]))
+        self.lr[0:2].fill_(float(self.alg.optimizer.param_groups[0]["lr"]))
+        if self.rnd is not None:
+            self.lr[2] = self.rnd_part.learning_rate()
+        self._refresh_shadows()
+
+    def _refresh_shadows(self) -> None:
         for net in self.nets:
             net.refresh_shadows()
+        if self.rnd is not None:
+            for plan in self.rnd_part.plans:
+                plan.refresh_shadows()
 
     def broadcast_parameters(self) -> None:
+        """Make every rank start from rank 0's parameters and normaliser buffers."""
+        extra = [] if self.rnd is None else self.rnd_part.broadcast_modules()
         if self.comm is not None:
             self.comm.broadcast_(self.flat, status=self.status)
-            for model in (self.actor, self.critic):
+            for model in [self.actor, self.critic] + ([self.rnd.predictor] if self.rnd is not None else []):
                 for b in model.buffers():
                     self.comm.broadcast_(b, status=self.status)
+            for m in extra:
+                for t in m.state_dict().values():
+                    self.comm.broadcast_(t, status=self.status)
             self._check_status()
         else:
-            for model in (self.actor, self.critic):
+            for model in [self.actor, self.critic] + ([self.rnd] if self.rnd is not None else []):
                 for t in model.state_dict().values():
                     torch.distributed.broadcast(t, src=0)
-        for net in self.nets:
-            net.refresh_shadows()
+        self._refresh_shadows()
 
 
-__all__ = ["RecurrentPPOEngine"]
+__all__ = ["RecurrentPPOEngine", "rnn_model_reason"]

@@ -36,6 +36,8 @@ void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b
   check_cuda(b, "b");
   check_cuda(out, "out");
   TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16, "gemm operands must be bf16");
+  TORCH_CHECK(epilogue >= rlb::kEpiF32 && epilogue <= rlb::kEpiPartialF32,
+              "gemm: unknown epilogue (the recurrent-cell epilogue is rnn_step_fused)");
   const bool out_f32 = epilogue == rlb::kEpiF32 || epilogue == rlb::kEpiPartialF32;
   TORCH_CHECK(out.scalar_type() == (out_f32 ? torch::kFloat32 : torch::kBFloat16), "gemm: wrong output dtype");
   // extent checks (elements reachable by the kernel)

@@ -443,7 +443,8 @@ int64_t mse_blocks(int64_t rows) { return rlb::mse_blocks(static_cast<int>(rows)
 
 void mse_grad(const Tensor& pred, int64_t ld_pred, const Tensor& target, int64_t ld_target, int64_t rows, int64_t A,
               bool huber, const Tensor& grad, int64_t ld_grad, int64_t head_cols, const Tensor& loss_partial,
-              const Tensor& colsum_partial, const Tensor& loss_acc, const Tensor& ticket) {
+              const Tensor& colsum_partial, const Tensor& loss_acc, const Tensor& ticket, const OptT& last_weight,
+              int64_t denom_rows) {
   check_f32(pred, "pred");
   check_f32(target, "target");
   check_bf16(grad, "grad");
@@ -457,7 +458,15 @@ void mse_grad(const Tensor& pred, int64_t ld_pred, const Tensor& target, int64_t
   rlb::MseArgs a{P<const float>(pred), static_cast<int>(ld_pred), P<const float>(target), static_cast<int>(ld_target),
                  static_cast<int>(rows), static_cast<int>(A), huber ? 1 : 0, grad.data_ptr(),
                  static_cast<int>(ld_grad), static_cast<int>(head_cols), P<float>(loss_partial),
-                 P<float>(colsum_partial), P<float>(loss_acc), reinterpret_cast<unsigned int*>(ticket.data_ptr())};
+                 P<float>(colsum_partial), P<float>(loss_acc), reinterpret_cast<unsigned int*>(ticket.data_ptr()),
+                 nullptr, static_cast<int>(denom_rows)};
+  TORCH_CHECK(denom_rows >= 0 && !(denom_rows > 0 && last_weight.has_value()),
+              "mse_grad: denom_rows and last_weight are exclusive");
+  if (last_weight.has_value()) {
+    check_f32(*last_weight, "last_weight");
+    TORCH_CHECK(last_weight->numel() >= 1, "mse_grad: last_weight");
+    a.last_weight = P<const float>(*last_weight);
+  }
   ok(rlb::mse_grad(a, cur()), "mse_grad");
 }
 

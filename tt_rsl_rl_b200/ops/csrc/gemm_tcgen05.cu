@@ -62,7 +62,7 @@ struct Cfg {
   static constexpr int kSmemBudget = kMinBlocks == 1 ? kSmemLimit : (228 * 1024) / 2 - 1024;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr bool kStaged = !(EPI == kEpiF32 || EPI == kEpiPartialF32);  // bf16 outputs go through smem
+  static constexpr bool kStaged = !(EPI == kEpiF32 || EPI == kEpiPartialF32 || EPI == kEpiRnnCell);  // bf16 via smem
   static constexpr int kStagingBytes = kStaged ? kEpiWarps * 2 * kEpiBufBytes : 0;
   static constexpr int kBiasBytes = kStaged ? kEpiWarps * 32 * 4 : 0;
   static constexpr int kColsumBytes = EPI == kEpiDgradElu ? 2 * 4 * BN * 4 : 0;  // double-buffered by tile parity
@@ -73,7 +73,8 @@ struct Cfg {
   static constexpr int kStagesFit = (kSmemBudget - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesFit > 6 ? 6 : kStagesFit;
   static constexpr int kAccCols = BN < 32 ? 32 : BN;
-  static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators
+  // two accumulators; the allocation is a power of two columns (192-column cell tiles allocate 512)
+  static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 2 * kAccCols <= 256 ? 256 : 512;
   static constexpr int kSmemBytes = kFixed + kStages * kStageBytes;
   static_assert(kStages >= 2, "pipeline needs at least two stages");
   static_assert(kTmemCols * kMinBlocks <= 512, "TMEM holds 512 columns per SM");
@@ -191,7 +192,13 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
             for (int j = 0; j < kBM / 64; ++j)
               if (tc.m0 + 64 * j < p.M) tma_load_2d(a_dst + j * kMNBoxBytes, &tmA, &full[s], tc.m0 + 64 * j, kc);
           }
-          if (!B_MN) {
+          if constexpr (EPI == kEpiRnnCell) {
+            // the tile's units of every gate: G boxes of kRnnUnits rows, stacked in the B stage
+            const int u0 = (t % n_tiles) * kRnnUnits;
+#pragma unroll
+            for (int g = 0; g < BN / kRnnUnits; ++g)
+              tma_load_2d(b_dst + g * kRnnUnits * kBK * 2, &tmB, &full[s], kc, g * p.cell.H + u0);
+          } else if (!B_MN) {
             tma_load_2d(b_dst, &tmB, &full[s], kc, tc.n0);
           } else {
 #pragma unroll
@@ -408,6 +415,130 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
       bulk_wait_group<0>();  // outputs written before the kernel ends
     }
     __syncwarp();
+  } else if constexpr (EPI == kEpiRnnCell) {
+    // ---------------- recurrent-cell epilogue (warps 2..9) ----------------
+    // A thread owns one row (TMEM lane); the kPerQuad warps of a quadrant split the tile's kRnnUnits units in chunks
+    // of 32. Per chunk: the G gate columns of the accumulator, + b_hh, then the cell four units at a time with
+    // 16-byte loads of gi / the input state and 16-byte (fp32) or 8-byte (bf16) stores of every output.
+    constexpr int G = BN / kRnnUnits;
+    const int ew = warp - 2;
+    const int q = warp & 3;  // TMEM lane quadrant: hardware rule warp % 4
+    const int slot = ew >> 2;
+    const RnnCellEpi& e = p.cell;
+    const int H = e.H;
+    int j = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
+      const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
+      const int u0 = (t % n_tiles) * kRnnUnits;
+      const int b = j & 1;
+      const uint32_t use = static_cast<uint32_t>(j >> 1);
+      uint32_t ok = 1;
+      if (lane == 0) ok = mbar_wait(&acc_full[b], use & 1) ? 1u : 0u;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) report_error(p.status, kTimeoutAccum, 6);
+        break;
+      }
+      tc_fence_after();
+      const long long row = tc.m0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
+#pragma unroll 1
+      for (int c = slot * 32; c < kRnnUnits; c += kPerQuad * 32) {
+        const int u = u0 + c;  // first hidden unit of the chunk
+        float gh[G][32];
+#pragma unroll
+        for (int g = 0; g < G; ++g) tmem_ld_32x32b_x32(acc + static_cast<uint32_t>(g * kRnnUnits + c), gh[g]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float bl = __ldg(p.bias + g * H + u + lane);  // lane l holds the bias of unit u + l
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) gh[g][jj] += __shfl_sync(0xffffffffu, bl, jj);
+        }
+        if (!row_ok) continue;
+        const float keep = e.done ? 1.0f - e.done[row] : 1.0f;
+        const float* gi = e.gi + row * e.ld_gi + u;
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 4) {
+          float hn[4], cn[4], sv[5][4];
+          if constexpr (G == 3) {  // GRU: r, z, n
+            const float4 xr = *reinterpret_cast<const float4*>(gi + jj);
+            const float4 xz = *reinterpret_cast<const float4*>(gi + H + jj);
+            const float4 xn = *reinterpret_cast<const float4*>(gi + 2 * H + jj);
+            const float4 h4 = *reinterpret_cast<const float4*>(e.h_in + row * e.ld_h_in + u + jj);
+            const float ar[4] = {xr.x, xr.y, xr.z, xr.w}, az[4] = {xz.x, xz.y, xz.z, xz.w};
+            const float an[4] = {xn.x, xn.y, xn.z, xn.w}, hh[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float r = 1.0f / (1.0f + __expf(-(ar[k] + gh[0][jj + k])));
+              const float z = 1.0f / (1.0f + __expf(-(az[k] + gh[1][jj + k])));
+              const float ghn = gh[2][jj + k];
+              const float n = tanhf(an[k] + r * ghn);
+              hn[k] = (1.0f - z) * n + z * hh[k];
+              cn[k] = 0.f;
+              sv[0][k] = r;
+              sv[1][k] = z;
+              sv[2][k] = n;
+              sv[3][k] = ghn;
+              sv[4][k] = 0.f;
+            }
+          } else {  // LSTM: i, f, g, o
+            const float4 xi = *reinterpret_cast<const float4*>(gi + jj);
+            const float4 xf = *reinterpret_cast<const float4*>(gi + H + jj);
+            const float4 xg = *reinterpret_cast<const float4*>(gi + 2 * H + jj);
+            const float4 xo = *reinterpret_cast<const float4*>(gi + 3 * H + jj);
+            const float4 c4 = *reinterpret_cast<const float4*>(e.c_in + row * e.ld_c_in + u + jj);
+            const float ai[4] = {xi.x, xi.y, xi.z, xi.w}, af[4] = {xf.x, xf.y, xf.z, xf.w};
+            const float ag[4] = {xg.x, xg.y, xg.z, xg.w}, ao[4] = {xo.x, xo.y, xo.z, xo.w};
+            const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float ig = 1.0f / (1.0f + __expf(-(ai[k] + gh[0][jj + k])));
+              const float fg = 1.0f / (1.0f + __expf(-(af[k] + gh[1][jj + k])));
+              const float gg = tanhf(ag[k] + gh[2][jj + k]);
+              const float og = 1.0f / (1.0f + __expf(-(ao[k] + gh[3][jj + k])));
+              cn[k] = fg * cc[k] + ig * gg;
+              const float tcn = tanhf(cn[k]);
+              hn[k] = og * tcn;
+              sv[0][k] = ig;
+              sv[1][k] = fg;
+              sv[2][k] = gg;
+              sv[3][k] = og;
+              sv[4][k] = tcn;
+            }
+          }
+          const long long col = u + jj;
+          if (e.h_out)
+            *reinterpret_cast<float4*>(e.h_out + row * e.ld_h_out + col) = make_float4(hn[0], hn[1], hn[2], hn[3]);
+          if (e.h_out_bf16)
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(e.h_out_bf16) + row * e.ld_h_out_bf16 + col) =
+                make_uint2(pack_bf16x2(hn[0], hn[1]), pack_bf16x2(hn[2], hn[3]));
+          if (G == 4 && e.c_out)
+            *reinterpret_cast<float4*>(e.c_out + row * e.ld_c_out + col) = make_float4(cn[0], cn[1], cn[2], cn[3]);
+          if (e.next_h)
+            *reinterpret_cast<float4*>(e.next_h + row * e.ld_next_h + col) =
+                make_float4(hn[0] * keep, hn[1] * keep, hn[2] * keep, hn[3] * keep);
+          if (e.next_h_bf16)
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(e.next_h_bf16) + row * e.ld_next_h_bf16 + col) =
+                make_uint2(pack_bf16x2(hn[0] * keep, hn[1] * keep), pack_bf16x2(hn[2] * keep, hn[3] * keep));
+          if (G == 4 && e.next_c)
+            *reinterpret_cast<float4*>(e.next_c + row * e.ld_next_c + col) =
+                make_float4(cn[0] * keep, cn[1] * keep, cn[2] * keep, cn[3] * keep);
+          if (e.save) {
+            float* sp = e.save + row * e.ld_save + col;
+#pragma unroll
+            for (int sidx = 0; sidx < (G == 4 ? 5 : 4); ++sidx)
+              *reinterpret_cast<float4*>(sp + sidx * H) = make_float4(sv[sidx][0], sv[sidx][1], sv[sidx][2],
+                                                                      sv[sidx][3]);
+          }
+        }
+      }
+      // accumulator b fully read by this warp: hand it back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
   } else {
     // ---------------- fp32-output epilogue (warps 2..9) ----------------
     const int ew = warp - 2;
@@ -533,7 +664,9 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   if (attr_err != cudaSuccess) return attr_err;
   CUtensorMap ta, tb;
   bool ok = A_MN ? make_map(&ta, p.a, p.M, p.K, p.lda, 64, 64) : make_map(&ta, p.a, p.K, p.M, p.lda, 64, kBM);
-  ok = ok && (B_MN ? make_map(&tb, p.b, p.N, p.K, p.ldb, 64, 64) : make_map(&tb, p.b, p.K, p.N, p.ldb, 64, BN));
+  // K-major B: one box per tile, or per gate of the tile's units in the recurrent-cell epilogue
+  const uint32_t b_rows = EPI == kEpiRnnCell ? static_cast<uint32_t>(kRnnUnits) : static_cast<uint32_t>(BN);
+  ok = ok && (B_MN ? make_map(&tb, p.b, p.N, p.K, p.ldb, 64, 64) : make_map(&tb, p.b, p.K, p.N, p.ldb, 64, b_rows));
   // epilogue maps: bf16 output (TMA store) and ELU-output aux (TMA load), 32 x 32 boxes with 64-byte swizzle
   CUtensorMap to = ta, tx = ta;
   if constexpr (C::kStaged) ok = ok && make_map(&to, p.out, p.N, p.M, p.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
@@ -609,6 +742,23 @@ cudaError_t gemm_launch(const GemmParams& p, cudaStream_t stream) {
   if (p.epilogue == kEpiDgradElu && ((p.ld_aux % 8) != 0 || (reinterpret_cast<uintptr_t>(p.aux) & 15)))
     return cudaErrorInvalidValue;
   const bool am = p.a_mn_major, bm = p.b_mn_major;
+  if (p.epilogue == kEpiRnnCell) {
+    const RnnCellEpi& e = p.cell;
+    const int G = e.lstm ? 4 : 3;
+    auto f32ok = [](const void* q, long long ld) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0 && ld % 4 == 0; };
+    auto bf16ok = [](const void* q, long long ld) { return (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ld % 4 == 0; };
+    if (am || bm || e.H <= 0 || e.H % kRnnUnits != 0 || p.K != e.H || p.N != G * e.H || p.bias == nullptr ||
+        e.gi == nullptr || !f32ok(e.gi, e.ld_gi) || (e.lstm ? e.c_in == nullptr : e.h_in == nullptr))
+      return cudaErrorInvalidValue;
+    if ((e.h_in && !f32ok(e.h_in, e.ld_h_in)) || (e.c_in && !f32ok(e.c_in, e.ld_c_in)) ||
+        (e.h_out && !f32ok(e.h_out, e.ld_h_out)) || (e.c_out && !f32ok(e.c_out, e.ld_c_out)) ||
+        (e.next_h && !f32ok(e.next_h, e.ld_next_h)) || (e.next_c && !f32ok(e.next_c, e.ld_next_c)) ||
+        (e.save && !f32ok(e.save, e.ld_save)) || (e.h_out_bf16 && !bf16ok(e.h_out_bf16, e.ld_h_out_bf16)) ||
+        (e.next_h_bf16 && !bf16ok(e.next_h_bf16, e.ld_next_h_bf16)))
+      return cudaErrorInvalidValue;
+    return e.lstm ? launch_t<4 * kRnnUnits, false, false, kEpiRnnCell, false>(p, stream)
+                  : launch_t<3 * kRnnUnits, false, false, kEpiRnnCell, false>(p, stream);
+  }
   switch (p.epilogue) {
     case kEpiF32:
       if (!am && !bm) return launch_bn<false, false, kEpiF32>(p, stream);

@@ -21,6 +21,39 @@ enum GemmEpilogue : int {
   kEpiBiasBf16 = 2,    // out bf16 = acc + bias[n]
   kEpiDgradElu = 3,    // out bf16 = acc * elu'(aux[m, n]) with aux = elu output (bf16); colsum partials of out
   kEpiPartialF32 = 4,  // out fp32 split partial: out[z * split_stride + m * ldo + n] = acc over split z
+  kEpiRnnCell = 5,     // one GRU / LSTM step: the cell applied to gh = acc + bias (RnnCellEpi), no `out`
+};
+
+// Fused recurrent step (kEpiRnnCell): A = the bf16 input state [M, H] (K-major), B = W_hh [G*H, H] (K-major, G = 3
+// GRU, 4 LSTM), N = G*H, K = H, bias = b_hh. A tile spans kRnnUnits hidden units of every gate (B rows g*H + u0 ..
+// g*H + u0 + kRnnUnits - 1 for g = 0 .. G-1, loaded as G boxes), so its epilogue owns whole units and applies the
+// torch.nn.GRU / torch.nn.LSTM cell with the gate order and outputs of rnn_kernels.cuh RnnCellFwdArgs. H must be a
+// multiple of kRnnUnits; fp32 arrays need 16-byte aligned bases and pitches that are multiples of 4 elements, bf16
+// arrays 8-byte aligned bases and pitches that are multiples of 4. No output may alias the A operand.
+constexpr int kRnnUnits = 64;
+struct RnnCellEpi {
+  int H = 0, lstm = 0;
+  const float* gi = nullptr;  // [M, G*H] input-side pre-activations (x W_ih^T + b_ih)
+  long long ld_gi = 0;
+  const float* h_in = nullptr;  // fp32 state entering the step
+  long long ld_h_in = 0;
+  const float* c_in = nullptr;  // LSTM cell state entering the step
+  long long ld_c_in = 0;
+  float* h_out = nullptr;  // optional fp32 h'
+  long long ld_h_out = 0;
+  void* h_out_bf16 = nullptr;  // optional bf16 h'
+  long long ld_h_out_bf16 = 0;
+  float* c_out = nullptr;  // optional LSTM c'
+  long long ld_c_out = 0;
+  const float* done = nullptr;  // optional [M]: the next-step outputs are masked by 1 - done
+  float* next_h = nullptr;
+  long long ld_next_h = 0;
+  void* next_h_bf16 = nullptr;
+  long long ld_next_h_bf16 = 0;
+  float* next_c = nullptr;
+  long long ld_next_c = 0;
+  float* save = nullptr;  // optional [M, S*H]: GRU r, z, n, gh_n (S = 4); LSTM i, f, g, o, tanh(c') (S = 5)
+  long long ld_save = 0;
 };
 
 struct GemmParams {
@@ -42,6 +75,7 @@ struct GemmParams {
   float* colsum = nullptr;    // fp32 [colsum_rows, N]: per-CTA column sums of the stored output (bias gradients)
   int colsum_rows = 0;        // rows of colsum (>= the launch's CTA count, gemm_colsum_rows()); N <= kColsumMaxN
   unsigned int* status = nullptr;
+  RnnCellEpi cell;            // kEpiRnnCell only
 };
 
 // Widest output whose column sums the data-gradient epilogue accumulates per CTA (shared memory, fp32).

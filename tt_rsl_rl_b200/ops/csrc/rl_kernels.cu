@@ -949,7 +949,9 @@ constexpr int kMseRowsPerBlock = kMseWarps * kMseRowsPerWarp;
 
 __global__ void __launch_bounds__(kMseWarps * 32) mse_grad_kernel(const MseArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float inv_n = 1.0f / (static_cast<float>(a.rows) * static_cast<float>(a.A));
+  const float w_last = a.last_weight ? *a.last_weight : 1.0f;
+  const float n_rows = a.denom_rows > 0 ? static_cast<float>(a.denom_rows) : static_cast<float>(a.rows - 1) + w_last;
+  const float inv_n = 1.0f / (n_rows * static_cast<float>(a.A));
   float col[2] = {0.f, 0.f};
   float loss = 0.f;
   const int ngroups = (a.rows + kMseRowsPerBlock - 1) / kMseRowsPerBlock;
@@ -958,6 +960,7 @@ __global__ void __launch_bounds__(kMseWarps * 32) mse_grad_kernel(const MseArgs 
     const int i = grp * kMseRowsPerBlock + warp * kMseRowsPerWarp + r;
     if (i >= a.rows) break;
     __nv_bfloat16* g = static_cast<__nv_bfloat16*>(a.grad) + static_cast<size_t>(i) * a.ld_grad;
+    const float w = i == a.rows - 1 ? w_last : 1.0f;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int j = lane + 32 * k;
@@ -966,11 +969,11 @@ __global__ void __launch_bounds__(kMseWarps * 32) mse_grad_kernel(const MseArgs 
         float gd;
         if (a.huber) {  // torch huber_loss, delta = 1: 0.5 d^2 inside |d| < 1, |d| - 0.5 outside
           const float ad = fabsf(d);
-          loss += ad < 1.f ? 0.5f * d * d : ad - 0.5f;
-          gd = fminf(fmaxf(d, -1.f), 1.f) * inv_n;
+          loss += w * (ad < 1.f ? 0.5f * d * d : ad - 0.5f);
+          gd = fminf(fmaxf(d, -1.f), 1.f) * (w * inv_n);
         } else {
-          loss += d * d;
-          gd = 2.f * d * inv_n;
+          loss += w * (d * d);
+          gd = 2.f * d * (w * inv_n);
         }
         g[j] = __float2bfloat16_rn(gd);
         col[k] += gd;

@@ -198,6 +198,13 @@ struct MseArgs {
   float* colsum_partial;  // [blocks, head_cols]
   float* loss_acc;        // [1], accumulated
   unsigned int* ticket;   // [1], zero between launches
+  // optional [1] on the device: the last row stands for this many identical rows (its loss and gradient are scaled
+  // by it and the mean is over rows - 1 + weight rows); used for the zero-padded trajectory entries of recurrent
+  // minibatches, which all share one input row
+  const float* last_weight;
+  // > 0: the mean is over this many rows instead (a window of several steps of denom_rows rows each, every step's
+  // loss a mean of its own: the gradient of the sum of the step means)
+  int denom_rows;
 };
 int mse_blocks(int rows);
 

@@ -173,6 +173,29 @@ __global__ void __launch_bounds__(256) rnn_mask_kernel(const RnnMaskArgs a) {
   }
 }
 
+// One block of 256 threads: integer counts per thread, a warp butterfly and a fixed-order sum of the eight warps
+// (exact, so the result is independent of the launch shape).
+__global__ void __launch_bounds__(256) rnn_pad_entries_kernel(const float* done, int T, int N, int lo, int Be,
+                                                              float* out) {
+  const long long n = static_cast<long long>(T - 1) * Be;
+  int count = 0;
+  for (long long k = threadIdx.x; k < n; k += blockDim.x) {
+    const int t = static_cast<int>(k / Be);
+    const int e = static_cast<int>(k - static_cast<long long>(t) * Be);
+    count += done[static_cast<long long>(t) * N + lo + e] != 0.0f ? 1 : 0;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) count += __shfl_xor_sync(0xffffffffu, count, off);
+  __shared__ int s_count[8];
+  if ((threadIdx.x & 31) == 0) s_count[threadIdx.x >> 5] = count;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long total = 0;
+    for (int w = 0; w < 8; ++w) total += s_count[w];
+    out[0] = static_cast<float>(total * T);
+  }
+}
+
 int elementwise_grid(long long n) {
   long long blocks = (n + 255) / 256;
   const long long cap = 148LL * 8;
@@ -180,6 +203,12 @@ int elementwise_grid(long long n) {
 }
 
 }  // namespace
+
+cudaError_t rnn_pad_entries(const float* done, int T, int N, int lo, int Be, float* out, cudaStream_t s) {
+  if (!done || !out || T <= 0 || Be <= 0 || lo < 0 || lo + Be > N) return cudaErrorInvalidValue;
+  rnn_pad_entries_kernel<<<1, 256, 0, s>>>(done, T, N, lo, Be, out);
+  return cudaGetLastError();
+}
 
 cudaError_t rnn_cell_fwd(const RnnCellFwdArgs& a, cudaStream_t s) {
   if (a.rows <= 0 || a.H <= 0 || !a.gi || !a.gh || !a.h_in || (a.lstm && !a.c_in)) return cudaErrorInvalidValue;

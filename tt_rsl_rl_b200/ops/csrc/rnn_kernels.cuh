@@ -92,6 +92,11 @@ struct RnnMaskArgs {
   long long ld_dst_c;
 };
 
+// Zero-padded trajectory entries of a recurrent minibatch (environments lo .. lo + Be - 1 of a time-major done
+// array [T, N]): every environment contributes one trajectory plus one per done before its last step, and each
+// trajectory is padded to T steps, so out[0] = T * (number of nonzero done[t, e], t < T - 1). One block.
+cudaError_t rnn_pad_entries(const float* done, int T, int N, int lo, int Be, float* out, cudaStream_t s);
+
 cudaError_t rnn_cell_fwd(const RnnCellFwdArgs& a, cudaStream_t s);
 cudaError_t rnn_cell_bwd(const RnnCellBwdArgs& a, cudaStream_t s);
 cudaError_t rnn_mask(const RnnMaskArgs& a, cudaStream_t s);
