@@ -23,7 +23,7 @@ def _models(obs, A, rnn_type, teacher_rnn):
                            rnn_type=rnn_type, rnn_hidden_dim=96)
     else:
         teacher = MLPModel(obs, groups, "teacher", A, hidden_dims=[128, 64], obs_normalization=True)
-    return student, teacher
+    return student.to("cuda"), teacher.to("cuda")
 
 
 def _alg(env, T, engine, student, teacher, gl, epochs, graphs=False, loss_type="mse"):
@@ -76,8 +76,8 @@ def test_recurrent_distillation_rollout_matches_modules(rnn_type, teacher_rnn):
         with torch.inference_mode():
             obs, rew, dones, extras = env.step(actions)
             alg.process_env_step(obs, rew, dones, extras)
-        s_ref.reset(dones)
-        t_ref.reset(dones)
+            s_ref.reset(dones)
+            t_ref.reset(dones)
 
 
 @pytest.mark.parametrize("rnn_type,gl,epochs", [("gru", 4, 2), ("lstm", 3, 2), ("gru", 5, 2)])

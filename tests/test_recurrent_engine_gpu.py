@@ -32,8 +32,9 @@ def _sequence_means(actor, obs_seq, dones_seq, h0):
     return torch.stack(out)
 
 
-@pytest.mark.parametrize("rnn_type,per_mb", [("gru", False), ("lstm", False), ("gru", True)])
-def test_recurrent_engine_matches_torch_path(rnn_type, per_mb):
+@pytest.mark.parametrize("rnn_type,per_mb,fused", [("gru", False, "auto"), ("lstm", False, "auto"), ("gru", True, "auto"),
+                                                    ("lstm", False, True), ("gru", False, False)])
+def test_recurrent_engine_matches_torch_path(rnn_type, per_mb, fused):
     from tt_rsl_rl_b200.algorithms import PPO
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv
     from tt_rsl_rl_b200.storage import RolloutStorage
@@ -47,10 +48,12 @@ def test_recurrent_engine_matches_torch_path(rnn_type, per_mb):
     storage = RolloutStorage("rl", N, T, obs, [env.num_actions], "cuda")
     alg_t = PPO(actor, critic, storage, device="cuda", b200_cfg={"engine": "torch"}, **kw)
     alg_e = PPO(copy.deepcopy(actor), copy.deepcopy(critic), None, device="cuda",
-                b200_cfg={"engine": "cuda", "graphs": False}, num_steps_per_env=T, num_envs=N, **kw)
+                b200_cfg={"engine": "cuda", "graphs": False, "rnn_fused_step": fused}, num_steps_per_env=T,
+                num_envs=N, **kw)
     from tt_rsl_rl_b200.engine import RecurrentPPOEngine
 
     assert isinstance(alg_e.engine, RecurrentPPOEngine)
+    assert alg_e.engine.net_a.fused_step == (fused is True or (fused == "auto" and rnn_type == "gru"))
     # two rollouts on the PyTorch path; the second starts from a non-zero state
     for it in range(2):
         with torch.inference_mode():

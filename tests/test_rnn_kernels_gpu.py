@@ -163,10 +163,11 @@ def test_fused_step_matches_gemm_plus_cell(lstm, H):
                                view(hb, t + 1), T * H, *c_next, save, S * H, status)
         else:
             gh = torch.zeros(rows, GH, **f32)
+            c_scratch = torch.zeros(rows, H, **f32) if lstm else None
             Gm.gemm(view(hb, t), T * H, False, w, H, False, rows, GH, H, Gm.EPI_F32, gh, GH, bias=b, status=status)
             C().rnn_cell_fwd(rows, H, lstm, view(gi_buf, t), T * GH, gh, GH, view(h_buf, t), T * H, *c_in, None, 0,
-                             hout_bf, H, None, 0, done, view(nh, t + 1), T * H, view(hb, t + 1), T * H, *c_next, save,
-                             S * H)
+                             hout_bf, H, c_scratch, H, done, view(nh, t + 1), T * H, view(hb, t + 1), T * H, *c_next,
+                             save, S * H)
         torch.cuda.synchronize()
         outs[fused] = (hout_bf.float(), nh[:, t + 1], hb[:, t + 1].float(), save, nc[:, t + 1] if lstm else None,
                        hb[:, t].float(), hb[:, t - 1].float())

@@ -32,7 +32,7 @@ B200_CFG_DEFAULTS = {
     "comm_timeout_ms": 10000,  # device-side wait limit of the peer-to-peer gradient exchange
     "exchange": "auto",  # gradient exchange: "one_shot", "two_shot", or "auto" (one shot)
     "model_streams": 2,  # 2: actor and critic kernels on two streams where independent (fork / join); 1: serial
-    "rnn_fused_step": True,  # recurrent training steps as one launch (hidden GEMM with the cell in its epilogue)
+    "rnn_fused_step": "auto",  # recurrent training steps as one launch (hidden GEMM + cell): True, False, "auto" (GRU)
     "gemm_dtype": "bf16",  # GEMM operand precision of the fused path ("bf16")
     "section_timing": False,  # time rollout / returns / update with CUDA events (Perf/section_*) and NVTX ranges
 }
@@ -44,6 +44,8 @@ def resolve_b200_cfg(cfg: dict | None) -> dict:
         if k not in B200_CFG_DEFAULTS:
             raise ValueError(f"Unknown b200_cfg key '{k}'. Valid keys: {list(B200_CFG_DEFAULTS)}")
         out[k] = v
+    if out["rnn_fused_step"] not in (True, False, "auto"):
+        raise ValueError(f"b200_cfg.rnn_fused_step must be True, False or 'auto', got {out['rnn_fused_step']!r}")
     if out["exchange"] not in ("auto", "one_shot", "two_shot"):
         raise ValueError(f"b200_cfg.exchange must be 'auto', 'one_shot' or 'two_shot', got {out['exchange']!r}")
     return out

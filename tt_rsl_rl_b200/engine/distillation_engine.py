@@ -454,7 +454,7 @@ class RecurrentDistillationEngine(DistillationEngine):
         # a training sequence is at most one window of steps over all environments, time-major
         self.L_max = min(self.GL, self.T)
         self.snet = _RecurrentNet(st, self.N, self.L_max, self.N, self.device, self.sm_count,
-                                  bool(alg.b200_cfg["rnn_fused_step"]))
+                                  alg.b200_cfg["rnn_fused_step"])
         self.snet.refresh_shadows()
         self.plan_s = self.snet.head
         self.head_s = self.plan_s.head_cols

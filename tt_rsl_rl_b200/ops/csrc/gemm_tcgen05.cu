@@ -37,6 +37,16 @@ constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMNBoxBytes = 64 * kBK * 2;  // one {64 MN x 64 K} box
 constexpr int kEpiBufBytes = 32 * 32 * 2;  // one epilogue step: 32 rows x 32 bf16 columns (64-byte rows)
 constexpr int kSmemLimit = 227 * 1024;
+// Recurrent-cell epilogue: per warp, five [32 rows x 16 units] fp32 blocks with a row stride of 20 floats (80 bytes:
+// row-per-thread float4 accesses hit distinct banks) through which it turns row-per-thread data into row-contiguous
+// 64-byte global accesses
+constexpr int kRnnRowStride = 20;
+constexpr int kRnnBlockFloats = 32 * kRnnRowStride;
+constexpr int kRnnWarpBytes = 5 * kRnnBlockFloats * 4;
+// fp32-output epilogues: per warp one [32 rows x 32 columns] block, row stride 36 floats (conflict-free float4 row
+// writes and 32-lane reads); rows leave as 128-byte row-contiguous stores
+constexpr int kF32RowStride = 36;
+constexpr int kF32WarpBytes = 32 * kF32RowStride * 4;
 
 // Resident CTAs per SM: the bf16-output epilogues (forward activations, data gradients that also stream the ELU
 // activations in) run two CTAs per SM (BN <= 128, TMEM 2 x 2 x 128 columns) to keep 16 epilogue warps per SM; the
@@ -63,7 +73,9 @@ struct Cfg {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr bool kStaged = !(EPI == kEpiF32 || EPI == kEpiPartialF32 || EPI == kEpiRnnCell);  // bf16 via smem
-  static constexpr int kStagingBytes = kStaged ? kEpiWarps * 2 * kEpiBufBytes : 0;
+  static constexpr int kStagingBytes = kStaged                 ? kEpiWarps * 2 * kEpiBufBytes
+                                       : EPI == kEpiRnnCell     ? kEpiWarps * kRnnWarpBytes
+                                                                : kEpiWarps * kF32WarpBytes;
   static constexpr int kBiasBytes = kStaged ? kEpiWarps * 32 * 4 : 0;
   static constexpr int kColsumBytes = EPI == kEpiDgradElu ? 2 * 4 * BN * 4 : 0;  // double-buffered by tile parity
   static constexpr int kColAccBytes = EPI == kEpiDgradElu ? kColsumMaxN * 4 : 0;   // the CTA's running column sums
@@ -443,96 +455,153 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
       const long long row = tc.m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
-#pragma unroll 1
-      for (int c = slot * 32; c < kRnnUnits; c += kPerQuad * 32) {
-        const int u = u0 + c;  // first hidden unit of the chunk
-        float gh[G][32];
+      const float keep = (row_ok && e.done) ? 1.0f - __ldg(e.done + row) : 1.0f;
+      // Global memory is accessed row-contiguously: lane l moves 16 bytes of row (l >> 2) + 8 i, i = 0..3 (four
+      // lanes per 64-byte row segment); the warp's shared blocks turn that into one row per thread and back.
+      const long long row_base = tc.m0 + q * 32;
+      const int cr = lane >> 2, cq = lane & 3;
+      float* const wbuf = reinterpret_cast<float*>(staging) + ew * (kRnnWarpBytes / 4);
+      // copies between global rows [row_base, row_base + 32) x 16 columns and block `blk` of the warp's buffer
+      auto gather = [&](const float* src, long long ld, int blk) {
+        float4 v[4];
 #pragma unroll
-        for (int g = 0; g < G; ++g) tmem_ld_32x32b_x32(acc + static_cast<uint32_t>(g * kRnnUnits + c), gh[g]);
+        for (int i = 0; i < 4; ++i) {
+          const long long r = row_base + cr + 8 * i;
+          v[i] = r < p.M ? __ldg(reinterpret_cast<const float4*>(src + r * ld) + cq) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<float4*>(wbuf + blk * kRnnBlockFloats + (cr + 8 * i) * kRnnRowStride + 4 * cq) = v[i];
+      };
+      auto scatter = [&](float* dst, long long ld, int blk) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const long long r = row_base + cr + 8 * i;
+          const float4 v =
+              *reinterpret_cast<const float4*>(wbuf + blk * kRnnBlockFloats + (cr + 8 * i) * kRnnRowStride + 4 * cq);
+          if (r < p.M) *(reinterpret_cast<float4*>(dst + r * ld) + cq) = v;
+        }
+      };
+      auto put_row = [&](int blk, const float (&v)[16]) {  // this thread's row of a block
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          *reinterpret_cast<float4*>(wbuf + blk * kRnnBlockFloats + lane * kRnnRowStride + 4 * q4) =
+              make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+      };
+      auto get_row = [&](int blk, float (&v)[16]) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 t4 = *reinterpret_cast<const float4*>(wbuf + blk * kRnnBlockFloats + lane * kRnnRowStride + 4 * q4);
+          v[4 * q4] = t4.x;
+          v[4 * q4 + 1] = t4.y;
+          v[4 * q4 + 2] = t4.z;
+          v[4 * q4 + 3] = t4.w;
+        }
+      };
+      // bf16 rows (32 bytes) of block `blk`: thread-row packs, then lane l stores 16 bytes of row (l >> 1) + 16 i
+      auto scatter_bf16 = [&](void* dst, long long ld, int blk, const float (&v)[16], float scale) {
+        uint4* rowp = reinterpret_cast<uint4*>(wbuf + blk * kRnnBlockFloats + lane * 12);  // 48-byte rows
+        rowp[0] = make_uint4(pack_bf16x2(v[0] * scale, v[1] * scale), pack_bf16x2(v[2] * scale, v[3] * scale),
+                             pack_bf16x2(v[4] * scale, v[5] * scale), pack_bf16x2(v[6] * scale, v[7] * scale));
+        rowp[1] = make_uint4(pack_bf16x2(v[8] * scale, v[9] * scale), pack_bf16x2(v[10] * scale, v[11] * scale),
+                             pack_bf16x2(v[12] * scale, v[13] * scale), pack_bf16x2(v[14] * scale, v[15] * scale));
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int rr = (lane >> 1) + 16 * i;
+          const long long r = row_base + rr;
+          const uint4 w = reinterpret_cast<const uint4*>(wbuf + blk * kRnnBlockFloats + rr * 12)[lane & 1];
+          if (r < p.M)
+            reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dst) + r * ld + (lane & 1) * 8)[0] = w;
+        }
+      };
+#pragma unroll 1
+      for (int c = slot * 16; c < kRnnUnits; c += kPerQuad * 16) {
+        const int u = u0 + c;  // first hidden unit of the sub-chunk
+        float gh[G][16];
+#pragma unroll
+        for (int g = 0; g < G; ++g) tmem_ld_32x32b_x16(acc + static_cast<uint32_t>(g * kRnnUnits + c), gh[g]);
         tmem_wait_ld();
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          const float bl = __ldg(p.bias + g * H + u + lane);  // lane l holds the bias of unit u + l
+          const float bl = __ldg(p.bias + g * H + u + (lane & 15));  // lanes l and l + 16 hold the bias of unit u + l
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) gh[g][jj] += __shfl_sync(0xffffffffu, bl, jj);
+          for (int jj = 0; jj < 16; ++jj) gh[g][jj] += __shfl_sync(0xffffffffu, bl, jj);
         }
-        if (!row_ok) continue;
-        const float keep = e.done ? 1.0f - e.done[row] : 1.0f;
-        const float* gi = e.gi + row * e.ld_gi + u;
+        // inputs: the G gate blocks of gi and the state block (h_in for GRU, c_in for LSTM)
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 4) {
-          float hn[4], cn[4], sv[5][4];
-          if constexpr (G == 3) {  // GRU: r, z, n
-            const float4 xr = *reinterpret_cast<const float4*>(gi + jj);
-            const float4 xz = *reinterpret_cast<const float4*>(gi + H + jj);
-            const float4 xn = *reinterpret_cast<const float4*>(gi + 2 * H + jj);
-            const float4 h4 = *reinterpret_cast<const float4*>(e.h_in + row * e.ld_h_in + u + jj);
-            const float ar[4] = {xr.x, xr.y, xr.z, xr.w}, az[4] = {xz.x, xz.y, xz.z, xz.w};
-            const float an[4] = {xn.x, xn.y, xn.z, xn.w}, hh[4] = {h4.x, h4.y, h4.z, h4.w};
+        for (int g = 0; g < G; ++g) gather(e.gi + g * H + u, e.ld_gi, g);
+        if constexpr (G == 4) gather(e.c_in + u, e.ld_c_in, G);
+        else gather(e.h_in + u, e.ld_h_in, G);
+        __syncwarp();
+        float x[G][16], st[16];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float r = 1.0f / (1.0f + __expf(-(ar[k] + gh[0][jj + k])));
-              const float z = 1.0f / (1.0f + __expf(-(az[k] + gh[1][jj + k])));
-              const float ghn = gh[2][jj + k];
-              const float n = tanhf(an[k] + r * ghn);
-              hn[k] = (1.0f - z) * n + z * hh[k];
-              cn[k] = 0.f;
-              sv[0][k] = r;
-              sv[1][k] = z;
-              sv[2][k] = n;
-              sv[3][k] = ghn;
-              sv[4][k] = 0.f;
-            }
-          } else {  // LSTM: i, f, g, o
-            const float4 xi = *reinterpret_cast<const float4*>(gi + jj);
-            const float4 xf = *reinterpret_cast<const float4*>(gi + H + jj);
-            const float4 xg = *reinterpret_cast<const float4*>(gi + 2 * H + jj);
-            const float4 xo = *reinterpret_cast<const float4*>(gi + 3 * H + jj);
-            const float4 c4 = *reinterpret_cast<const float4*>(e.c_in + row * e.ld_c_in + u + jj);
-            const float ai[4] = {xi.x, xi.y, xi.z, xi.w}, af[4] = {xf.x, xf.y, xf.z, xf.w};
-            const float ag[4] = {xg.x, xg.y, xg.z, xg.w}, ao[4] = {xo.x, xo.y, xo.z, xo.w};
-            const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+        for (int g = 0; g < G; ++g) get_row(g, x[g]);
+        get_row(G, st);
+        __syncwarp();
+        // the cell; saved activations go straight to this thread's row of blocks 0 .. S-1 (inputs are in registers)
+        constexpr int S = G == 4 ? 5 : 4;
+        float hn[16], cn[16];
+        float* my = wbuf + lane * kRnnRowStride;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float ig = 1.0f / (1.0f + __expf(-(ai[k] + gh[0][jj + k])));
-              const float fg = 1.0f / (1.0f + __expf(-(af[k] + gh[1][jj + k])));
-              const float gg = tanhf(ag[k] + gh[2][jj + k]);
-              const float og = 1.0f / (1.0f + __expf(-(ao[k] + gh[3][jj + k])));
-              cn[k] = fg * cc[k] + ig * gg;
-              const float tcn = tanhf(cn[k]);
-              hn[k] = og * tcn;
-              sv[0][k] = ig;
-              sv[1][k] = fg;
-              sv[2][k] = gg;
-              sv[3][k] = og;
-              sv[4][k] = tcn;
-            }
-          }
-          const long long col = u + jj;
-          if (e.h_out)
-            *reinterpret_cast<float4*>(e.h_out + row * e.ld_h_out + col) = make_float4(hn[0], hn[1], hn[2], hn[3]);
-          if (e.h_out_bf16)
-            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(e.h_out_bf16) + row * e.ld_h_out_bf16 + col) =
-                make_uint2(pack_bf16x2(hn[0], hn[1]), pack_bf16x2(hn[2], hn[3]));
-          if (G == 4 && e.c_out)
-            *reinterpret_cast<float4*>(e.c_out + row * e.ld_c_out + col) = make_float4(cn[0], cn[1], cn[2], cn[3]);
-          if (e.next_h)
-            *reinterpret_cast<float4*>(e.next_h + row * e.ld_next_h + col) =
-                make_float4(hn[0] * keep, hn[1] * keep, hn[2] * keep, hn[3] * keep);
-          if (e.next_h_bf16)
-            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(e.next_h_bf16) + row * e.ld_next_h_bf16 + col) =
-                make_uint2(pack_bf16x2(hn[0] * keep, hn[1] * keep), pack_bf16x2(hn[2] * keep, hn[3] * keep));
-          if (G == 4 && e.next_c)
-            *reinterpret_cast<float4*>(e.next_c + row * e.ld_next_c + col) =
-                make_float4(cn[0] * keep, cn[1] * keep, cn[2] * keep, cn[3] * keep);
-          if (e.save) {
-            float* sp = e.save + row * e.ld_save + col;
-#pragma unroll
-            for (int sidx = 0; sidx < (G == 4 ? 5 : 4); ++sidx)
-              *reinterpret_cast<float4*>(sp + sidx * H) = make_float4(sv[sidx][0], sv[sidx][1], sv[sidx][2],
-                                                                      sv[sidx][3]);
+        for (int k = 0; k < 16; ++k) {
+          if constexpr (G == 3) {  // GRU: r, z, n; st = h_in
+            const float r = 1.0f / (1.0f + __expf(-(x[0][k] + gh[0][k])));
+            const float z = 1.0f / (1.0f + __expf(-(x[1][k] + gh[1][k])));
+            const float ghn = gh[2][k];
+            const float n = tanhf(x[2][k] + r * ghn);
+            hn[k] = (1.0f - z) * n + z * st[k];
+            cn[k] = 0.f;
+            my[k] = r;
+            my[kRnnBlockFloats + k] = z;
+            my[2 * kRnnBlockFloats + k] = n;
+            my[3 * kRnnBlockFloats + k] = ghn;
+          } else {  // LSTM: i, f, g, o; st = c_in
+            const float ig = 1.0f / (1.0f + __expf(-(x[0][k] + gh[0][k])));
+            const float fg = 1.0f / (1.0f + __expf(-(x[1][k] + gh[1][k])));
+            const float gg = tanhf(x[2][k] + gh[2][k]);
+            const float og = 1.0f / (1.0f + __expf(-(x[3][k] + gh[3][k])));
+            cn[k] = fg * st[k] + ig * gg;
+            const float tcn = tanhf(cn[k]);
+            hn[k] = og * tcn;
+            my[k] = ig;
+            my[kRnnBlockFloats + k] = fg;
+            my[2 * kRnnBlockFloats + k] = gg;
+            my[3 * kRnnBlockFloats + k] = og;
+            my[4 * kRnnBlockFloats + k] = tcn;
           }
         }
+        __syncwarp();
+        if (e.save) {
+#pragma unroll
+          for (int sidx = 0; sidx < S; ++sidx) scatter(e.save + sidx * H + u, e.ld_save, sidx);
+        }
+        __syncwarp();
+        // fp32 states: h', h' (1 - done), c', c' (1 - done)
+        float hk[16], ck[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          hk[k] = hn[k] * keep;
+          ck[k] = cn[k] * keep;
+        }
+        put_row(0, hn);
+        put_row(1, hk);
+        if constexpr (G == 4) {
+          put_row(2, cn);
+          put_row(3, ck);
+        }
+        __syncwarp();
+        if (e.h_out) scatter(e.h_out + u, e.ld_h_out, 0);
+        if (e.next_h) scatter(e.next_h + u, e.ld_next_h, 1);
+        if constexpr (G == 4) {
+          if (e.c_out) scatter(e.c_out + u, e.ld_c_out, 2);
+          if (e.next_c) scatter(e.next_c + u, e.ld_next_c, 3);
+        }
+        __syncwarp();
+        if (e.h_out_bf16) scatter_bf16(static_cast<__nv_bfloat16*>(e.h_out_bf16) + u, e.ld_h_out_bf16, 0, hn, 1.0f);
+        if (e.next_h_bf16)
+          scatter_bf16(static_cast<__nv_bfloat16*>(e.next_h_bf16) + u, e.ld_next_h_bf16, 1, hn, keep);
+        __syncwarp();
       }
       // accumulator b fully read by this warp: hand it back to the MMA issuer
       tc_fence_before();
@@ -545,6 +614,10 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
     const int q = warp & 3;  // TMEM lane quadrant: hardware rule warp % 4
     const int slot = ew >> 2;
     constexpr int CW = BN >= 64 ? 64 : 32;  // columns per chunk
+    float* const fbuf = reinterpret_cast<float*>(staging) + ew * (kF32WarpBytes / 4);
+    // 16-byte row stores need 16-byte aligned rows
+    const bool vec_ok = (p.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+                        (EPI != kEpiPartialF32 || p.split_stride % 4 == 0);
     int j = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
       const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
@@ -558,8 +631,6 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
         break;
       }
       tc_fence_after();
-      const int row = tc.m0 + q * 32 + lane;
-      const bool row_ok = row < p.M;
       const uint32_t acc = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * C::kAccCols);
 #pragma unroll 1
       for (int c = slot * CW; c < BN; c += kPerQuad * CW) {
@@ -579,20 +650,31 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
               for (int jj = 0; jj < 32; ++jj) v[jj] += __shfl_sync(0xffffffffu, my_bias, jj);
             }
           }
+          // the warp's 32 x 32 block goes through shared memory so that rows leave contiguously (a row-per-thread
+          // store would touch 32 rows per instruction)
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            *reinterpret_cast<float4*>(fbuf + lane * kF32RowStride + 4 * c4) =
+                make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+          __syncwarp();
           float* o = static_cast<float*>(p.out) +
-                     (EPI == kEpiPartialF32 ? static_cast<long long>(tc.split) * p.split_stride : 0ll) +
-                     static_cast<size_t>(row) * p.ldo + sb;
-          if (row_ok) {
-            if (sb + 32 <= p.N && (p.ldo % 4) == 0) {
+                     (EPI == kEpiPartialF32 ? static_cast<long long>(tc.split) * p.split_stride : 0ll) + sb;
+          const long long row0 = tc.m0 + q * 32;
+          if (vec_ok && sb + 32 <= p.N) {
+            // lane l: 16 bytes of row 4 i + l / 8 (eight lanes per 128-byte row)
 #pragma unroll
-              for (int jj = 0; jj < 32; jj += 4)
-                *reinterpret_cast<float4*>(o + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
-            } else {
-#pragma unroll
-              for (int jj = 0; jj < 32; ++jj)
-                if (sb + jj < p.N) o[jj] = v[jj];
+            for (int i = 0; i < 8; ++i) {
+              const int rr = 4 * i + (lane >> 3);
+              const float4 val = *reinterpret_cast<const float4*>(fbuf + rr * kF32RowStride + 4 * (lane & 7));
+              if (row0 + rr < p.M) *reinterpret_cast<float4*>(o + (row0 + rr) * p.ldo + 4 * (lane & 7)) = val;
             }
+          } else {
+            // lane l: column sb + l of every row
+#pragma unroll 4
+            for (int rr = 0; rr < 32; ++rr)
+              if (row0 + rr < p.M && sb + lane < p.N) o[(row0 + rr) * p.ldo + lane] = fbuf[rr * kF32RowStride + lane];
           }
+          __syncwarp();
         }
       }
       // accumulator b fully read by this warp: hand it back to the MMA issuer
@@ -746,7 +828,7 @@ cudaError_t gemm_launch(const GemmParams& p, cudaStream_t stream) {
     const RnnCellEpi& e = p.cell;
     const int G = e.lstm ? 4 : 3;
     auto f32ok = [](const void* q, long long ld) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0 && ld % 4 == 0; };
-    auto bf16ok = [](const void* q, long long ld) { return (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ld % 4 == 0; };
+    auto bf16ok = [](const void* q, long long ld) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0 && ld % 8 == 0; };
     if (am || bm || e.H <= 0 || e.H % kRnnUnits != 0 || p.K != e.H || p.N != G * e.H || p.bias == nullptr ||
         e.gi == nullptr || !f32ok(e.gi, e.ld_gi) || (e.lstm ? e.c_in == nullptr : e.h_in == nullptr))
       return cudaErrorInvalidValue;

@@ -29,7 +29,7 @@ enum GemmEpilogue : int {
 // g*H + u0 + kRnnUnits - 1 for g = 0 .. G-1, loaded as G boxes), so its epilogue owns whole units and applies the
 // torch.nn.GRU / torch.nn.LSTM cell with the gate order and outputs of rnn_kernels.cuh RnnCellFwdArgs. H must be a
 // multiple of kRnnUnits; fp32 arrays need 16-byte aligned bases and pitches that are multiples of 4 elements, bf16
-// arrays 8-byte aligned bases and pitches that are multiples of 4. No output may alias the A operand.
+// arrays 16-byte aligned bases and pitches that are multiples of 8. No output may alias the A operand.
 constexpr int kRnnUnits = 64;
 struct RnnCellEpi {
   int H = 0, lstm = 0;
