@@ -792,6 +792,13 @@ cudaError_t launch_bn_t(const GemmParams& p, cudaStream_t stream) {
   constexpr bool one_cta = Shape<EPI, WIDE>::kMinBlocks == 1;
   if (!B_MN && p.N <= 32) return launch_t<32, A_MN, B_MN, EPI, WIDE>(p, stream);
   if (p.N <= 64) return launch_t<64, A_MN, B_MN, EPI, WIDE>(p, stream);
+  if constexpr (EPI == kEpiF32) {
+    // few row tiles (a recurrent step of a few thousand rows): narrower tiles, so that at least half the SMs work
+    // (a 4096 x 256 output with K = 768 runs on 128 CTAs instead of 32)
+    const int m_tiles = (p.M + kBM - 1) / kBM, half = sm_count() / 2;
+    if (m_tiles * ((p.N + 127) / 128) < half) return launch_t<64, A_MN, B_MN, EPI, WIDE>(p, stream);
+    if (p.N > 128 && m_tiles * ((p.N + 255) / 256) < half) return launch_t<128, A_MN, B_MN, EPI, WIDE>(p, stream);
+  }
   if (p.N <= 128 || !one_cta) return launch_t<128, A_MN, B_MN, EPI, WIDE>(p, stream);
   if constexpr (one_cta) return launch_t<256, A_MN, B_MN, EPI, WIDE>(p, stream);
   return cudaErrorInvalidValue;

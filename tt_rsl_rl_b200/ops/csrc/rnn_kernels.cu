@@ -23,13 +23,15 @@ __global__ void __launch_bounds__(256) rnn_cell_fwd_kernel(const RnnCellFwdArgs 
     const int j = static_cast<int>(e - static_cast<long long>(row) * H);
     const float* gi = a.gi + row * a.ld_gi;
     const float* gh = a.gh + row * a.ld_gh;
-    const float h = a.h_in[row * a.ld_h_in + j];
+    // inputs are never written by this launch (outputs may alias h_in only element for element): non-coherent
+    // loads, which the compiler may issue ahead of the previous element's stores
+    const float h = __ldg(a.h_in + row * a.ld_h_in + j);
     float hn, cn = 0.f;
     if (!a.lstm) {
-      const float r = sigmoid_f(gi[j] + gh[j]);
-      const float z = sigmoid_f(gi[H + j] + gh[H + j]);
-      const float ghn = gh[2 * H + j];
-      const float n = tanhf(gi[2 * H + j] + r * ghn);
+      const float r = sigmoid_f(__ldg(gi + j) + __ldg(gh + j));
+      const float z = sigmoid_f(__ldg(gi + H + j) + __ldg(gh + H + j));
+      const float ghn = __ldg(gh + 2 * H + j);
+      const float n = tanhf(__ldg(gi + 2 * H + j) + r * ghn);
       hn = (1.0f - z) * n + z * h;
       if (a.save) {
         float* sv = a.save + row * a.ld_save;
@@ -39,11 +41,11 @@ __global__ void __launch_bounds__(256) rnn_cell_fwd_kernel(const RnnCellFwdArgs 
         sv[3 * H + j] = ghn;
       }
     } else {
-      const float c = a.c_in[row * a.ld_c_in + j];
-      const float ig = sigmoid_f(gi[j] + gh[j]);
-      const float fg = sigmoid_f(gi[H + j] + gh[H + j]);
-      const float gg = tanhf(gi[2 * H + j] + gh[2 * H + j]);
-      const float og = sigmoid_f(gi[3 * H + j] + gh[3 * H + j]);
+      const float c = __ldg(a.c_in + row * a.ld_c_in + j);
+      const float ig = sigmoid_f(__ldg(gi + j) + __ldg(gh + j));
+      const float fg = sigmoid_f(__ldg(gi + H + j) + __ldg(gh + H + j));
+      const float gg = tanhf(__ldg(gi + 2 * H + j) + __ldg(gh + 2 * H + j));
+      const float og = sigmoid_f(__ldg(gi + 3 * H + j) + __ldg(gh + 3 * H + j));
       cn = fg * c + ig * gg;
       const float tc = tanhf(cn);
       hn = og * tc;
@@ -59,7 +61,7 @@ __global__ void __launch_bounds__(256) rnn_cell_fwd_kernel(const RnnCellFwdArgs 
     }
     if (a.h_out) a.h_out[row * a.ld_h_out + j] = hn;
     if (a.h_out_bf16) store_bf16(a.h_out_bf16, a.ld_h_out_bf16, row, j, hn);
-    const float keep = a.done ? 1.0f - a.done[row] : 1.0f;
+    const float keep = a.done ? 1.0f - __ldg(a.done + row) : 1.0f;
     if (a.next_h) a.next_h[row * a.ld_next_h + j] = hn * keep;
     if (a.next_h_bf16) store_bf16(a.next_h_bf16, a.ld_next_h_bf16, row, j, hn * keep);
     if (a.lstm && a.next_c) a.next_c[row * a.ld_next_c + j] = cn * keep;
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(256) rnn_pad_entries_kernel(const float* done,
 
 int elementwise_grid(long long n) {
   long long blocks = (n + 255) / 256;
-  const long long cap = 148LL * 8;
+  const long long cap = 148LL * 32;  // one element per thread up to ~1.2 M elements (a minibatch step)
   return static_cast<int>(blocks < cap ? (blocks < 1 ? 1 : blocks) : cap);
 }
 

@@ -73,7 +73,7 @@ struct RnnCellBwdArgs {
 };
 
 // Rows handled by one block of the backward cell (the row count of its column-sum partials is ceil(rows / this)).
-constexpr int kRnnBwdRows = 8;
+constexpr int kRnnBwdRows = 4;
 inline int rnn_bwd_blocks(int rows) { return (rows + kRnnBwdRows - 1) / kRnnBwdRows; }
 
 // dst = src (1 - done) for the fp32 state (and bf16 copy, and LSTM cell state); src may alias dst.
