@@ -69,9 +69,10 @@ def test_cell_forward_and_masks(lstm):
 
 
 @pytest.mark.parametrize("lstm", [False, True])
-def test_cell_backward_matches_autograd(lstm):
+@pytest.mark.parametrize("H", [256, 480, 1024])
+def test_cell_backward_matches_autograd(lstm, H):
     torch.manual_seed(1)
-    rows, H = 700, 256
+    rows = 700
     G, S = (4, 5) if lstm else (3, 4)
     gi = torch.randn(rows, G * H, device="cuda", requires_grad=True)
     gh = torch.randn(rows, G * H, device="cuda", requires_grad=True)

@@ -73,14 +73,17 @@ constexpr int kMaxColIter = 4;  // H <= 1024
 
 // A block takes kRnnBwdRows rows; thread t handles hidden units t, t + 256, ... of every row and keeps the column
 // sums of its gate gradients in registers (written once per block: deterministic partials).
+// KI = ceil(H / 256) unit slots per thread (a kernel per KI: the column-sum registers of unused slots would cost
+// occupancy; H = 256 runs KI = 1).
+template <int KI>
 __global__ void __launch_bounds__(kBwdThreads) rnn_cell_bwd_kernel(const RnnCellBwdArgs a) {
   const int H = a.H;
   const int G = a.lstm ? 4 : 3;
   const int row0 = blockIdx.x * kRnnBwdRows;
-  float cs_gi[4][kMaxColIter];
-  float cs_ghn[kMaxColIter];
+  float cs_gi[4][KI];
+  float cs_ghn[KI];
 #pragma unroll
-  for (int k = 0; k < kMaxColIter; ++k) {
+  for (int k = 0; k < KI; ++k) {
     cs_ghn[k] = 0.f;
 #pragma unroll
     for (int g = 0; g < 4; ++g) cs_gi[g][k] = 0.f;
@@ -91,7 +94,7 @@ __global__ void __launch_bounds__(kBwdThreads) rnn_cell_bwd_kernel(const RnnCell
     const float keep = a.done ? 1.0f - a.done[row] : 1.0f;
     const float* sv = a.save + row * a.ld_save;
 #pragma unroll
-    for (int k = 0; k < kMaxColIter; ++k) {
+    for (int k = 0; k < KI; ++k) {
       const int j = threadIdx.x + k * kBwdThreads;
       if (j >= H) break;
       float dh = a.dh_head[row * a.ld_dh_head + j];
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(kBwdThreads) rnn_cell_bwd_kernel(const RnnCell
   }
   const long long GH = static_cast<long long>(G) * H;
 #pragma unroll
-  for (int k = 0; k < kMaxColIter; ++k) {
+  for (int k = 0; k < KI; ++k) {
     const int j = threadIdx.x + k * kBwdThreads;
     if (j >= H) break;
     // one partial row per block, accumulated over the steps of a BPTT sweep (steps run in stream order)
@@ -223,7 +226,11 @@ cudaError_t rnn_cell_bwd(const RnnCellBwdArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   if (!a.lstm && (!a.h_in || !a.dgh)) return cudaErrorInvalidValue;
   if (a.lstm && !a.c_in) return cudaErrorInvalidValue;
-  rnn_cell_bwd_kernel<<<rnn_bwd_blocks(a.rows), kBwdThreads, 0, s>>>(a);
+  const int ki = (a.H + kBwdThreads - 1) / kBwdThreads;
+  const int blocks = rnn_bwd_blocks(a.rows);
+  if (ki == 1) rnn_cell_bwd_kernel<1><<<blocks, kBwdThreads, 0, s>>>(a);
+  else if (ki == 2) rnn_cell_bwd_kernel<2><<<blocks, kBwdThreads, 0, s>>>(a);
+  else rnn_cell_bwd_kernel<4><<<blocks, kBwdThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
