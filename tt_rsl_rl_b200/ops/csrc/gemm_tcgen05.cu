@@ -154,6 +154,9 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
     if constexpr (C::kStaged) tma_prefetch_desc(&tmO);
     if constexpr (EPI == kEpiDgradElu) tma_prefetch_desc(&tmX);
   }
+  // Launched with programmatic stream serialization: the barrier setup above overlaps the previous kernel's tail.
+  // Nothing before this wait touches global memory or TMEM.
+  griddep_wait();
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
@@ -162,6 +165,9 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Every CTA of this grid holds its TMEM now, so the next kernel may be scheduled: it waits for this grid's
+  // completion before it allocates TMEM or touches memory, so a waiting CTA never holds what this grid needs.
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -734,6 +740,16 @@ int sm_count() {
   return n;
 }
 
+// Programmatic dependent launch of every GEMM (the next launch's setup overlaps this one's tail); RLB_PDL=0 in the
+// environment turns it off (read once).
+bool pdl_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("RLB_PDL");
+    return e == nullptr || e[0] != '0';
+  }();
+  return v;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, bool WIDE>
 cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN, EPI, WIDE>;
@@ -763,9 +779,17 @@ cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   const long long slots = static_cast<long long>(sm_count()) * C::kMinBlocks;
   const int grid = static_cast<int>(tiles < slots ? tiles : slots);
   if (EPI == kEpiDgradElu && p.colsum != nullptr && grid > p.colsum_rows) return cudaErrorInvalidValue;
-  kern<<<grid, Shape<EPI, WIDE>::kThreads, C::kSmemBytes, stream>>>(ta, tb, to, tx, p, num_kb, n_tiles, m_tiles,
-                                                                    p.splits);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Shape<EPI, WIDE>::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tx, p, num_kb, n_tiles, m_tiles, p.splits);
 }
 
 // Layout choice for the bf16-output epilogues. Measured on the benchmark shapes (393,216 rows): the one-CTA,

@@ -211,6 +211,13 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// ---- programmatic dependent launch --------------------------------------------------------------------------------
+// A kernel launched with programmatic stream serialization may start while the previous kernel of its stream is still
+// running; griddep_wait() returns once that kernel has completed and its memory is visible. griddep_launch_dependents()
+// allows the next kernel of the stream to be scheduled once every CTA of this grid has called it (or exited).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---- UMMA descriptors --------------------------------------------------------------------------------------------
 // Shared-memory matrix descriptor (sm100 "version 1"), 128-byte swizzle. Addresses/offsets are in bytes.
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
