@@ -87,3 +87,27 @@ def test_noalloc_header_declares_the_definition():
 
     assert params("gae_noalloc.h") == params("gae_noalloc.cu")
     assert '#include "gae_noalloc.h"' in (CSRC / "gae_noalloc.cu").read_text()
+
+
+def test_dependent_launches_wait_before_touching_memory():
+    """Every kernel launched with programmatic stream serialization waits for the previous kernel before anything
+    else; the GEMM waits before it allocates TMEM and lets dependents start only after it holds its TMEM (so a
+    dependent waiting on it never holds TMEM this grid needs)."""
+    srcs = {p: p.read_text() for p in CSRC.glob("*.cu")}
+    launched = set()
+    for text in srcs.values():
+        launched.update(re.findall(r"launch_pdl\((\w+)", text))
+    assert {"prep_obs_kernel", "gather_minibatch_kernel", "rnn_cell_bwd_kernel"} <= launched
+    for name in launched:
+        bodies = [t[m.end():] for t in srcs.values()
+                  for m in re.finditer(r"__global__ void[^;{]*?\b" + name + r"\s*\([^{]*\{", t)]
+        assert bodies, name
+        for body in bodies:
+            first = body.strip().splitlines()[0]
+            assert first.startswith("griddep_wait();"), (name, first)
+    gemm = srcs[CSRC / "gemm_tcgen05.cu"]
+    kernel = gemm[gemm.index("gemm_tc_kernel(const __grid_constant__"):]
+    i_wait, i_alloc, i_trigger = (kernel.index("griddep_wait();"), kernel.index("tmem_alloc(tmem_slot"),
+                                  kernel.index("griddep_launch_dependents();"))
+    assert i_wait < i_alloc < i_trigger
+    assert "cudaLaunchKernelEx" in gemm

@@ -740,16 +740,6 @@ int sm_count() {
   return n;
 }
 
-// Programmatic dependent launch of every GEMM (the next launch's setup overlaps this one's tail); RLB_PDL=0 in the
-// environment turns it off (read once).
-bool pdl_enabled() {
-  static const bool v = [] {
-    const char* e = std::getenv("RLB_PDL");
-    return e == nullptr || e[0] != '0';
-  }();
-  return v;
-}
-
 template <int BN, bool A_MN, bool B_MN, int EPI, bool WIDE>
 cudaError_t launch_t(const GemmParams& p, cudaStream_t stream) {
   using C = Cfg<BN, EPI, WIDE>;
@@ -838,6 +828,16 @@ cudaError_t launch_bn(const GemmParams& p, cudaStream_t stream) {
 }
 
 }  // namespace
+
+// Programmatic dependent launch of the framework's kernels (the next launch's setup overlaps this one's tail);
+// RLB_PDL=0 in the environment turns it off (read once).
+bool pdl_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("RLB_PDL");
+    return e == nullptr || e[0] != '0';
+  }();
+  return v;
+}
 
 cudaError_t gemm_launch(const GemmParams& p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.splits < 1) return cudaErrorInvalidValue;

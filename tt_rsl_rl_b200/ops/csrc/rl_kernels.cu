@@ -29,6 +29,8 @@ __device__ __forceinline__ float load_flag(const void* p, int dtype, int i) {
 constexpr int kPrepMaxD = 1024;
 // One warp per row; lanes walk the columns of each group (coalesced), normaliser constants staged in shared memory.
 __global__ void __launch_bounds__(256) prep_obs_kernel(const PrepObsArgs a, int D) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   __shared__ float s_mean[kPrepMaxD];
   __shared__ float s_inv[kPrepMaxD];
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
@@ -75,6 +77,8 @@ __device__ __forceinline__ void last_block_advance(uint64_t* counter, unsigned i
 }
 
 __global__ void gaussian_sample_kernel(const SampleArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint64_t offset = *a.counter;
@@ -118,6 +122,8 @@ __global__ void gaussian_sample_kernel(const SampleArgs a) {
 // the four normals of one Philox block (counter word 1 = action group), so each block is computed once instead of by
 // four lanes; same streams and results as gaussian_sample_kernel.
 __global__ void __launch_bounds__(256) gaussian_sample_rows8_kernel(const SampleArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int l8 = lane & 7;
   const uint64_t offset = *a.counter;
@@ -163,6 +169,8 @@ __global__ void __launch_bounds__(256) gaussian_sample_rows8_kernel(const Sample
 // process_step
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void process_step_kernel(const ProcessArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.rows; i += gridDim.x * blockDim.x) {
     float r = a.rewards[i];
     if (a.intrinsic) r += a.intrinsic[i];
@@ -346,6 +354,8 @@ __device__ __forceinline__ int perm_col(const int* p, int n, unsigned int* statu
 }
 
 __global__ void __launch_bounds__(256, 3) gather_minibatch_kernel(const GatherArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   __shared__ __align__(16) float s_mean[kGatherModels][kGatherMaxD];
   __shared__ __align__(16) float s_inv[kGatherModels][kGatherMaxD];
   int max_rows = 0;
@@ -478,6 +488,8 @@ __device__ __forceinline__ void max_grad_split(float a, float b, float& ga, floa
 // and std, scalars) and only then computes, so each warp keeps its rows' loads in flight together.
 template <bool kSym>
 __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel(const PpoLossArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const float invP = 1.0f / static_cast<float>(a.aug ? a.B : a.n0);
@@ -733,6 +745,8 @@ constexpr int kLoss8Warps = 8;
 static_assert(kLoss8Warps * 4 == kLossRowsPerBlock, "row groups of the two loss kernels must match");
 
 __global__ void __launch_bounds__(kLoss8Warps * 32, 2) ppo_loss_rows8_kernel(const PpoLossArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 3;   // row of the warp's four
@@ -948,6 +962,8 @@ constexpr int kMseRowsPerWarp = 4;
 constexpr int kMseRowsPerBlock = kMseWarps * kMseRowsPerWarp;
 
 __global__ void __launch_bounds__(kMseWarps * 32) mse_grad_kernel(const MseArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float w_last = a.last_weight ? *a.last_weight : 1.0f;
   const float n_rows = a.denom_rows > 0 ? static_cast<float>(a.denom_rows) : static_cast<float>(a.rows - 1) + w_last;
@@ -1028,6 +1044,8 @@ constexpr int kReduceWarps = 8;
 __global__ void __launch_bounds__(kReduceWarps * 32)
     reduce_segments_kernel(const ReduceSegment* __restrict__ segs, int nseg, int total_chunks, float* send0,
                            float* send1, const unsigned int* epoch, int accumulate) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   float* dst_base = (((epoch ? *epoch : 0u) + 1u) & 1u) ? send1 : send0;
   const int warps = gridDim.x * kReduceWarps;
@@ -1535,21 +1553,21 @@ cudaError_t prep_obs(const PrepObsArgs& a, cudaStream_t s) {
   int D = 0;
   for (int g = 0; g < a.groups; ++g) D += a.width[g];
   if (a.groups < 1 || a.groups > kMaxObsGroups || a.rows <= 0 || D > kPrepMaxD) return cudaErrorInvalidValue;
-  prep_obs_kernel<<<grid_for(a.rows, 8, 148 * 16), 256, 0, s>>>(a, D);
+  launch_pdl(prep_obs_kernel, dim3(grid_for(a.rows, 8, 148 * 16)), dim3(256), 0, s, a, D);
   return cudaGetLastError();
 }
 
 cudaError_t gaussian_sample(const SampleArgs& a, cudaStream_t s) {
   if (a.A > 64 || a.rows <= 0) return cudaErrorInvalidValue;
   if (a.A <= 32)
-    gaussian_sample_rows8_kernel<<<grid_for(a.rows, 32), 256, 0, s>>>(a);
+    launch_pdl(gaussian_sample_rows8_kernel, dim3(grid_for(a.rows, 32)), dim3(256), 0, s, a);
   else
-    gaussian_sample_kernel<<<grid_for(a.rows, 8), 256, 0, s>>>(a);
+    launch_pdl(gaussian_sample_kernel, dim3(grid_for(a.rows, 8)), dim3(256), 0, s, a);
   return cudaGetLastError();
 }
 
 cudaError_t process_step(const ProcessArgs& a, cudaStream_t s) {
-  process_step_kernel<<<grid_for(a.rows, 256), 256, 0, s>>>(a);
+  launch_pdl(process_step_kernel, dim3(grid_for(a.rows, 256)), dim3(256), 0, s, a);
   return cudaGetLastError();
 }
 
@@ -1583,7 +1601,7 @@ cudaError_t gather_minibatch(const GatherArgs& a, cudaStream_t s) {
     if (a.dim[m] > kGatherMaxD || a.rows[m] < 1 || a.rows[m] > a.copies * a.B) return cudaErrorInvalidValue;
     max_rows = max(max_rows, a.rows[m]);
   }
-  gather_minibatch_kernel<<<grid_for(max_rows, 8 * kGatherRows, 148 * 16), 256, 0, s>>>(a);
+  launch_pdl(gather_minibatch_kernel, dim3(grid_for(max_rows, 8 * kGatherRows, 148 * 16)), dim3(256), 0, s, a);
   return cudaGetLastError();
 }
 
@@ -1618,11 +1636,11 @@ cudaError_t ppo_loss(const PpoLossArgs& a, cudaStream_t s) {
   const bool aligned = (reinterpret_cast<uintptr_t>(a.d_head) & 7) == 0 && (a.ld_dhead % 4) == 0 &&
                        (a.ld_dvalue != 8 || (reinterpret_cast<uintptr_t>(a.d_value) & 15) == 0);
   if (a.copies > 1)
-    ppo_loss_kernel<true><<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
+    launch_pdl(ppo_loss_kernel<true>, dim3(ppo_loss_blocks(a.B)), dim3(kLossWarps * 32), 0, s, a);
   else if (a.A <= 32 && aligned)
-    ppo_loss_rows8_kernel<<<ppo_loss_blocks(a.B), kLoss8Warps * 32, 0, s>>>(a);
+    launch_pdl(ppo_loss_rows8_kernel, dim3(ppo_loss_blocks(a.B)), dim3(kLoss8Warps * 32), 0, s, a);
   else
-    ppo_loss_kernel<false><<<ppo_loss_blocks(a.B), kLossWarps * 32, 0, s>>>(a);
+    launch_pdl(ppo_loss_kernel<false>, dim3(ppo_loss_blocks(a.B)), dim3(kLossWarps * 32), 0, s, a);
   return cudaGetLastError();
 }
 
@@ -1638,8 +1656,8 @@ cudaError_t reduce_segments(const ReduceSegment* segs_dev, int nseg, int total_c
   }
   const int want = (total_chunks + kReduceWarps - 1) / kReduceWarps;
   const int grid = want < sms * 8 ? want : sms * 8;  // up to 64 resident warps per SM
-  reduce_segments_kernel<<<grid, kReduceWarps * 32, 0, s>>>(segs_dev, nseg, total_chunks, send0, send1, epoch,
-                                                            accumulate);
+  launch_pdl(reduce_segments_kernel, dim3(grid), dim3(kReduceWarps * 32), 0, s, segs_dev, nseg, total_chunks, send0,
+             send1, epoch, accumulate);
   return cudaGetLastError();
 }
 
@@ -1648,6 +1666,8 @@ __global__ void __launch_bounds__(256) rnd_intrinsic_kernel(const float* __restr
                                                             int dim, const float* __restrict__ weight,
                                                             float* __restrict__ out, float* __restrict__ disc,
                                                             float gamma) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const float w = disc ? 1.0f : *weight;
   for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < rows; i += (gridDim.x * blockDim.x) >> 5) {
@@ -1677,8 +1697,8 @@ __global__ void __launch_bounds__(256) rnd_reward_scale_kernel(float* __restrict
 cudaError_t rnd_intrinsic(const float* target, int ld_target, const float* pred, int ld_pred, int rows, int dim,
                           const float* weight, float* out, float* disc, float gamma, cudaStream_t s) {
   if (rows <= 0 || dim <= 0) return cudaErrorInvalidValue;
-  rnd_intrinsic_kernel<<<grid_for(rows, 8, 148 * 16), 256, 0, s>>>(target, ld_target, pred, ld_pred, rows, dim,
-                                                                    weight, out, disc, gamma);
+  launch_pdl(rnd_intrinsic_kernel, dim3(grid_for(rows, 8, 148 * 16)), dim3(256), 0, s, target, ld_target, pred,
+             ld_pred, rows, dim, weight, out, disc, gamma);
   return cudaGetLastError();
 }
 
@@ -1696,7 +1716,7 @@ int mse_blocks(int rows) {
 cudaError_t mse_grad(const MseArgs& a, cudaStream_t s) {
   if (a.A > 64 || a.rows <= 0 || a.ld_grad > 64 || a.head_cols > 64 || a.head_cols < a.A || a.ld_grad < a.A)
     return cudaErrorInvalidValue;
-  mse_grad_kernel<<<mse_blocks(a.rows), kMseWarps * 32, 0, s>>>(a);
+  launch_pdl(mse_grad_kernel, dim3(mse_blocks(a.rows)), dim3(kMseWarps * 32), 0, s, a);
   return cudaGetLastError();
 }
 

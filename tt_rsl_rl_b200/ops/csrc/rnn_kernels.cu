@@ -3,6 +3,7 @@
 #include <cuda_bf16.h>
 
 #include "rnn_kernels.cuh"
+#include "sm100_primitives.cuh"
 
 namespace rlb {
 namespace {
@@ -15,6 +16,8 @@ __device__ __forceinline__ void store_bf16(void* base, long long ld, int row, in
 
 // one thread per (row, hidden unit)
 __global__ void __launch_bounds__(256) rnn_cell_fwd_kernel(const RnnCellFwdArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const long long total = static_cast<long long>(a.rows) * a.H;
   const int H = a.H;
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
@@ -77,6 +80,8 @@ constexpr int kMaxColIter = 4;  // H <= 1024
 // occupancy; H = 256 runs KI = 1).
 template <int KI>
 __global__ void __launch_bounds__(kBwdThreads) rnn_cell_bwd_kernel(const RnnCellBwdArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const int H = a.H;
   const int G = a.lstm ? 4 : 3;
   const int row0 = blockIdx.x * kRnnBwdRows;
@@ -165,6 +170,8 @@ __global__ void __launch_bounds__(kBwdThreads) rnn_cell_bwd_kernel(const RnnCell
 }
 
 __global__ void __launch_bounds__(256) rnn_mask_kernel(const RnnMaskArgs a) {
+  griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
+  griddep_launch_dependents();
   const long long total = static_cast<long long>(a.rows) * a.H;
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -217,7 +224,7 @@ cudaError_t rnn_pad_entries(const float* done, int T, int N, int lo, int Be, flo
 
 cudaError_t rnn_cell_fwd(const RnnCellFwdArgs& a, cudaStream_t s) {
   if (a.rows <= 0 || a.H <= 0 || !a.gi || !a.gh || !a.h_in || (a.lstm && !a.c_in)) return cudaErrorInvalidValue;
-  rnn_cell_fwd_kernel<<<elementwise_grid(static_cast<long long>(a.rows) * a.H), 256, 0, s>>>(a);
+  launch_pdl(rnn_cell_fwd_kernel, dim3(elementwise_grid(static_cast<long long>(a.rows) * a.H)), dim3(256), 0, s, a);
   return cudaGetLastError();
 }
 
@@ -228,15 +235,15 @@ cudaError_t rnn_cell_bwd(const RnnCellBwdArgs& a, cudaStream_t s) {
   if (a.lstm && !a.c_in) return cudaErrorInvalidValue;
   const int ki = (a.H + kBwdThreads - 1) / kBwdThreads;
   const int blocks = rnn_bwd_blocks(a.rows);
-  if (ki == 1) rnn_cell_bwd_kernel<1><<<blocks, kBwdThreads, 0, s>>>(a);
-  else if (ki == 2) rnn_cell_bwd_kernel<2><<<blocks, kBwdThreads, 0, s>>>(a);
-  else rnn_cell_bwd_kernel<4><<<blocks, kBwdThreads, 0, s>>>(a);
+  if (ki == 1) launch_pdl(rnn_cell_bwd_kernel<1>, dim3(blocks), dim3(kBwdThreads), 0, s, a);
+  else if (ki == 2) launch_pdl(rnn_cell_bwd_kernel<2>, dim3(blocks), dim3(kBwdThreads), 0, s, a);
+  else launch_pdl(rnn_cell_bwd_kernel<4>, dim3(blocks), dim3(kBwdThreads), 0, s, a);
   return cudaGetLastError();
 }
 
 cudaError_t rnn_mask(const RnnMaskArgs& a, cudaStream_t s) {
   if (a.rows <= 0 || a.H <= 0 || !a.src_h) return cudaErrorInvalidValue;
-  rnn_mask_kernel<<<elementwise_grid(static_cast<long long>(a.rows) * a.H), 256, 0, s>>>(a);
+  launch_pdl(rnn_mask_kernel, dim3(elementwise_grid(static_cast<long long>(a.rows) * a.H)), dim3(256), 0, s, a);
   return cudaGetLastError();
 }
 
