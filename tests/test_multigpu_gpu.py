@@ -53,9 +53,20 @@ def _cfg(kind: str) -> dict:
                           "state_normalization": True}
         alg["symmetry_cfg"] = {"data_augmentation_func": _mirror, "use_data_augmentation": True,
                                "use_mirror_loss": True, "mirror_loss_coeff": 1.0}
-    elif kind in ("gru", "lstm"):
+    elif kind in ("gru", "lstm", "gru_rnd"):
         for k in ("actor", "critic"):
-            cfg[k].update({"class_name": "RNNModel", "rnn_type": kind, "rnn_hidden_dim": 64})
+            cfg[k].update({"class_name": "RNNModel", "rnn_type": kind[:4].rstrip("_"), "rnn_hidden_dim": 64})
+        if kind == "gru_rnd":
+            cfg["obs_groups"]["rnd_state"] = ["critic"]
+            alg["rnd_cfg"] = {"num_outputs": 8, "predictor_hidden_dims": [64], "target_hidden_dims": [64],
+                              "weight": 0.5, "state_normalization": True}
+    elif kind == "distill_rnn":
+        cfg = {"num_steps_per_env": 8, "save_interval": 1000,
+               "obs_groups": {"student": ["policy"], "teacher": ["critic"]},
+               "algorithm": {"class_name": "Distillation", "num_learning_epochs": 2, "gradient_length": 3,
+                             "b200_cfg": {"comm_timeout_ms": 20000, "engine": "cuda"}},
+               "student": dict(mlp(dist), class_name="RNNModel", rnn_type="gru", rnn_hidden_dim=64),
+               "teacher": dict(mlp({}), class_name="RNNModel", rnn_type="lstm", rnn_hidden_dim=64)}
     elif kind == "distill":
         cfg = {"num_steps_per_env": 8, "save_interval": 1000,
                "obs_groups": {"student": ["policy"], "teacher": ["critic"]},
@@ -82,15 +93,15 @@ def _worker(rank: int, world: int, port: int, out_dir: str, kind: str = "mlp") -
     cfg = _cfg(kind)
     env = LinearGaussianVecEnv(512, obs_dim=48, num_actions=12, privileged_dim=3, device=f"cuda:{rank}",
                                seed=10 + rank, reset_prob=0.02)
-    runner_cls = DistillationRunner if kind == "distill" else OnPolicyRunner
+    runner_cls = DistillationRunner if kind.startswith("distill") else OnPolicyRunner
     runner = runner_cls(env, cfg, log_dir=None, device=f"cuda:{rank}")
-    if kind == "distill":
+    if kind.startswith("distill"):
         runner.alg.teacher_loaded = True
     assert runner.alg.engine is not None and runner.alg.engine.comm is not None
     runner.learn(3)
     eng = runner.alg.engine
     flat = eng.flat.double()
-    norm = (runner.alg.student if kind == "distill" else runner.alg.actor).obs_normalizer
+    norm = (runner.alg.student if kind.startswith("distill") else runner.alg.actor).obs_normalizer
     res = {
         "rank": rank,
         "checksum": float(flat.sum()),
@@ -100,9 +111,9 @@ def _worker(rank: int, world: int, port: int, out_dir: str, kind: str = "mlp") -
         "status": eng.status.tolist(),
         "lr": runner.alg.learning_rate,
     }
-    if kind == "distill":  # the frozen teacher must be rank 0's on every rank
+    if kind.startswith("distill"):  # the frozen teacher must be rank 0's on every rank
         res["teacher"] = float(sum(p.double().sum() for p in runner.alg.teacher.parameters()))
-    if kind == "rnd_sym":
+    if kind in ("rnd_sym", "gru_rnd"):
         res["rnd_target"] = float(sum(p.double().sum() for p in runner.alg.rnd.target.parameters()))
         res["rnd_count"] = int(runner.alg.rnd.state_normalizer.count)
     gathered = [torch.zeros_like(eng.flat) for _ in range(world)]
@@ -130,7 +141,7 @@ def test_data_parallel_replicas_bit_identical():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("kind", ["rnd_sym", "gru", "lstm", "distill"])
+@pytest.mark.parametrize("kind", ["rnd_sym", "gru", "lstm", "gru_rnd", "distill", "distill_rnn"])
 def test_data_parallel_engines_bit_identical(kind):
     world = 2
     out_dir = tempfile.mkdtemp()
