@@ -1447,14 +1447,31 @@ __global__ void colstats_kernel(const ColStatsArgs a) {
   const int col = blockIdx.x * 32 + threadIdx.x;
   const long long r0 = static_cast<long long>(blockIdx.y) * kStatsRowsPerChunk;
   const long long r1 = min(a.rows, r0 + kStatsRowsPerChunk);
-  double s = 0.0, ss = 0.0;
+  // four independent accumulator pairs, so four rows' loads are in flight per thread (the sums are combined in a
+  // fixed order: deterministic)
+  double s4[4] = {0.0, 0.0, 0.0, 0.0}, ss4[4] = {0.0, 0.0, 0.0, 0.0};
   if (col < a.dim) {
-    for (long long r = r0 + threadIdx.y; r < r1; r += blockDim.y) {
-      const double v = a.x[static_cast<size_t>(r) * a.ld + col];
-      s += v;
-      ss += v * v;
+    const long long step = blockDim.y;
+    long long r = r0 + threadIdx.y;
+    for (; r + 3 * step < r1; r += 4 * step) {
+      float v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = __ldg(a.x + static_cast<size_t>(r + k * step) * a.ld + col);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const double d = v[k];
+        s4[k] += d;
+        ss4[k] += d * d;
+      }
+    }
+    for (; r < r1; r += step) {
+      const double d = __ldg(a.x + static_cast<size_t>(r) * a.ld + col);
+      s4[0] += d;
+      ss4[0] += d * d;
     }
   }
+  const double s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+  const double ss = (ss4[0] + ss4[1]) + (ss4[2] + ss4[3]);
   __shared__ double sh[2][8][33];
   sh[0][threadIdx.y][threadIdx.x] = s;
   sh[1][threadIdx.y][threadIdx.x] = ss;
