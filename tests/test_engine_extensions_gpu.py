@@ -103,9 +103,12 @@ def test_engine_symmetry_matches_torch_path(aug, mirror):
         m_old, v_old = alg_t.actor(probe).clone(), alg_t.critic(probe).clone()
     loss_t = alg_t.update()
     loss_e = alg_e.update()
+    # bounds: 3 x the bf16 noise floor measured on B200 (the PyTorch path under bf16 autocast against fp32 on the
+    # same data, augmentation + mirror loss, 3 seeds): actor means up to 0.0081, values up to 0.0038 of the update
+    # (the engine: 0.0092 / 0.0015)
     with torch.no_grad():
-        assert _dev(alg_e.actor(probe), alg_t.actor(probe), m_old) < 0.15
-        assert _dev(alg_e.critic(probe), alg_t.critic(probe), v_old) < 0.15
+        assert _dev(alg_e.actor(probe), alg_t.actor(probe), m_old) < 0.025
+        assert _dev(alg_e.critic(probe), alg_t.critic(probe), v_old) < 0.012
     for k in ("value", "surrogate", "entropy", "symmetry"):
         assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=2e-3), (k, loss_e[k], loss_t[k])
     assert alg_e.learning_rate == pytest.approx(alg_t.learning_rate, rel=1e-6)
@@ -139,10 +142,12 @@ def test_engine_rnd_matches_torch_path(reward_norm):
         p_old = alg_t.rnd.predictor(s).clone()
     loss_t = alg_t.update()
     loss_e = alg_e.update()
+    # bounds: 3 x the bf16 noise floor measured on B200 (3 seeds): actor means up to 0.0111, values 0.0019, RND
+    # predictor 0.0024 of the update (the engine: 0.0090 / 0.0019 / 0.0023)
     with torch.no_grad():
-        assert _dev(alg_e.actor(probe), alg_t.actor(probe), m_old) < 0.15
-        assert _dev(alg_e.critic(probe), alg_t.critic(probe), v_old) < 0.15
-        assert _dev(alg_e.rnd.predictor(s), alg_t.rnd.predictor(s), p_old) < 0.15
+        assert _dev(alg_e.actor(probe), alg_t.actor(probe), m_old) < 0.034
+        assert _dev(alg_e.critic(probe), alg_t.critic(probe), v_old) < 0.006
+        assert _dev(alg_e.rnd.predictor(s), alg_t.rnd.predictor(s), p_old) < 0.0075
     for k in ("value", "surrogate", "entropy", "rnd"):
         assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=2e-3), (k, loss_e[k], loss_t[k])
     # the predictor has its own optimizer: step count and learning rate are separate from PPO's

@@ -113,7 +113,9 @@ def test_recurrent_distillation_update_matches_torch_path(rnn_type, gl, epochs):
     new_t = _sequence_outputs(alg_t.student, obs_seq, dones_seq, None)
     new_e = _sequence_outputs(alg_e.student, obs_seq, dones_seq, None)
     dev = ((new_e - new_t).norm() / (new_t - old).norm()).item()
-    assert dev < 2e-2, dev
+    # 3 x the bf16 noise floor measured on B200 (the PyTorch path under bf16 autocast against fp32, GRU gl 4 and
+    # LSTM gl 3, 3 seeds): up to 0.0021 of the update (the engine: up to 0.0024)
+    assert dev < 6.5e-3, dev
     windows = epochs * T // gl
     assert int(alg_e.engine.step[0].item()) == windows
     # the state the next update starts from (and the rollout continues from)

@@ -83,13 +83,16 @@ def test_recurrent_engine_matches_torch_path(rnn_type, per_mb, fused):
     h0 = h0a[None] if c0a is None else (h0a[None].clone(), c0a[None].clone())
     new_e = _sequence_means(alg_e.actor, obs_seq, dones_seq, h0)
     dev = ((new_e - new_t).norm() / (new_t - old).norm()).item()
-    assert dev < 0.2, dev
+    # bounds: 3 x the bf16 noise floor measured on B200 (the PyTorch path under bf16 autocast against fp32 on the
+    # same data, GRU and LSTM, 3 seeds): sequence means up to 0.039, W_hh up to 0.047 of the update (the engine:
+    # 0.024 / 0.026)
+    assert dev < 0.12, dev
     for k in ("value", "surrogate", "entropy"):
         assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=3e-3), (k, loss_e[k], loss_t[k])
     assert alg_e.learning_rate == pytest.approx(alg_t.learning_rate, rel=1e-6)
     # recurrent weights moved like the PyTorch path's
     wt, we = alg_t.actor.rnn.rnn.weight_hh_l0.detach(), alg_e.actor.rnn.rnn.weight_hh_l0.detach()
-    assert ((we - wt).norm() / (wt - w0).norm()).item() < 0.25
+    assert ((we - wt).norm() / (wt - w0).norm()).item() < 0.14
 
 
 @pytest.mark.parametrize("rnn_type", ["gru", "lstm"])
@@ -191,7 +194,8 @@ def test_recurrent_engine_rnd_matches_torch_path(rnn_type):
     loss_e = alg_e.update()
     with torch.no_grad():
         p_t, p_e = alg_t.rnd.predictor(probe), alg_e.rnd.predictor(probe)
-    assert ((p_e - p_t).norm() / (p_t - p_old).norm()).item() < 0.1
+    # 3 x the bf16 noise floor measured on B200 (3 seeds): up to 0.0028 of the update (the engine: 0.0026)
+    assert ((p_e - p_t).norm() / (p_t - p_old).norm()).item() < 0.0085
     for k in ("value", "surrogate", "entropy", "rnd"):
         assert loss_e[k] == pytest.approx(loss_t[k], rel=5e-2, abs=3e-3), (k, loss_e[k], loss_t[k])
     assert int(alg_e.engine.step[2].item()) == 2 * 4
