@@ -12,12 +12,18 @@ pytestmark = pytest.mark.gpu
 
 
 def _models(obs, A, rnn_type, teacher_rnn):
+    """A GRU / LSTM student (``rnn_type``; "mlp": an MLP student) and an MLP or recurrent teacher."""
     from tt_rsl_rl_b200.models import MLPModel, RNNModel
 
     groups = {"student": ["policy"], "teacher": ["critic"]}
-    student = RNNModel(obs, groups, "student", A, hidden_dims=[64, 32], obs_normalization=True,
-                       distribution_cfg={"class_name": "GaussianDistribution", "init_std": 1.0}, rnn_type=rnn_type,
-                       rnn_hidden_dim=64)
+    dist = {"class_name": "GaussianDistribution", "init_std": 1.0}
+    if rnn_type == "mlp":
+        student = MLPModel(obs, groups, "student", A, hidden_dims=[64, 32], obs_normalization=True,
+                           distribution_cfg=dist)
+        rnn_type = "gru"
+    else:
+        student = RNNModel(obs, groups, "student", A, hidden_dims=[64, 32], obs_normalization=True,
+                           distribution_cfg=dist, rnn_type=rnn_type, rnn_hidden_dim=64)
     if teacher_rnn:
         teacher = RNNModel(obs, groups, "teacher", A, hidden_dims=[64, 32], obs_normalization=True,
                            rnn_type=rnn_type, rnn_hidden_dim=96)
@@ -48,9 +54,11 @@ def _sequence_outputs(model, obs_seq, dones_seq, state):
     return torch.stack(out)
 
 
-@pytest.mark.parametrize("rnn_type,teacher_rnn", [("gru", True), ("lstm", False)])
+@pytest.mark.parametrize("rnn_type,teacher_rnn", [("gru", True), ("lstm", False), ("mlp", True)])
 def test_recurrent_distillation_rollout_matches_modules(rnn_type, teacher_rnn):
-    from tt_rsl_rl_b200.engine import RecurrentDistillationEngine
+    """Student means and teacher targets of the fused rollout against the PyTorch modules stepping the same
+    observations ("mlp": the MLP-student engine with a recurrent teacher)."""
+    from tt_rsl_rl_b200.engine import DistillationEngine, RecurrentDistillationEngine
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv
 
     torch.manual_seed(0)
@@ -60,7 +68,7 @@ def test_recurrent_distillation_rollout_matches_modules(rnn_type, teacher_rnn):
     student, teacher = _models(obs, A, rnn_type, teacher_rnn)
     s_ref, t_ref = copy.deepcopy(student), copy.deepcopy(teacher)
     alg = _alg(env, T, "cuda", student, teacher, gl=3, epochs=1)
-    assert isinstance(alg.engine, RecurrentDistillationEngine)
+    assert isinstance(alg.engine, DistillationEngine if rnn_type == "mlp" else RecurrentDistillationEngine)
     eng = alg.engine
     for t in range(T):
         with torch.inference_mode():
@@ -80,10 +88,11 @@ def test_recurrent_distillation_rollout_matches_modules(rnn_type, teacher_rnn):
             t_ref.reset(dones)
 
 
-@pytest.mark.parametrize("rnn_type,gl,epochs", [("gru", 4, 2), ("lstm", 3, 2), ("gru", 5, 2)])
+@pytest.mark.parametrize("rnn_type,gl,epochs", [("gru", 4, 2), ("lstm", 3, 2), ("gru", 5, 2), ("gru", 10, 3)])
 def test_recurrent_distillation_update_matches_torch_path(rnn_type, gl, epochs):
     """T = 8: gl 4 (windows inside epochs), gl 3 (a window across the epoch boundary, one leftover step), gl 5
-    (every window but the first crosses an epoch boundary or ends an epoch)."""
+    (every window but the first crosses an epoch boundary or ends an epoch), gl 10 (windows longer than an epoch:
+    every window spans epochs, four leftover steps)."""
     from tt_rsl_rl_b200.env import LinearGaussianVecEnv
 
     torch.manual_seed(1)
