@@ -63,6 +63,25 @@ def _teacher_reason(m) -> str | None:
     return rnn_model_reason("teacher", m) if isinstance(m, RNNModel) else _mlp_model_reason("teacher", m)
 
 
+def window_segments(epochs: int, steps: int, gradient_length: int) -> list[tuple[int, int, int, bool, bool, bool]]:
+    """The sequences a recurrent student trains on: ``(epoch, t0, L, first_in_window, train, apply)`` per run of
+    ``L`` consecutive steps from ``t0`` that lies in one epoch and one window of ``gradient_length`` steps (windows
+    count steps across epochs, as upstream's loss sum does). ``train``: the run belongs to a window that reaches an
+    optimizer step (steps left over after the last full window only contribute their loss); ``apply``: the window
+    ends with this run."""
+    applied = (epochs * steps) // gradient_length * gradient_length
+    out, count = [], 0
+    for e in range(epochs):
+        t = 0
+        while t < steps:
+            L = min(steps - t, gradient_length - count % gradient_length)
+            train = count + L <= applied
+            out.append((e, t, L, count % gradient_length == 0, train, train and (count + L) % gradient_length == 0))
+            count += L
+            t += L
+    return out
+
+
 def _common_reason(alg) -> str | None:
     sd = alg.student.distribution
     if sd is not None and not isinstance(sd, (GaussianDistribution, HeteroscedasticGaussianDistribution)):
@@ -501,36 +520,29 @@ class RecurrentDistillationEngine(DistillationEngine):
         H = net.H
         huber = self.alg.loss_type == "huber"
         self.loss_acc.zero_()
-        applied = (self.E * T) // GL * GL  # steps of the windows that reach an optimizer step
         carry = (self.carry_h, self.carry_hbf, self.carry_c)
-        count = 0
-        for _ in range(self.E):
-            t = 0
-            while t < T:
-                L = min(T - t, GL - count % GL)  # up to the end of the window or of the epoch
-                init = (self.h_last, self.c_last) if t == 0 else (self.carry_h, self.carry_c)
-                x = self.x_s[t * N : (t + L) * N]
-                rows = L * N
-                used = C.mse_blocks(rows)
-                if used < self.mse_blocks:  # fewer loss blocks: clear the output-bias partial rows they leave
-                    self.dhead_colsum[used:].zero_()
-                net.forward_sequence(0, N, self.st_dones, head.out_train, head.out_train.shape[1], self.status, L=L,
-                                     t0=t, time_major=True, x=x, init=init, carry=carry)
-                # every step's loss is a mean over its N rows: the window's gradient is the sum of the step means'
-                C.mse_grad(head.out_train, head.out_train.shape[1], self.targets[t * N : (t + L) * N], self.head_t,
-                           rows, self.A, huber, head.d_head, head.d_head.shape[1], self.head_s, self.loss_partial,
-                           self.dhead_colsum, self.loss_acc, self.loss_ticket, None, N)
-                if count + L <= applied:
-                    net.backward_sequence(0, N, self.st_dones, self.status, L=L, t0=t, time_major=True, x=x)
-                    self._reduce(accumulate=count % GL != 0)
-                    if (count + L) % GL == 0:
-                        self._adam()
-                count += L
-                t += L
+        for _, t, L, first, train, apply in window_segments(self.E, T, GL):
+            init = (self.h_last, self.c_last) if t == 0 else (self.carry_h, self.carry_c)
+            x = self.x_s[t * N : (t + L) * N]
+            rows = L * N
+            used = C.mse_blocks(rows)
+            if used < self.mse_blocks:  # fewer loss blocks: clear the output-bias partial rows they leave
+                self.dhead_colsum[used:].zero_()
+            net.forward_sequence(0, N, self.st_dones, head.out_train, head.out_train.shape[1], self.status, L=L, t0=t,
+                                 time_major=True, x=x, init=init, carry=carry)
+            # every step's loss is a mean over its N rows: the window's gradient is the sum of the step means'
+            C.mse_grad(head.out_train, head.out_train.shape[1], self.targets[t * N : (t + L) * N], self.head_t, rows,
+                       self.A, huber, head.d_head, head.d_head.shape[1], self.head_s, self.loss_partial,
+                       self.dhead_colsum, self.loss_acc, self.loss_ticket, None, N)
+            if train:
+                net.backward_sequence(0, N, self.st_dones, self.status, L=L, t0=t, time_major=True, x=x)
+                self._reduce(accumulate=not first)
+                if apply:
+                    self._adam()
         # the next update's epochs start from the state this one ended with, and the rollout continues from it
         C.rnn_mask(N, H, self.carry_h, H, self.carry_c, H, None, self.h_last, H, None, 0, self.c_last, H)
         C.rnn_mask(N, H, self.carry_h, H, self.carry_c, H, None, net.h, H, net.h_bf, H, net.c, H)
         self._normalizer_update("student", self.student, self.obs_s, self.total, self.Ds)
 
 
-__all__ = ["DistillationEngine", "RecurrentDistillationEngine"]
+__all__ = ["DistillationEngine", "RecurrentDistillationEngine", "window_segments"]
