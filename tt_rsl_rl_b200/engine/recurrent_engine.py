@@ -9,14 +9,18 @@ starts from the state stored at the rollout's first step), and the loss averages
 unpadded upstream outputs do. That form needs no data-dependent padding, so a minibatch is:
 
 * forward: one GEMM ``gi = x W_ih^T + b_ih`` over all ``T x B`` rows (env-major ``[B, T, .]`` layout, so an env range
-  is contiguous), then per step ``gh = h W_hh^T + b_hh`` (tcgen05 GEMM) and the fused cell (gates, new state, masked
-  next-step input, saved activations); the MLP head and the PPO loss over all rows;
+  is contiguous), then per step ``gh = h W_hh^T + b_hh`` (tcgen05 GEMM) and the cell (gates, new state, masked
+  next-step input, saved activations) -- as one launch with the cell in the GEMM's epilogue when
+  ``b200_cfg.rnn_fused_step`` selects it (GRU by default); the MLP head and the PPO loss over all rows;
 * backward: head backward including the gradient of its input, then backpropagation through time, per step in
   reverse: the backward cell (gate gradients, bias-gradient column sums, masked recurrent gradients) and the GEMM
   ``dh = dgh W_hh``; the weight gradients of ``W_ih`` and ``W_hh`` as two split-K GEMMs over all rows;
 * the gradient reduction and the fused clip + adaptive-LR + Adam kernel shared with the MLP engine.
 
 Rollout steps run the same cell on the persistent per-environment state; ``process_env_step`` masks it at dones.
+With RND the intrinsic reward is added during the rollout and the predictor trains on each minibatch as upstream's
+does on the padded trajectories (``rnd_part.py``; ``_rnd_minibatch``). The sequence functions also serve the
+recurrent distillation student (time-major windows of steps over all environments).
 """
 
 from __future__ import annotations
