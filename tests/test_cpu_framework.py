@@ -609,6 +609,8 @@ def test_mlp_plan_buffers_and_reduction_segments(in_dim, hidden, A, rows):
     plan = MLPPlan(mlp, in_dim, rows_roll=rows // 4, rows_train=rows, device=torch.device("cpu"), sm_count=sm)
     bf16 = [plan.x_roll, plan.x_train, plan.d_head, *plan.h_roll, *plan.h_train, *plan.dz, *plan.w_bf16]
     assert all(t.dtype == torch.bfloat16 and t.shape[-1] % 8 == 0 for t in bf16)  # 16-byte pitches
+    # fp32 head outputs: pitch rounded up to whole 32-column chunks of the GEMM epilogue
+    assert plan.out_roll.shape[1] == plan.out_train.shape[1] == plan.out_pitch == (A + 31) // 32 * 32
     assert plan.widths == [in_dim, *hidden, A]
     for lin, s, part in zip(plan.linears, plan.splits, plan.wgrad_partial):
         kb = (rows + 63) // 64

@@ -37,6 +37,29 @@ def test_forward_f32_bias(M, N, K):
     assert_parity(out, ref, "fp32_elementwise", f"gemm fp32 epilogue {M}x{N}x{K}")
 
 
+@pytest.mark.parametrize("M,N,K", [(1000, 29, 128), (300, 58, 96), (77, 1, 64)])
+def test_forward_f32_padded_output_columns(M, N, K):
+    """out_cols: a row pitch rounded up to 32-column chunks takes whole chunks (zeros past N), nothing past out_cols."""
+    from tt_rsl_rl_b200.ops import gemm as G
+
+    torch.manual_seed(2)
+    kp = G.pad8(K)
+    x = torch.zeros(M, kp, device="cuda", dtype=torch.bfloat16)
+    x[:, :K] = _bf16((M, K))
+    w = torch.zeros(N, kp, device="cuda", dtype=torch.bfloat16)
+    w[:, :K] = _bf16((N, K), 0.1)
+    bias = torch.randn(N, device="cuda")
+    pitch = (N + 31) // 32 * 32
+    out = torch.full((M, pitch + 8), float("nan"), device="cuda")  # 8 columns beyond the writable ones
+    G.gemm(x, kp, False, w, kp, False, M, N, K, G.EPI_F32, out, pitch + 8, bias=bias, out_cols=pitch)
+    torch.cuda.synchronize()
+    ref = _ref(x[:, :K], w[:, :K]) + bias
+    torch.testing.assert_close(out[:, :N], ref, atol=2e-3 * (K ** 0.5), rtol=1e-3)
+    pad = out[:, N:pitch]
+    assert ((pad == 0) | pad.isnan()).all()  # zeros where a whole chunk was stored, untouched otherwise
+    assert out[:, pitch:].isnan().all()
+
+
 @pytest.mark.parametrize("M,N,K", [(300, 512, 96), (1000, 256, 512), (129, 128, 256), (77, 40, 64)])
 def test_forward_bias_elu_bf16(M, N, K):
     from tt_rsl_rl_b200.ops import gemm as G

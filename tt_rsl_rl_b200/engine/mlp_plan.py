@@ -51,14 +51,17 @@ class MLPPlan:
         # rollout activations
         self.x_roll = torch.zeros(rows_roll, pad8(in_dim), **bf)
         self.h_roll = [torch.zeros(rows_roll, pad8(w), **bf) for w in self.widths[1:-1]]
-        self.out_roll = torch.zeros(rows_roll, self.head_cols, **f32)
+        # head outputs with the row pitch rounded up to 32 columns: the head GEMM then stores whole 32-column chunks
+        # (the padding columns hold zeros); consumers read them at this pitch (``out.shape[1]``)
+        self.out_pitch = (self.head_cols + 31) // 32 * 32
+        self.out_roll = torch.zeros(rows_roll, self.out_pitch, **f32)
         self.train = train
         if not train:
             return
         B = rows_train
         self.x_train = torch.zeros(B, pad8(in_dim), **bf)
         self.h_train = [torch.zeros(B, pad8(w), **bf) for w in self.widths[1:-1]]
-        self.out_train = torch.zeros(B, self.head_cols, **f32)
+        self.out_train = torch.zeros(B, self.out_pitch, **f32)
         self.grads = grads
         if not grads:  # inference-only training-size buffers (a frozen network evaluated on minibatches)
             return
@@ -96,8 +99,10 @@ class MLPPlan:
                        dst.shape[1], bias=lin.bias.data, status=status)
                 src = dst
             else:
+                # the plan's own head buffers may take whole 32-column chunks (their padding is this plan's)
+                own = out is self.out_roll or (self.train and out is self.out_train)
                 G.gemm(src, src.shape[1], False, w, w.shape[1], False, rows, N, K, G.EPI_F32, out, out_ld,
-                       bias=lin.bias.data, status=status)
+                       bias=lin.bias.data, status=status, out_cols=out_ld if own and out_ld >= N else 0)
 
     # ---- backward ---------------------------------------------------------------------------------------------------
     def backward(self, rows: int, status: torch.Tensor | None = None, x: torch.Tensor | None = None,

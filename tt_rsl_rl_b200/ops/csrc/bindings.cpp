@@ -4,6 +4,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
+
 #include "gemm_tcgen05.cuh"
 #include "kernels.cuh"
 
@@ -31,7 +33,8 @@ void raise_on(cudaError_t e, const char* what) {
 void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b, int64_t ldb, bool b_mn, int64_t M,
           int64_t N, int64_t K, int64_t epilogue, const torch::Tensor& out, int64_t ldo, int64_t splits,
           int64_t split_stride, const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& aux,
-          int64_t ld_aux, const c10::optional<torch::Tensor>& colsum, const c10::optional<torch::Tensor>& status) {
+          int64_t ld_aux, const c10::optional<torch::Tensor>& colsum, const c10::optional<torch::Tensor>& status,
+          int64_t out_cols) {
   check_cuda(a, "a");
   check_cuda(b, "b");
   check_cuda(out, "out");
@@ -45,7 +48,9 @@ void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b
   const int64_t b_need = b_mn ? (K - 1) * ldb + N : (N - 1) * ldb + K;
   TORCH_CHECK(avail(a) >= a_need, "gemm: A too small");
   TORCH_CHECK(avail(b) >= b_need, "gemm: B too small");
-  TORCH_CHECK(avail(out) >= (splits - 1) * split_stride + (M - 1) * ldo + N, "gemm: out too small");
+  TORCH_CHECK(avail(out) >= (splits - 1) * split_stride + (M - 1) * ldo + std::max(N, out_cols), "gemm: out too small");
+  TORCH_CHECK(out_cols == 0 || (epilogue == rlb::kEpiF32 && out_cols >= N && out_cols <= ldo),
+              "gemm: out_cols (fp32 output only) must lie in [N, ldo]");
   if (bias.has_value() && bias->defined()) {
     TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "gemm: bad bias");
   }
@@ -83,6 +88,7 @@ void gemm(const torch::Tensor& a, int64_t lda, bool a_mn, const torch::Tensor& b
   p.colsum = ptr_or_null<float>(colsum);
   p.colsum_rows = static_cast<int>(colsum_rows);
   p.status = ptr_or_null<unsigned int>(status);
+  p.out_cols = static_cast<int>(out_cols);
   raise_on(rlb::gemm_launch(p, at::cuda::getCurrentCUDAStream()), "gemm");
 }
 

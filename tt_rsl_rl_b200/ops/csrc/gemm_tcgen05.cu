@@ -624,6 +624,7 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
     // 16-byte row stores need 16-byte aligned rows
     const bool vec_ok = (p.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
                         (EPI != kEpiPartialF32 || p.split_stride % 4 == 0);
+    const int wcols = p.out_cols > p.N ? p.out_cols : p.N;  // writable columns of a row
     int j = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
       const TileCoord tc = decode_tile(t, n_tiles, m_tiles, splits, num_kb, BN);
@@ -666,7 +667,7 @@ __global__ void __launch_bounds__(Shape<EPI, WIDE>::kThreads, Shape<EPI, WIDE>::
           float* o = static_cast<float*>(p.out) +
                      (EPI == kEpiPartialF32 ? static_cast<long long>(tc.split) * p.split_stride : 0ll) + sb;
           const long long row0 = tc.m0 + q * 32;
-          if (vec_ok && sb + 32 <= p.N) {
+          if (vec_ok && sb + 32 <= wcols) {
             // lane l: 16 bytes of row 4 i + l / 8 (eight lanes per 128-byte row)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -847,6 +848,7 @@ cudaError_t gemm_launch(const GemmParams& p, cudaStream_t stream) {
   if (p.splits > num_kb) return cudaErrorInvalidValue;
   if (p.splits > 1 && p.epilogue != kEpiPartialF32) return cudaErrorInvalidValue;
   if (p.epilogue == kEpiDgradElu && p.aux == nullptr) return cudaErrorInvalidValue;
+  if (p.out_cols != 0 && (p.epilogue != kEpiF32 || p.out_cols < p.N || p.out_cols > p.ldo)) return cudaErrorInvalidValue;
   if (p.epilogue == kEpiDgradElu && p.colsum != nullptr && (p.N > kColsumMaxN || p.colsum_rows < 1))
     return cudaErrorInvalidValue;
   const bool staged = p.epilogue == kEpiBiasEluBf16 || p.epilogue == kEpiBiasBf16 || p.epilogue == kEpiDgradElu;

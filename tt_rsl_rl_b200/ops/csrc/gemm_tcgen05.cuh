@@ -75,6 +75,9 @@ struct GemmParams {
   float* colsum = nullptr;    // fp32 [colsum_rows, N]: per-CTA column sums of the stored output (bias gradients)
   int colsum_rows = 0;        // rows of colsum (>= the launch's CTA count, gemm_colsum_rows()); N <= kColsumMaxN
   unsigned int* status = nullptr;
+  // kEpiF32: columns of each output row the epilogue may write (N .. ldo; 0 = N). Above N it stores whole 32-column
+  // chunks (the padding columns receive zeros), so a padded output leaves through 16-byte row stores.
+  int out_cols = 0;
   RnnCellEpi cell;            // kEpiRnnCell only
 };
 

@@ -57,10 +57,12 @@ def gemm(
     ld_aux: int = 0,
     colsum: torch.Tensor | None = None,
     status: torch.Tensor | None = None,
+    out_cols: int = 0,
 ) -> None:
-    """out[M, N] = sum_k A(m, k) B(n, k) with the selected epilogue (see ``gemm_tcgen05.cuh``)."""
+    """out[M, N] = sum_k A(m, k) B(n, k) with the selected epilogue (see ``gemm_tcgen05.cuh``). ``out_cols`` (fp32
+    outputs): columns of each row that may be written, N .. ldo (padding columns receive zeros)."""
     ext().gemm(a, lda, a_mn, b, ldb, b_mn, M, N, K, epilogue, out, ldo, splits, split_stride, bias, aux, ld_aux,
-               colsum, status)
+               colsum, status, out_cols)
 
 
 def linear_forward(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor, *, elu: bool,
