@@ -222,6 +222,22 @@ def test_b200_cfg_rejects_unknown_keys():
         resolve_b200_cfg({"nope": 1})
 
 
+def test_b200_cfg_value_checks_and_exchange_policy():
+    from tt_rsl_rl_b200.algorithms.ppo import resolve_b200_cfg, use_two_shot
+
+    cfg = resolve_b200_cfg(None)
+    assert cfg["exchange"] == "auto" and cfg["rnn_fused_step"] == "auto"
+    for key, bad in (("exchange", "three_shot"), ("rnn_fused_step", "yes")):
+        with pytest.raises(ValueError):
+            resolve_b200_cfg({key: bad})
+    for v in (True, False, "auto"):
+        assert resolve_b200_cfg({"rnn_fused_step": v})["rnn_fused_step"] == v
+    # "auto" exchanges in one shot (measured faster at the benchmark's size); two-shot only when asked, on 2+ ranks
+    assert not any(use_two_shot(resolve_b200_cfg({"exchange": m}), w) for m in ("auto", "one_shot") for w in (1, 2, 8))
+    assert use_two_shot(resolve_b200_cfg({"exchange": "two_shot"}), 2)
+    assert not use_two_shot(resolve_b200_cfg({"exchange": "two_shot"}), 1)
+
+
 # ---- data parallel over gloo (two CPU ranks) ------------------------------------------------------------------------------
 def _free_port():
     with socket.socket() as s:
