@@ -484,10 +484,11 @@ __device__ __forceinline__ void max_grad_split(float a, float b, float& ga, floa
 //   entropy and KL: copy 0 only (mean over n0), as upstream evaluates them on the original samples;
 //   mirror loss: copies >= 1, MSE between the row's mean and the mirrored mean of its original (target detached).
 // kSym = false compiles the plain path (one copy) without the symmetry branches and their registers.
-// The plain path first issues every load of the warp's kLossRowsPerWarp rows (random storage rows: actions, old mean
-// and std, scalars) and only then computes, so each warp keeps its rows' loads in flight together.
+// Both paths first issue every load of the warp's kLossRowsPerWarp rows (random storage rows: actions, old mean and
+// std, scalars; with copies the permuted actions and mirror targets) and only then compute, so each warp keeps its
+// rows' loads in flight together.
 template <bool kSym>
-__global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel(const PpoLossArgs a) {
+__global__ void __launch_bounds__(kLossWarps * 32, 2) ppo_loss_kernel(const PpoLossArgs a) {
   griddep_wait();  // launched with programmatic stream serialization (launch_pdl)
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
@@ -514,46 +515,52 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
   const int ngroups = (a.B + kLossRowsPerBlock - 1) / kLossRowsPerBlock;
   for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
   const int row0 = grp * kLossRowsPerBlock + warp * kLossRowsPerWarp;
-  // prefetch (plain path): storage rows of all of this warp's rows
-  constexpr int PF = kSym ? 1 : kLossRowsPerWarp;
-  float pf_act[PF][2], pf_omu[PF][2], pf_osd[PF][2], pf_mu[PF][2], pf_raw[PF][2];
+  // prefetch: every load of this warp's rows (random storage rows; with symmetry copies the signed-permuted action
+  // columns and the mirror targets) before any arithmetic
+  constexpr int PF = kLossRowsPerWarp;
+  float pf_act[PF][2], pf_omu[PF][2], pf_osd[PF][2], pf_mu[PF][2], pf_raw[PF][2], pf_mt[PF][2];
   float pf_adv[PF], pf_lp[PF], pf_ret[PF], pf_vold[PF], pf_v[PF];
-  if constexpr (!kSym) {
 #pragma unroll
-    for (int rr = 0; rr < PF; ++rr) {
-      const int i = row0 + rr;
-      const bool in = i < a.B;
-      int src = in ? a.idx[i] : 0;
-      RL_CHECK_INDEX(src, a.total, a.status, 44);
-      const float* h = a.head + static_cast<size_t>(in ? i : 0) * a.ld_head;
+  for (int rr = 0; rr < PF; ++rr) {
+    const int i = row0 + rr;
+    const bool in = i < a.B;
+    const int copy = (kSym && in) ? i / a.n0 : 0;
+    const int o = in ? i - copy * a.n0 : 0;
+    int src = in ? a.idx[o] : 0;
+    RL_CHECK_INDEX(src, a.total, a.status, 44);
+    const float* h = a.head + static_cast<size_t>(in ? i : 0) * a.ld_head;
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int j = lane + 32 * k;
-        const bool ok = in && j < a.A;
-        const size_t so = static_cast<size_t>(src) * a.A + j;
-        pf_act[rr][k] = ok ? a.st_actions[so] : 0.f;
-        pf_omu[rr][k] = ok ? a.st_mean[so] : 0.f;
-        pf_osd[rr][k] = ok ? a.st_std[so] : 1.f;
-        pf_mu[rr][k] = ok ? h[j] : 0.f;
-        pf_raw[rr][k] = (ok && a.hetero) ? h[a.A + j] : 1.f;  // non-hetero: the shared parameter, read below
+    for (int k = 0; k < 2; ++k) {
+      const int j = lane + 32 * k;
+      const bool ok = in && j < a.A;
+      int aj = j;
+      float asg = 1.f, mt = 0.f;
+      if (kSym && ok && copy > 0) {  // the copy's action and mirror target: signed permutation of the original's
+        aj = a.act_perm[copy * a.A + j];
+        RL_CHECK_INDEX(aj, a.A, a.status, 45);
+        asg = a.act_sign[copy * a.A + j];
+        mt = asg * a.head[static_cast<size_t>(o) * a.ld_head + aj];
       }
-      pf_adv[rr] = in ? (a.adv_override ? a.adv_override[i] : a.st_adv[src]) : 0.f;
-      pf_lp[rr] = in ? a.st_logp[src] : 0.f;
-      pf_ret[rr] = in ? a.st_ret[src] : 0.f;
-      pf_vold[rr] = in ? a.st_val[src] : 0.f;
-      pf_v[rr] = in ? a.value[static_cast<size_t>(i) * a.ld_value] : 0.f;
+      const size_t so = static_cast<size_t>(src) * a.A + j;
+      pf_act[rr][k] = ok ? asg * a.st_actions[static_cast<size_t>(src) * a.A + aj] : 0.f;
+      pf_omu[rr][k] = (ok && copy == 0) ? a.st_mean[so] : 0.f;
+      pf_osd[rr][k] = (ok && copy == 0) ? a.st_std[so] : 1.f;
+      pf_mu[rr][k] = ok ? h[j] : 0.f;
+      pf_raw[rr][k] = (ok && a.hetero) ? h[a.A + j] : 1.f;  // non-hetero: the shared parameter, read below
+      pf_mt[rr][k] = mt;
     }
+    pf_adv[rr] = in ? (a.adv_override ? a.adv_override[o] : a.st_adv[src]) : 0.f;
+    pf_lp[rr] = in ? a.st_logp[src] : 0.f;
+    pf_ret[rr] = in ? a.st_ret[src] : 0.f;
+    pf_vold[rr] = in ? a.st_val[src] : 0.f;
+    pf_v[rr] = in ? a.value[static_cast<size_t>(i) * a.ld_value] : 0.f;
   }
 #pragma unroll
   for (int rr = 0; rr < kLossRowsPerWarp; ++rr) {
     const int i = row0 + rr;
     if (i >= a.B) break;
     const int copy = kSym ? i / a.n0 : 0;
-    const int o = i - copy * a.n0;
     const bool ppo_row = a.aug || copy == 0;
-    int src = kSym ? a.idx[o] : 0;
-    RL_CHECK_INDEX(src, a.total, a.status, 44);
-    const float* h = a.head + static_cast<size_t>(i) * a.ld_head;
     float mu[2], sd[2], isd[2], raw[2], act[2], mt[2];
     float lp = 0.f, ent = 0.f, kl = 0.f, sym = 0.f;
 #pragma unroll
@@ -565,29 +572,22 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
       isd[k] = c_isd[k];
       float lsd = c_lsd[k];
       if (j < a.A) {
-        const int pr = kSym ? 0 : rr;
-        mu[k] = kSym ? h[j] : pf_mu[pr][k];
+        mu[k] = pf_mu[rr][k];
         if (a.hetero) {
-          raw[k] = kSym ? h[a.A + j] : pf_raw[pr][k];
+          raw[k] = pf_raw[rr][k];
           std_terms(raw[k], a, sd[k], lsd, isd[k]);
         }
-        int aj = j;
-        float asg = 1.f;
-        if (copy > 0) {  // the copy's action and mirror target: signed permutation of the original's columns
-          aj = a.act_perm[copy * a.A + j];
-          RL_CHECK_INDEX(aj, a.A, a.status, 45);
-          asg = a.act_sign[copy * a.A + j];
-          mt[k] = asg * a.head[static_cast<size_t>(o) * a.ld_head + aj];
+        if (copy > 0) {  // mirror loss against the original's signed-permuted mean
+          mt[k] = pf_mt[rr][k];
           const float dm = mu[k] - mt[k];
           sym += dm * dm;
         }
-        act[k] = kSym ? asg * a.st_actions[static_cast<size_t>(src) * a.A + aj] : pf_act[pr][k];
+        act[k] = pf_act[rr][k];
         const float z = (act[k] - mu[k]) * isd[k];
         lp += -0.5f * z * z - lsd - kLogSqrt2Pi;
         if (copy == 0) {
-          const size_t so = static_cast<size_t>(src) * a.A + j;
-          const float omu = kSym ? a.st_mean[so] : pf_omu[pr][k];
-          const float osd = kSym ? a.st_std[so] : pf_osd[pr][k];
+          const float omu = pf_omu[rr][k];
+          const float osd = pf_osd[rr][k];
           ent += 0.5f + kLogSqrt2Pi + lsd;
           // KL(old || new) for diagonal Gaussians; only compared against the adaptive-LR thresholds, so the fast
           // logarithm suffices: log(vr) = 2 log(osd / sd)
@@ -606,10 +606,9 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
     }
     float d_lp = 0.f, dv = 0.f, surr = 0.f, vloss = 0.f;
     if (ppo_row) {
-      const int pr = kSym ? 0 : rr;
       // surrogate (identical on every lane)
-      const float adv = kSym ? (a.adv_override ? a.adv_override[o] : a.st_adv[src]) : pf_adv[pr];
-      const float ratio = expf(lp - (kSym ? a.st_logp[src] : pf_lp[pr]));
+      const float adv = pf_adv[rr];
+      const float ratio = expf(lp - pf_lp[rr]);
       const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
       const float rc = fminf(fmaxf(ratio, lo), hi);
       const float s1 = -adv * ratio, s2 = -adv * rc;
@@ -620,9 +619,9 @@ __global__ void __launch_bounds__(kLossWarps * 32, kSym ? 3 : 2) ppo_loss_kernel
       d_lp = d_ratio * ratio;
       surr = fmaxf(s1, s2);
       // value loss
-      const float v = kSym ? a.value[static_cast<size_t>(i) * a.ld_value] : pf_v[pr];
-      const float ret = kSym ? a.st_ret[src] : pf_ret[pr];
-      const float vold = kSym ? a.st_val[src] : pf_vold[pr];
+      const float v = pf_v[rr];
+      const float ret = pf_ret[rr];
+      const float vold = pf_vold[rr];
       if (a.clipped_value) {
         const float dvv = v - vold;
         const float vc = vold + fminf(fmaxf(dvv, -a.clip), a.clip);
